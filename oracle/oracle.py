@@ -1,0 +1,374 @@
+"""ctypes binding of the CPU oracle (liboracle.so) — TEST INFRASTRUCTURE ONLY.
+
+Imported only by tests/, __graft_entry__.smoke() and bench.py's CPU-baseline
+leg, as the checker.  The product (tts-rs_b200/) never imports this module.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = None
+
+F = C.POINTER(C.c_float)
+I64 = C.POINTER(C.c_int64)
+
+
+class LMCfg(C.Structure):
+    _fields_ = [("hidden", C.c_int), ("inter", C.c_int), ("n_layers", C.c_int),
+                ("n_heads", C.c_int), ("n_kv", C.c_int), ("head_dim", C.c_int),
+                ("eps", C.c_float), ("theta", C.c_float)]
+
+
+class Layer(C.Structure):
+    _fields_ = [(n, F) for n in ("in_norm", "post_norm", "wq", "wk", "wv", "wo",
+                                 "q_norm", "k_norm", "w_gate", "w_up", "w_down")]
+
+
+class Stack(C.Structure):
+    _fields_ = [("cfg", LMCfg), ("layers", C.POINTER(Layer)), ("final_norm", F)]
+
+
+class KV(C.Structure):
+    _fields_ = [("k", F), ("v", F), ("len", C.c_int), ("cap", C.c_int),
+                ("n_kv", C.c_int), ("head_dim", C.c_int)]
+
+
+class Sampling(C.Structure):
+    _fields_ = [("do_sample", C.c_int), ("temperature", C.c_float), ("top_k", C.c_int),
+                ("top_p", C.c_float), ("repetition_penalty", C.c_float)]
+
+
+class Talker(C.Structure):
+    _fields_ = [("talker", Stack), ("predictor", Stack), ("codec_head", F),
+                ("talker_codec_emb", F), ("cp_codec_emb", C.POINTER(F)),
+                ("lm_heads", C.POINTER(F)), ("vocab", C.c_int), ("cp_vocab", C.c_int),
+                ("n_groups", C.c_int)]
+
+
+class ResUnit(C.Structure):
+    _fields_ = [(n, F) for n in ("w1", "b1", "w2", "b2", "a1_alpha", "a1_beta",
+                                 "a2_alpha", "a2_beta")]
+
+
+class WaveStage(C.Structure):
+    _fields_ = [("snake_alpha", F), ("snake_beta", F), ("wt", F), ("bt", F),
+                ("ru", ResUnit * 3)]
+
+
+class ConvNeXt(C.Structure):
+    _fields_ = [(n, F) for n in ("wt", "bt", "dw_w", "dw_b", "ln_w", "ln_b", "pw1_w",
+                                 "pw1_b", "pw2_w", "pw2_b", "gamma")]
+
+
+class CodecLayer(C.Structure):
+    _fields_ = [(n, F) for n in ("in_norm", "post_norm", "wq", "wk", "wv", "wo",
+                                 "attn_scale", "mlp_scale", "w_gate", "w_up", "w_down")]
+
+
+class Codec(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_q", "n_semantic", "codebook_size", "codebook_dim",
+                                       "latent", "decoder_dim", "hidden", "inter", "n_layers",
+                                       "n_heads", "n_kv", "head_dim")] + \
+               [("eps", C.c_float), ("theta", C.c_float), ("n_up", C.c_int),
+                ("up_ratio", C.c_int * 4), ("n_stage", C.c_int), ("rates", C.c_int * 8),
+                ("emb_sum", C.POINTER(F)), ("usage", C.POINTER(F)),
+                ("first_out_proj", F), ("rest_out_proj", F), ("pre_conv_w", F),
+                ("pre_conv_b", F), ("in_proj_w", F), ("in_proj_b", F), ("out_proj_w", F),
+                ("out_proj_b", F), ("final_norm", F), ("layers", C.POINTER(CodecLayer)),
+                ("up", C.POINTER(ConvNeXt)), ("in_conv_w", F), ("in_conv_b", F),
+                ("stages", C.POINTER(WaveStage)), ("out_alpha", F), ("out_beta", F),
+                ("out_conv_w", F), ("out_conv_b", F)]
+
+
+def lib():
+    """Load liboracle.so, building it with make if it is missing."""
+    global _LIB
+    if _LIB is None:
+        path = os.path.join(_HERE, "liboracle.so")
+        if not os.path.exists(path):
+            subprocess.run(["make", "-C", _HERE], check=True, capture_output=True)
+        L = C.CDLL(path)
+        L.orc_bf16_round.restype = C.c_float
+        L.orc_bf16_round.argtypes = [C.c_float]
+        L.orc_sample_token.restype = C.c_int64
+        L.orc_sample_token.argtypes = [F, C.c_int, C.POINTER(Sampling), I64, C.c_int, C.c_float]
+        L.orc_apply_repetition_penalty.argtypes = [F, C.c_int, I64, C.c_int, C.c_float]
+        L.orc_repetition_penalty_enabled.argtypes = [C.c_float]
+        L.orc_build_suppress_ids.argtypes = [C.c_int, C.c_int64, I64]
+        L.orc_kv_forward.argtypes = [C.POINTER(KV), F, F, C.c_int, F, F]
+        L.orc_kv_reset_preserve.argtypes = [C.POINTER(KV)]
+        L.orc_stack_forward.argtypes = [C.POINTER(Stack), C.POINTER(KV), F, C.c_int, F]
+        L.orc_linear.argtypes = [F, F, F, C.c_int, C.c_int, C.c_int, F]
+        L.orc_gen_start.restype = C.c_void_p
+        L.orc_gen_start.argtypes = [C.POINTER(Talker), F, C.c_int, F, C.c_int, F,
+                                    C.POINTER(Sampling), C.POINTER(Sampling), C.c_int,
+                                    C.c_int64, I64, C.c_int, C.c_int64, F,
+                                    C.POINTER(C.c_int)]
+        L.orc_gen_step.argtypes = [C.c_void_p, I64, F, F, F, F]
+        L.orc_gen_num_frames.argtypes = [C.c_void_p]
+        L.orc_gen_codes.argtypes = [C.c_void_p, I64]
+        L.orc_gen_free.argtypes = [C.c_void_p]
+        L.orc_predict_frame.argtypes = [C.POINTER(Talker), F, C.c_int64, C.POINTER(Sampling),
+                                        I64, F, I64, F]
+        L.orc_codec_group_embedding.argtypes = [C.POINTER(Talker), I64, F, F]
+        L.orc_codec_out_len.restype = C.c_int64
+        L.orc_codec_out_len.argtypes = [C.POINTER(Codec), C.c_int]
+        L.orc_codec_decode.argtypes = [C.POINTER(Codec), I64, C.c_int, C.c_int, F]
+        L.orc_codec_decode_tap.restype = C.c_int64
+        L.orc_codec_decode_tap.argtypes = [C.POINTER(Codec), I64, C.c_int, C.c_int, F]
+        L.orc_pad_1d.argtypes = [F, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, F]
+        L.orc_conv1d_padding.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int,
+                                         C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        L.orc_to_pcm.argtypes = [F, C.c_int64, C.POINTER(C.c_int16)]
+        L.orc_sdpa.argtypes = [F, F, F, C.POINTER(C.c_uint8), C.c_int, C.c_int, C.c_int,
+                               C.c_int, C.c_float, F]
+        L.orc_set_threads.argtypes = [C.c_int]
+        L.orc_get_threads.restype = C.c_int
+        _LIB = L
+    return _LIB
+
+
+def fp(a):
+    return None if a is None else a.ctypes.data_as(F)
+
+
+def ip(a):
+    return None if a is None else a.ctypes.data_as(I64)
+
+
+def f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def sampling(do_sample=False, temperature=1.0, top_k=0, top_p=1.0, repetition_penalty=0.0):
+    return Sampling(int(do_sample), float(temperature), int(top_k or 0), float(top_p),
+                    float(repetition_penalty if repetition_penalty is not None else 0.0))
+
+
+class OracleTalker:
+    """Talker + code predictor bound to the oracle; keeps the numpy weights
+    alive for as long as the ctypes structs point at them."""
+
+    def __init__(self, cfg, weights: dict):
+        self.cfg = cfg
+        self.w = {k: f32(v) for k, v in weights.items()}
+        self._keep = []
+        self.s = Talker()
+        self.s.talker = self._stack("talker.model", cfg.talker)
+        self.s.predictor = self._stack("talker.code_predictor.model", cfg.predictor)
+        self.s.codec_head = fp(self.w["talker.codec_head.weight"])
+        self.s.talker_codec_emb = fp(self.w["talker.model.codec_embedding.weight"])
+        G = cfg.n_groups
+        emb = (F * (G - 1))(*[fp(self.w[f"talker.code_predictor.model.codec_embedding.{j}.weight"])
+                              for j in range(G - 1)])
+        heads = (F * (G - 1))(*[fp(self.w[f"talker.code_predictor.lm_head.{j}.weight"])
+                                for j in range(G - 1)])
+        self._keep += [emb, heads]
+        self.s.cp_codec_emb = C.cast(emb, C.POINTER(F))
+        self.s.lm_heads = C.cast(heads, C.POINTER(F))
+        self.s.vocab = cfg.talker.vocab
+        self.s.cp_vocab = cfg.predictor.vocab
+        self.s.n_groups = G
+
+    def _stack(self, prefix, c):
+        layers = (Layer * c.n_layers)()
+        for l in range(c.n_layers):
+            p = f"{prefix}.layers.{l}"
+            w = self.w
+            layers[l] = Layer(fp(w[f"{p}.input_layernorm.weight"]),
+                              fp(w[f"{p}.post_attention_layernorm.weight"]),
+                              fp(w[f"{p}.self_attn.q_proj.weight"]), fp(w[f"{p}.self_attn.k_proj.weight"]),
+                              fp(w[f"{p}.self_attn.v_proj.weight"]), fp(w[f"{p}.self_attn.o_proj.weight"]),
+                              fp(w[f"{p}.self_attn.q_norm.weight"]), fp(w[f"{p}.self_attn.k_norm.weight"]),
+                              fp(w[f"{p}.mlp.gate_proj.weight"]), fp(w[f"{p}.mlp.up_proj.weight"]),
+                              fp(w[f"{p}.mlp.down_proj.weight"]))
+        self._keep.append(layers)
+        st = Stack(LMCfg(c.hidden, c.inter, c.n_layers, c.n_heads, c.n_kv, c.head_dim,
+                         c.eps, c.theta), C.cast(layers, C.POINTER(Layer)),
+                   fp(self.w[f"{prefix}.norm.weight"]))
+        return st
+
+    # --- dense batch-1 caches ------------------------------------------------
+    def make_caches(self, which="talker", cap=4096):
+        c = self.cfg.talker if which == "talker" else self.cfg.predictor
+        mems, kvs = [], (KV * c.n_layers)()
+        for l in range(c.n_layers):
+            k = np.zeros((c.n_kv, cap, c.head_dim), np.float32)
+            v = np.zeros_like(k)
+            mems.append((k, v))
+            kvs[l] = KV(fp(k), fp(v), 0, cap, c.n_kv, c.head_dim)
+        return kvs, mems
+
+    def stack_forward(self, which, kvs, x):
+        x = f32(x)
+        S = x.shape[0]
+        st = self.s.talker if which == "talker" else self.s.predictor
+        H = st.cfg.hidden
+        out = np.zeros((S, H), np.float32)
+        lib().orc_stack_forward(C.byref(st), kvs, fp(x), S, fp(out))
+        return out
+
+    def codec_head(self, hidden):
+        h = f32(hidden).reshape(-1, self.cfg.talker.hidden)
+        out = np.zeros((h.shape[0], self.cfg.talker.vocab), np.float32)
+        lib().orc_linear(fp(self.w["talker.codec_head.weight"]), None, fp(h), h.shape[0],
+                         self.cfg.talker.hidden, self.cfg.talker.vocab, fp(out))
+        return out
+
+    def predict_frame(self, hidden, code0, samp=None, forced=None, u=None):
+        G, V = self.cfg.n_groups, self.cfg.predictor.vocab
+        codes = np.zeros(G, np.int64)
+        logits = np.zeros((G - 1, V), np.float32)
+        s = samp or sampling()
+        fz = None if forced is None else np.ascontiguousarray(forced, np.int64)
+        uu = None if u is None else f32(u)
+        lib().orc_predict_frame(C.byref(self.s), fp(f32(hidden)), int(code0), C.byref(s),
+                                ip(fz), fp(uu), ip(codes), fp(logits))
+        return codes, logits
+
+    def group_embedding(self, codes, extra=None):
+        out = np.zeros(self.cfg.talker.hidden, np.float32)
+        lib().orc_codec_group_embedding(C.byref(self.s), ip(np.ascontiguousarray(codes, np.int64)),
+                                        fp(None if extra is None else f32(extra)), fp(out))
+        return out
+
+
+class OracleGenerator:
+    """TalkerGenerator restatement (talker/infer/mod.rs:17-311)."""
+
+    def __init__(self, talker: OracleTalker, prompt, trailing, pad, talker_s=None, cp_s=None,
+                 max_new_tokens=64, eos=-1, suppress=None, forced_first=-1):
+        self.t = talker
+        self._in = [f32(prompt), f32(trailing), f32(pad)]
+        self.ts = talker_s or sampling()
+        self.cs = cp_s or sampling()
+        sup = np.ascontiguousarray(suppress if suppress is not None else [], np.int64)
+        self._sup = sup
+        self.first_logits = np.zeros(talker.cfg.talker.vocab, np.float32)
+        st = C.c_int(0)
+        self.h = lib().orc_gen_start(C.byref(talker.s), fp(self._in[0]), self._in[0].shape[0],
+                                     fp(self._in[1]), self._in[1].shape[0], fp(self._in[2]),
+                                     C.byref(self.ts), C.byref(self.cs), int(max_new_tokens),
+                                     int(eos), ip(sup) if len(sup) else None, len(sup),
+                                     int(forced_first), fp(self.first_logits), C.byref(st))
+        if st.value != 0:
+            raise ValueError(f"oracle start failed: {st.value}")
+
+    def step(self, forced=None, u=None):
+        G = self.t.cfg.n_groups
+        tl = np.zeros(self.t.cfg.talker.vocab, np.float32)
+        cl = np.zeros((G - 1, self.t.cfg.predictor.vocab), np.float32)
+        hid = np.zeros(self.t.cfg.talker.hidden, np.float32)
+        fz = None if forced is None else np.ascontiguousarray(forced, np.int64)
+        uu = None if u is None else f32(u)
+        r = lib().orc_gen_step(self.h, ip(fz), fp(uu), fp(tl), fp(cl), fp(hid))
+        return r, tl, cl, hid
+
+    def codes(self):
+        T = lib().orc_gen_num_frames(self.h)
+        out = np.zeros((self.t.cfg.n_groups, T), np.int64)
+        if T:
+            lib().orc_gen_codes(self.h, ip(out))
+        return out
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().orc_gen_free(self.h)
+            self.h = None
+
+
+class OracleCodec:
+    """Codec decoder restatement (codec/network/decoder.rs:250-278)."""
+
+    def __init__(self, cfg, weights: dict):
+        self.cfg = cfg
+        w = {k: f32(v) for k, v in weights.items()}
+        self.w = w
+        self._keep = []
+        c = Codec()
+        for n in ("n_q", "n_semantic", "codebook_size", "codebook_dim", "latent", "decoder_dim",
+                  "hidden", "inter", "n_layers", "n_heads", "n_kv", "head_dim"):
+            setattr(c, n, getattr(cfg, n))
+        c.eps, c.theta = cfg.eps, cfg.theta
+        c.n_up = len(cfg.up_ratios)
+        for i, r in enumerate(cfg.up_ratios):
+            c.up_ratio[i] = r
+        c.n_stage = len(cfg.rates)
+        for i, r in enumerate(cfg.rates):
+            c.rates[i] = r
+        names = [f"decoder.quantizer.rvq_first.vq.layers.{i}._codebook" for i in range(cfg.n_semantic)] + \
+                [f"decoder.quantizer.rvq_rest.vq.layers.{i}._codebook" for i in range(cfg.n_q - cfg.n_semantic)]
+        es = (F * cfg.n_q)(*[fp(w[n + ".embedding_sum"]) for n in names])
+        us = (F * cfg.n_q)(*[fp(w[n + ".cluster_usage"]) for n in names])
+        self._keep += [es, us]
+        c.emb_sum, c.usage = C.cast(es, C.POINTER(F)), C.cast(us, C.POINTER(F))
+        c.first_out_proj = fp(w["decoder.quantizer.rvq_first.output_proj.weight"])
+        c.rest_out_proj = fp(w["decoder.quantizer.rvq_rest.output_proj.weight"])
+        c.pre_conv_w, c.pre_conv_b = fp(w["decoder.pre_conv.conv.weight"]), fp(w["decoder.pre_conv.conv.bias"])
+        pt = "decoder.pre_transformer"
+        c.in_proj_w, c.in_proj_b = fp(w[f"{pt}.input_proj.weight"]), fp(w[f"{pt}.input_proj.bias"])
+        c.out_proj_w, c.out_proj_b = fp(w[f"{pt}.output_proj.weight"]), fp(w[f"{pt}.output_proj.bias"])
+        c.final_norm = fp(w[f"{pt}.norm.weight"])
+        layers = (CodecLayer * cfg.n_layers)()
+        for l in range(cfg.n_layers):
+            p = f"{pt}.layers.{l}"
+            layers[l] = CodecLayer(*[fp(w[f"{p}.{n}"]) for n in (
+                "input_layernorm.weight", "post_attention_layernorm.weight",
+                "self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight",
+                "self_attn.o_proj.weight", "self_attn_layer_scale.scale", "mlp_layer_scale.scale",
+                "mlp.gate_proj.weight", "mlp.up_proj.weight", "mlp.down_proj.weight")])
+        ups = (ConvNeXt * len(cfg.up_ratios))()
+        for u in range(len(cfg.up_ratios)):
+            p = f"decoder.upsample.{u}"
+            ups[u] = ConvNeXt(*[fp(w[f"{p}.{n}"]) for n in (
+                "0.conv.weight", "0.conv.bias", "1.dwconv.conv.weight", "1.dwconv.conv.bias",
+                "1.norm.weight", "1.norm.bias", "1.pwconv1.weight", "1.pwconv1.bias",
+                "1.pwconv2.weight", "1.pwconv2.bias", "1.gamma")])
+        stages = (WaveStage * len(cfg.rates))()
+        for i in range(len(cfg.rates)):
+            p = f"decoder.decoder.{i + 1}.block"
+            st = WaveStage()
+            st.snake_alpha, st.snake_beta = fp(w[f"{p}.0.alpha"]), fp(w[f"{p}.0.beta"])
+            st.wt, st.bt = fp(w[f"{p}.1.conv.weight"]), fp(w[f"{p}.1.conv.bias"])
+            for ru in range(3):
+                q = f"{p}.{ru + 2}"
+                st.ru[ru] = ResUnit(fp(w[f"{q}.conv1.conv.weight"]), fp(w[f"{q}.conv1.conv.bias"]),
+                                    fp(w[f"{q}.conv2.conv.weight"]), fp(w[f"{q}.conv2.conv.bias"]),
+                                    fp(w[f"{q}.act1.alpha"]), fp(w[f"{q}.act1.beta"]),
+                                    fp(w[f"{q}.act2.alpha"]), fp(w[f"{q}.act2.beta"]))
+            stages[i] = st
+        self._keep += [layers, ups, stages]
+        c.layers = C.cast(layers, C.POINTER(CodecLayer))
+        c.up = C.cast(ups, C.POINTER(ConvNeXt))
+        c.stages = C.cast(stages, C.POINTER(WaveStage))
+        c.in_conv_w, c.in_conv_b = fp(w["decoder.decoder.0.conv.weight"]), fp(w["decoder.decoder.0.conv.bias"])
+        n = len(cfg.rates)
+        c.out_alpha, c.out_beta = fp(w[f"decoder.decoder.{n + 1}.alpha"]), fp(w[f"decoder.decoder.{n + 1}.beta"])
+        c.out_conv_w = fp(w[f"decoder.decoder.{n + 2}.conv.weight"])
+        c.out_conv_b = fp(w[f"decoder.decoder.{n + 2}.conv.bias"])
+        self.s = c
+
+    def out_len(self, T):
+        return lib().orc_codec_out_len(C.byref(self.s), T)
+
+    def decode(self, codes):
+        codes = np.ascontiguousarray(codes, np.int64)
+        B, _, T = codes.shape
+        out = np.zeros((B, self.out_len(T)), np.float32)
+        r = lib().orc_codec_decode(C.byref(self.s), ip(codes), B, T, fp(out))
+        if r != 0:
+            raise ValueError("oracle codec: invalid codes")
+        return out
+
+    def tap(self, codes, tap):
+        codes = np.ascontiguousarray(codes, np.int64)
+        T = codes.shape[-1]
+        n = lib().orc_codec_decode_tap(C.byref(self.s), ip(codes), T, tap, None)
+        out = np.zeros(n, np.float32)
+        lib().orc_codec_decode_tap(C.byref(self.s), ip(codes), T, tap, fp(out))
+        return out

@@ -1,0 +1,149 @@
+"""Pins the CPU oracle to the reference's own known-answer tests (extracted
+from the Rust sources into tests/golden/reference_kats.json by
+tests/golden/make_golden.py)."""
+import math
+
+import numpy as np
+import pytest
+
+import oracle as O
+import synthetic as S
+
+
+def test_sample_token_skips_masked_logits(kats):
+    k = kats["sample_suppress"]
+    lg = np.array(k["logits"], np.float32)
+    sup = np.array(k["suppress"], np.int64)
+    s = O.sampling()
+    tok = O.lib().orc_sample_token(O.fp(lg), len(lg), s, O.ip(sup), len(sup), 0.5)
+    assert tok == k["expected"]
+
+
+@pytest.mark.parametrize("u", [0.0, 0.3, 0.999])
+def test_top_k_one_returns_argmax(kats, u):
+    k = kats["sample_topk1"]
+    lg = np.array(k["logits"], np.float32)
+    s = O.sampling(do_sample=k["do_sample"], temperature=k["temperature"], top_k=k["top_k"],
+                   top_p=k["top_p"])
+    assert O.lib().orc_sample_token(O.fp(lg), len(lg), s, None, 0, u) == k["expected"]
+
+
+def test_repetition_penalty_enabled(kats):
+    for c in kats["repetition_penalty_enabled"]["cases"]:
+        p = 0.0 if c["penalty"] is None else float(c["penalty"])
+        assert bool(O.lib().orc_repetition_penalty_enabled(p)) == c["enabled"], c
+
+
+def _kv(cache_dims):
+    _, heads, cap, hd = cache_dims
+    k = np.zeros((heads, cap, hd), np.float32)
+    v = np.zeros_like(k)
+    return O.KV(O.fp(k), O.fp(v), 0, cap, heads, hd), (k, v)
+
+
+def test_kv_reset_preserves_allocation(kats):
+    k = kats["kv_reset_len"]
+    kv, mem = _kv(k["cache"])
+    _, h, s, d = k["input"]
+    ones = np.ones((h, s, d), np.float32)
+    O.lib().orc_kv_forward(kv, O.fp(ones), O.fp(ones), s, None, None)
+    assert kv.len == k["len_after_forward"]
+    O.lib().orc_kv_reset_preserve(kv)
+    assert kv.len == k["len_after_reset"]
+
+
+def test_kv_reset_exposes_only_new_values(kats):
+    k = kats["kv_reset_values"]
+    kv, mem = _kv(k["cache"])
+    fk = np.array(k["first_key"], np.float32).reshape(1, -1, 1)
+    fv = np.array(k["first_value"], np.float32).reshape(1, -1, 1)
+    O.lib().orc_kv_forward(kv, O.fp(fk), O.fp(fv), fk.shape[1], None, None)
+    O.lib().orc_kv_reset_preserve(kv)
+    nk = np.array(k["next_key"], np.float32).reshape(1, -1, 1)
+    nv = np.array(k["next_value"], np.float32).reshape(1, -1, 1)
+    ko = np.zeros(4, np.float32)
+    vo = np.zeros(4, np.float32)
+    n = O.lib().orc_kv_forward(kv, O.fp(nk), O.fp(nv), nk.shape[1], O.fp(ko), O.fp(vo))
+    assert n == k["len"] == kv.len
+    assert list(ko[:n]) == k["key_out"]
+    assert list(vo[:n]) == k["value_out"]
+
+
+def test_kv_sliding_window_keeps_latest():
+    # kv.rs:109-132: a full cache drops the oldest steps
+    kv, mem = _kv([1, 1, 4, 1])
+    for step in range(6):
+        t = np.array([[[float(step)]]], np.float32)
+        out = np.zeros(4, np.float32)
+        n = O.lib().orc_kv_forward(kv, O.fp(t), O.fp(t), 1, O.fp(out), O.fp(out.copy()))
+    assert n == 4 and list(out) == [2.0, 3.0, 4.0, 5.0]
+
+
+def test_pad_1d(kats):
+    for k in kats["pad_1d"]:
+        x = np.array(k["input"], np.float32)
+        out = np.zeros(len(x) + k["left"] + k["right"], np.float32)
+        O.lib().orc_pad_1d(O.fp(x), 1, len(x), k["left"], k["right"],
+                           0 if k["mode"] == "constant" else 1, O.fp(out))
+        assert list(out) == k["expected"], k["source"]
+
+
+def test_config_fixture_matches_synthetic_dims(kats):
+    c = kats["talker_config"]["config"]
+    cfg = S.TalkerConfig()
+    t, p = cfg.talker, cfg.predictor
+    assert (t.hidden, t.inter, t.n_layers, t.n_heads, t.n_kv, t.head_dim, t.vocab) == (
+        c["hidden_size"], c["intermediate_size"], c["num_hidden_layers"],
+        c["num_attention_heads"], c["num_key_value_heads"], c["head_dim"], c["vocab_size"])
+    pc = c["code_predictor_config"]
+    assert (p.hidden, p.inter, p.n_layers, p.n_heads, p.n_kv, p.head_dim, p.vocab) == (
+        pc["hidden_size"], pc["intermediate_size"], pc["num_hidden_layers"],
+        pc["num_attention_heads"], pc["num_key_value_heads"], pc["head_dim"], pc["vocab_size"])
+    assert cfg.n_groups == c["num_code_groups"] == pc["num_code_groups"]
+    assert t.eps == c["rms_norm_eps"] and t.theta == c["rope_theta"]
+    assert p.theta == pc["rope_theta"]
+
+
+def test_sdpa_kat_shape_and_masking(kats):
+    k = kats["sdpa_shape"]
+    q = np.array(k["query"], np.float32).reshape(2, 2, 2)
+    kk = np.array(k["key"], np.float32).reshape(2, 2, 2)
+    v = np.array(k["value"], np.float32).reshape(2, 2, 2)
+    mask = np.array(k["mask"], np.uint8).reshape(2, 2)
+    out = np.zeros((2, 2, 2), np.float32)
+    scale = 1.0 / math.sqrt(2.0)
+    O.lib().orc_sdpa(O.fp(q), O.fp(kk), O.fp(v), mask.ctypes.data_as(O.C.POINTER(O.C.c_uint8)),
+                     2, 2, 2, 2, scale, O.fp(out))
+    # row 0 attends to key 0 only (mask [0, 1]); row 1 to both
+    np.testing.assert_allclose(out[:, 0], v[:, 0], rtol=0, atol=1e-7)
+    for h in range(2):
+        s = q[h, 1] @ kk[h].T * scale
+        p = np.exp(s - s.max()); p /= p.sum()
+        np.testing.assert_allclose(out[h, 1], p @ v[h], rtol=1e-6)
+
+
+def test_suppress_ids():
+    out = np.zeros(4096, np.int64)
+    n = O.lib().orc_build_suppress_ids(3072, 2150, O.ip(out))
+    ids = list(out[:n])
+    assert n == 1023 and ids[0] == 2048 and ids[-1] == 3071 and 2150 not in ids
+
+
+def test_repetition_penalty_accumulates_duplicates():
+    lg = np.array([2.0, -1.0, 4.0], np.float32)
+    hist = np.array([0, 0, 1], np.int64)
+    O.lib().orc_apply_repetition_penalty(O.fp(lg), 3, O.ip(hist), 3, 2.0)
+    # delta = logit * (1/p - 1) scatter-added per occurrence, sign ignored
+    np.testing.assert_allclose(lg, [2.0 - 1.0 - 1.0, -1.0 + 0.5, 4.0])
+
+
+def test_codec_output_length():
+    assert S.CodecConfig().out_len(750) == 1_439_445
+    assert S.CodecConfig().out_len(4) == ((((16 - 1) * 8 - 1) * 5 - 1) * 4 - 1) * 3
+
+
+def test_to_pcm_rounding():
+    x = np.array([0.0, 1.0, -1.0, 2.0, 0.5 / 32768, -1.5 / 32768], np.float32)
+    out = np.zeros(len(x), np.int16)
+    O.lib().orc_to_pcm(O.fp(x), len(x), out.ctypes.data_as(O.C.POINTER(O.C.c_int16)))
+    assert list(out) == [0, 32767, -32768, 32767, 1, -2]
