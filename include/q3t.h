@@ -1,0 +1,255 @@
+/*
+ * q3t.h — C ABI of the B200 (sm_100a) Qwen3-TTS synthesis hot path.
+ *
+ * Drop-in boundary for the `tts_qwen3_tts` driver of onenewcode/tts-rs: the
+ * Rust driver keeps its surface (surface/mod.rs), package loading and
+ * request compiler, and replaces three things with calls into this library:
+ *   - the Burn weight load        (tts_qwen3_tts/src/loading/runtime.rs:131-156)
+ *   - TalkerGenerator start/step/finalize
+ *                                 (tts_qwen3_tts/src/model/talker/infer/mod.rs:69-311)
+ *   - decode_waveform + to_pcm    (tts_qwen3_tts/src/model/codec/infer/mod.rs:61-111)
+ * and gains a ragged continuous-batching scheduler (no reference counterpart:
+ * the reference is batch-1, talker/infer/mod.rs:92-96).
+ *
+ * Conventions: plain pointers and sizes; host buffers are owned by the
+ * caller and copied on entry/exit; every device buffer (weights, KV pages,
+ * activations, workspaces) is owned by the library and freed by *_free.
+ * Every call returns a q3t_status; q3t_last_error() gives the message of the
+ * last failure on the calling thread.  A model handle is immutable after load
+ * and may be shared by threads; sessions and batches are single-threaded.
+ */
+#ifndef Q3T_H
+#define Q3T_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Q3T_ABI_VERSION 1
+
+/* Status codes.  The first four mirror Qwen3TtsInferenceError variants
+ * (tts_qwen3_tts/src/error.rs:64-101) so the Rust side maps them 1:1. */
+typedef enum {
+  Q3T_OK = 0,
+  Q3T_INVALID_INPUT = 1,   /* QwenTtsInferenceError::InvalidInput */
+  Q3T_RUNTIME_LOAD = 2,    /* QwenTtsInferenceError::RuntimeLoad (missing / bad tensor) */
+  Q3T_TENSOR_READ = 3,     /* QwenTtsInferenceError::TensorRead (device -> host read failed) */
+  Q3T_DEVICE_TIMEOUT = 4,  /* a bounded device-side wait gave up */
+  Q3T_OUT_OF_PAGES = 5,    /* KV page pool exhausted (the reference slides; see q3t_session_desc) */
+  Q3T_CUDA_ERROR = 6       /* CUDA runtime error (message has the CUDA error string) */
+} q3t_status;
+
+typedef enum { Q3T_F32 = 0, Q3T_BF16 = 1 } q3t_dtype;
+
+/* Decoder-stack hyper-parameters (tts_qwen3_tts/src/model/talker/config.rs:18-61).
+ * Kernels are specialised for head_dim 128, hidden % 256 == 0, intermediate % 256 == 0. */
+typedef struct {
+  int hidden_size;
+  int intermediate_size;
+  int num_hidden_layers;
+  int num_attention_heads;
+  int num_key_value_heads;
+  int head_dim;
+  int vocab_size;
+  float rms_norm_eps;
+  float rope_theta;
+} q3t_lm_config;
+
+typedef struct {
+  q3t_lm_config talker;      /* talker_config */
+  q3t_lm_config predictor;   /* talker_config.code_predictor_config */
+  int num_code_groups;       /* 16 */
+} q3t_talker_config;
+
+/* Speech-tokenizer decoder config (tts_qwen3_tts/src/model/codec/config.rs:50-76). */
+typedef struct {
+  int num_quantizers;            /* 16 */
+  int num_semantic_quantizers;   /* 1 */
+  int codebook_size;             /* 2048 */
+  int codebook_dim;              /* 512 (tables are codebook_dim / 2 wide) */
+  int latent_dim;                /* 1024 */
+  int decoder_dim;               /* 1536 */
+  int hidden_size;               /* pre-transformer width, 512 */
+  int intermediate_size;         /* 1024 */
+  int num_hidden_layers;         /* 8 */
+  int num_attention_heads;       /* 16 */
+  int num_key_value_heads;       /* 16 */
+  int head_dim;                  /* 64 */
+  float rms_norm_eps;            /* 1e-5 */
+  float rope_theta;              /* 1e4 */
+  int num_upsampling_ratios;
+  int upsampling_ratios[4];      /* [2, 2] */
+  int num_upsample_rates;
+  int upsample_rates[8];         /* [8, 5, 4, 3] */
+  int output_sample_rate;        /* 24000 */
+} q3t_codec_config;
+
+/* One named tensor in PyTorch layout (Linear [out,in], Conv1d [out,in/g,k],
+ * ConvTranspose1d [in,out,k]).  Names are the checkpoint names the reference
+ * loads (talker/weights.rs:14, codec/weights.rs:13-33), e.g.
+ * "talker.model.layers.0.self_attn.q_proj.weight" or
+ * "decoder.quantizer.rvq_rest.vq.layers.3._codebook.embedding_sum". */
+typedef struct {
+  const char *name;
+  int dtype;                 /* q3t_dtype of `data` (host memory) */
+  int ndim;
+  int64_t shape[4];
+  const void *data;
+} q3t_tensor;
+
+typedef struct {
+  int device;                /* CUDA device ordinal */
+  q3t_talker_config talker;
+  int has_talker;            /* 0: codec-only model */
+  q3t_codec_config codec;
+  int has_codec;             /* 0: talker-only model */
+  const q3t_tensor *tensors;
+  int num_tensors;
+  int64_t kv_pages;          /* talker KV pool size in 16-token pages (0: 8192) */
+  int max_active;            /* max requests in one batched step, 1..64 (0: 64) */
+} q3t_model_desc;
+
+typedef struct q3t_model q3t_model;
+
+/* Replaces loading/runtime.rs:131-156 (safetensors -> Burn with the bf16
+ * load-time cast): copies and packs every tensor into device memory. */
+q3t_status q3t_model_load(const q3t_model_desc *desc, q3t_model **out);
+void q3t_model_free(q3t_model *model);
+
+/* Sampling (tts_qwen3_tts/src/model/talker/infer/sampling.rs:12-31).
+ * top_k <= 0: none; repetition_penalty <= 0, NaN or 1: none.  seed drives the
+ * on-device categorical draw (Burn's RNG stream is not reproducible). */
+typedef struct {
+  int do_sample;
+  float temperature;
+  int top_k;
+  float top_p;
+  float repetition_penalty;
+  uint64_t seed;
+} q3t_sampling;
+
+/* TalkerGeneratorStart (talker/infer/mod.rs:49-60).  Positions are
+ * arange(prompt_len) in all three MRoPE rows (session_seed.rs:90-92), so
+ * they are implied.  The attention mask is all ones in the reference. */
+typedef struct {
+  const float *inputs_embeds;   /* [prompt_len][hidden] */
+  int prompt_len;
+  const float *trailing_text;   /* [trailing_len][hidden], trailing_len > 0 */
+  int trailing_len;
+  const float *pad_embed;       /* [hidden] */
+  q3t_sampling talker_sampling;
+  q3t_sampling predictor_sampling;
+  int max_new_tokens;           /* > 0 (infer/mod.rs:86-91) */
+  int64_t eos_token_id;         /* < 0: None */
+  const int64_t *suppress_ids;  /* applied to the first talker token only */
+  int num_suppress;
+  /* teacher forcing (tests; absent in the reference): >= 0 replaces the
+   * first sampled talker token; first_logits (nullable) receives its logits */
+  int64_t forced_first_token;
+  float *first_logits;          /* [vocab] */
+} q3t_session_desc;
+
+typedef struct q3t_session q3t_session;
+
+/* TalkerGenerator::start (infer/mod.rs:69-188): prefill + first sample. */
+q3t_status q3t_session_start(q3t_model *model, const q3t_session_desc *desc,
+                             q3t_session **out);
+/* TalkerGenerator::step (infer/mod.rs:190-299).  *state: 0 = None (already
+ * finished), 1 = advanced, 2 = finished.  INVALID_INPUT for "EOS before any
+ * audio codec token" (:197-202). */
+q3t_status q3t_session_step(q3t_session *s, int *state);
+/* Teacher-forced step: codes[num_code_groups] replace the sampled codes of
+ * this frame (codes[0] the talker token, codes[1..] the predictor's); the
+ * logits computed on the way are written out (nullable):
+ * talker_logits [vocab] = the next talker token's logits (after the
+ * repetition penalty), predictor_logits [num_code_groups-1][cp_vocab],
+ * hidden [hidden] = the talker's new last hidden state. */
+q3t_status q3t_session_step_forced(q3t_session *s, const int64_t *codes,
+                                   float *talker_logits, float *predictor_logits,
+                                   float *hidden, int *state);
+/* TalkerGenerator::finalize (infer/mod.rs:301-311): codes [G][T] (pass
+ * out = NULL to query T).  INVALID_INPUT if no codec tokens were generated. */
+q3t_status q3t_session_codes(q3t_session *s, int64_t *out, int *num_frames);
+/* SessionImpl::finish (execution/loaded_model.rs:112-152) without the
+ * voice-clone prefix: codec-decodes the generated codes; wave (nullable)
+ * receives f32 samples, pcm (nullable) the i16 PCM of Waveform::to_pcm. */
+q3t_status q3t_session_finish(q3t_session *s, float *wave, int16_t *pcm,
+                              int64_t capacity, int64_t *num_samples);
+/* Isolated talker decode step (decode_step + codec_head, infer/mod.rs:
+ * 410-432 and 268-273): inputs_embeds [hidden] at position = cache length;
+ * appends K/V; writes logits [vocab] and hidden [hidden] (nullable). */
+q3t_status q3t_session_decode_embeds(q3t_session *s, const float *inputs_embeds,
+                                     float *logits, float *hidden);
+/* Test hook: overwrite the talker KV cache with `len` positions of bf16 K/V,
+ * k/v laid out [num_layers][num_kv_heads][len][head_dim] (bit patterns),
+ * and set the session's current hidden state [hidden] (nullable). */
+q3t_status q3t_session_load_kv(q3t_session *s, const uint16_t *k, const uint16_t *v,
+                               int len, const float *hidden);
+/* Device time (ms) of the last step / decode call on this session. */
+q3t_status q3t_session_last_ms(q3t_session *s, float *ms);
+void q3t_session_free(q3t_session *s);
+
+/* Codec decode (decode_waveform, codec/infer/mod.rs:94-111): codes
+ * [B][num_quantizers][T] -> wave [B][n] f32 clamped to [-1, 1] and/or pcm
+ * [B][n] i16 (to_pcm, :80-90).  *n = samples per item = (((4T-1)*8-1)*5-1)...
+ * for the default config (the transposed convs trim k - stride from both
+ * ends, conv.rs:19-31).  Codes outside [0, codebook_size) are INVALID_INPUT. */
+q3t_status q3t_codec_decode(q3t_model *model, const int64_t *codes, int B, int T,
+                            float *wave, int16_t *pcm, int64_t *n);
+q3t_status q3t_codec_out_len(const q3t_model *model, int T, int64_t *n);
+
+/* ------------------------ ragged continuous batching --------------------- */
+typedef struct {
+  int max_active;            /* <= model max_active */
+  int codec_mode;            /* 0: none, 1: full-sequence decode at retire
+                                (reference semantics), 2: chunked streaming */
+  int chunk_frames;          /* codec_mode 2: frames emitted per chunk */
+  int left_context;          /* codec_mode 2: frames of left context per chunk */
+  int keep_output;           /* 1: keep codes/PCM for q3t_batch_take */
+} q3t_batch_desc;
+
+typedef struct {
+  int active;                /* requests in the decode step */
+  int admitted;              /* requests prefilled this step */
+  int retired;               /* requests finished this step */
+  int64_t frames;            /* frames generated this step */
+  int64_t samples;           /* PCM samples emitted this step */
+  float device_ms;           /* device time of this step (CUDA events) */
+} q3t_step_stats;
+
+typedef struct q3t_batch q3t_batch;
+
+q3t_status q3t_batch_create(q3t_model *model, const q3t_batch_desc *desc, q3t_batch **out);
+/* Queue a request; forced_codes (nullable) [max_new_tokens][G] teacher-forces
+ * every frame (then EOS is ignored and the request runs max_new_tokens). */
+q3t_status q3t_batch_submit(q3t_batch *b, const q3t_session_desc *req,
+                            const int64_t *forced_codes, int64_t *request_id);
+/* One scheduler iteration: admit + prefill queued requests into free slots,
+ * one decode frame for every active request, retire finished ones (codec
+ * decode per codec_mode). */
+q3t_status q3t_batch_step(q3t_batch *b, q3t_step_stats *stats);
+/* state: 0 queued, 1 active, 2 finished, 3 failed */
+q3t_status q3t_batch_poll(q3t_batch *b, int64_t request_id, int *state, int64_t *frames,
+                          int64_t *samples);
+/* Copy out (and release) a finished request's codes [G][T], the tokens the
+ * sampler picked before teacher forcing replaced them (sampled [G][T], for
+ * argmax-agreement checks; nullable) and its samples (codec_mode 1/2). */
+q3t_status q3t_batch_take(q3t_batch *b, int64_t request_id, int64_t *codes, int32_t *sampled,
+                          int max_frames, float *wave, int64_t max_samples);
+q3t_status q3t_batch_pending(q3t_batch *b, int *queued, int *active);
+void q3t_batch_free(q3t_batch *b);
+
+/* ------------------------------- misc ----------------------------------- */
+const char *q3t_last_error(void);
+const char *q3t_version(void);
+/* Number of kernel launches this thread has issued into the library's
+ * streams since load (graph replays count their kernel nodes). */
+int64_t q3t_kernel_launches(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* Q3T_H */

@@ -546,7 +546,11 @@ int orc_gen_step(orc_gen *g, const int64_t *forced, const float *u,
     g->finished = 1;
     return 0;
   }
-  int64_t code0 = forced ? forced[0] : g->selected;
+  int64_t code0 = g->selected;
+  if (forced) { /* teacher forcing replaces the token where it was sampled */
+    code0 = forced[0];
+    g->hist[g->step_idx] = code0;
+  }
   int64_t *codes = g->codes + (size_t)g->step_idx * G;
   predict_frame_with(m, g->pkv, g->hidden, code0, &g->cs, forced, u, codes, cp_logits);
   float *emb = (float *)malloc((size_t)H * sizeof(float));

@@ -1,0 +1,275 @@
+"""Talker / code-predictor parity: CUDA path (through the C ABI) vs the CPU
+oracle on the same seeded weights and teacher-forced inputs.
+
+Tolerance (floating point, bf16 weights): logits within |gpu - ref| <=
+2e-2 + 1e-2 * |ref| element-wise, and >= 99.5 % argmax agreement.  Token
+bookkeeping (codes, page tables) is compared exactly.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+import q3t
+import synthetic as S
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL, ARGMAX_AGREE = 2e-2, 1e-2, 0.995
+
+
+def assert_close(gpu, ref, what):
+    gpu, ref = np.asarray(gpu, np.float64), np.asarray(ref, np.float64)
+    err = np.abs(gpu - ref)
+    bad = err > ATOL + RTOL * np.abs(ref)
+    assert not bad.any(), f"{what}: {bad.sum()} of {bad.size} outside tolerance, max err {err.max():.3e}"
+
+
+def argmax_agreement(gpu_rows, ref_rows):
+    g = np.asarray(gpu_rows).reshape(-1, np.asarray(gpu_rows).shape[-1]).argmax(-1)
+    r = np.asarray(ref_rows).reshape(-1, np.asarray(ref_rows).shape[-1]).argmax(-1)
+    return float((g == r).mean())
+
+
+@pytest.fixture(scope="module")
+def small():
+    cfg = S.TalkerConfig().small(talker_layers=2, predictor_layers=5)
+    w = S.make_talker_weights(cfg, seed=0)
+    model = q3t.Model(cfg, w, kv_pages=2048, max_active=8)
+    yield cfg, w, model, O.OracleTalker(cfg, w)
+    model.close()
+
+
+def _random_kv(cfg, L, seed):
+    c = cfg.talker
+    g = np.random.default_rng([seed, 5])
+    k = g.standard_normal((c.n_layers, c.n_kv, L, c.head_dim), dtype=np.float32)
+    v = g.standard_normal((c.n_layers, c.n_kv, L, c.head_dim), dtype=np.float32)
+    return S.bf16_round(k), S.bf16_round(v)
+
+
+def _decode_vs_oracle(cfg, w, model, ot, L, seed=0):
+    k, v = _random_kv(cfg, L, seed)
+    prompt, trailing, pad = S.synthetic_talker_inputs(cfg, 1, seed)
+    sess = model.session(prompt, trailing, pad, max_new_tokens=4)
+    sess.load_kv(S.bf16_bits(k), S.bf16_bits(v), L)
+    emb = np.random.default_rng([seed, 9]).standard_normal(cfg.talker.hidden).astype(np.float32)
+    logits, hidden = sess.decode_embeds(emb)
+    kvs, mems = ot.make_caches("talker", cap=L + 8)
+    for l in range(cfg.talker.n_layers):
+        mems[l][0][:, :L] = k[l]
+        mems[l][1][:, :L] = v[l]
+        kvs[l].len = L
+    ref_h = ot.stack_forward("talker", kvs, emb[None])[0]
+    ref_logits = ot.codec_head(ref_h)[0]
+    sess.close()
+    return logits, hidden, ref_logits, ref_h
+
+
+def test_decode_step_small_matches_oracle(small):
+    cfg, w, model, ot = small
+    logits, hidden, ref_logits, ref_h = _decode_vs_oracle(cfg, w, model, ot, L=100)
+    assert_close(hidden, ref_h, "hidden")
+    assert_close(logits, ref_logits, "logits")
+    assert logits.argmax() == ref_logits.argmax()
+
+
+@pytest.mark.parametrize("L", [1, 15, 16, 17, 64, 65, 300])
+def test_decode_step_kv_lengths(small, L):
+    cfg, w, model, ot = small
+    logits, hidden, ref_logits, ref_h = _decode_vs_oracle(cfg, w, model, ot, L=L, seed=L)
+    assert_close(logits, ref_logits, f"logits L={L}")
+
+
+def test_session_teacher_forced_matches_oracle(small):
+    cfg, w, model, ot = small
+    S_len, frames = 9, 6
+    prompt, trailing, pad = S.synthetic_talker_inputs(cfg, S_len, seed=1)
+    trailing = np.concatenate([trailing, trailing * 0.5, trailing * -0.25])  # 3 trailing rows
+    codes = S.teacher_codes(frames + 1, seed=1)
+    sess = model.session(prompt, trailing, pad, max_new_tokens=frames + 1, forced_first=int(codes[0, 0]),
+                         first_logits=True)
+    og = O.OracleGenerator(ot, prompt, trailing, pad, max_new_tokens=frames + 1,
+                           forced_first=int(codes[0, 0]))
+    assert_close(sess.first_logits, og.first_logits, "first logits")
+    tl_all, otl_all, pl_all, opl_all = [], [], [], []
+    for f in range(frames):
+        st, tl, pl, hid = sess.step_forced(codes[f])
+        r, otl, opl, ohid = og.step(forced=codes[f])
+        assert st == 1 and r == 1
+        assert_close(pl, opl, f"predictor logits frame {f}")
+        assert_close(hid, ohid, f"hidden frame {f}")
+        assert_close(tl, otl, f"talker logits frame {f}")
+        tl_all.append(tl); otl_all.append(otl); pl_all.append(pl); opl_all.append(opl)
+    assert argmax_agreement(np.array(pl_all), np.array(opl_all)) >= ARGMAX_AGREE
+    assert argmax_agreement(np.array(tl_all), np.array(otl_all)) >= ARGMAX_AGREE
+    # the frame limit: one more forced step finishes (infer/mod.rs:235-238)
+    st, *_ = sess.step_forced(codes[frames])
+    assert st == 2
+    assert sess.step() == 0
+    got = sess.codes()
+    np.testing.assert_array_equal(got, codes[:frames + 1].T)
+    np.testing.assert_array_equal(got, og.codes())
+    sess.close()
+
+
+def test_session_errors(small):
+    cfg, w, model, ot = small
+    prompt, trailing, pad = S.synthetic_talker_inputs(cfg, 4)
+    with pytest.raises(q3t.Q3TError) as e:
+        model.session(prompt, trailing, pad, max_new_tokens=0)
+    assert e.value.status == q3t.INVALID_INPUT
+    with pytest.raises(q3t.Q3TError) as e:
+        model.session(prompt, trailing[:0], pad, max_new_tokens=2)
+    assert e.value.status == q3t.INVALID_INPUT
+    # EOS as the first token -> "EOS before any audio codec token" on step
+    s = model.session(prompt, trailing, pad, max_new_tokens=3, eos=7, forced_first=7)
+    with pytest.raises(q3t.Q3TError) as e:
+        s.step()
+    assert e.value.status == q3t.INVALID_INPUT and "EOS" in str(e.value)
+    s.close()
+    s = model.session(prompt, trailing, pad, max_new_tokens=3)
+    with pytest.raises(q3t.Q3TError):
+        s.codes()  # no codec tokens were generated
+    with pytest.raises(q3t.Q3TError):
+        s.step_forced(np.full(cfg.n_groups, 5000, np.int64))
+    s.close()
+
+
+def test_suppress_list_applies_to_first_token_only(small):
+    cfg, w, model, ot = small
+    prompt, trailing, pad = S.synthetic_talker_inputs(cfg, 5, seed=3)
+    s0 = model.session(prompt, trailing, pad, max_new_tokens=2, first_logits=True)
+    top = int(s0.first_logits.argmax())
+    s0.close()
+    sup = np.array([top], np.int64)
+    s1 = model.session(prompt, trailing, pad, max_new_tokens=2, suppress=sup, first_logits=True)
+    ref = O.lib().orc_sample_token(O.fp(s1.first_logits), cfg.talker.vocab, O.sampling(), O.ip(sup), 1, 0.5)
+    s1.step()
+    assert int(s1.codes()[0, 0]) == ref != top
+    s1.close()
+
+
+def test_greedy_session_matches_oracle(small):
+    cfg, w, model, ot = small
+    prompt, trailing, pad = S.synthetic_talker_inputs(cfg, 6, seed=4)
+    sess = model.session(prompt, trailing, pad, max_new_tokens=3)
+    og = O.OracleGenerator(ot, prompt, trailing, pad, max_new_tokens=3)
+    while sess.step() == 1:
+        pass
+    while og.step()[0] == 1:
+        pass
+    g, r = sess.codes(), og.codes()
+    assert g.shape == r.shape
+    assert (g == r).mean() >= 0.95, (g, r)
+    sess.close()
+
+
+def test_repetition_penalty_matches_oracle(small):
+    cfg, w, model, ot = small
+    prompt, trailing, pad = S.synthetic_talker_inputs(cfg, 5, seed=6)
+    ts = q3t.sampling(repetition_penalty=1.3)
+    cs = q3t.sampling(repetition_penalty=1.1)
+    codes = S.teacher_codes(4, seed=6)
+    codes[1, 0] = codes[0, 0]  # a repeated talker token
+    codes[2, 3] = codes[2, 1]  # a repeated predictor code
+    sess = model.session(prompt, trailing, pad, talker_sampling=ts, predictor_sampling=cs,
+                         max_new_tokens=8, forced_first=int(codes[0, 0]))
+    og = O.OracleGenerator(ot, prompt, trailing, pad, talker_s=O.sampling(repetition_penalty=1.3),
+                           cp_s=O.sampling(repetition_penalty=1.1), max_new_tokens=8,
+                           forced_first=int(codes[0, 0]))
+    for f in range(3):
+        st, tl, pl, _ = sess.step_forced(codes[f])
+        r, otl, opl, _ = og.step(forced=codes[f])
+        assert_close(pl, opl, f"penalised predictor logits {f}")
+        assert_close(tl, otl, f"penalised talker logits {f}")
+    sess.close()
+
+
+def test_batch_ragged_matches_oracle_argmax(small):
+    """Three requests of different prompt lengths and frame counts share the
+    batched step; every sampled token (before teacher forcing) must agree
+    with the oracle's argmax on the same teacher-forced inputs."""
+    cfg, w, model, ot = small
+    b = model.batch(max_active=4)
+    specs = [(5, 4, 10), (17, 6, 11), (33, 3, 12)]
+    ids, refs = [], []
+    for S_len, frames, seed in specs:
+        prompt, trailing, pad = S.synthetic_talker_inputs(cfg, S_len, seed=seed)
+        codes = S.teacher_codes(frames, seed=seed)
+        ids.append(b.submit(prompt, trailing, pad, frames, forced=codes))
+        og = O.OracleGenerator(ot, prompt, trailing, pad, max_new_tokens=frames,
+                               forced_first=int(codes[0, 0]))
+        samp = np.zeros((cfg.n_groups, frames), np.int64)
+        samp[0, 0] = og.first_logits.argmax()
+        for f in range(frames):
+            r, otl, opl, _ = og.step(forced=codes[f])
+            samp[1:, f] = opl.argmax(-1)
+            if f + 1 < frames:
+                samp[0, f + 1] = otl.argmax()
+        refs.append((codes, samp))
+    for _ in range(50):
+        st = b.step()
+        if st["active"] == 0 and b.pending() == (0, 0):
+            break
+    agree, total = 0, 0
+    for rid, (codes, samp) in zip(ids, refs):
+        state, T, _ = b.poll(rid)
+        assert state == 2 and T == codes.shape[0]
+        got, sampled, _ = b.take(rid)
+        np.testing.assert_array_equal(got, codes.T)
+        agree += (sampled == samp).sum()
+        total += samp.size
+    assert agree / total >= ARGMAX_AGREE, agree / total
+    b.close()
+
+
+def test_kernel_launches_are_counted(small):
+    cfg, w, model, ot = small
+    n0 = q3t.kernel_launches()
+    prompt, trailing, pad = S.synthetic_talker_inputs(cfg, 3)
+    s = model.session(prompt, trailing, pad, max_new_tokens=2)
+    s.step()
+    s.close()
+    assert q3t.kernel_launches() > n0
+
+
+@pytest.fixture(scope="module")
+def full():
+    cfg = S.TalkerConfig()
+    w = S.make_talker_weights(cfg, seed=0)
+    model = q3t.Model(cfg, w, kv_pages=1024, max_active=2)
+    yield cfg, w, model, O.OracleTalker(cfg, w)
+    model.close()
+
+
+def test_full_decode_step_l1024_matches_oracle(full):
+    """The isolated 28-layer talker decode step at KV length 1024."""
+    cfg, w, model, ot = full
+    logits, hidden, ref_logits, ref_h = _decode_vs_oracle(cfg, w, model, ot, L=1024, seed=2)
+    assert_close(hidden, ref_h, "hidden")
+    assert_close(logits, ref_logits, "logits")
+    assert logits.argmax() == ref_logits.argmax()
+
+
+def test_full_pipeline_teacher_forced(full):
+    """28-layer talker + 5-layer predictor, 64-token prompt, teacher-forced
+    frames: per-frame talker and predictor logits vs the oracle."""
+    cfg, w, model, ot = full
+    frames = 8
+    prompt, trailing, pad = S.synthetic_talker_inputs(cfg, 64, seed=0)
+    codes = S.teacher_codes(frames + 1, seed=0)
+    sess = model.session(prompt, trailing, pad, max_new_tokens=frames + 1, forced_first=int(codes[0, 0]),
+                         first_logits=True)
+    og = O.OracleGenerator(ot, prompt, trailing, pad, max_new_tokens=frames + 1,
+                           forced_first=int(codes[0, 0]))
+    assert_close(sess.first_logits, og.first_logits, "first logits")
+    P, OP, T, OT = [], [], [], []
+    for f in range(frames):
+        st, tl, pl, hid = sess.step_forced(codes[f])
+        r, otl, opl, ohid = og.step(forced=codes[f])
+        assert_close(pl, opl, f"predictor logits frame {f}")
+        assert_close(tl, otl, f"talker logits frame {f}")
+        P.append(pl); OP.append(opl); T.append(tl); OT.append(otl)
+    assert argmax_agreement(np.array(P), np.array(OP)) >= ARGMAX_AGREE
+    assert argmax_agreement(np.array(T), np.array(OT)) >= ARGMAX_AGREE
+    sess.close()

@@ -1,0 +1,74 @@
+// Shared device helpers for the sm_100a kernels.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define Q3T_DEV __device__ __forceinline__
+
+namespace q3t {
+
+using bf16 = __nv_bfloat16;
+
+Q3T_DEV float bf2f(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+Q3T_DEV uint16_t f2bf(float f) {
+  bf16 h = __float2bfloat16_rn(f);
+  return *reinterpret_cast<uint16_t *>(&h);
+}
+Q3T_DEV uint32_t pack_bf16x2(float lo, float hi) {
+  return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
+}
+Q3T_DEV float bf16_round(float f) { return bf2f(f2bf(f)); }
+
+// Programmatic dependent launch: everything before pdl_wait() may only read
+// data no earlier kernel writes (weights); pdl_wait() returns once the
+// preceding grid has completed and its memory is visible.  Both are no-ops
+// when the kernel was launched without the PDL attribute.
+Q3T_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+Q3T_DEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Streaming 16-byte load that does not allocate in L1 (weights are read once).
+Q3T_DEV uint4 ldg_stream(const uint4 *p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// D = A * B + D, m16n8k16, bf16 inputs, f32 accumulators.
+Q3T_DEV void mma_16816(float *c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                       uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+Q3T_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+Q3T_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum for blockDim.x <= 1024 (uses 33 floats of smem).
+Q3T_DEV float block_sum(float v, float *red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  float r = lane < nw ? red[lane] : 0.f;
+  r = warp_sum(r);
+  return r;
+}
+
+Q3T_DEV float silu(float x) { return x / (1.f + expf(-x)); }
+
+}  // namespace q3t

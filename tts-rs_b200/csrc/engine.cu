@@ -1,0 +1,1201 @@
+// Host runtime of the B200 Qwen3-TTS hot path: model load (bf16 cast +
+// fragment packing), paged KV pools, the ragged batch engine (admission,
+// prefill, one CUDA-graph-replayed decode frame per step, retirement) and
+// the C ABI of include/q3t.h.
+//
+// The per-request state machine mirrors TalkerGenerator
+// (tts_qwen3_tts/src/model/talker/infer/mod.rs:69-311): start = prefill +
+// first sample with the suppress list; step = code predictor (15 codebooks)
+// -> codec-group embedding (+ trailing text / pad) -> push codes -> stop at
+// max_new_tokens -> talker decode -> codec_head -> repetition penalty ->
+// sample -> EOS check; finalize = codes [G][T].
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <deque>
+#include <memory>
+#include <mutex>
+
+#include "codec.cuh"
+#include "engine.h"
+#include "lm_kernels.cuh"
+
+namespace q3t {
+
+thread_local std::string g_err;
+thread_local int64_t g_thread_launch_base = 0;
+
+void set_error(const char *fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+}
+
+template <class F>
+static q3t_status guard(F &&f) {
+  try {
+    f();
+    return Q3T_OK;
+  } catch (const Status &s) {
+    return s.code;
+  } catch (const CudaFail &c) {
+    set_error("CUDA error %s (%s) in %s", cudaGetErrorName(c.err), cudaGetErrorString(c.err),
+              c.what.c_str());
+    return Q3T_CUDA_ERROR;
+  } catch (const std::bad_alloc &) {
+    set_error("host allocation failed");
+    return Q3T_CUDA_ERROR;
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Weight upload
+// ----------------------------------------------------------------------------
+struct Tensors {
+  std::map<std::string, const q3t_tensor *> m;
+  explicit Tensors(const q3t_model_desc *d) {
+    for (int i = 0; i < d->num_tensors; i++)
+      if (d->tensors[i].name) m[d->tensors[i].name] = &d->tensors[i];
+  }
+  const q3t_tensor *get(const std::string &name, std::vector<int64_t> shape) const {
+    auto it = m.find(name);
+    if (it == m.end()) FAIL(Q3T_RUNTIME_LOAD, "missing tensor %s", name.c_str());
+    const q3t_tensor *t = it->second;
+    int64_t n1 = 1, n2 = 1;
+    for (int i = 0; i < t->ndim; i++) n1 *= t->shape[i];
+    for (auto s : shape) n2 *= s;
+    bool ok = n1 == n2 && t->data && (t->dtype == Q3T_F32 || t->dtype == Q3T_BF16);
+    if (ok && t->ndim == (int)shape.size())
+      for (int i = 0; i < t->ndim; i++) ok = ok && t->shape[i] == shape[i];
+    if (!ok) FAIL(Q3T_RUNTIME_LOAD, "tensor %s has an unexpected shape, dtype or no data", name.c_str());
+    return t;
+  }
+};
+
+static int64_t numel(const q3t_tensor *t) {
+  int64_t n = 1;
+  for (int i = 0; i < t->ndim; i++) n *= t->shape[i];
+  return n;
+}
+
+// host tensor -> device bf16 row-major (temporary unless arena given)
+static uint16_t *to_dev_bf16(const q3t_tensor *t, DevArena *ar, cudaStream_t st) {
+  const int64_t n = numel(t);
+  uint16_t *d;
+  if (ar)
+    d = ar->alloc<uint16_t>(n);
+  else
+    CK(cudaMalloc(&d, n * 2));
+  if (t->dtype == Q3T_BF16) {
+    CK(cudaMemcpy(d, t->data, n * 2, cudaMemcpyHostToDevice));
+  } else {
+    float *tmp;
+    CK(cudaMalloc(&tmp, n * 4));
+    CK(cudaMemcpy(tmp, t->data, n * 4, cudaMemcpyHostToDevice));
+    f32_to_bf16(tmp, d, n, st);
+    CK(cudaStreamSynchronize(st));
+    CK(cudaFree(tmp));
+  }
+  return d;
+}
+
+float *upload_f32(const q3t_tensor *t, DevArena &ar) {
+  const int64_t n = numel(t);
+  float *d = ar.alloc<float>(n);
+  if (t->dtype == Q3T_F32) {
+    CK(cudaMemcpy(d, t->data, n * 4, cudaMemcpyHostToDevice));
+  } else {
+    std::vector<float> h(n);
+    const uint16_t *s = reinterpret_cast<const uint16_t *>(t->data);
+    for (int64_t i = 0; i < n; i++) {
+      uint32_t u = (uint32_t)s[i] << 16;
+      memcpy(&h[i], &u, 4);
+    }
+    CK(cudaMemcpy(d, h.data(), n * 4, cudaMemcpyHostToDevice));
+  }
+  return d;
+}
+
+uint16_t *upload_bf16(const q3t_tensor *t, DevArena &ar, cudaStream_t st) {
+  return to_dev_bf16(t, &ar, st);
+}
+
+// pack W [N][K] into dst (fragment order) at element offset
+static void pack_into(const q3t_tensor *t, uint16_t *dst, int N, int K, cudaStream_t st) {
+  if (N % 16 || K % 64) FAIL(Q3T_RUNTIME_LOAD, "linear %s: dims %d x %d not multiples of 16/64", t->name, N, K);
+  uint16_t *tmp = to_dev_bf16(t, nullptr, st);
+  pack_weight(tmp, dst, N, K, st);
+  CK(cudaStreamSynchronize(st));
+  CK(cudaFree(tmp));
+}
+
+static void load_stack(q3t_model *m, LMStack &S, const q3t_lm_config &c, const std::string &prefix,
+                       const Tensors &T, cudaStream_t st) {
+  S.cfg = c;
+  const int H = c.hidden_size, I = c.intermediate_size, nh = c.num_attention_heads,
+            nkv = c.num_key_value_heads, hd = c.head_dim;
+  if (hd != 128) FAIL(Q3T_INVALID_INPUT, "%s: head_dim %d unsupported (kernels are built for 128)", prefix.c_str(), hd);
+  if (H % 256 || I % 256) FAIL(Q3T_INVALID_INPUT, "%s: hidden/intermediate must be multiples of 256", prefix.c_str());
+  if (nh != 2 * nkv) FAIL(Q3T_INVALID_INPUT, "%s: kernels are built for 2 query heads per kv head", prefix.c_str());
+  auto &ar = m->arena;
+  for (int l = 0; l < c.num_hidden_layers; l++) {
+    const std::string p = prefix + ".layers." + std::to_string(l);
+    S.in_norm.push_back(upload_f32(T.get(p + ".input_layernorm.weight", {H}), ar));
+    S.post_norm.push_back(upload_f32(T.get(p + ".post_attention_layernorm.weight", {H}), ar));
+    S.q_norm.push_back(upload_f32(T.get(p + ".self_attn.q_norm.weight", {hd}), ar));
+    S.k_norm.push_back(upload_f32(T.get(p + ".self_attn.k_norm.weight", {hd}), ar));
+    const int Nq = nh * hd, Nk = nkv * hd;
+    uint16_t *qkv = ar.alloc<uint16_t>((size_t)(Nq + 2 * Nk) * H);
+    pack_into(T.get(p + ".self_attn.q_proj.weight", {Nq, H}), qkv, Nq, H, st);
+    pack_into(T.get(p + ".self_attn.k_proj.weight", {Nk, H}), qkv + (size_t)Nq * H, Nk, H, st);
+    pack_into(T.get(p + ".self_attn.v_proj.weight", {Nk, H}), qkv + (size_t)(Nq + Nk) * H, Nk, H, st);
+    S.wqkv.push_back(qkv);
+    uint16_t *wo = ar.alloc<uint16_t>((size_t)H * Nq);
+    pack_into(T.get(p + ".self_attn.o_proj.weight", {H, Nq}), wo, H, Nq, st);
+    S.wo.push_back(wo);
+    uint16_t *gu = ar.alloc<uint16_t>((size_t)2 * I * H);
+    pack_into(T.get(p + ".mlp.gate_proj.weight", {I, H}), gu, I, H, st);
+    pack_into(T.get(p + ".mlp.up_proj.weight", {I, H}), gu + (size_t)I * H, I, H, st);
+    S.wgu.push_back(gu);
+    uint16_t *wd = ar.alloc<uint16_t>((size_t)H * I);
+    pack_into(T.get(p + ".mlp.down_proj.weight", {H, I}), wd, H, I, st);
+    S.wdown.push_back(wd);
+  }
+  S.final_norm = upload_f32(T.get(prefix + ".norm.weight", {H}), ar);
+  // rope.rs:21-24: inv_freq[i] = 1 / theta^(i / half), computed in f32 on the host
+  std::vector<float> inv(hd / 2);
+  for (int i = 0; i < hd / 2; i++) inv[i] = 1.0f / powf(c.rope_theta, (float)i / (float)(hd / 2));
+  S.inv_freq = ar.alloc<float>(hd / 2);
+  CK(cudaMemcpy(S.inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice));
+}
+
+}  // namespace q3t
+
+using namespace q3t;
+
+extern "C" q3t_status q3t_model_load(const q3t_model_desc *desc, q3t_model **out) {
+  if (!desc || !out) {
+    set_error("q3t_model_load: null argument");
+    return Q3T_INVALID_INPUT;
+  }
+  *out = nullptr;
+  auto *m = new q3t_model();
+  q3t_status rc = guard([&] {
+    CK(cudaSetDevice(desc->device));
+    m->device = desc->device;
+    m->tc = desc->talker;
+    m->cc = desc->codec;
+    m->has_talker = desc->has_talker != 0;
+    m->has_codec = desc->has_codec != 0;
+    m->kv_pages = desc->kv_pages > 0 ? desc->kv_pages : 8192;
+    m->max_active = desc->max_active > 0 ? desc->max_active : 64;
+    if (m->max_active > 64) FAIL(Q3T_INVALID_INPUT, "max_active %d > 64", m->max_active);
+    init_kernel_attributes();
+    cudaStream_t st;
+    CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    Tensors T(desc);
+    if (m->has_talker) {
+      const auto &tc = m->tc;
+      const int G = tc.num_code_groups;
+      if (G < 2 || G > 32) FAIL(Q3T_INVALID_INPUT, "num_code_groups %d unsupported", G);
+      if (tc.predictor.hidden_size != tc.talker.hidden_size)
+        FAIL(Q3T_INVALID_INPUT, "code predictor hidden %d != talker hidden %d (small_to_mtp_projection unsupported)",
+             tc.predictor.hidden_size, tc.talker.hidden_size);
+      if (tc.talker.vocab_size > 4096 || tc.predictor.vocab_size > 4096 || tc.talker.vocab_size % 64 ||
+          tc.predictor.vocab_size % 64)
+        FAIL(Q3T_INVALID_INPUT, "vocab sizes must be multiples of 64 and <= 4096");
+      load_stack(m, m->talker, tc.talker, "talker.model", T, st);
+      load_stack(m, m->pred, tc.predictor, "talker.code_predictor.model", T, st);
+      const int H = tc.talker.hidden_size, V = tc.talker.vocab_size, PV = tc.predictor.vocab_size;
+      m->codec_head = m->arena.alloc<uint16_t>((size_t)V * H);
+      pack_into(T.get("talker.codec_head.weight", {V, H}), m->codec_head, V, H, st);
+      m->talker_emb = upload_bf16(T.get("talker.model.codec_embedding.weight", {V, H}), m->arena, st);
+      for (int j = 0; j < G - 1; j++) {
+        m->cp_emb.push_back(upload_bf16(
+            T.get("talker.code_predictor.model.codec_embedding." + std::to_string(j) + ".weight", {PV, H}),
+            m->arena, st));
+        uint16_t *lh = m->arena.alloc<uint16_t>((size_t)PV * H);
+        pack_into(T.get("talker.code_predictor.lm_head." + std::to_string(j) + ".weight", {PV, H}), lh, PV,
+                  H, st);
+        m->lm_heads.push_back(lh);
+      }
+      m->cp_emb_dev = m->arena.alloc<uint16_t *>(G - 1);
+      CK(cudaMemcpy(m->cp_emb_dev, m->cp_emb.data(), (G - 1) * sizeof(uint16_t *), cudaMemcpyHostToDevice));
+    }
+    if (m->has_codec) m->codec = codec_load(m, desc, st);
+    CK(cudaStreamSynchronize(st));
+    CK(cudaStreamDestroy(st));
+  });
+  if (rc != Q3T_OK) {
+    q3t_model_free(m);
+    return rc;
+  }
+  *out = m;
+  return Q3T_OK;
+}
+
+extern "C" void q3t_model_free(q3t_model *m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  if (m->codec) codec_free(m->codec);
+  delete m;
+}
+
+// ----------------------------------------------------------------------------
+// Batch engine
+// ----------------------------------------------------------------------------
+namespace q3t {
+
+}  // namespace q3t
+
+namespace q3t {
+
+static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
+  b->m = m;
+  b->desc = d;
+  const auto &tc = m->tc;
+  b->A = d.max_active;
+  b->G = tc.num_code_groups;
+  b->H = tc.talker.hidden_size;
+  b->V = tc.talker.vocab_size;
+  b->PV = tc.predictor.vocab_size;
+  b->NQKV = (tc.talker.num_attention_heads + 2 * tc.talker.num_key_value_heads) * 128;
+  b->NQKVP = (tc.predictor.num_attention_heads + 2 * tc.predictor.num_key_value_heads) * 128;
+  b->I2 = 2 * std::max(tc.talker.intermediate_size, tc.predictor.intermediate_size);
+  const char *g = getenv("Q3T_GRAPHS");
+  b->use_graphs = !(g && g[0] == '0');
+  CK(cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking));
+  CK(cudaEventCreate(&b->ev0));
+  CK(cudaEventCreate(&b->ev1));
+  auto &ar = b->ar;
+  const int A = b->A;
+  // talker KV pool
+  const int nkv = tc.talker.num_key_value_heads, L = tc.talker.num_hidden_layers;
+  b->n_pages = (int)std::min<int64_t>(m->kv_pages, (int64_t)A * kPtStride);
+  b->t_layer_stride = (int64_t)b->n_pages * nkv * kPage * 128;
+  b->tk = ar.alloc<uint16_t>((size_t)b->t_layer_stride * L);
+  b->tv = ar.alloc<uint16_t>((size_t)b->t_layer_stride * L);
+  for (int p = b->n_pages - 1; p >= 0; p--) b->free_pages.push_back(p);
+  b->h_pt.assign((size_t)A * kPtStride, 0);
+  b->d_pt = ar.zalloc<int>((size_t)A * kPtStride);
+  // predictor pool: slot s owns pages 2s, 2s+1 (capacity 32 >= num_code_groups + 1)
+  const int pnkv = tc.predictor.num_key_value_heads, PL = tc.predictor.num_hidden_layers;
+  b->p_layer_stride = (int64_t)2 * A * pnkv * kPage * 128;
+  b->pk = ar.alloc<uint16_t>((size_t)b->p_layer_stride * PL);
+  b->pv = ar.alloc<uint16_t>((size_t)b->p_layer_stride * PL);
+  {
+    std::vector<int> ppt((size_t)A * 2);
+    for (int s = 0; s < A; s++) ppt[2 * s] = 2 * s, ppt[2 * s + 1] = 2 * s + 1;
+    b->d_ppt = ar.alloc<int>(ppt.size());
+    CK(cudaMemcpy(b->d_ppt, ppt.data(), ppt.size() * 4, cudaMemcpyHostToDevice));
+  }
+  // slot state
+  b->maxF = kMaxSeq;
+  b->hist_cap = kMaxSeq + 1;
+  const int G = b->G, H = b->H;
+  b->d_codes = ar.zalloc<int64_t>((size_t)A * G);
+  b->d_hist_codes = ar.zalloc<int64_t>((size_t)A * b->maxF * G);
+  b->d_forced = ar.zalloc<int64_t>((size_t)A * b->maxF * G);
+  b->d_forced_count = ar.zalloc<int>(A);
+  b->d_raw = ar.zalloc<int32_t>((size_t)A * b->maxF * G);
+  b->d_eos = ar.zalloc<int64_t>(A);
+  b->d_suppress = ar.zalloc<int64_t>(b->n_suppress_cap);
+  b->d_hidden = ar.zalloc<float>((size_t)A * H);
+  b->d_thist = ar.zalloc<int32_t>((size_t)A * b->hist_cap);
+  b->d_thist_len = ar.zalloc<int>(A);
+  b->d_sup_on = ar.zalloc<int>(A);
+  b->d_params = ar.zalloc<SampleParams>((size_t)A * 2);
+  // activations: up to 2A tokens (predictor prefill) or one prefill chunk
+  b->Tmax = std::max(2 * A, kPrefillTok);
+  const int T = b->Tmax;
+  b->x = ar.zalloc<float>((size_t)T * H);
+  b->xn = ar.zalloc<uint16_t>((size_t)T * H);
+  b->qkv = ar.zalloc<float>((size_t)T * std::max(b->NQKV, b->NQKVP));
+  b->q = ar.zalloc<uint16_t>((size_t)T * 128 * std::max(tc.talker.num_attention_heads, tc.predictor.num_attention_heads));
+  b->attn = ar.zalloc<uint16_t>((size_t)T * 128 * std::max(tc.talker.num_attention_heads, tc.predictor.num_attention_heads));
+  b->gu = ar.zalloc<float>((size_t)T * b->I2);
+  b->tlog = ar.zalloc<float>((size_t)T * b->V);
+  b->plog = ar.zalloc<float>((size_t)(G - 1) * A * b->PV);
+  b->ws.max_split = kMaxSplit;
+  const int mkv = std::max(nkv, pnkv);
+  b->ws.part = ar.zalloc<float>((size_t)T * mkv * kMaxSplit * 2 * 132);
+  b->ws.counters = ar.zalloc<int>((size_t)T * mkv);
+  // metadata
+  b->meta_n = M_HDR + 8 * A;
+  b->d_meta = ar.zalloc<int>(b->meta_n);
+  CK(cudaMallocHost(&b->h_meta, b->meta_n * sizeof(int)));
+  memset(b->h_meta, 0, b->meta_n * sizeof(int));
+  b->d_extra = ar.zalloc<const float *>(A);
+  CK(cudaMallocHost(&b->h_extra, A * sizeof(float *)));
+  const int nchunks = kMaxSeq / kPrefillTok;
+  b->d_pmeta = ar.zalloc<int>((size_t)nchunks * b->pmeta_stride());
+  CK(cudaMallocHost(&b->h_pmeta, (size_t)nchunks * b->pmeta_stride() * sizeof(int)));
+  b->d_eosflag = ar.zalloc<int>(T);
+  CK(cudaMallocHost(&b->h_eosflag, T * sizeof(int)));
+  CK(cudaMallocHost(&b->h_codes, (size_t)A * G * sizeof(int64_t)));
+  b->slots.assign(A, nullptr);
+  CK(cudaStreamSynchronize(b->st));
+}
+
+static void batch_destroy(q3t_batch *b) {
+  for (auto &kv : b->graphs) cudaGraphExecDestroy(kv.second.exec);
+  b->graphs.clear();
+  for (auto &r : b->reqs) {
+    if (r.second->d_trailing) cudaFree(r.second->d_trailing);
+    if (r.second->d_pad) cudaFree(r.second->d_pad);
+  }
+  if (b->h_meta) cudaFreeHost(b->h_meta);
+  if (b->h_extra) cudaFreeHost(b->h_extra);
+  if (b->h_pmeta) cudaFreeHost(b->h_pmeta);
+  if (b->h_eosflag) cudaFreeHost(b->h_eosflag);
+  if (b->h_codes) cudaFreeHost(b->h_codes);
+  if (b->ev0) cudaEventDestroy(b->ev0);
+  if (b->ev1) cudaEventDestroy(b->ev1);
+  if (b->st) cudaStreamDestroy(b->st);
+  b->ar.release();
+}
+
+template <class F>
+static void run_graph(q3t_batch *b, std::tuple<int, int, int> key, F &&body) {
+  if (!b->use_graphs) {
+    body();
+    return;
+  }
+  auto it = b->graphs.find(key);
+  if (it == b->graphs.end()) {
+    const int64_t l0 = g_launches;
+    CK(cudaStreamBeginCapture(b->st, cudaStreamCaptureModeThreadLocal));
+    body();
+    cudaGraph_t graph = nullptr;
+    cudaError_t e = cudaStreamEndCapture(b->st, &graph);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      b->use_graphs = false;
+      g_launches = l0;
+      body();
+      return;
+    }
+    GraphEntry ge;
+    ge.nodes = g_launches - l0;
+    g_launches = l0;
+    CK(cudaGraphInstantiate(&ge.exec, graph, 0));
+    cudaGraphDestroy(graph);
+    it = b->graphs.emplace(key, ge).first;
+  }
+  CK(cudaGraphLaunch(it->second.exec, b->st));
+  g_launches += it->second.nodes;
+}
+
+static int bucket_tok(int B) {
+  if (B <= 1) return 1;
+  int n = 8;
+  while (n < B) n <<= 1;
+  return n;
+}
+static int bucket_split(int L) {
+  int s = (L + kChunk - 1) / kChunk, n = 1;
+  while (n < s) n <<= 1;
+  return n;
+}
+
+// One decoder stack over the token batch described by tv.
+static void run_stack(q3t_batch *b, const LMStack &S, KVView kv, TokView tv, int max_tok, bool fused,
+                      int max_split) {
+  const auto &c = S.cfg;
+  const int H = c.hidden_size, I = c.intermediate_size, nh = c.num_attention_heads,
+            nkv = c.num_key_value_heads;
+  const int NQ = (nh + 2 * nkv) * 128, QD = nh * 128;
+  for (int l = 0; l < c.num_hidden_layers; l++) {
+    rmsnorm(b->x, H, 1, 0, S.in_norm[l], b->xn, H, H, c.rms_norm_eps, tv.ntok, max_tok, b->qkv, NQ, NQ,
+            nullptr, nullptr, b->st);
+    linear(S.wqkv[l], NQ, H, b->xn, H, 0, b->qkv, NQ, tv.ntok, max_tok, b->st);
+    if (!fused)
+      qkv_post(b->qkv, NQ, S.q_norm[l], S.k_norm[l], S.inv_freq, c.rms_norm_eps, nh, nkv, tv, max_tok,
+               b->q, kv, l, b->st);
+    attention(fused ? 1 : 0, b->qkv, NQ, S.q_norm[l], S.k_norm[l], S.inv_freq, c.rms_norm_eps, b->q, kv, l,
+              tv, max_tok, nh, kChunk, max_split, b->ws, b->attn, b->st);
+    linear(S.wo[l], H, QD, b->attn, QD, 0, b->x, H, tv.ntok, max_tok, b->st);
+    rmsnorm(b->x, H, 1, 0, S.post_norm[l], b->xn, H, H, c.rms_norm_eps, tv.ntok, max_tok, b->gu, 2 * I,
+            2 * I, nullptr, nullptr, b->st);
+    linear(S.wgu[l], 2 * I, H, b->xn, H, 0, b->gu, 2 * I, tv.ntok, max_tok, b->st);
+    linear(S.wdown[l], H, I, b->gu, 2 * I, 1, b->x, H, tv.ntok, max_tok, b->st);
+  }
+}
+
+static KVView talker_kv(q3t_batch *b) {
+  return KVView{b->tk, b->tv, b->t_layer_stride, b->d_pt, kPtStride,
+                b->m->tc.talker.num_key_value_heads};
+}
+static KVView pred_kv(q3t_batch *b) {
+  return KVView{b->pk, b->pv, b->p_layer_stride, b->d_ppt, 2, b->m->tc.predictor.num_key_value_heads};
+}
+
+static SampleArgs base_sample(q3t_batch *b) {
+  SampleArgs a{};
+  a.params = b->d_params;
+  a.codes = b->d_codes;
+  a.G = b->G;
+  a.forced = b->d_forced;
+  a.force_on = b->d_forced_count;
+  a.max_frames = b->maxF;
+  a.hist = b->d_thist;
+  a.hist_len = b->d_thist_len;
+  a.hist_cap = b->hist_cap;
+  a.eos = b->d_eos;
+  a.raw = b->d_raw;
+  return a;
+}
+
+// The decode frame for the B active requests described by the step metadata.
+static void enqueue_frame(q3t_batch *b, int mt, int max_split, int step_seed) {
+  q3t_model *m = b->m;
+  const auto &tc = m->tc;
+  const int G = b->G, H = b->H, PV = b->PV, V = b->V;
+  int *meta = b->d_meta;
+  const int *ntokB = meta + M_NTOK_B, *ntok2B = meta + M_NTOK_2B;
+  const int *slot = meta + b->off_slot(), *frame = meta + b->off_frame();
+  // ---- code predictor (infer/mod.rs:434-535) ----
+  pred_input0(b->d_hidden, m->talker_emb, b->d_codes, G, slot, ntokB, mt, H, b->x, b->st);
+  TokView tv0{ntok2B, meta + b->off_p0seq(), meta + b->off_p0pos(), 0};
+  run_stack(b, m->pred, pred_kv(b), tv0, 2 * mt, false, 1);
+  const auto &pc = tc.predictor;
+  for (int j = 0; j < G - 1; j++) {
+    if (j > 0) {
+      pred_input(m->cp_emb[j - 1], b->d_codes, G, j, slot, ntokB, mt, H, b->x, b->st);
+      TokView tvj{ntokB, slot, meta + b->off_zero(), j + 1};
+      run_stack(b, m->pred, pred_kv(b), tvj, mt, true, 1);
+    }
+    float *lg = b->plog + (size_t)j * b->A * PV;
+    rmsnorm(b->x, H, j == 0 ? 2 : 1, j == 0 ? 1 : 0, m->pred.final_norm, b->xn, H, H, pc.rms_norm_eps, ntokB,
+            mt, lg, PV, PV, nullptr, nullptr, b->st);
+    linear(m->lm_heads[j], PV, H, b->xn, H, 0, lg, PV, ntokB, mt, b->st);
+    SampleArgs a = base_sample(b);
+    a.logits = lg;
+    a.ldl = PV;
+    a.V = PV;
+    a.ntok = ntokB;
+    a.slot = slot;
+    a.use_pred_params = 1;
+    a.col = j + 1;
+    a.frame = frame;
+    a.fadd = 0;
+    a.hist_mode = 2;
+    a.step_seed = step_seed;
+    sample(a, mt, b->st);
+  }
+  // ---- next talker input: codec-group embedding + trailing text / pad ----
+  embed_codes(m->talker_emb, (const uint16_t *const *)m->cp_emb_dev, G, H, b->d_codes, slot, b->d_extra, frame,
+              b->d_hist_codes, b->maxF, ntokB, mt, b->x, b->st);
+  // ---- talker decode (model.rs:94-113) + codec_head + sample ----
+  TokView tvt{ntokB, slot, meta + b->off_tpos(), 0};
+  run_stack(b, m->talker, talker_kv(b), tvt, mt, true, max_split);
+  rmsnorm(b->x, H, 1, 0, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps, ntokB, mt, b->tlog, V, V,
+          b->d_hidden, slot, b->st);
+  linear(m->codec_head, V, H, b->xn, H, 0, b->tlog, V, ntokB, mt, b->st);
+  SampleArgs a = base_sample(b);
+  a.logits = b->tlog;
+  a.ldl = V;
+  a.V = V;
+  a.ntok = ntokB;
+  a.slot = slot;
+  a.use_pred_params = 0;
+  a.col = 0;
+  a.frame = frame;
+  a.fadd = 1;
+  a.hist_mode = 1;
+  a.eos_flag = b->d_eosflag;
+  a.step_seed = step_seed + 1;
+  sample(a, mt, b->st);
+}
+
+static int alloc_page(q3t_batch *b, Req *r) {
+  if (b->free_pages.empty()) return -1;
+  const int p = b->free_pages.back();
+  b->free_pages.pop_back();
+  const int idx = (int)r->pages.size();
+  r->pages.push_back(p);
+  b->h_pt[(size_t)r->slot * kPtStride + idx] = p;
+  CK(cudaMemcpyAsync(b->d_pt + (size_t)r->slot * kPtStride + idx, &b->h_pt[(size_t)r->slot * kPtStride + idx],
+                     sizeof(int), cudaMemcpyHostToDevice, b->st));
+  return p;
+}
+
+static bool ensure_pages(q3t_batch *b, Req *r, int len) {
+  const int need = (len + kPage - 1) / kPage;
+  if (need > kPtStride) return false;
+  while ((int)r->pages.size() < need)
+    if (alloc_page(b, r) < 0) return false;
+  return true;
+}
+
+static void release(q3t_batch *b, Req *r) {
+  for (int p : r->pages) b->free_pages.push_back(p);
+  r->pages.clear();
+  if (r->slot >= 0) b->slots[r->slot] = nullptr;
+  r->slot = -1;
+  if (r->d_trailing) cudaFree(r->d_trailing);
+  if (r->d_pad) cudaFree(r->d_pad);
+  r->d_trailing = r->d_pad = nullptr;
+}
+
+static SampleParams to_params(const q3t_sampling &s) {
+  SampleParams p{};
+  p.do_sample = s.do_sample;
+  p.temperature = s.temperature;
+  p.top_k = s.top_k;
+  p.top_p = s.top_p;
+  const float rp = s.repetition_penalty;
+  p.rep_penalty = (std::isfinite(rp) && rp > 0.f && std::fabs(rp - 1.f) > 1.1920929e-7f) ? rp : 0.f;
+  p.seed = s.seed;
+  return p;
+}
+
+// TalkerGenerator::start: prefill the prompt into the request's pages, then
+// codec_head + first sample with the suppress list (infer/mod.rs:135-157).
+static void prefill(q3t_batch *b, Req *r) {
+  q3t_model *m = b->m;
+  const auto &tc = m->tc;
+  const int H = b->H, V = b->V, s = r->slot;
+  if (!ensure_pages(b, r, r->S)) FAIL(Q3T_OUT_OF_PAGES, "KV page pool exhausted (prompt of %d tokens)", r->S);
+  // per-slot state
+  SampleParams pp[2] = {to_params(r->ts), to_params(r->cs)};
+  CK(cudaMemcpyAsync(b->d_params + 2 * s, pp, sizeof pp, cudaMemcpyHostToDevice, b->st));
+  CK(cudaMemcpyAsync(b->d_eos + s, &r->eos, sizeof(int64_t), cudaMemcpyHostToDevice, b->st));
+  const int zero = 0, one = 1;
+  CK(cudaMemcpyAsync(b->d_thist_len + s, &zero, sizeof(int), cudaMemcpyHostToDevice, b->st));
+  const int nsup = std::min<int>((int)r->suppress.size(), b->n_suppress_cap);
+  if (nsup) CK(cudaMemcpyAsync(b->d_suppress, r->suppress.data(), nsup * 8, cudaMemcpyHostToDevice, b->st));
+  CK(cudaMemcpyAsync(b->d_sup_on + s, nsup ? &one : &zero, sizeof(int), cudaMemcpyHostToDevice, b->st));
+  const int fc = r->forced.empty() ? 0 : r->max_new;
+  CK(cudaMemcpyAsync(b->d_forced_count + s, &fc, sizeof(int), cudaMemcpyHostToDevice, b->st));
+  if (fc)
+    CK(cudaMemcpyAsync(b->d_forced + (size_t)s * b->maxF * b->G, r->forced.data(), r->forced.size() * 8,
+                       cudaMemcpyHostToDevice, b->st));
+  CK(cudaMalloc(&r->d_trailing, (size_t)r->trailing_len * H * 4));
+  CK(cudaMalloc(&r->d_pad, (size_t)H * 4));
+  CK(cudaMemcpyAsync(r->d_trailing, r->trailing.data(), r->trailing.size() * 4, cudaMemcpyHostToDevice, b->st));
+  CK(cudaMemcpyAsync(r->d_pad, r->pad.data(), r->pad.size() * 4, cudaMemcpyHostToDevice, b->st));
+  float *d_prompt;
+  CK(cudaMallocAsync((void **)&d_prompt, (size_t)r->S * H * 4, b->st));
+  CK(cudaMemcpyAsync(d_prompt, r->prompt.data(), r->prompt.size() * 4, cudaMemcpyHostToDevice, b->st));
+  // chunks of kPrefillTok tokens; each token attends to [0, pos] (causal by position)
+  const int nch = (r->S + kPrefillTok - 1) / kPrefillTok;
+  const int ps = b->pmeta_stride();
+  int last_n = 0;
+  for (int c = 0; c < nch; c++) {
+    const int c0 = c * kPrefillTok, n = std::min(kPrefillTok, r->S - c0);
+    int *hm = b->h_pmeta + (size_t)c * ps;
+    hm[0] = n;
+    hm[1] = 1;
+    hm[2] = s;
+    for (int i = 0; i < n; i++) {
+      hm[8 + i] = s;
+      hm[8 + kPrefillTok + i] = c0 + i;
+    }
+    int *dm = b->d_pmeta + (size_t)c * ps;
+    CK(cudaMemcpyAsync(dm, hm, ps * sizeof(int), cudaMemcpyHostToDevice, b->st));
+    CK(cudaMemcpyAsync(b->x, d_prompt + (size_t)c0 * H, (size_t)n * H * 4, cudaMemcpyDeviceToDevice, b->st));
+    TokView tv{dm, dm + 8, dm + 8 + kPrefillTok, 0};
+    run_stack(b, m->talker, talker_kv(b), tv, n, false, bucket_split(c0 + n));
+    last_n = n;
+  }
+  CK(cudaFreeAsync(d_prompt, b->st));
+  int *dm = b->d_pmeta + (size_t)(nch - 1) * ps;
+  // final norm of the last prompt token -> hidden[slot] and codec_head input
+  rmsnorm(b->x, H, 1, last_n - 1, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps, dm + 1, 1, b->tlog,
+          V, V, b->d_hidden, dm + 2, b->st);
+  linear(m->codec_head, V, H, b->xn, H, 0, b->tlog, V, dm + 1, 1, b->st);
+  if (r->first_logits)
+    CK(cudaMemcpyAsync(r->first_logits, b->tlog, (size_t)V * 4, cudaMemcpyDeviceToHost, b->st));
+  SampleArgs a = base_sample(b);
+  a.logits = b->tlog;
+  a.ldl = V;
+  a.V = V;
+  a.ntok = dm + 1;
+  a.slot = dm + 2;
+  a.use_pred_params = 0;
+  a.suppress = b->d_suppress;
+  a.n_suppress = nsup;
+  a.sup_on = b->d_sup_on;
+  a.col = 0;
+  a.forced = nullptr;
+  a.hist_mode = 1;
+  a.eos_flag = b->d_eosflag;
+  a.frame = dm + 2;
+  a.raw = nullptr;
+  sample(a, 1, b->st);
+  // teacher forcing of the first token replaces it where it was sampled
+  CK(cudaMemcpyAsync(b->h_codes, b->d_codes + (size_t)s * b->G, 8, cudaMemcpyDeviceToHost, b->st));
+  CK(cudaStreamSynchronize(b->st));
+  const int64_t raw_first = b->h_codes[0];
+  int64_t ff = r->forced_first;
+  if (ff < 0 && !r->forced.empty()) ff = r->forced[0];
+  if (ff >= 0) {
+    const int32_t f32v = (int32_t)ff;
+    CK(cudaMemcpyAsync(b->d_codes + (size_t)s * b->G, &ff, 8, cudaMemcpyHostToDevice, b->st));
+    CK(cudaMemcpyAsync(b->d_thist + (size_t)s * b->hist_cap, &f32v, 4, cudaMemcpyHostToDevice, b->st));
+  }
+  CK(cudaMemcpyAsync(b->h_codes, b->d_codes + (size_t)s * b->G, 8, cudaMemcpyDeviceToHost, b->st));
+  CK(cudaStreamSynchronize(b->st));
+  r->first_token = b->h_codes[0];
+  r->first_token_raw = raw_first;
+  r->eos_seen = r->eos >= 0 && r->first_token == r->eos;
+  r->cache_len = r->S;
+  r->step_idx = 0;
+}
+
+static void admit(q3t_batch *b, int *admitted) {
+  while (!b->queue.empty()) {
+    int s = -1;
+    for (int i = 0; i < b->A; i++)
+      if (!b->slots[i]) {
+        s = i;
+        break;
+      }
+    if (s < 0) break;
+    Req *r = b->queue.front();
+    const int need = (r->S + kPage - 1) / kPage + 1;
+    if ((int)b->free_pages.size() < need) break;  // wait for pages
+    b->queue.pop_front();
+    r->slot = s;
+    b->slots[s] = r;
+    r->state = 1;
+    try {
+      prefill(b, r);
+    } catch (const Status &st) {
+      r->state = 3;
+      r->error = g_err;
+      release(b, r);
+      continue;
+    }
+    if (admitted) (*admitted)++;
+  }
+}
+
+static void retire(q3t_batch *b, Req *r, int64_t *samples) {
+  const int T = r->step_idx, G = b->G;
+  std::vector<int64_t> tg((size_t)T * G);
+  if (T > 0)
+    CK(cudaMemcpy(tg.data(), b->d_hist_codes + (size_t)r->slot * b->maxF * G, tg.size() * 8,
+                  cudaMemcpyDeviceToHost));
+  std::vector<int32_t> rg((size_t)T * G);
+  if (T > 0)
+    CK(cudaMemcpy(rg.data(), b->d_raw + (size_t)r->slot * b->maxF * G, rg.size() * 4, cudaMemcpyDeviceToHost));
+  r->codes.assign((size_t)G * T, 0);
+  r->sampled.assign((size_t)G * T, 0);
+  for (int t = 0; t < T; t++)
+    for (int q = 0; q < G; q++) {
+      r->codes[(size_t)q * T + t] = tg[(size_t)t * G + q];
+      r->sampled[(size_t)q * T + t] = rg[(size_t)t * G + q];
+    }
+  r->sampled[0] = (int32_t)r->first_token_raw;
+  if (b->desc.codec_mode == 1 && b->m->has_codec && T > 0) {
+    int64_t n = 0;
+    codec_out_len(b->m->codec, T, &n);
+    if (b->desc.keep_output) r->wave.resize(n);
+    codec_decode_host_codes(b->m, r->codes.data(), 1, T, b->desc.keep_output ? r->wave.data() : nullptr,
+                            nullptr, b->st);
+    r->samples = n;
+    if (samples) *samples += n;
+  }
+  if (!b->desc.keep_output && !b->session_mode) r->codes.clear();
+  r->state = 2;
+  release(b, r);
+}
+
+static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
+  q3t_step_stats S{};
+  admit(b, &S.admitted);
+  std::vector<Req *> act;
+  for (int i = 0; i < b->A; i++) {
+    Req *r = b->slots[i];
+    if (!r) continue;
+    if (r->finished) continue;
+    if (r->eos_seen) {  // infer/mod.rs:197-204
+      if (r->step_idx == 0) {
+        r->state = 3;
+        r->error = "talker emitted EOS before any audio codec token";
+        release(b, r);
+      } else {
+        r->finished = true;
+        retire(b, r, &S.samples);
+        S.retired++;
+      }
+      continue;
+    }
+    act.push_back(r);
+  }
+  const int B = (int)act.size();
+  S.active = B;
+  if (B == 0) {
+    if (stats) *stats = S;
+    return;
+  }
+  int maxlen = 1;
+  int *hm = b->h_meta;
+  for (int i = 0; i < B; i++) {
+    Req *r = act[i];
+    if (r->cache_len + 1 > kMaxSeq || r->step_idx >= b->maxF || !ensure_pages(b, r, r->cache_len + 1)) {
+      // the reference slides its 4096-entry window here (kv.rs:109-132); this
+      // build stops the request with an explicit error instead
+      FAIL(Q3T_OUT_OF_PAGES, "request %lld: KV capacity exhausted at %d tokens", (long long)r->id, r->cache_len);
+    }
+    hm[b->off_slot() + i] = r->slot;
+    hm[b->off_tpos() + i] = r->cache_len;
+    hm[b->off_frame() + i] = r->step_idx;
+    hm[b->off_zero() + i] = 0;
+    hm[b->off_p0seq() + 2 * i] = hm[b->off_p0seq() + 2 * i + 1] = r->slot;
+    hm[b->off_p0pos() + 2 * i] = 0;
+    hm[b->off_p0pos() + 2 * i + 1] = 1;
+    b->h_extra[i] = r->step_idx < r->trailing_len ? r->d_trailing + (size_t)r->step_idx * b->H : r->d_pad;
+    maxlen = std::max(maxlen, r->cache_len + 1);
+  }
+  hm[M_NTOK_B] = B;
+  hm[M_NTOK_2B] = 2 * B;
+  hm[M_ONE] = 1;
+  CK(cudaMemcpyAsync(b->d_meta, hm, b->meta_n * sizeof(int), cudaMemcpyHostToDevice, b->st));
+  CK(cudaMemcpyAsync(b->d_extra, b->h_extra, B * sizeof(float *), cudaMemcpyHostToDevice, b->st));
+  const int mt = bucket_tok(B), ms = bucket_split(maxlen);
+  const int seed = act[0]->step_idx;
+  CK(cudaEventRecord(b->ev0, b->st));
+  run_graph(b, std::make_tuple(0, mt, ms), [&] { enqueue_frame(b, mt, ms, seed); });
+  CK(cudaEventRecord(b->ev1, b->st));
+  CK(cudaMemcpyAsync(b->h_eosflag, b->d_eosflag, B * sizeof(int), cudaMemcpyDeviceToHost, b->st));
+  CK(cudaStreamSynchronize(b->st));
+  CK(cudaEventElapsedTime(&b->last_ms, b->ev0, b->ev1));
+  S.device_ms = b->last_ms;
+  for (int i = 0; i < B; i++) {
+    Req *r = act[i];
+    r->step_idx++;
+    S.frames++;
+    if (r->step_idx >= r->max_new) {
+      r->finished = true;
+    } else {
+      r->cache_len++;
+      if (r->forced.empty() && b->h_eosflag[i]) {
+        r->eos_seen = true;
+        r->finished = true;
+      }
+    }
+  }
+  if (b->desc.codec_mode == 2 && b->m->has_codec) codec_stream_step(b->m, b, act, &S.samples);
+  for (Req *r : act)
+    if (r->finished) {
+      retire(b, r, &S.samples);
+      S.retired++;
+    }
+  if (stats) *stats = S;
+}
+
+static Req *new_request(q3t_batch *b, const q3t_session_desc *d, const int64_t *forced) {
+  const auto &tc = b->m->tc;
+  const int H = tc.talker.hidden_size;
+  if (d->max_new_tokens <= 0) FAIL(Q3T_INVALID_INPUT, "talker max_new_tokens must be greater than zero");
+  if (!d->inputs_embeds || d->prompt_len <= 0) FAIL(Q3T_INVALID_INPUT, "prompt must be non-empty");
+  if (!d->trailing_text || d->trailing_len <= 0 || !d->pad_embed)
+    FAIL(Q3T_INVALID_INPUT,
+         "generation side input length mismatch: trailing length must be > 0 and pad length must be 1");
+  if (d->prompt_len + 1 > kMaxSeq) FAIL(Q3T_INVALID_INPUT, "prompt of %d tokens exceeds %d", d->prompt_len, kMaxSeq);
+  if (d->max_new_tokens > kMaxSeq) FAIL(Q3T_INVALID_INPUT, "max_new_tokens %d exceeds %d", d->max_new_tokens, kMaxSeq);
+  if (d->num_suppress > b->n_suppress_cap) FAIL(Q3T_INVALID_INPUT, "too many suppress ids");
+  auto r = std::make_unique<Req>();
+  r->id = b->next_id++;
+  r->S = d->prompt_len;
+  r->prompt.assign(d->inputs_embeds, d->inputs_embeds + (size_t)d->prompt_len * H);
+  r->trailing_len = d->trailing_len;
+  r->trailing.assign(d->trailing_text, d->trailing_text + (size_t)d->trailing_len * H);
+  r->pad.assign(d->pad_embed, d->pad_embed + H);
+  r->ts = d->talker_sampling;
+  r->cs = d->predictor_sampling;
+  r->max_new = d->max_new_tokens;
+  r->eos = d->eos_token_id;
+  if (d->suppress_ids && d->num_suppress > 0) r->suppress.assign(d->suppress_ids, d->suppress_ids + d->num_suppress);
+  r->forced_first = d->forced_first_token;
+  r->first_logits = d->first_logits;
+  const int G = b->G;
+  if (forced) {
+    r->forced.assign(forced, forced + (size_t)d->max_new_tokens * G);
+    for (int f = 0; f < d->max_new_tokens; f++)
+      for (int q = 0; q < G; q++) {
+        const int64_t c = r->forced[(size_t)f * G + q];
+        const int lim = q == 0 ? tc.talker.vocab_size : tc.predictor.vocab_size;
+        if (c < 0 || c >= lim) FAIL(Q3T_INVALID_INPUT, "forced code %lld out of range at frame %d group %d", (long long)c, f, q);
+      }
+  }
+  if (r->forced_first >= tc.talker.vocab_size) FAIL(Q3T_INVALID_INPUT, "forced first token out of range");
+  for (auto id : r->suppress)
+    if (id < 0) FAIL(Q3T_INVALID_INPUT, "negative suppress id");
+  Req *raw = r.get();
+  b->reqs[raw->id] = std::move(r);
+  return raw;
+}
+
+}  // namespace q3t
+
+// ----------------------------------------------------------------------------
+// C ABI: batches
+// ----------------------------------------------------------------------------
+extern "C" q3t_status q3t_batch_create(q3t_model *m, const q3t_batch_desc *d, q3t_batch **out) {
+  if (!m || !d || !out) {
+    set_error("q3t_batch_create: null argument");
+    return Q3T_INVALID_INPUT;
+  }
+  *out = nullptr;
+  if (!m->has_talker) {
+    set_error("model has no talker");
+    return Q3T_INVALID_INPUT;
+  }
+  if (d->max_active <= 0 || d->max_active > m->max_active) {
+    set_error("max_active %d outside 1..%d", d->max_active, m->max_active);
+    return Q3T_INVALID_INPUT;
+  }
+  if (d->codec_mode < 0 || d->codec_mode > 2 || (d->codec_mode && !m->has_codec)) {
+    set_error("codec_mode %d unsupported by this model", d->codec_mode);
+    return Q3T_INVALID_INPUT;
+  }
+  auto *b = new q3t_batch();
+  q3t_status rc = guard([&] {
+    CK(cudaSetDevice(m->device));
+    batch_init(b, m, *d);
+    if (d->codec_mode == 2) codec_stream_init(m, b);
+  });
+  if (rc != Q3T_OK) {
+    batch_destroy(b);
+    delete b;
+    return rc;
+  }
+  *out = b;
+  return Q3T_OK;
+}
+
+extern "C" q3t_status q3t_batch_submit(q3t_batch *b, const q3t_session_desc *req, const int64_t *forced,
+                                       int64_t *id) {
+  if (!b || !req) {
+    set_error("q3t_batch_submit: null argument");
+    return Q3T_INVALID_INPUT;
+  }
+  return guard([&] {
+    Req *r = new_request(b, req, forced);
+    b->queue.push_back(r);
+    if (id) *id = r->id;
+  });
+}
+
+extern "C" q3t_status q3t_batch_step(q3t_batch *b, q3t_step_stats *stats) {
+  if (!b) {
+    set_error("q3t_batch_step: null batch");
+    return Q3T_INVALID_INPUT;
+  }
+  return guard([&] {
+    CK(cudaSetDevice(b->m->device));
+    batch_step(b, stats);
+  });
+}
+
+extern "C" q3t_status q3t_batch_poll(q3t_batch *b, int64_t id, int *state, int64_t *frames, int64_t *samples) {
+  if (!b) return Q3T_INVALID_INPUT;
+  auto it = b->reqs.find(id);
+  if (it == b->reqs.end()) {
+    set_error("unknown request %lld", (long long)id);
+    return Q3T_INVALID_INPUT;
+  }
+  Req *r = it->second.get();
+  if (state) *state = r->state;
+  if (frames) *frames = r->step_idx;
+  if (samples) *samples = r->samples;
+  if (r->state == 3) set_error("%s", r->error.c_str());
+  return Q3T_OK;
+}
+
+extern "C" q3t_status q3t_batch_take(q3t_batch *b, int64_t id, int64_t *codes, int32_t *sampled,
+                                     int max_frames, float *wave, int64_t max_samples) {
+  if (!b) return Q3T_INVALID_INPUT;
+  auto it = b->reqs.find(id);
+  if (it == b->reqs.end()) {
+    set_error("unknown request %lld", (long long)id);
+    return Q3T_INVALID_INPUT;
+  }
+  Req *r = it->second.get();
+  if (r->state != 2) {
+    set_error("request %lld is not finished", (long long)id);
+    return Q3T_INVALID_INPUT;
+  }
+  const int T = r->step_idx, G = b->G;
+  if (codes) {
+    if (max_frames < T || (int64_t)r->codes.size() != (int64_t)G * T) {
+      set_error("codes unavailable or buffer too small (%d frames)", T);
+      return Q3T_INVALID_INPUT;
+    }
+    memcpy(codes, r->codes.data(), r->codes.size() * 8);
+  }
+  if (sampled) {
+    if (max_frames < T || (int64_t)r->sampled.size() != (int64_t)G * T) {
+      set_error("sampled codes unavailable or buffer too small (%d frames)", T);
+      return Q3T_INVALID_INPUT;
+    }
+    memcpy(sampled, r->sampled.data(), r->sampled.size() * 4);
+  }
+  if (wave) {
+    if ((int64_t)r->wave.size() > max_samples) {
+      set_error("wave buffer too small (%lld samples)", (long long)r->wave.size());
+      return Q3T_INVALID_INPUT;
+    }
+    memcpy(wave, r->wave.data(), r->wave.size() * 4);
+  }
+  b->reqs.erase(it);
+  return Q3T_OK;
+}
+
+extern "C" q3t_status q3t_batch_pending(q3t_batch *b, int *queued, int *active) {
+  if (!b) return Q3T_INVALID_INPUT;
+  int a = 0;
+  for (auto *r : b->slots) a += r != nullptr;
+  if (queued) *queued = (int)b->queue.size();
+  if (active) *active = a;
+  return Q3T_OK;
+}
+
+extern "C" void q3t_batch_free(q3t_batch *b) {
+  if (!b) return;
+  cudaSetDevice(b->m->device);
+  if (b->desc.codec_mode == 2) codec_stream_free(b);
+  batch_destroy(b);
+  delete b;
+}
+
+// ----------------------------------------------------------------------------
+// C ABI: sessions (batch of one, reference TalkerGenerator semantics)
+// ----------------------------------------------------------------------------
+struct q3t_session {
+  q3t_batch *b = nullptr;
+  q3t::Req *r = nullptr;
+};
+
+extern "C" q3t_status q3t_session_start(q3t_model *m, const q3t_session_desc *d, q3t_session **out) {
+  if (!m || !d || !out) {
+    set_error("q3t_session_start: null argument");
+    return Q3T_INVALID_INPUT;
+  }
+  *out = nullptr;
+  q3t_batch_desc bd{};
+  bd.max_active = 1;
+  bd.codec_mode = 0;
+  bd.keep_output = 1;
+  q3t_batch *b = nullptr;
+  q3t_status rc = q3t_batch_create(m, &bd, &b);
+  if (rc != Q3T_OK) return rc;
+  b->session_mode = true;
+  auto *s = new q3t_session();
+  s->b = b;
+  rc = guard([&] {
+    s->r = new_request(b, d, nullptr);
+    b->queue.push_back(s->r);
+    admit(b, nullptr);
+    if (s->r->state == 3) FAIL(Q3T_INVALID_INPUT, "%s", s->r->error.c_str());
+  });
+  if (rc != Q3T_OK) {
+    q3t_batch_free(b);
+    delete s;
+    return rc;
+  }
+  *out = s;
+  return Q3T_OK;
+}
+
+static q3t_status session_step(q3t_session *s, const int64_t *forced, float *tl, float *pl, float *hid,
+                               int *state) {
+  if (!s) {
+    set_error("null session");
+    return Q3T_INVALID_INPUT;
+  }
+  q3t_batch *b = s->b;
+  Req *r = s->r;
+  return guard([&] {
+    CK(cudaSetDevice(b->m->device));
+    if (state) *state = 0;
+    if (r->state == 2 || r->finished) return;  // Ok(None)
+    if (r->state == 3) FAIL(Q3T_INVALID_INPUT, "%s", r->error.c_str());
+    if (r->eos_seen) {
+      if (r->step_idx == 0) {
+        r->state = 3;
+        r->error = "talker emitted EOS before any audio codec token";
+        FAIL(Q3T_INVALID_INPUT, "talker emitted EOS before any audio codec token");
+      }
+      r->finished = true;
+      r->state = 2;
+      return;
+    }
+    const int G = b->G, sl = r->slot, f = r->step_idx;
+    if (forced) {
+      for (int q = 0; q < G; q++) {
+        const int lim = q == 0 ? b->V : b->PV;
+        if (forced[q] < 0 || forced[q] >= lim) FAIL(Q3T_INVALID_INPUT, "forced code out of range");
+      }
+      CK(cudaMemcpyAsync(b->d_forced + ((size_t)sl * b->maxF + f) * G, forced, G * 8, cudaMemcpyHostToDevice, b->st));
+      const int fc = f + 1;
+      CK(cudaMemcpyAsync(b->d_forced_count + sl, &fc, 4, cudaMemcpyHostToDevice, b->st));
+      const int32_t c0 = (int32_t)forced[0];
+      CK(cudaMemcpyAsync(b->d_codes + (size_t)sl * G, forced, 8, cudaMemcpyHostToDevice, b->st));
+      CK(cudaMemcpyAsync(b->d_thist + (size_t)sl * b->hist_cap + f, &c0, 4, cudaMemcpyHostToDevice, b->st));
+    }
+    batch_step(b, nullptr);
+    if (tl) CK(cudaMemcpy(tl, b->tlog, (size_t)b->V * 4, cudaMemcpyDeviceToHost));
+    if (pl)
+      for (int j = 0; j < G - 1; j++)
+        CK(cudaMemcpy(pl + (size_t)j * b->PV, b->plog + (size_t)j * b->A * b->PV, (size_t)b->PV * 4,
+                      cudaMemcpyDeviceToHost));
+    if (hid) CK(cudaMemcpy(hid, b->d_hidden + (size_t)sl * b->H, (size_t)b->H * 4, cudaMemcpyDeviceToHost));
+    if (state) *state = r->finished ? 2 : 1;
+  });
+}
+
+extern "C" q3t_status q3t_session_step(q3t_session *s, int *state) {
+  return session_step(s, nullptr, nullptr, nullptr, nullptr, state);
+}
+
+extern "C" q3t_status q3t_session_step_forced(q3t_session *s, const int64_t *codes, float *tl, float *pl,
+                                              float *hid, int *state) {
+  if (!codes) {
+    set_error("q3t_session_step_forced: null codes");
+    return Q3T_INVALID_INPUT;
+  }
+  return session_step(s, codes, tl, pl, hid, state);
+}
+
+extern "C" q3t_status q3t_session_codes(q3t_session *s, int64_t *out, int *num_frames) {
+  if (!s) return Q3T_INVALID_INPUT;
+  return guard([&] {
+    q3t_batch *b = s->b;
+    Req *r = s->r;
+    const int T = r->step_idx, G = b->G;
+    if (num_frames) *num_frames = T;
+    if (T == 0) FAIL(Q3T_INVALID_INPUT, "no codec tokens were generated");
+    if (!out) return;
+    if ((int)r->codes.size() == G * T) {
+      memcpy(out, r->codes.data(), r->codes.size() * 8);
+      return;
+    }
+    std::vector<int64_t> tg((size_t)T * G);
+    CK(cudaMemcpy(tg.data(), b->d_hist_codes + (size_t)r->slot * b->maxF * G, tg.size() * 8,
+                  cudaMemcpyDeviceToHost));
+    for (int t = 0; t < T; t++)
+      for (int q = 0; q < G; q++) out[(size_t)q * T + t] = tg[(size_t)t * G + q];
+  });
+}
+
+extern "C" q3t_status q3t_session_finish(q3t_session *s, float *wave, int16_t *pcm, int64_t capacity,
+                                         int64_t *num_samples) {
+  if (!s) return Q3T_INVALID_INPUT;
+  return guard([&] {
+    q3t_batch *b = s->b;
+    if (!b->m->has_codec) FAIL(Q3T_INVALID_INPUT, "model has no codec");
+    int T = 0;
+    q3t_status rc = q3t_session_codes(s, nullptr, &T);
+    if (rc != Q3T_OK) throw Status{rc, ""};
+    std::vector<int64_t> codes((size_t)b->G * T);
+    rc = q3t_session_codes(s, codes.data(), &T);
+    if (rc != Q3T_OK) throw Status{rc, ""};
+    int64_t n = 0;
+    codec_out_len(b->m->codec, T, &n);
+    if (num_samples) *num_samples = n;
+    if ((wave || pcm) && capacity < n) FAIL(Q3T_INVALID_INPUT, "output buffer holds %lld samples, need %lld",
+                                            (long long)capacity, (long long)n);
+    codec_decode_host_codes(b->m, codes.data(), 1, T, wave, pcm, b->st);
+  });
+}
+
+extern "C" q3t_status q3t_session_decode_embeds(q3t_session *s, const float *embeds, float *logits,
+                                                float *hidden) {
+  if (!s || !embeds) {
+    set_error("q3t_session_decode_embeds: null argument");
+    return Q3T_INVALID_INPUT;
+  }
+  return guard([&] {
+    q3t_batch *b = s->b;
+    Req *r = s->r;
+    q3t_model *m = b->m;
+    CK(cudaSetDevice(m->device));
+    if (r->slot < 0) FAIL(Q3T_INVALID_INPUT, "session is finished");
+    if (r->cache_len + 1 > kMaxSeq || !ensure_pages(b, r, r->cache_len + 1))
+      FAIL(Q3T_OUT_OF_PAGES, "KV capacity exhausted at %d tokens", r->cache_len);
+    int *hm = b->h_meta;
+    hm[b->off_slot()] = r->slot;
+    hm[b->off_tpos()] = r->cache_len;
+    hm[M_NTOK_B] = 1;
+    hm[M_NTOK_2B] = 2;
+    hm[M_ONE] = 1;
+    CK(cudaMemcpyAsync(b->d_meta, hm, b->meta_n * sizeof(int), cudaMemcpyHostToDevice, b->st));
+    CK(cudaMemcpyAsync(b->x, embeds, (size_t)b->H * 4, cudaMemcpyHostToDevice, b->st));
+    const int ms = bucket_split(r->cache_len + 1);
+    CK(cudaEventRecord(b->ev0, b->st));
+    run_graph(b, std::make_tuple(1, 1, ms), [&] {
+      const int *ntok = b->d_meta + M_NTOK_B, *slot = b->d_meta + b->off_slot();
+      TokView tvt{ntok, slot, b->d_meta + b->off_tpos(), 0};
+      run_stack(b, m->talker, talker_kv(b), tvt, 1, true, ms);
+      rmsnorm(b->x, b->H, 1, 0, m->talker.final_norm, b->xn, b->H, b->H, m->tc.talker.rms_norm_eps, ntok, 1,
+              b->tlog, b->V, b->V, b->d_hidden, slot, b->st);
+      linear(m->codec_head, b->V, b->H, b->xn, b->H, 0, b->tlog, b->V, ntok, 1, b->st);
+    });
+    CK(cudaEventRecord(b->ev1, b->st));
+    if (logits) CK(cudaMemcpyAsync(logits, b->tlog, (size_t)b->V * 4, cudaMemcpyDeviceToHost, b->st));
+    if (hidden)
+      CK(cudaMemcpyAsync(hidden, b->d_hidden + (size_t)r->slot * b->H, (size_t)b->H * 4, cudaMemcpyDeviceToHost,
+                         b->st));
+    CK(cudaStreamSynchronize(b->st));
+    CK(cudaEventElapsedTime(&b->last_ms, b->ev0, b->ev1));
+    r->cache_len++;
+  });
+}
+
+extern "C" q3t_status q3t_session_load_kv(q3t_session *s, const uint16_t *k, const uint16_t *v, int len,
+                                          const float *hidden) {
+  if (!s || (len > 0 && (!k || !v)) || len < 0) {
+    set_error("q3t_session_load_kv: bad argument");
+    return Q3T_INVALID_INPUT;
+  }
+  return guard([&] {
+    q3t_batch *b = s->b;
+    Req *r = s->r;
+    q3t_model *m = b->m;
+    CK(cudaSetDevice(m->device));
+    if (r->slot < 0) FAIL(Q3T_INVALID_INPUT, "session is finished");
+    if (len + 1 > kMaxSeq || !ensure_pages(b, r, len + 1)) FAIL(Q3T_OUT_OF_PAGES, "KV capacity exhausted");
+    const auto &c = m->tc.talker;
+    const size_t n = (size_t)c.num_hidden_layers * c.num_key_value_heads * len * 128;
+    if (len > 0) {
+      uint16_t *dk, *dv;
+      CK(cudaMalloc(&dk, n * 2));
+      CK(cudaMalloc(&dv, n * 2));
+      CK(cudaMemcpy(dk, k, n * 2, cudaMemcpyHostToDevice));
+      CK(cudaMemcpy(dv, v, n * 2, cudaMemcpyHostToDevice));
+      kv_import(dk, dv, c.num_hidden_layers, len, talker_kv(b), r->slot, b->st);
+      CK(cudaStreamSynchronize(b->st));
+      CK(cudaFree(dk));
+      CK(cudaFree(dv));
+    }
+    r->cache_len = len;
+    if (hidden)
+      CK(cudaMemcpy(b->d_hidden + (size_t)r->slot * b->H, hidden, (size_t)b->H * 4, cudaMemcpyHostToDevice));
+  });
+}
+
+extern "C" q3t_status q3t_session_last_ms(q3t_session *s, float *ms) {
+  if (!s || !ms) return Q3T_INVALID_INPUT;
+  *ms = s->b->last_ms;
+  return Q3T_OK;
+}
+
+extern "C" void q3t_session_free(q3t_session *s) {
+  if (!s) return;
+  q3t_batch_free(s->b);
+  delete s;
+}
+
+// ----------------------------------------------------------------------------
+extern "C" const char *q3t_last_error(void) { return q3t::g_err.c_str(); }
+extern "C" const char *q3t_version(void) { return "q3t-b200 0.1 (sm_100a)"; }
+extern "C" int64_t q3t_kernel_launches(void) { return q3t::g_launches; }

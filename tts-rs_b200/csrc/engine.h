@@ -1,0 +1,201 @@
+// Host runtime shared by the C ABI (engine.cu) and the codec (codec.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <deque>
+#include <map>
+#include <memory>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/q3t.h"
+#include "lm_kernels.cuh"
+
+namespace q3t {
+
+void set_error(const char *fmt, ...);
+
+struct CudaFail {
+  cudaError_t err;
+  std::string what;
+};
+
+// Throws CudaFail; every ABI entry point converts it to Q3T_CUDA_ERROR.
+#define CK(call)                                                   \
+  do {                                                             \
+    cudaError_t e_ = (call);                                       \
+    if (e_ != cudaSuccess) throw ::q3t::CudaFail{e_, #call};       \
+  } while (0)
+
+struct Status {
+  q3t_status code;
+  std::string msg;
+};
+#define FAIL(code, ...)                   \
+  do {                                    \
+    ::q3t::set_error(__VA_ARGS__);        \
+    throw ::q3t::Status{code, ""};        \
+  } while (0)
+
+// Device allocations owned by an object, released together.
+struct DevArena {
+  std::vector<void *> ptrs;
+  template <typename T>
+  T *alloc(size_t n) {
+    void *p = nullptr;
+    if (n == 0) n = 1;
+    CK(cudaMalloc(&p, n * sizeof(T)));
+    ptrs.push_back(p);
+    return reinterpret_cast<T *>(p);
+  }
+  template <typename T>
+  T *zalloc(size_t n) {
+    T *p = alloc<T>(n);
+    CK(cudaMemset(p, 0, (n ? n : 1) * sizeof(T)));
+    return p;
+  }
+  void release() {
+    for (void *p : ptrs) cudaFree(p);
+    ptrs.clear();
+  }
+  ~DevArena() { release(); }
+};
+
+// Device-side decoder stack (talker or code predictor).
+struct LMStack {
+  q3t_lm_config cfg{};
+  std::vector<float *> in_norm, post_norm, q_norm, k_norm;  // f32
+  std::vector<uint16_t *> wqkv, wo, wgu, wdown;              // fragment-packed bf16
+  float *final_norm = nullptr;
+  float *inv_freq = nullptr;  // [head_dim / 2]
+};
+
+struct CodecModel;  // codec.cu
+
+constexpr int kPage = 16;
+constexpr int kMaxSeq = 4096;                 // the reference's talker cache capacity
+constexpr int kPtStride = kMaxSeq / kPage;    // pages per sequence
+constexpr int kChunk = 64;                    // keys per attention split
+constexpr int kMaxSplit = kMaxSeq / kChunk;
+constexpr int kPrefillTok = 64;
+
+struct Req {
+  int64_t id = 0;
+  int state = 0;  // 0 queued, 1 active, 2 finished, 3 failed
+  int slot = -1;
+  std::vector<float> prompt, trailing, pad;
+  int S = 0, trailing_len = 0;
+  q3t_sampling ts{}, cs{};
+  int max_new = 0;
+  int64_t eos = -1;
+  std::vector<int64_t> suppress;
+  std::vector<int64_t> forced;  // [max_new][G]
+  int64_t forced_first = -1;
+  float *first_logits = nullptr;
+  int step_idx = 0;
+  bool eos_seen = false, finished = false;
+  int cache_len = 0;
+  std::vector<int> pages;
+  float *d_trailing = nullptr, *d_pad = nullptr;
+  std::vector<int64_t> codes;  // [G][T] once retired
+  std::vector<int32_t> sampled;  // [G][T] sampled tokens before teacher forcing
+  std::vector<float> wave;
+  int64_t samples = 0;
+  int64_t first_token = -1, first_token_raw = -1;
+  std::string error;
+};
+
+struct GraphEntry {
+  cudaGraphExec_t exec = nullptr;
+  int64_t nodes = 0;
+};
+
+enum MetaOff {
+  M_NTOK_B = 0,
+  M_NTOK_2B = 1,
+  M_ONE = 2,
+  M_NPRE = 3,
+  M_HDR = 8,
+};
+
+}  // namespace q3t
+
+struct q3t_model {
+  int device = 0;
+  q3t_talker_config tc{};
+  q3t_codec_config cc{};
+  bool has_talker = false, has_codec = false;
+  q3t::LMStack talker, pred;
+  uint16_t *codec_head = nullptr;            // packed [vocab][H]
+  uint16_t *talker_emb = nullptr;            // row-major bf16 [vocab][H]
+  std::vector<uint16_t *> cp_emb, lm_heads;  // row-major bf16 / packed
+  uint16_t **cp_emb_dev = nullptr;           // device array of cp_emb pointers
+  int64_t kv_pages = 8192;
+  int max_active = 64;
+  q3t::CodecModel *codec = nullptr;
+  q3t::DevArena arena;
+};
+
+struct q3t_batch {
+  q3t_model *m = nullptr;
+  q3t_batch_desc desc{};
+  int A = 0, G = 0, H = 0, V = 0, PV = 0, NQKV = 0, NQKVP = 0, I2 = 0;
+  cudaStream_t st = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  q3t::DevArena ar;
+  // talker pool
+  uint16_t *tk = nullptr, *tv = nullptr;
+  int64_t t_layer_stride = 0;
+  int n_pages = 0;
+  std::vector<int> free_pages;
+  int *d_pt = nullptr;
+  std::vector<int> h_pt;
+  // predictor pool (2 pages per slot)
+  uint16_t *pk = nullptr, *pv = nullptr;
+  int64_t p_layer_stride = 0;
+  int *d_ppt = nullptr;
+  // slot state
+  int maxF = 0;
+  int64_t *d_codes = nullptr, *d_hist_codes = nullptr, *d_forced = nullptr, *d_eos = nullptr;
+  int64_t *d_suppress = nullptr;
+  int32_t *d_raw = nullptr;
+  int n_suppress_cap = 4096;
+  float *d_hidden = nullptr;
+  int32_t *d_thist = nullptr;
+  int *d_thist_len = nullptr, *d_sup_on = nullptr, *d_forced_count = nullptr;
+  int hist_cap = 0;
+  q3t::SampleParams *d_params = nullptr;
+  // activations
+  int Tmax = 0;
+  float *x = nullptr, *qkv = nullptr, *gu = nullptr, *tlog = nullptr, *plog = nullptr;
+  uint16_t *xn = nullptr, *q = nullptr, *attn = nullptr;
+  q3t::AttnWork ws{};
+  // metadata
+  int meta_n = 0;
+  int *d_meta = nullptr, *h_meta = nullptr;
+  const float **d_extra = nullptr, **h_extra = nullptr;
+  int *d_pmeta = nullptr, *h_pmeta = nullptr;  // prefill metadata, one block per chunk
+  int *d_eosflag = nullptr, *h_eosflag = nullptr;
+  int64_t *h_codes = nullptr;
+  // graphs
+  bool use_graphs = true;
+  std::map<std::tuple<int, int, int>, q3t::GraphEntry> graphs;
+  // requests
+  std::vector<q3t::Req *> slots;
+  std::deque<q3t::Req *> queue;
+  std::map<int64_t, std::unique_ptr<q3t::Req>> reqs;
+  int64_t next_id = 1;
+  float last_ms = 0.f;
+  bool session_mode = false;
+
+  int off_slot() const { return q3t::M_HDR; }
+  int off_tpos() const { return q3t::M_HDR + A; }
+  int off_frame() const { return q3t::M_HDR + 2 * A; }
+  int off_zero() const { return q3t::M_HDR + 3 * A; }
+  int off_p0seq() const { return q3t::M_HDR + 4 * A; }
+  int off_p0pos() const { return q3t::M_HDR + 6 * A; }
+  int pmeta_stride() const { return 8 + 2 * q3t::kPrefillTok + 8; }
+};
+
