@@ -91,11 +91,12 @@ static uint16_t *to_dev_bf16(const q3t_tensor *t, DevArena *ar, cudaStream_t st)
   else
     CK(cudaMalloc(&d, n * 2));
   if (t->dtype == Q3T_BF16) {
-    CK(cudaMemcpy(d, t->data, n * 2, cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(d, t->data, n * 2, cudaMemcpyHostToDevice, st));
+    CK(cudaStreamSynchronize(st));
   } else {
     float *tmp;
     CK(cudaMalloc(&tmp, n * 4));
-    CK(cudaMemcpy(tmp, t->data, n * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(tmp, t->data, n * 4, cudaMemcpyHostToDevice, st));
     f32_to_bf16(tmp, d, n, st);
     CK(cudaStreamSynchronize(st));
     CK(cudaFree(tmp));
@@ -103,11 +104,12 @@ static uint16_t *to_dev_bf16(const q3t_tensor *t, DevArena *ar, cudaStream_t st)
   return d;
 }
 
-float *upload_f32(const q3t_tensor *t, DevArena &ar) {
+float *upload_f32(const q3t_tensor *t, DevArena &ar, cudaStream_t st) {
   const int64_t n = numel(t);
   float *d = ar.alloc<float>(n);
   if (t->dtype == Q3T_F32) {
-    CK(cudaMemcpy(d, t->data, n * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(d, t->data, n * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaStreamSynchronize(st));
   } else {
     std::vector<float> h(n);
     const uint16_t *s = reinterpret_cast<const uint16_t *>(t->data);
@@ -115,7 +117,8 @@ float *upload_f32(const q3t_tensor *t, DevArena &ar) {
       uint32_t u = (uint32_t)s[i] << 16;
       memcpy(&h[i], &u, 4);
     }
-    CK(cudaMemcpy(d, h.data(), n * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(d, h.data(), n * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaStreamSynchronize(st));
   }
   return d;
 }
@@ -144,10 +147,10 @@ static void load_stack(q3t_model *m, LMStack &S, const q3t_lm_config &c, const s
   auto &ar = m->arena;
   for (int l = 0; l < c.num_hidden_layers; l++) {
     const std::string p = prefix + ".layers." + std::to_string(l);
-    S.in_norm.push_back(upload_f32(T.get(p + ".input_layernorm.weight", {H}), ar));
-    S.post_norm.push_back(upload_f32(T.get(p + ".post_attention_layernorm.weight", {H}), ar));
-    S.q_norm.push_back(upload_f32(T.get(p + ".self_attn.q_norm.weight", {hd}), ar));
-    S.k_norm.push_back(upload_f32(T.get(p + ".self_attn.k_norm.weight", {hd}), ar));
+    S.in_norm.push_back(upload_f32(T.get(p + ".input_layernorm.weight", {H}), ar, st));
+    S.post_norm.push_back(upload_f32(T.get(p + ".post_attention_layernorm.weight", {H}), ar, st));
+    S.q_norm.push_back(upload_f32(T.get(p + ".self_attn.q_norm.weight", {hd}), ar, st));
+    S.k_norm.push_back(upload_f32(T.get(p + ".self_attn.k_norm.weight", {hd}), ar, st));
     const int Nq = nh * hd, Nk = nkv * hd;
     uint16_t *qkv = ar.alloc<uint16_t>((size_t)(Nq + 2 * Nk) * H);
     pack_into(T.get(p + ".self_attn.q_proj.weight", {Nq, H}), qkv, Nq, H, st);
@@ -165,12 +168,13 @@ static void load_stack(q3t_model *m, LMStack &S, const q3t_lm_config &c, const s
     pack_into(T.get(p + ".mlp.down_proj.weight", {H, I}), wd, H, I, st);
     S.wdown.push_back(wd);
   }
-  S.final_norm = upload_f32(T.get(prefix + ".norm.weight", {H}), ar);
+  S.final_norm = upload_f32(T.get(prefix + ".norm.weight", {H}), ar, st);
   // rope.rs:21-24: inv_freq[i] = 1 / theta^(i / half), computed in f32 on the host
   std::vector<float> inv(hd / 2);
   for (int i = 0; i < hd / 2; i++) inv[i] = 1.0f / powf(c.rope_theta, (float)i / (float)(hd / 2));
   S.inv_freq = ar.alloc<float>(hd / 2);
-  CK(cudaMemcpy(S.inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpyAsync(S.inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice, st));
+  CK(cudaStreamSynchronize(st));
 }
 
 }  // namespace q3t
@@ -224,11 +228,15 @@ extern "C" q3t_status q3t_model_load(const q3t_model_desc *desc, q3t_model **out
         m->lm_heads.push_back(lh);
       }
       m->cp_emb_dev = m->arena.alloc<uint16_t *>(G - 1);
-      CK(cudaMemcpy(m->cp_emb_dev, m->cp_emb.data(), (G - 1) * sizeof(uint16_t *), cudaMemcpyHostToDevice));
+      CK(cudaMemcpyAsync(m->cp_emb_dev, m->cp_emb.data(), (G - 1) * sizeof(uint16_t *), cudaMemcpyHostToDevice,
+                         st));
     }
     if (m->has_codec) m->codec = codec_load(m, desc, st);
     CK(cudaStreamSynchronize(st));
     CK(cudaStreamDestroy(st));
+    // zero-fills (cudaMemset) run on the legacy stream: finish them before any
+    // non-blocking library stream touches the buffers
+    CK(cudaDeviceSynchronize());
   });
   if (rc != Q3T_OK) {
     q3t_model_free(m);
@@ -291,7 +299,7 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
     std::vector<int> ppt((size_t)A * 2);
     for (int s = 0; s < A; s++) ppt[2 * s] = 2 * s, ppt[2 * s + 1] = 2 * s + 1;
     b->d_ppt = ar.alloc<int>(ppt.size());
-    CK(cudaMemcpy(b->d_ppt, ppt.data(), ppt.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(b->d_ppt, ppt.data(), ppt.size() * 4, cudaMemcpyHostToDevice, b->st));
   }
   // slot state
   b->maxF = kMaxSeq;
@@ -339,6 +347,7 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
   CK(cudaMallocHost(&b->h_codes, (size_t)A * G * sizeof(int64_t)));
   b->slots.assign(A, nullptr);
   CK(cudaStreamSynchronize(b->st));
+  CK(cudaDeviceSynchronize());  // the arena's cudaMemset zero-fills run on the legacy stream
 }
 
 static void batch_destroy(q3t_batch *b) {
@@ -359,10 +368,17 @@ static void batch_destroy(q3t_batch *b) {
   b->ar.release();
 }
 
+static void check_launches() {
+  const char *k = "";
+  cudaError_t e = take_launch_error(&k);
+  if (e != cudaSuccess) throw CudaFail{e, k};
+}
+
 template <class F>
 static void run_graph(q3t_batch *b, std::tuple<int, int, int> key, F &&body) {
   if (!b->use_graphs) {
     body();
+    check_launches();
     return;
   }
   auto it = b->graphs.find(key);
@@ -372,11 +388,17 @@ static void run_graph(q3t_batch *b, std::tuple<int, int, int> key, F &&body) {
     body();
     cudaGraph_t graph = nullptr;
     cudaError_t e = cudaStreamEndCapture(b->st, &graph);
-    if (e != cudaSuccess) {
+    const char *kname = "";
+    cudaError_t le = take_launch_error(&kname);
+    if (e != cudaSuccess || le != cudaSuccess) {
+      fprintf(stderr, "q3t: graph capture failed (%s / %s in %s); running without graphs\n",
+              cudaGetErrorString(e), cudaGetErrorString(le), kname);
+      if (graph) cudaGraphDestroy(graph);
       cudaGetLastError();
       b->use_graphs = false;
       g_launches = l0;
       body();
+      check_launches();
       return;
     }
     GraphEntry ge;
@@ -629,6 +651,7 @@ static void prefill(q3t_batch *b, Req *r) {
   a.raw = nullptr;
   sample(a, 1, b->st);
   // teacher forcing of the first token replaces it where it was sampled
+  check_launches();
   CK(cudaMemcpyAsync(b->h_codes, b->d_codes + (size_t)s * b->G, 8, cudaMemcpyDeviceToHost, b->st));
   CK(cudaStreamSynchronize(b->st));
   const int64_t raw_first = b->h_codes[0];
@@ -679,12 +702,14 @@ static void admit(q3t_batch *b, int *admitted) {
 static void retire(q3t_batch *b, Req *r, int64_t *samples) {
   const int T = r->step_idx, G = b->G;
   std::vector<int64_t> tg((size_t)T * G);
-  if (T > 0)
-    CK(cudaMemcpy(tg.data(), b->d_hist_codes + (size_t)r->slot * b->maxF * G, tg.size() * 8,
-                  cudaMemcpyDeviceToHost));
   std::vector<int32_t> rg((size_t)T * G);
-  if (T > 0)
-    CK(cudaMemcpy(rg.data(), b->d_raw + (size_t)r->slot * b->maxF * G, rg.size() * 4, cudaMemcpyDeviceToHost));
+  if (T > 0) {
+    CK(cudaMemcpyAsync(tg.data(), b->d_hist_codes + (size_t)r->slot * b->maxF * G, tg.size() * 8,
+                       cudaMemcpyDeviceToHost, b->st));
+    CK(cudaMemcpyAsync(rg.data(), b->d_raw + (size_t)r->slot * b->maxF * G, rg.size() * 4,
+                       cudaMemcpyDeviceToHost, b->st));
+    CK(cudaStreamSynchronize(b->st));
+  }
   r->codes.assign((size_t)G * T, 0);
   r->sampled.assign((size_t)G * T, 0);
   for (int t = 0; t < T; t++)
@@ -1043,12 +1068,14 @@ static q3t_status session_step(q3t_session *s, const int64_t *forced, float *tl,
       CK(cudaMemcpyAsync(b->d_thist + (size_t)sl * b->hist_cap + f, &c0, 4, cudaMemcpyHostToDevice, b->st));
     }
     batch_step(b, nullptr);
-    if (tl) CK(cudaMemcpy(tl, b->tlog, (size_t)b->V * 4, cudaMemcpyDeviceToHost));
+    if (tl) CK(cudaMemcpyAsync(tl, b->tlog, (size_t)b->V * 4, cudaMemcpyDeviceToHost, b->st));
     if (pl)
       for (int j = 0; j < G - 1; j++)
-        CK(cudaMemcpy(pl + (size_t)j * b->PV, b->plog + (size_t)j * b->A * b->PV, (size_t)b->PV * 4,
-                      cudaMemcpyDeviceToHost));
-    if (hid) CK(cudaMemcpy(hid, b->d_hidden + (size_t)sl * b->H, (size_t)b->H * 4, cudaMemcpyDeviceToHost));
+        CK(cudaMemcpyAsync(pl + (size_t)j * b->PV, b->plog + (size_t)j * b->A * b->PV, (size_t)b->PV * 4,
+                           cudaMemcpyDeviceToHost, b->st));
+    if (hid)
+      CK(cudaMemcpyAsync(hid, b->d_hidden + (size_t)sl * b->H, (size_t)b->H * 4, cudaMemcpyDeviceToHost, b->st));
+    CK(cudaStreamSynchronize(b->st));
     if (state) *state = r->finished ? 2 : 1;
   });
 }
@@ -1080,8 +1107,9 @@ extern "C" q3t_status q3t_session_codes(q3t_session *s, int64_t *out, int *num_f
       return;
     }
     std::vector<int64_t> tg((size_t)T * G);
-    CK(cudaMemcpy(tg.data(), b->d_hist_codes + (size_t)r->slot * b->maxF * G, tg.size() * 8,
-                  cudaMemcpyDeviceToHost));
+    CK(cudaMemcpyAsync(tg.data(), b->d_hist_codes + (size_t)r->slot * b->maxF * G, tg.size() * 8,
+                       cudaMemcpyDeviceToHost, b->st));
+    CK(cudaStreamSynchronize(b->st));
     for (int t = 0; t < T; t++)
       for (int q = 0; q < G; q++) out[(size_t)q * T + t] = tg[(size_t)t * G + q];
   });
@@ -1170,8 +1198,8 @@ extern "C" q3t_status q3t_session_load_kv(q3t_session *s, const uint16_t *k, con
       uint16_t *dk, *dv;
       CK(cudaMalloc(&dk, n * 2));
       CK(cudaMalloc(&dv, n * 2));
-      CK(cudaMemcpy(dk, k, n * 2, cudaMemcpyHostToDevice));
-      CK(cudaMemcpy(dv, v, n * 2, cudaMemcpyHostToDevice));
+      CK(cudaMemcpyAsync(dk, k, n * 2, cudaMemcpyHostToDevice, b->st));
+      CK(cudaMemcpyAsync(dv, v, n * 2, cudaMemcpyHostToDevice, b->st));
       kv_import(dk, dv, c.num_hidden_layers, len, talker_kv(b), r->slot, b->st);
       CK(cudaStreamSynchronize(b->st));
       CK(cudaFree(dk));
@@ -1179,7 +1207,9 @@ extern "C" q3t_status q3t_session_load_kv(q3t_session *s, const uint16_t *k, con
     }
     r->cache_len = len;
     if (hidden)
-      CK(cudaMemcpy(b->d_hidden + (size_t)r->slot * b->H, hidden, (size_t)b->H * 4, cudaMemcpyHostToDevice));
+      CK(cudaMemcpyAsync(b->d_hidden + (size_t)r->slot * b->H, hidden, (size_t)b->H * 4, cudaMemcpyHostToDevice,
+                         b->st));
+    CK(cudaStreamSynchronize(b->st));
   });
 }
 

@@ -74,6 +74,10 @@ struct LMStack {
 
 struct CodecModel;  // codec.cu
 
+// host tensor -> device (engine.cu); copies run on `st`
+float *upload_f32(const q3t_tensor *t, DevArena &ar, cudaStream_t st);
+uint16_t *upload_bf16(const q3t_tensor *t, DevArena &ar, cudaStream_t st);
+
 constexpr int kPage = 16;
 constexpr int kMaxSeq = 4096;                 // the reference's talker cache capacity
 constexpr int kPtStride = kMaxSeq / kPage;    // pages per sequence

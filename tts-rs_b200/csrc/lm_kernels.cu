@@ -7,6 +7,7 @@
 // Every kernel is PDL-aware: the weight stream of a linear starts before
 // griddepcontrol.wait, so it overlaps the tail of the previous kernel.
 #include <cfloat>
+#include <cstdlib>
 #include <utility>
 
 #include "common.cuh"
@@ -16,6 +17,22 @@ namespace q3t {
 
 bool g_use_pdl = true;
 int64_t g_launches = 0;
+cudaError_t g_launch_err = cudaSuccess;
+const char *g_launch_err_kernel = "";
+
+cudaError_t take_launch_error(const char **kernel) {
+  cudaError_t e = g_launch_err;
+  if (kernel) *kernel = g_launch_err_kernel;
+  g_launch_err = cudaSuccess;
+  return e;
+}
+
+static void note(cudaError_t e, const char *what) {
+  if (e != cudaSuccess && g_launch_err == cudaSuccess) {
+    g_launch_err = e;
+    g_launch_err_kernel = what;
+  }
+}
 
 template <typename... KArgs, typename... Args>
 static void launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
@@ -30,7 +47,7 @@ static void launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = g_use_pdl ? 1 : 0;
-  cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+  note(cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...), "kernel launch");
   g_launches++;
 }
 
@@ -65,6 +82,7 @@ __global__ void k_pack(const uint16_t *__restrict__ src, uint16_t *__restrict__ 
 void pack_weight(const uint16_t *src, uint16_t *dst, int N, int K, cudaStream_t st) {
   int64_t n = (int64_t)(N / 16) * (K / 16) * 32;
   k_pack<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(src, dst, N, K);
+  note(cudaGetLastError(), "k_pack");
   g_launches++;
 }
 
@@ -76,19 +94,20 @@ __global__ void k_f32_to_bf16(const float *__restrict__ s, uint16_t *__restrict_
 
 void f32_to_bf16(const float *src, uint16_t *dst, int64_t n, cudaStream_t st) {
   k_f32_to_bf16<<<1184, 256, 0, st>>>(src, dst, n);
+  note(cudaGetLastError(), "k_f32_to_bf16");
   g_launches++;
 }
 
 // ---------------------------------------------------------------------------
 // RMSNorm (burn::nn::RmsNorm: x / sqrt(mean(x^2) + eps) * gamma) -> bf16
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) k_rmsnorm(const float *__restrict__ x, int ldx, int row_mul,
+__global__ void __launch_bounds__(256) k_rmsnorm(const float *x, int ldx, int row_mul,
                                                  int row_add, const float *__restrict__ gamma,
-                                                 uint16_t *__restrict__ out, int ldo, int H,
-                                                 float eps, const int *__restrict__ ntok,
-                                                 float *__restrict__ zero, int ldz, int zero_cols,
-                                                 float *__restrict__ out_f32,
-                                                 const int *__restrict__ slot) {
+                                                 uint16_t *out, int ldo, int H,
+                                                 float eps, const int *ntok,
+                                                 float *zero, int ldz, int zero_cols,
+                                                 float *out_f32,
+                                                 const int *slot) {
   __shared__ float red[33];
   pdl_wait();
   const int t = blockIdx.x;
@@ -135,9 +154,9 @@ void rmsnorm(const float *x, int ldx, int row_mul, int row_add, const float *gam
 // ---------------------------------------------------------------------------
 template <int NT, int XMODE>
 __global__ void __launch_bounds__(128) k_linear(const uint4 *__restrict__ W, int N, int K, int kc,
-                                                const void *__restrict__ X, int ldx,
-                                                float *__restrict__ Y, int ldy,
-                                                const int *__restrict__ ntok_p, int tok_base) {
+                                                const void *X, int ldx,
+                                                float *Y, int ldy,
+                                                const int *ntok_p, int tok_base) {
   constexpr int FR = 16;
   extern __shared__ __align__(16) uint16_t xs[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -242,7 +261,7 @@ void linear(const uint16_t *Wp, int N, int K, const void *X, int ldx, int xmode,
 // holds dims [4l, 4l+4); the rotate-half partner of dim d is d +- 64, i.e.
 // lane l ^ 16.
 // ---------------------------------------------------------------------------
-Q3T_DEV void norm_rope_lane(float4 v, const float *__restrict__ gm, float eps, int lane, int pos,
+Q3T_DEV void norm_rope_lane(float4 v, const float *gm, float eps, int lane, int pos,
                             const float *__restrict__ inv_freq, float out[4]) {
   const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
   const float rms = sqrtf(ss / 128.f + eps);
@@ -263,12 +282,12 @@ Q3T_DEV size_t page_elem(const KVView &kv, int seq, int pos, int h) {
   return (((size_t)page * kv.n_kv + h) * 16 + (pos & 15)) * 128;
 }
 
-__global__ void __launch_bounds__(1024) k_qkv_post(const float *__restrict__ qkv, int ldqkv,
+__global__ void __launch_bounds__(1024) k_qkv_post(const float *qkv, int ldqkv,
                                                    const float *__restrict__ q_norm,
                                                    const float *__restrict__ k_norm,
                                                    const float *__restrict__ inv_freq, float eps,
                                                    int nh, int nkv, TokView tv,
-                                                   uint16_t *__restrict__ qout, KVView kv,
+                                                   uint16_t *qout, KVView kv,
                                                    int layer) {
   pdl_wait();
   const int t = blockIdx.x;
@@ -318,13 +337,13 @@ void qkv_post(const float *qkv, int ldqkv, const float *q_norm, const float *k_n
 constexpr int kPart = 132;
 
 template <bool FUSED>
-__global__ void __launch_bounds__(128) k_attn(const float *__restrict__ qkv, int ldqkv,
+__global__ void __launch_bounds__(128) k_attn(const float *qkv, int ldqkv,
                                               const float *__restrict__ q_norm,
                                               const float *__restrict__ k_norm,
                                               const float *__restrict__ inv_freq, float eps,
-                                              const uint16_t *__restrict__ qin, KVView kv,
+                                              const uint16_t *qin, KVView kv,
                                               int layer, TokView tv, int nh, int chunk,
-                                              float scale, AttnWork ws, uint16_t *__restrict__ out) {
+                                              float scale, AttnWork ws, uint16_t *out) {
   __shared__ float qs[2][128];
   __shared__ float sc[2][256];
   __shared__ float red[2][4];
@@ -512,12 +531,12 @@ void attention(int fused, const float *qkv, int ldqkv, const float *q_norm, cons
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_embed(const uint16_t *__restrict__ emb0,
                                                const uint16_t *const *__restrict__ embs, int G,
-                                               int H, const int64_t *__restrict__ codes,
-                                               const int *__restrict__ slot,
-                                               const float *const *__restrict__ extra,
-                                               const int *__restrict__ frame,
-                                               int64_t *__restrict__ hist, int hist_frames,
-                                               const int *__restrict__ ntok, float *__restrict__ x) {
+                                               int H, const int64_t *codes,
+                                               const int *slot,
+                                               const float *const *extra,
+                                               const int *frame,
+                                               int64_t *hist, int hist_frames,
+                                               const int *ntok, float *x) {
   pdl_wait();
   const int t = blockIdx.x;
   if (t < *ntok) {
@@ -557,12 +576,12 @@ void embed_codes(const uint16_t *emb0, const uint16_t *const *embs, int G, int H
          hist, hist_frames, ntok, x);
 }
 
-__global__ void __launch_bounds__(256) k_pred_input0(const float *__restrict__ hidden,
+__global__ void __launch_bounds__(256) k_pred_input0(const float *hidden,
                                                      const uint16_t *__restrict__ emb0,
-                                                     const int64_t *__restrict__ codes, int G,
-                                                     const int *__restrict__ slot,
-                                                     const int *__restrict__ ntok, int H,
-                                                     float *__restrict__ x) {
+                                                     const int64_t *codes, int G,
+                                                     const int *slot,
+                                                     const int *ntok, int H,
+                                                     float *x) {
   pdl_wait();
   const int b = blockIdx.x;
   if (b < *ntok) {
@@ -582,10 +601,10 @@ void pred_input0(const float *hidden, const uint16_t *emb0, const int64_t *codes
 }
 
 __global__ void __launch_bounds__(256) k_pred_input(const uint16_t *__restrict__ emb,
-                                                    const int64_t *__restrict__ codes, int G,
-                                                    int col, const int *__restrict__ slot,
-                                                    const int *__restrict__ ntok, int H,
-                                                    float *__restrict__ x) {
+                                                    const int64_t *codes, int G,
+                                                    int col, const int *slot,
+                                                    const int *ntok, int H,
+                                                    float *x) {
   pdl_wait();
   const int b = blockIdx.x;
   if (b < *ntok) {
@@ -797,10 +816,12 @@ void sample(const SampleArgs &a, int max_tok, cudaStream_t st) {
 
 void init_kernel_attributes() {
   cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSampleSmem);
+  const char *e = getenv("Q3T_PDL");
+  if (e && e[0] == '0') g_use_pdl = false;
 }
 
 // ---------------------------------------------------------------------------
-__global__ void k_kv_import(const uint16_t *__restrict__ k, const uint16_t *__restrict__ v,
+__global__ void k_kv_import(const uint16_t *k, const uint16_t *v,
                             int len, KVView kv, int seq) {
   const int l = blockIdx.z, h = blockIdx.y, j = blockIdx.x;
   const size_t src = (((size_t)l * kv.n_kv + h) * len + j) * 128;
@@ -815,6 +836,7 @@ void kv_import(const uint16_t *k, const uint16_t *v, int layers, int len, KVView
                cudaStream_t st) {
   if (len <= 0) return;
   k_kv_import<<<dim3(len, kv.n_kv, layers), 128, 0, st>>>(k, v, len, kv, seq);
+  note(cudaGetLastError(), "k_kv_import");
   g_launches++;
 }
 

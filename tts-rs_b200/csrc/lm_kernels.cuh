@@ -36,6 +36,8 @@ extern bool g_use_pdl;
 // one-time kernel attribute setup (dynamic shared memory limits)
 void init_kernel_attributes();
 extern int64_t g_launches;
+// first launch error since the last call (cudaSuccess if none)
+cudaError_t take_launch_error(const char **kernel);
 
 // Packs W [N][K] bf16 row-major into m16n8k16 A-fragment order.
 void pack_weight(const uint16_t *src, uint16_t *dst, int N, int K, cudaStream_t st);
