@@ -1,0 +1,344 @@
+#!/usr/bin/env python
+"""Benchmark: Qwen3-TTS continuous-batching ragged decode, audio-seconds per second.
+
+Workload (the headline configuration): 512 requests, prompt lengths uniform in
+[16, 256], target lengths uniform in [100, 1500] frames, 16-token KV pages,
+at most 64 active requests per GPU, full talker + code predictor + streaming
+codec decode per step, replicated bf16 weights from seed 0, requests
+round-robin partitioned across the GPUs (data parallel, no collective on the
+hot path).  Frames are teacher-forced with uniform codes in [0, 2048) so every
+request runs exactly its target length (the sampler still runs each step).
+
+One step = one scheduler iteration (q3t_batch_step): admit + prefill queued
+requests into free slots, one frame for every active request, emit the
+codec chunks that are due, retire finished requests.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Multi-GPU: python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "tts-rs_b200"))
+
+import synthetic as S  # noqa: E402
+
+FRAME_S = 0.08          # one frame = 1920 samples at 24 kHz
+SAMPLE_RATE = 24000
+METRIC = "audio-sec/sec per box (batch 64 ragged continuous batching)"
+WORKLOAD = ("qwen3-tts-12hz-0.6b continuous batching: 512 requests, prompt U[16,256], "
+            "target U[100,1500] frames, 16-token pages, <=64 active/GPU, talker+predictor+streaming codec")
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=300)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--requests", type=int, default=512)
+    p.add_argument("--max-active", type=int, default=64)
+    p.add_argument("--chunk", type=int, default=16)
+    p.add_argument("--left-context", type=int, default=8)
+    p.add_argument("--cpu-frames", type=int, default=48, help="bounded CPU-baseline sample (frames)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def workload(n_req, seed=0):
+    g = np.random.default_rng([seed, 2024])
+    S_len = g.integers(16, 257, n_req)
+    T_len = g.integers(100, 1501, n_req)
+    return [(int(a), int(b)) for a, b in zip(S_len, T_len)]
+
+
+def request_inputs(i, S_len, T_len, H=1024):
+    g = np.random.default_rng([0, 77, i])
+    prompt = (g.standard_normal((S_len, H), dtype=np.float32) * 0.5)
+    trailing = (g.standard_normal((1, H), dtype=np.float32) * 0.5)
+    pad = (g.standard_normal((H,), dtype=np.float32) * 0.5)
+    codes = g.integers(0, 2048, size=(T_len, 16), dtype=np.int64)
+    return prompt, trailing, pad, codes
+
+
+# per-step algorithmic HBM bytes (weights read once per step, KV read per token)
+def step_bytes(stats, cfg):
+    t, p = cfg.talker, cfg.predictor
+    layer = lambda c: (c.hidden * (c.n_heads + 2 * c.n_kv) * c.head_dim + c.hidden * c.n_heads * c.head_dim
+                       + 3 * c.hidden * c.inter) * 2
+    talker_w = t.n_layers * layer(t) + t.vocab * t.hidden * 2
+    pred_w = (cfg.n_groups - 1) * (p.n_layers * layer(p) + p.vocab * p.hidden * 2)
+    kv = stats["kv_tokens"] * t.n_layers * 2 * t.n_kv * t.head_dim * 2
+    return talker_w + pred_w + kv
+
+
+class Clocks:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, gpu_index, out):
+        self.p = None
+        try:
+            self.f = open(out, "w")
+            self.p = subprocess.Popen(
+                ["nvidia-smi", f"--id={gpu_index}",
+                 "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+        self.path = out
+
+    def stop(self):
+        if not self.p:
+            return None
+        self.p.terminate()
+        self.p.wait()
+        self.f.close()
+        sm, mx, reasons = [], 0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(n_frames, threads=0):
+    """The CPU oracle (C restatement of the reference math, OpenMP) on a
+    bounded sample of the same workload: one batch-1 request (the reference
+    is batch-1), 64-token prompt, n_frames teacher-forced frames, then the
+    codec decode of those frames.  Returns (audio-s/s, cores, seconds)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    if threads:
+        O.lib().orc_set_threads(threads)
+    cfg = S.TalkerConfig()
+    ot = O.OracleTalker(cfg, S.make_talker_weights(cfg))
+    cc = S.CodecConfig()
+    oc = O.OracleCodec(cc, S.make_codec_weights(cc))
+    prompt, trailing, pad, codes = request_inputs(0, 64, n_frames + 1)
+    t0 = time.perf_counter()
+    g = O.OracleGenerator(ot, prompt, trailing, pad, max_new_tokens=n_frames, forced_first=int(codes[0, 0]))
+    for f in range(n_frames):
+        g.step(forced=codes[f])
+    oc.decode(g.codes()[None])
+    dt = time.perf_counter() - t0
+    return n_frames * FRAME_S / dt, O.lib().orc_get_threads(), dt
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+    import torch
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    torch.cuda.set_device(local)
+    import q3t
+
+    cfg = S.TalkerConfig()
+    cc = S.CodecConfig()
+    model = q3t.Model(cfg, S.make_talker_weights(cfg, 0), cc, S.make_codec_weights(cc, 0), device=local,
+                      kv_pages=8192, max_active=args.max_active)
+    reqs = workload(args.requests)
+    mine = [i for i in range(len(reqs)) if i % world == rank]
+    inputs = {i: request_inputs(i, *reqs[i]) for i in mine}
+
+    def submit(b, i):
+        prompt, trailing, pad, codes = inputs[i]
+        return b.submit(prompt, trailing, pad, codes.shape[0], forced=codes)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+
+    # ---------------- value: inputs resident, PCM stays on the device --------
+    b = model.batch(max_active=args.max_active, codec_mode=2, chunk_frames=args.chunk,
+                    left_context=args.left_context, keep_output=0)
+    for i in mine:
+        submit(b, i)
+    for _ in range(args.warmup):
+        b.step()
+    stream = torch.cuda.ExternalStream(b.stream(), device=local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(local, os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out"))
+                                        else "/tmp", f"clocks_r{rank}.csv"))
+    launches0 = q3t.kernel_launches()
+    barrier()
+    e0.record(stream)
+    t0 = time.perf_counter()
+    steps = [b.step() for _ in range(args.steps)]
+    e1.record(stream)
+    barrier()
+    wall = time.perf_counter() - t0
+    launches = q3t.kernel_launches() - launches0
+    ck = clocks.stop()
+    dev_s = e0.elapsed_time(e1) / 1e3
+    samples = sum(s["samples"] for s in steps)
+    frames = sum(s["frames"] for s in steps)
+    step_ms = [s["device_ms"] for s in steps]
+    decode_ms = [s["device_ms"] for s in steps if s["admitted"] == 0 and s["samples"] == 0 and s["active"] > 0]
+    bytes_ = [step_bytes(s, cfg) for s in steps if s["admitted"] == 0 and s["samples"] == 0 and s["active"] > 0]
+    b.close()
+
+    # ---------------- e2e: host buffers in and out through the C ABI ---------
+    e2e = None
+    if not args.no_e2e:
+        b2 = model.batch(max_active=args.max_active, codec_mode=2, chunk_frames=args.chunk,
+                         left_context=args.left_context, keep_output=1)
+        pending = list(mine)
+
+        def top_up():
+            q, a = b2.pending()
+            while pending and q + a < args.max_active:
+                submit(b2, pending.pop(0))
+                q += 1
+
+        for _ in range(args.warmup):
+            top_up()
+            b2.step()
+        barrier()
+        t0 = time.perf_counter()
+        st2 = []
+        for _ in range(args.steps):
+            top_up()
+            st2.append(b2.step())
+        barrier()
+        wall2 = time.perf_counter() - t0
+        b2.close()
+        e2e_samples = sum(s["samples"] for s in st2)
+        e2e = {"value": None, "unit": "audio-s/s",
+               "h2d_bytes_per_step": int(np.mean([s["h2d_bytes"] for s in st2])),
+               "d2h_bytes_per_step": int(np.mean([s["d2h_bytes"] for s in st2])),
+               "_samples": e2e_samples, "_wall": wall2}
+
+    # ---------------- reduce over ranks --------------------------------------
+    def reduce(v, op):
+        if not dist:
+            return v
+        t = torch.tensor([float(v)], device="cuda")
+        dist.all_reduce(t, op=op)
+        return t.item()
+
+    if dist:
+        from torch.distributed import ReduceOp
+        tot_samples = reduce(samples, ReduceOp.SUM)
+        tot_frames = reduce(frames, ReduceOp.SUM)
+        max_dev = reduce(dev_s, ReduceOp.MAX)
+        if e2e:
+            e2e_tot = reduce(e2e["_samples"], ReduceOp.SUM)
+            e2e_wall = reduce(e2e["_wall"], ReduceOp.MAX)
+    else:
+        tot_samples, tot_frames, max_dev = samples, frames, dev_s
+        if e2e:
+            e2e_tot, e2e_wall = e2e["_samples"], e2e["_wall"]
+    value = tot_samples / SAMPLE_RATE / max_dev
+    if e2e:
+        e2e["value"] = round(e2e_tot / SAMPLE_RATE / e2e_wall, 3)
+        e2e.pop("_samples")
+        e2e.pop("_wall")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, dt = cpu_baseline(args.cpu_frames)
+        cpu = {"value": round(v, 4), "unit": "audio-s/s", "cores": cores, "kind": "port",
+               "sample": f"one batch-1 request, 64-token prompt, {args.cpu_frames} teacher-forced frames "
+                         f"(28-layer talker + 5-layer predictor) + codec decode, {dt:.1f} s"}
+
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    med_ms = float(np.median(decode_ms)) if decode_ms else float(np.median(step_ms))
+    ach = (float(np.median(bytes_)) / 1e9) / (med_ms / 1e3) if bytes_ else None
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": "audio-s/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(max_dev * 1e3 / args.steps, 4),
+            "p50_step_ms": round(float(np.median(step_ms)), 4),
+            "p50_decode_step_ms": round(med_ms, 4),
+            "frames": int(tot_frames),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seed-0 random-init weights, teacher-forced uniform codes)",
+            "config": {"workload": WORKLOAD, "requests": args.requests, "max_active_per_gpu": args.max_active,
+                       "page_tokens": 16, "codec": f"streaming chunks of {args.chunk} frames, "
+                       f"{args.left_context} frames left context", "parallelism": f"dp{world} (replicas)",
+                       "l2_policy": "working set > L2 (talker+predictor weights 1.2 GB per step)"},
+            "roofline": {"bound": "hbm", "unit": "GB/s",
+                         "kernel": "decode frame step (CUDA graph of talker + predictor kernels)",
+                         "achieved": round(ach, 1) if ach else None, "peak": hbm_peak,
+                         "frac": round(ach / hbm_peak, 4) if ach else None, "traffic": None,
+                         "peak_source": "measured" if "hbm_gbs" in peaks else "fallback"},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "clocks": ck,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def reference_arm(args, rank, world):
+    """The reference's CPU path: the oracle restatement of the Burn flex
+    path (the Rust reference cannot be built here), all host threads,
+    batch-1 as the reference is; each step = one frame of one request (plus
+    its share of the codec decode at the end)."""
+    if rank != 0:
+        return
+    n = max(1, args.steps)
+    w = max(0, min(args.warmup, 3))
+    v, cores, dt = cpu_baseline(n + w)
+    print(json.dumps({
+        "metric": METRIC, "impl": "reference", "value": round(v, 4), "unit": "audio-s/s",
+        "n_gpus": world, "steps": n, "warmup": w, "ms_per_step": round(dt * 1e3 / (n + w), 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seed-0 random-init weights, teacher-forced uniform codes)",
+        "config": {"workload": WORKLOAD + " (CPU: one batch-1 request, 64-token prompt)"},
+        "cpu_baseline": {"value": round(v, 4), "unit": "audio-s/s", "cores": cores, "kind": "port",
+                         "sample": f"{n + w} frames of one request + codec decode ({dt:.1f} s)"},
+        "e2e": {"value": round(v, 4), "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -218,13 +218,18 @@ typedef struct {
   int64_t frames;            /* frames generated this step */
   int64_t samples;           /* PCM samples emitted this step */
   float device_ms;           /* device time of this step (CUDA events) */
+  int64_t kv_tokens;         /* sum over the decode tokens of their KV length */
+  int64_t h2d_bytes;         /* host -> device bytes copied during this step */
+  int64_t d2h_bytes;         /* device -> host bytes copied during this step */
 } q3t_step_stats;
 
 typedef struct q3t_batch q3t_batch;
 
 q3t_status q3t_batch_create(q3t_model *model, const q3t_batch_desc *desc, q3t_batch **out);
-/* Queue a request; forced_codes (nullable) [max_new_tokens][G] teacher-forces
- * every frame (then EOS is ignored and the request runs max_new_tokens). */
+/* Queue a request; its inputs are copied to device memory now, so a later
+ * step finds them resident.  forced_codes (nullable) [max_new_tokens][G]
+ * teacher-forces every frame (then EOS is ignored and the request runs
+ * max_new_tokens). */
 q3t_status q3t_batch_submit(q3t_batch *b, const q3t_session_desc *req,
                             const int64_t *forced_codes, int64_t *request_id);
 /* One scheduler iteration: admit + prefill queued requests into free slots,
@@ -240,6 +245,9 @@ q3t_status q3t_batch_poll(q3t_batch *b, int64_t request_id, int *state, int64_t 
 q3t_status q3t_batch_take(q3t_batch *b, int64_t request_id, int64_t *codes, int32_t *sampled,
                           int max_frames, float *wave, int64_t max_samples);
 q3t_status q3t_batch_pending(q3t_batch *b, int *queued, int *active);
+/* The CUDA stream (cudaStream_t) all of the batch's device work runs on, for
+ * callers that time steps with their own CUDA events. */
+q3t_status q3t_batch_stream(q3t_batch *b, void **stream);
 void q3t_batch_free(q3t_batch *b);
 
 /* ------------------------------- misc ----------------------------------- */

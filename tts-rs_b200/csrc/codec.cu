@@ -966,52 +966,65 @@ void codec_stream_step(q3t_model *m, q3t_batch *b, const std::vector<Req *> &act
   auto &S = g_streams[b];
   const int chunk = std::max(1, b->desc.chunk_frames), ctx = std::max(0, b->desc.left_context);
   const int nq = c->c.num_quantizers;
-  const int64_t per_frame = 1920;  // samples per frame at the default rates
-  (void)per_frame;
+  int64_t spf = 1;  // samples per frame (1920 at the default rates)
+  for (int i = 0; i < c->c.num_upsampling_ratios; i++) spf *= c->c.upsampling_ratios[i];
+  for (int i = 0; i < c->c.num_upsample_rates; i++) spf *= c->c.upsample_rates[i];
+  struct Win {
+    Req *r;
+    int e, n, f0;
+  };
+  std::map<int, std::vector<Win>> groups;  // window length -> windows
   for (Req *r : act) {
-    int &e = S.emitted[r->id];
-    const int avail = r->step_idx;
+    const int e = S.emitted[r->id], avail = r->step_idx;
     if (!(avail - e >= chunk || (r->finished && avail > e))) continue;
-    const int n = std::min(chunk, avail - e);
-    const int f0 = std::max(0, e - ctx), Tw = e + n - f0;
-    // codes must be valid for the codec: talker code 0 may exceed codebook_size
-    int64_t nout = 0, nwin_ctx = 0;
+    const int n = std::min(chunk, avail - e), f0 = std::max(0, e - ctx);
+    groups[e + n - f0].push_back(Win{r, e, n, f0});
+  }
+  for (auto &kv : groups) {
+    const int Tw = kv.first, Bw = (int)kv.second.size();
+    int64_t nout = 0;
     codec_out_len(c, Tw, &nout);
-    if (nout <= 0) {
-      e += n;
-      continue;
-    }
-    if (S.codes_cap < (size_t)nq * Tw) {
+    const int64_t deficit = spf * Tw - nout;  // samples the both-side trims drop at the end (555)
+    if (S.codes_cap < (size_t)Bw * nq * Tw) {
       if (S.d_codes) cudaFree(S.d_codes);
-      S.codes_cap = (size_t)nq * Tw * 2;
+      S.codes_cap = (size_t)Bw * nq * Tw * 2;
       CK(cudaMalloc(&S.d_codes, S.codes_cap * 8));
     }
-    if (S.wave_cap < (size_t)nout) {
+    if (S.wave_cap < (size_t)Bw * std::max<int64_t>(nout, 1)) {
       if (S.d_wave) cudaFree(S.d_wave);
-      S.wave_cap = (size_t)nout * 2;
+      S.wave_cap = (size_t)Bw * std::max<int64_t>(nout, 1) * 2;
       CK(cudaMalloc(&S.d_wave, S.wave_cap * 4));
     }
-    k_window_codes<<<8, 256, 0, b->st>>>(b->d_hist_codes, b->maxF, b->G, nq, r->slot, f0, Tw, S.d_codes);
-    CK(cudaGetLastError());
-    g_launches++;
-    decode_device(c, S.d_codes, 1, Tw, S.d_wave, nullptr, b->st);
-    // samples of frames [e, e + n) of this window; the last window of a
-    // request runs to the end of its decode
-    codec_out_len(c, e - f0, &nwin_ctx);
-    const int64_t s0 = e - f0 > 0 ? std::min<int64_t>(nout, (int64_t)(e - f0) * 1920 - 555) : 0;
-    const int64_t s1 = (r->finished && e + n == avail) ? nout : std::min<int64_t>(nout, (int64_t)(e + n - f0) * 1920 - 555);
-    if (s1 > s0) {
-      if (b->desc.keep_output) {
-        const size_t old = r->wave.size();
-        r->wave.resize(old + (s1 - s0));
-        CK(cudaMemcpyAsync(r->wave.data() + old, S.d_wave + s0, (s1 - s0) * 4, cudaMemcpyDeviceToHost, b->st));
-        CK(cudaStreamSynchronize(b->st));
-      }
-      r->samples += s1 - s0;
-      if (samples) *samples += s1 - s0;
+    for (int i = 0; i < Bw; i++) {
+      k_window_codes<<<8, 256, 0, b->st>>>(b->d_hist_codes, b->maxF, b->G, nq, kv.second[i].r->slot, kv.second[i].f0,
+                                           Tw, S.d_codes + (size_t)i * nq * Tw);
+      CK(cudaGetLastError());
+      g_launches++;
     }
-    e += n;
-    if (r->finished && e >= avail) S.emitted.erase(r->id);
+    if (nout > 0) decode_device(c, S.d_codes, Bw, Tw, S.d_wave, nullptr, b->st);
+    for (int i = 0; i < Bw; i++) {
+      Win &w = kv.second[i];
+      Req *r = w.r;
+      // window-relative frames [e - f0, e - f0 + n) map to samples shifted by
+      // the trim deficit, so consecutive chunks tile the full-length output
+      const int64_t a0 = w.e - w.f0;
+      const int64_t s0 = a0 > 0 ? std::min<int64_t>(nout, a0 * spf - deficit) : 0;
+      const int64_t s1 = std::min<int64_t>(nout, (a0 + w.n) * spf - deficit);
+      if (s1 > s0) {
+        if (b->desc.keep_output) {
+          const size_t old = r->wave.size();
+          r->wave.resize(old + (s1 - s0));
+          CK(cudaMemcpyAsync(r->wave.data() + old, S.d_wave + (size_t)i * nout + s0, (s1 - s0) * 4,
+                             cudaMemcpyDeviceToHost, b->st));
+          b->d2h += (s1 - s0) * 4;
+        }
+        r->samples += s1 - s0;
+        if (samples) *samples += s1 - s0;
+      }
+      S.emitted[r->id] = w.e + w.n;
+      if (r->finished && w.e + w.n >= r->step_idx) S.emitted.erase(r->id);
+    }
+    if (b->desc.keep_output) CK(cudaStreamSynchronize(b->st));
   }
 }
 

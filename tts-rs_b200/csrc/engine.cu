@@ -199,6 +199,12 @@ extern "C" q3t_status q3t_model_load(const q3t_model_desc *desc, q3t_model **out
     m->max_active = desc->max_active > 0 ? desc->max_active : 64;
     if (m->max_active > 64) FAIL(Q3T_INVALID_INPUT, "max_active %d > 64", m->max_active);
     init_kernel_attributes();
+    {  // keep stream-ordered allocations (codec workspaces) cached between calls
+      cudaMemPool_t pool;
+      CK(cudaDeviceGetDefaultMemPool(&pool, desc->device));
+      uint64_t thr = UINT64_MAX;
+      CK(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr));
+    }
     cudaStream_t st;
     CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
     Tensors T(desc);
@@ -353,10 +359,10 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
 static void batch_destroy(q3t_batch *b) {
   for (auto &kv : b->graphs) cudaGraphExecDestroy(kv.second.exec);
   b->graphs.clear();
-  for (auto &r : b->reqs) {
-    if (r.second->d_trailing) cudaFree(r.second->d_trailing);
-    if (r.second->d_pad) cudaFree(r.second->d_pad);
-  }
+  for (auto &r : b->reqs)
+    for (void *p : {(void *)r.second->d_trailing, (void *)r.second->d_pad, (void *)r.second->d_prompt,
+                    (void *)r.second->d_forced})
+      if (p) cudaFree(p);
   if (b->h_meta) cudaFreeHost(b->h_meta);
   if (b->h_extra) cudaFreeHost(b->h_extra);
   if (b->h_pmeta) cudaFreeHost(b->h_pmeta);
@@ -559,9 +565,10 @@ static void release(q3t_batch *b, Req *r) {
   r->pages.clear();
   if (r->slot >= 0) b->slots[r->slot] = nullptr;
   r->slot = -1;
-  if (r->d_trailing) cudaFree(r->d_trailing);
-  if (r->d_pad) cudaFree(r->d_pad);
-  r->d_trailing = r->d_pad = nullptr;
+  for (void *p : {(void *)r->d_trailing, (void *)r->d_pad, (void *)r->d_prompt, (void *)r->d_forced})
+    if (p) cudaFree(p);
+  r->d_trailing = r->d_pad = r->d_prompt = nullptr;
+  r->d_forced = nullptr;
 }
 
 static SampleParams to_params(const q3t_sampling &s) {
@@ -595,15 +602,9 @@ static void prefill(q3t_batch *b, Req *r) {
   const int fc = r->forced.empty() ? 0 : r->max_new;
   CK(cudaMemcpyAsync(b->d_forced_count + s, &fc, sizeof(int), cudaMemcpyHostToDevice, b->st));
   if (fc)
-    CK(cudaMemcpyAsync(b->d_forced + (size_t)s * b->maxF * b->G, r->forced.data(), r->forced.size() * 8,
-                       cudaMemcpyHostToDevice, b->st));
-  CK(cudaMalloc(&r->d_trailing, (size_t)r->trailing_len * H * 4));
-  CK(cudaMalloc(&r->d_pad, (size_t)H * 4));
-  CK(cudaMemcpyAsync(r->d_trailing, r->trailing.data(), r->trailing.size() * 4, cudaMemcpyHostToDevice, b->st));
-  CK(cudaMemcpyAsync(r->d_pad, r->pad.data(), r->pad.size() * 4, cudaMemcpyHostToDevice, b->st));
-  float *d_prompt;
-  CK(cudaMallocAsync((void **)&d_prompt, (size_t)r->S * H * 4, b->st));
-  CK(cudaMemcpyAsync(d_prompt, r->prompt.data(), r->prompt.size() * 4, cudaMemcpyHostToDevice, b->st));
+    CK(cudaMemcpyAsync(b->d_forced + (size_t)s * b->maxF * b->G, r->d_forced, r->forced.size() * 8,
+                       cudaMemcpyDeviceToDevice, b->st));
+  const float *d_prompt = r->d_prompt;
   // chunks of kPrefillTok tokens; each token attends to [0, pos] (causal by position)
   const int nch = (r->S + kPrefillTok - 1) / kPrefillTok;
   const int ps = b->pmeta_stride();
@@ -625,7 +626,6 @@ static void prefill(q3t_batch *b, Req *r) {
     run_stack(b, m->talker, talker_kv(b), tv, n, false, bucket_split(c0 + n));
     last_n = n;
   }
-  CK(cudaFreeAsync(d_prompt, b->st));
   int *dm = b->d_pmeta + (size_t)(nch - 1) * ps;
   // final norm of the last prompt token -> hidden[slot] and codec_head input
   rmsnorm(b->x, H, 1, last_n - 1, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps, dm + 1, 1, b->tlog,
@@ -709,6 +709,7 @@ static void retire(q3t_batch *b, Req *r, int64_t *samples) {
     CK(cudaMemcpyAsync(rg.data(), b->d_raw + (size_t)r->slot * b->maxF * G, rg.size() * 4,
                        cudaMemcpyDeviceToHost, b->st));
     CK(cudaStreamSynchronize(b->st));
+    b->d2h += (int64_t)T * G * 12;
   }
   r->codes.assign((size_t)G * T, 0);
   r->sampled.assign((size_t)G * T, 0);
@@ -726,6 +727,7 @@ static void retire(q3t_batch *b, Req *r, int64_t *samples) {
                             nullptr, b->st);
     r->samples = n;
     if (samples) *samples += n;
+    if (b->desc.keep_output) b->d2h += n * 4;
   }
   if (!b->desc.keep_output && !b->session_mode) r->codes.clear();
   r->state = 2;
@@ -734,6 +736,7 @@ static void retire(q3t_batch *b, Req *r, int64_t *samples) {
 
 static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
   q3t_step_stats S{};
+  CK(cudaEventRecord(b->ev0, b->st));
   admit(b, &S.admitted);
   std::vector<Req *> act;
   for (int i = 0; i < b->A; i++) {
@@ -756,8 +759,18 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
   }
   const int B = (int)act.size();
   S.active = B;
-  if (B == 0) {
+  auto report = [&] {
+    CK(cudaEventRecord(b->ev1, b->st));
+    CK(cudaEventSynchronize(b->ev1));
+    CK(cudaEventElapsedTime(&b->last_ms, b->ev0, b->ev1));
+    S.device_ms = b->last_ms;
+    S.h2d_bytes = b->h2d;
+    S.d2h_bytes = b->d2h;
+    b->h2d = b->d2h = 0;
     if (stats) *stats = S;
+  };
+  if (B == 0) {
+    report();
     return;
   }
   int maxlen = 1;
@@ -778,6 +791,7 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
     hm[b->off_p0pos() + 2 * i + 1] = 1;
     b->h_extra[i] = r->step_idx < r->trailing_len ? r->d_trailing + (size_t)r->step_idx * b->H : r->d_pad;
     maxlen = std::max(maxlen, r->cache_len + 1);
+    S.kv_tokens += r->cache_len + 1;
   }
   hm[M_NTOK_B] = B;
   hm[M_NTOK_2B] = 2 * B;
@@ -786,13 +800,11 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
   CK(cudaMemcpyAsync(b->d_extra, b->h_extra, B * sizeof(float *), cudaMemcpyHostToDevice, b->st));
   const int mt = bucket_tok(B), ms = bucket_split(maxlen);
   const int seed = act[0]->step_idx;
-  CK(cudaEventRecord(b->ev0, b->st));
+  b->h2d += b->meta_n * sizeof(int) + B * sizeof(float *);
   run_graph(b, std::make_tuple(0, mt, ms), [&] { enqueue_frame(b, mt, ms, seed); });
-  CK(cudaEventRecord(b->ev1, b->st));
   CK(cudaMemcpyAsync(b->h_eosflag, b->d_eosflag, B * sizeof(int), cudaMemcpyDeviceToHost, b->st));
   CK(cudaStreamSynchronize(b->st));
-  CK(cudaEventElapsedTime(&b->last_ms, b->ev0, b->ev1));
-  S.device_ms = b->last_ms;
+  b->d2h += B * sizeof(int);
   for (int i = 0; i < B; i++) {
     Req *r = act[i];
     r->step_idx++;
@@ -813,7 +825,7 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
       retire(b, r, &S.samples);
       S.retired++;
     }
-  if (stats) *stats = S;
+  report();
 }
 
 static Req *new_request(q3t_batch *b, const q3t_session_desc *d, const int64_t *forced) {
@@ -854,6 +866,21 @@ static Req *new_request(q3t_batch *b, const q3t_session_desc *d, const int64_t *
   if (r->forced_first >= tc.talker.vocab_size) FAIL(Q3T_INVALID_INPUT, "forced first token out of range");
   for (auto id : r->suppress)
     if (id < 0) FAIL(Q3T_INVALID_INPUT, "negative suppress id");
+  // inputs go to device memory at submit time, so admission finds them resident
+  CK(cudaMalloc(&r->d_prompt, r->prompt.size() * 4));
+  CK(cudaMalloc(&r->d_trailing, r->trailing.size() * 4));
+  CK(cudaMalloc(&r->d_pad, r->pad.size() * 4));
+  CK(cudaMemcpyAsync(r->d_prompt, r->prompt.data(), r->prompt.size() * 4, cudaMemcpyHostToDevice, b->st));
+  CK(cudaMemcpyAsync(r->d_trailing, r->trailing.data(), r->trailing.size() * 4, cudaMemcpyHostToDevice, b->st));
+  CK(cudaMemcpyAsync(r->d_pad, r->pad.data(), r->pad.size() * 4, cudaMemcpyHostToDevice, b->st));
+  b->h2d += (r->prompt.size() + r->trailing.size() + r->pad.size()) * 4;
+  if (!r->forced.empty()) {
+    CK(cudaMalloc(&r->d_forced, r->forced.size() * 8));
+    CK(cudaMemcpyAsync(r->d_forced, r->forced.data(), r->forced.size() * 8, cudaMemcpyHostToDevice, b->st));
+    b->h2d += r->forced.size() * 8;
+  }
+  CK(cudaStreamSynchronize(b->st));
+  std::vector<float>().swap(r->prompt);  // the device copy is the one that is used
   Req *raw = r.get();
   b->reqs[raw->id] = std::move(r);
   return raw;
@@ -981,6 +1008,12 @@ extern "C" q3t_status q3t_batch_pending(q3t_batch *b, int *queued, int *active) 
   for (auto *r : b->slots) a += r != nullptr;
   if (queued) *queued = (int)b->queue.size();
   if (active) *active = a;
+  return Q3T_OK;
+}
+
+extern "C" q3t_status q3t_batch_stream(q3t_batch *b, void **stream) {
+  if (!b || !stream) return Q3T_INVALID_INPUT;
+  *stream = (void *)b->st;
   return Q3T_OK;
 }
 

@@ -102,7 +102,8 @@ struct Req {
   bool eos_seen = false, finished = false;
   int cache_len = 0;
   std::vector<int> pages;
-  float *d_trailing = nullptr, *d_pad = nullptr;
+  float *d_trailing = nullptr, *d_pad = nullptr, *d_prompt = nullptr;
+  int64_t *d_forced = nullptr;
   std::vector<int64_t> codes;  // [G][T] once retired
   std::vector<int32_t> sampled;  // [G][T] sampled tokens before teacher forcing
   std::vector<float> wave;
@@ -193,6 +194,7 @@ struct q3t_batch {
   int64_t next_id = 1;
   float last_ms = 0.f;
   bool session_mode = false;
+  int64_t h2d = 0, d2h = 0;  // bytes copied since the last step report
 
   int off_slot() const { return q3t::M_HDR; }
   int off_tpos() const { return q3t::M_HDR + A; }

@@ -90,7 +90,8 @@ class BatchDesc(C.Structure):
 
 class StepStats(C.Structure):
     _fields_ = [("active", C.c_int), ("admitted", C.c_int), ("retired", C.c_int),
-                ("frames", C.c_int64), ("samples", C.c_int64), ("device_ms", C.c_float)]
+                ("frames", C.c_int64), ("samples", C.c_int64), ("device_ms", C.c_float),
+                ("kv_tokens", C.c_int64), ("h2d_bytes", C.c_int64), ("d2h_bytes", C.c_int64)]
 
 
 EXPORTS = [
@@ -99,7 +100,7 @@ EXPORTS = [
     "q3t_session_decode_embeds", "q3t_session_load_kv", "q3t_session_last_ms",
     "q3t_session_free", "q3t_codec_decode", "q3t_codec_out_len", "q3t_batch_create",
     "q3t_batch_submit", "q3t_batch_step", "q3t_batch_poll", "q3t_batch_take",
-    "q3t_batch_pending", "q3t_batch_free", "q3t_last_error", "q3t_version",
+    "q3t_batch_pending", "q3t_batch_stream", "q3t_batch_free", "q3t_last_error", "q3t_version",
     "q3t_kernel_launches",
 ]
 
@@ -141,6 +142,7 @@ def lib():
         L.q3t_batch_take.argtypes = [C.c_void_p, C.c_int64, _I64, C.POINTER(C.c_int32), C.c_int, _F,
                                      C.c_int64]
         L.q3t_batch_pending.argtypes = [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        L.q3t_batch_stream.argtypes = [C.c_void_p, C.POINTER(C.c_void_p)]
         L.q3t_batch_free.argtypes = [C.c_void_p]
         L.q3t_batch_free.restype = None
         _LIB = L
@@ -381,7 +383,8 @@ class Batch:
         s = StepStats()
         check(lib().q3t_batch_step(self.h, C.byref(s)))
         return {"active": s.active, "admitted": s.admitted, "retired": s.retired,
-                "frames": s.frames, "samples": s.samples, "device_ms": s.device_ms}
+                "frames": s.frames, "samples": s.samples, "device_ms": s.device_ms,
+                "kv_tokens": s.kv_tokens, "h2d_bytes": s.h2d_bytes, "d2h_bytes": s.d2h_bytes}
 
     def poll(self, rid):
         st, fr, sm = C.c_int(), C.c_int64(), C.c_int64()
@@ -398,6 +401,12 @@ class Batch:
                                    sampled.ctypes.data_as(C.POINTER(C.c_int32)), T, _fp(wave),
                                    0 if wave is None else ns))
         return codes, sampled, wave
+
+    def stream(self):
+        """cudaStream_t of the batch, as an int (torch.cuda.ExternalStream)."""
+        p = C.c_void_p()
+        check(lib().q3t_batch_stream(self.h, C.byref(p)))
+        return p.value or 0
 
     def pending(self):
         q, a = C.c_int(), C.c_int()
