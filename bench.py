@@ -50,6 +50,9 @@ def parse():
     p.add_argument("--cpu-frames", type=int, default=48, help="bounded CPU-baseline sample (frames)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--kv-pages", type=int, default=8192, help="talker KV pool size (16-token pages)")
+    p.add_argument("--profile", action="store_true",
+                   help="bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     return p.parse_args()
 
 
@@ -166,7 +169,7 @@ def main():
     cfg = S.TalkerConfig()
     cc = S.CodecConfig()
     model = q3t.Model(cfg, S.make_talker_weights(cfg, 0), cc, S.make_codec_weights(cc, 0), device=local,
-                      kv_pages=8192, max_active=args.max_active)
+                      kv_pages=args.kv_pages, max_active=args.max_active)
     reqs = workload(args.requests)
     mine = [i for i in range(len(reqs)) if i % world == rank]
     inputs = {i: request_inputs(i, *reqs[i]) for i in mine}
@@ -193,11 +196,15 @@ def main():
                                         else "/tmp", f"clocks_r{rank}.csv"))
     launches0 = q3t.kernel_launches()
     barrier()
+    if args.profile:
+        torch.cuda.profiler.start()
     e0.record(stream)
     t0 = time.perf_counter()
     steps = [b.step() for _ in range(args.steps)]
     e1.record(stream)
     barrier()
+    if args.profile:
+        torch.cuda.profiler.stop()
     wall = time.perf_counter() - t0
     launches = q3t.kernel_launches() - launches0
     ck = clocks.stop()
