@@ -733,7 +733,7 @@ static ConvArgs conv_args(const ConvW &w, const __half *X, int B, int Lin, int i
 static void decode_device(CodecModel *c, const int64_t *d_codes, int B, int T, float *d_wave, int16_t *d_pcm,
                           cudaStream_t st) {
   const auto &k = c->c;
-  const int half = k.codebook_dim / 2, D = k.codebook_dim, LAT = k.latent_dim, H = k.hidden_size;
+  const int half = k.codebook_dim / 2, LAT = k.latent_dim, H = k.hidden_size;
   const int nh = k.num_attention_heads, nkv = k.num_key_value_heads, qd = nh * 64, kd = nkv * 64;
   const int M0 = B * T;
   // workspace sizes

@@ -328,10 +328,23 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
   const int T = b->Tmax;
   b->x = ar.zalloc<float>((size_t)T * H);
   b->xn = ar.zalloc<uint16_t>((size_t)T * H);
-  b->qkv = ar.zalloc<float>((size_t)T * std::max(b->NQKV, b->NQKVP));
+  // partial-sum workspaces: at most K / 64 splits of T rows each
+  const int Hm = std::max(tc.talker.hidden_size, tc.predictor.hidden_size);
+  const int Im = std::max(tc.talker.intermediate_size, tc.predictor.intermediate_size);
+  const int QDm = 128 * std::max(tc.talker.num_attention_heads, tc.predictor.num_attention_heads);
+  b->n_qkv = (long long)(Hm / 64) * T * std::max(b->NQKV, b->NQKVP);
+  b->n_o = (long long)(QDm / 64) * T * Hm;
+  b->n_gu = (long long)(Hm / 64) * T * 2 * Im;
+  b->n_down = (long long)(Im / 64) * T * Hm;
+  b->n_head = (long long)(Hm / 64) * T * std::max(b->V, b->PV);
+  b->ws_qkv = ar.alloc<float>(b->n_qkv);
+  b->ws_o = ar.alloc<float>(b->n_o);
+  b->ws_gu = ar.alloc<float>(b->n_gu);
+  b->ws_down = ar.alloc<float>(b->n_down);
+  b->ws_head = ar.alloc<float>(b->n_head);
   b->q = ar.zalloc<uint16_t>((size_t)T * 128 * std::max(tc.talker.num_attention_heads, tc.predictor.num_attention_heads));
   b->attn = ar.zalloc<uint16_t>((size_t)T * 128 * std::max(tc.talker.num_attention_heads, tc.predictor.num_attention_heads));
-  b->gu = ar.zalloc<float>((size_t)T * b->I2);
+  b->act = ar.zalloc<uint16_t>((size_t)T * b->I2 / 2);
   b->tlog = ar.zalloc<float>((size_t)T * b->V);
   b->plog = ar.zalloc<float>((size_t)(G - 1) * A * b->PV);
   b->ws.max_split = kMaxSplit;
@@ -352,6 +365,12 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
   CK(cudaMallocHost(&b->h_eosflag, T * sizeof(int)));
   CK(cudaMallocHost(&b->h_codes, (size_t)A * G * sizeof(int64_t)));
   b->slots.assign(A, nullptr);
+  b->d_ctr = ar.zalloc<unsigned>(kFrameCtrWords);
+  b->d_err = ar.zalloc<int>(1);
+  CK(cudaMallocHost(&b->h_err, sizeof(int)));
+  *b->h_err = 0;
+  const char *fe = getenv("Q3T_FRAME");
+  b->use_frame_kernel = !(fe && fe[0] == '0');
   CK(cudaStreamSynchronize(b->st));
   CK(cudaDeviceSynchronize());  // the arena's cudaMemset zero-fills run on the legacy stream
 }
@@ -359,6 +378,9 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
 static void batch_destroy(q3t_batch *b) {
   for (auto &kv : b->graphs) cudaGraphExecDestroy(kv.second.exec);
   b->graphs.clear();
+  for (auto &kv : b->programs) cudaFree(kv.second.dev);
+  b->programs.clear();
+  if (b->h_err) cudaFreeHost(b->h_err);
   for (auto &r : b->reqs)
     for (void *p : {(void *)r.second->d_trailing, (void *)r.second->d_pad, (void *)r.second->d_prompt,
                     (void *)r.second->d_forced})
@@ -430,28 +452,32 @@ static int bucket_split(int L) {
   return n;
 }
 
-// One decoder stack over the token batch described by tv.
-static void run_stack(q3t_batch *b, const LMStack &S, KVView kv, TokView tv, int max_tok, bool fused,
+// One decoder stack over the token batch described by tv.  Returns the
+// pending split-K partials of the last down projection, which the caller's
+// final RMSNorm folds into the residual stream.
+static Part run_stack(q3t_batch *b, const LMStack &S, KVView kv, TokView tv, int max_tok, bool fused,
                       int max_split) {
   const auto &c = S.cfg;
   const int H = c.hidden_size, I = c.intermediate_size, nh = c.num_attention_heads,
             nkv = c.num_key_value_heads;
   const int NQ = (nh + 2 * nkv) * 128, QD = nh * 128;
+  const int T = b->Tmax;
+  Part pending{nullptr, 0, 0, 0};
   for (int l = 0; l < c.num_hidden_layers; l++) {
-    rmsnorm(b->x, H, 1, 0, S.in_norm[l], b->xn, H, H, c.rms_norm_eps, tv.ntok, max_tok, b->qkv, NQ, NQ,
-            nullptr, nullptr, b->st);
-    linear(S.wqkv[l], NQ, H, b->xn, H, 0, b->qkv, NQ, tv.ntok, max_tok, b->st);
+    rmsnorm(b->x, H, 1, 0, pending, S.in_norm[l], b->xn, H, H, c.rms_norm_eps, tv.ntok, max_tok, nullptr, nullptr,
+            b->st);
+    const Part qkv = linear(S.wqkv[l], NQ, H, b->xn, H, b->ws_qkv, b->n_qkv, T, tv.ntok, max_tok, b->st);
     if (!fused)
-      qkv_post(b->qkv, NQ, S.q_norm[l], S.k_norm[l], S.inv_freq, c.rms_norm_eps, nh, nkv, tv, max_tok,
-               b->q, kv, l, b->st);
-    attention(fused ? 1 : 0, b->qkv, NQ, S.q_norm[l], S.k_norm[l], S.inv_freq, c.rms_norm_eps, b->q, kv, l,
-              tv, max_tok, nh, kChunk, max_split, b->ws, b->attn, b->st);
-    linear(S.wo[l], H, QD, b->attn, QD, 0, b->x, H, tv.ntok, max_tok, b->st);
-    rmsnorm(b->x, H, 1, 0, S.post_norm[l], b->xn, H, H, c.rms_norm_eps, tv.ntok, max_tok, b->gu, 2 * I,
-            2 * I, nullptr, nullptr, b->st);
-    linear(S.wgu[l], 2 * I, H, b->xn, H, 0, b->gu, 2 * I, tv.ntok, max_tok, b->st);
-    linear(S.wdown[l], H, I, b->gu, 2 * I, 1, b->x, H, tv.ntok, max_tok, b->st);
+      qkv_post(qkv, S.q_norm[l], S.k_norm[l], S.inv_freq, c.rms_norm_eps, nh, nkv, tv, max_tok, b->q, kv, l, b->st);
+    attention(fused ? 1 : 0, qkv, S.q_norm[l], S.k_norm[l], S.inv_freq, c.rms_norm_eps, b->q, kv, l, tv, max_tok, nh,
+              kChunk, max_split, b->ws, b->attn, b->st);
+    const Part o = linear(S.wo[l], H, QD, b->attn, QD, b->ws_o, b->n_o, T, tv.ntok, max_tok, b->st);
+    rmsnorm(b->x, H, 1, 0, o, S.post_norm[l], b->xn, H, H, c.rms_norm_eps, tv.ntok, max_tok, nullptr, nullptr, b->st);
+    const Part gu = linear(S.wgu[l], 2 * I, H, b->xn, H, b->ws_gu, b->n_gu, T, tv.ntok, max_tok, b->st);
+    silu_mul(gu, I, tv.ntok, max_tok, b->act, b->st);
+    pending = linear(S.wdown[l], H, I, b->act, I, b->ws_down, b->n_down, T, tv.ntok, max_tok, b->st);
   }
+  return pending;
 }
 
 static KVView talker_kv(q3t_batch *b) {
@@ -461,6 +487,77 @@ static KVView talker_kv(q3t_batch *b) {
 static KVView pred_kv(q3t_batch *b) {
   return KVView{b->pk, b->pv, b->p_layer_stride, b->d_ppt, 2, b->m->tc.predictor.num_key_value_heads};
 }
+
+
+// ---------------------------------------------------------------------------
+// The decode frame as a phase program (lm_kernels.cuh Phase): built once per
+// (token bucket mt, attention split bucket ms) and replayed every step; the
+// per-step inputs (active slots, positions, frames, trailing-text rows, step
+// counter) live in the device metadata the phases point at.
+// ---------------------------------------------------------------------------
+struct ProgBuilder {
+  q3t_batch *b;
+  std::vector<Phase> ph;
+  int target;
+  Phase &add(int type, int max_tok) {
+    ph.emplace_back();
+    memset(&ph.back(), 0, sizeof(Phase));
+    ph.back().type = type;
+    ph.back().max_tok = max_tok;
+    return ph.back();
+  }
+  void norm(const RmsArgs &a, int max_tok) { add(PH_NORM, max_tok).norm = a; }
+  Part gemm(const uint16_t *W, int N, int K, const uint16_t *X, int ldx, float *ws, long long cap, const int *ntok,
+            int max_tok) {
+    Part P;
+    const LinArgs a = linear_plan(W, N, K, X, ldx, ws, cap, b->Tmax, ntok, max_tok, target, &P);
+    add(PH_GEMM, max_tok).lin = a;
+    return P;
+  }
+  // one decoder stack; the first layer's input norm must already have been
+  // emitted by the caller (it builds the input rows); returns the pending
+  // down-projection partials
+  Part stack(const LMStack &S, KVView kv, TokView tv, int max_tok, bool fused, int max_split) {
+    const auto &c = S.cfg;
+    const int H = c.hidden_size, I = c.intermediate_size, nh = c.num_attention_heads, nkv = c.num_key_value_heads;
+    const int NQ = (nh + 2 * nkv) * 128, QD = nh * 128;
+    Part pending{nullptr, 0, 0, 0};
+    for (int l = 0; l < c.num_hidden_layers; l++) {
+      if (l > 0)
+        norm(rms_args(b->x, H, 1, 0, pending, S.in_norm[l], b->xn, H, H, c.rms_norm_eps, tv.ntok, nullptr, nullptr),
+             max_tok);
+      const Part qkv = gemm(S.wqkv[l], NQ, H, b->xn, H, b->ws_qkv, b->n_qkv, tv.ntok, max_tok);
+      if (!fused) {
+        Phase &q = add(PH_QKV, max_tok);
+        q.qkv = QkvArgs{qkv, S.q_norm[l], S.k_norm[l], S.inv_freq, c.rms_norm_eps, nh, nkv, tv, b->q, kv, l};
+      }
+      Phase &at = add(PH_ATTN, max_tok);
+      AttnArgs &aa = at.attn;
+      aa.qkv = qkv;
+      aa.q_norm = S.q_norm[l];
+      aa.k_norm = S.k_norm[l];
+      aa.inv_freq = S.inv_freq;
+      aa.eps = c.rms_norm_eps;
+      aa.qin = b->q;
+      aa.kv = kv;
+      aa.layer = l;
+      aa.tv = tv;
+      aa.nh = nh;
+      aa.chunk = kChunk;
+      aa.max_split = max_split;
+      aa.fused = fused ? 1 : 0;
+      aa.scale = 1.0f / sqrtf(128.0f);
+      aa.ws = b->ws;
+      aa.out = b->attn;
+      const Part o = gemm(S.wo[l], H, QD, b->attn, QD, b->ws_o, b->n_o, tv.ntok, max_tok);
+      norm(rms_args(b->x, H, 1, 0, o, S.post_norm[l], b->xn, H, H, c.rms_norm_eps, tv.ntok, nullptr, nullptr), max_tok);
+      const Part gu = gemm(S.wgu[l], 2 * I, H, b->xn, H, b->ws_gu, b->n_gu, tv.ntok, max_tok);
+      add(PH_SILU, max_tok).silu = SiluArgs{gu, I, tv.ntok, b->act};
+      pending = gemm(S.wdown[l], H, I, b->act, I, b->ws_down, b->n_down, tv.ntok, max_tok);
+    }
+    return pending;
+  }
+};
 
 static SampleArgs base_sample(q3t_batch *b) {
   SampleArgs a{};
@@ -478,31 +575,43 @@ static SampleArgs base_sample(q3t_batch *b) {
   return a;
 }
 
-// The decode frame for the B active requests described by the step metadata.
-static void enqueue_frame(q3t_batch *b, int mt, int max_split, int step_seed) {
+static void build_frame(q3t_batch *b, int mt, int max_split, std::vector<Phase> &out) {
   q3t_model *m = b->m;
   const auto &tc = m->tc;
   const int G = b->G, H = b->H, PV = b->PV, V = b->V;
   int *meta = b->d_meta;
   const int *ntokB = meta + M_NTOK_B, *ntok2B = meta + M_NTOK_2B;
   const int *slot = meta + b->off_slot(), *frame = meta + b->off_frame();
-  // ---- code predictor (infer/mod.rs:434-535) ----
-  pred_input0(b->d_hidden, m->talker_emb, b->d_codes, G, slot, ntokB, mt, H, b->x, b->st);
-  TokView tv0{ntok2B, meta + b->off_p0seq(), meta + b->off_p0pos(), 0};
-  run_stack(b, m->pred, pred_kv(b), tv0, 2 * mt, false, 1);
+  ProgBuilder P{b, {}, frame_target_items()};
   const auto &pc = tc.predictor;
+  // ---- code predictor (infer/mod.rs:434-535) ----
+  // pass 0 input rows: [talker hidden, talker codec embedding of code 0]
+  {
+    RmsArgs a = rms_args(b->x, H, 1, 0, Part{}, m->pred.in_norm[0], b->xn, H, H, pc.rms_norm_eps, ntok2B, nullptr,
+                         nullptr);
+    a.emb.src = 1;
+    a.emb.G = G;
+    a.emb.hidden = b->d_hidden;
+    a.emb.emb0 = m->talker_emb;
+    a.emb.codes = b->d_codes;
+    a.emb.slot = slot;
+    P.norm(a, 2 * mt);
+  }
   for (int j = 0; j < G - 1; j++) {
-    if (j > 0) {
-      pred_input(m->cp_emb[j - 1], b->d_codes, G, j, slot, ntokB, mt, H, b->x, b->st);
+    Part pend;
+    if (j == 0) {
+      TokView tv0{ntok2B, meta + b->off_p0seq(), meta + b->off_p0pos(), 0};
+      pend = P.stack(m->pred, pred_kv(b), tv0, 2 * mt, false, 1);
+    } else {
       TokView tvj{ntokB, slot, meta + b->off_zero(), j + 1};
-      run_stack(b, m->pred, pred_kv(b), tvj, mt, true, 1);
+      pend = P.stack(m->pred, pred_kv(b), tvj, mt, true, 1);
     }
-    float *lg = b->plog + (size_t)j * b->A * PV;
-    rmsnorm(b->x, H, j == 0 ? 2 : 1, j == 0 ? 1 : 0, m->pred.final_norm, b->xn, H, H, pc.rms_norm_eps, ntokB,
-            mt, lg, PV, PV, nullptr, nullptr, b->st);
-    linear(m->lm_heads[j], PV, H, b->xn, H, 0, lg, PV, ntokB, mt, b->st);
+    P.norm(rms_args(b->x, H, j == 0 ? 2 : 1, j == 0 ? 1 : 0, pend, m->pred.final_norm, b->xn, H, H, pc.rms_norm_eps,
+                    ntokB, nullptr, nullptr),
+           mt);
     SampleArgs a = base_sample(b);
-    a.logits = lg;
+    a.part = P.gemm(m->lm_heads[j], PV, H, b->xn, H, b->ws_head, b->n_head, ntokB, mt);
+    a.logits = b->plog + (size_t)j * b->A * PV;
     a.ldl = PV;
     a.V = PV;
     a.ntok = ntokB;
@@ -512,19 +621,46 @@ static void enqueue_frame(q3t_batch *b, int mt, int max_split, int step_seed) {
     a.frame = frame;
     a.fadd = 0;
     a.hist_mode = 2;
-    a.step_seed = step_seed;
-    sample(a, mt, b->st);
+    a.seed_p = meta + M_SEED;
+    a.step_seed = 0;
+    Phase &sp = P.add(PH_SAMPLE, mt);
+    sp.smp = a;
+    sp.has_tail = 1;
+    // the tail builds the next input row of this token and normalises it
+    if (j + 1 < G - 1) {
+      RmsArgs t = rms_args(b->x, H, 1, 0, Part{}, m->pred.in_norm[0], b->xn, H, H, pc.rms_norm_eps, ntokB, nullptr,
+                           nullptr);
+      t.emb.src = 2;
+      t.emb.G = G;
+      t.emb.col = j + 1;
+      t.emb.emb = m->cp_emb[j];
+      t.emb.codes = b->d_codes;
+      t.emb.slot = slot;
+      sp.tail = t;
+    } else {  // next talker input: codec-group embedding + trailing text / pad
+      RmsArgs t = rms_args(b->x, H, 1, 0, Part{}, m->talker.in_norm[0], b->xn, H, H, tc.talker.rms_norm_eps, ntokB,
+                           nullptr, nullptr);
+      t.emb.src = 3;
+      t.emb.G = G;
+      t.emb.emb0 = m->talker_emb;
+      t.emb.embs = (const uint16_t *const *)m->cp_emb_dev;
+      t.emb.codes = b->d_codes;
+      t.emb.slot = slot;
+      t.emb.extra = b->d_extra;
+      t.emb.frame = frame;
+      t.emb.hist = b->d_hist_codes;
+      t.emb.hist_frames = b->maxF;
+      sp.tail = t;
+    }
   }
-  // ---- next talker input: codec-group embedding + trailing text / pad ----
-  embed_codes(m->talker_emb, (const uint16_t *const *)m->cp_emb_dev, G, H, b->d_codes, slot, b->d_extra, frame,
-              b->d_hist_codes, b->maxF, ntokB, mt, b->x, b->st);
   // ---- talker decode (model.rs:94-113) + codec_head + sample ----
   TokView tvt{ntokB, slot, meta + b->off_tpos(), 0};
-  run_stack(b, m->talker, talker_kv(b), tvt, mt, true, max_split);
-  rmsnorm(b->x, H, 1, 0, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps, ntokB, mt, b->tlog, V, V,
-          b->d_hidden, slot, b->st);
-  linear(m->codec_head, V, H, b->xn, H, 0, b->tlog, V, ntokB, mt, b->st);
+  const Part tp = P.stack(m->talker, talker_kv(b), tvt, mt, true, max_split);
+  P.norm(rms_args(b->x, H, 1, 0, tp, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps, ntokB, b->d_hidden,
+                  slot),
+         mt);
   SampleArgs a = base_sample(b);
+  a.part = P.gemm(m->codec_head, V, H, b->xn, H, b->ws_head, b->n_head, ntokB, mt);
   a.logits = b->tlog;
   a.ldl = V;
   a.V = V;
@@ -536,8 +672,35 @@ static void enqueue_frame(q3t_batch *b, int mt, int max_split, int step_seed) {
   a.fadd = 1;
   a.hist_mode = 1;
   a.eos_flag = b->d_eosflag;
-  a.step_seed = step_seed + 1;
-  sample(a, mt, b->st);
+  a.seed_p = meta + M_SEED;
+  a.step_seed = 1;
+  P.add(PH_SAMPLE, mt).smp = a;
+  out.swap(P.ph);
+}
+
+// Runs the decode frame: the persistent kernel (default) or, with
+// Q3T_FRAME=0, one standalone kernel per phase.
+static void enqueue_frame(q3t_batch *b, int mt, int max_split) {
+  auto key = std::make_pair(mt, max_split);
+  auto it = b->programs.find(key);
+  if (it == b->programs.end()) {
+    std::vector<Phase> ph;
+    build_frame(b, mt, max_split, ph);
+    check_launches();
+    Program pr;
+    pr.host = ph;
+    CK(cudaMalloc(&pr.dev, ph.size() * sizeof(Phase)));
+    CK(cudaMemcpyAsync(pr.dev, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice, b->st));
+    CK(cudaStreamSynchronize(b->st));
+    it = b->programs.emplace(key, std::move(pr)).first;
+  }
+  const Program &pr = it->second;
+  if (b->use_frame_kernel) {
+    frame_launch(pr.dev, (int)pr.host.size(), FrameCtl{b->d_ctr, b->d_err}, b->st);
+  } else {
+    run_graph(b, std::make_tuple(0, mt, max_split), [&] { run_phases(pr.host.data(), (int)pr.host.size(), b->st); });
+  }
+  check_launches();
 }
 
 static int alloc_page(q3t_batch *b, Req *r) {
@@ -623,17 +786,20 @@ static void prefill(q3t_batch *b, Req *r) {
     CK(cudaMemcpyAsync(dm, hm, ps * sizeof(int), cudaMemcpyHostToDevice, b->st));
     CK(cudaMemcpyAsync(b->x, d_prompt + (size_t)c0 * H, (size_t)n * H * 4, cudaMemcpyDeviceToDevice, b->st));
     TokView tv{dm, dm + 8, dm + 8 + kPrefillTok, 0};
-    run_stack(b, m->talker, talker_kv(b), tv, n, false, bucket_split(c0 + n));
+    Part pend = run_stack(b, m->talker, talker_kv(b), tv, n, false, bucket_split(c0 + n));
+    // fold the last layer's partials into the residual of every prompt row
+    rmsnorm(b->x, H, 1, 0, pend, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps, dm, n, nullptr, nullptr,
+            b->st);
     last_n = n;
   }
   int *dm = b->d_pmeta + (size_t)(nch - 1) * ps;
   // final norm of the last prompt token -> hidden[slot] and codec_head input
-  rmsnorm(b->x, H, 1, last_n - 1, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps, dm + 1, 1, b->tlog,
-          V, V, b->d_hidden, dm + 2, b->st);
-  linear(m->codec_head, V, H, b->xn, H, 0, b->tlog, V, dm + 1, 1, b->st);
-  if (r->first_logits)
-    CK(cudaMemcpyAsync(r->first_logits, b->tlog, (size_t)V * 4, cudaMemcpyDeviceToHost, b->st));
+  rmsnorm(b->x, H, 1, last_n - 1, Part{nullptr, 0, 0, 0}, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps,
+          dm + 1, 1, b->d_hidden, dm + 2, b->st);
+  const Part head = linear(m->codec_head, V, H, b->xn, H, b->ws_head, b->n_head, b->Tmax, dm + 1, 1, b->st);
+
   SampleArgs a = base_sample(b);
+  a.part = head;
   a.logits = b->tlog;
   a.ldl = V;
   a.V = V;
@@ -650,6 +816,8 @@ static void prefill(q3t_batch *b, Req *r) {
   a.frame = dm + 2;
   a.raw = nullptr;
   sample(a, 1, b->st);
+  if (r->first_logits)  // the reduced logits (the sampler writes them before suppression)
+    CK(cudaMemcpyAsync(r->first_logits, b->tlog, (size_t)V * 4, cudaMemcpyDeviceToHost, b->st));
   // teacher forcing of the first token replaces it where it was sampled
   check_launches();
   CK(cudaMemcpyAsync(b->h_codes, b->d_codes + (size_t)s * b->G, 8, cudaMemcpyDeviceToHost, b->st));
@@ -796,15 +964,21 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
   hm[M_NTOK_B] = B;
   hm[M_NTOK_2B] = 2 * B;
   hm[M_ONE] = 1;
+  hm[M_SEED] = b->step_counter++;
   CK(cudaMemcpyAsync(b->d_meta, hm, b->meta_n * sizeof(int), cudaMemcpyHostToDevice, b->st));
   CK(cudaMemcpyAsync(b->d_extra, b->h_extra, B * sizeof(float *), cudaMemcpyHostToDevice, b->st));
   const int mt = bucket_tok(B), ms = bucket_split(maxlen);
-  const int seed = act[0]->step_idx;
   b->h2d += b->meta_n * sizeof(int) + B * sizeof(float *);
-  run_graph(b, std::make_tuple(0, mt, ms), [&] { enqueue_frame(b, mt, ms, seed); });
+  enqueue_frame(b, mt, ms);
   CK(cudaMemcpyAsync(b->h_eosflag, b->d_eosflag, B * sizeof(int), cudaMemcpyDeviceToHost, b->st));
+  CK(cudaMemcpyAsync(b->h_err, b->d_err, sizeof(int), cudaMemcpyDeviceToHost, b->st));
   CK(cudaStreamSynchronize(b->st));
-  b->d2h += B * sizeof(int);
+  b->d2h += B * sizeof(int) + sizeof(int);
+  if (*b->h_err) {
+    *b->h_err = 0;
+    CK(cudaMemsetAsync(b->d_err, 0, sizeof(int), b->st));
+    FAIL(Q3T_DEVICE_TIMEOUT, "decode frame: a grid barrier wait timed out");
+  }
   for (int i = 0; i < B; i++) {
     Req *r = act[i];
     r->step_idx++;
@@ -1196,10 +1370,11 @@ extern "C" q3t_status q3t_session_decode_embeds(q3t_session *s, const float *emb
     run_graph(b, std::make_tuple(1, 1, ms), [&] {
       const int *ntok = b->d_meta + M_NTOK_B, *slot = b->d_meta + b->off_slot();
       TokView tvt{ntok, slot, b->d_meta + b->off_tpos(), 0};
-      run_stack(b, m->talker, talker_kv(b), tvt, 1, true, ms);
-      rmsnorm(b->x, b->H, 1, 0, m->talker.final_norm, b->xn, b->H, b->H, m->tc.talker.rms_norm_eps, ntok, 1,
-              b->tlog, b->V, b->V, b->d_hidden, slot, b->st);
-      linear(m->codec_head, b->V, b->H, b->xn, b->H, 0, b->tlog, b->V, ntok, 1, b->st);
+      const Part tp = run_stack(b, m->talker, talker_kv(b), tvt, 1, true, ms);
+      rmsnorm(b->x, b->H, 1, 0, tp, m->talker.final_norm, b->xn, b->H, b->H, m->tc.talker.rms_norm_eps, ntok, 1,
+              b->d_hidden, slot, b->st);
+      const Part head = linear(m->codec_head, b->V, b->H, b->xn, b->H, b->ws_head, b->n_head, b->Tmax, ntok, 1, b->st);
+      reduce_rows(head, b->V, ntok, 1, b->tlog, b->st);
     });
     CK(cudaEventRecord(b->ev1, b->st));
     if (logits) CK(cudaMemcpyAsync(logits, b->tlog, (size_t)b->V * 4, cudaMemcpyDeviceToHost, b->st));

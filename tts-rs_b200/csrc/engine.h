@@ -112,6 +112,11 @@ struct Req {
   std::string error;
 };
 
+struct Program {
+  std::vector<Phase> host;
+  Phase *dev = nullptr;
+};
+
 struct GraphEntry {
   cudaGraphExec_t exec = nullptr;
   int64_t nodes = 0;
@@ -122,6 +127,7 @@ enum MetaOff {
   M_NTOK_2B = 1,
   M_ONE = 2,
   M_NPRE = 3,
+  M_SEED = 4,
   M_HDR = 8,
 };
 
@@ -174,8 +180,11 @@ struct q3t_batch {
   q3t::SampleParams *d_params = nullptr;
   // activations
   int Tmax = 0;
-  float *x = nullptr, *qkv = nullptr, *gu = nullptr, *tlog = nullptr, *plog = nullptr;
-  uint16_t *xn = nullptr, *q = nullptr, *attn = nullptr;
+  float *x = nullptr, *tlog = nullptr, *plog = nullptr;
+  // split-K partial-sum workspaces of the linears (one per output kind)
+  float *ws_qkv = nullptr, *ws_o = nullptr, *ws_gu = nullptr, *ws_down = nullptr, *ws_head = nullptr;
+  long long n_qkv = 0, n_o = 0, n_gu = 0, n_down = 0, n_head = 0;
+  uint16_t *xn = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
   q3t::AttnWork ws{};
   // metadata
   int meta_n = 0;
@@ -187,6 +196,11 @@ struct q3t_batch {
   // graphs
   bool use_graphs = true;
   std::map<std::tuple<int, int, int>, q3t::GraphEntry> graphs;
+  std::map<std::pair<int, int>, q3t::Program> programs;  // decode-frame phase programs
+  bool use_frame_kernel = true;
+  unsigned *d_ctr = nullptr;  // frame-kernel barrier counters
+  int *d_err = nullptr, *h_err = nullptr;
+  int step_counter = 0;
   // requests
   std::vector<q3t::Req *> slots;
   std::deque<q3t::Req *> queue;
