@@ -370,7 +370,7 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
   CK(cudaMallocHost(&b->h_err, sizeof(int)));
   *b->h_err = 0;
   const char *fe = getenv("Q3T_FRAME");
-  b->use_frame_kernel = !(fe && fe[0] == '0');
+  b->use_frame_kernel = fe && fe[0] == '1';
   CK(cudaStreamSynchronize(b->st));
   CK(cudaDeviceSynchronize());  // the arena's cudaMemset zero-fills run on the legacy stream
 }
@@ -678,8 +678,14 @@ static void build_frame(q3t_batch *b, int mt, int max_split, std::vector<Phase> 
   out.swap(P.ph);
 }
 
-// Runs the decode frame: the persistent kernel (default) or, with
-// Q3T_FRAME=0, one standalone kernel per phase.
+// phases the talker part of the frame program takes (it is the tail)
+static int m_talker_phases(q3t_batch *b) {
+  const int L = b->m->tc.talker.num_hidden_layers;
+  return 1 + (L * 8 - 1) + 1 + 1 + 1;
+}
+
+// Runs the decode frame: one standalone kernel per phase, captured in a CUDA
+// graph (default), or the persistent frame kernel with Q3T_FRAME=1.
 static void enqueue_frame(q3t_batch *b, int mt, int max_split) {
   auto key = std::make_pair(mt, max_split);
   auto it = b->programs.find(key);
@@ -696,7 +702,32 @@ static void enqueue_frame(q3t_batch *b, int mt, int max_split) {
   }
   const Program &pr = it->second;
   if (b->use_frame_kernel) {
-    frame_launch(pr.dev, (int)pr.host.size(), FrameCtl{b->d_ctr, b->d_err}, b->st);
+    unsigned long long *stamps = nullptr;
+    if (getenv("Q3T_FRAME_PROFILE")) {  // per-phase device timestamps, summarised on stderr
+      CK(cudaMallocAsync((void **)&stamps, (pr.host.size() + 1) * 8, b->st));
+    }
+    frame_launch(pr.dev, (int)pr.host.size(), FrameCtl{b->d_ctr, b->d_err, stamps}, b->st);
+    if (stamps) {
+      std::vector<unsigned long long> h(pr.host.size() + 1);
+      CK(cudaMemcpyAsync(h.data(), stamps, h.size() * 8, cudaMemcpyDeviceToHost, b->st));
+      CK(cudaStreamSynchronize(b->st));
+      CK(cudaFreeAsync(stamps, b->st));
+      double by_type[8] = {0};
+      int cnt[8] = {0};
+      double pred = 0, talk = 0;
+      const size_t talker_from = pr.host.size() - (size_t)m_talker_phases(b);
+      for (size_t i = 0; i + 1 < h.size(); i++) {
+        const double us = (h[i + 1] - h[i]) / 1e3;
+        by_type[pr.host[i].type] += us;
+        cnt[pr.host[i].type]++;
+        (i < talker_from ? pred : talk) += us;
+      }
+      fprintf(stderr, "frame profile mt=%d ms=%d phases=%zu: pred %.1f us talker %.1f us |", mt, max_split,
+              pr.host.size(), pred, talk);
+      const char *nm[8] = {"", "norm", "gemm", "qkv", "attn", "silu", "sample", ""};
+      for (int k = 1; k < 7; k++) fprintf(stderr, " %s %d %.1f us", nm[k], cnt[k], by_type[k]);
+      fprintf(stderr, "\n");
+    }
   } else {
     run_graph(b, std::make_tuple(0, mt, max_split), [&] { run_phases(pr.host.data(), (int)pr.host.size(), b->st); });
   }

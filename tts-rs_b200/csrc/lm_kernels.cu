@@ -416,6 +416,11 @@ __global__ void __launch_bounds__(kFrameThreads, 2) k_frame(const Phase *phases,
       have_pre = true;
     }
     if (i > 0 && !grid_barrier(ctl, (unsigned)i, sh)) return;
+    if (ctl.t && blockIdx.x == 0 && threadIdx.x == 0) {
+      unsigned long long now;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+      ctl.t[i] = now;
+    }
     switch (ph.type) {
       case PH_NORM:
         for (int t = blockIdx.x; t < ph.max_tok; t += gridDim.x) d_rmsnorm(ph.norm, t, sh.red);
@@ -464,6 +469,11 @@ __global__ void __launch_bounds__(kFrameThreads, 2) k_frame(const Phase *phases,
         break;
     }
     __syncthreads();
+  }
+  if (ctl.t && grid_barrier(ctl, (unsigned)n_phases, sh) && blockIdx.x == 0 && threadIdx.x == 0) {
+    unsigned long long now;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+    ctl.t[n_phases] = now;
   }
 }
 

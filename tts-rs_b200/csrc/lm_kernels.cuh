@@ -239,8 +239,9 @@ struct Phase {
 };
 
 struct FrameCtl {
-  unsigned *ctr;  // barrier counters, kFrameCtrWords words, zeroed before each launch
-  int *err;       // set to 1 when a barrier wait times out
+  unsigned *ctr;          // barrier counters, kFrameCtrWords words, zeroed before each launch
+  int *err;               // set to 1 when a barrier wait times out
+  unsigned long long *t;  // optional [n_phases + 1] %globaltimer stamps at phase starts (CTA 0)
 };
 constexpr int kFrameCtrWords = 17 * 32;
 // grid size (CTAs) the frame kernel runs with on the current device
