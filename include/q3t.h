@@ -201,6 +201,21 @@ q3t_status q3t_codec_decode(q3t_model *model, const int64_t *codes, int B, int T
                             float *wave, int16_t *pcm, int64_t *n);
 q3t_status q3t_codec_out_len(const q3t_model *model, int T, int64_t *n);
 
+/* No reference counterpart.  q3t_codec_decode that allocates nothing, for
+ * callers that may not allocate device memory: a real-time audio thread
+ * (cudaMalloc can wait for the whole device) or a host framework whose own
+ * allocator owns all device memory.  The codes, every intermediate buffer and
+ * the samples use one static 48 MiB device array per process: B x T up to
+ * about 26 frames (a 24-frame streaming window at B = 1); larger requests are
+ * INVALID_INPUT with the needed size in q3t_last_error().  Runs on `stream`
+ * (a cudaStream_t; NULL is the default stream) and returns when wave / pcm
+ * (host buffers, nullable) hold the result.  The first call on each device
+ * looks up the array's address (cudaGetSymbolAddress) with the model's device
+ * current; make that first call before any stream capture.  Calls that
+ * overlap in time on one device share the array and race: serialise them. */
+q3t_status q3t_codec_decode_static(q3t_model *model, const int64_t *codes, int B, int T,
+                                   float *wave, int16_t *pcm, int64_t *n, void *stream);
+
 /* ------------------------ ragged continuous batching --------------------- */
 typedef struct {
   int max_active;            /* <= model max_active */

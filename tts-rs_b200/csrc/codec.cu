@@ -19,6 +19,7 @@
 
 #include <cmath>
 #include <cstring>
+#include <mutex>
 
 #include "codec.cuh"
 #include "common.cuh"
@@ -730,13 +731,18 @@ static ConvArgs conv_args(const ConvW &w, const __half *X, int B, int Lin, int i
 }
 
 // Decodes codes [B][nq][T] (device) into wave / pcm [B][n] (device, nullable).
-static void decode_device(CodecModel *c, const int64_t *d_codes, int B, int T, float *d_wave, int16_t *d_pcm,
-                          cudaStream_t st) {
+// Intermediate buffers of one decode of B x T frames and their sizes in bytes.
+struct CodecScratch {
+  enum { X32, A0, A1, HH, F1, G, Q, K, V, HRES, N };
+  int64_t bytes[N];
+  void *p[N];
+};
+
+static CodecScratch codec_scratch(const CodecModel *c, int B, int T) {
   const auto &k = c->c;
   const int half = k.codebook_dim / 2, LAT = k.latent_dim, H = k.hidden_size;
   const int nh = k.num_attention_heads, nkv = k.num_key_value_heads, qd = nh * 64, kd = nkv * 64;
   const int M0 = B * T;
-  // workspace sizes
   int64_t Lmax = T;
   for (int i = 0; i < k.num_upsampling_ratios; i++) Lmax *= k.upsampling_ratios[i];
   const int64_t Lup = Lmax;
@@ -748,19 +754,42 @@ static void decode_device(CodecModel *c, const int64_t *d_codes, int B, int T, f
   big *= B;
   const int64_t pre = (int64_t)M0 * std::max(std::max(qd + 2 * kd, 2 * k.intermediate_size), LAT);
   const int64_t upn = B * Lup * 4 * (int64_t)LAT;
-  float *X32, *F1, *Q, *K, *V;
-  __half *A0, *A1, *Hh, *G;
-  CK(cudaMallocAsync((void **)&X32, std::max(big, (int64_t)B * Lup * LAT) * 4, st));
-  CK(cudaMallocAsync((void **)&A0, std::max(big, upn) * 2, st));
-  CK(cudaMallocAsync((void **)&A1, std::max(big, (int64_t)B * Lup * LAT) * 2, st));
-  CK(cudaMallocAsync((void **)&Hh, std::max(big, (int64_t)M0 * 2 * half) * 2, st));
-  CK(cudaMallocAsync((void **)&F1, std::max(pre, (int64_t)M0 * H) * 4, st));
-  CK(cudaMallocAsync((void **)&G, std::max(pre, (int64_t)M0 * qd) * 2, st));
-  CK(cudaMallocAsync((void **)&Q, (int64_t)M0 * qd * 4, st));
-  CK(cudaMallocAsync((void **)&K, (int64_t)M0 * kd * 4, st));
-  CK(cudaMallocAsync((void **)&V, (int64_t)M0 * kd * 4, st));
-  float *hres;  // pre-transformer residual [M0][H]
-  CK(cudaMallocAsync((void **)&hres, (int64_t)M0 * H * 4, st));
+  CodecScratch s{};
+  s.bytes[CodecScratch::X32] = std::max(big, (int64_t)B * Lup * LAT) * 4;
+  s.bytes[CodecScratch::A0] = std::max(big, upn) * 2;
+  s.bytes[CodecScratch::A1] = std::max(big, (int64_t)B * Lup * LAT) * 2;
+  s.bytes[CodecScratch::HH] = std::max(big, (int64_t)M0 * 2 * half) * 2;
+  s.bytes[CodecScratch::F1] = std::max(pre, (int64_t)M0 * H) * 4;
+  s.bytes[CodecScratch::G] = std::max(pre, (int64_t)M0 * qd) * 2;
+  s.bytes[CodecScratch::Q] = (int64_t)M0 * qd * 4;
+  s.bytes[CodecScratch::K] = (int64_t)M0 * kd * 4;
+  s.bytes[CodecScratch::V] = (int64_t)M0 * kd * 4;
+  s.bytes[CodecScratch::HRES] = (int64_t)M0 * H * 4;  // pre-transformer residual [M0][H]
+  return s;
+}
+
+static void decode_with(CodecModel *c, const CodecScratch &ws, const int64_t *d_codes, int B, int T,
+                        float *d_wave, int16_t *d_pcm, cudaStream_t st);
+
+static void decode_device(CodecModel *c, const int64_t *d_codes, int B, int T, float *d_wave, int16_t *d_pcm,
+                          cudaStream_t st) {
+  CodecScratch ws = codec_scratch(c, B, T);
+  for (int i = 0; i < CodecScratch::N; i++) CK(cudaMallocAsync(&ws.p[i], ws.bytes[i], st));
+  decode_with(c, ws, d_codes, B, T, d_wave, d_pcm, st);
+  for (int i = 0; i < CodecScratch::N; i++) CK(cudaFreeAsync(ws.p[i], st));
+}
+
+static void decode_with(CodecModel *c, const CodecScratch &ws, const int64_t *d_codes, int B, int T,
+                        float *d_wave, int16_t *d_pcm, cudaStream_t st) {
+  const auto &k = c->c;
+  const int half = k.codebook_dim / 2, LAT = k.latent_dim, H = k.hidden_size;
+  const int nh = k.num_attention_heads, nkv = k.num_key_value_heads;
+  const int M0 = B * T;
+  float *X32 = (float *)ws.p[CodecScratch::X32], *F1 = (float *)ws.p[CodecScratch::F1];
+  float *Q = (float *)ws.p[CodecScratch::Q], *K = (float *)ws.p[CodecScratch::K];
+  float *V = (float *)ws.p[CodecScratch::V], *hres = (float *)ws.p[CodecScratch::HRES];
+  __half *A0 = (__half *)ws.p[CodecScratch::A0], *A1 = (__half *)ws.p[CodecScratch::A1];
+  __half *Hh = (__half *)ws.p[CodecScratch::HH], *G = (__half *)ws.p[CodecScratch::G];
 
   // quantizer: gather-sum + both output projections in one GEMM
   k_gather<<<M0, 256, 0, st>>>(d_codes, k.num_quantizers, k.num_semantic_quantizers, T, c->cent, k.codebook_size,
@@ -890,9 +919,6 @@ static void decode_device(CodecModel *c, const int64_t *d_codes, int B, int T, f
     CK(cudaGetLastError());
     g_launches++;
   }
-  for (void *p : {(void *)X32, (void *)F1, (void *)Q, (void *)K, (void *)V, (void *)A0, (void *)A1, (void *)Hh,
-                  (void *)G, (void *)hres})
-    CK(cudaFreeAsync(p, st));
 }
 
 static void check_codes(const CodecModel *c, const int64_t *codes, int64_t n) {
@@ -925,6 +951,67 @@ void codec_decode_host_codes(q3t_model *m, const int64_t *codes, int B, int T, f
   CK(cudaFreeAsync(dc, st));
   if (dw) CK(cudaFreeAsync(dw, st));
   if (dp) CK(cudaFreeAsync(dp, st));
+  CK(cudaStreamSynchronize(st));
+}
+
+// ---------------------------------------------------------------------------
+// decode without allocation: the codes, every intermediate buffer and the
+// output samples are carved out of one file-scope device array.  No part of it
+// needs to start at zero: each kernel writes its output buffer before a later
+// kernel reads it.  Calls that overlap in time on one device (from any thread
+// or stream) share the array and race.
+// ---------------------------------------------------------------------------
+constexpr int64_t kStaticScratchBytes = 48ll << 20;  // one 24-frame window at B = 1 needs 42.7 MiB
+constexpr int kStaticMaxDevices = 64;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+static void *g_static_addr[kStaticMaxDevices];
+static std::mutex g_static_mu;
+
+// Device address of g_static_scratch on `dev` (the current device): looked up
+// once per device, on the first call.
+static unsigned char *static_scratch(int dev) {
+  if (dev < 0 || dev >= kStaticMaxDevices) FAIL(Q3T_INVALID_INPUT, "device %d beyond %d", dev, kStaticMaxDevices);
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_static_addr[dev]) CK(cudaGetSymbolAddress(&g_static_addr[dev], g_static_scratch));
+  return (unsigned char *)g_static_addr[dev];
+}
+
+static void codec_decode_static(q3t_model *m, const int64_t *codes, int B, int T, float *wave, int16_t *pcm,
+                                cudaStream_t st) {
+  CodecModel *c = m->codec;
+  if (!c) FAIL(Q3T_INVALID_INPUT, "model has no codec");
+  if (B <= 0 || T <= 0) FAIL(Q3T_INVALID_INPUT, "codec decode needs B > 0 and T > 0");
+  const int64_t ncodes = (int64_t)B * c->c.num_quantizers * T;
+  check_codes(c, codes, ncodes);
+  int64_t n = 0;
+  codec_out_len(c, T, &n);
+  if (n <= 0) FAIL(Q3T_INVALID_INPUT, "T = %d frames decode to no samples", T);
+  CodecScratch ws = codec_scratch(c, B, T);
+  auto up = [](int64_t b) { return (b + 255) & ~(int64_t)255; };
+  const int64_t codes_b = up(ncodes * 8), wave_b = wave ? up(B * n * 4) : 0, pcm_b = pcm ? up(B * n * 2) : 0;
+  int64_t need = codes_b + wave_b + pcm_b;
+  for (int i = 0; i < CodecScratch::N; i++) need += up(ws.bytes[i]);
+  if (need > kStaticScratchBytes)
+    FAIL(Q3T_INVALID_INPUT,
+         "static codec decode of B = %d x T = %d frames needs %lld bytes of scratch; the static array holds %lld "
+         "(about 26 frames in total)",
+         B, T, (long long)need, (long long)kStaticScratchBytes);
+  unsigned char *base = static_scratch(m->device);
+  int64_t off = 0;
+  int64_t *dc = (int64_t *)(base + off);
+  off += codes_b;
+  float *dw = wave ? (float *)(base + off) : nullptr;
+  off += wave_b;
+  int16_t *dp = pcm ? (int16_t *)(base + off) : nullptr;
+  off += pcm_b;
+  for (int i = 0; i < CodecScratch::N; i++) {
+    ws.p[i] = base + off;
+    off += up(ws.bytes[i]);
+  }
+  CK(cudaMemcpyAsync(dc, codes, ncodes * 8, cudaMemcpyHostToDevice, st));
+  decode_with(c, ws, dc, B, T, dw, dp, st);
+  if (wave) CK(cudaMemcpyAsync(wave, dw, (size_t)B * n * 4, cudaMemcpyDeviceToHost, st));
+  if (pcm) CK(cudaMemcpyAsync(pcm, dp, (size_t)B * n * 2, cudaMemcpyDeviceToHost, st));
   CK(cudaStreamSynchronize(st));
 }
 
@@ -1062,6 +1149,28 @@ extern "C" q3t_status q3t_codec_decode(q3t_model *m, const int64_t *codes, int B
       throw;
     }
     CK(cudaStreamDestroy(st));
+    return Q3T_OK;
+  } catch (const Status &s) {
+    return s.code;
+  } catch (const CudaFail &c) {
+    set_error("CUDA error %s (%s) in %s", cudaGetErrorName(c.err), cudaGetErrorString(c.err), c.what.c_str());
+    return Q3T_CUDA_ERROR;
+  }
+}
+
+extern "C" q3t_status q3t_codec_decode_static(q3t_model *m, const int64_t *codes, int B, int T, float *wave,
+                                              int16_t *pcm, int64_t *n, void *stream) {
+  if (!m || !codes) {
+    set_error("q3t_codec_decode_static: null argument");
+    return Q3T_INVALID_INPUT;
+  }
+  try {
+    CK(cudaSetDevice(m->device));
+    if (!m->has_codec || !m->codec) FAIL(Q3T_INVALID_INPUT, "model has no codec");
+    int64_t len = 0;
+    codec_out_len(m->codec, T > 0 ? T : 1, &len);
+    if (n) *n = len;
+    codec_decode_static(m, codes, B, T, wave, pcm, (cudaStream_t)stream);
     return Q3T_OK;
   } catch (const Status &s) {
     return s.code;

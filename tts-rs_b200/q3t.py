@@ -98,7 +98,8 @@ EXPORTS = [
     "q3t_model_load", "q3t_model_free", "q3t_session_start", "q3t_session_step",
     "q3t_session_step_forced", "q3t_session_codes", "q3t_session_finish",
     "q3t_session_decode_embeds", "q3t_session_load_kv", "q3t_session_last_ms",
-    "q3t_session_free", "q3t_codec_decode", "q3t_codec_out_len", "q3t_batch_create",
+    "q3t_session_free", "q3t_codec_decode", "q3t_codec_out_len", "q3t_codec_decode_static",
+    "q3t_batch_create",
     "q3t_batch_submit", "q3t_batch_step", "q3t_batch_poll", "q3t_batch_take",
     "q3t_batch_pending", "q3t_batch_stream", "q3t_batch_free", "q3t_last_error", "q3t_version",
     "q3t_kernel_launches",
@@ -135,6 +136,8 @@ def lib():
         L.q3t_session_free.restype = None
         L.q3t_codec_decode.argtypes = [C.c_void_p, _I64, C.c_int, C.c_int, _F, C.POINTER(C.c_int16), _I64]
         L.q3t_codec_out_len.argtypes = [C.c_void_p, C.c_int, _I64]
+        L.q3t_codec_decode_static.argtypes = [C.c_void_p, _I64, C.c_int, C.c_int, _F,
+                                              C.POINTER(C.c_int16), _I64, C.c_void_p]
         L.q3t_batch_create.argtypes = [C.c_void_p, C.POINTER(BatchDesc), C.POINTER(C.c_void_p)]
         L.q3t_batch_submit.argtypes = [C.c_void_p, C.POINTER(SessionDesc), _I64, _I64]
         L.q3t_batch_step.argtypes = [C.c_void_p, C.POINTER(StepStats)]
