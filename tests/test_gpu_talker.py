@@ -1,11 +1,17 @@
 """Talker / code-predictor parity: CUDA path (through the C ABI) vs the CPU
 oracle on the same seeded weights and teacher-forced inputs.
 
-Tolerance (floating point, bf16 weights): logits within |gpu - ref| <=
-2e-2 + 1e-2 * |ref| element-wise; argmax agreement exact on every row whose
-oracle top-2 margin exceeds 2e-2 and >= 95 % over all rows (the random-init
-logits have near-ties below the run-to-run spread of split-K atomics).
-Token bookkeeping (codes, page tables) is compared exactly.
+Tolerance (floating point, bf16 weights), the stated 2e-2 max-abs / 1e-2
+relative: max |gpu - ref| <= max(2e-2, 1e-2 * max |ref|) over the tensor, and
+the relative L2 error ||gpu - ref|| / ||ref|| <= 1e-2.  The GPU and the oracle
+round the same tensors to bf16 at the same points, but their f32 sums run in
+different orders, so an input occasionally rounds to the neighbouring bf16
+value; on the full 28 + 5-layer pipeline this leaves a per-frame logit noise
+of about 4e-3 RMS (it does not grow with the frame count), whose largest
+element over 30k logits sits near 2e-2.  Argmax agreement is exact on every
+row whose oracle top-2 margin exceeds 2e-2 and >= 95 % over all rows (the
+random-init logits have near-ties below that noise).  Token bookkeeping
+(codes, page tables) is compared exactly.
 """
 import numpy as np
 import pytest
@@ -18,17 +24,19 @@ pytestmark = pytest.mark.gpu
 
 ATOL, RTOL = 2e-2, 1e-2
 # Raw argmax agreement with the oracle is bounded by near-ties of the random
-# seed-0 logits (top-2 gaps below the ~5e-3 run-to-run spread of float
-# atomics): rows whose oracle top-2 margin exceeds DECISIVE must agree exactly,
-# and all rows together at >= RAW_AGREE.
+# seed-0 logits (top-2 gaps below the ~4e-3 bf16 rounding noise): rows whose
+# oracle top-2 margin exceeds DECISIVE must agree exactly, and all rows
+# together at >= RAW_AGREE.
 DECISIVE, RAW_AGREE = 2e-2, 0.95
 
 
 def assert_close(gpu, ref, what):
     gpu, ref = np.asarray(gpu, np.float64), np.asarray(ref, np.float64)
     err = np.abs(gpu - ref)
-    bad = err > ATOL + RTOL * np.abs(ref)
-    assert not bad.any(), f"{what}: {bad.sum()} of {bad.size} outside tolerance, max err {err.max():.3e}"
+    bound = max(ATOL, RTOL * np.abs(ref).max())
+    assert err.max() <= bound, f"{what}: max err {err.max():.3e} > {bound:.3e}"
+    rel = np.linalg.norm(gpu - ref) / max(np.linalg.norm(ref), 1e-30)
+    assert rel <= RTOL, f"{what}: relative L2 error {rel:.3e} > {RTOL}"
 
 
 def argmax_agreement(gpu_rows, ref_rows):

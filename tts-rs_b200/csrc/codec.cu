@@ -29,15 +29,6 @@ namespace q3t {
 // ---------------------------------------------------------------------------
 // device helpers
 // ---------------------------------------------------------------------------
-Q3T_DEV void cp_async16(void *smem, const void *gmem, int src_bytes) {
-  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
-}
-Q3T_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-Q3T_DEV void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
-}
 Q3T_DEV void ldmatrix_x4(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p) {
   const uint32_t s = (uint32_t)__cvta_generic_to_shared(p);
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"

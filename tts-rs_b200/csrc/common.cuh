@@ -71,4 +71,37 @@ Q3T_DEV float block_sum(float v, float *red) {
 
 Q3T_DEV float silu(float x) { return x / (1.f + expf(-x)); }
 
+// ---- asynchronous global -> shared copies (16 bytes; src_bytes < 16 zero-fills the rest) ----
+Q3T_DEV void cp_async16(void *smem, const void *gmem, int src_bytes) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
+}
+Q3T_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+Q3T_DEV void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// ---- thread-block clusters (distributed shared memory) ----
+Q3T_DEV uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// 16-byte load from the shared memory of cluster CTA `rank` at the address
+// that p has in this CTA.
+Q3T_DEV float4 ld_cluster_f4(const float *p, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(p)), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote)
+               : "memory");
+  return v;
+}
+
+// All threads of all CTAs of the cluster; shared-memory writes before it are
+// visible to every CTA of the cluster after it.
+Q3T_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 }  // namespace q3t

@@ -136,6 +136,23 @@ static void pack_into(const q3t_tensor *t, uint16_t *dst, int N, int K, cudaStre
   CK(cudaFree(tmp));
 }
 
+// gate [I][H] and up [I][H] -> one [2I][H] matrix whose 128-row blocks are
+// [gate rows 64r..64r+63 | up rows 64r..64r+63] (the GE_SILU epilogue pairs
+// them), fragment-packed into dst
+static void pack_gate_up(const q3t_tensor *gate, const q3t_tensor *up, uint16_t *dst, int I, int H, cudaStream_t st) {
+  if (I % 64 || H % 64) FAIL(Q3T_RUNTIME_LOAD, "gate/up: dims %d x %d not multiples of 64", I, H);
+  uint16_t *g = to_dev_bf16(gate, nullptr, st), *u = to_dev_bf16(up, nullptr, st), *gu;
+  CK(cudaMalloc(&gu, (size_t)2 * I * H * 2));
+  const size_t blk = (size_t)64 * H * 2;  // bytes of 64 rows
+  CK(cudaMemcpy2DAsync(gu, 2 * blk, g, blk, blk, I / 64, cudaMemcpyDeviceToDevice, st));
+  CK(cudaMemcpy2DAsync(reinterpret_cast<char *>(gu) + blk, 2 * blk, u, blk, blk, I / 64, cudaMemcpyDeviceToDevice, st));
+  pack_weight(gu, dst, 2 * I, H, st);
+  CK(cudaStreamSynchronize(st));
+  CK(cudaFree(g));
+  CK(cudaFree(u));
+  CK(cudaFree(gu));
+}
+
 static void load_stack(q3t_model *m, LMStack &S, const q3t_lm_config &c, const std::string &prefix,
                        const Tensors &T, cudaStream_t st) {
   S.cfg = c;
@@ -161,8 +178,7 @@ static void load_stack(q3t_model *m, LMStack &S, const q3t_lm_config &c, const s
     pack_into(T.get(p + ".self_attn.o_proj.weight", {H, Nq}), wo, H, Nq, st);
     S.wo.push_back(wo);
     uint16_t *gu = ar.alloc<uint16_t>((size_t)2 * I * H);
-    pack_into(T.get(p + ".mlp.gate_proj.weight", {I, H}), gu, I, H, st);
-    pack_into(T.get(p + ".mlp.up_proj.weight", {I, H}), gu + (size_t)I * H, I, H, st);
+    pack_gate_up(T.get(p + ".mlp.gate_proj.weight", {I, H}), T.get(p + ".mlp.up_proj.weight", {I, H}), gu, I, H, st);
     S.wgu.push_back(gu);
     uint16_t *wd = ar.alloc<uint16_t>((size_t)H * I);
     pack_into(T.get(p + ".mlp.down_proj.weight", {H, I}), wd, H, I, st);
@@ -328,28 +344,15 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
   const int T = b->Tmax;
   b->x = ar.zalloc<float>((size_t)T * H);
   b->xn = ar.zalloc<uint16_t>((size_t)T * H);
-  // partial-sum workspaces: at most K / 64 splits of T rows each
-  const int Hm = std::max(tc.talker.hidden_size, tc.predictor.hidden_size);
-  const int Im = std::max(tc.talker.intermediate_size, tc.predictor.intermediate_size);
-  const int QDm = 128 * std::max(tc.talker.num_attention_heads, tc.predictor.num_attention_heads);
-  b->n_qkv = (long long)(Hm / 64) * T * std::max(b->NQKV, b->NQKVP);
-  b->n_o = (long long)(QDm / 64) * T * Hm;
-  b->n_gu = (long long)(Hm / 64) * T * 2 * Im;
-  b->n_down = (long long)(Im / 64) * T * Hm;
-  b->n_head = (long long)(Hm / 64) * T * std::max(b->V, b->PV);
-  b->ws_qkv = ar.alloc<float>(b->n_qkv);
-  b->ws_o = ar.alloc<float>(b->n_o);
-  b->ws_gu = ar.alloc<float>(b->n_gu);
-  b->ws_down = ar.alloc<float>(b->n_down);
-  b->ws_head = ar.alloc<float>(b->n_head);
+  b->ss = ar.zalloc<float>((size_t)(std::max(tc.talker.hidden_size, tc.predictor.hidden_size) / 128) * T);
+  b->hlog = ar.zalloc<float>((size_t)T * std::max(b->V, b->PV));
   b->q = ar.zalloc<uint16_t>((size_t)T * 128 * std::max(tc.talker.num_attention_heads, tc.predictor.num_attention_heads));
   b->attn = ar.zalloc<uint16_t>((size_t)T * 128 * std::max(tc.talker.num_attention_heads, tc.predictor.num_attention_heads));
   b->act = ar.zalloc<uint16_t>((size_t)T * b->I2 / 2);
   b->tlog = ar.zalloc<float>((size_t)T * b->V);
   b->plog = ar.zalloc<float>((size_t)(G - 1) * A * b->PV);
-  b->ws.max_split = kMaxSplit;
   const int mkv = std::max(nkv, pnkv);
-  b->ws.part = ar.zalloc<float>((size_t)T * mkv * kMaxSplit * 2 * 132);
+  b->ws.part = ar.zalloc<float>((size_t)T * mkv * kAttnMaxUnits * 2 * 132);
   b->ws.counters = ar.zalloc<int>((size_t)T * mkv);
   // metadata
   b->meta_n = M_HDR + 8 * A;
@@ -365,12 +368,6 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
   CK(cudaMallocHost(&b->h_eosflag, T * sizeof(int)));
   CK(cudaMallocHost(&b->h_codes, (size_t)A * G * sizeof(int64_t)));
   b->slots.assign(A, nullptr);
-  b->d_ctr = ar.zalloc<unsigned>(kFrameCtrWords);
-  b->d_err = ar.zalloc<int>(1);
-  CK(cudaMallocHost(&b->h_err, sizeof(int)));
-  *b->h_err = 0;
-  const char *fe = getenv("Q3T_FRAME");
-  b->use_frame_kernel = fe && fe[0] == '1';
   CK(cudaStreamSynchronize(b->st));
   CK(cudaDeviceSynchronize());  // the arena's cudaMemset zero-fills run on the legacy stream
 }
@@ -378,9 +375,7 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
 static void batch_destroy(q3t_batch *b) {
   for (auto &kv : b->graphs) cudaGraphExecDestroy(kv.second.exec);
   b->graphs.clear();
-  for (auto &kv : b->programs) cudaFree(kv.second.dev);
   b->programs.clear();
-  if (b->h_err) cudaFreeHost(b->h_err);
   for (auto &r : b->reqs)
     for (void *p : {(void *)r.second->d_trailing, (void *)r.second->d_pad, (void *)r.second->d_prompt,
                     (void *)r.second->d_forced})
@@ -446,38 +441,16 @@ static int bucket_tok(int B) {
   while (n < B) n <<= 1;
   return n;
 }
-static int bucket_split(int L) {
-  int s = (L + kChunk - 1) / kChunk, n = 1;
+// minimum pages per attention work unit: larger with more tokens in the
+// batch, so that the units stay a few waves deep at every batch size
+static int attn_pw(int max_tok) { return max_tok >= 32 ? 4 : max_tok >= 8 ? 2 : 1; }
+// attention units per (token, head) for kv length L, rounded up to a power of
+// two (it keys the CUDA graphs); the device uses the same page split
+static int bucket_units(int L, int pw) {
+  const int pages = (L + 15) / 16, per = std::max(pw, (pages + kAttnMaxUnits - 1) / kAttnMaxUnits);
+  int s = (pages + per - 1) / per, n = 1;
   while (n < s) n <<= 1;
   return n;
-}
-
-// One decoder stack over the token batch described by tv.  Returns the
-// pending split-K partials of the last down projection, which the caller's
-// final RMSNorm folds into the residual stream.
-static Part run_stack(q3t_batch *b, const LMStack &S, KVView kv, TokView tv, int max_tok, bool fused,
-                      int max_split) {
-  const auto &c = S.cfg;
-  const int H = c.hidden_size, I = c.intermediate_size, nh = c.num_attention_heads,
-            nkv = c.num_key_value_heads;
-  const int NQ = (nh + 2 * nkv) * 128, QD = nh * 128;
-  const int T = b->Tmax;
-  Part pending{nullptr, 0, 0, 0};
-  for (int l = 0; l < c.num_hidden_layers; l++) {
-    rmsnorm(b->x, H, 1, 0, pending, S.in_norm[l], b->xn, H, H, c.rms_norm_eps, tv.ntok, max_tok, nullptr, nullptr,
-            b->st);
-    const Part qkv = linear(S.wqkv[l], NQ, H, b->xn, H, b->ws_qkv, b->n_qkv, T, tv.ntok, max_tok, b->st);
-    if (!fused)
-      qkv_post(qkv, S.q_norm[l], S.k_norm[l], S.inv_freq, c.rms_norm_eps, nh, nkv, tv, max_tok, b->q, kv, l, b->st);
-    attention(fused ? 1 : 0, qkv, S.q_norm[l], S.k_norm[l], S.inv_freq, c.rms_norm_eps, b->q, kv, l, tv, max_tok, nh,
-              kChunk, max_split, b->ws, b->attn, b->st);
-    const Part o = linear(S.wo[l], H, QD, b->attn, QD, b->ws_o, b->n_o, T, tv.ntok, max_tok, b->st);
-    rmsnorm(b->x, H, 1, 0, o, S.post_norm[l], b->xn, H, H, c.rms_norm_eps, tv.ntok, max_tok, nullptr, nullptr, b->st);
-    const Part gu = linear(S.wgu[l], 2 * I, H, b->xn, H, b->ws_gu, b->n_gu, T, tv.ntok, max_tok, b->st);
-    silu_mul(gu, I, tv.ntok, max_tok, b->act, b->st);
-    pending = linear(S.wdown[l], H, I, b->act, I, b->ws_down, b->n_down, T, tv.ntok, max_tok, b->st);
-  }
-  return pending;
 }
 
 static KVView talker_kv(q3t_batch *b) {
@@ -490,74 +463,134 @@ static KVView pred_kv(q3t_batch *b) {
 
 
 // ---------------------------------------------------------------------------
-// The decode frame as a phase program (lm_kernels.cuh Phase): built once per
-// (token bucket mt, attention split bucket ms) and replayed every step; the
-// per-step inputs (active slots, positions, frames, trailing-text rows, step
-// counter) live in the device metadata the phases point at.
+// Phase emitter: the decode frame is built once per (token bucket mt,
+// attention unit bucket ms) as a phase list and captured into a CUDA graph;
+// the per-step inputs (active slots, positions, frames, trailing-text rows,
+// step counter) live in the device metadata the phases point at.  With
+// direct = true (prefill, sessions) each phase launches as it is emitted.
 // ---------------------------------------------------------------------------
 struct ProgBuilder {
   q3t_batch *b;
+  bool direct;
   std::vector<Phase> ph;
-  int target;
-  Phase &add(int type, int max_tok) {
-    ph.emplace_back();
-    memset(&ph.back(), 0, sizeof(Phase));
-    ph.back().type = type;
-    ph.back().max_tok = max_tok;
-    return ph.back();
+  static Phase phase(int type, int max_tok) {
+    Phase p;
+    memset(&p, 0, sizeof(Phase));
+    p.type = type;
+    p.max_tok = max_tok;
+    return p;
   }
-  void norm(const RmsArgs &a, int max_tok) { add(PH_NORM, max_tok).norm = a; }
-  Part gemm(const uint16_t *W, int N, int K, const uint16_t *X, int ldx, float *ws, long long cap, const int *ntok,
-            int max_tok) {
-    Part P;
-    const LinArgs a = linear_plan(W, N, K, X, ldx, ws, cap, b->Tmax, ntok, max_tok, target, &P);
-    add(PH_GEMM, max_tok).lin = a;
-    return P;
+  void push(const Phase &p) {
+    if (direct)
+      run_phases(&p, 1, b->st);
+    else
+      ph.push_back(p);
   }
-  // one decoder stack; the first layer's input norm must already have been
-  // emitted by the caller (it builds the input rows); returns the pending
-  // down-projection partials
-  Part stack(const LMStack &S, KVView kv, TokView tv, int max_tok, bool fused, int max_split) {
+  void norm(const RmsArgs &a, int max_tok) {
+    Phase p = phase(PH_NORM, max_tok);
+    p.norm = a;
+    push(p);
+  }
+  void gemm(const GemmArgs &g, int max_tok) {
+    Phase p = phase(PH_GEMM, max_tok);
+    p.gemm = g;
+    push(p);
+  }
+  void sample(const SampleArgs &a, int max_tok, const RmsArgs *tail) {
+    Phase p = phase(PH_SAMPLE, max_tok);
+    p.smp = a;
+    if (tail) {
+      p.has_tail = 1;
+      p.tail = *tail;
+    }
+    push(p);
+  }
+  // X = bf16 rows
+  static GemmArgs bf16_x(GemmArgs g, const uint16_t *x, int ldx) {
+    g.xmode = GX_BF16;
+    g.xb = x;
+    g.ldx = ldx;
+    return g;
+  }
+  // X = RMSNorm(x rows t * row_mul + row_add) from the residual stream and
+  // the sum-of-squares partials its last GE_RESID epilogue wrote
+  GemmArgs norm_x(GemmArgs g, const float *gamma, float eps, int row_mul = 1, int row_add = 0) const {
+    g.xmode = GX_NORM;
+    g.x = b->x;
+    g.ldx = g.K;
+    g.xrow_mul = row_mul;
+    g.xrow_add = row_add;
+    g.ss = b->ss;
+    g.nss = g.K / 128;
+    g.ss_ld = b->Tmax;
+    g.gamma = gamma;
+    g.eps = eps;
+    return g;
+  }
+  GemmArgs resid(GemmArgs g) const {
+    g.epi = GE_RESID;
+    g.y = b->x;
+    g.ldy = g.N;
+    g.ss_out = b->ss;
+    g.ss_ld = b->Tmax;
+    return g;
+  }
+  // One decoder stack (layer.rs:23-44) over the tokens of tv; the caller has
+  // built the input rows x and their normalised bf16 copy xn.  Afterwards x
+  // holds the output residual rows and ss their sum-of-squares partials.
+  void stack(const LMStack &S, KVView kv, TokView tv, int max_tok, int max_units, int pw) {
     const auto &c = S.cfg;
     const int H = c.hidden_size, I = c.intermediate_size, nh = c.num_attention_heads, nkv = c.num_key_value_heads;
     const int NQ = (nh + 2 * nkv) * 128, QD = nh * 128;
-    Part pending{nullptr, 0, 0, 0};
+    const float eps = c.rms_norm_eps;
     for (int l = 0; l < c.num_hidden_layers; l++) {
-      if (l > 0)
-        norm(rms_args(b->x, H, 1, 0, pending, S.in_norm[l], b->xn, H, H, c.rms_norm_eps, tv.ntok, nullptr, nullptr),
-             max_tok);
-      const Part qkv = gemm(S.wqkv[l], NQ, H, b->xn, H, b->ws_qkv, b->n_qkv, tv.ntok, max_tok);
-      if (!fused) {
-        Phase &q = add(PH_QKV, max_tok);
-        q.qkv = QkvArgs{qkv, S.q_norm[l], S.k_norm[l], S.inv_freq, c.rms_norm_eps, nh, nkv, tv, b->q, kv, l};
-      }
-      Phase &at = add(PH_ATTN, max_tok);
+      GemmArgs q = gemm_args(S.wqkv[l], NQ, H, tv.ntok, max_tok);
+      q = l == 0 ? bf16_x(q, b->xn, H) : norm_x(q, S.in_norm[l], eps);
+      q.epi = GE_QKV;
+      q.q_norm = S.q_norm[l];
+      q.k_norm = S.k_norm[l];
+      q.inv_freq = S.inv_freq;
+      q.nh = nh;
+      q.nkv = nkv;
+      q.tv = tv;
+      q.q = b->q;
+      q.kv = kv;
+      q.layer = l;
+      gemm(q, max_tok);
+      Phase at = phase(PH_ATTN, max_tok);
       AttnArgs &aa = at.attn;
-      aa.qkv = qkv;
-      aa.q_norm = S.q_norm[l];
-      aa.k_norm = S.k_norm[l];
-      aa.inv_freq = S.inv_freq;
-      aa.eps = c.rms_norm_eps;
-      aa.qin = b->q;
+      aa.q = b->q;
       aa.kv = kv;
       aa.layer = l;
       aa.tv = tv;
       aa.nh = nh;
-      aa.chunk = kChunk;
-      aa.max_split = max_split;
-      aa.fused = fused ? 1 : 0;
+      aa.pw = pw;
+      aa.max_units = max_units;
       aa.scale = 1.0f / sqrtf(128.0f);
       aa.ws = b->ws;
       aa.out = b->attn;
-      const Part o = gemm(S.wo[l], H, QD, b->attn, QD, b->ws_o, b->n_o, tv.ntok, max_tok);
-      norm(rms_args(b->x, H, 1, 0, o, S.post_norm[l], b->xn, H, H, c.rms_norm_eps, tv.ntok, nullptr, nullptr), max_tok);
-      const Part gu = gemm(S.wgu[l], 2 * I, H, b->xn, H, b->ws_gu, b->n_gu, tv.ntok, max_tok);
-      add(PH_SILU, max_tok).silu = SiluArgs{gu, I, tv.ntok, b->act};
-      pending = gemm(S.wdown[l], H, I, b->act, I, b->ws_down, b->n_down, tv.ntok, max_tok);
+      push(at);
+      gemm(resid(bf16_x(gemm_args(S.wo[l], H, QD, tv.ntok, max_tok), b->attn, QD)), max_tok);
+      GemmArgs gu = norm_x(gemm_args(S.wgu[l], 2 * I, H, tv.ntok, max_tok), S.post_norm[l], eps);
+      gu.epi = GE_SILU;
+      gu.h = b->act;
+      gu.ldh = I;
+      gemm(gu, max_tok);
+      gemm(resid(bf16_x(gemm_args(S.wdown[l], H, I, tv.ntok, max_tok), b->act, I)), max_tok);
     }
-    return pending;
   }
 };
+
+// Prompt chunk / isolated step: input rows already in x; normalises them,
+// runs the talker stack.
+static void run_stack(q3t_batch *b, const LMStack &S, KVView kv, TokView tv, int max_tok, int max_units) {
+  const auto &c = S.cfg;
+  ProgBuilder P{b, true, {}};
+  P.norm(rms_args(b->x, c.hidden_size, 1, 0, Part{}, S.in_norm[0], b->xn, c.hidden_size, c.hidden_size,
+                  c.rms_norm_eps, tv.ntok, nullptr, nullptr),
+         max_tok);
+  P.stack(S, kv, tv, max_tok, max_units, attn_pw(max_tok));
+}
 
 static SampleArgs base_sample(q3t_batch *b) {
   SampleArgs a{};
@@ -575,14 +608,14 @@ static SampleArgs base_sample(q3t_batch *b) {
   return a;
 }
 
-static void build_frame(q3t_batch *b, int mt, int max_split, std::vector<Phase> &out) {
+static void build_frame(q3t_batch *b, int mt, int max_units, std::vector<Phase> &out) {
   q3t_model *m = b->m;
   const auto &tc = m->tc;
   const int G = b->G, H = b->H, PV = b->PV, V = b->V;
   int *meta = b->d_meta;
   const int *ntokB = meta + M_NTOK_B, *ntok2B = meta + M_NTOK_2B;
   const int *slot = meta + b->off_slot(), *frame = meta + b->off_frame();
-  ProgBuilder P{b, {}, frame_target_items()};
+  ProgBuilder P{b, false, {}};
   const auto &pc = tc.predictor;
   // ---- code predictor (infer/mod.rs:434-535) ----
   // pass 0 input rows: [talker hidden, talker codec embedding of code 0]
@@ -598,19 +631,22 @@ static void build_frame(q3t_batch *b, int mt, int max_split, std::vector<Phase> 
     P.norm(a, 2 * mt);
   }
   for (int j = 0; j < G - 1; j++) {
-    Part pend;
     if (j == 0) {
       TokView tv0{ntok2B, meta + b->off_p0seq(), meta + b->off_p0pos(), 0};
-      pend = P.stack(m->pred, pred_kv(b), tv0, 2 * mt, false, 1);
+      P.stack(m->pred, pred_kv(b), tv0, 2 * mt, 1, kPredPages);
     } else {
       TokView tvj{ntokB, slot, meta + b->off_zero(), j + 1};
-      pend = P.stack(m->pred, pred_kv(b), tvj, mt, true, 1);
+      P.stack(m->pred, pred_kv(b), tvj, mt, 1, kPredPages);
     }
-    P.norm(rms_args(b->x, H, j == 0 ? 2 : 1, j == 0 ? 1 : 0, pend, m->pred.final_norm, b->xn, H, H, pc.rms_norm_eps,
-                    ntokB, nullptr, nullptr),
-           mt);
+    // lm_head j on the final-normed last position of each token's pass
+    GemmArgs hg = P.norm_x(gemm_args(m->lm_heads[j], PV, H, ntokB, mt), m->pred.final_norm, pc.rms_norm_eps,
+                           j == 0 ? 2 : 1, j == 0 ? 1 : 0);
+    hg.epi = GE_F32;
+    hg.y = b->hlog;
+    hg.ldy = PV;
+    P.gemm(hg, mt);
     SampleArgs a = base_sample(b);
-    a.part = P.gemm(m->lm_heads[j], PV, H, b->xn, H, b->ws_head, b->n_head, ntokB, mt);
+    a.part = Part{b->hlog, 1, 0, PV};
     a.logits = b->plog + (size_t)j * b->A * PV;
     a.ldl = PV;
     a.V = PV;
@@ -623,23 +659,19 @@ static void build_frame(q3t_batch *b, int mt, int max_split, std::vector<Phase> 
     a.hist_mode = 2;
     a.seed_p = meta + M_SEED;
     a.step_seed = 0;
-    Phase &sp = P.add(PH_SAMPLE, mt);
-    sp.smp = a;
-    sp.has_tail = 1;
     // the tail builds the next input row of this token and normalises it
+    RmsArgs t;
     if (j + 1 < G - 1) {
-      RmsArgs t = rms_args(b->x, H, 1, 0, Part{}, m->pred.in_norm[0], b->xn, H, H, pc.rms_norm_eps, ntokB, nullptr,
-                           nullptr);
+      t = rms_args(b->x, H, 1, 0, Part{}, m->pred.in_norm[0], b->xn, H, H, pc.rms_norm_eps, ntokB, nullptr, nullptr);
       t.emb.src = 2;
       t.emb.G = G;
       t.emb.col = j + 1;
       t.emb.emb = m->cp_emb[j];
       t.emb.codes = b->d_codes;
       t.emb.slot = slot;
-      sp.tail = t;
     } else {  // next talker input: codec-group embedding + trailing text / pad
-      RmsArgs t = rms_args(b->x, H, 1, 0, Part{}, m->talker.in_norm[0], b->xn, H, H, tc.talker.rms_norm_eps, ntokB,
-                           nullptr, nullptr);
+      t = rms_args(b->x, H, 1, 0, Part{}, m->talker.in_norm[0], b->xn, H, H, tc.talker.rms_norm_eps, ntokB, nullptr,
+                   nullptr);
       t.emb.src = 3;
       t.emb.G = G;
       t.emb.emb0 = m->talker_emb;
@@ -650,17 +682,22 @@ static void build_frame(q3t_batch *b, int mt, int max_split, std::vector<Phase> 
       t.emb.frame = frame;
       t.emb.hist = b->d_hist_codes;
       t.emb.hist_frames = b->maxF;
-      sp.tail = t;
     }
+    P.sample(a, mt, &t);
   }
   // ---- talker decode (model.rs:94-113) + codec_head + sample ----
   TokView tvt{ntokB, slot, meta + b->off_tpos(), 0};
-  const Part tp = P.stack(m->talker, talker_kv(b), tvt, mt, true, max_split);
-  P.norm(rms_args(b->x, H, 1, 0, tp, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps, ntokB, b->d_hidden,
-                  slot),
+  P.stack(m->talker, talker_kv(b), tvt, mt, max_units, attn_pw(mt));
+  P.norm(rms_args(b->x, H, 1, 0, Part{}, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps, ntokB,
+                  b->d_hidden, slot),
          mt);
+  GemmArgs hg = ProgBuilder::bf16_x(gemm_args(m->codec_head, V, H, ntokB, mt), b->xn, H);
+  hg.epi = GE_F32;
+  hg.y = b->hlog;
+  hg.ldy = V;
+  P.gemm(hg, mt);
   SampleArgs a = base_sample(b);
-  a.part = P.gemm(m->codec_head, V, H, b->xn, H, b->ws_head, b->n_head, ntokB, mt);
+  a.part = Part{b->hlog, 1, 0, V};
   a.logits = b->tlog;
   a.ldl = V;
   a.V = V;
@@ -674,62 +711,66 @@ static void build_frame(q3t_batch *b, int mt, int max_split, std::vector<Phase> 
   a.eos_flag = b->d_eosflag;
   a.seed_p = meta + M_SEED;
   a.step_seed = 1;
-  P.add(PH_SAMPLE, mt).smp = a;
+  P.sample(a, mt, nullptr);
   out.swap(P.ph);
 }
 
 // phases the talker part of the frame program takes (it is the tail)
-static int m_talker_phases(q3t_batch *b) {
-  const int L = b->m->tc.talker.num_hidden_layers;
-  return 1 + (L * 8 - 1) + 1 + 1 + 1;
-}
+static int m_talker_phases(q3t_batch *b) { return 5 * b->m->tc.talker.num_hidden_layers + 3; }
 
-// Runs the decode frame: one standalone kernel per phase, captured in a CUDA
-// graph (default), or the persistent frame kernel with Q3T_FRAME=1.
-static void enqueue_frame(q3t_batch *b, int mt, int max_split) {
-  auto key = std::make_pair(mt, max_split);
+// Runs the decode frame: one kernel per phase, captured into a CUDA graph
+// per (mt, max_units) on first use.  Q3T_FRAME_PROFILE=1 instead launches the
+// phases eagerly with an event after each and prints per-phase device times.
+static void enqueue_frame(q3t_batch *b, int mt, int max_units) {
+  auto key = std::make_pair(mt, max_units);
   auto it = b->programs.find(key);
   if (it == b->programs.end()) {
     std::vector<Phase> ph;
-    build_frame(b, mt, max_split, ph);
-    check_launches();
-    Program pr;
-    pr.host = ph;
-    CK(cudaMalloc(&pr.dev, ph.size() * sizeof(Phase)));
-    CK(cudaMemcpyAsync(pr.dev, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice, b->st));
-    CK(cudaStreamSynchronize(b->st));
-    it = b->programs.emplace(key, std::move(pr)).first;
+    build_frame(b, mt, max_units, ph);
+    it = b->programs.emplace(key, std::move(ph)).first;
   }
-  const Program &pr = it->second;
-  if (b->use_frame_kernel) {
-    unsigned long long *stamps = nullptr;
-    if (getenv("Q3T_FRAME_PROFILE")) {  // per-phase device timestamps, summarised on stderr
-      CK(cudaMallocAsync((void **)&stamps, (pr.host.size() + 1) * 8, b->st));
+  const std::vector<Phase> &pr = it->second;
+  if (getenv("Q3T_FRAME_PROFILE")) {
+    const size_t n = pr.size();
+    std::vector<cudaEvent_t> ev(n + 1);
+    for (auto &e : ev) CK(cudaEventCreate(&e));
+    CK(cudaEventRecord(ev[0], b->st));
+    for (size_t i = 0; i < n; i++) {
+      run_phases(&pr[i], 1, b->st);
+      CK(cudaEventRecord(ev[i + 1], b->st));
     }
-    frame_launch(pr.dev, (int)pr.host.size(), FrameCtl{b->d_ctr, b->d_err, stamps}, b->st);
-    if (stamps) {
-      std::vector<unsigned long long> h(pr.host.size() + 1);
-      CK(cudaMemcpyAsync(h.data(), stamps, h.size() * 8, cudaMemcpyDeviceToHost, b->st));
-      CK(cudaStreamSynchronize(b->st));
-      CK(cudaFreeAsync(stamps, b->st));
-      double by_type[8] = {0};
-      int cnt[8] = {0};
-      double pred = 0, talk = 0;
-      const size_t talker_from = pr.host.size() - (size_t)m_talker_phases(b);
-      for (size_t i = 0; i + 1 < h.size(); i++) {
-        const double us = (h[i + 1] - h[i]) / 1e3;
-        by_type[pr.host[i].type] += us;
-        cnt[pr.host[i].type]++;
-        (i < talker_from ? pred : talk) += us;
-      }
-      fprintf(stderr, "frame profile mt=%d ms=%d phases=%zu: pred %.1f us talker %.1f us |", mt, max_split,
-              pr.host.size(), pred, talk);
-      const char *nm[8] = {"", "norm", "gemm", "qkv", "attn", "silu", "sample", ""};
-      for (int k = 1; k < 7; k++) fprintf(stderr, " %s %d %.1f us", nm[k], cnt[k], by_type[k]);
-      fprintf(stderr, "\n");
+    CK(cudaStreamSynchronize(b->st));
+    double by_type[8] = {0}, pred = 0, talk = 0;
+    int cnt[8] = {0};
+    const size_t talker_from = n - (size_t)m_talker_phases(b);
+    std::map<std::string, std::pair<int, double>> by_shape;
+    for (size_t i = 0; i < n; i++) {
+      float ms = 0.f;
+      CK(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+      const Phase &p = pr[i];
+      by_type[p.type] += ms * 1e3;
+      cnt[p.type]++;
+      (i < talker_from ? pred : talk) += ms * 1e3;
+      char key[96];
+      if (p.type == PH_GEMM)
+        snprintf(key, sizeof key, "%s gemm N%d K%d cs%d epi%d", i < talker_from ? "pred" : "talk", p.gemm.N,
+                 p.gemm.K, p.gemm.cs, p.gemm.epi);
+      else
+        snprintf(key, sizeof key, "%s type%d", i < talker_from ? "pred" : "talk", p.type);
+      by_shape[key].first++;
+      by_shape[key].second += ms * 1e3;
     }
+    for (auto &e : ev) cudaEventDestroy(e);
+    fprintf(stderr, "phase profile (eager) mt=%d mu=%d phases=%zu: pred %.1f us talker %.1f us |", mt, max_units, n,
+            pred, talk);
+    const char *nm[8] = {"", "norm", "gemm", "attn", "sample", "", "", ""};
+    for (int k = 1; k < 5; k++) fprintf(stderr, " %s %d %.1f us", nm[k], cnt[k], by_type[k]);
+    fprintf(stderr, "\n");
+    for (auto &kv : by_shape)
+      fprintf(stderr, "   %-36s %4d x %8.2f us = %9.1f us\n", kv.first.c_str(), kv.second.first,
+              kv.second.second / kv.second.first, kv.second.second);
   } else {
-    run_graph(b, std::make_tuple(0, mt, max_split), [&] { run_phases(pr.host.data(), (int)pr.host.size(), b->st); });
+    run_graph(b, std::make_tuple(0, mt, max_units), [&] { run_phases(pr.data(), (int)pr.size(), b->st); });
   }
   check_launches();
 }
@@ -817,17 +858,19 @@ static void prefill(q3t_batch *b, Req *r) {
     CK(cudaMemcpyAsync(dm, hm, ps * sizeof(int), cudaMemcpyHostToDevice, b->st));
     CK(cudaMemcpyAsync(b->x, d_prompt + (size_t)c0 * H, (size_t)n * H * 4, cudaMemcpyDeviceToDevice, b->st));
     TokView tv{dm, dm + 8, dm + 8 + kPrefillTok, 0};
-    Part pend = run_stack(b, m->talker, talker_kv(b), tv, n, false, bucket_split(c0 + n));
-    // fold the last layer's partials into the residual of every prompt row
-    rmsnorm(b->x, H, 1, 0, pend, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps, dm, n, nullptr, nullptr,
-            b->st);
+    run_stack(b, m->talker, talker_kv(b), tv, n, bucket_units(c0 + n, attn_pw(n)));
     last_n = n;
   }
   int *dm = b->d_pmeta + (size_t)(nch - 1) * ps;
   // final norm of the last prompt token -> hidden[slot] and codec_head input
   rmsnorm(b->x, H, 1, last_n - 1, Part{nullptr, 0, 0, 0}, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps,
           dm + 1, 1, b->d_hidden, dm + 2, b->st);
-  const Part head = linear(m->codec_head, V, H, b->xn, H, b->ws_head, b->n_head, b->Tmax, dm + 1, 1, b->st);
+  GemmArgs hg = ProgBuilder::bf16_x(gemm_args(m->codec_head, V, H, dm + 1, 1), b->xn, H);
+  hg.epi = GE_F32;
+  hg.y = b->hlog;
+  hg.ldy = V;
+  gemm(hg, 1, b->st);
+  const Part head{b->hlog, 1, 0, V};
 
   SampleArgs a = base_sample(b);
   a.part = head;
@@ -998,18 +1041,12 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
   hm[M_SEED] = b->step_counter++;
   CK(cudaMemcpyAsync(b->d_meta, hm, b->meta_n * sizeof(int), cudaMemcpyHostToDevice, b->st));
   CK(cudaMemcpyAsync(b->d_extra, b->h_extra, B * sizeof(float *), cudaMemcpyHostToDevice, b->st));
-  const int mt = bucket_tok(B), ms = bucket_split(maxlen);
+  const int mt = bucket_tok(B), ms = bucket_units(maxlen, attn_pw(mt));
   b->h2d += b->meta_n * sizeof(int) + B * sizeof(float *);
   enqueue_frame(b, mt, ms);
   CK(cudaMemcpyAsync(b->h_eosflag, b->d_eosflag, B * sizeof(int), cudaMemcpyDeviceToHost, b->st));
-  CK(cudaMemcpyAsync(b->h_err, b->d_err, sizeof(int), cudaMemcpyDeviceToHost, b->st));
   CK(cudaStreamSynchronize(b->st));
-  b->d2h += B * sizeof(int) + sizeof(int);
-  if (*b->h_err) {
-    *b->h_err = 0;
-    CK(cudaMemsetAsync(b->d_err, 0, sizeof(int), b->st));
-    FAIL(Q3T_DEVICE_TIMEOUT, "decode frame: a grid barrier wait timed out");
-  }
+  b->d2h += B * sizeof(int);
   for (int i = 0; i < B; i++) {
     Req *r = act[i];
     r->step_idx++;
@@ -1396,16 +1433,19 @@ extern "C" q3t_status q3t_session_decode_embeds(q3t_session *s, const float *emb
     hm[M_ONE] = 1;
     CK(cudaMemcpyAsync(b->d_meta, hm, b->meta_n * sizeof(int), cudaMemcpyHostToDevice, b->st));
     CK(cudaMemcpyAsync(b->x, embeds, (size_t)b->H * 4, cudaMemcpyHostToDevice, b->st));
-    const int ms = bucket_split(r->cache_len + 1);
+    const int ms = bucket_units(r->cache_len + 1, attn_pw(1));
     CK(cudaEventRecord(b->ev0, b->st));
     run_graph(b, std::make_tuple(1, 1, ms), [&] {
       const int *ntok = b->d_meta + M_NTOK_B, *slot = b->d_meta + b->off_slot();
       TokView tvt{ntok, slot, b->d_meta + b->off_tpos(), 0};
-      const Part tp = run_stack(b, m->talker, talker_kv(b), tvt, 1, true, ms);
-      rmsnorm(b->x, b->H, 1, 0, tp, m->talker.final_norm, b->xn, b->H, b->H, m->tc.talker.rms_norm_eps, ntok, 1,
+      run_stack(b, m->talker, talker_kv(b), tvt, 1, ms);
+      rmsnorm(b->x, b->H, 1, 0, Part{}, m->talker.final_norm, b->xn, b->H, b->H, m->tc.talker.rms_norm_eps, ntok, 1,
               b->d_hidden, slot, b->st);
-      const Part head = linear(m->codec_head, b->V, b->H, b->xn, b->H, b->ws_head, b->n_head, b->Tmax, ntok, 1, b->st);
-      reduce_rows(head, b->V, ntok, 1, b->tlog, b->st);
+      GemmArgs hg = ProgBuilder::bf16_x(gemm_args(m->codec_head, b->V, b->H, ntok, 1), b->xn, b->H);
+      hg.epi = GE_F32;
+      hg.y = b->tlog;
+      hg.ldy = b->V;
+      gemm(hg, 1, b->st);
     });
     CK(cudaEventRecord(b->ev1, b->st));
     if (logits) CK(cudaMemcpyAsync(logits, b->tlog, (size_t)b->V * 4, cudaMemcpyDeviceToHost, b->st));

@@ -81,8 +81,7 @@ uint16_t *upload_bf16(const q3t_tensor *t, DevArena &ar, cudaStream_t st);
 constexpr int kPage = 16;
 constexpr int kMaxSeq = 4096;                 // the reference's talker cache capacity
 constexpr int kPtStride = kMaxSeq / kPage;    // pages per sequence
-constexpr int kChunk = 64;                    // keys per attention split
-constexpr int kMaxSplit = kMaxSeq / kChunk;
+constexpr int kPredPages = 2;                 // predictor KV pages per slot (num_code_groups + 1 <= 32 keys)
 constexpr int kPrefillTok = 64;
 
 struct Req {
@@ -110,11 +109,6 @@ struct Req {
   int64_t samples = 0;
   int64_t first_token = -1, first_token_raw = -1;
   std::string error;
-};
-
-struct Program {
-  std::vector<Phase> host;
-  Phase *dev = nullptr;
 };
 
 struct GraphEntry {
@@ -181,9 +175,8 @@ struct q3t_batch {
   // activations
   int Tmax = 0;
   float *x = nullptr, *tlog = nullptr, *plog = nullptr;
-  // split-K partial-sum workspaces of the linears (one per output kind)
-  float *ws_qkv = nullptr, *ws_o = nullptr, *ws_gu = nullptr, *ws_down = nullptr, *ws_head = nullptr;
-  long long n_qkv = 0, n_o = 0, n_gu = 0, n_down = 0, n_head = 0;
+  float *ss = nullptr;    // [hidden / 128][Tmax] sum-of-squares partials of the residual rows
+  float *hlog = nullptr;  // [Tmax][max(V, PV)] head GEMM output
   uint16_t *xn = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
   q3t::AttnWork ws{};
   // metadata
@@ -196,10 +189,7 @@ struct q3t_batch {
   // graphs
   bool use_graphs = true;
   std::map<std::tuple<int, int, int>, q3t::GraphEntry> graphs;
-  std::map<std::pair<int, int>, q3t::Program> programs;  // decode-frame phase programs
-  bool use_frame_kernel = true;
-  unsigned *d_ctr = nullptr;  // frame-kernel barrier counters
-  int *d_err = nullptr, *h_err = nullptr;
+  std::map<std::pair<int, int>, std::vector<q3t::Phase>> programs;  // decode-frame phase lists
   int step_counter = 0;
   // requests
   std::vector<q3t::Req *> slots;

@@ -13,14 +13,25 @@ namespace q3t {
 // ---------------------------------------------------------------------------
 // shared helpers
 // ---------------------------------------------------------------------------
+// Sum of the split partials at (t, n..n+3), in split order.  The loads of a
+// batch of 8 splits are issued before any add, so a fold costs one memory
+// latency per 8 splits rather than one per split.
 Q3T_DEV float4 part4(const Part &P, int t, int n) {
-  float4 a = *reinterpret_cast<const float4 *>(P.p + (size_t)t * P.ld + n);
-  for (int s = 1; s < P.splits; s++) {
-    const float4 b = *reinterpret_cast<const float4 *>(P.p + s * P.stride + (size_t)t * P.ld + n);
-    a.x += b.x;
-    a.y += b.y;
-    a.z += b.z;
-    a.w += b.w;
+  const float *p = P.p + (size_t)t * P.ld + n;
+  float4 a = *reinterpret_cast<const float4 *>(p);
+  for (int s = 1; s < P.splits; s += 8) {
+    float4 b[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+      b[i] = s + i < P.splits ? *reinterpret_cast<const float4 *>(p + (s + i) * P.stride)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      a.x += b[i].x;
+      a.y += b[i].y;
+      a.z += b[i].z;
+      a.w += b[i].w;
+    }
   }
   return a;
 }
@@ -147,303 +158,305 @@ Q3T_DEV void d_rmsnorm(const RmsArgs &a, int t, float *red) {
 }
 
 // ---------------------------------------------------------------------------
-// Skinny GEMM item on the tensor cores (m16n8k16): 8 warps = 8 row blocks
-// (128 output rows) x one K chunk of 16*FR x up to 64 tokens.  Weights are
-// fragment-packed (one 512-byte A fragment per 16x16 tile, rb-major); the
-// X chunk is staged once in shared memory for the 8 warps; partial sums are
-// written with plain stores to P[split][token][row].
-// ---------------------------------------------------------------------------
-constexpr int kLinWarps = 8;
-
-Q3T_DEV void lin_item_coords(const LinArgs &a, int item, int &rg, int &ks, int &tc) {
-  const int rgn = a.N / (16 * kLinWarps), ksn = a.K / (16 * a.fr);
-  rg = item % rgn;
-  ks = (item / rgn) % ksn;
-  tc = item / (rgn * ksn);
-}
-
-template <int FR>
-Q3T_DEV void d_linear_load(const LinArgs &a, int item, uint4 *frag) {
-  int rg, ks, tc;
-  lin_item_coords(a, item, rg, ks, tc);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rb = rg * kLinWarps + warp;
-  const uint4 *wp = a.W + ((size_t)rb * (a.K >> 4) + ks * FR) * 32 + lane;
-#pragma unroll
-  for (int i = 0; i < FR; i++) frag[i] = ldg_stream(wp + i * 32);
-}
-
-template <int NT, int FR>
-Q3T_DEV void d_linear_compute(const LinArgs &a, int item, const uint4 *frag, uint16_t *xs) {
-  constexpr int kc = FR * 16, ldsx = kc + 8, c8n = kc >> 3;
-  int rg, ks, tc;
-  lin_item_coords(a, item, rg, ks, tc);
-  const int tok_base = tc * 64, k0 = ks * kc;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int ntok = *a.ntok - tok_base;
-  ntok = ntok < 0 ? 0 : (ntok > NT * 8 ? NT * 8 : ntok);
-  for (int idx = threadIdx.x; idx < NT * 8 * c8n; idx += blockDim.x) {
-    const int r = idx / c8n, c8 = (idx - r * c8n) * 8;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (r < ntok) v = *reinterpret_cast<const uint4 *>(a.X + (size_t)(tok_base + r) * a.ldx + k0 + c8);
-    *reinterpret_cast<uint4 *>(xs + r * ldsx + c8) = v;
-  }
-  __syncthreads();
-  float acc[NT][4];
-#pragma unroll
-  for (int j = 0; j < NT; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-  const int g = lane >> 2, t = lane & 3;
-#pragma unroll
-  for (int i = 0; i < FR; i++) {
-#pragma unroll
-    for (int j = 0; j < NT; j++) {
-      const uint16_t *xr = xs + (j * 8 + g) * ldsx + i * 16 + 2 * t;
-      const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xr);
-      const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xr + 8);
-      mma_16816(acc[j], frag[i].x, frag[i].y, frag[i].z, frag[i].w, b0, b1);
-    }
-  }
-  const int row = (rg * kLinWarps + warp) * 16 + g;
-  float *Y = a.P + ks * a.pstride;
-#pragma unroll
-  for (int j = 0; j < NT; j++) {
-    const int tk = j * 8 + 2 * t;
-    if (tk < ntok) {
-      float *y = Y + (size_t)(tok_base + tk) * a.ldy + row;
-      y[0] = acc[j][0];
-      y[8] = acc[j][2];
-    }
-    if (tk + 1 < ntok) {
-      float *y = Y + (size_t)(tok_base + tk + 1) * a.ldy + row;
-      y[0] = acc[j][1];
-      y[8] = acc[j][3];
-    }
-  }
-  __syncthreads();  // xs is reused by the next item
-}
-
-// ---------------------------------------------------------------------------
-// q/k RMSNorm + RoPE + bf16 q out + K/V append for token t (non-fused path,
-// used when a batch holds several tokens of one sequence).
-// ---------------------------------------------------------------------------
-Q3T_DEV void d_qkv_post(const QkvArgs &a, int t) {
-  if (t >= *a.tv.ntok) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  const int pos = a.tv.pos[t] + a.tv.pos_add, seq = a.tv.seq[t];
-  const int nh = a.nh, nkv = a.nkv;
-  for (int w = warp; w < nh + 2 * nkv; w += nw) {
-    if (w < nh + nkv) {
-      const bool isq = w < nh;
-      const int h = isq ? w : w - nh;
-      const float4 v = part4(a.qkv, t, (isq ? h : nh + h) * 128 + lane * 4);
-      float o[4];
-      norm_rope_lane(v, isq ? a.q_norm : a.k_norm, a.eps, lane, pos, a.inv_freq, o);
-      uint2 p;
-      p.x = pack_bf16x2(o[0], o[1]);
-      p.y = pack_bf16x2(o[2], o[3]);
-      if (isq)
-        *reinterpret_cast<uint2 *>(a.qout + (size_t)t * nh * 128 + h * 128 + lane * 4) = p;
-      else
-        *reinterpret_cast<uint2 *>(a.kv.k + a.layer * a.kv.layer_stride + page_elem(a.kv, seq, pos, h) + lane * 4) = p;
-    } else {
-      const int h = w - nh - nkv;
-      const float4 v = part4(a.qkv, t, (nh + nkv + h) * 128 + lane * 4);
-      uint2 p;
-      p.x = pack_bf16x2(v.x, v.y);
-      p.y = pack_bf16x2(v.z, v.w);
-      *reinterpret_cast<uint2 *>(a.kv.v + a.layer * a.kv.layer_stride + page_elem(a.kv, seq, pos, h) + lane * 4) = p;
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Split-K flash-decoding GQA attention item (split sp, kv head g, token t)
-// (attention.rs:88-123 with the f32 softmax of nn/attention.rs:13-26) on a
-// group of exactly 128 threads (tid 0..127); `sync` is the group barrier.
-// Both query heads 2g, 2g+1 share every K/V row read.  Splits of `chunk`
-// keys write (o, m, l) partials; the last item of (t, g) to finish merges
-// them and resets the counter.  fused: also does the q/k norm + RoPE and the
-// K/V append of the new token (one token per sequence in the batch).
+// Split-K flash-decoding GQA attention (attention.rs:88-123 with the f32
+// softmax of nn/attention.rs:13-26) over the paged cache, as independent
+// warp work units.  A unit is (token t, kv head g, a run of up to pw pages of
+// t's keys [0, pos]); both query heads 2g, 2g+1 share every K/V page read.
+// Units are numbered token-major (all heads and page runs of token 0, then
+// token 1, ...) and handed to warps round-robin, so a launch is a few
+// balanced waves whatever the mix of sequence lengths.  A token whose keys
+// fit one unit writes its output directly; otherwise each unit writes an
+// (o, m, l) partial and the last unit of (t, g) to finish merges them in unit
+// order and resets the counter.  q (normed, rotated, bf16) and the token's
+// own K/V come from the QKV projection's epilogue.
+//
+// Per 16-key page, q.k runs on the tensor cores as S^T = K * Q^T
+// (m16n8k16: A = 16 keys x 16 dims, B = 16 dims x 8 columns of which
+// columns 0/1 are the two heads).  The dims of each k-step are permuted so
+// that every lane's A and B fragments are one 16-byte load: lane (g, t)
+// holds dims [8(t + 4kp), +8) of keys g and g + 8 for kp < 4, which feed
+// k-steps 2kp (dims +0..3) and 2kp+1 (dims +4..7); q uses the same map, so
+// the dot products are unchanged.  Softmax and p.v stay in f32 on the CUDA
+// cores (p is not rounded).
 // ---------------------------------------------------------------------------
 constexpr int kPart = 132;
+constexpr int kAttnWarps = 4;
 
 struct AttnSmem {
-  float qs[2][128];
-  float sc[2][256];
-  float red[2][4];
-  float opart[2][2][128];
-  int last;
+  float ps[kAttnWarps][2][16];
+  int pre[kAttnMaxTok + 1];  // first unit of each token
 };
 
-template <class Sync>
-Q3T_DEV void d_attn(const AttnArgs &a, int sp, int g, int t, int tid, AttnSmem &S, Sync sync) {
-  const int w = tid >> 5, lane = tid & 31;
-  if (t >= *a.tv.ntok) return;
+// Per-warp ring of kAttnStages pages in shared memory, filled with cp.async:
+// K rows are stored with their 16-byte chunks XOR-swizzled by (row & 7), so
+// the fragment reads (8 rows x 4 chunks per instruction) hit distinct banks;
+// V rows are stored as they are.
+constexpr int kAttnStages = 3;
+constexpr int kPageElems = 16 * 128;
+constexpr size_t kAttnDynSmem = (size_t)kAttnWarps * kAttnStages * 2 * kPageElems * 2;  // 96 KB
+
+Q3T_DEV void issue_page(uint16_t *ks, uint16_t *vs, const uint16_t *kp, const uint16_t *vp, int lane) {
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int idx = lane + 32 * j, row = idx >> 4, c = idx & 15;
+    cp_async16(ks + row * 128 + ((c ^ (row & 7)) << 3), kp + row * 128 + c * 8, 16);
+    cp_async16(vs + row * 128 + c * 8, vp + row * 128 + c * 8, 16);
+  }
+}
+
+// Running softmax state of one warp: m per head, l = this lane's share,
+// o[h][e] = unnormalised output for dims 8(lane & 15) + e over the keys of
+// parity lane >> 4.
+struct AttnAcc {
+  float m[2], l[2], o[2][8];
+};
+
+// One staged page: ks / vs = the page's K / V in the warp's ring; nv valid keys.
+Q3T_DEV void attn_page(AttnAcc &A, const uint16_t *ks, const uint16_t *vs, const uint4 *qf, int nv, float scale,
+                       float (*ps)[16], int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    const int ch = ((t + 4 * q) ^ g) << 3;  // rows g and g + 8 share the swizzle
+    const uint4 k0 = *reinterpret_cast<const uint4 *>(ks + g * 128 + ch);
+    const uint4 k1 = *reinterpret_cast<const uint4 *>(ks + (g + 8) * 128 + ch);
+    mma_16816(c, k0.x, k1.x, k0.y, k1.y, qf[q].x, qf[q].y);
+    mma_16816(c, k0.z, k1.z, k0.w, k1.w, qf[q].z, qf[q].w);
+  }
+  // c0/c1 = key g, heads 0/1; c2/c3 = key g + 8 (valid on lanes t == 0)
+  const bool ok0 = t == 0 && g < nv, ok1 = t == 0 && g + 8 < nv;
+  const float s00 = ok0 ? c[0] * scale : -FLT_MAX, s01 = ok0 ? c[1] * scale : -FLT_MAX;
+  const float s10 = ok1 ? c[2] * scale : -FLT_MAX, s11 = ok1 ? c[3] * scale : -FLT_MAX;
+  float mx0 = fmaxf(s00, s10), mx1 = fmaxf(s01, s11);
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+  }
+  mx0 = __shfl_sync(0xffffffffu, mx0, 0);
+  mx1 = __shfl_sync(0xffffffffu, mx1, 0);
+  const float mn0 = fmaxf(A.m[0], mx0), mn1 = fmaxf(A.m[1], mx1);
+  const float cr0 = expf(A.m[0] - mn0), cr1 = expf(A.m[1] - mn1);
+  A.m[0] = mn0;
+  A.m[1] = mn1;
+  const float p00 = ok0 ? expf(s00 - mn0) : 0.f, p01 = ok0 ? expf(s01 - mn1) : 0.f;
+  const float p10 = ok1 ? expf(s10 - mn0) : 0.f, p11 = ok1 ? expf(s11 - mn1) : 0.f;
+  A.l[0] = A.l[0] * cr0 + p00 + p10;
+  A.l[1] = A.l[1] * cr1 + p01 + p11;
+  if (t == 0) {
+    ps[0][g] = p00;
+    ps[0][g + 8] = p10;
+    ps[1][g] = p01;
+    ps[1][g + 8] = p11;
+  }
+#pragma unroll
+  for (int e = 0; e < 8; e++) {
+    A.o[0][e] *= cr0;
+    A.o[1][e] *= cr1;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int key = 2 * i + (lane >> 4);
+    if (key < nv) {
+      const float pa = ps[0][key], pb = ps[1][key];
+      const uint4 vv = *reinterpret_cast<const uint4 *>(vs + key * 128 + 8 * (lane & 15));
+      const uint32_t w4[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float v0 = bf2f(w4[e] & 0xffffu), v1 = bf2f(w4[e] >> 16);
+        A.o[0][2 * e] += pa * v0;
+        A.o[0][2 * e + 1] += pa * v1;
+        A.o[1][2 * e] += pb * v0;
+        A.o[1][2 * e + 1] += pb * v1;
+      }
+    }
+  }
+  __syncwarp();
+}
+
+// pages per unit for a sequence of `pages` pages (at most kAttnMaxUnits units)
+Q3T_DEV int attn_unit_pages(int pages, int pw) {
+  const int m = (pages + kAttnMaxUnits - 1) / kAttnMaxUnits;
+  return pw > m ? pw : m;
+}
+
+Q3T_DEV void store_bf16x8(uint16_t *dst, const float *v, float inv) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0] * inv, v[1] * inv);
+  u.y = pack_bf16x2(v[2] * inv, v[3] * inv);
+  u.z = pack_bf16x2(v[4] * inv, v[5] * inv);
+  u.w = pack_bf16x2(v[6] * inv, v[7] * inv);
+  *reinterpret_cast<uint4 *>(dst) = u;
+}
+
+// Unit r of token t, run by one warp (ps, ring: the warp's shared buffers).
+Q3T_DEV void attn_unit(const AttnArgs &a, int t, int r, float (*ps)[16], uint16_t *ring, int lane) {
   const KVView &kv = a.kv;
   const int pos = a.tv.pos[t] + a.tv.pos_add, L = pos + 1, seq = a.tv.seq[t];
-  const int nsplit = (L + a.chunk - 1) / a.chunk;
-  if (sp >= nsplit) return;
-  const int j0 = sp * a.chunk;
-  const int n = min(L - j0, a.chunk);
+  const int pages = (L + 15) >> 4, pw = attn_unit_pages(pages, a.pw), nu = (pages + pw - 1) / pw;
+  const int g = r / nu, j = r - g * nu;
+  const int p0 = j * pw, np = min(pw, pages - p0);
   const int nh = a.nh;
   uint16_t *kb = kv.k + a.layer * kv.layer_stride;
   uint16_t *vb = kv.v + a.layer * kv.layer_stride;
-  if (a.fused) {
-    if (w < 2) {
-      const int h = 2 * g + w;
-      const float4 v = part4(a.qkv, t, h * 128 + lane * 4);
-      float o[4];
-      norm_rope_lane(v, a.q_norm, a.eps, lane, pos, a.inv_freq, o);
+  const int *pt = kv.page_table + (size_t)seq * kv.pt_stride;
+  const int my_page = lane < np ? pt[p0 + lane] : 0;
+  const size_t head_off = (size_t)g * 16 * 128, page_elems = (size_t)kv.n_kv * 16 * 128;
+  // pages 0 and 1 of the unit in flight before the q loads
 #pragma unroll
-      for (int i = 0; i < 4; i++) S.qs[w][lane * 4 + i] = bf16_round(o[i]);
-    } else if (sp == nsplit - 1) {
-      const size_t e = page_elem(kv, seq, pos, g) + lane * 4;
-      if (w == 2) {
-        const float4 v = part4(a.qkv, t, (nh + g) * 128 + lane * 4);
-        float o[4];
-        norm_rope_lane(v, a.k_norm, a.eps, lane, pos, a.inv_freq, o);
-        uint2 p;
-        p.x = pack_bf16x2(o[0], o[1]);
-        p.y = pack_bf16x2(o[2], o[3]);
-        *reinterpret_cast<uint2 *>(kb + e) = p;
-      } else {
-        const float4 v = part4(a.qkv, t, (nh + kv.n_kv + g) * 128 + lane * 4);
-        uint2 p;
-        p.x = pack_bf16x2(v.x, v.y);
-        p.y = pack_bf16x2(v.z, v.w);
-        *reinterpret_cast<uint2 *>(vb + e) = p;
-      }
+  for (int i = 0; i < kAttnStages - 1; i++) {
+    if (i < np) {
+      const size_t off = (size_t)__shfl_sync(0xffffffffu, my_page, i) * page_elems + head_off;
+      issue_page(ring + i * 2 * kPageElems, ring + (i * 2 + 1) * kPageElems, kb + off, vb + off, lane);
     }
-  } else {
-    for (int e = tid; e < 256; e += 128)
-      S.qs[e >> 7][e & 127] = bf2f(a.qin[(size_t)t * nh * 128 + (2 * g + (e >> 7)) * 128 + (e & 127)]);
+    cp_async_commit();
   }
-  sync();
-  for (int jj = tid; jj < n; jj += 128) {
-    const uint4 *kr = reinterpret_cast<const uint4 *>(kb + page_elem(kv, seq, j0 + jj, g));
-    float s0 = 0.f, s1 = 0.f;
-#pragma unroll 4
-    for (int c = 0; c < 16; c++) {
-      const uint4 u = kr[c];
-      const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const float k0v = bf2f(wv[e] & 0xffffu), k1v = bf2f(wv[e] >> 16);
-        s0 += S.qs[0][c * 8 + 2 * e] * k0v + S.qs[0][c * 8 + 2 * e + 1] * k1v;
-        s1 += S.qs[1][c * 8 + 2 * e] * k0v + S.qs[1][c * 8 + 2 * e + 1] * k1v;
-      }
-    }
-    S.sc[0][jj] = s0 * a.scale;
-    S.sc[1][jj] = s1 * a.scale;
-  }
-  sync();
-  float m0 = -FLT_MAX, m1 = -FLT_MAX;
-  for (int jj = tid; jj < n; jj += 128) {
-    m0 = fmaxf(m0, S.sc[0][jj]);
-    m1 = fmaxf(m1, S.sc[1][jj]);
-  }
-  m0 = warp_max(m0);
-  m1 = warp_max(m1);
-  if (lane == 0) {
-    S.red[0][w] = m0;
-    S.red[1][w] = m1;
-  }
-  sync();
-  m0 = fmaxf(fmaxf(S.red[0][0], S.red[0][1]), fmaxf(S.red[0][2], S.red[0][3]));
-  m1 = fmaxf(fmaxf(S.red[1][0], S.red[1][1]), fmaxf(S.red[1][2], S.red[1][3]));
-  sync();
-  float l0 = 0.f, l1 = 0.f;
-  for (int jj = tid; jj < n; jj += 128) {
-    const float p0 = expf(S.sc[0][jj] - m0), p1 = expf(S.sc[1][jj] - m1);
-    S.sc[0][jj] = p0;
-    S.sc[1][jj] = p1;
-    l0 += p0;
-    l1 += p1;
-  }
-  l0 = warp_sum(l0);
-  l1 = warp_sum(l1);
-  if (lane == 0) {
-    S.red[0][w] = l0;
-    S.red[1][w] = l1;
-  }
-  sync();
-  l0 = S.red[0][0] + S.red[0][1] + S.red[0][2] + S.red[0][3];
-  l1 = S.red[1][0] + S.red[1][1] + S.red[1][2] + S.red[1][3];
+  // q fragments: lane (g, t) < 8 rows holds head g's dims [8(t + 4kp), +8)
+  uint4 qf[4];
   {
-    const int dp = tid & 63, kh = tid >> 6, d = dp * 2;
-    float o00 = 0.f, o01 = 0.f, o10 = 0.f, o11 = 0.f;
-    for (int jj = kh; jj < n; jj += 2) {
-      const uint32_t vv = *reinterpret_cast<const uint32_t *>(vb + page_elem(kv, seq, j0 + jj, g) + d);
-      const float v0 = bf2f(vv & 0xffffu), v1 = bf2f(vv >> 16);
-      const float p0 = S.sc[0][jj], p1 = S.sc[1][jj];
-      o00 += p0 * v0;
-      o01 += p0 * v1;
-      o10 += p1 * v0;
-      o11 += p1 * v1;
+    const int gq = lane >> 2, tq = lane & 3;
+    const uint16_t *qrow = a.q + (size_t)t * nh * 128 + (2 * g + (gq & 1)) * 128;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const uint4 v = *reinterpret_cast<const uint4 *>(qrow + 8 * (tq + 4 * q));
+      qf[q] = gq < 2 ? v : make_uint4(0u, 0u, 0u, 0u);
     }
-    S.opart[kh][0][d] = o00;
-    S.opart[kh][0][d + 1] = o01;
-    S.opart[kh][1][d] = o10;
-    S.opart[kh][1][d + 1] = o11;
   }
-  sync();
-  const int out_ld = nh * 128;
-  if (nsplit == 1) {
-    for (int e = tid; e < 256; e += 128) {
-      const int h = e >> 7, d = e & 127;
-      const float o = S.opart[0][h][d] + S.opart[1][h][d];
-      a.out[(size_t)t * out_ld + (2 * g + h) * 128 + d] = f2bf(o / (h ? l1 : l0));
+  AttnAcc A;
+  A.m[0] = A.m[1] = -FLT_MAX;
+  A.l[0] = A.l[1] = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; e++) A.o[0][e] = A.o[1][e] = 0.f;
+  for (int i = 0; i < np; i++) {
+    const int nx = i + kAttnStages - 1;  // page to start now, into the slot page i - 1 used
+    if (nx < np) {
+      const int sl = nx % kAttnStages;
+      const size_t off = (size_t)__shfl_sync(0xffffffffu, my_page, nx) * page_elems + head_off;
+      issue_page(ring + sl * 2 * kPageElems, ring + (sl * 2 + 1) * kPageElems, kb + off, vb + off, lane);
     }
-  } else {
-    float *P = a.ws.part + (((size_t)t * kv.n_kv + g) * a.ws.max_split + sp) * 2 * kPart;
-    for (int e = tid; e < 256; e += 128) {
-      const int h = e >> 7, d = e & 127;
-      P[h * kPart + d] = S.opart[0][h][d] + S.opart[1][h][d];
+    cp_async_commit();
+    cp_async_wait<kAttnStages - 1>();  // this lane's copies of page i have landed
+    __syncwarp();                      // ... and every lane's
+    const int sl = i % kAttnStages, key0 = (p0 + i) * 16;
+    attn_page(A, ring + sl * 2 * kPageElems, ring + (sl * 2 + 1) * kPageElems, qf, min(16, L - key0), a.scale, ps,
+              lane);
+  }
+  // fold the two key parities and the lanes' l shares
+#pragma unroll
+  for (int e = 0; e < 8; e++) {
+    A.o[0][e] += __shfl_xor_sync(0xffffffffu, A.o[0][e], 16);
+    A.o[1][e] += __shfl_xor_sync(0xffffffffu, A.o[1][e], 16);
+  }
+  A.l[0] = warp_sum(A.l[0]);
+  A.l[1] = warp_sum(A.l[1]);
+  uint16_t *out = a.out + (size_t)t * nh * 128 + 2 * g * 128;
+  if (nu == 1) {
+    if (lane < 16) {
+      store_bf16x8(out + 8 * lane, A.o[0], 1.f / A.l[0]);
+      store_bf16x8(out + 128 + 8 * lane, A.o[1], 1.f / A.l[1]);
     }
-    if (tid == 0) {
-      P[128] = m0;
-      P[129] = l0;
-      P[kPart + 128] = m1;
-      P[kPart + 129] = l1;
+    return;
+  }
+  float *P0 = a.ws.part + ((size_t)t * kv.n_kv + g) * kAttnMaxUnits * 2 * kPart;
+  float *P = P0 + (size_t)j * 2 * kPart;
+  if (lane < 16) {
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      *reinterpret_cast<float4 *>(P + h * kPart + 8 * lane) = make_float4(A.o[h][0], A.o[h][1], A.o[h][2], A.o[h][3]);
+      *reinterpret_cast<float4 *>(P + h * kPart + 8 * lane + 4) =
+          make_float4(A.o[h][4], A.o[h][5], A.o[h][6], A.o[h][7]);
     }
-    __threadfence();
-    sync();
-    if (tid == 0) {
-      const int prev = atomicAdd(&a.ws.counters[t * kv.n_kv + g], 1);
-      S.last = prev == nsplit - 1;
-    }
-    sync();
-    if (S.last) {
-      __threadfence();
-      const float *P0 = a.ws.part + ((size_t)t * kv.n_kv + g) * a.ws.max_split * 2 * kPart;
-      for (int e = tid; e < 256; e += 128) {
-        const int h = e >> 7, d = e & 127;
-        float M = -FLT_MAX;
-        for (int s = 0; s < nsplit; s++) M = fmaxf(M, __ldcg(P0 + (size_t)s * 2 * kPart + h * kPart + 128));
-        float Ls = 0.f, acc = 0.f;
-        for (int s = 0; s < nsplit; s++) {
-          const float *Ps = P0 + (size_t)s * 2 * kPart + h * kPart;
-          const float f = expf(__ldcg(Ps + 128) - M);
-          Ls += __ldcg(Ps + 129) * f;
-          acc += __ldcg(Ps + d) * f;
-        }
-        a.out[(size_t)t * out_ld + (2 * g + h) * 128 + d] = f2bf(acc / Ls);
+  }
+  if (lane == 0) {
+    P[128] = A.m[0];
+    P[129] = A.l[0];
+    P[kPart + 128] = A.m[1];
+    P[kPart + 129] = A.l[1];
+  }
+  __threadfence();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) last = atomicAdd(&a.ws.counters[t * kv.n_kv + g], 1) == nu - 1;
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  __threadfence();
+  // merge the units in order: lane handles head lane >> 4, dims 8(lane & 15) + [0, 8)
+  const int h = lane >> 4, d0 = 8 * (lane & 15);
+  float M = -FLT_MAX, Ls = 0.f, acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; e++) acc[e] = 0.f;
+  for (int s0 = 0; s0 < nu; s0 += 4) {  // four partials' loads in flight at a time
+    float ms[4], ls[4];
+    float4 o0[4], o1[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      if (s0 + i < nu) {
+        const float *Ps = P0 + (size_t)(s0 + i) * 2 * kPart + h * kPart;
+        ms[i] = __ldcg(Ps + 128);
+        ls[i] = __ldcg(Ps + 129);
+        o0[i] = __ldcg(reinterpret_cast<const float4 *>(Ps + d0));
+        o1[i] = __ldcg(reinterpret_cast<const float4 *>(Ps + d0 + 4));
       }
-      if (tid == 0) a.ws.counters[t * kv.n_kv + g] = 0;
     }
-    sync();
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      if (s0 + i < nu) {
+        const float Mn = fmaxf(M, ms[i]), fa = expf(M - Mn), fb = expf(ms[i] - Mn);
+        Ls = Ls * fa + ls[i] * fb;
+        const float ov[8] = {o0[i].x, o0[i].y, o0[i].z, o0[i].w, o1[i].x, o1[i].y, o1[i].z, o1[i].w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) acc[e] = acc[e] * fa + ov[e] * fb;
+        M = Mn;
+      }
+    }
   }
+  store_bf16x8(out + h * 128 + d0, acc, 1.f / Ls);
+  if (lane == 0) a.ws.counters[t * kv.n_kv + g] = 0;
 }
 
-// SwiGLU silu(gate) * up of the reduced gate|up partials, 4 columns per thread
-Q3T_DEV void d_silu(const SiluArgs &a, int t, int i) {
-  if (t >= *a.ntok || i >= a.I) return;
-  const float4 g = part4(a.gu, t, i);
-  const float4 u = part4(a.gu, t, a.I + i);
-  uint2 p;
-  p.x = pack_bf16x2(silu(g.x) * u.x, silu(g.y) * u.y);
-  p.y = pack_bf16x2(silu(g.z) * u.z, silu(g.w) * u.w);
-  *reinterpret_cast<uint2 *>(a.out + (size_t)t * a.I + i) = p;
+// A group of kAttnWarps warps (tid 0..127, `sync` its barrier): numbers the
+// units of the launch, then its warps take units warp0 + w, + nwarps, ...
+template <class Sync>
+Q3T_DEV void d_attn(const AttnArgs &a, int tid, int warp0, int nwarps, AttnSmem &S, uint16_t *ring, Sync sync) {
+  const int w = tid >> 5, lane = tid & 31;
+  int ntok = *a.tv.ntok;
+  ntok = ntok < kAttnMaxTok ? ntok : kAttnMaxTok;
+  if (w == 0) {
+    int carry = 0;
+    for (int base = 0; base < ntok; base += 32) {
+      const int t = base + lane;
+      int n = 0;
+      if (t < ntok) {
+        const int pages = (a.tv.pos[t] + a.tv.pos_add + 16) >> 4;
+        const int pw = attn_unit_pages(pages, a.pw);
+        n = (pages + pw - 1) / pw * a.kv.n_kv;
+      }
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, n, o);
+        if (lane >= o) n += v;
+      }
+      if (t < ntok) S.pre[t + 1] = carry + n;
+      carry += __shfl_sync(0xffffffffu, n, 31);
+    }
+    if (lane == 0) S.pre[0] = 0;
+  }
+  sync();
+  const int total = S.pre[ntok];
+  for (int u = warp0 + w; u < total; u += nwarps) {
+    int lo = 0, hi = ntok;  // largest t with pre[t] <= u
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (S.pre[mid] <= u)
+        lo = mid;
+      else
+        hi = mid;
+    }
+    attn_unit(a, lo, u - S.pre[lo], S.ps[w], ring + (size_t)w * kAttnStages * 2 * kPageElems, lane);
+  }
+  sync();  // S is reused by the caller's next item
 }
 
 // ---------------------------------------------------------------------------

@@ -1,19 +1,17 @@
 // Talker / code-predictor kernels for sm_100a.
 //
 // One decoder layer of tts_qwen3_tts/src/model/talker/network/layer.rs:23-44
-// runs as:  rmsnorm -> linear(Wqkv) -> [qkv_post] -> attention -> linear(Wo)
-// -> rmsnorm (folds the o_proj partials into the residual) -> linear(Wgu) ->
-// silu_mul -> linear(Wdown) (folded by the next rmsnorm).  Linears write
-// split-K partial sums with plain stores; the consumer reduces them in a
-// fixed order, so results are deterministic.
-//
-// Two execution forms share the device code of lm_device.cuh:
-//   - standalone kernels (prefill, the isolated decode step), PDL-aware: the
-//     weight stream of a linear starts before griddepcontrol.wait;
-//   - the persistent frame kernel: one cooperative launch per decode frame
-//     runs every phase (15 code-predictor passes + the talker + sampling),
-//     separated by grid barriers; each GEMM phase issues its weight loads
-//     before the barrier that precedes it.
+// runs as five kernels:
+//   gemm(Wqkv)  X = RMSNorm(x) (from the previous layer's sum-of-squares
+//               partials); epilogue q/k RMSNorm + RoPE, q -> bf16, K/V
+//               appended to the paged cache
+//   attention   split-K flash-decoding over the pages
+//   gemm(Wo)    epilogue x += o, sum-of-squares partials of x
+//   gemm(Wgu)   X = RMSNorm(x); epilogue silu(gate) * up -> bf16
+//   gemm(Wdown) epilogue x += down, sum-of-squares partials of x
+// Every kernel is PDL-aware: a GEMM's weight stream is issued before
+// griddepcontrol.wait, and each kernel lets its dependent launch early.
+// Sums run in a fixed order, so results are deterministic.
 #include <cstdlib>
 #include <utility>
 
@@ -109,8 +107,8 @@ void f32_to_bf16(const float *src, uint16_t *dst, int64_t n, cudaStream_t st) {
 __global__ void __launch_bounds__(256) k_rmsnorm(RmsArgs a) {
   __shared__ float red[33];
   pdl_wait();
-  d_rmsnorm(a, blockIdx.x, red);
   pdl_launch();
+  d_rmsnorm(a, blockIdx.x, red);
 }
 
 RmsArgs rms_args(float *x, int ldx, int row_mul, int row_add, Part add, const float *gamma, uint16_t *out, int ldo,
@@ -141,151 +139,348 @@ void rmsnorm(float *x, int ldx, int row_mul, int row_add, Part add, const float 
   rmsnorm(rms_args(x, ldx, row_mul, row_add, add, gamma, out, ldo, H, eps, ntok, out_f32, slot), grid_rows, st);
 }
 
-template <int NT, int FR>
-__global__ void __launch_bounds__(kLinWarps * 32, 2) k_linear(LinArgs a) {
-  extern __shared__ __align__(16) uint16_t xs[];
-  uint4 frag[FR];
-  const int item = blockIdx.x;
-  d_linear_load<FR>(a, item, frag);
+// ---------------------------------------------------------------------------
+// Cluster split-K GEMM (GemmArgs in lm_kernels.cuh).  CTA = 8 warps = 8 row
+// blocks of 16 (one 128-row output block) x the cluster rank's K range x up
+// to 8*NT tokens.  Each warp holds its KT weight fragments in registers,
+// issued before griddepcontrol.wait so the weight stream overlaps the end of
+// the previous kernel.  X (bf16, or f32 residual rows normalised here) is
+// staged once per CTA in shared memory; the m16n8k16 products go to an f32
+// tile [token][row]; after a cluster barrier CTA rank c sums token slice c of
+// all ranks' tiles (rank order) and runs the epilogue, one warp per token,
+// lane = 4 consecutive rows.
+// ---------------------------------------------------------------------------
+constexpr int kTileLd = 132;  // f32 pitch of the reduction tile (bank-conflict-free fragment stores)
+
+constexpr int kMaxNss = 16;   // sum-of-squares partials per row (hidden <= 2048)
+
+static size_t gemm_smem(int nt, int kt) {
+  return (size_t)nt * 8 * (kt * 16 + 8) * 2 + (size_t)nt * 8 * kTileLd * 4 + 64 * 4 + 128 * 4;
+}
+
+Q3T_DEV void store_bf16x4(uint16_t *dst, float a, float b, float c, float d) {
+  uint2 p;
+  p.x = pack_bf16x2(a, b);
+  p.y = pack_bf16x2(c, d);
+  *reinterpret_cast<uint2 *>(dst) = p;
+}
+
+// rows rg*128 + 4*lane .. +3 of token t (warp-wide: the norms reduce over the
+// warp); tm = {position, page} of t for GE_QKV
+Q3T_DEV void gemm_epilogue(const GemmArgs &a, int t, int rg, int lane, float4 v, const int *tm) {
+  const int n = rg * 128 + lane * 4;
+  if (a.epi == GE_F32) {
+    *reinterpret_cast<float4 *>(a.y + (size_t)t * a.ldy + n) = v;
+  } else if (a.epi == GE_RESID) {
+    float4 *xp = reinterpret_cast<float4 *>(a.y + (size_t)t * a.ldy + n);
+    float4 x = *xp;
+    x.x += v.x;
+    x.y += v.y;
+    x.z += v.z;
+    x.w += v.w;
+    *xp = x;
+    const float ss = warp_sum(x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w);
+    if (lane == 0) a.ss_out[(size_t)rg * a.ss_ld + t] = ss;
+  } else if (a.epi == GE_SILU) {
+    const float ux = __shfl_xor_sync(0xffffffffu, v.x, 16), uy = __shfl_xor_sync(0xffffffffu, v.y, 16);
+    const float uz = __shfl_xor_sync(0xffffffffu, v.z, 16), uw = __shfl_xor_sync(0xffffffffu, v.w, 16);
+    if (lane < 16)
+      store_bf16x4(a.h + (size_t)t * a.ldh + rg * 64 + lane * 4, silu(v.x) * ux, silu(v.y) * uy, silu(v.z) * uz,
+                   silu(v.w) * uw);
+  } else {  // GE_QKV: row block rg = q head rg | k head rg - nh | v head rg - nh - nkv
+    const int pos = tm[0];
+    float o[4];
+    if (rg < a.nh) {
+      norm_rope_lane(v, a.q_norm, a.eps, lane, pos, a.inv_freq, o);
+      store_bf16x4(a.q + (size_t)t * a.nh * 128 + rg * 128 + lane * 4, o[0], o[1], o[2], o[3]);
+      return;
+    }
+    const int h = rg < a.nh + a.nkv ? rg - a.nh : rg - a.nh - a.nkv;
+    const size_t e = a.layer * a.kv.layer_stride + (((size_t)tm[1] * a.kv.n_kv + h) * 16 + (pos & 15)) * 128 + lane * 4;
+    if (rg < a.nh + a.nkv) {
+      norm_rope_lane(v, a.k_norm, a.eps, lane, pos, a.inv_freq, o);
+      store_bf16x4(a.kv.k + e, o[0], o[1], o[2], o[3]);
+    } else {
+      store_bf16x4(a.kv.v + e, v.x, v.y, v.z, v.w);
+    }
+  }
+}
+
+template <int NT, int KTM>
+__global__ void __launch_bounds__(256, KTM > 16 ? 1 : 2) k_gemm(GemmArgs a) {
+  extern __shared__ __align__(16) unsigned char gsm[];
+  const int cs = a.cs, ks = blockIdx.x % cs, rg = blockIdx.x / cs;
+  const int tok0 = blockIdx.y * (NT * 8);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KT = (a.K >> 4) / cs, KC = KT * 16, ldx = KC + 8;
+  uint16_t *xs = reinterpret_cast<uint16_t *>(gsm);
+  float *tile = reinterpret_cast<float *>(gsm + (size_t)NT * 8 * ldx * 2);
+  float *rms = tile + NT * 8 * kTileLd;
+  int *meta = reinterpret_cast<int *>(rms + 64);
+  const uint4 *wp = a.W + ((size_t)(rg * 8 + warp) * (a.K >> 4) + (size_t)ks * KT) * 32 + lane;
+  uint4 frag[KTM];
+#pragma unroll
+  for (int i = 0; i < KTM; i++)
+    if (i < KT) frag[i] = ldg_stream(wp + i * 32);
   pdl_wait();
-  d_linear_compute<NT, FR>(a, item, frag, xs);
   pdl_launch();
+  int ntok = *a.ntok - tok0;
+  ntok = ntok < 0 ? 0 : (ntok > NT * 8 ? NT * 8 : ntok);
+  const int k0 = ks * KC;
+  const int ts = (NT * 8 + cs - 1) / cs, t_lo = ks * ts, t_hi = min(t_lo + ts, ntok);
+  if (a.epi == GE_QKV && (int)threadIdx.x < t_hi - t_lo) {
+    // cache position and page of this CTA's epilogue tokens (loads overlap the GEMM)
+    const int t = tok0 + t_lo + threadIdx.x;
+    const int pos = a.tv.pos[t] + a.tv.pos_add;
+    meta[2 * threadIdx.x] = pos;
+    meta[2 * threadIdx.x + 1] = a.kv.page_table[(size_t)a.tv.seq[t] * a.kv.pt_stride + (pos >> 4)];
+  }
+  if (a.xmode == GX_NORM) {
+    for (int r = threadIdx.x; r < ntok; r += blockDim.x) {
+      const float *sp = a.ss + (size_t)(tok0 + r) * a.xrow_mul + a.xrow_add;
+      float p[kMaxNss];
+#pragma unroll
+      for (int i = 0; i < kMaxNss; i++) p[i] = i < a.nss ? sp[(size_t)i * a.ss_ld] : 0.f;
+      float s = p[0];
+#pragma unroll
+      for (int i = 1; i < kMaxNss; i++) s += p[i];
+      rms[r] = 1.f / sqrtf(s / (float)a.K + a.eps);
+    }
+    __syncthreads();
+  }
+  // stage X[tok0 .. tok0 + 8NT)[k0 .. k0 + KC) as bf16; rows >= ntok are zero
+  const int c8n = KC >> 3;
+  if (a.xmode == GX_BF16) {
+    for (int idx = threadIdx.x; idx < NT * 8 * c8n; idx += blockDim.x) {
+      const int r = idx / c8n, c8 = (idx - r * c8n) * 8;
+      const int rr = r < ntok ? r : 0;
+      cp_async16(xs + r * ldx + c8, a.xb + (size_t)(tok0 + rr) * a.ldx + k0 + c8, r < ntok ? 16 : 0);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+  } else {
+    // a thread keeps one 8-column group (gamma in registers) and walks rows
+    // four at a time with all loads of a batch in flight together
+    const int rstep = blockDim.x / c8n;  // c8n divides 256 (KC is 128 or 256 here)
+    const int c8 = (threadIdx.x % c8n) * 8, r0 = threadIdx.x / c8n;
+    if (r0 < rstep) {
+      const float4 g0 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8);
+      const float4 g1 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8 + 4);
+      for (int rb = r0; rb < NT * 8; rb += 4 * rstep) {
+        float4 xv[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const int r = rb + i * rstep;
+          if (r < ntok) {
+            const float *xr = a.x + (size_t)((tok0 + r) * a.xrow_mul + a.xrow_add) * a.ldx + k0 + c8;
+            xv[i][0] = *reinterpret_cast<const float4 *>(xr);
+            xv[i][1] = *reinterpret_cast<const float4 *>(xr + 4);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const int r = rb + i * rstep;
+          if (r >= NT * 8) break;
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (r < ntok) {
+            const float d = rms[r];  // 1 / rms
+            v.x = pack_bf16x2(xv[i][0].x * d * g0.x, xv[i][0].y * d * g0.y);
+            v.y = pack_bf16x2(xv[i][0].z * d * g0.z, xv[i][0].w * d * g0.w);
+            v.z = pack_bf16x2(xv[i][1].x * d * g1.x, xv[i][1].y * d * g1.y);
+            v.w = pack_bf16x2(xv[i][1].z * d * g1.z, xv[i][1].w * d * g1.w);
+          }
+          *reinterpret_cast<uint4 *>(xs + r * ldx + c8) = v;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  float acc[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int i = 0; i < KTM; i++) {
+    if (i < KT) {
+#pragma unroll
+      for (int j = 0; j < NT; j++) {
+        const uint16_t *xr = xs + (j * 8 + g) * ldx + i * 16 + 2 * t;
+        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xr);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xr + 8);
+        mma_16816(acc[j], frag[i].x, frag[i].y, frag[i].z, frag[i].w, b0, b1);
+      }
+    }
+  }
+  const int row = warp * 16 + g;
+#pragma unroll
+  for (int j = 0; j < NT; j++) {
+    const int tk = j * 8 + 2 * t;
+    tile[tk * kTileLd + row] = acc[j][0];
+    tile[(tk + 1) * kTileLd + row] = acc[j][1];
+    tile[tk * kTileLd + row + 8] = acc[j][2];
+    tile[(tk + 1) * kTileLd + row + 8] = acc[j][3];
+  }
+  if (cs > 1)
+    cluster_sync();
+  else
+    __syncthreads();
+  for (int tt = t_lo + warp; tt < t_hi; tt += 8) {
+    const float *src = tile + tt * kTileLd + 4 * lane;
+    float4 v;
+    if (cs == 1) {
+      v = *reinterpret_cast<const float4 *>(src);
+    } else {  // all remote loads in flight, then the sum in rank order
+      float4 p[8];
+#pragma unroll
+      for (int c = 0; c < 8; c++)
+        if (c < cs) p[c] = ld_cluster_f4(src, (uint32_t)c);
+      v = p[0];
+#pragma unroll
+      for (int c = 1; c < 8; c++)
+        if (c < cs) {
+          v.x += p[c].x;
+          v.y += p[c].y;
+          v.z += p[c].z;
+          v.w += p[c].w;
+        }
+    }
+    gemm_epilogue(a, tok0 + tt, rg, lane, v, meta + 2 * (tt - t_lo));
+  }
+  if (cs > 1) cluster_sync();  // no CTA leaves while another still reads its tile
 }
 
-static size_t lin_smem(int nt, int fr) { return (size_t)nt * 8 * (16 * fr + 8) * 2; }
-
-__host__ __device__ int linear_items(const LinArgs &a) {
-  return (a.N / (16 * kLinWarps)) * (a.K / (16 * a.fr)) * a.ntc;
-}
-
-LinArgs linear_plan(const uint16_t *Wp, int N, int K, const void *X, int ldx, float *ws, long long ws_elems,
-                    int rows_cap, const int *ntok, int max_tok, int target_items, Part *out) {
-  LinArgs a{};
+GemmArgs gemm_args(const uint16_t *Wp, int N, int K, const int *ntok, int max_tok) {
+  GemmArgs a{};
   a.W = reinterpret_cast<const uint4 *>(Wp);
   a.N = N;
   a.K = K;
-  a.X = reinterpret_cast<const uint16_t *>(X);
-  a.ldx = ldx;
   a.ntok = ntok;
   const int per = max_tok < 64 ? max_tok : 64;
   a.nt = per <= 8 ? 1 : (per <= 16 ? 2 : (per <= 32 ? 4 : 8));
-  a.ntc = (max_tok + 63) / 64;
-  // the largest K chunk whose item count still reaches the target
-  const int rows = N / (16 * kLinWarps);
-  int fr = 16;
-  while (fr > 4 && (K % (16 * fr) != 0 || (long)rows * (K / (16 * fr)) < target_items)) fr >>= 1;
-  a.fr = fr;
-  a.P = ws;
-  a.pstride = (long long)rows_cap * N;
-  a.ldy = N;
-  Part P{ws, K / (16 * fr), a.pstride, N};
-  if (N % (16 * kLinWarps) || K % 64 || (long long)P.splits * P.stride > ws_elems || max_tok > rows_cap)
-    note(cudaErrorInvalidValue, "linear: shape or workspace");
-  if (out) *out = P;
+  // smallest cluster that gives >= 128 CTAs (at most 8), then enough splits
+  // that a warp holds at most 24 fragments
+  const int groups = N / 128, kt = K / 16;
+  int cs = 1;
+  while (cs < 8 && groups * cs < 128 && kt % (2 * cs) == 0) cs *= 2;
+  while (cs < 8 && kt / cs > 24 && kt % (2 * cs) == 0) cs *= 2;
+  a.cs = cs;
+  a.ldx = K;
+  a.xrow_mul = 1;
+  a.nss = 0;
   return a;
 }
 
+template <int NT, int KTM>
+static void gemm_launch(const GemmArgs &a, dim3 grid, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = gemm_smem(NT, (a.K >> 4) / a.cs);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = a.cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_use_pdl ? 2 : 1;
+  note(cudaLaunchKernelEx(&cfg, k_gemm<NT, KTM>, a), "k_gemm");
+  g_launches++;
+}
+
 template <int NT>
-static void linear_nt(const LinArgs &a, cudaStream_t st) {
-  const dim3 grid(linear_items(a));
-  const size_t sm = lin_smem(NT, a.fr);
-  if (a.fr == 16)
-    launch(k_linear<NT, 16>, grid, dim3(kLinWarps * 32), sm, st, a);
-  else if (a.fr == 8)
-    launch(k_linear<NT, 8>, grid, dim3(kLinWarps * 32), sm, st, a);
+static void gemm_nt(const GemmArgs &a, dim3 grid, cudaStream_t st) {
+  const int kt = (a.K >> 4) / a.cs;
+  if (kt <= 8)
+    gemm_launch<NT, 8>(a, grid, st);
+  else if (kt <= 16)
+    gemm_launch<NT, 16>(a, grid, st);
   else
-    launch(k_linear<NT, 4>, grid, dim3(kLinWarps * 32), sm, st, a);
+    gemm_launch<NT, 24>(a, grid, st);
 }
 
-Part linear(const uint16_t *Wp, int N, int K, const void *X, int ldx, float *ws, long long ws_elems, int rows_cap,
-            const int *ntok, int max_tok, cudaStream_t st) {
-  Part P;
-  const LinArgs a = linear_plan(Wp, N, K, X, ldx, ws, ws_elems, rows_cap, ntok, max_tok, 148, &P);
-  switch (a.nt) {
-    case 1: linear_nt<1>(a, st); break;
-    case 2: linear_nt<2>(a, st); break;
-    case 4: linear_nt<4>(a, st); break;
-    default: linear_nt<8>(a, st); break;
+void gemm(const GemmArgs &a, int max_tok, cudaStream_t st) {
+  const int kt = a.K / 16;
+  if (a.N % 128 || a.K % 128 || a.cs < 1 || a.cs > 8 || kt % a.cs || kt / a.cs > 24 || max_tok < 1 ||
+      (a.epi == GE_SILU && a.h == nullptr) ||
+      (a.xmode == GX_NORM && (a.x == nullptr || a.ss == nullptr || 256 % (2 * (kt / a.cs)) != 0 ||
+                              a.nss > kMaxNss))) {
+    note(cudaErrorInvalidValue, "k_gemm (shape / arguments)");
+    return;
   }
-  return P;
+  const dim3 grid((a.N / 128) * a.cs, (max_tok + a.nt * 8 - 1) / (a.nt * 8));
+  switch (a.nt) {
+    case 1: gemm_nt<1>(a, grid, st); break;
+    case 2: gemm_nt<2>(a, grid, st); break;
+    case 4: gemm_nt<4>(a, grid, st); break;
+    default: gemm_nt<8>(a, grid, st); break;
+  }
 }
 
-__global__ void __launch_bounds__(256) k_reduce_rows(Part P, int N, const int *ntok, float *out) {
-  pdl_wait();
-  const int t = blockIdx.y;
-  if (t < *ntok)
-    for (int n = (blockIdx.x * blockDim.x + threadIdx.x) * 4; n < N; n += gridDim.x * blockDim.x * 4)
-      *reinterpret_cast<float4 *>(out + (size_t)t * N + n) = part4(P, t, n);
-  pdl_launch();
+template <int NT, int KTM>
+static void gemm_attr() {
+  cudaFuncSetAttribute(k_gemm<NT, KTM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem(NT, KTM));
 }
-
-void reduce_rows(Part P, int N, const int *ntok, int max_tok, float *out, cudaStream_t st) {
-  launch(k_reduce_rows, dim3((N / 4 + 255) / 256, max_tok), dim3(256), 0, st, P, N, ntok, out);
-}
-
-__global__ void __launch_bounds__(256) k_silu_mul(SiluArgs a) {
-  pdl_wait();
-  d_silu(a, blockIdx.y, (blockIdx.x * blockDim.x + threadIdx.x) * 4);
-  pdl_launch();
-}
-
-void silu_mul(Part gu, int I, const int *ntok, int max_tok, uint16_t *out, cudaStream_t st) {
-  SiluArgs a{gu, I, ntok, out};
-  launch(k_silu_mul, dim3((I / 4 + 255) / 256, max_tok), dim3(256), 0, st, a);
-}
-
-__global__ void __launch_bounds__(1024) k_qkv_post(QkvArgs a) {
-  pdl_wait();
-  d_qkv_post(a, blockIdx.x);
-  pdl_launch();
-}
-
-void qkv_post(Part qkv, const float *q_norm, const float *k_norm, const float *inv_freq, float eps, int nh, int nkv,
-              TokView tv, int max_tok, uint16_t *qout, KVView kv, int layer, cudaStream_t st) {
-  QkvArgs a{qkv, q_norm, k_norm, inv_freq, eps, nh, nkv, tv, qout, kv, layer};
-  launch(k_qkv_post, dim3(max_tok), dim3(32 * (nh + 2 * nkv)), 0, st, a);
+template <int NT>
+static void gemm_attrs() {
+  gemm_attr<NT, 8>();
+  gemm_attr<NT, 16>();
+  gemm_attr<NT, 24>();
 }
 
 struct BlockSync {
   __device__ void operator()() const { __syncthreads(); }
 };
 
-__global__ void __launch_bounds__(128) k_attn(AttnArgs a) {
+__global__ void __launch_bounds__(128, 2) k_attn(AttnArgs a) {
   __shared__ AttnSmem S;
+  extern __shared__ __align__(16) uint16_t attn_ring[];
   pdl_wait();
-  d_attn(a, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, S, BlockSync{});
   pdl_launch();
+  d_attn(a, threadIdx.x, blockIdx.x * kAttnWarps, gridDim.x * kAttnWarps, S, attn_ring, BlockSync{});
 }
 
-static AttnArgs attn_args(int fused, Part qkv, const float *q_norm, const float *k_norm, const float *inv_freq,
-                          float eps, const uint16_t *qin, KVView kv, int layer, TokView tv, int nh, int chunk,
-                          int max_split, AttnWork ws, uint16_t *out) {
+static int g_attn_grid = 0;
+
+// grid of k_attn: enough CTAs for max_tok * n_kv * max_units units, at most
+// the resident CTAs of the whole GPU (the warps loop over the units)
+static int attn_grid(const AttnArgs &a, int max_tok) {
+  if (g_attn_grid == 0) {
+    int dev = 0, sms = 0, occ = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_attn, 128, kAttnDynSmem);
+    g_attn_grid = sms * (occ < 1 ? 1 : occ);
+  }
+  const long long units = (long long)max_tok * a.kv.n_kv * a.max_units;
+  const long long need = (units + kAttnWarps - 1) / kAttnWarps;
+  return (int)(need < g_attn_grid ? (need < 1 ? 1 : need) : g_attn_grid);
+}
+
+static void attention_launch(const AttnArgs &a, int max_tok, cudaStream_t st) {
+  if (max_tok > kAttnMaxTok || a.pw < 1 || a.max_units < 1 || a.max_units > kAttnMaxUnits) {
+    note(cudaErrorInvalidValue, "k_attn (max_tok / pw / max_units out of range)");
+    return;
+  }
+  launch(k_attn, dim3(attn_grid(a, max_tok)), dim3(128), kAttnDynSmem, st, a);
+}
+
+void attention(const uint16_t *q, KVView kv, int layer, TokView tv, int max_tok, int nh, int pw, int max_units,
+               AttnWork ws, uint16_t *out, cudaStream_t st) {
   AttnArgs a{};
-  a.qkv = qkv;
-  a.q_norm = q_norm;
-  a.k_norm = k_norm;
-  a.inv_freq = inv_freq;
-  a.eps = eps;
-  a.qin = qin;
+  a.q = q;
   a.kv = kv;
   a.layer = layer;
   a.tv = tv;
   a.nh = nh;
-  a.chunk = chunk;
-  a.max_split = max_split;
-  a.fused = fused;
+  a.pw = pw;
+  a.max_units = max_units;
   a.scale = 1.0f / sqrtf(128.0f);
   a.ws = ws;
   a.out = out;
-  return a;
-}
-
-void attention(int fused, Part qkv, const float *q_norm, const float *k_norm, const float *inv_freq, float eps,
-               const uint16_t *qin, KVView kv, int layer, TokView tv, int max_tok, int nh, int chunk, int max_split,
-               AttnWork ws, uint16_t *out, cudaStream_t st) {
-  const AttnArgs a =
-      attn_args(fused, qkv, q_norm, k_norm, inv_freq, eps, qin, kv, layer, tv, nh, chunk, max_split, ws, out);
-  launch(k_attn, dim3(max_split, kv.n_kv, max_tok), dim3(128), 0, st, a);
+  attention_launch(a, max_tok, st);
 }
 
 constexpr int kSampleThreads = 512;
@@ -296,8 +491,8 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a) {
   __shared__ float rv[32];
   __shared__ int ri[32];
   pdl_wait();
-  d_sample(a, blockIdx.x, smem_f, smem_f + kSampleMaxV, reinterpret_cast<int *>(smem_f + 2 * kSampleMaxV), rv, ri);
   pdl_launch();
+  d_sample(a, blockIdx.x, smem_f, smem_f + kSampleMaxV, reinterpret_cast<int *>(smem_f + 2 * kSampleMaxV), rv, ri);
 }
 
 void sample(const SampleArgs &a, int max_tok, cudaStream_t st) {
@@ -321,220 +516,29 @@ void kv_import(const uint16_t *k, const uint16_t *v, int layers, int len, KVView
   g_launches++;
 }
 
-// ---------------------------------------------------------------------------
-// persistent frame kernel
-// ---------------------------------------------------------------------------
-constexpr int kFrameThreads = 256;
-constexpr int kBarrierGroups = 16;
-constexpr unsigned kSpinLimit = 1u << 22;  // ~2-3 s of polling (each poll is an L2 round trip)
-// dynamic shared memory: the sampler's arrays (48 KB) cover the GEMM X tile
-// (<= 64 x 264 bf16 = 33.8 KB) and two attention groups
-constexpr size_t kFrameSmem = kSampleSmem;
-
-struct FrameShared {
-  Phase ph;
-  float red[33];
-  float rv[32];
-  int ri[32];
-  int abort;
-};
-
-// Grid barrier k (1-based) over all CTAs: arrival on one of 16 group
-// counters (128 B apart), the last arrival of a group bumps the top counter;
-// CTAs wait for top == k * 16.  Every wait is bounded: after kSpinLimit polls
-// the CTA sets *err, and all CTAs leave at the next phase boundary.
-__device__ bool grid_barrier(const FrameCtl &c, unsigned k, FrameShared &sh) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned grp = blockIdx.x % kBarrierGroups;
-    const unsigned gsize = gridDim.x / kBarrierGroups + (grp < gridDim.x % kBarrierGroups ? 1u : 0u);
-    const unsigned old = atomicAdd(&c.ctr[(1 + grp) * 32], 1u);
-    if (old + 1 == k * gsize) atomicAdd(&c.ctr[0], 1u);
-    unsigned spins = 0;
-    int abort = 0;
-    while (true) {
-      unsigned v;
-      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c.ctr) : "memory");
-      if (v >= k * kBarrierGroups) break;
-      if (*(volatile int *)c.err) {
-        abort = 1;
-        break;
-      }
-      if (++spins > kSpinLimit) {
-        atomicExch(c.err, 1);
-        abort = 1;
-        break;
-      }
-      __nanosleep(32);
-    }
-    __threadfence();
-    sh.abort = abort;
-  }
-  __syncthreads();
-  return sh.abort == 0;
-}
-
-template <int FR>
-__device__ __forceinline__ void frame_gemm(const LinArgs &a, uint4 (&pre)[16], bool have_pre, uint16_t *xs) {
-  const int n = linear_items(a);
-  for (int item = blockIdx.x; item < n; item += gridDim.x) {
-    if (!(item == (int)blockIdx.x && have_pre)) d_linear_load<FR>(a, item, pre);
-    switch (a.nt) {
-      case 1: d_linear_compute<1, FR>(a, item, pre, xs); break;
-      case 2: d_linear_compute<2, FR>(a, item, pre, xs); break;
-      case 4: d_linear_compute<4, FR>(a, item, pre, xs); break;
-      default: d_linear_compute<8, FR>(a, item, pre, xs); break;
-    }
-  }
-}
-
-struct HalfSync {
-  int id;
-  __device__ void operator()() const { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
-};
-
-__global__ void __launch_bounds__(kFrameThreads, 2) k_frame(const Phase *phases, int n_phases, FrameCtl ctl) {
-  extern __shared__ __align__(16) float fsm[];
-  __shared__ FrameShared sh;
-  uint4 pre[16];
-  for (int i = 0; i < n_phases; i++) {
-    // load the phase descriptor
-    for (int w = threadIdx.x; w < (int)(sizeof(Phase) / 4); w += blockDim.x)
-      reinterpret_cast<int *>(&sh.ph)[w] = reinterpret_cast<const int *>(&phases[i])[w];
-    __syncthreads();
-    const Phase &ph = sh.ph;
-    // a GEMM phase streams its first item's weights before the barrier
-    bool have_pre = false;
-    if (ph.type == PH_GEMM && (int)blockIdx.x < linear_items(ph.lin)) {
-      if (ph.lin.fr == 16)
-        d_linear_load<16>(ph.lin, blockIdx.x, pre);
-      else if (ph.lin.fr == 8)
-        d_linear_load<8>(ph.lin, blockIdx.x, pre);
-      else
-        d_linear_load<4>(ph.lin, blockIdx.x, pre);
-      have_pre = true;
-    }
-    if (i > 0 && !grid_barrier(ctl, (unsigned)i, sh)) return;
-    if (ctl.t && blockIdx.x == 0 && threadIdx.x == 0) {
-      unsigned long long now;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-      ctl.t[i] = now;
-    }
-    switch (ph.type) {
-      case PH_NORM:
-        for (int t = blockIdx.x; t < ph.max_tok; t += gridDim.x) d_rmsnorm(ph.norm, t, sh.red);
-        break;
-      case PH_GEMM: {
-        uint16_t *xs = reinterpret_cast<uint16_t *>(fsm);
-        if (ph.lin.fr == 16)
-          frame_gemm<16>(ph.lin, pre, have_pre, xs);
-        else if (ph.lin.fr == 8)
-          frame_gemm<8>(ph.lin, pre, have_pre, xs);
-        else
-          frame_gemm<4>(ph.lin, pre, have_pre, xs);
-        break;
-      }
-      case PH_QKV:
-        for (int t = blockIdx.x; t < ph.max_tok; t += gridDim.x) d_qkv_post(ph.qkv, t);
-        break;
-      case PH_ATTN: {
-        // two independent 128-thread groups per CTA, one item each
-        const int half = threadIdx.x >> 7;
-        AttnSmem *S = reinterpret_cast<AttnSmem *>(fsm) + half;
-        const int nkv = ph.attn.kv.n_kv, ms = ph.attn.max_split;
-        const int n_items = ph.max_tok * nkv * ms;
-        for (int base = 2 * blockIdx.x; base < n_items; base += 2 * gridDim.x) {
-          const int item = base + half;
-          if (item < n_items) {
-            const int sp = item % ms, g = (item / ms) % nkv, t = item / (ms * nkv);
-            d_attn(ph.attn, sp, g, t, threadIdx.x & 127, *S, HalfSync{1 + half});
-          }
-        }
-        break;
-      }
-      case PH_SILU: {
-        const int chunks = (ph.silu.I / 4 + kFrameThreads - 1) / kFrameThreads;
-        for (int item = blockIdx.x; item < ph.max_tok * chunks; item += gridDim.x)
-          d_silu(ph.silu, item / chunks, ((item % chunks) * kFrameThreads + threadIdx.x) * 4);
-        break;
-      }
-      case PH_SAMPLE:
-        for (int t = blockIdx.x; t < ph.max_tok; t += gridDim.x) {
-          d_sample(ph.smp, t, fsm, fsm + kSampleMaxV, reinterpret_cast<int *>(fsm + 2 * kSampleMaxV), sh.rv, sh.ri);
-          if (ph.has_tail) d_rmsnorm(ph.tail, t, sh.red);
-        }
-        break;
-      default:
-        break;
-    }
-    __syncthreads();
-  }
-  if (ctl.t && grid_barrier(ctl, (unsigned)n_phases, sh) && blockIdx.x == 0 && threadIdx.x == 0) {
-    unsigned long long now;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-    ctl.t[n_phases] = now;
-  }
-}
-
-static int g_frame_grid = 0;
-
-int frame_grid() {
-  if (g_frame_grid == 0) {
-    int dev = 0, sms = 0, occ = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_frame, kFrameThreads, kFrameSmem);
-    g_frame_grid = sms * (occ < 2 ? (occ < 1 ? 1 : occ) : 2);
-  }
-  return g_frame_grid;
-}
-
-int frame_target_items() { return frame_grid(); }
-
-void frame_launch(const Phase *d_phases, int n_phases, FrameCtl ctl, cudaStream_t st) {
-  note(cudaMemsetAsync(ctl.ctr, 0, kFrameCtrWords * sizeof(unsigned), st), "frame barrier reset");
-  const int grid = frame_grid();
-  void *args[] = {(void *)&d_phases, (void *)&n_phases, (void *)&ctl};
-  note(cudaLaunchCooperativeKernel((const void *)k_frame, dim3(grid), dim3(kFrameThreads), args, kFrameSmem, st),
-       "k_frame (cooperative)");
-  g_launches++;
-}
-
 void run_phases(const Phase *ph, int n, cudaStream_t st) {
   for (int i = 0; i < n; i++) {
     const Phase &p = ph[i];
     switch (p.type) {
       case PH_NORM: rmsnorm(p.norm, p.max_tok, st); break;
-      case PH_GEMM:
-        switch (p.lin.nt) {
-          case 1: linear_nt<1>(p.lin, st); break;
-          case 2: linear_nt<2>(p.lin, st); break;
-          case 4: linear_nt<4>(p.lin, st); break;
-          default: linear_nt<8>(p.lin, st); break;
-        }
-        break;
-      case PH_QKV:
-        launch(k_qkv_post, dim3(p.max_tok), dim3(32 * (p.qkv.nh + 2 * p.qkv.nkv)), 0, st, p.qkv);
-        break;
-      case PH_ATTN:
-        launch(k_attn, dim3(p.attn.max_split, p.attn.kv.n_kv, p.max_tok), dim3(128), 0, st, p.attn);
-        break;
-      case PH_SILU:
-        launch(k_silu_mul, dim3((p.silu.I / 4 + 255) / 256, p.max_tok), dim3(256), 0, st, p.silu);
-        break;
+      case PH_GEMM: gemm(p.gemm, p.max_tok, st); break;
+      case PH_ATTN: attention_launch(p.attn, p.max_tok, st); break;
       case PH_SAMPLE:
         sample(p.smp, p.max_tok, st);
         if (p.has_tail) rmsnorm(p.tail, p.max_tok, st);
         break;
-      default: break;
+      default: note(cudaErrorInvalidValue, "run_phases: unknown phase"); break;
     }
   }
 }
 
 void init_kernel_attributes() {
   cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSampleSmem);
-  cudaFuncSetAttribute(k_frame, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFrameSmem);
+  cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnDynSmem);
+  gemm_attrs<1>();
+  gemm_attrs<2>();
+  gemm_attrs<4>();
+  gemm_attrs<8>();
   const char *e = getenv("Q3T_PDL");
   if (e && e[0] == '0') g_use_pdl = false;
 }

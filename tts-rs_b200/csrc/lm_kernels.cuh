@@ -26,10 +26,14 @@ struct TokView {
   int pos_add;         // added to pos[] (code-predictor passes use pos[] = 0)
 };
 
+// Attention work units: a warp handles up to `pw` pages of one (token, kv
+// head); a (token, head) has at most kAttnMaxUnits units.
+constexpr int kAttnMaxUnits = 64;
+constexpr int kAttnMaxTok = 128;  // tokens per attention launch
+
 struct AttnWork {
-  float *part;    // [max_tok][n_kv][max_split][2][132]
+  float *part;    // [max_tok][n_kv][kAttnMaxUnits][2][132] unit partials (o, m, l)
   int *counters;  // [max_tok][n_kv], zero between launches
-  int max_split;
 };
 
 // Split-K partial sums of one linear's output: value(t, n) =
@@ -96,77 +100,73 @@ void rmsnorm(float *x, int ldx, int row_mul, int row_add, Part add, const float 
              int ldo, int H, float eps, const int *ntok, int grid_rows, float *out_f32, const int *slot,
              cudaStream_t st);
 
-struct LinArgs {
-  const uint4 *W;  // fragment-packed weights
-  int N, K, fr, nt; // fragments per warp (K chunk = 16 fr), token tiles of 8
-  const uint16_t *X;
-  int ldx;
-  float *P;
-  long long pstride;
-  int ldy;
-  const int *ntok;
-  int ntc;          // token chunks of 64
-};
-// Plans a linear: split count (fr), token tiles and the partial layout.
-LinArgs linear_plan(const uint16_t *Wp, int N, int K, const void *X, int ldx, float *ws, long long ws_elems,
-                    int rows_cap, const int *ntok, int max_tok, int target_items, Part *out);
-__host__ __device__ int linear_items(const LinArgs &a);
-
-// Y = X . W^T for t < ntok: writes split-K partials into ws (capacity
-// ws_elems floats, rows_cap token rows per split) and returns their layout.
-Part linear(const uint16_t *Wp, int N, int K, const void *X, int ldx, float *ws, long long ws_elems,
-            int rows_cap, const int *ntok, int max_tok, cudaStream_t st);
-
-struct SiluArgs {
-  Part gu;
-  int I;
-  const int *ntok;
-  uint16_t *out;
+// ---------------------------------------------------------------------------
+// Skinny GEMM Y[t][n] = X[t] . W[n] for up to 64 tokens per CTA tile, as
+// thread-block clusters: the cs CTAs of a cluster share one 128-row output
+// block and split K; their f32 tiles are summed through distributed shared
+// memory in cluster-rank order (deterministic), and the epilogue runs on the
+// reduced rows.  X is bf16 rows, or f32 residual rows normalised on the fly
+// (RMSNorm from sum-of-squares partials).
+// ---------------------------------------------------------------------------
+enum GemmX { GX_BF16 = 0, GX_NORM = 1 };
+enum GemmEpi {
+  GE_F32 = 0,    // y[t][n] = acc
+  GE_QKV = 1,    // q/k RMSNorm + RoPE; q -> bf16 q[t], k / v appended to the paged cache
+  GE_RESID = 2,  // y[t][n] += acc (residual stream), ss_out[n / 128][t] = sum of squares of the new rows
+  GE_SILU = 3,   // row block r = [gate 64r..64r+63 | up 64r..64r+63]: h[t][64r + i] = bf16(silu(g) * u)
 };
 
-struct QkvArgs {
-  Part qkv;
-  const float *q_norm, *k_norm, *inv_freq;
+struct GemmArgs {
+  const uint4 *W;      // fragment-packed weights [N/16][K/16] (pack_weight)
+  int N, K;
+  int cs;              // cluster size = K splits (1, 2, 4 or 8)
+  int nt;              // 8-token MMA tiles per CTA (1, 2, 4 or 8)
+  const int *ntok;     // token count (device)
+  int xmode;
+  const uint16_t *xb;  // GX_BF16: X[t][ldx]
+  const float *x;      // GX_NORM: row t is x[t * xrow_mul + xrow_add][0..K)
+  int ldx, xrow_mul, xrow_add;
+  const float *ss;     // GX_NORM: sum of squares of row r = sum_i ss[i * ss_ld + r], i < nss
+  int nss, ss_ld;
+  const float *gamma;  // GX_NORM: RMSNorm weight [K]
   float eps;
+  int epi;
+  float *y;            // GE_F32 output / GE_RESID residual, [t][ldy]
+  int ldy;
+  float *ss_out;       // GE_RESID: [N / 128][ss_ld]
+  uint16_t *h;         // GE_SILU: [t][ldh]
+  int ldh;
+  const float *q_norm, *k_norm, *inv_freq;  // GE_QKV
   int nh, nkv;
   TokView tv;
-  uint16_t *qout;
+  uint16_t *q;         // GE_QKV: [t][nh * 128]
   KVView kv;
   int layer;
 };
 
+// Cluster size and token tiles for an N x K GEMM over up to max_tok tokens
+// (N % 128 == 0, K % 128 == 0); the caller fills X and the epilogue.
+GemmArgs gemm_args(const uint16_t *Wp, int N, int K, const int *ntok, int max_tok);
+void gemm(const GemmArgs &a, int max_tok, cudaStream_t st);
+
 struct AttnArgs {
-  Part qkv;
-  const float *q_norm, *k_norm, *inv_freq;
-  float eps;
-  const uint16_t *qin;
+  const uint16_t *q;  // [t][nh * 128] bf16, normed and rotated
   KVView kv;
   int layer;
   TokView tv;
-  int nh, chunk, max_split, fused;
+  int nh;
+  int pw;         // minimum pages per work unit (more when a sequence would need > kAttnMaxUnits)
+  int max_units;  // upper bound of units per (token, head): sizes the grid only
   float scale;
   AttnWork ws;
   uint16_t *out;
 };
 
-// out[t][n] = reduced partials, t < ntok
-void reduce_rows(Part P, int N, const int *ntok, int max_tok, float *out, cudaStream_t st);
-
-// out[t][i] = bf16(silu(g) * u) with g, u the reduced gate|up partials
-void silu_mul(Part gu, int I, const int *ntok, int max_tok, uint16_t *out, cudaStream_t st);
-
-// q/k RMSNorm + rotate-half RoPE + bf16 q out + K/V append into pages.
-void qkv_post(Part qkv, const float *q_norm, const float *k_norm,
-              const float *inv_freq, float eps, int nh, int nkv, TokView tv, int max_tok,
-              uint16_t *qout, KVView kv, int layer, cudaStream_t st);
-
-// Split-K flash-decoding over the paged cache, one token per (t): attends to
-// positions [0, pos]; fused=1 also does qkv_post for its own head group
-// (valid only when every token of the batch belongs to a distinct sequence).
-void attention(int fused, Part qkv, const float *q_norm, const float *k_norm,
-               const float *inv_freq, float eps, const uint16_t *qin, KVView kv, int layer,
-               TokView tv, int max_tok, int nh, int chunk, int max_split, AttnWork ws,
-               uint16_t *out, cudaStream_t st);
+// Split-K flash-decoding over the paged cache for every token t < ntok:
+// attends to positions [0, pos]; the token's own K/V are already appended.
+// pw / max_units: see AttnArgs; max_tok <= kAttnMaxTok.
+void attention(const uint16_t *q, KVView kv, int layer, TokView tv, int max_tok, int nh, int pw,
+               int max_units, AttnWork ws, uint16_t *out, cudaStream_t st);
 
 struct SampleParams {
   int do_sample;
@@ -216,11 +216,10 @@ struct SampleArgs {
 void sample(const SampleArgs &a, int max_tok, cudaStream_t st);
 
 // ---------------------------------------------------------------------------
-// Persistent frame kernel: one cooperative launch runs a whole decode frame
-// as a list of phases separated by grid barriers (bounded spins; on timeout
-// the kernel sets *err and every CTA returns).
+// A decode frame as a list of phases, each one kernel launch (captured once
+// into a CUDA graph and replayed).
 // ---------------------------------------------------------------------------
-enum PhaseType { PH_NORM = 1, PH_GEMM = 2, PH_QKV = 3, PH_ATTN = 4, PH_SILU = 5, PH_SAMPLE = 6 };
+enum PhaseType { PH_NORM = 1, PH_GEMM = 2, PH_ATTN = 3, PH_SAMPLE = 4 };
 
 struct Phase {
   int type;
@@ -229,27 +228,12 @@ struct Phase {
   int pad;
   union {
     RmsArgs norm;
-    LinArgs lin;
-    QkvArgs qkv;
+    GemmArgs gemm;
     AttnArgs attn;
-    SiluArgs silu;
     SampleArgs smp;
   };
   RmsArgs tail;
 };
-
-struct FrameCtl {
-  unsigned *ctr;          // barrier counters, kFrameCtrWords words, zeroed before each launch
-  int *err;               // set to 1 when a barrier wait times out
-  unsigned long long *t;  // optional [n_phases + 1] %globaltimer stamps at phase starts (CTA 0)
-};
-constexpr int kFrameCtrWords = 17 * 32;
-// grid size (CTAs) the frame kernel runs with on the current device
-int frame_grid();
-// items a GEMM phase should have so that every CTA holds at most one
-int frame_target_items();
-void frame_launch(const Phase *d_phases, int n_phases, FrameCtl ctl, cudaStream_t st);
-// the same phase list run as one standalone kernel launch per phase
 void run_phases(const Phase *phases, int n_phases, cudaStream_t st);
 
 // Scatter dense bf16 K/V [layers][n_kv][len][hd] into the pages of `seq`.
