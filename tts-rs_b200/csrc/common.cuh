@@ -71,6 +71,8 @@ Q3T_DEV float block_sum(float v, float *red) {
 
 Q3T_DEV float silu(float x) { return x / (1.f + expf(-x)); }
 
+Q3T_DEV uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
 // ---- asynchronous global -> shared copies (16 bytes; src_bytes < 16 zero-fills the rest) ----
 Q3T_DEV void cp_async16(void *smem, const void *gmem, int src_bytes) {
   const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
@@ -82,8 +84,15 @@ Q3T_DEV void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
+// Four 8x8 b16 matrices from shared memory, transposed (lanes 8i..8i+7 give
+// the row addresses of matrix i; register i receives matrix i).
+Q3T_DEV void ldmatrix_x4_trans(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_addr(p)));
+}
+
 // ---- thread-block clusters (distributed shared memory) ----
-Q3T_DEV uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 // 16-byte load from the shared memory of cluster CTA `rank` at the address
 // that p has in this CTA.

@@ -127,30 +127,46 @@ uint16_t *upload_bf16(const q3t_tensor *t, DevArena &ar, cudaStream_t st) {
   return to_dev_bf16(t, &ar, st);
 }
 
-// pack W [N][K] into dst (fragment order) at element offset
-static void pack_into(const q3t_tensor *t, uint16_t *dst, int N, int K, cudaStream_t st) {
-  if (N % 16 || K % 64) FAIL(Q3T_RUNTIME_LOAD, "linear %s: dims %d x %d not multiples of 16/64", t->name, N, K);
+// host tensor -> dst (bf16, n elements) on the device
+static void upload_into(const q3t_tensor *t, uint16_t *dst, cudaStream_t st) {
   uint16_t *tmp = to_dev_bf16(t, nullptr, st);
-  pack_weight(tmp, dst, N, K, st);
+  CK(cudaMemcpyAsync(dst, tmp, (size_t)numel(t) * 2, cudaMemcpyDeviceToDevice, st));
   CK(cudaStreamSynchronize(st));
   CK(cudaFree(tmp));
 }
 
+// a [N][K] bf16 weight at w with its TMA descriptor
+static Linear make_linear(const uint16_t *w, int N, int K, const char *name) {
+  if (N % 128 || K % 128) FAIL(Q3T_RUNTIME_LOAD, "linear %s: dims %d x %d not multiples of 128", name, N, K);
+  Linear L;
+  L.w = w;
+  L.N = N;
+  L.K = K;
+  if (!make_tmap_bf16(&L.tm, w, (uint64_t)K, (uint64_t)N, (uint64_t)K * 2, 64, 128))
+    FAIL(Q3T_RUNTIME_LOAD, "linear %s: TMA descriptor encoding failed", name);
+  return L;
+}
+
+static Linear load_linear(const q3t_tensor *t, int N, int K, DevArena &ar, cudaStream_t st) {
+  uint16_t *w = ar.alloc<uint16_t>((size_t)N * K);
+  upload_into(t, w, st);
+  return make_linear(w, N, K, t->name);
+}
+
 // gate [I][H] and up [I][H] -> one [2I][H] matrix whose 128-row blocks are
-// [gate rows 64r..64r+63 | up rows 64r..64r+63] (the GE_SILU epilogue pairs
-// them), fragment-packed into dst
-static void pack_gate_up(const q3t_tensor *gate, const q3t_tensor *up, uint16_t *dst, int I, int H, cudaStream_t st) {
-  if (I % 64 || H % 64) FAIL(Q3T_RUNTIME_LOAD, "gate/up: dims %d x %d not multiples of 64", I, H);
-  uint16_t *g = to_dev_bf16(gate, nullptr, st), *u = to_dev_bf16(up, nullptr, st), *gu;
-  CK(cudaMalloc(&gu, (size_t)2 * I * H * 2));
+// [gate rows 64r..64r+63 | up rows 64r..64r+63] (the GE_SILU epilogue pairs them)
+static Linear load_gate_up(const q3t_tensor *gate, const q3t_tensor *up, int I, int H, DevArena &ar,
+                           cudaStream_t st) {
+  if (I % 64) FAIL(Q3T_RUNTIME_LOAD, "gate/up: intermediate %d not a multiple of 64", I);
+  uint16_t *g = to_dev_bf16(gate, nullptr, st), *u = to_dev_bf16(up, nullptr, st);
+  uint16_t *gu = ar.alloc<uint16_t>((size_t)2 * I * H);
   const size_t blk = (size_t)64 * H * 2;  // bytes of 64 rows
   CK(cudaMemcpy2DAsync(gu, 2 * blk, g, blk, blk, I / 64, cudaMemcpyDeviceToDevice, st));
   CK(cudaMemcpy2DAsync(reinterpret_cast<char *>(gu) + blk, 2 * blk, u, blk, blk, I / 64, cudaMemcpyDeviceToDevice, st));
-  pack_weight(gu, dst, 2 * I, H, st);
   CK(cudaStreamSynchronize(st));
   CK(cudaFree(g));
   CK(cudaFree(u));
-  CK(cudaFree(gu));
+  return make_linear(gu, 2 * I, H, gate->name);
 }
 
 static void load_stack(q3t_model *m, LMStack &S, const q3t_lm_config &c, const std::string &prefix,
@@ -170,19 +186,14 @@ static void load_stack(q3t_model *m, LMStack &S, const q3t_lm_config &c, const s
     S.k_norm.push_back(upload_f32(T.get(p + ".self_attn.k_norm.weight", {hd}), ar, st));
     const int Nq = nh * hd, Nk = nkv * hd;
     uint16_t *qkv = ar.alloc<uint16_t>((size_t)(Nq + 2 * Nk) * H);
-    pack_into(T.get(p + ".self_attn.q_proj.weight", {Nq, H}), qkv, Nq, H, st);
-    pack_into(T.get(p + ".self_attn.k_proj.weight", {Nk, H}), qkv + (size_t)Nq * H, Nk, H, st);
-    pack_into(T.get(p + ".self_attn.v_proj.weight", {Nk, H}), qkv + (size_t)(Nq + Nk) * H, Nk, H, st);
-    S.wqkv.push_back(qkv);
-    uint16_t *wo = ar.alloc<uint16_t>((size_t)H * Nq);
-    pack_into(T.get(p + ".self_attn.o_proj.weight", {H, Nq}), wo, H, Nq, st);
-    S.wo.push_back(wo);
-    uint16_t *gu = ar.alloc<uint16_t>((size_t)2 * I * H);
-    pack_gate_up(T.get(p + ".mlp.gate_proj.weight", {I, H}), T.get(p + ".mlp.up_proj.weight", {I, H}), gu, I, H, st);
-    S.wgu.push_back(gu);
-    uint16_t *wd = ar.alloc<uint16_t>((size_t)H * I);
-    pack_into(T.get(p + ".mlp.down_proj.weight", {H, I}), wd, H, I, st);
-    S.wdown.push_back(wd);
+    upload_into(T.get(p + ".self_attn.q_proj.weight", {Nq, H}), qkv, st);
+    upload_into(T.get(p + ".self_attn.k_proj.weight", {Nk, H}), qkv + (size_t)Nq * H, st);
+    upload_into(T.get(p + ".self_attn.v_proj.weight", {Nk, H}), qkv + (size_t)(Nq + Nk) * H, st);
+    S.qkv.push_back(make_linear(qkv, Nq + 2 * Nk, H, "qkv_proj"));
+    S.o.push_back(load_linear(T.get(p + ".self_attn.o_proj.weight", {H, Nq}), H, Nq, ar, st));
+    S.gu.push_back(
+        load_gate_up(T.get(p + ".mlp.gate_proj.weight", {I, H}), T.get(p + ".mlp.up_proj.weight", {I, H}), I, H, ar, st));
+    S.down.push_back(load_linear(T.get(p + ".mlp.down_proj.weight", {H, I}), H, I, ar, st));
   }
   S.final_norm = upload_f32(T.get(prefix + ".norm.weight", {H}), ar, st);
   // rope.rs:21-24: inv_freq[i] = 1 / theta^(i / half), computed in f32 on the host
@@ -231,23 +242,20 @@ extern "C" q3t_status q3t_model_load(const q3t_model_desc *desc, q3t_model **out
       if (tc.predictor.hidden_size != tc.talker.hidden_size)
         FAIL(Q3T_INVALID_INPUT, "code predictor hidden %d != talker hidden %d (small_to_mtp_projection unsupported)",
              tc.predictor.hidden_size, tc.talker.hidden_size);
-      if (tc.talker.vocab_size > 4096 || tc.predictor.vocab_size > 4096 || tc.talker.vocab_size % 64 ||
-          tc.predictor.vocab_size % 64)
-        FAIL(Q3T_INVALID_INPUT, "vocab sizes must be multiples of 64 and <= 4096");
+      if (tc.talker.vocab_size > 4096 || tc.predictor.vocab_size > 4096 || tc.talker.vocab_size % 128 ||
+          tc.predictor.vocab_size % 128)
+        FAIL(Q3T_INVALID_INPUT, "vocab sizes must be multiples of 128 and <= 4096");
       load_stack(m, m->talker, tc.talker, "talker.model", T, st);
       load_stack(m, m->pred, tc.predictor, "talker.code_predictor.model", T, st);
       const int H = tc.talker.hidden_size, V = tc.talker.vocab_size, PV = tc.predictor.vocab_size;
-      m->codec_head = m->arena.alloc<uint16_t>((size_t)V * H);
-      pack_into(T.get("talker.codec_head.weight", {V, H}), m->codec_head, V, H, st);
+      m->codec_head = load_linear(T.get("talker.codec_head.weight", {V, H}), V, H, m->arena, st);
       m->talker_emb = upload_bf16(T.get("talker.model.codec_embedding.weight", {V, H}), m->arena, st);
       for (int j = 0; j < G - 1; j++) {
         m->cp_emb.push_back(upload_bf16(
             T.get("talker.code_predictor.model.codec_embedding." + std::to_string(j) + ".weight", {PV, H}),
             m->arena, st));
-        uint16_t *lh = m->arena.alloc<uint16_t>((size_t)PV * H);
-        pack_into(T.get("talker.code_predictor.lm_head." + std::to_string(j) + ".weight", {PV, H}), lh, PV,
-                  H, st);
-        m->lm_heads.push_back(lh);
+        m->lm_heads.push_back(load_linear(
+            T.get("talker.code_predictor.lm_head." + std::to_string(j) + ".weight", {PV, H}), PV, H, m->arena, st));
       }
       m->cp_emb_dev = m->arena.alloc<uint16_t *>(G - 1);
       CK(cudaMemcpyAsync(m->cp_emb_dev, m->cp_emb.data(), (G - 1) * sizeof(uint16_t *), cudaMemcpyHostToDevice,
@@ -351,6 +359,9 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
   b->act = ar.zalloc<uint16_t>((size_t)T * b->I2 / 2);
   b->tlog = ar.zalloc<float>((size_t)T * b->V);
   b->plog = ar.zalloc<float>((size_t)(G - 1) * A * b->PV);
+  b->d_err = ar.zalloc<int>(1);
+  CK(cudaMallocHost(&b->h_err, sizeof(int)));
+  *b->h_err = 0;
   const int mkv = std::max(nkv, pnkv);
   b->ws.part = ar.zalloc<float>((size_t)T * mkv * kAttnMaxUnits * 2 * 132);
   b->ws.counters = ar.zalloc<int>((size_t)T * mkv);
@@ -376,6 +387,8 @@ static void batch_destroy(q3t_batch *b) {
   for (auto &kv : b->graphs) cudaGraphExecDestroy(kv.second.exec);
   b->graphs.clear();
   b->programs.clear();
+  b->xmaps.clear();
+  if (b->h_err) cudaFreeHost(b->h_err);
   for (auto &r : b->reqs)
     for (void *p : {(void *)r.second->d_trailing, (void *)r.second->d_pad, (void *)r.second->d_prompt,
                     (void *)r.second->d_forced})
@@ -463,6 +476,26 @@ static KVView pred_kv(q3t_batch *b) {
 
 
 // ---------------------------------------------------------------------------
+// X = bf16 rows [Tmax][ldx] of a batch buffer, loaded by TMA (descriptor per
+// buffer and token-tile height, made on first use); GEMM timeouts go to d_err.
+static GemmArgs gemm_bf16_x(q3t_batch *b, GemmArgs g, const uint16_t *x, int ldx) {
+  g.xmode = GX_BF16;
+  g.xb = x;
+  g.ldx = ldx;
+  g.err = b->d_err;
+  const auto key = std::make_tuple((const void *)x, ldx, g.nt);
+  auto it = b->xmaps.find(key);
+  if (it == b->xmaps.end()) {
+    CUtensorMap m;
+    if (!make_tmap_bf16(&m, x, (uint64_t)ldx, (uint64_t)b->Tmax, (uint64_t)ldx * 2, 64, (uint32_t)(8 * g.nt)))
+      FAIL(Q3T_CUDA_ERROR, "TMA descriptor encoding failed for an activation buffer");
+    it = b->xmaps.emplace(key, m).first;
+  }
+  g.tx = it->second;
+  return g;
+}
+
+// ---------------------------------------------------------------------------
 // Phase emitter: the decode frame is built once per (token bucket mt,
 // attention unit bucket ms) as a phase list and captured into a CUDA graph;
 // the per-step inputs (active slots, positions, frames, trailing-text rows,
@@ -505,13 +538,8 @@ struct ProgBuilder {
     }
     push(p);
   }
-  // X = bf16 rows
-  static GemmArgs bf16_x(GemmArgs g, const uint16_t *x, int ldx) {
-    g.xmode = GX_BF16;
-    g.xb = x;
-    g.ldx = ldx;
-    return g;
-  }
+  // X = bf16 rows [Tmax][ldx] of a batch buffer, loaded by TMA
+  GemmArgs bf16_x(GemmArgs g, const uint16_t *x, int ldx) const { return gemm_bf16_x(b, g, x, ldx); }
   // X = RMSNorm(x rows t * row_mul + row_add) from the residual stream and
   // the sum-of-squares partials its last GE_RESID epilogue wrote
   GemmArgs norm_x(GemmArgs g, const float *gamma, float eps, int row_mul = 1, int row_add = 0) const {
@@ -525,6 +553,7 @@ struct ProgBuilder {
     g.ss_ld = b->Tmax;
     g.gamma = gamma;
     g.eps = eps;
+    g.err = b->d_err;
     return g;
   }
   GemmArgs resid(GemmArgs g) const {
@@ -544,7 +573,7 @@ struct ProgBuilder {
     const int NQ = (nh + 2 * nkv) * 128, QD = nh * 128;
     const float eps = c.rms_norm_eps;
     for (int l = 0; l < c.num_hidden_layers; l++) {
-      GemmArgs q = gemm_args(S.wqkv[l], NQ, H, tv.ntok, max_tok);
+      GemmArgs q = gemm_args(S.qkv[l], tv.ntok, max_tok);
       q = l == 0 ? bf16_x(q, b->xn, H) : norm_x(q, S.in_norm[l], eps);
       q.epi = GE_QKV;
       q.q_norm = S.q_norm[l];
@@ -570,13 +599,13 @@ struct ProgBuilder {
       aa.ws = b->ws;
       aa.out = b->attn;
       push(at);
-      gemm(resid(bf16_x(gemm_args(S.wo[l], H, QD, tv.ntok, max_tok), b->attn, QD)), max_tok);
-      GemmArgs gu = norm_x(gemm_args(S.wgu[l], 2 * I, H, tv.ntok, max_tok), S.post_norm[l], eps);
+      gemm(resid(bf16_x(gemm_args(S.o[l], tv.ntok, max_tok), b->attn, QD)), max_tok);
+      GemmArgs gu = norm_x(gemm_args(S.gu[l], tv.ntok, max_tok), S.post_norm[l], eps);
       gu.epi = GE_SILU;
       gu.h = b->act;
       gu.ldh = I;
       gemm(gu, max_tok);
-      gemm(resid(bf16_x(gemm_args(S.wdown[l], H, I, tv.ntok, max_tok), b->act, I)), max_tok);
+      gemm(resid(bf16_x(gemm_args(S.down[l], tv.ntok, max_tok), b->act, I)), max_tok);
     }
   }
 };
@@ -639,7 +668,7 @@ static void build_frame(q3t_batch *b, int mt, int max_units, std::vector<Phase> 
       P.stack(m->pred, pred_kv(b), tvj, mt, 1, kPredPages);
     }
     // lm_head j on the final-normed last position of each token's pass
-    GemmArgs hg = P.norm_x(gemm_args(m->lm_heads[j], PV, H, ntokB, mt), m->pred.final_norm, pc.rms_norm_eps,
+    GemmArgs hg = P.norm_x(gemm_args(m->lm_heads[j], ntokB, mt), m->pred.final_norm, pc.rms_norm_eps,
                            j == 0 ? 2 : 1, j == 0 ? 1 : 0);
     hg.epi = GE_F32;
     hg.y = b->hlog;
@@ -691,7 +720,7 @@ static void build_frame(q3t_batch *b, int mt, int max_units, std::vector<Phase> 
   P.norm(rms_args(b->x, H, 1, 0, Part{}, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps, ntokB,
                   b->d_hidden, slot),
          mt);
-  GemmArgs hg = ProgBuilder::bf16_x(gemm_args(m->codec_head, V, H, ntokB, mt), b->xn, H);
+  GemmArgs hg = P.bf16_x(gemm_args(m->codec_head, ntokB, mt), b->xn, H);
   hg.epi = GE_F32;
   hg.y = b->hlog;
   hg.ldy = V;
@@ -865,7 +894,7 @@ static void prefill(q3t_batch *b, Req *r) {
   // final norm of the last prompt token -> hidden[slot] and codec_head input
   rmsnorm(b->x, H, 1, last_n - 1, Part{nullptr, 0, 0, 0}, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps,
           dm + 1, 1, b->d_hidden, dm + 2, b->st);
-  GemmArgs hg = ProgBuilder::bf16_x(gemm_args(m->codec_head, V, H, dm + 1, 1), b->xn, H);
+  GemmArgs hg = gemm_bf16_x(b, gemm_args(m->codec_head, dm + 1, 1), b->xn, H);
   hg.epi = GE_F32;
   hg.y = b->hlog;
   hg.ldy = V;
@@ -1045,8 +1074,15 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
   b->h2d += b->meta_n * sizeof(int) + B * sizeof(float *);
   enqueue_frame(b, mt, ms);
   CK(cudaMemcpyAsync(b->h_eosflag, b->d_eosflag, B * sizeof(int), cudaMemcpyDeviceToHost, b->st));
+  CK(cudaMemcpyAsync(b->h_err, b->d_err, sizeof(int), cudaMemcpyDeviceToHost, b->st));
   CK(cudaStreamSynchronize(b->st));
-  b->d2h += B * sizeof(int);
+  b->d2h += B * sizeof(int) + sizeof(int);
+  if (*b->h_err) {
+    const int e = *b->h_err;
+    *b->h_err = 0;
+    CK(cudaMemsetAsync(b->d_err, 0, sizeof(int), b->st));
+    FAIL(Q3T_DEVICE_TIMEOUT, "decode frame: a bounded device wait gave up (code %d)", e);
+  }
   for (int i = 0; i < B; i++) {
     Req *r = act[i];
     r->step_idx++;
@@ -1441,7 +1477,7 @@ extern "C" q3t_status q3t_session_decode_embeds(q3t_session *s, const float *emb
       run_stack(b, m->talker, talker_kv(b), tvt, 1, ms);
       rmsnorm(b->x, b->H, 1, 0, Part{}, m->talker.final_norm, b->xn, b->H, b->H, m->tc.talker.rms_norm_eps, ntok, 1,
               b->d_hidden, slot, b->st);
-      GemmArgs hg = ProgBuilder::bf16_x(gemm_args(m->codec_head, b->V, b->H, ntok, 1), b->xn, b->H);
+      GemmArgs hg = gemm_bf16_x(b, gemm_args(m->codec_head, ntok, 1), b->xn, b->H);
       hg.epi = GE_F32;
       hg.y = b->tlog;
       hg.ldy = b->V;

@@ -67,7 +67,7 @@ struct DevArena {
 struct LMStack {
   q3t_lm_config cfg{};
   std::vector<float *> in_norm, post_norm, q_norm, k_norm;  // f32
-  std::vector<uint16_t *> wqkv, wo, wgu, wdown;              // fragment-packed bf16
+  std::vector<q3t::Linear> qkv, o, gu, down;  // bf16 row-major (gate/up interleaved per 64 rows)
   float *final_norm = nullptr;
   float *inv_freq = nullptr;  // [head_dim / 2]
 };
@@ -133,9 +133,10 @@ struct q3t_model {
   q3t_codec_config cc{};
   bool has_talker = false, has_codec = false;
   q3t::LMStack talker, pred;
-  uint16_t *codec_head = nullptr;            // packed [vocab][H]
+  q3t::Linear codec_head;                    // [vocab][H]
   uint16_t *talker_emb = nullptr;            // row-major bf16 [vocab][H]
-  std::vector<uint16_t *> cp_emb, lm_heads;  // row-major bf16 / packed
+  std::vector<uint16_t *> cp_emb;            // row-major bf16
+  std::vector<q3t::Linear> lm_heads;
   uint16_t **cp_emb_dev = nullptr;           // device array of cp_emb pointers
   int64_t kv_pages = 8192;
   int max_active = 64;
@@ -190,6 +191,8 @@ struct q3t_batch {
   bool use_graphs = true;
   std::map<std::tuple<int, int, int>, q3t::GraphEntry> graphs;
   std::map<std::pair<int, int>, std::vector<q3t::Phase>> programs;  // decode-frame phase lists
+  std::map<std::tuple<const void *, int, int>, CUtensorMap> xmaps;  // (X buffer, K, token tiles) -> TMA map
+  int *d_err = nullptr, *h_err = nullptr;  // bounded-wait timeouts reported by the GEMM kernels
   int step_counter = 0;
   // requests
   std::vector<q3t::Req *> slots;

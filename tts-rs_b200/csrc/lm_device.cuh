@@ -184,37 +184,43 @@ constexpr int kAttnWarps = 4;
 
 struct AttnSmem {
   float ps[kAttnWarps][2][16];
+  float ob[kAttnWarps][2][128];
   int pre[kAttnMaxTok + 1];  // first unit of each token
 };
 
-// Per-warp ring of kAttnStages pages in shared memory, filled with cp.async:
-// K rows are stored with their 16-byte chunks XOR-swizzled by (row & 7), so
-// the fragment reads (8 rows x 4 chunks per instruction) hit distinct banks;
-// V rows are stored as they are.
+// Per-warp ring of kAttnStages pages in shared memory, filled with cp.async.
+// K and V rows are stored with their 16-byte chunks XOR-swizzled by
+// (row & 7), so the K fragment loads (8 rows x 4 chunks) and the V ldmatrix
+// loads (8 rows of one chunk) hit distinct banks.  Rows at or beyond the
+// valid key count are zero-filled (the pool may hold stale or uninitialised
+// values there).
 constexpr int kAttnStages = 3;
 constexpr int kPageElems = 16 * 128;
 constexpr size_t kAttnDynSmem = (size_t)kAttnWarps * kAttnStages * 2 * kPageElems * 2;  // 96 KB
 
-Q3T_DEV void issue_page(uint16_t *ks, uint16_t *vs, const uint16_t *kp, const uint16_t *vp, int lane) {
+Q3T_DEV void issue_page(uint16_t *ks, uint16_t *vs, const uint16_t *kp, const uint16_t *vp, int nv, int lane) {
 #pragma unroll
   for (int j = 0; j < 8; j++) {
-    const int idx = lane + 32 * j, row = idx >> 4, c = idx & 15;
-    cp_async16(ks + row * 128 + ((c ^ (row & 7)) << 3), kp + row * 128 + c * 8, 16);
-    cp_async16(vs + row * 128 + c * 8, vp + row * 128 + c * 8, 16);
+    const int idx = lane + 32 * j, row = idx >> 4, c = idx & 15, sw = ((c ^ (row & 7)) << 3);
+    const int n = row < nv ? 16 : 0;
+    cp_async16(ks + row * 128 + sw, kp + row * 128 + c * 8, n);
+    cp_async16(vs + row * 128 + sw, vp + row * 128 + c * 8, n);
   }
 }
 
-// Running softmax state of one warp: m per head, l = this lane's share,
-// o[h][e] = unnormalised output for dims 8(lane & 15) + e over the keys of
-// parity lane >> 4.
+// Running softmax state of one warp: m / l per head (l = this lane's share);
+// c[dt] = the m16n8k16 accumulator of O^T dims [16dt, 16dt + 16) x columns
+// (heads) 0..7: on lanes with (lane & 3) == 0, c0/c1 = dim 16dt + lane/4 of
+// heads 0/1 and c2/c3 = dim 16dt + 8 + lane/4.
 struct AttnAcc {
-  float m[2], l[2], o[2][8];
+  float m[2], l[2], c[8][4];
 };
 
 // One staged page: ks / vs = the page's K / V in the warp's ring; nv valid keys.
 Q3T_DEV void attn_page(AttnAcc &A, const uint16_t *ks, const uint16_t *vs, const uint4 *qf, int nv, float scale,
                        float (*ps)[16], int lane) {
   const int g = lane >> 2, t = lane & 3;
+  // S^T = K Q^T on the tensor cores
   float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int q = 0; q < 4; q++) {
@@ -251,27 +257,37 @@ Q3T_DEV void attn_page(AttnAcc &A, const uint16_t *ks, const uint16_t *vs, const
     ps[1][g + 8] = p11;
   }
 #pragma unroll
-  for (int e = 0; e < 8; e++) {
-    A.o[0][e] *= cr0;
-    A.o[1][e] *= cr1;
+  for (int dt = 0; dt < 8; dt++) {
+    A.c[dt][0] *= cr0;
+    A.c[dt][1] *= cr1;
+    A.c[dt][2] *= cr0;
+    A.c[dt][3] *= cr1;
   }
   __syncwarp();
+  // O^T += V^T P^T: B = P^T (16 keys x heads), split p = hi + lo in bf16 so
+  // the products keep ~16 mantissa bits of p
+  uint32_t bh0 = 0u, bh1 = 0u, bl0 = 0u, bl1 = 0u;
+  if (g < 2) {
+    const float pv[4] = {ps[g][2 * t], ps[g][2 * t + 1], ps[g][2 * t + 8], ps[g][2 * t + 9]};
+    float hi[4], lo[4];
 #pragma unroll
-  for (int i = 0; i < 8; i++) {
-    const int key = 2 * i + (lane >> 4);
-    if (key < nv) {
-      const float pa = ps[0][key], pb = ps[1][key];
-      const uint4 vv = *reinterpret_cast<const uint4 *>(vs + key * 128 + 8 * (lane & 15));
-      const uint32_t w4[4] = {vv.x, vv.y, vv.z, vv.w};
-#pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const float v0 = bf2f(w4[e] & 0xffffu), v1 = bf2f(w4[e] >> 16);
-        A.o[0][2 * e] += pa * v0;
-        A.o[0][2 * e + 1] += pa * v1;
-        A.o[1][2 * e] += pb * v0;
-        A.o[1][2 * e + 1] += pb * v1;
-      }
+    for (int i = 0; i < 4; i++) {
+      hi[i] = bf16_round(pv[i]);
+      lo[i] = pv[i] - hi[i];
     }
+    bh0 = pack_bf16x2(hi[0], hi[1]);
+    bh1 = pack_bf16x2(hi[2], hi[3]);
+    bl0 = pack_bf16x2(lo[0], lo[1]);
+    bl1 = pack_bf16x2(lo[2], lo[3]);
+  }
+  const int mi = lane >> 3, vr = (lane & 7) + ((mi >> 1) << 3);  // ldmatrix: matrix mi, key row vr
+#pragma unroll
+  for (int dt = 0; dt < 8; dt++) {
+    const int ch = ((2 * dt + (mi & 1)) ^ (vr & 7)) << 3;
+    uint32_t a0, a1, a2, a3;
+    ldmatrix_x4_trans(a0, a1, a2, a3, vs + vr * 128 + ch);
+    mma_16816(A.c[dt], a0, a1, a2, a3, bh0, bh1);
+    mma_16816(A.c[dt], a0, a1, a2, a3, bl0, bl1);
   }
   __syncwarp();
 }
@@ -291,8 +307,9 @@ Q3T_DEV void store_bf16x8(uint16_t *dst, const float *v, float inv) {
   *reinterpret_cast<uint4 *>(dst) = u;
 }
 
-// Unit r of token t, run by one warp (ps, ring: the warp's shared buffers).
-Q3T_DEV void attn_unit(const AttnArgs &a, int t, int r, float (*ps)[16], uint16_t *ring, int lane) {
+// Unit r of token t, run by one warp (ps, ob, ring: the warp's shared buffers).
+Q3T_DEV void attn_unit(const AttnArgs &a, int t, int r, float (*ps)[16], float (*ob)[128], uint16_t *ring,
+                       int lane) {
   const KVView &kv = a.kv;
   const int pos = a.tv.pos[t] + a.tv.pos_add, L = pos + 1, seq = a.tv.seq[t];
   const int pages = (L + 15) >> 4, pw = attn_unit_pages(pages, a.pw), nu = (pages + pw - 1) / pw;
@@ -309,7 +326,8 @@ Q3T_DEV void attn_unit(const AttnArgs &a, int t, int r, float (*ps)[16], uint16_
   for (int i = 0; i < kAttnStages - 1; i++) {
     if (i < np) {
       const size_t off = (size_t)__shfl_sync(0xffffffffu, my_page, i) * page_elems + head_off;
-      issue_page(ring + i * 2 * kPageElems, ring + (i * 2 + 1) * kPageElems, kb + off, vb + off, lane);
+      issue_page(ring + i * 2 * kPageElems, ring + (i * 2 + 1) * kPageElems, kb + off, vb + off,
+                 L - (p0 + i) * 16, lane);
     }
     cp_async_commit();
   }
@@ -328,13 +346,14 @@ Q3T_DEV void attn_unit(const AttnArgs &a, int t, int r, float (*ps)[16], uint16_
   A.m[0] = A.m[1] = -FLT_MAX;
   A.l[0] = A.l[1] = 0.f;
 #pragma unroll
-  for (int e = 0; e < 8; e++) A.o[0][e] = A.o[1][e] = 0.f;
+  for (int dt = 0; dt < 8; dt++) A.c[dt][0] = A.c[dt][1] = A.c[dt][2] = A.c[dt][3] = 0.f;
   for (int i = 0; i < np; i++) {
     const int nx = i + kAttnStages - 1;  // page to start now, into the slot page i - 1 used
     if (nx < np) {
       const int sl = nx % kAttnStages;
       const size_t off = (size_t)__shfl_sync(0xffffffffu, my_page, nx) * page_elems + head_off;
-      issue_page(ring + sl * 2 * kPageElems, ring + (sl * 2 + 1) * kPageElems, kb + off, vb + off, lane);
+      issue_page(ring + sl * 2 * kPageElems, ring + (sl * 2 + 1) * kPageElems, kb + off, vb + off,
+                 L - (p0 + nx) * 16, lane);
     }
     cp_async_commit();
     cp_async_wait<kAttnStages - 1>();  // this lane's copies of page i have landed
@@ -343,19 +362,32 @@ Q3T_DEV void attn_unit(const AttnArgs &a, int t, int r, float (*ps)[16], uint16_
     attn_page(A, ring + sl * 2 * kPageElems, ring + (sl * 2 + 1) * kPageElems, qf, min(16, L - key0), a.scale, ps,
               lane);
   }
-  // fold the two key parities and the lanes' l shares
-#pragma unroll
-  for (int e = 0; e < 8; e++) {
-    A.o[0][e] += __shfl_xor_sync(0xffffffffu, A.o[0][e], 16);
-    A.o[1][e] += __shfl_xor_sync(0xffffffffu, A.o[1][e], 16);
-  }
+  // O^T from the accumulators (lanes t == 0) through shared memory: lane
+  // l < 16 then holds dims 8l..8l+7 of both heads in o[h][e]
   A.l[0] = warp_sum(A.l[0]);
   A.l[1] = warp_sum(A.l[1]);
+  if ((lane & 3) == 0) {
+    const int gg = lane >> 2;
+#pragma unroll
+    for (int dt = 0; dt < 8; dt++) {
+      ob[0][16 * dt + gg] = A.c[dt][0];
+      ob[1][16 * dt + gg] = A.c[dt][1];
+      ob[0][16 * dt + 8 + gg] = A.c[dt][2];
+      ob[1][16 * dt + 8 + gg] = A.c[dt][3];
+    }
+  }
+  __syncwarp();
+  float o[2][8];
+#pragma unroll
+  for (int h = 0; h < 2; h++)
+#pragma unroll
+    for (int e = 0; e < 8; e++) o[h][e] = ob[h][8 * (lane & 15) + e];
+  __syncwarp();  // ob is rewritten by the warp's next unit
   uint16_t *out = a.out + (size_t)t * nh * 128 + 2 * g * 128;
   if (nu == 1) {
     if (lane < 16) {
-      store_bf16x8(out + 8 * lane, A.o[0], 1.f / A.l[0]);
-      store_bf16x8(out + 128 + 8 * lane, A.o[1], 1.f / A.l[1]);
+      store_bf16x8(out + 8 * lane, o[0], 1.f / A.l[0]);
+      store_bf16x8(out + 128 + 8 * lane, o[1], 1.f / A.l[1]);
     }
     return;
   }
@@ -364,9 +396,8 @@ Q3T_DEV void attn_unit(const AttnArgs &a, int t, int r, float (*ps)[16], uint16_
   if (lane < 16) {
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-      *reinterpret_cast<float4 *>(P + h * kPart + 8 * lane) = make_float4(A.o[h][0], A.o[h][1], A.o[h][2], A.o[h][3]);
-      *reinterpret_cast<float4 *>(P + h * kPart + 8 * lane + 4) =
-          make_float4(A.o[h][4], A.o[h][5], A.o[h][6], A.o[h][7]);
+      *reinterpret_cast<float4 *>(P + h * kPart + 8 * lane) = make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
+      *reinterpret_cast<float4 *>(P + h * kPart + 8 * lane + 4) = make_float4(o[h][4], o[h][5], o[h][6], o[h][7]);
     }
   }
   if (lane == 0) {
@@ -454,7 +485,7 @@ Q3T_DEV void d_attn(const AttnArgs &a, int tid, int warp0, int nwarps, AttnSmem 
       else
         hi = mid;
     }
-    attn_unit(a, lo, u - S.pre[lo], S.ps[w], ring + (size_t)w * kAttnStages * 2 * kPageElems, lane);
+    attn_unit(a, lo, u - S.pre[lo], S.ps[w], S.ob[w], ring + (size_t)w * kAttnStages * 2 * kPageElems, lane);
   }
   sync();  // S is reused by the caller's next item
 }

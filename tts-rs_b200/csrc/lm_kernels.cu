@@ -15,7 +15,10 @@
 #include <cstdlib>
 #include <utility>
 
+#include <cudaTypedefs.h>
+
 #include "lm_device.cuh"
+#include "umma.cuh"
 
 namespace q3t {
 
@@ -140,23 +143,39 @@ void rmsnorm(float *x, int ldx, int row_mul, int row_add, Part add, const float 
 }
 
 // ---------------------------------------------------------------------------
-// Cluster split-K GEMM (GemmArgs in lm_kernels.cuh).  CTA = 8 warps = 8 row
-// blocks of 16 (one 128-row output block) x the cluster rank's K range x up
-// to 8*NT tokens.  Each warp holds its KT weight fragments in registers,
-// issued before griddepcontrol.wait so the weight stream overlaps the end of
-// the previous kernel.  X (bf16, or f32 residual rows normalised here) is
-// staged once per CTA in shared memory; the m16n8k16 products go to an f32
-// tile [token][row]; after a cluster barrier CTA rank c sums token slice c of
-// all ranks' tiles (rank order) and runs the epilogue, one warp per token,
-// lane = 4 consecutive rows.
+// Cluster split-K GEMM on the 5th-generation tensor cores (GemmArgs in
+// lm_kernels.cuh).  A CTA owns one 128-row output block and the cluster
+// rank's K range (KA atoms of 64) for up to N = 8*NT tokens:
+//   - one thread issues the TMA loads of its weight tile (K-major,
+//     SWIZZLE_128B) before griddepcontrol.wait, so the weight stream overlaps
+//     the end of the previous kernel;
+//   - X arrives by TMA (bf16 rows) or is staged by all threads from the f32
+//     residual rows, RMS-normalised and rounded to bf16, straight into the
+//     swizzled operand layout;
+//   - the same thread issues KA*4 tcgen05.mma (M = 128, N, K = 16) into a
+//     TMEM accumulator and commits them to an mbarrier;
+//   - warps 0..3 read the accumulator back (tcgen05.ld, one row per thread)
+//     into an f32 tile [token][row] over the consumed weight tile; after a
+//     cluster barrier CTA rank c sums token slice c of all ranks' tiles
+//     through distributed shared memory (rank order) and runs the epilogue,
+//     one warp per token, lane = 4 consecutive rows.
+// Every mbarrier wait is bounded; a timeout sets a bit in *err and the kernel
+// still runs to completion with the same barriers, so a cluster never hangs.
 // ---------------------------------------------------------------------------
-constexpr int kTileLd = 132;  // f32 pitch of the reduction tile (bank-conflict-free fragment stores)
-
+constexpr int kTileLd = 132;  // f32 pitch of the reduction tile
 constexpr int kMaxNss = 16;   // sum-of-squares partials per row (hidden <= 2048)
 
-static size_t gemm_smem(int nt, int kt) {
-  return (size_t)nt * 8 * (kt * 16 + 8) * 2 + (size_t)nt * 8 * kTileLd * 4 + 64 * 4 + 128 * 4;
-}
+template <int NT, int KA>
+struct GemmSmem {
+  static constexpr int N = NT * 8;
+  static constexpr int kW = KA * 16384;   // weight tile: KA atoms of 128 rows x 128 B
+  static constexpr int kXAtom = N * 128;  // one X atom: N rows x 128 B
+  static constexpr int kTile = N * kTileLd * 4;
+  static constexpr int kR0 = kW > kTile ? kW : (kTile + 1023) / 1024 * 1024;
+  static constexpr int kX = KA * kXAtom;
+  static constexpr int kMisc = 1024;       // mbarriers, TMEM slot, rms, token metadata
+  static constexpr size_t kBytes = (size_t)kR0 + kX + kMisc + 1024;  // + alignment slack
+};
 
 Q3T_DEV void store_bf16x4(uint16_t *dst, float a, float b, float c, float d) {
   uint2 p;
@@ -206,36 +225,57 @@ Q3T_DEV void gemm_epilogue(const GemmArgs &a, int t, int rg, int lane, float4 v,
   }
 }
 
-template <int NT, int KTM>
-__global__ void __launch_bounds__(256, KTM > 16 ? 1 : 2) k_gemm(GemmArgs a) {
-  extern __shared__ __align__(16) unsigned char gsm[];
+template <int NT, int KA>
+__global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_constant__ GemmArgs a) {
+  using L = GemmSmem<NT, KA>;
+  constexpr int N = L::N, KC = KA * 64;
+  constexpr uint32_t kCols = N < 32 ? 32 : N;
+  extern __shared__ unsigned char gsm_raw[];
+  unsigned char *gsm = gsm_raw + ((1024 - (smem_addr(gsm_raw) & 1023)) & 1023);
+  unsigned char *wsm = gsm, *xsm = gsm + L::kR0;
+  float *tile = reinterpret_cast<float *>(gsm);  // after the MMA, over the weights
+  uint64_t *bars = reinterpret_cast<uint64_t *>(xsm + L::kX);  // weights, X, MMA done
+  uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 3);
+  float *rms = reinterpret_cast<float *>(bars + 4);             // [64]
+  int *meta = reinterpret_cast<int *>(rms + 64);                // [128]
   const int cs = a.cs, ks = blockIdx.x % cs, rg = blockIdx.x / cs;
-  const int tok0 = blockIdx.y * (NT * 8);
+  const int tok0 = blockIdx.y * N, k0 = ks * KC;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KT = (a.K >> 4) / cs, KC = KT * 16, ldx = KC + 8;
-  uint16_t *xs = reinterpret_cast<uint16_t *>(gsm);
-  float *tile = reinterpret_cast<float *>(gsm + (size_t)NT * 8 * ldx * 2);
-  float *rms = tile + NT * 8 * kTileLd;
-  int *meta = reinterpret_cast<int *>(rms + 64);
-  const uint4 *wp = a.W + ((size_t)(rg * 8 + warp) * (a.K >> 4) + (size_t)ks * KT) * 32 + lane;
-  uint4 frag[KTM];
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    mbar_init(&bars[2], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(tslot, kCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  if (threadIdx.x == 0) {  // weights: independent of earlier kernels
+    mbar_expect_tx(&bars[0], L::kW);
 #pragma unroll
-  for (int i = 0; i < KTM; i++)
-    if (i < KT) frag[i] = ldg_stream(wp + i * 32);
+    for (int i = 0; i < KA; i++) tma_load_2d(wsm + i * 16384, &a.tw, k0 + 64 * i, rg * 128, &bars[0]);
+  }
   pdl_wait();
   pdl_launch();
   int ntok = *a.ntok - tok0;
-  ntok = ntok < 0 ? 0 : (ntok > NT * 8 ? NT * 8 : ntok);
-  const int k0 = ks * KC;
-  const int ts = (NT * 8 + cs - 1) / cs, t_lo = ks * ts, t_hi = min(t_lo + ts, ntok);
+  ntok = ntok < 0 ? 0 : (ntok > N ? N : ntok);
+  const int ts = (N + cs - 1) / cs, t_lo = ks * ts, t_hi = min(t_lo + ts, ntok);
   if (a.epi == GE_QKV && (int)threadIdx.x < t_hi - t_lo) {
-    // cache position and page of this CTA's epilogue tokens (loads overlap the GEMM)
+    // position and page of this CTA's epilogue tokens (loads overlap the GEMM)
     const int t = tok0 + t_lo + threadIdx.x;
     const int pos = a.tv.pos[t] + a.tv.pos_add;
     meta[2 * threadIdx.x] = pos;
     meta[2 * threadIdx.x + 1] = a.kv.page_table[(size_t)a.tv.seq[t] * a.kv.pt_stride + (pos >> 4)];
   }
-  if (a.xmode == GX_NORM) {
+  if (a.xmode == GX_BF16) {
+    if (threadIdx.x == 0) {
+      mbar_expect_tx(&bars[1], L::kX);
+#pragma unroll
+      for (int i = 0; i < KA; i++) tma_load_2d(xsm + i * L::kXAtom, &a.tx, k0 + 64 * i, tok0, &bars[1]);
+    }
+  } else {
     for (int r = threadIdx.x; r < ntok; r += blockDim.x) {
       const float *sp = a.ss + (size_t)(tok0 + r) * a.xrow_mul + a.xrow_add;
       float p[kMaxNss];
@@ -247,79 +287,57 @@ __global__ void __launch_bounds__(256, KTM > 16 ? 1 : 2) k_gemm(GemmArgs a) {
       rms[r] = 1.f / sqrtf(s / (float)a.K + a.eps);
     }
     __syncthreads();
-  }
-  // stage X[tok0 .. tok0 + 8NT)[k0 .. k0 + KC) as bf16; rows >= ntok are zero
-  const int c8n = KC >> 3;
-  if (a.xmode == GX_BF16) {
-    for (int idx = threadIdx.x; idx < NT * 8 * c8n; idx += blockDim.x) {
-      const int r = idx / c8n, c8 = (idx - r * c8n) * 8;
-      const int rr = r < ntok ? r : 0;
-      cp_async16(xs + r * ldx + c8, a.xb + (size_t)(tok0 + rr) * a.ldx + k0 + c8, r < ntok ? 16 : 0);
-    }
-    cp_async_commit();
-    cp_async_wait<0>();
-  } else {
-    // a thread keeps one 8-column group (gamma in registers) and walks rows
-    // four at a time with all loads of a batch in flight together
-    const int rstep = blockDim.x / c8n;  // c8n divides 256 (KC is 128 or 256 here)
-    const int c8 = (threadIdx.x % c8n) * 8, r0 = threadIdx.x / c8n;
-    if (r0 < rstep) {
-      const float4 g0 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8);
-      const float4 g1 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8 + 4);
-      for (int rb = r0; rb < NT * 8; rb += 4 * rstep) {
-        float4 xv[4][2];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const int r = rb + i * rstep;
-          if (r < ntok) {
-            const float *xr = a.x + (size_t)((tok0 + r) * a.xrow_mul + a.xrow_add) * a.ldx + k0 + c8;
-            xv[i][0] = *reinterpret_cast<const float4 *>(xr);
-            xv[i][1] = *reinterpret_cast<const float4 *>(xr + 4);
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const int r = rb + i * rstep;
-          if (r >= NT * 8) break;
-          uint4 v = make_uint4(0u, 0u, 0u, 0u);
-          if (r < ntok) {
-            const float d = rms[r];  // 1 / rms
-            v.x = pack_bf16x2(xv[i][0].x * d * g0.x, xv[i][0].y * d * g0.y);
-            v.y = pack_bf16x2(xv[i][0].z * d * g0.z, xv[i][0].w * d * g0.w);
-            v.z = pack_bf16x2(xv[i][1].x * d * g1.x, xv[i][1].y * d * g1.y);
-            v.w = pack_bf16x2(xv[i][1].z * d * g1.z, xv[i][1].w * d * g1.w);
-          }
-          *reinterpret_cast<uint4 *>(xs + r * ldx + c8) = v;
-        }
+    // one 8-column chunk per thread and step: x * (1 / rms) * gamma -> bf16,
+    // stored at chunk (c ^ (row & 7)) of the row's 128-byte atom line
+    constexpr int c8n = KC / 8;
+    for (int idx = threadIdx.x; idx < N * c8n; idx += blockDim.x) {
+      const int r = idx / c8n, c8 = idx - r * c8n;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (r < ntok) {
+        const float *xr = a.x + (size_t)((tok0 + r) * a.xrow_mul + a.xrow_add) * a.ldx + k0 + c8 * 8;
+        const float4 x0 = *reinterpret_cast<const float4 *>(xr), x1 = *reinterpret_cast<const float4 *>(xr + 4);
+        const float4 g0 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8 * 8);
+        const float4 g1 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8 * 8 + 4);
+        const float d = rms[r];
+        v.x = pack_bf16x2(x0.x * d * g0.x, x0.y * d * g0.y);
+        v.y = pack_bf16x2(x0.z * d * g0.z, x0.w * d * g0.w);
+        v.z = pack_bf16x2(x1.x * d * g1.x, x1.y * d * g1.y);
+        v.w = pack_bf16x2(x1.z * d * g1.z, x1.w * d * g1.w);
       }
+      *reinterpret_cast<uint4 *>(xsm + (c8 >> 3) * L::kXAtom + r * 128 + (((c8 & 7) ^ (r & 7)) << 4)) = v;
     }
+    fence_proxy_async();
   }
   __syncthreads();
-  float acc[NT][4];
+  uint32_t err = 0;
+  if (threadIdx.x == 0) {
+    if (!mbar_wait(&bars[0], 0)) err |= 1u;
+    if (a.xmode == GX_BF16 && !mbar_wait(&bars[1], 0)) err |= 2u;
+    tc_fence_after();
+    constexpr uint32_t idesc = umma_idesc_bf16(128, N);
 #pragma unroll
-  for (int j = 0; j < NT; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-  const int g = lane >> 2, t = lane & 3;
+    for (int s = 0; s < KA * 4; s++) {
+      const int at = s >> 2, off = (s & 3) * 32;
+      umma_bf16(tmem, sw128_desc(wsm + at * 16384 + off), sw128_desc(xsm + at * L::kXAtom + off), idesc,
+                s > 0 ? 1u : 0u);
+    }
+    umma_commit(&bars[2]);
+  }
+  if (!mbar_wait(&bars[2], 0)) err |= 4u;
+  tc_fence_after();
+  if (warp < 4) {  // accumulator lane = output row, column = token
+    const uint32_t tq = tmem + ((uint32_t)(32 * warp) << 16);
+    const int row = 32 * warp + lane;
 #pragma unroll
-  for (int i = 0; i < KTM; i++) {
-    if (i < KT) {
+    for (int c0 = 0; c0 < N; c0 += 8) {
+      float v[8];
+      tmem_ld8(tq + c0, v);
 #pragma unroll
-      for (int j = 0; j < NT; j++) {
-        const uint16_t *xr = xs + (j * 8 + g) * ldx + i * 16 + 2 * t;
-        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xr);
-        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xr + 8);
-        mma_16816(acc[j], frag[i].x, frag[i].y, frag[i].z, frag[i].w, b0, b1);
-      }
+      for (int j = 0; j < 8; j++) tile[(c0 + j) * kTileLd + row] = v[j];
     }
   }
-  const int row = warp * 16 + g;
-#pragma unroll
-  for (int j = 0; j < NT; j++) {
-    const int tk = j * 8 + 2 * t;
-    tile[tk * kTileLd + row] = acc[j][0];
-    tile[(tk + 1) * kTileLd + row] = acc[j][1];
-    tile[tk * kTileLd + row + 8] = acc[j][2];
-    tile[(tk + 1) * kTileLd + row + 8] = acc[j][3];
-  }
+  if (err && a.err) atomicOr(a.err, (int)err);
+  tc_fence_before();
   if (cs > 1)
     cluster_sync();
   else
@@ -347,35 +365,37 @@ __global__ void __launch_bounds__(256, KTM > 16 ? 1 : 2) k_gemm(GemmArgs a) {
     gemm_epilogue(a, tok0 + tt, rg, lane, v, meta + 2 * (tt - t_lo));
   }
   if (cs > 1) cluster_sync();  // no CTA leaves while another still reads its tile
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kCols);
 }
 
-GemmArgs gemm_args(const uint16_t *Wp, int N, int K, const int *ntok, int max_tok) {
-  GemmArgs a{};
-  a.W = reinterpret_cast<const uint4 *>(Wp);
-  a.N = N;
-  a.K = K;
+GemmArgs gemm_args(const Linear &W, const int *ntok, int max_tok) {
+  GemmArgs a;
+  memset(&a, 0, sizeof a);
+  a.tw = W.tm;
+  a.N = W.N;
+  a.K = W.K;
   a.ntok = ntok;
   const int per = max_tok < 64 ? max_tok : 64;
   a.nt = per <= 8 ? 1 : (per <= 16 ? 2 : (per <= 32 ? 4 : 8));
-  // smallest cluster that gives >= 128 CTAs (at most 8), then enough splits
-  // that a warp holds at most 24 fragments
-  const int groups = N / 128, kt = K / 16;
+  // smallest cluster that gives >= 128 CTAs (at most 8) whose K range is a
+  // whole number of 64-wide atoms, then enough splits for <= 6 atoms per CTA
+  const int groups = W.N / 128, atoms = W.K / 64;
   int cs = 1;
-  while (cs < 8 && groups * cs < 128 && kt % (2 * cs) == 0) cs *= 2;
-  while (cs < 8 && kt / cs > 24 && kt % (2 * cs) == 0) cs *= 2;
+  while (cs < 8 && groups * cs < 128 && atoms % (2 * cs) == 0) cs *= 2;
+  while (cs < 8 && atoms / cs > 6 && atoms % (2 * cs) == 0) cs *= 2;
   a.cs = cs;
-  a.ldx = K;
+  a.ldx = W.K;
   a.xrow_mul = 1;
-  a.nss = 0;
   return a;
 }
 
-template <int NT, int KTM>
+template <int NT, int KA>
 static void gemm_launch(const GemmArgs &a, dim3 grid, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = gemm_smem(NT, (a.K >> 4) / a.cs);
+  cfg.dynamicSmemBytes = GemmSmem<NT, KA>::kBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -386,27 +406,25 @@ static void gemm_launch(const GemmArgs &a, dim3 grid, cudaStream_t st) {
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = g_use_pdl ? 2 : 1;
-  note(cudaLaunchKernelEx(&cfg, k_gemm<NT, KTM>, a), "k_gemm");
+  note(cudaLaunchKernelEx(&cfg, k_gemm<NT, KA>, a), "k_gemm");
   g_launches++;
 }
 
 template <int NT>
 static void gemm_nt(const GemmArgs &a, dim3 grid, cudaStream_t st) {
-  const int kt = (a.K >> 4) / a.cs;
-  if (kt <= 8)
-    gemm_launch<NT, 8>(a, grid, st);
-  else if (kt <= 16)
-    gemm_launch<NT, 16>(a, grid, st);
-  else
-    gemm_launch<NT, 24>(a, grid, st);
+  switch ((a.K / 64) / a.cs) {
+    case 2: gemm_launch<NT, 2>(a, grid, st); break;
+    case 4: gemm_launch<NT, 4>(a, grid, st); break;
+    case 6: gemm_launch<NT, 6>(a, grid, st); break;
+    default: note(cudaErrorInvalidValue, "k_gemm (K range per CTA must be 2, 4 or 6 atoms of 64)"); break;
+  }
 }
 
 void gemm(const GemmArgs &a, int max_tok, cudaStream_t st) {
-  const int kt = a.K / 16;
-  if (a.N % 128 || a.K % 128 || a.cs < 1 || a.cs > 8 || kt % a.cs || kt / a.cs > 24 || max_tok < 1 ||
-      (a.epi == GE_SILU && a.h == nullptr) ||
-      (a.xmode == GX_NORM && (a.x == nullptr || a.ss == nullptr || 256 % (2 * (kt / a.cs)) != 0 ||
-                              a.nss > kMaxNss))) {
+  const int atoms = a.K / 64;
+  if (a.N % 128 || a.K % 64 || a.cs < 1 || a.cs > 8 || atoms % a.cs || max_tok < 1 ||
+      (a.epi == GE_SILU && a.h == nullptr) || (a.xmode == GX_NORM && (a.x == nullptr || a.ss == nullptr)) ||
+      a.nss > kMaxNss || (a.epi == GE_RESID && (a.ss_out == nullptr || a.y == nullptr))) {
     note(cudaErrorInvalidValue, "k_gemm (shape / arguments)");
     return;
   }
@@ -419,15 +437,35 @@ void gemm(const GemmArgs &a, int max_tok, cudaStream_t st) {
   }
 }
 
-template <int NT, int KTM>
+template <int NT, int KA>
 static void gemm_attr() {
-  cudaFuncSetAttribute(k_gemm<NT, KTM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem(NT, KTM));
+  cudaFuncSetAttribute(k_gemm<NT, KA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmSmem<NT, KA>::kBytes);
 }
 template <int NT>
 static void gemm_attrs() {
-  gemm_attr<NT, 8>();
-  gemm_attr<NT, 16>();
-  gemm_attr<NT, 24>();
+  gemm_attr<NT, 2>();
+  gemm_attr<NT, 4>();
+  gemm_attr<NT, 6>();
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+
+bool make_tmap_bf16(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                    uint32_t box_inner, uint32_t box_rows) {
+  if (!g_encode_tiled) {
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void **>(&g_encode_tiled),
+                                cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return false;
+  }
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  return g_encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 struct BlockSync {

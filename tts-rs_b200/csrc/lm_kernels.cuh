@@ -1,5 +1,6 @@
 // Host-side launchers of the talker / code-predictor kernels (lm_kernels.cu).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -116,8 +117,21 @@ enum GemmEpi {
   GE_SILU = 3,   // row block r = [gate 64r..64r+63 | up 64r..64r+63]: h[t][64r + i] = bf16(silu(g) * u)
 };
 
+// A weight matrix W [N][K] bf16 row-major with its TMA descriptor (box 64 x
+// 128, SWIZZLE_128B).
+struct Linear {
+  const uint16_t *w = nullptr;
+  int N = 0, K = 0;
+  CUtensorMap tm;
+};
+// Encodes a 2-D bf16 TMA descriptor over rows x inner elements (row pitch
+// row_bytes) with boxes of box_inner x box_rows, SWIZZLE_128B; false on error.
+bool make_tmap_bf16(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                    uint32_t box_inner, uint32_t box_rows);
+
 struct GemmArgs {
-  const uint4 *W;      // fragment-packed weights [N/16][K/16] (pack_weight)
+  CUtensorMap tw;      // weights W [N][K] (Linear::tm)
+  CUtensorMap tx;      // GX_BF16: X rows [rows][K], box 64 x 8*nt
   int N, K;
   int cs;              // cluster size = K splits (1, 2, 4 or 8)
   int nt;              // 8-token MMA tiles per CTA (1, 2, 4 or 8)
@@ -142,11 +156,12 @@ struct GemmArgs {
   uint16_t *q;         // GE_QKV: [t][nh * 128]
   KVView kv;
   int layer;
+  int *err;            // set (bitwise or) when a bounded wait gave up; nullable
 };
 
 // Cluster size and token tiles for an N x K GEMM over up to max_tok tokens
 // (N % 128 == 0, K % 128 == 0); the caller fills X and the epilogue.
-GemmArgs gemm_args(const uint16_t *Wp, int N, int K, const int *ntok, int max_tok);
+GemmArgs gemm_args(const Linear &W, const int *ntok, int max_tok);
 void gemm(const GemmArgs &a, int max_tok, cudaStream_t st);
 
 struct AttnArgs {
