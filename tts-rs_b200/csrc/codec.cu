@@ -23,6 +23,7 @@
 
 #include "codec.cuh"
 #include "common.cuh"
+#include "umma.cuh"
 
 namespace q3t {
 
@@ -202,10 +203,210 @@ __global__ void __launch_bounds__(256) k_conv(ConvArgs a) {
 
 static size_t conv_smem(int BN) { return (size_t)kStages * (kBM + BN) * kLDS * sizeof(__half); }
 
+// ---------------------------------------------------------------------------
+// The same convolution on the 5th-generation tensor cores.  A CTA computes a
+// tile of 128 output steps of one sequence and phase x N output channels:
+//   warp 0 lane 0  streams, per K step (tap j, ACH input channels), the
+//                  im2col tile X[b][tq0 + in_off + j*dil + 0..127][c0..c0+ACH)
+//                  (a 3-D TMA box: rows outside [0, Lin) read zeros, which is
+//                  the causal padding) and the weight tile W[phase][j][n0..
+//                  n0+N)[c0..c0+ACH) into a ring of S stages;
+//   warp 1 lane 0  issues tcgen05.mma (M = 128, N, K = 16) into a TMEM
+//                  accumulator and releases each stage with tcgen05.commit;
+//   all 4 warps    read the accumulator back (thread = output step, 16
+//                  channels per tcgen05.ld) and run the k_conv epilogue.
+// Operands are K-major with SWIZZLE_128B (ACH = 64) or SWIZZLE_64B (ACH = 32)
+// atoms.  Every mbarrier wait is bounded; a timeout sets a bit in *err.
+// ---------------------------------------------------------------------------
+struct ConvTc {
+  CUtensorMap tx;  // X [B][Lin][Cin], box ACH x 128 x 1
+  CUtensorMap tw;  // W [phases * taps * Cout][Cin], box ACH x N
+  ConvArgs a;
+  int tiles;       // 128-step tiles per sequence
+  int *err;
+};
+
+template <int N, int ACH, int S>
+struct ConvTcSmem {
+  static constexpr int kA = 128 * ACH * 2, kB = N * ACH * 2, kStage = kA + kB;
+  static constexpr size_t kBytes = (size_t)S * kStage + (2 * S + 2) * 8 + 1024;
+};
+
+Q3T_DEV void conv_epilogue16(const ConvArgs &a, size_t orow, int n, const float *v) {
+  float y[16];
+#pragma unroll
+  for (int j = 0; j < 16; j++) {
+    float t = v[j];
+    if (a.bias) t += a.bias[n + j];
+    if (a.scale) t *= a.scale[n + j];
+    y[j] = t;
+  }
+  const size_t e = orow * a.Cout + n;
+  if (a.R) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const float4 r = *reinterpret_cast<const float4 *>(a.R + e + 4 * q);
+      y[4 * q] += r.x;
+      y[4 * q + 1] += r.y;
+      y[4 * q + 2] += r.z;
+      y[4 * q + 3] += r.w;
+    }
+  }
+  if (a.Yf) {
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+      *reinterpret_cast<float4 *>(a.Yf + e + 4 * q) = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+  }
+  if (a.Yh) {
+    __half2 h[8];
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+      float h0 = y[j], h1 = y[j + 1];
+      if (a.act == ACT_SNAKE) {
+        h0 = snake(h0, a.act_a[n + j], a.act_b[n + j]);
+        h1 = snake(h1, a.act_a[n + j + 1], a.act_b[n + j + 1]);
+      } else if (a.act == ACT_GELU) {
+        h0 = gelu_erf(h0);
+        h1 = gelu_erf(h1);
+      }
+      h[j / 2] = __floats2half2_rn(h0, h1);
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(a.Yh + e);
+    dst[0] = *reinterpret_cast<const uint4 *>(&h[0]);
+    dst[1] = *reinterpret_cast<const uint4 *>(&h[4]);
+  }
+}
+
+template <int N, int ACH, int S>
+__global__ void __launch_bounds__(128) k_conv_tc(const __grid_constant__ ConvTc c) {
+  using L = ConvTcSmem<N, ACH, S>;
+  constexpr uint32_t kCols = N <= 128 ? 128 : 256;
+  extern __shared__ unsigned char csm_raw[];
+  unsigned char *sm = csm_raw + ((1024 - (smem_addr(csm_raw) & 1023)) & 1023);
+  uint64_t *full = reinterpret_cast<uint64_t *>(sm + S * L::kStage), *empty = full + S, *accb = empty + S;
+  uint32_t *tslot = reinterpret_cast<uint32_t *>(accb + 1);
+  const ConvArgs &a = c.a;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x / c.tiles, tq0 = (blockIdx.x - b * c.tiles) * 128;
+  const int n0 = blockIdx.y * N, phase = blockIdx.z;
+  const int kc = a.Cin / ACH, KS = a.taps * kc;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accb, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(tslot, kCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  uint32_t err = 0;
+  if (warp == 0 && lane == 0) {  // TMA producer
+    for (int ks = 0; ks < KS; ks++) {
+      const int s = ks % S, i = ks / S;
+      if (i > 0 && !mbar_wait(&empty[s], (i - 1) & 1)) {
+        err |= 1u;
+        break;
+      }
+      const int tap = ks / kc, c0 = (ks - tap * kc) * ACH;
+      unsigned char *st = sm + s * L::kStage;
+      mbar_expect_tx(&full[s], L::kStage);
+      tma_load_3d(st, &c.tx, c0, tq0 + a.in_off + tap * a.dil, b, &full[s]);
+      tma_load_2d(st + L::kA, &c.tw, c0, (phase * a.taps + tap) * a.Cout + n0, &full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {  // MMA issuer
+    constexpr uint32_t idesc = umma_idesc_f16(128, N);
+    for (int ks = 0; ks < KS; ks++) {
+      const int s = ks % S;
+      if (!mbar_wait(&full[s], (ks / S) & 1)) {
+        err |= 2u;
+        break;
+      }
+      tc_fence_after();
+      const unsigned char *st = sm + s * L::kStage;
+#pragma unroll
+      for (int kk = 0; kk < ACH / 16; kk++) {
+        const uint64_t ad = ACH == 64 ? sw128_desc(st + kk * 32) : sw64_desc(st + kk * 32);
+        const uint64_t bd = ACH == 64 ? sw128_desc(st + L::kA + kk * 32) : sw64_desc(st + L::kA + kk * 32);
+        umma_kf16(tmem, ad, bd, idesc, (ks | kk) != 0 ? 1u : 0u);
+      }
+      umma_commit(&empty[s]);
+    }
+    umma_commit(accb);
+  }
+  __syncwarp();
+  if (!mbar_wait(accb, 0)) err |= 4u;
+  __syncwarp();  // tcgen05.ld below is warp-collective
+  tc_fence_after();
+  const int tq = tq0 + 32 * warp + lane;
+  const bool valid = tq < a.Lq;
+  const size_t orow = (size_t)b * a.Lout + (size_t)tq * a.ostride + phase;
+  const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+#pragma unroll 1
+  for (int cc = 0; cc < N; cc += 16) {
+    float v[16];
+    tmem_ld16(trow + cc, v);
+    if (valid) conv_epilogue16(a, orow, n0 + cc, v);
+  }
+  if (err && c.err) atomicOr(c.err, (int)err);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kCols);
+}
+
+static int *g_conv_err = nullptr;  // device word for bounded-wait timeouts of k_conv_tc
+
+template <int N, int ACH, int S>
+static void conv_tc_launch(const ConvArgs &a, int phases, cudaStream_t st) {
+  using L = ConvTcSmem<N, ACH, S>;
+  static bool attr = false;
+  if (!attr) {
+    CK(cudaFuncSetAttribute(k_conv_tc<N, ACH, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kBytes));
+    attr = true;
+  }
+  ConvTc c;
+  memset(&c, 0, sizeof c);
+  const CUtensorMapSwizzle sw = ACH == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  {
+    const uint64_t dims[3] = {(uint64_t)a.Cin, (uint64_t)a.Lin, (uint64_t)a.B};
+    const uint64_t strides[2] = {(uint64_t)a.Cin * 2, (uint64_t)a.Lin * a.Cin * 2};
+    const uint32_t box[3] = {(uint32_t)ACH, 128, 1};
+    if (!make_tmap(&c.tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, a.X, dims, strides, box, sw))
+      FAIL(Q3T_CUDA_ERROR, "codec conv: TMA descriptor of the input failed");
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)a.Cin, (uint64_t)phases * a.taps * a.Cout};
+    const uint64_t strides[1] = {(uint64_t)a.Cin * 2};
+    const uint32_t box[2] = {(uint32_t)ACH, (uint32_t)N};
+    if (!make_tmap(&c.tw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.W, dims, strides, box, sw))
+      FAIL(Q3T_CUDA_ERROR, "codec conv: TMA descriptor of the weights failed");
+  }
+  c.a = a;
+  c.tiles = (a.Lq + 127) / 128;
+  c.err = g_conv_err;
+  const dim3 grid((unsigned)(a.B * c.tiles), a.Cout / N, phases);
+  k_conv_tc<N, ACH, S><<<grid, 128, L::kBytes, st>>>(c);
+}
+
 static void launch_conv(const ConvArgs &a, int phases, cudaStream_t st) {
   const int M = a.B * a.Lq;
   if (M <= 0) return;
-  if (a.Cout % 128 == 0) {
+  if (!g_conv_err) CK(cudaMalloc(&g_conv_err, sizeof(int)));
+  const bool tc = a.Cin % 32 == 0 && (a.Cout % 128 == 0 || a.Cout % 96 == 0) && !getenv("Q3T_CONV_MMA_SYNC");
+  if (tc) {
+    const bool wide = a.Cin % 64 == 0, n128 = a.Cout % 128 == 0;
+    if (wide && n128)
+      conv_tc_launch<128, 64, 3>(a, phases, st);
+    else if (wide)
+      conv_tc_launch<96, 64, 3>(a, phases, st);
+    else if (n128)
+      conv_tc_launch<128, 32, 6>(a, phases, st);
+    else
+      conv_tc_launch<96, 32, 6>(a, phases, st);
+  } else if (a.Cout % 128 == 0) {
     dim3 grid((M + kBM - 1) / kBM, a.Cout / 128, phases);
     k_conv<128><<<grid, 256, conv_smem(128), st>>>(a);
   } else if (a.Cout % 96 == 0) {

@@ -570,7 +570,7 @@ struct ProgBuilder {
   void stack(const LMStack &S, KVView kv, TokView tv, int max_tok, int max_units, int pw) {
     const auto &c = S.cfg;
     const int H = c.hidden_size, I = c.intermediate_size, nh = c.num_attention_heads, nkv = c.num_key_value_heads;
-    const int NQ = (nh + 2 * nkv) * 128, QD = nh * 128;
+    const int QD = nh * 128;
     const float eps = c.rms_norm_eps;
     for (int l = 0; l < c.num_hidden_layers; l++) {
       GemmArgs q = gemm_args(S.qkv[l], tv.ntok, max_tok);

@@ -318,12 +318,13 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
 #pragma unroll
     for (int s = 0; s < KA * 4; s++) {
       const int at = s >> 2, off = (s & 3) * 32;
-      umma_bf16(tmem, sw128_desc(wsm + at * 16384 + off), sw128_desc(xsm + at * L::kXAtom + off), idesc,
+      umma_kf16(tmem, sw128_desc(wsm + at * 16384 + off), sw128_desc(xsm + at * L::kXAtom + off), idesc,
                 s > 0 ? 1u : 0u);
     }
     umma_commit(&bars[2]);
   }
   if (!mbar_wait(&bars[2], 0)) err |= 4u;
+  __syncwarp();  // tcgen05.ld below is warp-collective
   tc_fence_after();
   if (warp < 4) {  // accumulator lane = output row, column = token
     const uint32_t tq = tmem + ((uint32_t)(32 * warp) << 16);
@@ -450,8 +451,8 @@ static void gemm_attrs() {
 
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
 
-bool make_tmap_bf16(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, uint64_t row_bytes,
-                    uint32_t box_inner, uint32_t box_rows) {
+bool make_tmap(CUtensorMap *m, CUtensorMapDataType type, int rank, const void *base, const uint64_t *dims,
+               const uint64_t *strides, const uint32_t *box, CUtensorMapSwizzle swizzle) {
   if (!g_encode_tiled) {
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void **>(&g_encode_tiled),
@@ -459,13 +460,23 @@ bool make_tmap_bf16(CUtensorMap *m, const void *base, uint64_t inner, uint64_t r
         q != cudaDriverEntryPointSuccess)
       return false;
   }
-  cuuint64_t dims[2] = {inner, rows};
-  cuuint64_t strides[1] = {row_bytes};
-  cuuint32_t box[2] = {box_inner, box_rows};
-  cuuint32_t es[2] = {1, 1};
-  return g_encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; i++) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) st[i] = strides[i];
+  }
+  return g_encode_tiled(m, type, rank, const_cast<void *>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_tmap_bf16(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                    uint32_t box_inner, uint32_t box_rows) {
+  const uint64_t dims[2] = {inner, rows}, strides[1] = {row_bytes};
+  const uint32_t box[2] = {box_inner, box_rows};
+  return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 struct BlockSync {

@@ -128,6 +128,9 @@ struct Linear {
 // row_bytes) with boxes of box_inner x box_rows, SWIZZLE_128B; false on error.
 bool make_tmap_bf16(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, uint64_t row_bytes,
                     uint32_t box_inner, uint32_t box_rows);
+// General form: rank dims (innermost first), rank - 1 byte strides.
+bool make_tmap(CUtensorMap *m, CUtensorMapDataType type, int rank, const void *base, const uint64_t *dims,
+               const uint64_t *strides, const uint32_t *box, CUtensorMapSwizzle swizzle);
 
 struct GemmArgs {
   CUtensorMap tw;      // weights W [N][K] (Linear::tm)

@@ -65,9 +65,9 @@ Q3T_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 Q3T_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 Q3T_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, bf16 inputs, f32 accumulate;
-// one thread issues it.
-Q3T_DEV void umma_bf16(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (fp16 or bf16 inputs
+// as the instruction descriptor says), f32 accumulate; one thread issues it.
+Q3T_DEV void umma_kf16(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
   const uint32_t mask = 0u;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
@@ -80,6 +80,29 @@ Q3T_DEV void umma_bf16(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t ides
 Q3T_DEV void umma_commit(uint64_t *bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
                : "memory");
+}
+
+// 3-D TMA tile load (x innermost); out-of-range coordinates read zeros
+Q3T_DEV void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          smem_addr(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// 32 TMEM lanes x 16 consecutive f32 columns
+Q3T_DEV void tmem_ld16(uint32_t taddr, float *v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
 // 32 TMEM lanes (one per thread of the warp) x 8 consecutive f32 columns
@@ -104,6 +127,19 @@ Q3T_DEV uint64_t sw128_desc(const void *p) {
          | ((uint64_t)(1024 >> 4) << 32)   // stride byte offset: 8 rows x 128 B
          | (1ull << 46)                    // descriptor version (Blackwell)
          | (2ull << 61);                   // SWIZZLE_128B
+}
+
+// The same for a K-major SWIZZLE_64B operand: rows of 32 16-bit elements
+// (64 bytes), 8-row groups 512 bytes apart, 512-byte-aligned atoms.
+Q3T_DEV uint64_t sw64_desc(const void *p) {
+  const uint64_t a = smem_addr(p);
+  return ((a & 0x3FFFFull) >> 4) | (1ull << 16) | ((uint64_t)(512 >> 4) << 32) | (1ull << 46) | (4ull << 61);
+}
+
+// Instruction descriptor of tcgen05.mma kind::f16 with fp16 A and B (both
+// K-major), f32 D, M x N.
+constexpr uint32_t umma_idesc_f16(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 // Instruction descriptor of tcgen05.mma kind::f16: bf16 A and B (both
