@@ -202,6 +202,9 @@ def main():
     t0 = time.perf_counter()
     steps = [b.step() for _ in range(args.steps)]
     e1.record(stream)
+    if os.environ.get("Q3T_BENCH_STEP_LOG"):
+        with open(os.environ["Q3T_BENCH_STEP_LOG"], "w") as f:
+            json.dump(steps, f)
     barrier()
     if args.profile:
         torch.cuda.profiler.stop()

@@ -213,8 +213,10 @@ static size_t conv_smem(int BN) { return (size_t)kStages * (kBM + BN) * kLDS * s
 //                  n0+N)[c0..c0+ACH) into a ring of S stages;
 //   warp 1 lane 0  issues tcgen05.mma (M = 128, N, K = 16) into a TMEM
 //                  accumulator and releases each stage with tcgen05.commit;
-//   all 4 warps    read the accumulator back (thread = output step, 16
-//                  channels per tcgen05.ld) and run the k_conv epilogue.
+//   warps 0..3     read the accumulator back (thread = output step, 16
+//                  channels per tcgen05.ld) into an f32 tile in shared memory;
+//   all 8 warps    then sweep the tile row-major (coalesced) through the
+//                  k_conv epilogue.
 // Operands are K-major with SWIZZLE_128B (ACH = 64) or SWIZZLE_64B (ACH = 32)
 // atoms.  Every mbarrier wait is bounded; a timeout sets a bit in *err.
 // ---------------------------------------------------------------------------
@@ -232,53 +234,8 @@ struct ConvTcSmem {
   static constexpr size_t kBytes = (size_t)S * kStage + (2 * S + 2) * 8 + 1024;
 };
 
-Q3T_DEV void conv_epilogue16(const ConvArgs &a, size_t orow, int n, const float *v) {
-  float y[16];
-#pragma unroll
-  for (int j = 0; j < 16; j++) {
-    float t = v[j];
-    if (a.bias) t += a.bias[n + j];
-    if (a.scale) t *= a.scale[n + j];
-    y[j] = t;
-  }
-  const size_t e = orow * a.Cout + n;
-  if (a.R) {
-#pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const float4 r = *reinterpret_cast<const float4 *>(a.R + e + 4 * q);
-      y[4 * q] += r.x;
-      y[4 * q + 1] += r.y;
-      y[4 * q + 2] += r.z;
-      y[4 * q + 3] += r.w;
-    }
-  }
-  if (a.Yf) {
-#pragma unroll
-    for (int q = 0; q < 4; q++)
-      *reinterpret_cast<float4 *>(a.Yf + e + 4 * q) = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
-  }
-  if (a.Yh) {
-    __half2 h[8];
-#pragma unroll
-    for (int j = 0; j < 16; j += 2) {
-      float h0 = y[j], h1 = y[j + 1];
-      if (a.act == ACT_SNAKE) {
-        h0 = snake(h0, a.act_a[n + j], a.act_b[n + j]);
-        h1 = snake(h1, a.act_a[n + j + 1], a.act_b[n + j + 1]);
-      } else if (a.act == ACT_GELU) {
-        h0 = gelu_erf(h0);
-        h1 = gelu_erf(h1);
-      }
-      h[j / 2] = __floats2half2_rn(h0, h1);
-    }
-    uint4 *dst = reinterpret_cast<uint4 *>(a.Yh + e);
-    dst[0] = *reinterpret_cast<const uint4 *>(&h[0]);
-    dst[1] = *reinterpret_cast<const uint4 *>(&h[4]);
-  }
-}
-
 template <int N, int ACH, int S>
-__global__ void __launch_bounds__(128) k_conv_tc(const __grid_constant__ ConvTc c) {
+__global__ void __launch_bounds__(256) k_conv_tc(const __grid_constant__ ConvTc c) {
   using L = ConvTcSmem<N, ACH, S>;
   constexpr uint32_t kCols = N <= 128 ? 128 : 256;
   extern __shared__ unsigned char csm_raw[];
@@ -336,20 +293,88 @@ __global__ void __launch_bounds__(128) k_conv_tc(const __grid_constant__ ConvTc 
       umma_commit(&empty[s]);
     }
     umma_commit(accb);
+    if (!mbar_wait(accb, 0)) err |= 4u;  // the other threads block in the barrier below, not polling
   }
-  __syncwarp();
-  if (!mbar_wait(accb, 0)) err |= 4u;
-  __syncwarp();  // tcgen05.ld below is warp-collective
+  tc_fence_before();
+  __syncthreads();
   tc_fence_after();
-  const int tq = tq0 + 32 * warp + lane;
-  const bool valid = tq < a.Lq;
-  const size_t orow = (size_t)b * a.Lout + (size_t)tq * a.ostride + phase;
-  const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+  // accumulator -> f32 tile [128 steps][N + 4] over the (drained) stage ring
+  constexpr int TP = N + 4;
+  float *tile = reinterpret_cast<float *>(sm);
+  if (warp < 4) {
+    const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+    float *dst = tile + (32 * warp + lane) * TP;
 #pragma unroll 1
-  for (int cc = 0; cc < N; cc += 16) {
-    float v[16];
-    tmem_ld16(trow + cc, v);
-    if (valid) conv_epilogue16(a, orow, n0 + cc, v);
+    for (int cc = 0; cc < N; cc += 16) {
+      float v[16];
+      tmem_ld16(trow + cc, v);
+#pragma unroll
+      for (int j = 0; j < 16; j++) dst[cc + j] = v[j];
+    }
+  }
+  __syncthreads();
+  // row-major sweep by all 8 warps: consecutive threads take consecutive
+  // 4-channel groups of a row, UN groups in flight per thread
+  constexpr int G4 = N / 4, UN = 4, NTH = 256;
+  const int rows = min(128, a.Lq - tq0);
+  const int total = rows * G4;
+  const size_t base0 = (size_t)b * a.Lout + phase;
+  for (int f0 = threadIdx.x; f0 < total; f0 += NTH * UN) {
+    float4 v[UN], r[UN];
+    size_t e[UN];
+    int nn[UN];
+#pragma unroll
+    for (int u = 0; u < UN; u++) {
+      const int f = f0 + NTH * u;
+      const int ff = f < total ? f : 0, row = ff / G4, c4 = ff - row * G4;
+      nn[u] = f < total ? n0 + 4 * c4 : -1;
+      v[u] = *reinterpret_cast<const float4 *>(tile + row * TP + 4 * c4);
+      e[u] = (base0 + (size_t)(tq0 + row) * a.ostride) * a.Cout + n0 + 4 * c4;
+      if (nn[u] >= 0 && a.R) r[u] = *reinterpret_cast<const float4 *>(a.R + e[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < UN; u++) {
+      const int n = nn[u];
+      if (n < 0) continue;
+      float y[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      if (a.bias) {
+        const float4 bb = *reinterpret_cast<const float4 *>(a.bias + n);
+        y[0] += bb.x;
+        y[1] += bb.y;
+        y[2] += bb.z;
+        y[3] += bb.w;
+      }
+      if (a.scale) {
+        const float4 sc = *reinterpret_cast<const float4 *>(a.scale + n);
+        y[0] *= sc.x;
+        y[1] *= sc.y;
+        y[2] *= sc.z;
+        y[3] *= sc.w;
+      }
+      if (a.R) {
+        y[0] += r[u].x;
+        y[1] += r[u].y;
+        y[2] += r[u].z;
+        y[3] += r[u].w;
+      }
+      if (a.Yf) *reinterpret_cast<float4 *>(a.Yf + e[u]) = make_float4(y[0], y[1], y[2], y[3]);
+      if (a.Yh) {
+        float h[4] = {y[0], y[1], y[2], y[3]};
+        if (a.act == ACT_SNAKE) {
+          const float4 ea = *reinterpret_cast<const float4 *>(a.act_a + n);
+          const float4 ib = *reinterpret_cast<const float4 *>(a.act_b + n);
+          h[0] = snake(y[0], ea.x, ib.x);
+          h[1] = snake(y[1], ea.y, ib.y);
+          h[2] = snake(y[2], ea.z, ib.z);
+          h[3] = snake(y[3], ea.w, ib.w);
+        } else if (a.act == ACT_GELU) {
+#pragma unroll
+          for (int j = 0; j < 4; j++) h[j] = gelu_erf(y[j]);
+        }
+        __half2 p[2] = {__floats2half2_rn(h[0], h[1]), __floats2half2_rn(h[2], h[3])};
+        *reinterpret_cast<uint2 *>(a.Yh + e[u]) = *reinterpret_cast<const uint2 *>(p);
+      }
+    }
   }
   if (err && c.err) atomicOr(c.err, (int)err);
   tc_fence_before();
@@ -388,7 +413,7 @@ static void conv_tc_launch(const ConvArgs &a, int phases, cudaStream_t st) {
   c.tiles = (a.Lq + 127) / 128;
   c.err = g_conv_err;
   const dim3 grid((unsigned)(a.B * c.tiles), a.Cout / N, phases);
-  k_conv_tc<N, ACH, S><<<grid, 128, L::kBytes, st>>>(c);
+  k_conv_tc<N, ACH, S><<<grid, 256, L::kBytes, st>>>(c);
 }
 
 static void launch_conv(const ConvArgs &a, int phases, cudaStream_t st) {
@@ -572,28 +597,34 @@ __global__ void __launch_bounds__(256) k_dwconv_ln(const float *y, int L, int C,
 }
 
 // output conv C -> 1, k7, causal, + clamp (decoder.rs:273-276) and PCM
-// (codec/infer/mod.rs:80-90); rows [t0 - 6, t0 + 256) staged in shared memory
+// (codec/infer/mod.rs:80-90); rows [t0 - 6, t0 + kOutTile) staged in shared
+// memory with a row pitch of C + 2 halves (an odd number of 4-byte words, so
+// the 32 threads of a warp, one row each, read 32 different banks).
 constexpr int kOutTile = 128;
 __global__ void __launch_bounds__(kOutTile) k_out_conv(const __half *a, int L, int C, const float *w, float bias,
                                                        float *wave, int16_t *pcm) {
   extern __shared__ __half tile[];
   __shared__ float ws[7 * 192];
-  const int b = blockIdx.y, t0 = blockIdx.x * kOutTile;
+  const int b = blockIdx.y, t0 = blockIdx.x * kOutTile, cp = C + 2;
   for (int e = threadIdx.x; e < 7 * C; e += blockDim.x) ws[e] = w[e];
-  const int rows = kOutTile + 6;
-  for (int e = threadIdx.x; e < rows * C / 2; e += blockDim.x) {
-    const int r = e / (C / 2), c2 = e - r * (C / 2);
+  const int rows = kOutTile + 6, c8n = C / 8;
+  for (int e = threadIdx.x; e < rows * c8n; e += blockDim.x) {
+    const int r = e / c8n, c8 = e - r * c8n;
     const int tt = t0 - 6 + r;
-    __half2 v = __floats2half2_rn(0.f, 0.f);
-    if (tt >= 0 && tt < L) v = *reinterpret_cast<const __half2 *>(a + ((size_t)b * L + tt) * C + 2 * c2);
-    reinterpret_cast<__half2 *>(tile)[e] = v;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (tt >= 0 && tt < L) v = *reinterpret_cast<const uint4 *>(a + ((size_t)b * L + tt) * C + 8 * c8);
+    uint32_t *d = reinterpret_cast<uint32_t *>(tile + (size_t)r * cp + 8 * c8);
+    d[0] = v.x;
+    d[1] = v.y;
+    d[2] = v.z;
+    d[3] = v.w;
   }
   __syncthreads();
   const int t = t0 + threadIdx.x;
   if (t >= L) return;
   float acc = bias;
   for (int j = 0; j < 7; j++) {
-    const __half *row = tile + (size_t)(threadIdx.x + j) * C;
+    const __half *row = tile + (size_t)(threadIdx.x + j) * cp;
     for (int c = 0; c < C; c += 2) {
       const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(row + c));
       acc += f.x * ws[j * C + c] + f.y * ws[j * C + c + 1];
@@ -1104,9 +1135,10 @@ static void decode_with(CodecModel *c, const CodecScratch &ws, const int64_t *d_
     }
   }
   const int C = c->stages.back().cout;
+  if (C % 8 || C > 192) FAIL(Q3T_INVALID_INPUT, "codec output conv: %d channels (multiple of 8, <= 192 supported)", C);
   {
     dim3 grid((Lc + kOutTile - 1) / kOutTile, B);
-    const size_t sm = (size_t)(kOutTile + 6) * C * sizeof(__half);
+    const size_t sm = (size_t)(kOutTile + 6) * (C + 2) * sizeof(__half);
     k_out_conv<<<grid, kOutTile, sm, st>>>(act, Lc, C, c->out_w, c->out_b, d_wave, d_pcm);
     CK(cudaGetLastError());
     g_launches++;
@@ -1222,7 +1254,36 @@ struct StreamState {
 };
 static std::map<q3t_batch *, StreamState> g_streams;
 
-void codec_stream_init(q3t_model *, q3t_batch *b) { g_streams[b] = StreamState{}; }
+// Sizes the window buffers for max_active windows of left_context +
+// chunk_frames frames and runs one decode of each window length the stream
+// uses (chunk_frames for a request's first window, left_context +
+// chunk_frames after), so the stream-ordered workspace pool and the kernels
+// are set up before the first chunk is due rather than inside a step.
+void codec_stream_init(q3t_model *m, q3t_batch *b) {
+  StreamState S;
+  CodecModel *c = m->codec;
+  const int chunk = std::max(1, b->desc.chunk_frames), ctx = std::max(0, b->desc.left_context);
+  const int Bw = std::max(1, b->A), nq = c->c.num_quantizers;
+  for (int Tw : {chunk, chunk + ctx}) {
+    int64_t nout = 0;
+    codec_out_len(c, Tw, &nout);
+    if (nout <= 0) continue;
+    if (S.codes_cap < (size_t)Bw * nq * Tw) {
+      if (S.d_codes) cudaFree(S.d_codes);
+      S.codes_cap = (size_t)Bw * nq * Tw;
+      CK(cudaMalloc(&S.d_codes, S.codes_cap * 8));
+    }
+    if (S.wave_cap < (size_t)Bw * nout) {
+      if (S.d_wave) cudaFree(S.d_wave);
+      S.wave_cap = (size_t)Bw * nout;
+      CK(cudaMalloc(&S.d_wave, S.wave_cap * 4));
+    }
+    CK(cudaMemsetAsync(S.d_codes, 0, (size_t)Bw * nq * Tw * 8, b->st));
+    decode_device(c, S.d_codes, Bw, Tw, S.d_wave, nullptr, b->st);
+  }
+  CK(cudaStreamSynchronize(b->st));
+  g_streams[b] = S;
+}
 
 void codec_stream_free(q3t_batch *b) {
   auto it = g_streams.find(b);

@@ -1044,7 +1044,6 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
     report();
     return;
   }
-  int maxlen = 1;
   int *hm = b->h_meta;
   for (int i = 0; i < B; i++) {
     Req *r = act[i];
@@ -1061,7 +1060,6 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
     hm[b->off_p0pos() + 2 * i] = 0;
     hm[b->off_p0pos() + 2 * i + 1] = 1;
     b->h_extra[i] = r->step_idx < r->trailing_len ? r->d_trailing + (size_t)r->step_idx * b->H : r->d_pad;
-    maxlen = std::max(maxlen, r->cache_len + 1);
     S.kv_tokens += r->cache_len + 1;
   }
   hm[M_NTOK_B] = B;
@@ -1070,7 +1068,9 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
   hm[M_SEED] = b->step_counter++;
   CK(cudaMemcpyAsync(b->d_meta, hm, b->meta_n * sizeof(int), cudaMemcpyHostToDevice, b->st));
   CK(cudaMemcpyAsync(b->d_extra, b->h_extra, B * sizeof(float *), cudaMemcpyHostToDevice, b->st));
-  const int mt = bucket_tok(B), ms = bucket_units(maxlen, attn_pw(mt));
+  // the attention's unit bound only sizes its (persistent) grid, so the frame
+  // graph uses the largest and is captured once per token bucket
+  const int mt = bucket_tok(B), ms = kAttnMaxUnits;
   b->h2d += b->meta_n * sizeof(int) + B * sizeof(float *);
   enqueue_frame(b, mt, ms);
   CK(cudaMemcpyAsync(b->h_eosflag, b->d_eosflag, B * sizeof(int), cudaMemcpyDeviceToHost, b->st));

@@ -322,9 +322,10 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
                 s > 0 ? 1u : 0u);
     }
     umma_commit(&bars[2]);
+    if (!mbar_wait(&bars[2], 0)) err |= 4u;  // the other threads block in the barrier below, not polling
   }
-  if (!mbar_wait(&bars[2], 0)) err |= 4u;
-  __syncwarp();  // tcgen05.ld below is warp-collective
+  tc_fence_before();
+  __syncthreads();
   tc_fence_after();
   if (warp < 4) {  // accumulator lane = output row, column = token
     const uint32_t tq = tmem + ((uint32_t)(32 * warp) << 16);
