@@ -28,6 +28,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "tts-rs_b200"))
 
+import dp  # noqa: E402
 import synthetic as S  # noqa: E402
 
 FRAME_S = 0.08          # one frame = 1920 samples at 24 kHz
@@ -162,7 +163,7 @@ def main():
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     torch.cuda.set_device(local)
     import q3t
 
@@ -171,7 +172,7 @@ def main():
     model = q3t.Model(cfg, S.make_talker_weights(cfg, 0), cc, S.make_codec_weights(cc, 0), device=local,
                       kv_pages=args.kv_pages, max_active=args.max_active)
     reqs = workload(args.requests)
-    mine = [i for i in range(len(reqs)) if i % world == rank]
+    mine = dp.partition(len(reqs), rank, world)
     inputs = {i: request_inputs(i, *reqs[i]) for i in mine}
 
     def submit(b, i):
@@ -250,26 +251,13 @@ def main():
                "d2h_bytes_per_step": int(np.mean([s["d2h_bytes"] for s in st2])),
                "_samples": e2e_samples, "_wall": wall2}
 
-    # ---------------- reduce over ranks --------------------------------------
-    def reduce(v, op):
-        if not dist:
-            return v
-        t = torch.tensor([float(v)], device="cuda")
-        dist.all_reduce(t, op=op)
-        return t.item()
-
-    if dist:
-        from torch.distributed import ReduceOp
-        tot_samples = reduce(samples, ReduceOp.SUM)
-        tot_frames = reduce(frames, ReduceOp.SUM)
-        max_dev = reduce(dev_s, ReduceOp.MAX)
-        if e2e:
-            e2e_tot = reduce(e2e["_samples"], ReduceOp.SUM)
-            e2e_wall = reduce(e2e["_wall"], ReduceOp.MAX)
-    else:
-        tot_samples, tot_frames, max_dev = samples, frames, dev_s
-        if e2e:
-            e2e_tot, e2e_wall = e2e["_samples"], e2e["_wall"]
+    # ---------------- reduce over ranks (the one collective) -----------------
+    red = dp.reduce_stats({"samples": (samples, "sum"), "frames": (frames, "sum"), "dev_s": (dev_s, "max"),
+                           "e2e_samples": (e2e["_samples"] if e2e else 0, "sum"),
+                           "e2e_wall": (e2e["_wall"] if e2e else 0.0, "max")},
+                          device="cuda" if dist else "cpu")
+    tot_samples, tot_frames, max_dev = red["samples"], red["frames"], red["dev_s"]
+    e2e_tot, e2e_wall = red["e2e_samples"], red["e2e_wall"]
     value = tot_samples / SAMPLE_RATE / max_dev
     if e2e:
         e2e["value"] = round(e2e_tot / SAMPLE_RATE / e2e_wall, 3)

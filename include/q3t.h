@@ -115,7 +115,8 @@ typedef struct {
 typedef struct q3t_model q3t_model;
 
 /* Replaces loading/runtime.rs:131-156 (safetensors -> Burn with the bf16
- * load-time cast): copies and packs every tensor into device memory. */
+ * load-time cast): copies every tensor into device memory (bf16 for the
+ * linears, with their TMA descriptors; f32 for norms and codec tables). */
 q3t_status q3t_model_load(const q3t_model_desc *desc, q3t_model **out);
 void q3t_model_free(q3t_model *model);
 
