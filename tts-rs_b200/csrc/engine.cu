@@ -456,7 +456,7 @@ static int bucket_tok(int B) {
 }
 // minimum pages per attention work unit: larger with more tokens in the
 // batch, so that the units stay a few waves deep at every batch size
-static int attn_pw(int max_tok) { return max_tok >= 32 ? 4 : max_tok >= 8 ? 2 : 1; }
+static int attn_pw(int max_tok) { return max_tok >= 32 ? 8 : max_tok >= 8 ? 2 : 1; }
 // attention units per (token, head) for kv length L, rounded up to a power of
 // two (it keys the CUDA graphs); the device uses the same page split
 static int bucket_units(int L, int pw) {

@@ -194,9 +194,9 @@ struct AttnSmem {
 // loads (8 rows of one chunk) hit distinct banks.  Rows at or beyond the
 // valid key count are zero-filled (the pool may hold stale or uninitialised
 // values there).
-constexpr int kAttnStages = 3;
+constexpr int kAttnStages = 2;
 constexpr int kPageElems = 16 * 128;
-constexpr size_t kAttnDynSmem = (size_t)kAttnWarps * kAttnStages * 2 * kPageElems * 2;  // 96 KB
+constexpr size_t kAttnDynSmem = (size_t)kAttnWarps * kAttnStages * 2 * kPageElems * 2;  // 64 KB
 
 Q3T_DEV void issue_page(uint16_t *ks, uint16_t *vs, const uint16_t *kp, const uint16_t *vp, int nv, int lane) {
 #pragma unroll
@@ -220,16 +220,18 @@ struct AttnAcc {
 Q3T_DEV void attn_page(AttnAcc &A, const uint16_t *ks, const uint16_t *vs, const uint4 *qf, int nv, float scale,
                        float (*ps)[16], int lane) {
   const int g = lane >> 2, t = lane & 3;
-  // S^T = K Q^T on the tensor cores
-  float c[4] = {0.f, 0.f, 0.f, 0.f};
+  // S^T = K Q^T on the tensor cores (two accumulators halve the dependent chain)
+  float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int q = 0; q < 4; q++) {
     const int ch = ((t + 4 * q) ^ g) << 3;  // rows g and g + 8 share the swizzle
     const uint4 k0 = *reinterpret_cast<const uint4 *>(ks + g * 128 + ch);
     const uint4 k1 = *reinterpret_cast<const uint4 *>(ks + (g + 8) * 128 + ch);
     mma_16816(c, k0.x, k1.x, k0.y, k1.y, qf[q].x, qf[q].y);
-    mma_16816(c, k0.z, k1.z, k0.w, k1.w, qf[q].z, qf[q].w);
+    mma_16816(c2, k0.z, k1.z, k0.w, k1.w, qf[q].z, qf[q].w);
   }
+#pragma unroll
+  for (int i = 0; i < 4; i++) c[i] += c2[i];
   // c0/c1 = key g, heads 0/1; c2/c3 = key g + 8 (valid on lanes t == 0)
   const bool ok0 = t == 0 && g < nv, ok1 = t == 0 && g + 8 < nv;
   const float s00 = ok0 ? c[0] * scale : -FLT_MAX, s01 = ok0 ? c[1] * scale : -FLT_MAX;

@@ -484,7 +484,7 @@ struct BlockSync {
   __device__ void operator()() const { __syncthreads(); }
 };
 
-__global__ void __launch_bounds__(128, 2) k_attn(AttnArgs a) {
+__global__ void __launch_bounds__(128, 3) k_attn(AttnArgs a) {
   __shared__ AttnSmem S;
   extern __shared__ __align__(16) uint16_t attn_ring[];
   pdl_wait();
