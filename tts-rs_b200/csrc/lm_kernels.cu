@@ -185,14 +185,16 @@ Q3T_DEV void store_bf16x4(uint16_t *dst, float a, float b, float c, float d) {
 }
 
 // rows rg*128 + 4*lane .. +3 of token t (warp-wide: the norms reduce over the
-// warp); tm = {position, page} of t for GE_QKV
-Q3T_DEV void gemm_epilogue(const GemmArgs &a, int t, int rg, int lane, float4 v, const int *tm) {
+// warp); tm = {position, page} of t for GE_QKV; xpre = the residual rows
+// already loaded for GE_RESID when have_pre
+Q3T_DEV void gemm_epilogue(const GemmArgs &a, int t, int rg, int lane, float4 v, const int *tm, float4 xpre,
+                           bool have_pre) {
   const int n = rg * 128 + lane * 4;
   if (a.epi == GE_F32) {
     *reinterpret_cast<float4 *>(a.y + (size_t)t * a.ldy + n) = v;
   } else if (a.epi == GE_RESID) {
     float4 *xp = reinterpret_cast<float4 *>(a.y + (size_t)t * a.ldy + n);
-    float4 x = *xp;
+    float4 x = have_pre ? xpre : *xp;
     x.x += v.x;
     x.y += v.y;
     x.z += v.z;
@@ -269,6 +271,16 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
     meta[2 * threadIdx.x] = pos;
     meta[2 * threadIdx.x + 1] = a.kv.page_table[(size_t)a.tv.seq[t] * a.kv.pt_stride + (pos >> 4)];
   }
+  // GE_RESID: the residual rows of this warp's first two epilogue tokens,
+  // loaded now (they are final once the previous kernel completed)
+  float4 xres[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  if (a.epi == GE_RESID) {
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      const int tt = t_lo + warp + 8 * i;
+      if (tt < t_hi) xres[i] = *reinterpret_cast<const float4 *>(a.y + (size_t)(tok0 + tt) * a.ldy + rg * 128 + lane * 4);
+    }
+  }
   if (a.xmode == GX_BF16) {
     if (threadIdx.x == 0) {
       mbar_expect_tx(&bars[1], L::kX);
@@ -287,24 +299,41 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
       rms[r] = 1.f / sqrtf(s / (float)a.K + a.eps);
     }
     __syncthreads();
-    // one 8-column chunk per thread and step: x * (1 / rms) * gamma -> bf16,
-    // stored at chunk (c ^ (row & 7)) of the row's 128-byte atom line
-    constexpr int c8n = KC / 8;
-    for (int idx = threadIdx.x; idx < N * c8n; idx += blockDim.x) {
-      const int r = idx / c8n, c8 = idx - r * c8n;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (r < ntok) {
-        const float *xr = a.x + (size_t)((tok0 + r) * a.xrow_mul + a.xrow_add) * a.ldx + k0 + c8 * 8;
-        const float4 x0 = *reinterpret_cast<const float4 *>(xr), x1 = *reinterpret_cast<const float4 *>(xr + 4);
-        const float4 g0 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8 * 8);
-        const float4 g1 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8 * 8 + 4);
-        const float d = rms[r];
-        v.x = pack_bf16x2(x0.x * d * g0.x, x0.y * d * g0.y);
-        v.y = pack_bf16x2(x0.z * d * g0.z, x0.w * d * g0.w);
-        v.z = pack_bf16x2(x1.x * d * g1.x, x1.y * d * g1.y);
-        v.w = pack_bf16x2(x1.z * d * g1.z, x1.w * d * g1.w);
+    // 8-column chunks: x * (1 / rms) * gamma -> bf16, stored at chunk
+    // (c ^ (row & 7)) of the row's 128-byte atom line.  A thread keeps one
+    // chunk column (gamma in registers) and takes its rows four at a time
+    // with all loads of a batch in flight together.
+    constexpr int c8n = KC / 8, rstep = 256 / c8n;  // c8n is 16, 32 or 48
+    const int c8 = threadIdx.x % c8n, r0 = threadIdx.x / c8n;
+    if (r0 < rstep) {
+      const float4 g0 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8 * 8);
+      const float4 g1 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8 * 8 + 4);
+      for (int rb = r0; rb < N; rb += 4 * rstep) {
+        float4 xv[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const int r = rb + i * rstep;
+          if (r < ntok) {
+            const float *xr = a.x + (size_t)((tok0 + r) * a.xrow_mul + a.xrow_add) * a.ldx + k0 + c8 * 8;
+            xv[i][0] = *reinterpret_cast<const float4 *>(xr);
+            xv[i][1] = *reinterpret_cast<const float4 *>(xr + 4);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const int r = rb + i * rstep;
+          if (r >= N) break;
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (r < ntok) {
+            const float d = rms[r];
+            v.x = pack_bf16x2(xv[i][0].x * d * g0.x, xv[i][0].y * d * g0.y);
+            v.y = pack_bf16x2(xv[i][0].z * d * g0.z, xv[i][0].w * d * g0.w);
+            v.z = pack_bf16x2(xv[i][1].x * d * g1.x, xv[i][1].y * d * g1.y);
+            v.w = pack_bf16x2(xv[i][1].z * d * g1.z, xv[i][1].w * d * g1.w);
+          }
+          *reinterpret_cast<uint4 *>(xsm + (c8 >> 3) * L::kXAtom + r * 128 + (((c8 & 7) ^ (r & 7)) << 4)) = v;
+        }
       }
-      *reinterpret_cast<uint4 *>(xsm + (c8 >> 3) * L::kXAtom + r * 128 + (((c8 & 7) ^ (r & 7)) << 4)) = v;
     }
     fence_proxy_async();
   }
@@ -364,7 +393,8 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
           v.w += p[c].w;
         }
     }
-    gemm_epilogue(a, tok0 + tt, rg, lane, v, meta + 2 * (tt - t_lo));
+    const int i = (tt - t_lo - warp) >> 3;
+    gemm_epilogue(a, tok0 + tt, rg, lane, v, meta + 2 * (tt - t_lo), i == 0 ? xres[0] : xres[1], i < 2);
   }
   if (cs > 1) cluster_sync();  // no CTA leaves while another still reads its tile
   __syncthreads();
