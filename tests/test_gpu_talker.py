@@ -310,3 +310,32 @@ def test_full_pipeline_teacher_forced(full):
     assert_agreement(np.array(P), np.array(OP), "predictor")
     assert_agreement(np.array(T), np.array(OT), "talker")
     sess.close()
+
+
+@pytest.mark.parametrize("path", ["streamed", "per-layer"])
+@pytest.mark.parametrize("L", [15, 300])
+def test_decode_step_both_paths_match_oracle(small, monkeypatch, path, L):
+    """Single-token steps run on the streamed persistent kernel by default and
+    on the per-layer kernels with Q3T_MK=0; both must match the oracle, and
+    consecutive steps (the KV append of the streamed path) too."""
+    cfg, w, model, ot = small
+    if path == "per-layer":
+        monkeypatch.setenv("Q3T_MK", "0")
+    k, v = _random_kv(cfg, L, seed=L + 100)
+    prompt, trailing, pad = S.synthetic_talker_inputs(cfg, 1, seed=3)
+    sess = model.session(prompt, trailing, pad, max_new_tokens=4)
+    sess.load_kv(S.bf16_bits(k), S.bf16_bits(v), L)
+    kvs, mems = ot.make_caches("talker", cap=L + 8)
+    for l in range(cfg.talker.n_layers):
+        mems[l][0][:, :L] = k[l]
+        mems[l][1][:, :L] = v[l]
+        kvs[l].len = L
+    g = np.random.default_rng([L, 11])
+    for step in range(3):
+        emb = g.standard_normal(cfg.talker.hidden).astype(np.float32)
+        logits, hidden = sess.decode_embeds(emb)
+        ref_h = ot.stack_forward("talker", kvs, emb[None])[0]
+        ref_logits = ot.codec_head(ref_h)[0]
+        assert_close(hidden, ref_h, f"{path} hidden step {step}")
+        assert_close(logits, ref_logits, f"{path} logits step {step}")
+    sess.close()

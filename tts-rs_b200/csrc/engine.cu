@@ -226,6 +226,7 @@ extern "C" q3t_status q3t_model_load(const q3t_model_desc *desc, q3t_model **out
     m->max_active = desc->max_active > 0 ? desc->max_active : 64;
     if (m->max_active > 64) FAIL(Q3T_INVALID_INPUT, "max_active %d > 64", m->max_active);
     init_kernel_attributes();
+    mk_init_attributes();
     {  // keep stream-ordered allocations (codec workspaces) cached between calls
       cudaMemPool_t pool;
       CK(cudaDeviceGetDefaultMemPool(&pool, desc->device));
@@ -365,6 +366,25 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
   const int mkv = std::max(nkv, pnkv);
   b->ws.part = ar.zalloc<float>((size_t)T * mkv * kAttnMaxUnits * 2 * 132);
   b->ws.counters = ar.zalloc<int>((size_t)T * mkv);
+  // streamed small-batch kernel: on unless Q3T_MK=0 or the device cannot host it
+  {
+    const char *e = getenv("Q3T_MK");
+    b->mk_grid = mk_grid(m->device);
+    b->use_mk = !(e && e[0] == '0') && b->mk_grid > 0;
+    if (!(e && e[0] == '0') && b->mk_grid <= 0)
+      fprintf(stderr, "q3t: the streamed small-batch kernel cannot be resident on device %d; "
+                      "single-token steps use the per-layer kernels\n", m->device);
+    const int Hm = std::max(tc.talker.hidden_size, tc.predictor.hidden_size);
+    b->mk_x = ar.zalloc<uint2>((size_t)2 * kMkMaxTok * Hm);
+    b->mk_qkv = ar.zalloc<uint2>((size_t)kMkMaxTok * std::max(b->NQKV, b->NQKVP));
+    b->mk_act = ar.zalloc<uint2>((size_t)kMkMaxTok * b->I2 / 2);
+    b->mk_attn = ar.zalloc<uint2>((size_t)kMkMaxTok * 128 *
+                                  std::max(tc.talker.num_attention_heads, tc.predictor.num_attention_heads));
+    b->mk_part = ar.zalloc<uint2>((size_t)kMkMaxTok * mkv * kAttnMaxUnits * 2 * kMkPartLd);
+    b->mk_ctr = ar.zalloc<unsigned>(2);
+    const unsigned epoch1 = 1u;  // tags of epoch 0 would match the zero-filled buffers
+    CK(cudaMemcpy(b->mk_ctr, &epoch1, sizeof epoch1, cudaMemcpyHostToDevice));
+  }
   // metadata
   b->meta_n = M_HDR + 8 * A;
   b->d_meta = ar.zalloc<int>(b->meta_n);
@@ -609,6 +629,145 @@ struct ProgBuilder {
     }
   }
 };
+
+// ---------------------------------------------------------------------------
+// Programs of the streamed small-batch kernel (mk.cu): the same decoder
+// stack as ProgBuilder::stack, as GEMV and attention stages over the batch
+// buffers; token rows 0..ntok-1 of x / act / attn.
+// ---------------------------------------------------------------------------
+static MkStage mk_gemv(const Linear &W) {
+  MkStage s;
+  memset(&s, 0, sizeof s);
+  s.op = MK_GEMV;
+  s.g.w = W.w;
+  s.g.N = W.N;
+  s.g.K = W.K;
+  return s;
+}
+
+// One decoder stack over input rows x; returns the stack's output rows.
+// The residual stream alternates between the two tagged x buffers.
+static MkIn mk_stack(q3t_batch *b, const LMStack &S, KVView kv, MkIn x, std::vector<MkStage> &out) {
+  const auto &c = S.cfg;
+  const int H = c.hidden_size, I = c.intermediate_size, nh = c.num_attention_heads, nkv = c.num_key_value_heads;
+  const int NQ = (nh + 2 * nkv) * 128;
+  const float eps = c.rms_norm_eps;
+  int buf = 0;
+  auto xbuf = [&](int stage) {
+    MkIn r{nullptr, b->mk_x + (size_t)buf * kMkMaxTok * H, stage, H};
+    buf ^= 1;
+    return r;
+  };
+  for (int l = 0; l < c.num_hidden_layers; l++) {
+    const int s_qkv = (int)out.size();
+    MkStage q = mk_gemv(S.qkv[l]);
+    q.g.xsrc = MKX_NORM;
+    q.g.x = x;
+    q.g.gamma = S.in_norm[l];
+    q.g.eps = eps;
+    q.g.epi = MKE_TAG;
+    q.g.yt = b->mk_qkv;
+    q.g.ldy = NQ;
+    out.push_back(q);
+    const int s_at = (int)out.size();
+    MkStage at;
+    memset(&at, 0, sizeof at);
+    at.op = MK_ATTN;
+    at.a.qkv = b->mk_qkv;
+    at.a.qkv_stage = s_qkv;
+    at.a.ldq = NQ;
+    at.a.q_norm = S.q_norm[l];
+    at.a.k_norm = S.k_norm[l];
+    at.a.inv_freq = S.inv_freq;
+    at.a.eps = eps;
+    at.a.scale = 1.0f / sqrtf(128.0f);
+    at.a.kv = kv;
+    at.a.layer = l;
+    at.a.nh = nh;
+    at.a.part = b->mk_part;
+    at.a.out = b->mk_attn;
+    at.a.ldo = nh * 128;
+    out.push_back(at);
+    MkStage o = mk_gemv(S.o[l]);
+    o.g.xsrc = MKX_TAGGED;
+    o.g.x = MkIn{nullptr, b->mk_attn, s_at, nh * 128};
+    o.g.epi = MKE_RESID;
+    o.g.res = x;
+    const MkIn xo = xbuf((int)out.size());
+    o.g.yt = const_cast<uint2 *>(xo.w);
+    o.g.ldy = H;
+    out.push_back(o);
+    x = xo;
+    const int s_gu = (int)out.size();
+    MkStage gu = mk_gemv(S.gu[l]);
+    gu.g.pairs = 1;
+    gu.g.xsrc = MKX_NORM;
+    gu.g.x = x;
+    gu.g.gamma = S.post_norm[l];
+    gu.g.eps = eps;
+    gu.g.epi = MKE_SILU;
+    gu.g.yt = b->mk_act;
+    gu.g.ldy = I;
+    out.push_back(gu);
+    MkStage dn = mk_gemv(S.down[l]);
+    dn.g.xsrc = MKX_TAGGED;
+    dn.g.x = MkIn{nullptr, b->mk_act, s_gu, I};
+    dn.g.epi = MKE_RESID;
+    dn.g.res = x;
+    const MkIn xd = xbuf((int)out.size());
+    dn.g.yt = const_cast<uint2 *>(xd.w);
+    dn.g.ldy = H;
+    out.push_back(dn);
+    x = xd;
+  }
+  return x;
+}
+
+enum MkProg { MKP_TALKER_DECODE = 1 };
+
+// The device copy of a program, built on first use.
+static std::pair<MkStage *, int> mk_program(q3t_batch *b, int kind) {
+  auto it = b->mk_progs.find(kind);
+  if (it != b->mk_progs.end()) return it->second;
+  q3t_model *m = b->m;
+  std::vector<MkStage> st;
+  if (kind == MKP_TALKER_DECODE) {  // talker decode step (model.rs:94-113) + codec_head
+    const MkIn x = mk_stack(b, m->talker, talker_kv(b), MkIn{b->x, nullptr, -1, b->H}, st);
+    MkStage hd = mk_gemv(m->codec_head);
+    hd.g.xsrc = MKX_NORM;
+    hd.g.x = x;
+    hd.g.gamma = m->talker.final_norm;
+    hd.g.eps = m->tc.talker.rms_norm_eps;
+    hd.g.hid_out = b->d_hidden;
+    hd.g.hid_slot = b->d_meta + b->off_slot();
+    hd.g.epi = MKE_F32;
+    hd.g.y = b->tlog;
+    hd.g.ldy = b->V;
+    st.push_back(hd);
+  }
+  for (const MkStage &s : st) {
+    if (s.op == MK_GEMV && ((s.g.K != 1024 && s.g.K != 2048 && s.g.K != 3072) || (s.g.pairs && s.g.N % 128) ||
+                            (s.g.epi == MKE_RESID && (s.g.N + b->mk_grid - 1) / b->mk_grid > kMkMaxRes)))
+      FAIL(Q3T_INVALID_INPUT, "streamed kernel: unsupported GEMV shape %d x %d", s.g.N, s.g.K);
+  }
+  if (st.empty() || (int)st.size() > kMkMaxStages) FAIL(Q3T_INVALID_INPUT, "streamed kernel: bad program size");
+  MkStage *d = b->ar.alloc<MkStage>(st.size());
+  CK(cudaMemcpyAsync(d, st.data(), st.size() * sizeof(MkStage), cudaMemcpyHostToDevice, b->st));
+  CK(cudaStreamSynchronize(b->st));
+  return b->mk_progs[kind] = std::make_pair(d, (int)st.size());
+}
+
+// Reads and clears the device error word; DEVICE_TIMEOUT if a bounded wait gave up.
+static void check_device_error(q3t_batch *b, const char *what) {
+  CK(cudaMemcpyAsync(b->h_err, b->d_err, sizeof(int), cudaMemcpyDeviceToHost, b->st));
+  CK(cudaStreamSynchronize(b->st));
+  if (*b->h_err) {
+    const int e = *b->h_err;
+    *b->h_err = 0;
+    CK(cudaMemsetAsync(b->d_err, 0, sizeof(int), b->st));
+    FAIL(Q3T_DEVICE_TIMEOUT, "%s: a bounded device wait gave up (code %d)", what, e);
+  }
+}
 
 // Prompt chunk / isolated step: input rows already in x; normalises them,
 // runs the talker stack.
@@ -1471,6 +1630,32 @@ extern "C" q3t_status q3t_session_decode_embeds(q3t_session *s, const float *emb
     CK(cudaMemcpyAsync(b->x, embeds, (size_t)b->H * 4, cudaMemcpyHostToDevice, b->st));
     const int ms = bucket_units(r->cache_len + 1, attn_pw(1));
     CK(cudaEventRecord(b->ev0, b->st));
+    if (b->use_mk) {
+      const auto prog = mk_program(b, MKP_TALKER_DECODE);
+      MkArgs ma{prog.first, prog.second,
+                TokView{b->d_meta + M_NTOK_B, b->d_meta + b->off_slot(), b->d_meta + b->off_tpos(), 0}, b->mk_ctr,
+                b->d_err, nullptr};
+      const char *tr = getenv("Q3T_MK_TRACE");  // profiling: per-stage device timestamps to this file
+      if (tr && tr[0]) {
+        const size_t nt = (size_t)b->mk_grid * prog.second * 8;
+        CK(cudaMallocAsync((void **)&ma.trace, nt * 8, b->st));
+        CK(cudaMemsetAsync(ma.trace, 0, nt * 8, b->st));
+        mk_launch(ma, b->mk_grid, b->st);
+        check_launches();
+        std::vector<unsigned long long> h(nt);
+        CK(cudaMemcpyAsync(h.data(), ma.trace, nt * 8, cudaMemcpyDeviceToHost, b->st));
+        CK(cudaStreamSynchronize(b->st));
+        CK(cudaFreeAsync(ma.trace, b->st));
+        if (FILE *f = fopen(tr, "wb")) {
+          const int hdr[2] = {b->mk_grid, prog.second};
+          fwrite(hdr, sizeof hdr, 1, f);
+          fwrite(h.data(), 8, nt, f);
+          fclose(f);
+        }
+      } else {
+        run_graph(b, std::make_tuple(3, MKP_TALKER_DECODE, 0), [&] { mk_launch(ma, b->mk_grid, b->st); });
+      }
+    } else
     run_graph(b, std::make_tuple(1, 1, ms), [&] {
       const int *ntok = b->d_meta + M_NTOK_B, *slot = b->d_meta + b->off_slot();
       TokView tvt{ntok, slot, b->d_meta + b->off_tpos(), 0};
@@ -1490,6 +1675,7 @@ extern "C" q3t_status q3t_session_decode_embeds(q3t_session *s, const float *emb
                          b->st));
     CK(cudaStreamSynchronize(b->st));
     CK(cudaEventElapsedTime(&b->last_ms, b->ev0, b->ev1));
+    check_device_error(b, "talker decode step");
     r->cache_len++;
   });
 }

@@ -12,6 +12,7 @@
 
 #include "../../include/q3t.h"
 #include "lm_kernels.cuh"
+#include "mk.cuh"
 
 namespace q3t {
 
@@ -193,6 +194,16 @@ struct q3t_batch {
   std::map<std::pair<int, int>, std::vector<q3t::Phase>> programs;  // decode-frame phase lists
   std::map<std::tuple<const void *, int, int>, CUtensorMap> xmaps;  // (X buffer, K, token tiles) -> TMA map
   int *d_err = nullptr, *h_err = nullptr;  // bounded-wait timeouts reported by the GEMM kernels
+  // streamed small-batch kernel (mk.cu): programs by kind, raw q/k/v rows, stage counters
+  bool use_mk = false;
+  int mk_grid = 0;
+  uint2 *mk_x = nullptr;     // [2][kMkMaxTok][hidden] tagged residual rows (alternating)
+  uint2 *mk_qkv = nullptr;   // [kMkMaxTok][max NQKV] tagged raw q/k/v rows
+  uint2 *mk_act = nullptr;   // [kMkMaxTok][max intermediate] tagged SwiGLU rows
+  uint2 *mk_attn = nullptr;  // [kMkMaxTok][max heads x 128] tagged attention output rows
+  uint2 *mk_part = nullptr;  // [kMkMaxTok][max kv heads][kAttnMaxUnits][2][kMkPartLd] tagged attention partials
+  unsigned *mk_ctr = nullptr;  // launch epoch, finished CTAs
+  std::map<int, std::pair<q3t::MkStage *, int>> mk_progs;
   int step_counter = 0;
   // requests
   std::vector<q3t::Req *> slots;

@@ -41,6 +41,8 @@ static void note(cudaError_t e, const char *what) {
   }
 }
 
+void note_launch(cudaError_t e, const char *what) { note(e, what); }
+
 template <typename... KArgs, typename... Args>
 static void launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args &&...args) {
   cudaLaunchConfig_t cfg = {};

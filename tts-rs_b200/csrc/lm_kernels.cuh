@@ -53,6 +53,8 @@ void init_kernel_attributes();
 extern int64_t g_launches;
 // first launch error since the last call (cudaSuccess if none)
 cudaError_t take_launch_error(const char **kernel);
+// records a launch error (kept until take_launch_error)
+void note_launch(cudaError_t e, const char *what);
 
 // Packs W [N][K] bf16 row-major into m16n8k16 A-fragment order.
 void pack_weight(const uint16_t *src, uint16_t *dst, int N, int K, cudaStream_t st);
