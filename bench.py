@@ -51,6 +51,10 @@ def parse():
     p.add_argument("--cpu-frames", type=int, default=48, help="bounded CPU-baseline sample (frames)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-b1", action="store_true", help="skip the batch-1 talker step measurement")
+    p.add_argument("--only-b1", action="store_true",
+                   help="run only the batch-1 talker step (prints its JSON object; for profiling)")
+    p.add_argument("--b1-steps", type=int, default=256)
     p.add_argument("--kv-pages", type=int, default=8192, help="talker KV pool size (16-token pages)")
     p.add_argument("--profile", action="store_true",
                    help="bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)")
@@ -150,6 +154,39 @@ def cpu_baseline(n_frames, threads=0):
     return n_frames * FRAME_S / dt, O.lib().orc_get_threads(), dt
 
 
+def talker_b1_step(model, cfg, L=1024, steps=256, warmup=3, peak=6558.1):
+    """Isolated batch-1 talker decode step (hidden ~N(0,1) in, codec-head
+    logits out) against a KV cache of length L (K/V ~N(0,1) bf16), through the
+    session C ABI (q3t_session_decode_embeds); device time per step from the
+    library's CUDA events.  Algorithmic bytes per step: every talker weight and
+    the codec head once (bf16) plus K/V of every cached position and layer."""
+    c = cfg.talker
+    g = np.random.default_rng([0, 31])
+    k = S.bf16_bits(g.standard_normal((c.n_layers, c.n_kv, L, c.head_dim), dtype=np.float32))
+    v = S.bf16_bits(g.standard_normal((c.n_layers, c.n_kv, L, c.head_dim), dtype=np.float32))
+    prompt, trailing, pad = S.synthetic_talker_inputs(cfg, 1, 0)
+    sess = model.session(prompt, trailing, pad, max_new_tokens=4)
+    sess.load_kv(k, v, L)
+    emb = g.standard_normal(c.hidden).astype(np.float32)
+    us, lens = [], []
+    for i in range(warmup + steps):
+        sess.decode_embeds(emb)
+        if i >= warmup:
+            us.append(sess.last_ms() * 1e3)
+            lens.append(L + i + 1)
+    sess.close()
+    layer = (c.hidden * (c.n_heads + 2 * c.n_kv) * c.head_dim + c.hidden * c.n_heads * c.head_dim
+             + 3 * c.hidden * c.inter) * 2
+    wbytes = c.n_layers * layer + c.vocab * c.hidden * 2
+    kv_per_pos = c.n_layers * 2 * c.n_kv * c.head_dim * 2
+    byt = wbytes + kv_per_pos * float(np.median(lens))
+    med = float(np.median(us))
+    return {"workload": f"talker decode step, batch 1, KV length {L}..{L + warmup + steps}, {steps} steps",
+            "us_per_step_p50": round(med, 2), "bytes_per_step": int(byt),
+            "achieved_gbs": round(byt / med / 1e3, 1), "peak_gbs": peak,
+            "frac": round(byt / med / 1e3 / peak, 4)}
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -169,6 +206,13 @@ def main():
 
     cfg = S.TalkerConfig()
     cc = S.CodecConfig()
+    if args.only_b1:
+        model = q3t.Model(cfg, S.make_talker_weights(cfg, 0), device=local, kv_pages=128, max_active=1)
+        peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))).get("hbm_gbs", 6650.0) \
+            if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 6650.0
+        print(json.dumps(talker_b1_step(model, cfg, steps=args.b1_steps, peak=peak)), flush=True)
+        model.close()
+        return
     model = q3t.Model(cfg, S.make_talker_weights(cfg, 0), cc, S.make_codec_weights(cc, 0), device=local,
                       kv_pages=args.kv_pages, max_active=args.max_active)
     reqs = workload(args.requests)
@@ -264,6 +308,16 @@ def main():
         e2e.pop("_samples")
         e2e.pop("_wall")
 
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    b1 = None
+    if rank == 0 and not args.no_b1:
+        b1 = talker_b1_step(model, cfg, steps=args.b1_steps, peak=hbm_peak)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, cores, dt = cpu_baseline(args.cpu_frames)
@@ -271,14 +325,18 @@ def main():
                "sample": f"one batch-1 request, 64-token prompt, {args.cpu_frames} teacher-forced frames "
                          f"(28-layer talker + 5-layer predictor) + codec decode, {dt:.1f} s"}
 
-    peaks = {}
-    try:
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-    except Exception:
-        pass
-    hbm_peak = peaks.get("hbm_gbs", 6650.0)
     med_ms = float(np.median(decode_ms)) if decode_ms else float(np.median(step_ms))
     ach = (float(np.median(bytes_)) / 1e9) / (med_ms / 1e3) if bytes_ else None
+    # DRAM bytes per decode step: the ncu-measured ratio of DRAM reads to
+    # algorithmic bytes (profiles/decode_step_dram_bench64.md) times this
+    # run's algorithmic bytes per step
+    traffic = None
+    try:
+        for line in open(os.path.join(ROOT, "profiles", "decode_step_dram_bench64.md")):
+            if line.startswith("traffic_ratio_to_algorithmic:") and bytes_:
+                traffic = int(float(line.split(":")[1]) * float(np.median(bytes_)))
+    except OSError:
+        pass
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -303,8 +361,11 @@ def main():
             "roofline": {"bound": "hbm", "unit": "GB/s",
                          "kernel": "decode frame step (CUDA graph of talker + predictor kernels)",
                          "achieved": round(ach, 1) if ach else None, "peak": hbm_peak,
-                         "frac": round(ach / hbm_peak, 4) if ach else None, "traffic": None,
+                         "frac": round(ach / hbm_peak, 4) if ach else None, "traffic": traffic,
+                         "traffic_unit": "bytes per decode step (ncu DRAM reads, scaled from a 64-request capture)",
+                         "algorithmic_bytes": int(np.median(bytes_)) if bytes_ else None,
                          "peak_source": "measured" if "hbm_gbs" in peaks else "fallback"},
+            "talker_b1": b1,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": int(launches),
