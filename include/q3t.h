@@ -217,6 +217,20 @@ q3t_status q3t_codec_out_len(const q3t_model *model, int T, int64_t *n);
 q3t_status q3t_codec_decode_static(q3t_model *model, const int64_t *codes, int B, int T,
                                    float *wave, int16_t *pcm, int64_t *n, void *stream);
 
+/* Prompt text projection: project_text_ids
+ * (tts_qwen3_tts/src/execution/compiler/session_seed.rs:668-679) =
+ * Qwen3TtsTalkerResizeMlp (talker/network/mlp.rs:36-40, config.rs:200-209)
+ * over the text embedding: out[i] = linear_fc2(silu(linear_fc1(
+ * text_embedding[ids[i]]))) with biases, [n][hidden] f32 rows holding bf16
+ * values (the model dtype).  The session seed is assembled from these rows by
+ * the caller (session_seed.rs:151-215).  Needs the optional tensors
+ * talker.model.text_embedding.weight [text_vocab][text_hidden] and
+ * talker.text_projection.linear_fc{1,2}.{weight,bias} in q3t_model_load;
+ * INVALID_INPUT without them or for ids outside [0, text_vocab). */
+q3t_status q3t_text_project(q3t_model *model, const int64_t *ids, int n, float *out);
+/* text_vocab / text_hidden of the loaded text projection (0 if absent). */
+q3t_status q3t_text_dims(const q3t_model *model, int *text_vocab, int *text_hidden);
+
 /* ------------------------ ragged continuous batching --------------------- */
 typedef struct {
   int max_active;            /* <= model max_active */

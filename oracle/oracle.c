@@ -89,6 +89,26 @@ static void rmsnorm(const float *x, const float *g, int n, float eps,
 
 static float silu(float x) { return x / (1.f + expf(-x)); }
 
+/* project_text_ids (execution/compiler/session_seed.rs:668-679):
+ * Qwen3TtsTalkerResizeMlp (talker/network/mlp.rs:36-40) over the text
+ * embedding.  emb [vocab][Ht], w1 [Ht][Ht] + b1, w2 [H][Ht] + b2 (bf16 values
+ * held as f32).  Rounding points: silu(fc1 + b1) and fc2 + b2 are rounded to
+ * bf16 (the model dtype); sums run in f32. */
+void orc_text_project(const float *emb, const float *w1, const float *b1, const float *w2,
+                      const float *b2, int Ht, int H, const int64_t *ids, int n, float *out) {
+  float *x = (float *)malloc((size_t)Ht * sizeof(float));
+  float *h = (float *)malloc((size_t)Ht * sizeof(float));
+  for (int i = 0; i < n; i++) {
+    memcpy(x, emb + (size_t)ids[i] * Ht, (size_t)Ht * sizeof(float));
+    orc_linear(w1, b1, x, 1, Ht, Ht, h);
+    for (int j = 0; j < Ht; j++) h[j] = orc_bf16_round(silu(h[j]));
+    orc_linear(w2, b2, h, 1, Ht, H, out + (size_t)i * H);
+    for (int j = 0; j < H; j++) out[(size_t)i * H + j] = orc_bf16_round(out[(size_t)i * H + j]);
+  }
+  free(x);
+  free(h);
+}
+
 /* ------------------------------------------------------------------------ */
 /* KV cache: talker/network/kv.rs:56-161                                     */
 /* ------------------------------------------------------------------------ */

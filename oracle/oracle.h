@@ -81,6 +81,11 @@ void orc_stack_forward(const orc_stack *st, orc_kv *caches, const float *x,
 void orc_linear(const float *W, const float *bias, const float *x, int S,
                 int K, int N, float *y);
 
+/* session_seed.rs:668-679 + mlp.rs:36-40: text embedding -> fc1 + b1 -> silu
+ * (bf16) -> fc2 + b2 (bf16); out [n][H] */
+void orc_text_project(const float *emb, const float *w1, const float *b1, const float *w2,
+                      const float *b2, int Ht, int H, const int64_t *ids, int n, float *out);
+
 /* --------------------------- sampling ----------------------------------- */
 typedef struct {
   int do_sample;

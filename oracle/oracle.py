@@ -104,6 +104,7 @@ def lib():
         L.orc_kv_reset_preserve.argtypes = [C.POINTER(KV)]
         L.orc_stack_forward.argtypes = [C.POINTER(Stack), C.POINTER(KV), F, C.c_int, F]
         L.orc_linear.argtypes = [F, F, F, C.c_int, C.c_int, C.c_int, F]
+        L.orc_text_project.argtypes = [F, F, F, F, F, C.c_int, C.c_int, I64, C.c_int, F]
         L.orc_gen_start.restype = C.c_void_p
         L.orc_gen_start.argtypes = [C.POINTER(Talker), F, C.c_int, F, C.c_int, F,
                                     C.POINTER(Sampling), C.POINTER(Sampling), C.c_int,
@@ -211,6 +212,19 @@ class OracleTalker:
         H = st.cfg.hidden
         out = np.zeros((S, H), np.float32)
         lib().orc_stack_forward(C.byref(st), kvs, fp(x), S, fp(out))
+        return out
+
+    def text_project(self, ids):
+        """project_text_ids (session_seed.rs:668-679): [n][hidden] bf16-valued rows."""
+        w = self.w
+        emb = f32(w["talker.model.text_embedding.weight"])
+        Ht = emb.shape[1]
+        H = self.cfg.talker.hidden
+        ids = np.ascontiguousarray(ids, np.int64)
+        out = np.zeros((len(ids), H), np.float32)
+        keep = [f32(w[f"talker.text_projection.linear_fc{i}.{k}"]) for i in (1, 2) for k in ("weight", "bias")]
+        lib().orc_text_project(fp(emb), fp(keep[0]), fp(keep[1]), fp(keep[2]), fp(keep[3]), Ht, H,
+                               ids.ctypes.data_as(I64), len(ids), fp(out))
         return out
 
     def codec_head(self, hidden):

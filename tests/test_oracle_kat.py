@@ -147,3 +147,28 @@ def test_to_pcm_rounding():
     out = np.zeros(len(x), np.int16)
     O.lib().orc_to_pcm(O.fp(x), len(x), out.ctypes.data_as(O.C.POINTER(O.C.c_int16)))
     assert list(out) == [0, 32767, -32768, 32767, 1, -2]
+
+
+def test_text_projection_oracle_matches_numpy():
+    """The oracle's project_text_ids (session_seed.rs:668-679, mlp.rs:36-40)
+    against an independent numpy restatement of the same rounding points:
+    bf16(silu(fc1 x + b1)), then bf16(fc2 h + b2).  Sums differ only in
+    order, so an occasional element rounds to the neighbouring bf16 value
+    (and a flipped hidden value moves the smallest outputs by ~1e-6)."""
+    cfg = S.TalkerConfig().small(talker_layers=1, predictor_layers=1)
+    w = S.make_talker_weights(cfg, seed=0)
+    w.update(S.make_text_weights(cfg, seed=0, text_vocab=512, text_hidden=256))
+    ot = O.OracleTalker(cfg, w)
+    ids = np.array([0, 511, 7, 7, 300], np.int64)
+    got = ot.text_project(ids)
+    e = w["talker.model.text_embedding.weight"][ids].astype(np.float64)
+    a = e @ w["talker.text_projection.linear_fc1.weight"].T.astype(np.float64) + w["talker.text_projection.linear_fc1.bias"]
+    h = S.bf16_round((a / (1 + np.exp(-a))).astype(np.float32)).astype(np.float64)
+    o = h @ w["talker.text_projection.linear_fc2.weight"].T.astype(np.float64) + w["talker.text_projection.linear_fc2.bias"]
+    ref = S.bf16_round(o.astype(np.float32))
+    assert got.shape == (5, cfg.talker.hidden)
+    assert np.array_equal(got, S.bf16_round(got)), "outputs are bf16 values"
+    diff = np.abs(got - ref)
+    assert (diff <= np.abs(ref) * 2.0 ** -7 + 1e-3 * np.abs(ref).max()).all()
+    assert (diff == 0).mean() > 0.97
+    assert np.array_equal(got[2], got[3]), "equal ids give equal rows"

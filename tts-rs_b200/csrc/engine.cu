@@ -61,6 +61,10 @@ struct Tensors {
     for (int i = 0; i < d->num_tensors; i++)
       if (d->tensors[i].name) m[d->tensors[i].name] = &d->tensors[i];
   }
+  const q3t_tensor *find(const std::string &name) const {
+    auto it = m.find(name);
+    return it == m.end() ? nullptr : it->second;
+  }
   const q3t_tensor *get(const std::string &name, std::vector<int64_t> shape) const {
     auto it = m.find(name);
     if (it == m.end()) FAIL(Q3T_RUNTIME_LOAD, "missing tensor %s", name.c_str());
@@ -262,6 +266,20 @@ extern "C" q3t_status q3t_model_load(const q3t_model_desc *desc, q3t_model **out
       CK(cudaMemcpyAsync(m->cp_emb_dev, m->cp_emb.data(), (G - 1) * sizeof(uint16_t *), cudaMemcpyHostToDevice,
                          st));
     }
+    if (m->has_talker && T.find("talker.model.text_embedding.weight")) {
+      // text projection (talker/network/model.rs:22, 76; config.rs:200-209)
+      const q3t_tensor *e = T.find("talker.model.text_embedding.weight");
+      if (e->ndim != 2) FAIL(Q3T_RUNTIME_LOAD, "talker.model.text_embedding.weight must be 2-D");
+      const int Vt = (int)e->shape[0], Ht = (int)e->shape[1], H = m->tc.talker.hidden_size;
+      if (Ht % 256 || Ht > 8192) FAIL(Q3T_RUNTIME_LOAD, "text hidden size %d unsupported (multiple of 256)", Ht);
+      m->text_vocab = Vt;
+      m->text_hidden = Ht;
+      m->text_emb = upload_bf16(T.get("talker.model.text_embedding.weight", {Vt, Ht}), m->arena, st);
+      m->tp_fc1 = load_linear(T.get("talker.text_projection.linear_fc1.weight", {Ht, Ht}), Ht, Ht, m->arena, st);
+      m->tp_b1 = upload_f32(T.get("talker.text_projection.linear_fc1.bias", {Ht}), m->arena, st);
+      m->tp_fc2 = load_linear(T.get("talker.text_projection.linear_fc2.weight", {H, Ht}), H, Ht, m->arena, st);
+      m->tp_b2 = upload_f32(T.get("talker.text_projection.linear_fc2.bias", {H}), m->arena, st);
+    }
     if (m->has_codec) m->codec = codec_load(m, desc, st);
     CK(cudaStreamSynchronize(st));
     CK(cudaStreamDestroy(st));
@@ -280,6 +298,7 @@ extern "C" q3t_status q3t_model_load(const q3t_model_desc *desc, q3t_model **out
 extern "C" void q3t_model_free(q3t_model *m) {
   if (!m) return;
   cudaSetDevice(m->device);
+  if (m->tp_st) cudaStreamDestroy(m->tp_st);
   if (m->codec) codec_free(m->codec);
   delete m;
 }
@@ -1724,6 +1743,95 @@ extern "C" void q3t_session_free(q3t_session *s) {
   if (!s) return;
   q3t_batch_free(s->b);
   delete s;
+}
+
+// ----------------------------------------------------------------------------
+// Text projection of prompt token ids (project_text_ids,
+// execution/compiler/session_seed.rs:668-679; Qwen3TtsTalkerResizeMlp,
+// talker/network/mlp.rs:36-40): embedding gather, linear_fc1 + bias, SiLU
+// (rounded to bf16), linear_fc2 + bias (rounded to bf16), 64 ids per pass on
+// the tensor-core GEMM.
+// ----------------------------------------------------------------------------
+extern "C" q3t_status q3t_text_project(q3t_model *m, const int64_t *ids, int n, float *out) {
+  if (!m || n < 0 || (n > 0 && (!ids || !out))) {
+    set_error("q3t_text_project: bad argument");
+    return Q3T_INVALID_INPUT;
+  }
+  if (!m->text_emb) {
+    set_error("q3t_text_project: the model has no text_embedding / text_projection tensors");
+    return Q3T_INVALID_INPUT;
+  }
+  for (int i = 0; i < n; i++)
+    if (ids[i] < 0 || ids[i] >= m->text_vocab) {
+      set_error("q3t_text_project: token id %lld outside [0, %d)", (long long)ids[i], m->text_vocab);
+      return Q3T_INVALID_INPUT;
+    }
+  std::lock_guard<std::mutex> lock(m->tp_mu);
+  return guard([&] {
+    CK(cudaSetDevice(m->device));
+    const int Ht = m->text_hidden, H = m->tc.talker.hidden_size, TB = 64;
+    if (!m->tp_st) {
+      CK(cudaStreamCreateWithFlags(&m->tp_st, cudaStreamNonBlocking));
+      m->tp_x = m->arena.alloc<uint16_t>((size_t)TB * Ht);
+      m->tp_h = m->arena.alloc<uint16_t>((size_t)TB * Ht);
+      m->tp_out = m->arena.alloc<float>((size_t)TB * H);
+      m->tp_ids = m->arena.alloc<int>(TB);
+      m->tp_ntok = m->arena.alloc<int>(1);
+      m->tp_err = m->arena.zalloc<int>(1);
+      CK(cudaDeviceSynchronize());
+      if (!make_tmap_bf16(&m->tp_xmap, m->tp_x, Ht, TB, (uint64_t)Ht * 2, 64, TB) ||
+          !make_tmap_bf16(&m->tp_hmap, m->tp_h, Ht, TB, (uint64_t)Ht * 2, 64, TB))
+        FAIL(Q3T_CUDA_ERROR, "TMA descriptor encoding failed for the text projection workspace");
+    }
+    cudaStream_t st = m->tp_st;
+    std::vector<int> hid(TB);
+    for (int c0 = 0; c0 < n; c0 += TB) {
+      const int cnt = std::min(TB, n - c0);
+      for (int i = 0; i < cnt; i++) hid[i] = (int)ids[c0 + i];
+      CK(cudaMemcpyAsync(m->tp_ids, hid.data(), cnt * sizeof(int), cudaMemcpyHostToDevice, st));
+      CK(cudaMemcpyAsync(m->tp_ntok, &cnt, sizeof(int), cudaMemcpyHostToDevice, st));
+      gather_rows_bf16(m->text_emb, m->tp_ids, cnt, Ht, m->tp_x, st);
+      GemmArgs g1 = gemm_args(m->tp_fc1, m->tp_ntok, TB);
+      g1.xmode = GX_BF16;
+      g1.tx = m->tp_xmap;
+      g1.xb = m->tp_x;
+      g1.ldx = Ht;
+      g1.epi = GE_BIAS_SILU;
+      g1.h = m->tp_h;
+      g1.ldh = Ht;
+      g1.bias = m->tp_b1;
+      g1.err = m->tp_err;
+      gemm(g1, TB, st);
+      GemmArgs g2 = gemm_args(m->tp_fc2, m->tp_ntok, TB);
+      g2.xmode = GX_BF16;
+      g2.tx = m->tp_hmap;
+      g2.xb = m->tp_h;
+      g2.ldx = Ht;
+      g2.epi = GE_BIAS_BF16;
+      g2.y = m->tp_out;
+      g2.ldy = H;
+      g2.bias = m->tp_b2;
+      g2.err = m->tp_err;
+      gemm(g2, TB, st);
+      check_launches();
+      CK(cudaMemcpyAsync(out + (size_t)c0 * H, m->tp_out, (size_t)cnt * H * sizeof(float), cudaMemcpyDeviceToHost,
+                         st));
+      CK(cudaStreamSynchronize(st));  // hid and the workspace are reused by the next pass
+    }
+    int e = 0;
+    CK(cudaMemcpy(&e, m->tp_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) {
+      CK(cudaMemset(m->tp_err, 0, sizeof(int)));
+      FAIL(Q3T_DEVICE_TIMEOUT, "text projection: a bounded device wait gave up (code %d)", e);
+    }
+  });
+}
+
+extern "C" q3t_status q3t_text_dims(const q3t_model *m, int *text_vocab, int *text_hidden) {
+  if (!m) return Q3T_INVALID_INPUT;
+  if (text_vocab) *text_vocab = m->text_vocab;
+  if (text_hidden) *text_hidden = m->text_hidden;
+  return Q3T_OK;
 }
 
 // ----------------------------------------------------------------------------

@@ -6,6 +6,7 @@
 #include <deque>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <tuple>
 #include <vector>
@@ -142,6 +143,18 @@ struct q3t_model {
   int64_t kv_pages = 8192;
   int max_active = 64;
   q3t::CodecModel *codec = nullptr;
+  // text projection (optional tensors): text_embedding [text_vocab][text_hidden]
+  // bf16, linear_fc1 [text_hidden][text_hidden] + bias, linear_fc2 [hidden][text_hidden] + bias
+  int text_vocab = 0, text_hidden = 0;
+  uint16_t *text_emb = nullptr;
+  q3t::Linear tp_fc1, tp_fc2;
+  float *tp_b1 = nullptr, *tp_b2 = nullptr;
+  std::mutex tp_mu;  // guards the workspace below (model handles are shared by threads)
+  cudaStream_t tp_st = nullptr;
+  uint16_t *tp_x = nullptr, *tp_h = nullptr;
+  float *tp_out = nullptr;
+  int *tp_ids = nullptr, *tp_ntok = nullptr, *tp_err = nullptr;
+  CUtensorMap tp_xmap, tp_hmap;
   q3t::DevArena arena;
 };
 

@@ -204,6 +204,14 @@ Q3T_DEV void gemm_epilogue(const GemmArgs &a, int t, int rg, int lane, float4 v,
     *xp = x;
     const float ss = warp_sum(x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w);
     if (lane == 0) a.ss_out[(size_t)rg * a.ss_ld + t] = ss;
+  } else if (a.epi == GE_BIAS_SILU || a.epi == GE_BIAS_BF16) {
+    const float4 b = *reinterpret_cast<const float4 *>(a.bias + n);
+    const float y0 = v.x + b.x, y1 = v.y + b.y, y2 = v.z + b.z, y3 = v.w + b.w;
+    if (a.epi == GE_BIAS_SILU)
+      store_bf16x4(a.h + (size_t)t * a.ldh + n, silu(y0), silu(y1), silu(y2), silu(y3));
+    else
+      *reinterpret_cast<float4 *>(a.y + (size_t)t * a.ldy + n) =
+          make_float4(bf16_round(y0), bf16_round(y1), bf16_round(y2), bf16_round(y3));
   } else if (a.epi == GE_SILU) {
     const float ux = __shfl_xor_sync(0xffffffffu, v.x, 16), uy = __shfl_xor_sync(0xffffffffu, v.y, 16);
     const float uz = __shfl_xor_sync(0xffffffffu, v.z, 16), uw = __shfl_xor_sync(0xffffffffu, v.w, 16);
@@ -458,6 +466,8 @@ void gemm(const GemmArgs &a, int max_tok, cudaStream_t st) {
   const int atoms = a.K / 64;
   if (a.N % 128 || a.K % 64 || a.cs < 1 || a.cs > 8 || atoms % a.cs || max_tok < 1 ||
       (a.epi == GE_SILU && a.h == nullptr) || (a.xmode == GX_NORM && (a.x == nullptr || a.ss == nullptr)) ||
+      ((a.epi == GE_BIAS_SILU || a.epi == GE_BIAS_BF16) && a.bias == nullptr) ||
+      (a.epi == GE_BIAS_SILU && a.h == nullptr) || (a.epi == GE_BIAS_BF16 && a.y == nullptr) ||
       a.nss > kMaxNss || (a.epi == GE_RESID && (a.ss_out == nullptr || a.y == nullptr))) {
     note(cudaErrorInvalidValue, "k_gemm (shape / arguments)");
     return;
@@ -579,6 +589,25 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a) {
 
 void sample(const SampleArgs &a, int max_tok, cudaStream_t st) {
   launch(k_sample, dim3(max_tok), dim3(kSampleThreads), kSampleSmem, st, a);
+}
+
+// out[i] = table[ids[i]] for i < n, rows of `width` bf16 (width % 8 == 0).
+__global__ void k_gather_rows(const uint16_t *__restrict__ table, const int *__restrict__ ids, int width,
+                              uint16_t *__restrict__ out) {
+  const uint4 *src = reinterpret_cast<const uint4 *>(table + (size_t)ids[blockIdx.x] * width);
+  uint4 *dst = reinterpret_cast<uint4 *>(out + (size_t)blockIdx.x * width);
+  for (int i = threadIdx.x; i < width / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+void gather_rows_bf16(const uint16_t *table, const int *ids, int n, int width, uint16_t *out, cudaStream_t st) {
+  if (n <= 0) return;
+  if (width % 8) {
+    note(cudaErrorInvalidValue, "k_gather_rows (width)");
+    return;
+  }
+  k_gather_rows<<<n, 128, 0, st>>>(table, ids, width, out);
+  note(cudaGetLastError(), "k_gather_rows");
+  g_launches++;
 }
 
 __global__ void k_kv_import(const uint16_t *k, const uint16_t *v, int len, KVView kv, int seq) {

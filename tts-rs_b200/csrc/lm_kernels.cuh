@@ -117,6 +117,8 @@ enum GemmEpi {
   GE_QKV = 1,    // q/k RMSNorm + RoPE; q -> bf16 q[t], k / v appended to the paged cache
   GE_RESID = 2,  // y[t][n] += acc (residual stream), ss_out[n / 128][t] = sum of squares of the new rows
   GE_SILU = 3,   // row block r = [gate 64r..64r+63 | up 64r..64r+63]: h[t][64r + i] = bf16(silu(g) * u)
+  GE_BIAS_SILU = 4,  // h[t][n] = bf16(silu(acc + bias[n]))
+  GE_BIAS_BF16 = 5,  // y[t][n] = bf16-rounded (acc + bias[n]), stored as f32
 };
 
 // A weight matrix W [N][K] bf16 row-major with its TMA descriptor (box 64 x
@@ -153,8 +155,9 @@ struct GemmArgs {
   float *y;            // GE_F32 output / GE_RESID residual, [t][ldy]
   int ldy;
   float *ss_out;       // GE_RESID: [N / 128][ss_ld]
-  uint16_t *h;         // GE_SILU: [t][ldh]
+  uint16_t *h;         // GE_SILU / GE_BIAS_SILU: [t][ldh]
   int ldh;
+  const float *bias;   // GE_BIAS_SILU / GE_BIAS_BF16: [N]
   const float *q_norm, *k_norm, *inv_freq;  // GE_QKV
   int nh, nkv;
   TokView tv;
@@ -255,6 +258,9 @@ struct Phase {
   RmsArgs tail;
 };
 void run_phases(const Phase *phases, int n_phases, cudaStream_t st);
+
+// out[i] = table[ids[i]] (device ids, i < n): rows of `width` bf16.
+void gather_rows_bf16(const uint16_t *table, const int *ids, int n, int width, uint16_t *out, cudaStream_t st);
 
 // Scatter dense bf16 K/V [layers][n_kv][len][hd] into the pages of `seq`.
 void kv_import(const uint16_t *k, const uint16_t *v, int layers, int len, KVView kv, int seq,

@@ -102,7 +102,7 @@ EXPORTS = [
     "q3t_batch_create",
     "q3t_batch_submit", "q3t_batch_step", "q3t_batch_poll", "q3t_batch_take",
     "q3t_batch_pending", "q3t_batch_stream", "q3t_batch_free", "q3t_last_error", "q3t_version",
-    "q3t_kernel_launches",
+    "q3t_kernel_launches", "q3t_text_project", "q3t_text_dims",
 ]
 
 _F = C.POINTER(C.c_float)
@@ -148,6 +148,8 @@ def lib():
         L.q3t_batch_stream.argtypes = [C.c_void_p, C.POINTER(C.c_void_p)]
         L.q3t_batch_free.argtypes = [C.c_void_p]
         L.q3t_batch_free.restype = None
+        L.q3t_text_project.argtypes = [C.c_void_p, _I64, C.c_int, _F]
+        L.q3t_text_dims.argtypes = [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int)]
         _LIB = L
     return _LIB
 
@@ -255,6 +257,13 @@ class Model:
                                      None if p is None else p.ctypes.data_as(C.POINTER(C.c_int16)),
                                      C.byref(nn)))
         return (wave, p) if pcm else wave
+
+    def text_project(self, ids):
+        """project_text_ids on the device: [n][hidden] f32 rows (bf16 values)."""
+        ids = np.ascontiguousarray(ids, np.int64)
+        out = np.zeros((len(ids), self.talker_cfg.talker.hidden), np.float32)
+        check(lib().q3t_text_project(self.h, ids.ctypes.data_as(_I64) if len(ids) else None, len(ids), _fp(out)))
+        return out
 
     def batch(self, max_active=64, codec_mode=0, chunk_frames=16, left_context=8, keep_output=1):
         return Batch(self, max_active, codec_mode, chunk_frames, left_context, keep_output)

@@ -174,6 +174,28 @@ def make_talker_weights(cfg: TalkerConfig, seed: int = 0) -> dict:
     return _parallel(one, talker_tensor_specs(cfg))
 
 
+def text_tensor_specs(cfg: TalkerConfig, text_vocab: int = 151936, text_hidden: int = 2048):
+    """The prompt text path (talker/config.rs:142-143, 200-209): text embedding
+    and the two-layer text projection with biases."""
+    H = cfg.talker.hidden
+    return [("talker.model.text_embedding.weight", (text_vocab, text_hidden), "embed"),
+            ("talker.text_projection.linear_fc1.weight", (text_hidden, text_hidden), "linear"),
+            ("talker.text_projection.linear_fc1.bias", (text_hidden,), "bias"),
+            ("talker.text_projection.linear_fc2.weight", (H, text_hidden), "linear"),
+            ("talker.text_projection.linear_fc2.bias", (H,), "bias")]
+
+
+def make_text_weights(cfg: TalkerConfig, seed: int = 0, text_vocab: int = 151936, text_hidden: int = 2048) -> dict:
+    """Seed-0 text path tensors (embedding ~N(0, 0.5), linears ~N(0, 0.02),
+    biases ~N(0, 0.02)), rounded to bf16.  Kept separate from the talker
+    bundle: the full text embedding alone is 151936 x 2048."""
+    def one(spec):
+        name, shape, kind = spec
+        a = _normal(seed, name, shape, 0.5 if kind == "embed" else 0.02)
+        return name, bf16_round(a)
+    return _parallel(one, text_tensor_specs(cfg, text_vocab, text_hidden))
+
+
 def codec_tensor_specs(c: CodecConfig):
     half, D, LAT, H = c.codebook_dim // 2, c.codebook_dim, c.latent, c.hidden
     s = []
