@@ -231,6 +231,27 @@ q3t_status q3t_text_project(q3t_model *model, const int64_t *ids, int n, float *
 /* text_vocab / text_hidden of the loaded text projection (0 if absent). */
 q3t_status q3t_text_dims(const q3t_model *model, int *text_vocab, int *text_hidden);
 
+/* ------------------------------- file IO --------------------------------- */
+/* A memory-mapped .safetensors checkpoint whose float tensors (F32 and BF16
+ * in place, F16 widened to F32; integer tensors skipped) are listed as
+ * q3t_tensor entries by their checkpoint names, ready for q3t_model_load
+ * (concatenate the lists of the talker and speech-tokenizer files).  Replaces
+ * the SafetensorsStore reads of talker/weights.rs:52-66 and
+ * codec/weights.rs:77-81 (driven by loading/runtime.rs:131-156); the key
+ * remaps there are Burn module renames, except the codec's legacy
+ * `._codebook.` spelling, which q3t_model_load accepts as well as
+ * `.codebook.`.  The list stays valid until q3t_tensor_set_free. */
+typedef struct q3t_tensor_set q3t_tensor_set;
+q3t_status q3t_safetensors_open(const char *path, q3t_tensor_set **out);
+q3t_status q3t_tensor_set_list(const q3t_tensor_set *set, const q3t_tensor **tensors, int *num_tensors);
+void q3t_tensor_set_free(q3t_tensor_set *set);
+
+/* PcmAudio::write_wav (tts_infer/src/audio.rs:12-49): the RIFF/WAVE image of
+ * 16-bit integer PCM (44-byte header, format 1, little-endian samples) into
+ * out[capacity]; *size = 44 + 2 * num_samples (out = NULL: size query). */
+q3t_status q3t_wav_write(const int16_t *pcm, int64_t num_samples, int sample_rate, int channels, uint8_t *out,
+                         int64_t capacity, int64_t *size);
+
 /* ------------------------ ragged continuous batching --------------------- */
 typedef struct {
   int max_active;            /* <= model max_active */

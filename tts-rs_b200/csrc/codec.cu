@@ -685,25 +685,42 @@ struct CodecModel {
   float out_b = 0.f;
 };
 
+// The tensor `name` (or its other checkpoint spelling, checkpoint_alias) with
+// `shape`'s element count, f32 or bf16.
 static const q3t_tensor *find(const q3t_model_desc *d, const std::string &name, std::vector<int64_t> shape) {
-  for (int i = 0; i < d->num_tensors; i++) {
-    const q3t_tensor *t = &d->tensors[i];
-    if (!t->name || name != t->name) continue;
-    int64_t n1 = 1, n2 = 1;
-    for (int k = 0; k < t->ndim; k++) n1 *= t->shape[k];
-    for (auto s : shape) n2 *= s;
-    if (n1 != n2 || !t->data || t->dtype != Q3T_F32)
-      FAIL(Q3T_RUNTIME_LOAD, "codec tensor %s: unexpected size or dtype (f32 expected)", name.c_str());
-    return t;
+  const std::string alt = checkpoint_alias(name);
+  for (int pass = 0; pass < 2; pass++) {
+    const std::string &want = pass == 0 ? name : alt;
+    if (want.empty()) break;
+    for (int i = 0; i < d->num_tensors; i++) {
+      const q3t_tensor *t = &d->tensors[i];
+      if (!t->name || want != t->name) continue;
+      int64_t n1 = 1, n2 = 1;
+      for (int k = 0; k < t->ndim; k++) n1 *= t->shape[k];
+      for (auto s : shape) n2 *= s;
+      if (n1 != n2 || !t->data || (t->dtype != Q3T_F32 && t->dtype != Q3T_BF16))
+        FAIL(Q3T_RUNTIME_LOAD, "codec tensor %s: unexpected size or dtype (f32 or bf16 expected)", want.c_str());
+      return t;
+    }
   }
   FAIL(Q3T_RUNTIME_LOAD, "missing tensor %s", name.c_str());
 }
 
+// f32 host copy of an f32 or bf16 tensor
 static std::vector<float> host(const q3t_tensor *t) {
   int64_t n = 1;
   for (int k = 0; k < t->ndim; k++) n *= t->shape[k];
-  const float *p = reinterpret_cast<const float *>(t->data);
-  return std::vector<float>(p, p + n);
+  if (t->dtype == Q3T_F32) {
+    const float *p = reinterpret_cast<const float *>(t->data);
+    return std::vector<float>(p, p + n);
+  }
+  std::vector<float> f((size_t)n);
+  const uint16_t *p = reinterpret_cast<const uint16_t *>(t->data);
+  for (int64_t i = 0; i < n; i++) {
+    const uint32_t u = (uint32_t)p[i] << 16;
+    memcpy(&f[i], &u, 4);
+  }
+  return f;
 }
 
 template <typename T>

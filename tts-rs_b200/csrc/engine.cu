@@ -63,10 +63,18 @@ struct Tensors {
   }
   const q3t_tensor *find(const std::string &name) const {
     auto it = m.find(name);
+    if (it == m.end()) {
+      const std::string alt = checkpoint_alias(name);
+      if (!alt.empty()) it = m.find(alt);
+    }
     return it == m.end() ? nullptr : it->second;
   }
   const q3t_tensor *get(const std::string &name, std::vector<int64_t> shape) const {
     auto it = m.find(name);
+    if (it == m.end()) {
+      const std::string alt = checkpoint_alias(name);
+      if (!alt.empty()) it = m.find(alt);
+    }
     if (it == m.end()) FAIL(Q3T_RUNTIME_LOAD, "missing tensor %s", name.c_str());
     const q3t_tensor *t = it->second;
     int64_t n1 = 1, n2 = 1;

@@ -41,6 +41,19 @@ struct Status {
     throw ::q3t::Status{code, ""};        \
   } while (0)
 
+// The other checkpoint spelling of a tensor name, or "" if it has none: the
+// codec's quantizer statistics are stored under `._codebook.` in legacy
+// checkpoints and `.codebook.` in newer ones, and the reference accepts both
+// (codec/weights.rs:27-33 remaps the legacy spelling at load).
+inline std::string checkpoint_alias(const std::string &n) {
+  const std::string legacy = "._codebook.", modern = ".codebook.";
+  size_t i = n.find(legacy);
+  if (i != std::string::npos) return n.substr(0, i) + modern + n.substr(i + legacy.size());
+  i = n.find(modern);
+  if (i != std::string::npos) return n.substr(0, i) + legacy + n.substr(i + modern.size());
+  return "";
+}
+
 // Device allocations owned by an object, released together.
 struct DevArena {
   std::vector<void *> ptrs;

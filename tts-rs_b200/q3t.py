@@ -103,6 +103,7 @@ EXPORTS = [
     "q3t_batch_submit", "q3t_batch_step", "q3t_batch_poll", "q3t_batch_take",
     "q3t_batch_pending", "q3t_batch_stream", "q3t_batch_free", "q3t_last_error", "q3t_version",
     "q3t_kernel_launches", "q3t_text_project", "q3t_text_dims",
+    "q3t_safetensors_open", "q3t_tensor_set_list", "q3t_tensor_set_free", "q3t_wav_write",
 ]
 
 _F = C.POINTER(C.c_float)
@@ -150,6 +151,12 @@ def lib():
         L.q3t_batch_free.restype = None
         L.q3t_text_project.argtypes = [C.c_void_p, _I64, C.c_int, _F]
         L.q3t_text_dims.argtypes = [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        L.q3t_safetensors_open.argtypes = [C.c_char_p, C.POINTER(C.c_void_p)]
+        L.q3t_tensor_set_list.argtypes = [C.c_void_p, C.POINTER(C.POINTER(Tensor)), C.POINTER(C.c_int)]
+        L.q3t_tensor_set_free.argtypes = [C.c_void_p]
+        L.q3t_tensor_set_free.restype = None
+        L.q3t_wav_write.argtypes = [C.POINTER(C.c_int16), C.c_int64, C.c_int, C.c_int, C.POINTER(C.c_uint8),
+                                    C.c_int64, _I64]
         _LIB = L
     return _LIB
 
@@ -191,14 +198,57 @@ def codec_config(c) -> CodecConfig:
     return cc
 
 
+class TensorSet:
+    """A memory-mapped .safetensors checkpoint (q3t_safetensors_open): its
+    float tensors by checkpoint name, ready for Model(tensor_sets=[...])."""
+
+    def __init__(self, path):
+        h = C.c_void_p()
+        check(lib().q3t_safetensors_open(os.fsencode(path), C.byref(h)))
+        self.h = h
+
+    def tensors(self):
+        """[(name, dtype, shape)] of the listed tensors (dtype 0 = f32, 1 = bf16)."""
+        p, n = C.POINTER(Tensor)(), C.c_int()
+        check(lib().q3t_tensor_set_list(self.h, C.byref(p), C.byref(n)))
+        return [(p[i].name.decode(), p[i].dtype, tuple(p[i].shape[:p[i].ndim])) for i in range(n.value)]
+
+    def raw(self):
+        p, n = C.POINTER(Tensor)(), C.c_int()
+        check(lib().q3t_tensor_set_list(self.h, C.byref(p), C.byref(n)))
+        return [p[i] for i in range(n.value)]
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().q3t_tensor_set_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
+def wav_bytes(pcm, sample_rate=24000, channels=1):
+    """PcmAudio::write_wav: the RIFF/WAVE image of int16 samples."""
+    pcm = np.ascontiguousarray(pcm, np.int16)
+    size = C.c_int64()
+    pp = pcm.ctypes.data_as(C.POINTER(C.c_int16)) if pcm.size else None
+    check(lib().q3t_wav_write(pp, pcm.size, sample_rate, channels, None, 0, C.byref(size)))
+    out = np.zeros(size.value, np.uint8)
+    check(lib().q3t_wav_write(pp, pcm.size, sample_rate, channels, out.ctypes.data_as(C.POINTER(C.c_uint8)),
+                              size.value, C.byref(size)))
+    return out.tobytes()
+
+
 class Model:
     """A loaded Qwen3-TTS model on one GPU (talker + code predictor and/or
     codec decoder).  Weight dicts map checkpoint names to float32 arrays."""
 
     def __init__(self, talker_cfg=None, talker_weights=None, codec_cfg=None, codec_weights=None,
-                 device=0, kv_pages=0, max_active=0):
+                 device=0, kv_pages=0, max_active=0, tensor_sets=()):
         L = lib()
         keep, tens = [], []
+        for ts in tensor_sets:
+            tens.extend(ts.raw())
         for wdict in (talker_weights or {}), (codec_weights or {}):
             for name, arr in wdict.items():
                 a = _f32(arr)
