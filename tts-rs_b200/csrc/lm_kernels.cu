@@ -269,11 +269,60 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
 #pragma unroll
     for (int i = 0; i < KA; i++) tma_load_2d(wsm + i * 16384, &a.tw, k0 + 64 * i, rg * 128, &bars[0]);
   }
+  // GX_NORM staging layout: a thread keeps one 8-column chunk (its gamma in
+  // registers, loaded before the dependency wait: weights are never written)
+  // and rows r0, r0 + rstep, ...
+  constexpr int c8n = KC / 8, rstep = 256 / c8n, NR = (N + rstep - 1) / rstep;
+  const int c8 = threadIdx.x % c8n, r0 = threadIdx.x / c8n;
+  float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0;
+  if constexpr (KA <= 4) {
+    if (a.xmode == GX_NORM && r0 < rstep) {
+      g0 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8 * 8);
+      g1 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8 * 8 + 4);
+    }
+  }
   pdl_wait();
   pdl_launch();
+  // Loads that do not wait for the token count: rows tok0 .. tok0 + N - 1 of
+  // every activation buffer exist (buffers hold >= tok0 + N rows); rows at or
+  // beyond the count are read but never used.
+  const int ts = (N + cs - 1) / cs, t_lo = ks * ts;
+  // GE_RESID: the residual rows of this warp's first two epilogue tokens
+  // (final once the previous kernel completed)
+  float4 xres[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  if (a.epi == GE_RESID) {
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      const int tt = t_lo + warp + 8 * i;
+      if (tt < t_lo + ts && tt < N)
+        xres[i] = *reinterpret_cast<const float4 *>(a.y + (size_t)(tok0 + tt) * a.ldy + rg * 128 + lane * 4);
+    }
+  }
+  // GX_NORM: this thread's x rows and (thread r < N) row r's sum-of-squares partials
+  float4 xv[KA <= 4 ? NR : 1][2];
+  float ssp[kMaxNss];
+  if constexpr (KA <= 4) {
+    if (a.xmode == GX_NORM) {
+#pragma unroll
+      for (int i = 0; i < NR; i++) {
+        const int r = r0 + i * rstep;
+        xv[i][0] = xv[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r0 < rstep && r < N) {
+          const float *xr = a.x + (size_t)((tok0 + r) * a.xrow_mul + a.xrow_add) * a.ldx + k0 + c8 * 8;
+          xv[i][0] = *reinterpret_cast<const float4 *>(xr);
+          xv[i][1] = *reinterpret_cast<const float4 *>(xr + 4);
+        }
+      }
+      if ((int)threadIdx.x < N) {
+        const float *sp = a.ss + (size_t)(tok0 + threadIdx.x) * a.xrow_mul + a.xrow_add;
+#pragma unroll
+        for (int i = 0; i < kMaxNss; i++) ssp[i] = i < a.nss ? sp[(size_t)i * a.ss_ld] : 0.f;
+      }
+    }
+  }
   int ntok = *a.ntok - tok0;
   ntok = ntok < 0 ? 0 : (ntok > N ? N : ntok);
-  const int ts = (N + cs - 1) / cs, t_lo = ks * ts, t_hi = min(t_lo + ts, ntok);
+  const int t_hi = min(t_lo + ts, ntok);
   if (a.epi == GE_QKV && (int)threadIdx.x < t_hi - t_lo) {
     // position and page of this CTA's epilogue tokens (loads overlap the GEMM)
     const int t = tok0 + t_lo + threadIdx.x;
@@ -281,68 +330,36 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
     meta[2 * threadIdx.x] = pos;
     meta[2 * threadIdx.x + 1] = a.kv.page_table[(size_t)a.tv.seq[t] * a.kv.pt_stride + (pos >> 4)];
   }
-  // GE_RESID: the residual rows of this warp's first two epilogue tokens,
-  // loaded now (they are final once the previous kernel completed)
-  float4 xres[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
-  if (a.epi == GE_RESID) {
-#pragma unroll
-    for (int i = 0; i < 2; i++) {
-      const int tt = t_lo + warp + 8 * i;
-      if (tt < t_hi) xres[i] = *reinterpret_cast<const float4 *>(a.y + (size_t)(tok0 + tt) * a.ldy + rg * 128 + lane * 4);
-    }
-  }
   if (a.xmode == GX_BF16) {
     if (threadIdx.x == 0) {
       mbar_expect_tx(&bars[1], L::kX);
 #pragma unroll
       for (int i = 0; i < KA; i++) tma_load_2d(xsm + i * L::kXAtom, &a.tx, k0 + 64 * i, tok0, &bars[1]);
     }
-  } else {
-    for (int r = threadIdx.x; r < ntok; r += blockDim.x) {
-      const float *sp = a.ss + (size_t)(tok0 + r) * a.xrow_mul + a.xrow_add;
-      float p[kMaxNss];
+  } else if constexpr (KA <= 4) {
+    // the scale of each row, then x * (1 / rms) * gamma -> bf16 at chunk
+    // (c ^ (row & 7)) of the row's 128-byte atom line
+    if ((int)threadIdx.x < ntok) {
+      float sum = ssp[0];
 #pragma unroll
-      for (int i = 0; i < kMaxNss; i++) p[i] = i < a.nss ? sp[(size_t)i * a.ss_ld] : 0.f;
-      float s = p[0];
-#pragma unroll
-      for (int i = 1; i < kMaxNss; i++) s += p[i];
-      rms[r] = 1.f / sqrtf(s / (float)a.K + a.eps);
+      for (int i = 1; i < kMaxNss; i++) sum += ssp[i];
+      rms[threadIdx.x] = 1.f / sqrtf(sum / (float)a.K + a.eps);
     }
     __syncthreads();
-    // 8-column chunks: x * (1 / rms) * gamma -> bf16, stored at chunk
-    // (c ^ (row & 7)) of the row's 128-byte atom line.  A thread keeps one
-    // chunk column (gamma in registers) and takes its rows four at a time
-    // with all loads of a batch in flight together.
-    constexpr int c8n = KC / 8, rstep = 256 / c8n;  // c8n is 16, 32 or 48
-    const int c8 = threadIdx.x % c8n, r0 = threadIdx.x / c8n;
     if (r0 < rstep) {
-      const float4 g0 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8 * 8);
-      const float4 g1 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8 * 8 + 4);
-      for (int rb = r0; rb < N; rb += 4 * rstep) {
-        float4 xv[4][2];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const int r = rb + i * rstep;
-          if (r < ntok) {
-            const float *xr = a.x + (size_t)((tok0 + r) * a.xrow_mul + a.xrow_add) * a.ldx + k0 + c8 * 8;
-            xv[i][0] = *reinterpret_cast<const float4 *>(xr);
-            xv[i][1] = *reinterpret_cast<const float4 *>(xr + 4);
-          }
+      for (int i = 0; i < NR; i++) {
+        const int r = r0 + i * rstep;
+        if (r >= N) break;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (r < ntok) {
+          const float d = rms[r];
+          v.x = pack_bf16x2(xv[i][0].x * d * g0.x, xv[i][0].y * d * g0.y);
+          v.y = pack_bf16x2(xv[i][0].z * d * g0.z, xv[i][0].w * d * g0.w);
+          v.z = pack_bf16x2(xv[i][1].x * d * g1.x, xv[i][1].y * d * g1.y);
+          v.w = pack_bf16x2(xv[i][1].z * d * g1.z, xv[i][1].w * d * g1.w);
         }
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const int r = rb + i * rstep;
-          if (r >= N) break;
-          uint4 v = make_uint4(0u, 0u, 0u, 0u);
-          if (r < ntok) {
-            const float d = rms[r];
-            v.x = pack_bf16x2(xv[i][0].x * d * g0.x, xv[i][0].y * d * g0.y);
-            v.y = pack_bf16x2(xv[i][0].z * d * g0.z, xv[i][0].w * d * g0.w);
-            v.z = pack_bf16x2(xv[i][1].x * d * g1.x, xv[i][1].y * d * g1.y);
-            v.w = pack_bf16x2(xv[i][1].z * d * g1.z, xv[i][1].w * d * g1.w);
-          }
-          *reinterpret_cast<uint4 *>(xsm + (c8 >> 3) * L::kXAtom + r * 128 + (((c8 & 7) ^ (r & 7)) << 4)) = v;
-        }
+        *reinterpret_cast<uint4 *>(xsm + (c8 >> 3) * L::kXAtom + r * 128 + (((c8 & 7) ^ (r & 7)) << 4)) = v;
       }
     }
     fence_proxy_async();
@@ -468,7 +485,8 @@ void gemm(const GemmArgs &a, int max_tok, cudaStream_t st) {
       (a.epi == GE_SILU && a.h == nullptr) || (a.xmode == GX_NORM && (a.x == nullptr || a.ss == nullptr)) ||
       ((a.epi == GE_BIAS_SILU || a.epi == GE_BIAS_BF16) && a.bias == nullptr) ||
       (a.epi == GE_BIAS_SILU && a.h == nullptr) || (a.epi == GE_BIAS_BF16 && a.y == nullptr) ||
-      a.nss > kMaxNss || (a.epi == GE_RESID && (a.ss_out == nullptr || a.y == nullptr))) {
+      a.nss > kMaxNss || (a.epi == GE_RESID && (a.ss_out == nullptr || a.y == nullptr)) ||
+      (a.xmode == GX_NORM && atoms / a.cs > 4)) {
     note(cudaErrorInvalidValue, "k_gemm (shape / arguments)");
     return;
   }
