@@ -55,6 +55,9 @@ def parse():
     p.add_argument("--only-b1", action="store_true",
                    help="run only the batch-1 talker step (prints its JSON object; for profiling)")
     p.add_argument("--b1-steps", type=int, default=256)
+    p.add_argument("--no-components", action="store_true",
+                   help="skip the predictor-loop (B=1/16/64) and codec (T=750, B=1/8) measurements")
+    p.add_argument("--c3-frames", type=int, default=512)
     p.add_argument("--kv-pages", type=int, default=8192, help="talker KV pool size (16-token pages)")
     p.add_argument("--profile", action="store_true",
                    help="bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)")
@@ -187,6 +190,80 @@ def talker_b1_step(model, cfg, L=1024, steps=256, warmup=3, peak=6558.1):
             "frac": round(byt / med / 1e3 / peak, 4)}
 
 
+def predictor_loop(model, cfg, batches=(1, 16, 64), frames=512, warmup=3, peak=6558.1):
+    """The 15-codebook code-predictor loop per decode frame at batch B
+    (teacher-forced, 16-token prompts, greedy sampler), timed on the device as
+    the frame's predictor graph (CUDA events on the batch stream).  Bytes per
+    frame-step: 15 passes x the 5 predictor layers + one lm_head each (bf16),
+    independent of B."""
+    p = cfg.predictor
+    layer = (p.hidden * (p.n_heads + 2 * p.n_kv) * p.head_dim + p.hidden * p.n_heads * p.head_dim
+             + 3 * p.hidden * p.inter) * 2
+    byt = (cfg.n_groups - 1) * (p.n_layers * layer + p.vocab * p.hidden * 2)
+    out = {"workload": f"code predictor loop, {frames} frames per batch size, 15 codebooks x 5 layers, greedy",
+           "bytes_per_frame_step": int(byt)}
+    for B in batches:
+        b = model.batch(max_active=B, codec_mode=0, keep_output=0)
+        for i in range(B):
+            prompt, trailing, pad, _ = request_inputs(10000 + i, 16, 1)
+            codes = np.random.default_rng([1, i]).integers(0, 2048, (frames + warmup + 2, 16), dtype=np.int64)
+            b.submit(prompt, trailing, pad, codes.shape[0], forced=codes)
+        st = [b.step() for _ in range(warmup + frames)]
+        b.close()
+        pm = [s["predictor_ms"] for s in st[warmup:] if s["active"] == B and s["admitted"] == 0]
+        tm = [s["talker_ms"] for s in st[warmup:] if s["active"] == B and s["admitted"] == 0]
+        med = float(np.median(pm))
+        out[f"B{B}"] = {"predictor_ms_per_frame_p50": round(med, 4), "talker_ms_per_frame_p50": round(float(np.median(tm)), 4),
+                        "achieved_gbs": round(byt / med / 1e6, 1), "frac": round(byt / med / 1e6 / peak, 4)}
+    out["peak_gbs"] = peak
+    return out
+
+
+def codec_flops_per_frame(c, T):
+    """Multiply-adds x 2 of one 12.5 Hz frame through the speech-tokenizer
+    decoder (quantizer projections, pre-conv, pre-transformer with T x T
+    attention, ConvNeXt upsampling, SnakeBeta wave decoder, output conv)."""
+    half, D, LAT, H = c.codebook_dim // 2, c.codebook_dim, c.latent, c.hidden
+    f = 2 * (2 * half * D) + 2 * 3 * D * LAT + 2 * LAT * H * 2
+    nq = c.n_heads * c.head_dim
+    f += c.n_layers * 2 * (H * (nq + 2 * c.n_kv * c.head_dim) + nq * H + 3 * H * c.inter + 2 * T * nq)
+    steps = 1
+    for r in c.up_ratios:
+        steps *= r
+        f += steps * 2 * (LAT * LAT + 7 * LAT + 2 * LAT * 4 * LAT)
+    f += steps * 2 * 7 * LAT * c.decoder_dim
+    ch = c.decoder_dim
+    for r in c.rates:
+        steps *= r
+        f += steps * 2 * (ch * (ch // 2) * 2 + 3 * (7 + 1) * (ch // 2) ** 2)
+        ch //= 2
+    return f + steps * 2 * 7 * ch
+
+
+def codec_decode_t750(model, cc, batches=(1, 8), T=750, reps=3, peak_tflops=1610.8):
+    """Speech-tokenizer decode of T frames (60 s of audio at T = 750) at batch
+    B, device time from the library's CUDA events (codes on the device ->
+    samples on the device); FLOPs from the decoder shapes."""
+    import q3t
+    fl = codec_flops_per_frame(cc, T)
+    out = {"workload": f"codec decoder, codes [B,16,{T}] uniform in [0,2048) -> 24 kHz f32 PCM",
+           "gflop_per_frame": round(fl / 1e9, 3)}
+    for B in batches:
+        codes = np.random.default_rng([B, 750]).integers(0, 2048, (B, 16, T), dtype=np.int64)
+        model.codec_decode(codes[:, :, :32])  # warm-up (workspace pools)
+        ms = []
+        for _ in range(reps):
+            model.codec_decode(codes)
+            ms.append(q3t.Model.codec_last_ms())
+        med = float(np.median(ms))
+        tf = fl * T * B / (med / 1e3) / 1e12
+        out[f"B{B}"] = {"ms": round(med, 2), "audio_s_per_s": round(B * T * FRAME_S / (med / 1e3), 1),
+                        "tflops": round(tf, 1), "frac": round(tf / peak_tflops, 4)}
+    out["peak_tflops"] = peak_tflops
+    out["peak_note"] = "measured bf16 dense GEMM burst peak (the codec's fp16 tensor-core rate is the same)"
+    return out
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -314,9 +391,12 @@ def main():
     except Exception:
         pass
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
-    b1 = None
+    b1 = c3 = c4 = None
     if rank == 0 and not args.no_b1:
         b1 = talker_b1_step(model, cfg, steps=args.b1_steps, peak=hbm_peak)
+    if rank == 0 and not args.no_components:
+        c3 = predictor_loop(model, cfg, frames=args.c3_frames, peak=hbm_peak)
+        c4 = codec_decode_t750(model, cc, peak_tflops=peaks.get("bf16_tflops", 1590.0))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -366,6 +446,8 @@ def main():
                          "algorithmic_bytes": int(np.median(bytes_)) if bytes_ else None,
                          "peak_source": "measured" if "hbm_gbs" in peaks else "fallback"},
             "talker_b1": b1,
+            "predictor_loop": c3,
+            "codec_t750": c4,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": int(launches),

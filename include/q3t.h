@@ -201,6 +201,9 @@ void q3t_session_free(q3t_session *s);
 q3t_status q3t_codec_decode(q3t_model *model, const int64_t *codes, int B, int T,
                             float *wave, int16_t *pcm, int64_t *n);
 q3t_status q3t_codec_out_len(const q3t_model *model, int T, int64_t *n);
+/* Device time (ms) of the calling thread's last q3t_codec_decode, from the
+ * codes on the device to the samples on the device (CUDA events). */
+q3t_status q3t_codec_last_ms(float *ms);
 
 /* No reference counterpart.  q3t_codec_decode that allocates nothing, for
  * callers that may not allocate device memory: a real-time audio thread
@@ -272,6 +275,8 @@ typedef struct {
   int64_t kv_tokens;         /* sum over the decode tokens of their KV length */
   int64_t h2d_bytes;         /* host -> device bytes copied during this step */
   int64_t d2h_bytes;         /* device -> host bytes copied during this step */
+  float predictor_ms;        /* device time of the frame's code-predictor loop (15 codebooks) */
+  float talker_ms;           /* device time of the frame's talker decode, codec_head and sampling */
 } q3t_step_stats;
 
 typedef struct q3t_batch q3t_batch;

@@ -1169,6 +1169,10 @@ static void check_codes(const CodecModel *c, const int64_t *codes, int64_t n) {
            c->c.codebook_size);
 }
 
+// device time of the calling thread's last q3t_codec_decode (codes on the
+// device -> samples on the device)
+static thread_local float g_codec_ms = 0.f;
+
 void codec_decode_host_codes(q3t_model *m, const int64_t *codes, int B, int T, float *wave, int16_t *pcm,
                              cudaStream_t st) {
   CodecModel *c = m->codec;
@@ -1186,13 +1190,27 @@ void codec_decode_host_codes(q3t_model *m, const int64_t *codes, int B, int T, f
   CK(cudaMemcpyAsync(dc, codes, ncodes * 8, cudaMemcpyHostToDevice, st));
   if (wave) CK(cudaMallocAsync((void **)&dw, (size_t)B * n * 4, st));
   if (pcm) CK(cudaMallocAsync((void **)&dp, (size_t)B * n * 2, st));
+  cudaEvent_t e0, e1;
+  CK(cudaEventCreate(&e0));
+  CK(cudaEventCreate(&e1));
+  CK(cudaEventRecord(e0, st));
   decode_device(c, dc, B, T, dw, dp, st);
+  CK(cudaEventRecord(e1, st));
   if (wave) CK(cudaMemcpyAsync(wave, dw, (size_t)B * n * 4, cudaMemcpyDeviceToHost, st));
   if (pcm) CK(cudaMemcpyAsync(pcm, dp, (size_t)B * n * 2, cudaMemcpyDeviceToHost, st));
   CK(cudaFreeAsync(dc, st));
   if (dw) CK(cudaFreeAsync(dw, st));
   if (dp) CK(cudaFreeAsync(dp, st));
   CK(cudaStreamSynchronize(st));
+  CK(cudaEventElapsedTime(&g_codec_ms, e0, e1));
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+}
+
+extern "C" q3t_status q3t_codec_last_ms(float *ms) {
+  if (!ms) return Q3T_INVALID_INPUT;
+  *ms = g_codec_ms;
+  return Q3T_OK;
 }
 
 // ---------------------------------------------------------------------------

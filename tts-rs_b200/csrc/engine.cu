@@ -337,6 +337,7 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
   CK(cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking));
   CK(cudaEventCreate(&b->ev0));
   CK(cudaEventCreate(&b->ev1));
+  for (auto &e : b->evf) CK(cudaEventCreate(&e));
   auto &ar = b->ar;
   const int A = b->A;
   // talker KV pool
@@ -447,6 +448,8 @@ static void batch_destroy(q3t_batch *b) {
   if (b->h_codes) cudaFreeHost(b->h_codes);
   if (b->ev0) cudaEventDestroy(b->ev0);
   if (b->ev1) cudaEventDestroy(b->ev1);
+  for (auto &e : b->evf)
+    if (e) cudaEventDestroy(e);
   if (b->st) cudaStreamDestroy(b->st);
   b->ar.release();
 }
@@ -985,7 +988,16 @@ static void enqueue_frame(q3t_batch *b, int mt, int max_units) {
       fprintf(stderr, "   %-36s %4d x %8.2f us = %9.1f us\n", kv.first.c_str(), kv.second.first,
               kv.second.second / kv.second.first, kv.second.second);
   } else {
-    run_graph(b, std::make_tuple(0, mt, max_units), [&] { run_phases(pr.data(), (int)pr.size(), b->st); });
+    // two graphs, the code-predictor loop and the talker step, with an event
+    // between them so a step reports both device times
+    const int talker_from = (int)pr.size() - m_talker_phases(b);
+    CK(cudaEventRecord(b->evf[0], b->st));
+    run_graph(b, std::make_tuple(4, mt, max_units), [&] { run_phases(pr.data(), talker_from, b->st); });
+    CK(cudaEventRecord(b->evf[1], b->st));
+    run_graph(b, std::make_tuple(5, mt, max_units),
+              [&] { run_phases(pr.data() + talker_from, (int)pr.size() - talker_from, b->st); });
+    CK(cudaEventRecord(b->evf[2], b->st));
+    b->frame_timed = true;
   }
   check_launches();
 }
@@ -1216,11 +1228,16 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
   }
   const int B = (int)act.size();
   S.active = B;
+  b->frame_timed = false;
   auto report = [&] {
     CK(cudaEventRecord(b->ev1, b->st));
     CK(cudaEventSynchronize(b->ev1));
     CK(cudaEventElapsedTime(&b->last_ms, b->ev0, b->ev1));
     S.device_ms = b->last_ms;
+    if (b->frame_timed) {
+      CK(cudaEventElapsedTime(&S.predictor_ms, b->evf[0], b->evf[1]));
+      CK(cudaEventElapsedTime(&S.talker_ms, b->evf[1], b->evf[2]));
+    }
     S.h2d_bytes = b->h2d;
     S.d2h_bytes = b->d2h;
     b->h2d = b->d2h = 0;

@@ -177,6 +177,8 @@ struct q3t_batch {
   int A = 0, G = 0, H = 0, V = 0, PV = 0, NQKV = 0, NQKVP = 0, I2 = 0;
   cudaStream_t st = nullptr;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  cudaEvent_t evf[3] = {nullptr, nullptr, nullptr};  // decode frame: start, predictor done, talker done
+  bool frame_timed = false;
   q3t::DevArena ar;
   // talker pool
   uint16_t *tk = nullptr, *tv = nullptr;

@@ -91,7 +91,8 @@ class BatchDesc(C.Structure):
 class StepStats(C.Structure):
     _fields_ = [("active", C.c_int), ("admitted", C.c_int), ("retired", C.c_int),
                 ("frames", C.c_int64), ("samples", C.c_int64), ("device_ms", C.c_float),
-                ("kv_tokens", C.c_int64), ("h2d_bytes", C.c_int64), ("d2h_bytes", C.c_int64)]
+                ("kv_tokens", C.c_int64), ("h2d_bytes", C.c_int64), ("d2h_bytes", C.c_int64),
+                ("predictor_ms", C.c_float), ("talker_ms", C.c_float)]
 
 
 EXPORTS = [
@@ -104,6 +105,7 @@ EXPORTS = [
     "q3t_batch_pending", "q3t_batch_stream", "q3t_batch_free", "q3t_last_error", "q3t_version",
     "q3t_kernel_launches", "q3t_text_project", "q3t_text_dims",
     "q3t_safetensors_open", "q3t_tensor_set_list", "q3t_tensor_set_free", "q3t_wav_write",
+    "q3t_codec_last_ms",
 ]
 
 _F = C.POINTER(C.c_float)
@@ -137,6 +139,7 @@ def lib():
         L.q3t_session_free.restype = None
         L.q3t_codec_decode.argtypes = [C.c_void_p, _I64, C.c_int, C.c_int, _F, C.POINTER(C.c_int16), _I64]
         L.q3t_codec_out_len.argtypes = [C.c_void_p, C.c_int, _I64]
+        L.q3t_codec_last_ms.argtypes = [_F]
         L.q3t_codec_decode_static.argtypes = [C.c_void_p, _I64, C.c_int, C.c_int, _F,
                                               C.POINTER(C.c_int16), _I64, C.c_void_p]
         L.q3t_batch_create.argtypes = [C.c_void_p, C.POINTER(BatchDesc), C.POINTER(C.c_void_p)]
@@ -315,6 +318,13 @@ class Model:
         check(lib().q3t_text_project(self.h, ids.ctypes.data_as(_I64) if len(ids) else None, len(ids), _fp(out)))
         return out
 
+    @staticmethod
+    def codec_last_ms():
+        """Device time (ms) of this thread's last codec decode."""
+        ms = C.c_float()
+        check(lib().q3t_codec_last_ms(C.byref(ms)))
+        return ms.value
+
     def batch(self, max_active=64, codec_mode=0, chunk_frames=16, left_context=8, keep_output=1):
         return Batch(self, max_active, codec_mode, chunk_frames, left_context, keep_output)
 
@@ -446,7 +456,8 @@ class Batch:
         check(lib().q3t_batch_step(self.h, C.byref(s)))
         return {"active": s.active, "admitted": s.admitted, "retired": s.retired,
                 "frames": s.frames, "samples": s.samples, "device_ms": s.device_ms,
-                "kv_tokens": s.kv_tokens, "h2d_bytes": s.h2d_bytes, "d2h_bytes": s.d2h_bytes}
+                "kv_tokens": s.kv_tokens, "h2d_bytes": s.h2d_bytes, "d2h_bytes": s.d2h_bytes,
+                "predictor_ms": s.predictor_ms, "talker_ms": s.talker_ms}
 
     def poll(self, rid):
         st, fr, sm = C.c_int(), C.c_int64(), C.c_int64()
