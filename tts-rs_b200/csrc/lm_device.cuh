@@ -43,21 +43,27 @@ Q3T_DEV size_t page_elem(const KVView &kv, int seq, int pos, int h) {
 
 // q_norm / k_norm + rotate-half RoPE (attention.rs:49-69, 126-134): one warp
 // per head, lane l holds dims [4l, 4l+4); the partner of dim d is d +- 64,
-// i.e. lane l ^ 16.
-Q3T_DEV void norm_rope_lane(float4 v, const float *__restrict__ gm, float eps, int lane, int pos,
-                            const float *__restrict__ inv_freq, float out[4]) {
+// i.e. lane l ^ 16.  gm / fr: this lane's gamma and inverse frequencies.
+Q3T_DEV void norm_rope_reg(float4 v, float4 gm, float4 fr, float eps, int lane, int pos, float out[4]) {
   const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
   const float rms = sqrtf(ss / 128.f + eps);
-  float e[4] = {v.x / rms * gm[lane * 4 + 0], v.y / rms * gm[lane * 4 + 1], v.z / rms * gm[lane * 4 + 2],
-                v.w / rms * gm[lane * 4 + 3]};
+  const float e[4] = {v.x / rms * gm.x, v.y / rms * gm.y, v.z / rms * gm.z, v.w / rms * gm.w};
+  const float f[4] = {fr.x, fr.y, fr.z, fr.w};
 #pragma unroll
   for (int i = 0; i < 4; i++) {
     const float p = __shfl_xor_sync(0xffffffffu, e[i], 16);
     const int d = lane * 4 + i;
     float s, c;
-    sincosf((float)pos * inv_freq[d & 63], &s, &c);
+    sincosf((float)pos * f[i], &s, &c);
     out[i] = d < 64 ? e[i] * c - p * s : e[i] * c + p * s;
   }
+}
+// The same with gamma and the inverse frequencies read here: lane l uses
+// gm[4l .. 4l + 3] and inv_freq[(4l .. 4l + 3) mod 64].
+Q3T_DEV void norm_rope_lane(float4 v, const float *__restrict__ gm, float eps, int lane, int pos,
+                            const float *__restrict__ inv_freq, float out[4]) {
+  norm_rope_reg(v, *reinterpret_cast<const float4 *>(gm + lane * 4),
+                *reinterpret_cast<const float4 *>(inv_freq + ((lane * 4) & 63)), eps, lane, pos, out);
 }
 
 // ---------------------------------------------------------------------------

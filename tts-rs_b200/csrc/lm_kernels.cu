@@ -190,7 +190,7 @@ Q3T_DEV void store_bf16x4(uint16_t *dst, float a, float b, float c, float d) {
 // warp); tm = {position, page} of t for GE_QKV; xpre = the residual rows
 // already loaded for GE_RESID when have_pre
 Q3T_DEV void gemm_epilogue(const GemmArgs &a, int t, int rg, int lane, float4 v, const int *tm, float4 xpre,
-                           bool have_pre) {
+                           bool have_pre, float4 gqk, float4 fr) {
   const int n = rg * 128 + lane * 4;
   if (a.epi == GE_F32) {
     *reinterpret_cast<float4 *>(a.y + (size_t)t * a.ldy + n) = v;
@@ -222,14 +222,14 @@ Q3T_DEV void gemm_epilogue(const GemmArgs &a, int t, int rg, int lane, float4 v,
     const int pos = tm[0];
     float o[4];
     if (rg < a.nh) {
-      norm_rope_lane(v, a.q_norm, a.eps, lane, pos, a.inv_freq, o);
+      norm_rope_reg(v, gqk, fr, a.eps, lane, pos, o);
       store_bf16x4(a.q + (size_t)t * a.nh * 128 + rg * 128 + lane * 4, o[0], o[1], o[2], o[3]);
       return;
     }
     const int h = rg < a.nh + a.nkv ? rg - a.nh : rg - a.nh - a.nkv;
     const size_t e = a.layer * a.kv.layer_stride + (((size_t)tm[1] * a.kv.n_kv + h) * 16 + (pos & 15)) * 128 + lane * 4;
     if (rg < a.nh + a.nkv) {
-      norm_rope_lane(v, a.k_norm, a.eps, lane, pos, a.inv_freq, o);
+      norm_rope_reg(v, gqk, fr, a.eps, lane, pos, o);
       store_bf16x4(a.kv.k + e, o[0], o[1], o[2], o[3]);
     } else {
       store_bf16x4(a.kv.v + e, v.x, v.y, v.z, v.w);
@@ -275,6 +275,13 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
   constexpr int c8n = KC / 8, rstep = 256 / c8n, NR = (N + rstep - 1) / rstep;
   const int c8 = threadIdx.x % c8n, r0 = threadIdx.x / c8n;
   float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0;
+  // GE_QKV: this lane's q_norm / k_norm gamma (by the row block's head) and
+  // RoPE inverse frequencies, for the epilogue
+  float4 gqk = g0, fr = g0;
+  if (a.epi == GE_QKV && rg < a.nh + a.nkv) {
+    gqk = *reinterpret_cast<const float4 *>((rg < a.nh ? a.q_norm : a.k_norm) + lane * 4);
+    fr = *reinterpret_cast<const float4 *>(a.inv_freq + ((lane * 4) & 63));
+  }
   if constexpr (KA <= 4) {
     if (a.xmode == GX_NORM && r0 < rstep) {
       g0 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8 * 8);
@@ -421,7 +428,7 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
         }
     }
     const int i = (tt - t_lo - warp) >> 3;
-    gemm_epilogue(a, tok0 + tt, rg, lane, v, meta + 2 * (tt - t_lo), i == 0 ? xres[0] : xres[1], i < 2);
+    gemm_epilogue(a, tok0 + tt, rg, lane, v, meta + 2 * (tt - t_lo), i == 0 ? xres[0] : xres[1], i < 2, gqk, fr);
   }
   if (cs > 1) cluster_sync();  // no CTA leaves while another still reads its tile
   __syncthreads();

@@ -524,24 +524,6 @@ Q3T_DEV void gemv_stage(const MkArgs &a, int si, const MkGemv &g, int T, unsigne
   }
 }
 
-// q_norm / k_norm + rotate-half RoPE of one head row (the arithmetic of
-// norm_rope_lane, lm_device.cuh) with this lane's gamma and inverse
-// frequencies already in registers: lane l holds dims [4l, 4l + 4).
-Q3T_DEV void norm_rope_reg(float4 v, float4 gm, float4 fr, float eps, int lane, int pos, float out[4]) {
-  const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
-  const float rms = sqrtf(ss / 128.f + eps);
-  const float e[4] = {v.x / rms * gm.x, v.y / rms * gm.y, v.z / rms * gm.z, v.w / rms * gm.w};
-  const float f[4] = {fr.x, fr.y, fr.z, fr.w};
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const float p = __shfl_xor_sync(0xffffffffu, e[i], 16);
-    const int d = lane * 4 + i;
-    float s, c;
-    sincosf((float)pos * f[i], &s, &c);
-    out[i] = d < 64 ? e[i] * c - p * s : e[i] * c + p * s;
-  }
-}
-
 Q3T_DEV void attn_stage(const MkArgs &a, int si, const MkAttn &at, int T, unsigned char *ring, MkMisc &M,
                         uint32_t &ci, uint32_t &err) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
