@@ -55,6 +55,9 @@ def parse():
     p.add_argument("--only-b1", action="store_true",
                    help="run only the batch-1 talker step (prints its JSON object; for profiling)")
     p.add_argument("--b1-steps", type=int, default=256)
+    p.add_argument("--only-codec", action="store_true",
+                   help="run only the T=750 codec decode measurement (prints its JSON object; for profiling)")
+    p.add_argument("--codec-batches", default="1,8")
     p.add_argument("--no-components", action="store_true",
                    help="skip the predictor-loop (B=1/16/64) and codec (T=750, B=1/8) measurements")
     p.add_argument("--c3-frames", type=int, default=512)
@@ -283,6 +286,14 @@ def main():
 
     cfg = S.TalkerConfig()
     cc = S.CodecConfig()
+    if args.only_codec:
+        model = q3t.Model(codec_cfg=cc, codec_weights=S.make_codec_weights(cc, 0), device=local)
+        pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))).get("bf16_tflops", 1590.0) \
+            if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
+        bs = tuple(int(x) for x in args.codec_batches.split(","))
+        print(json.dumps(codec_decode_t750(model, cc, batches=bs, peak_tflops=pk)), flush=True)
+        model.close()
+        return
     if args.only_b1:
         model = q3t.Model(cfg, S.make_talker_weights(cfg, 0), device=local, kv_pages=128, max_active=1)
         peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))).get("hbm_gbs", 6650.0) \

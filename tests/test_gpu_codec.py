@@ -33,7 +33,7 @@ def _codes(B, T, seed):
     return np.random.default_rng([seed, 13]).integers(0, 2048, size=(B, 16, T), dtype=np.int64)
 
 
-@pytest.mark.parametrize("B,T", [(1, 1), (1, 4), (2, 7), (1, 24)])
+@pytest.mark.parametrize("B,T", [(1, 1), (1, 4), (2, 7), (1, 24), (1, 70)])
 def test_codec_decode_matches_oracle(codec, B, T):
     cc, model, oc = codec
     codes = _codes(B, T, seed=T)

@@ -562,6 +562,144 @@ __global__ void __launch_bounds__(128) k_codec_attn(const float *q, const float 
   }
 }
 
+// The same attention on the tensor cores (flash-attention style): a CTA takes
+// 64 queries of one head, 4 warps x 16 query rows; keys and values stream
+// through shared memory in tiles of 64.  S = Q K^T and O += P V run as
+// mma.sync m16n8k16 with fp16 operands and f32 accumulators (the S
+// accumulators are reused as the A fragments of P), the softmax is online in
+// f32, keys beyond T are masked, and the output is rounded to fp16 as above.
+constexpr int kCaRows = 64, kCaLd = 72;  // padded rows: conflict-free ldmatrix
+
+Q3T_DEV void ldmatrix_x2_trans(uint32_t &r0, uint32_t &r1, const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];\n"
+               : "=r"(r0), "=r"(r1)
+               : "r"(smem_addr(p)));
+}
+
+Q3T_DEV uint32_t pack_half2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// rows [r0, r0 + 64) of a [T][64] f32 head matrix -> fp16 [64][kCaLd] in shared memory (zeros past T)
+Q3T_DEV void ca_load_tile(__half *dst, const float *src, int r0, int T) {
+  for (int e = threadIdx.x; e < kCaRows * 16; e += blockDim.x) {
+    const int row = e >> 4, c4 = e & 15;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r0 + row < T) v = *reinterpret_cast<const float4 *>(src + (size_t)(r0 + row) * 64 + c4 * 4);
+    uint2 u;
+    u.x = pack_half2(v.x, v.y);
+    u.y = pack_half2(v.z, v.w);
+    *reinterpret_cast<uint2 *>(dst + row * kCaLd + c4 * 4) = u;
+  }
+}
+
+__global__ void __launch_bounds__(128) k_codec_attn_tc(const float *q, const float *k, const float *v, int T, int nh,
+                                                       int nkv, float scale, __half *out) {
+  __shared__ __align__(16) __half Qs[kCaRows * kCaLd], Ks[kCaRows * kCaLd], Vs[kCaRows * kCaLd];
+  const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * kCaRows;
+  const int hk = h / (nh / nkv);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const float *qb = q + ((size_t)b * nh + h) * T * 64;
+  const float *kb = k + ((size_t)b * nkv + hk) * T * 64;
+  const float *vb = v + ((size_t)b * nkv + hk) * T * 64;
+  ca_load_tile(Qs, qb, q0, T);
+  __syncthreads();
+  uint32_t qa[4][4];  // A fragments of this warp's 16 query rows, 4 k-steps of 16 dims
+#pragma unroll
+  for (int ks = 0; ks < 4; ks++)
+    ldmatrix_x4(qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3],
+                Qs + (warp * 16 + (lane & 15)) * kCaLd + ks * 16 + (lane >> 4) * 8);
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows g and g + 8
+  for (int j0 = 0; j0 < T; j0 += kCaRows) {
+    __syncthreads();  // the previous tile is consumed
+    ca_load_tile(Ks, kb, j0, T);
+    ca_load_tile(Vs, vb, j0, T);
+    __syncthreads();
+    float s[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; nt++) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 4; ks++) {
+        uint32_t b0, b1;
+        ldmatrix_x2(b0, b1, Ks + (nt * 8 + (lane & 7)) * kCaLd + ks * 16 + ((lane >> 3) & 1) * 8);
+        mma_f16(s[nt], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
+      }
+    }
+    float mx0 = m0, mx1 = m1;
+#pragma unroll
+    for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int key = j0 + nt * 8 + 2 * t + (e & 1);
+        s[nt][e] = key < T ? s[nt][e] * scale : -INFINITY;
+        if (e < 2)
+          mx0 = fmaxf(mx0, s[nt][e]);
+        else
+          mx1 = fmaxf(mx1, s[nt][e]);
+      }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float c0 = expf(m0 - mx0), c1 = expf(m1 - mx1);  // the first tile has a valid key: mx finite
+    m0 = mx0;
+    m1 = mx1;
+    float r0 = 0.f, r1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 8; nt++) {
+      s[nt][0] = expf(s[nt][0] - m0);
+      s[nt][1] = expf(s[nt][1] - m0);
+      s[nt][2] = expf(s[nt][2] - m1);
+      s[nt][3] = expf(s[nt][3] - m1);
+      r0 += s[nt][0] + s[nt][1];
+      r1 += s[nt][2] + s[nt][3];
+    }
+    l0 = l0 * c0 + r0;  // this lane's share; the quad sums it at the end
+    l1 = l1 * c1 + r1;
+#pragma unroll
+    for (int dt = 0; dt < 8; dt++) {
+      o[dt][0] *= c0;
+      o[dt][1] *= c0;
+      o[dt][2] *= c1;
+      o[dt][3] *= c1;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+      const uint32_t pa0 = pack_half2(s[2 * kk][0], s[2 * kk][1]), pa1 = pack_half2(s[2 * kk][2], s[2 * kk][3]);
+      const uint32_t pa2 = pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      const uint32_t pa3 = pack_half2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int dt = 0; dt < 8; dt++) {
+        uint32_t b0, b1;
+        ldmatrix_x2_trans(b0, b1, Vs + (kk * 16 + (lane & 15)) * kCaLd + dt * 8);
+        mma_f16(o[dt], pa0, pa1, pa2, pa3, b0, b1);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 1; off < 4; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  const int ra = q0 + warp * 16 + g, rb = ra + 8;
+#pragma unroll
+  for (int dt = 0; dt < 8; dt++) {
+    const int d = dt * 8 + 2 * t;
+    if (ra < T)
+      *reinterpret_cast<__half2 *>(out + ((size_t)b * T + ra) * nh * 64 + h * 64 + d) =
+          __floats2half2_rn(o[dt][0] / l0, o[dt][1] / l0);
+    if (rb < T)
+      *reinterpret_cast<__half2 *>(out + ((size_t)b * T + rb) * nh * 64 + h * 64 + d) =
+          __floats2half2_rn(o[dt][2] / l1, o[dt][3] / l1);
+  }
+}
+
 __global__ void k_silu_mul_h(const float *gu, int I, __half *out) {
   const size_t row = blockIdx.x;
   for (int i = threadIdx.x; i < I; i += blockDim.x) {
@@ -1058,7 +1196,10 @@ static void decode_with(CodecModel *c, const CodecScratch &ws, const int64_t *d_
     a.Yf = F1;
     launch_conv(a, 1, st);
     k_codec_rope<<<M0, 256, 0, st>>>(F1, T, nh, nkv, 64, c->rope_th, Q, K, V);
-    k_codec_attn<<<dim3((T + 127) / 128, nh, B), 128, 0, st>>>(Q, K, V, T, nh, nkv, 0.125f, G);
+    if (getenv("Q3T_CODEC_ATTN_F32"))
+      k_codec_attn<<<dim3((T + 127) / 128, nh, B), 128, 0, st>>>(Q, K, V, T, nh, nkv, 0.125f, G);
+    else
+      k_codec_attn_tc<<<dim3((T + kCaRows - 1) / kCaRows, nh, B), 128, 0, st>>>(Q, K, V, T, nh, nkv, 0.125f, G);
     CK(cudaGetLastError());
     a = conv_args(Lw.o, G, B, T, 0, 1, T, 1, T);
     a.Yf = hres;
