@@ -86,3 +86,17 @@ def test_codec_long_sequence_properties(codec):
     assert np.isfinite(wave).all() and np.abs(wave).max() <= 1.0
     assert snr_db(wave[1], wave[0]) > 80
     assert wave[0].std() > 1e-3
+
+
+def test_codec_fused_residual_unit_matches_two_launches(codec, monkeypatch):
+    """The 96-channel residual units run as one launch (k7 conv, SnakeBeta,
+    k1 conv on the tensor cores, intermediate kept in shared memory); the
+    two-launch path (Q3T_CODEC_UNFUSED=1) rounds at the same points, so the
+    two decodes agree far inside the oracle tolerance."""
+    cc, model, oc = codec
+    codes = _codes(2, 70, seed=11)
+    fused = model.codec_decode(codes)
+    monkeypatch.setenv("Q3T_CODEC_UNFUSED", "1")
+    split = model.codec_decode(codes)
+    for b in range(2):
+        assert snr_db(fused[b], split[b]) > 90

@@ -219,14 +219,35 @@ static size_t conv_smem(int BN) { return (size_t)kStages * (kBM + BN) * kLDS * s
 //                  k_conv epilogue.
 // Operands are K-major with SWIZZLE_128B (ACH = 64) or SWIZZLE_64B (ACH = 32)
 // atoms.  Every mbarrier wait is bounded; a timeout sets a bit in *err.
+//
+// FUSE = 1 runs a whole residual unit (wave.rs:37-56) when the CTA owns all
+// N = C channels:  y = x + conv1(snake2(conv7_d(h) + b7)) + b1.  After the
+// k7 accumulator is complete, all 8 warps read it back, apply b7 and SnakeBeta
+// act2 and store the fp16 result, swizzled exactly as TMA would have stored
+// it, into the A halves of the next Cin / ACH ring stages; the producer
+// streams the k1 weight chunks into the B halves of the same stages; the MMA
+// warp runs the k1 GEMM into the same TMEM columns, and the epilogue above
+// finishes it (b1, residual, next SnakeBeta).  The intermediate activation
+// never leaves shared memory.
 // ---------------------------------------------------------------------------
 struct ConvTc {
   CUtensorMap tx;  // X [B][Lin][Cin], box ACH x 128 x 1
   CUtensorMap tw;  // W [phases * taps * Cout][Cin], box ACH x N
-  ConvArgs a;
+  CUtensorMap tw1; // FUSE: k1 weights W1 [Cout][Cout], box ACH x N
+  ConvArgs a;      // FUSE: a.bias is b1 (the k1 bias); the epilogue fields describe the unit's output
+  const float *mid_bias;  // FUSE: b7
+  const float *mid_a, *mid_b;  // FUSE: act2 SnakeBeta (e^alpha, 1 / (e^beta + 1e-9))
   int tiles;       // 128-step tiles per sequence
   int *err;
 };
+
+// Byte offset of 16-byte chunk j of row r in a K-major tile of ACH fp16 per
+// row, SWIZZLE_128B (ACH = 64) or SWIZZLE_64B (ACH = 32), as TMA stores it
+// into a 1024-byte-aligned buffer.
+template <int ACH>
+Q3T_DEV uint32_t swz_off(int r, int j) {
+  return ACH == 64 ? (uint32_t)(r * 128 + ((j ^ (r & 7)) << 4)) : (uint32_t)(r * 64 + ((j ^ ((r >> 1) & 3)) << 4));
+}
 
 template <int N, int ACH, int S>
 struct ConvTcSmem {
@@ -234,9 +255,10 @@ struct ConvTcSmem {
   static constexpr size_t kBytes = (size_t)S * kStage + (2 * S + 2) * 8 + 1024;
 };
 
-template <int N, int ACH, int S>
+template <int N, int ACH, int S, int FUSE>
 __global__ void __launch_bounds__(256) k_conv_tc(const __grid_constant__ ConvTc c) {
   using L = ConvTcSmem<N, ACH, S>;
+  static_assert(!FUSE || N / ACH <= S, "the fused k1 GEMM needs one ring stage per input chunk");
   constexpr uint32_t kCols = N <= 128 ? 128 : 256;
   extern __shared__ unsigned char csm_raw[];
   unsigned char *sm = csm_raw + ((1024 - (smem_addr(csm_raw) & 1023)) & 1023);
@@ -274,6 +296,17 @@ __global__ void __launch_bounds__(256) k_conv_tc(const __grid_constant__ ConvTc 
       tma_load_3d(st, &c.tx, c0, tq0 + a.in_off + tap * a.dil, b, &full[s]);
       tma_load_2d(st + L::kA, &c.tw, c0, (phase * a.taps + tap) * a.Cout + n0, &full[s]);
     }
+    if (FUSE && !err) {  // k1 weight chunks into the B halves of the next stages
+      for (int ks = KS; ks < KS + N / ACH; ks++) {
+        const int s = ks % S, i = ks / S;
+        if (i > 0 && !mbar_wait(&empty[s], (i - 1) & 1)) {
+          err |= 1u;
+          break;
+        }
+        mbar_expect_tx(&full[s], L::kB);
+        tma_load_2d(sm + s * L::kStage + L::kA, &c.tw1, (ks - KS) * ACH, 0, &full[s]);
+      }
+    }
   } else if (warp == 1 && lane == 0) {  // MMA issuer
     constexpr uint32_t idesc = umma_idesc_f16(128, N);
     for (int ks = 0; ks < KS; ks++) {
@@ -293,7 +326,59 @@ __global__ void __launch_bounds__(256) k_conv_tc(const __grid_constant__ ConvTc 
       umma_commit(&empty[s]);
     }
     umma_commit(accb);
-    if (!mbar_wait(accb, 0)) err |= 4u;  // the other threads block in the barrier below, not polling
+    if (!FUSE && !mbar_wait(accb, 0)) err |= 4u;  // the other threads block in the barrier below, not polling
+  }
+  if (FUSE) {
+    // act2(acc + b7) -> fp16 A operand of the k1 GEMM, chunk q of ACH
+    // channels in the A half of ring stage (KS + q) % S
+    if (!mbar_wait(accb, 0)) err |= 4u;
+    tc_fence_after();
+    __syncwarp();  // lane 0 of warps 0 / 1 comes from its producer / MMA loop; tcgen05.ld is warp-aligned
+    const int r = 32 * (warp & 3) + lane;
+    const uint32_t trow = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+    constexpr int G = N / 16;
+#pragma unroll 1
+    for (int g = (warp >> 2) * (G / 2); g < ((warp >> 2) + 1) * (G / 2); g++) {
+      float v[16];
+      tmem_ld16(trow + 16 * g, v);
+      const int col = 16 * g, q = col / ACH, j0 = (col - q * ACH) / 8;
+      unsigned char *dst = sm + ((KS + q) % S) * L::kStage;
+      uint32_t h[8];
+#pragma unroll
+      for (int e = 0; e < 16; e += 2) {
+        const int n = col + e;
+        const float y0 = snake(v[e] + c.mid_bias[n], c.mid_a[n], c.mid_b[n]);
+        const float y1 = snake(v[e + 1] + c.mid_bias[n + 1], c.mid_a[n + 1], c.mid_b[n + 1]);
+        const __half2 p = __floats2half2_rn(y0, y1);
+        h[e / 2] = *reinterpret_cast<const uint32_t *>(&p);
+      }
+      *reinterpret_cast<uint4 *>(dst + swz_off<ACH>(r, j0)) = make_uint4(h[0], h[1], h[2], h[3]);
+      *reinterpret_cast<uint4 *>(dst + swz_off<ACH>(r, j0 + 1)) = make_uint4(h[4], h[5], h[6], h[7]);
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1 && lane == 0) {
+      tc_fence_after();
+      constexpr uint32_t idesc = umma_idesc_f16(128, N);
+      for (int ks = KS; ks < KS + N / ACH && !err; ks++) {
+        const int s = ks % S;
+        if (!mbar_wait(&full[s], (ks / S) & 1)) {
+          err |= 2u;
+          break;
+        }
+        tc_fence_after();
+        const unsigned char *st = sm + s * L::kStage;
+#pragma unroll
+        for (int kk = 0; kk < ACH / 16; kk++) {
+          const uint64_t ad = ACH == 64 ? sw128_desc(st + kk * 32) : sw64_desc(st + kk * 32);
+          const uint64_t bd = ACH == 64 ? sw128_desc(st + L::kA + kk * 32) : sw64_desc(st + L::kA + kk * 32);
+          umma_kf16(tmem, ad, bd, idesc, (ks > KS || kk > 0) ? 1u : 0u);
+        }
+      }
+      umma_commit(accb);
+      if (!mbar_wait(accb, 1)) err |= 4u;
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -384,17 +469,37 @@ __global__ void __launch_bounds__(256) k_conv_tc(const __grid_constant__ ConvTc 
 
 static int *g_conv_err = nullptr;  // device word for bounded-wait timeouts of k_conv_tc
 
-template <int N, int ACH, int S>
-static void conv_tc_launch(const ConvArgs &a, int phases, cudaStream_t st) {
+// The fused residual unit's extra operands (FUSE = 1).
+struct ConvFuse {
+  const __half *W1;  // [C][C]
+  const float *mid_bias, *mid_a, *mid_b;
+};
+
+template <int N, int ACH, int S, int FUSE>
+static void conv_tc_launch(const ConvArgs &a, int phases, cudaStream_t st, const ConvFuse *fu = nullptr) {
   using L = ConvTcSmem<N, ACH, S>;
   static bool attr = false;
   if (!attr) {
-    CK(cudaFuncSetAttribute(k_conv_tc<N, ACH, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kBytes));
+    CK(cudaFuncSetAttribute(k_conv_tc<N, ACH, S, FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            (int)L::kBytes));
     attr = true;
   }
   ConvTc c;
   memset(&c, 0, sizeof c);
   const CUtensorMapSwizzle sw = ACH == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  if (FUSE) {
+    if (!fu || a.Cout != N || a.Cin != N || phases != 1)
+      FAIL(Q3T_INVALID_INPUT, "codec fused residual unit: %d -> %d channels, %d phases (%d -> %d, 1 expected)",
+           a.Cin, a.Cout, phases, N, N);
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)N};
+    const uint64_t strides[1] = {(uint64_t)N * 2};
+    const uint32_t box[2] = {(uint32_t)ACH, (uint32_t)N};
+    if (!make_tmap(&c.tw1, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, fu->W1, dims, strides, box, sw))
+      FAIL(Q3T_CUDA_ERROR, "codec conv: TMA descriptor of the k1 weights failed");
+    c.mid_bias = fu->mid_bias;
+    c.mid_a = fu->mid_a;
+    c.mid_b = fu->mid_b;
+  }
   {
     const uint64_t dims[3] = {(uint64_t)a.Cin, (uint64_t)a.Lin, (uint64_t)a.B};
     const uint64_t strides[2] = {(uint64_t)a.Cin * 2, (uint64_t)a.Lin * a.Cin * 2};
@@ -413,7 +518,7 @@ static void conv_tc_launch(const ConvArgs &a, int phases, cudaStream_t st) {
   c.tiles = (a.Lq + 127) / 128;
   c.err = g_conv_err;
   const dim3 grid((unsigned)(a.B * c.tiles), a.Cout / N, phases);
-  k_conv_tc<N, ACH, S><<<grid, 256, L::kBytes, st>>>(c);
+  k_conv_tc<N, ACH, S, FUSE><<<grid, 256, L::kBytes, st>>>(c);
 }
 
 static void launch_conv(const ConvArgs &a, int phases, cudaStream_t st) {
@@ -424,13 +529,13 @@ static void launch_conv(const ConvArgs &a, int phases, cudaStream_t st) {
   if (tc) {
     const bool wide = a.Cin % 64 == 0, n128 = a.Cout % 128 == 0;
     if (wide && n128)
-      conv_tc_launch<128, 64, 3>(a, phases, st);
+      conv_tc_launch<128, 64, 3, 0>(a, phases, st);
     else if (wide)
-      conv_tc_launch<96, 64, 3>(a, phases, st);
+      conv_tc_launch<96, 64, 3, 0>(a, phases, st);
     else if (n128)
-      conv_tc_launch<128, 32, 6>(a, phases, st);
+      conv_tc_launch<128, 32, 6, 0>(a, phases, st);
     else
-      conv_tc_launch<96, 32, 6>(a, phases, st);
+      conv_tc_launch<96, 32, 6, 0>(a, phases, st);
   } else if (a.Cout % 128 == 0) {
     dim3 grid((M + kBM - 1) / kBM, a.Cout / 128, phases);
     k_conv<128><<<grid, 256, conv_smem(128), st>>>(a);
@@ -440,6 +545,19 @@ static void launch_conv(const ConvArgs &a, int phases, cudaStream_t st) {
   } else {
     FAIL(Q3T_INVALID_INPUT, "codec conv: Cout %d is not a multiple of 96 or 128", a.Cout);
   }
+  CK(cudaGetLastError());
+  g_launches++;
+}
+
+// A whole residual unit in one launch (k_conv_tc FUSE = 1) where the stage
+// has 96 channels on the tensor-core path; false if the caller must run the
+// k7 and k1 convolutions as two launches.
+static bool fused_unit_ok(int C) { return C == 96 && !getenv("Q3T_CONV_MMA_SYNC") && !getenv("Q3T_CODEC_UNFUSED"); }
+
+static void launch_unit(const ConvArgs &a, const ConvFuse &fu, cudaStream_t st) {
+  if (a.B * a.Lq <= 0) return;
+  if (!g_conv_err) CK(cudaMalloc(&g_conv_err, sizeof(int)));
+  conv_tc_launch<96, 32, 6, 1>(a, 1, st, &fu);
   CK(cudaGetLastError());
   g_launches++;
 }
@@ -1275,13 +1393,29 @@ static void decode_with(CodecModel *c, const CodecScratch &ws, const int64_t *d_
     static const int dil[3] = {1, 3, 9};
     for (int j = 0; j < 3; j++) {
       const ResW &R = S.ru[j];
+      const SnakeP &nx = j < 2 ? S.ru[j + 1].a1 : (s + 1 < c->stages.size() ? c->stages[s + 1].s0 : c->out_snake);
+      if (fused_unit_ok(R.c1.cout)) {
+        // one launch; its fp16 output goes to the spare buffer because the
+        // k7 taps read rows of `act` that neighbouring tiles own
+        ConvArgs u = conv_args(R.c1, act, B, Lc, -6 * dil[j], dil[j], Lc, 1, Lc);
+        u.bias = R.c2.bias;
+        u.Yf = X32;
+        u.R = X32;
+        u.Yh = other;
+        u.act = ACT_SNAKE;
+        u.act_a = nx.ea;
+        u.act_b = nx.ib;
+        const ConvFuse fu{R.c2.w, R.c1.bias, R.a2.ea, R.a2.ib};
+        launch_unit(u, fu, st);
+        std::swap(act, other);
+        continue;
+      }
       ConvArgs c1 = conv_args(R.c1, act, B, Lc, -6 * dil[j], dil[j], Lc, 1, Lc);
       c1.Yh = Hh;
       c1.act = ACT_SNAKE;
       c1.act_a = R.a2.ea;
       c1.act_b = R.a2.ib;
       launch_conv(c1, 1, st);
-      const SnakeP &nx = j < 2 ? S.ru[j + 1].a1 : (s + 1 < c->stages.size() ? c->stages[s + 1].s0 : c->out_snake);
       ConvArgs c2 = conv_args(R.c2, Hh, B, Lc, 0, 1, Lc, 1, Lc);
       c2.Yf = X32;
       c2.R = X32;
