@@ -301,8 +301,12 @@ q3t_status q3t_batch_poll(q3t_batch *b, int64_t request_id, int *state, int64_t 
 q3t_status q3t_batch_take(q3t_batch *b, int64_t request_id, int64_t *codes, int32_t *sampled,
                           int max_frames, float *wave, int64_t max_samples);
 q3t_status q3t_batch_pending(q3t_batch *b, int *queued, int *active);
-/* The CUDA stream (cudaStream_t) all of the batch's device work runs on, for
- * callers that time steps with their own CUDA events. */
+/* The CUDA stream (cudaStream_t) the batch's device work is ordered on, for
+ * callers that time steps with their own CUDA events.  With codec_mode 2 a
+ * step's chunk decodes run on a second, lower-priority stream, overlapped
+ * with the next step's frame; the next q3t_batch_step joins them into this
+ * stream and counts their samples (a step in which a request finishes joins
+ * at once). */
 q3t_status q3t_batch_stream(q3t_batch *b, void **stream);
 void q3t_batch_free(q3t_batch *b);
 

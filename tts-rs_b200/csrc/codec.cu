@@ -17,6 +17,7 @@
 // decode; the residual streams stay f32.
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -1555,51 +1556,107 @@ static void codec_decode_static(q3t_model *m, const int64_t *codes, int B, int T
 // is decoded and the samples of its newest chunk are emitted.  With the
 // reference's non-causal pre-transformer this is an approximation of the
 // full-sequence decode (no reference counterpart; new mode).
+//
+// The windows of step n decode on a second, lowest-priority stream while the
+// (highest-priority) batch stream runs step n + 1's talker / predictor
+// kernels, which are latency bound and leave most of the GPU idle.  The
+// window codes are gathered on the batch stream (so a slot that a later step
+// reuses cannot change them), samples go to a pinned staging buffer, and the
+// next codec call joins the work: host wait, a device-side wait of the batch
+// stream, copies into the requests' sample vectors and the sample counts.
+// A step in which a request finishes joins at once, so a retired request's
+// output is complete.
 // ---------------------------------------------------------------------------
+struct StreamOut {
+  Req *r;
+  int64_t src, dst, n;  // staging offset, offset in r->wave, samples
+};
 struct StreamState {
   std::map<int64_t, int> emitted;  // request id -> frames emitted
-  int64_t *d_codes = nullptr;      // gathered windows [nwin][nq][Tw]
-  float *d_wave = nullptr;
+  int64_t *d_codes = nullptr;      // gathered windows of one step, back to back
+  float *d_wave = nullptr;         // their samples, back to back
+  float *h_wave = nullptr;         // pinned staging of the emitted samples
   size_t codes_cap = 0, wave_cap = 0;
+  cudaStream_t cst = nullptr;
+  cudaEvent_t ev_codes = nullptr, ev_done = nullptr;
+  std::vector<StreamOut> out;      // emitted by the work in flight
+  bool inflight = false;
 };
 static std::map<q3t_batch *, StreamState> g_streams;
 
-// Sizes the window buffers for max_active windows of left_context +
-// chunk_frames frames and runs one decode of each window length the stream
-// uses (chunk_frames for a request's first window, left_context +
-// chunk_frames after), so the stream-ordered workspace pool and the kernels
-// are set up before the first chunk is due rather than inside a step.
+static void stream_capacity(StreamState &S, size_t codes, size_t wave) {
+  if (S.codes_cap < codes) {
+    if (S.d_codes) CK(cudaFree(S.d_codes));
+    S.codes_cap = codes;
+    CK(cudaMalloc(&S.d_codes, S.codes_cap * 8));
+  }
+  if (S.wave_cap < wave) {
+    if (S.d_wave) CK(cudaFree(S.d_wave));
+    if (S.h_wave) CK(cudaFreeHost(S.h_wave));
+    S.wave_cap = wave;
+    CK(cudaMalloc(&S.d_wave, S.wave_cap * 4));
+    CK(cudaHostAlloc(&S.h_wave, S.wave_cap * 4, cudaHostAllocDefault));
+  }
+}
+
+// Sizes the buffers for max_active windows of left_context + chunk_frames
+// frames and runs one decode of each window length the stream uses
+// (chunk_frames for a request's first window, left_context + chunk_frames
+// after) on the codec stream, so its workspace pool and the kernels are set
+// up before the first chunk is due rather than inside a step.
 void codec_stream_init(q3t_model *m, q3t_batch *b) {
   StreamState S;
   CodecModel *c = m->codec;
   const int chunk = std::max(1, b->desc.chunk_frames), ctx = std::max(0, b->desc.left_context);
   const int Bw = std::max(1, b->A), nq = c->c.num_quantizers;
+  int least = 0, greatest = 0;
+  CK(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+  CK(cudaStreamCreateWithPriority(&S.cst, cudaStreamNonBlocking, least));
+  CK(cudaEventCreateWithFlags(&S.ev_codes, cudaEventDisableTiming));
+  CK(cudaEventCreateWithFlags(&S.ev_done, cudaEventDisableTiming));
+  int64_t nmax = 0;
+  codec_out_len(c, chunk + ctx, &nmax);
+  stream_capacity(S, (size_t)Bw * nq * (chunk + ctx), (size_t)Bw * std::max<int64_t>(nmax, 1));
   for (int Tw : {chunk, chunk + ctx}) {
     int64_t nout = 0;
     codec_out_len(c, Tw, &nout);
     if (nout <= 0) continue;
-    if (S.codes_cap < (size_t)Bw * nq * Tw) {
-      if (S.d_codes) cudaFree(S.d_codes);
-      S.codes_cap = (size_t)Bw * nq * Tw;
-      CK(cudaMalloc(&S.d_codes, S.codes_cap * 8));
-    }
-    if (S.wave_cap < (size_t)Bw * nout) {
-      if (S.d_wave) cudaFree(S.d_wave);
-      S.wave_cap = (size_t)Bw * nout;
-      CK(cudaMalloc(&S.d_wave, S.wave_cap * 4));
-    }
-    CK(cudaMemsetAsync(S.d_codes, 0, (size_t)Bw * nq * Tw * 8, b->st));
-    decode_device(c, S.d_codes, Bw, Tw, S.d_wave, nullptr, b->st);
+    CK(cudaMemsetAsync(S.d_codes, 0, (size_t)Bw * nq * Tw * 8, S.cst));
+    decode_device(c, S.d_codes, Bw, Tw, S.d_wave, nullptr, S.cst);
   }
-  CK(cudaStreamSynchronize(b->st));
+  CK(cudaStreamSynchronize(S.cst));
   g_streams[b] = S;
+}
+
+// Completes the codec work in flight (see above); samples (nullable) counts
+// the samples it emitted.
+void codec_stream_join(q3t_batch *b, int64_t *samples) {
+  auto it = g_streams.find(b);
+  if (it == g_streams.end() || !it->second.inflight) return;
+  StreamState &S = it->second;
+  CK(cudaEventSynchronize(S.ev_done));
+  CK(cudaStreamWaitEvent(b->st, S.ev_done, 0));
+  for (const StreamOut &o : S.out) {
+    if (b->desc.keep_output) memcpy(o.r->wave.data() + o.dst, S.h_wave + o.src, (size_t)o.n * 4);
+    o.r->samples += o.n;
+    if (samples) *samples += o.n;
+  }
+  S.out.clear();
+  S.inflight = false;
 }
 
 void codec_stream_free(q3t_batch *b) {
   auto it = g_streams.find(b);
   if (it == g_streams.end()) return;
-  if (it->second.d_codes) cudaFree(it->second.d_codes);
-  if (it->second.d_wave) cudaFree(it->second.d_wave);
+  StreamState &S = it->second;
+  if (S.inflight) cudaEventSynchronize(S.ev_done);
+  if (S.cst) cudaStreamSynchronize(S.cst);
+  if (S.d_codes) cudaFree(S.d_codes);
+  if (S.d_wave) cudaFree(S.d_wave);
+  if (S.h_wave) cudaFreeHost(S.h_wave);
+  if (S.ev_codes) cudaEventDestroy(S.ev_codes);
+  if (S.ev_done) cudaEventDestroy(S.ev_done);
+  if (S.cst) cudaStreamDestroy(S.cst);
   g_streams.erase(it);
 }
 
@@ -1613,6 +1670,7 @@ __global__ void k_window_codes(const int64_t *hist, int maxF, int G, int nq, int
 
 void codec_stream_step(q3t_model *m, q3t_batch *b, const std::vector<Req *> &act, int64_t *samples) {
   CodecModel *c = m->codec;
+  codec_stream_join(b, samples);  // the previous step's windows
   auto &S = g_streams[b];
   const int chunk = std::max(1, b->desc.chunk_frames), ctx = std::max(0, b->desc.left_context);
   const int nq = c->c.num_quantizers;
@@ -1622,60 +1680,89 @@ void codec_stream_step(q3t_model *m, q3t_batch *b, const std::vector<Req *> &act
   struct Win {
     Req *r;
     int e, n, f0;
+    int64_t s0, s1, dst;  // emitted samples [s0, s1) of the window's decode, offset in r->wave
   };
-  std::map<int, std::vector<Win>> groups;  // window length -> windows
+  std::vector<Win> wins;
+  auto add = [&](Req *r, int e, int n) {
+    const int f0 = std::max(0, e - ctx), Tw = e + n - f0;
+    int64_t nout = 0;
+    codec_out_len(c, Tw, &nout);
+    // window-relative frames [e - f0, e - f0 + n) map to samples shifted by
+    // the trim deficit (555 at the default rates), so consecutive chunks tile
+    // the full-length output
+    const int64_t deficit = spf * Tw - nout, a0 = e - f0;
+    const int64_t s0 = a0 > 0 ? std::min<int64_t>(nout, a0 * spf - deficit) : 0;
+    const int64_t s1 = std::min<int64_t>(nout, (a0 + n) * spf - deficit);
+    wins.push_back(Win{r, e, n, f0, s0, s1, 0});
+  };
+  // every request emits each chunk as soon as its frames exist; a finished
+  // request emits the frames it still owes
   for (Req *r : act) {
-    const int e = S.emitted[r->id], avail = r->step_idx;
-    if (!(avail - e >= chunk || (r->finished && avail > e))) continue;
-    const int n = std::min(chunk, avail - e), f0 = std::max(0, e - ctx);
-    groups[e + n - f0].push_back(Win{r, e, n, f0});
+    int e = S.emitted[r->id];
+    const int avail = r->step_idx;
+    while (avail - e >= chunk || (r->finished && avail > e)) {
+      const int n = std::min(chunk, avail - e);
+      add(r, e, n);
+      e += n;
+    }
   }
+  for (Req *r : act)
+    if (r->finished) S.emitted.erase(r->id);
+  if (wins.empty()) return;
+  for (Win &w : wins) {  // a request's windows were added in time order
+    if (!w.r->finished) S.emitted[w.r->id] = w.e + w.n;
+    if (w.s1 > w.s0 && b->desc.keep_output) {
+      w.dst = (int64_t)w.r->wave.size();
+      w.r->wave.resize(w.r->wave.size() + (w.s1 - w.s0));
+    }
+  }
+  std::map<int, std::vector<int>> groups;  // window length -> windows
+  for (int i = 0; i < (int)wins.size(); i++) groups[wins[i].e + wins[i].n - wins[i].f0].push_back(i);
+  size_t need_codes = 0, need_wave = 0;
+  for (auto &kv : groups) {
+    int64_t nout = 0;
+    codec_out_len(c, kv.first, &nout);
+    need_codes += kv.second.size() * (size_t)nq * kv.first;
+    need_wave += kv.second.size() * (size_t)std::max<int64_t>(nout, 1);
+  }
+  stream_capacity(S, need_codes, need_wave);  // nothing is in flight here
+  size_t coff = 0, woff = 0, hoff = 0;
   for (auto &kv : groups) {
     const int Tw = kv.first, Bw = (int)kv.second.size();
     int64_t nout = 0;
     codec_out_len(c, Tw, &nout);
-    const int64_t deficit = spf * Tw - nout;  // samples the both-side trims drop at the end (555)
-    if (S.codes_cap < (size_t)Bw * nq * Tw) {
-      if (S.d_codes) cudaFree(S.d_codes);
-      S.codes_cap = (size_t)Bw * nq * Tw * 2;
-      CK(cudaMalloc(&S.d_codes, S.codes_cap * 8));
-    }
-    if (S.wave_cap < (size_t)Bw * std::max<int64_t>(nout, 1)) {
-      if (S.d_wave) cudaFree(S.d_wave);
-      S.wave_cap = (size_t)Bw * std::max<int64_t>(nout, 1) * 2;
-      CK(cudaMalloc(&S.d_wave, S.wave_cap * 4));
-    }
+    int64_t *dc = S.d_codes + coff;
+    float *dw = S.d_wave + woff;
     for (int i = 0; i < Bw; i++) {
-      k_window_codes<<<8, 256, 0, b->st>>>(b->d_hist_codes, b->maxF, b->G, nq, kv.second[i].r->slot, kv.second[i].f0,
-                                           Tw, S.d_codes + (size_t)i * nq * Tw);
+      const Win &w = wins[kv.second[i]];
+      k_window_codes<<<8, 256, 0, b->st>>>(b->d_hist_codes, b->maxF, b->G, nq, w.r->slot, w.f0, Tw,
+                                           dc + (size_t)i * nq * Tw);
       CK(cudaGetLastError());
       g_launches++;
     }
-    if (nout > 0) decode_device(c, S.d_codes, Bw, Tw, S.d_wave, nullptr, b->st);
+    CK(cudaEventRecord(S.ev_codes, b->st));
+    CK(cudaStreamWaitEvent(S.cst, S.ev_codes, 0));
+    if (nout > 0) decode_device(c, dc, Bw, Tw, dw, nullptr, S.cst);
     for (int i = 0; i < Bw; i++) {
-      Win &w = kv.second[i];
-      Req *r = w.r;
-      // window-relative frames [e - f0, e - f0 + n) map to samples shifted by
-      // the trim deficit, so consecutive chunks tile the full-length output
-      const int64_t a0 = w.e - w.f0;
-      const int64_t s0 = a0 > 0 ? std::min<int64_t>(nout, a0 * spf - deficit) : 0;
-      const int64_t s1 = std::min<int64_t>(nout, (a0 + w.n) * spf - deficit);
-      if (s1 > s0) {
-        if (b->desc.keep_output) {
-          const size_t old = r->wave.size();
-          r->wave.resize(old + (s1 - s0));
-          CK(cudaMemcpyAsync(r->wave.data() + old, S.d_wave + (size_t)i * nout + s0, (s1 - s0) * 4,
-                             cudaMemcpyDeviceToHost, b->st));
-          b->d2h += (s1 - s0) * 4;
-        }
-        r->samples += s1 - s0;
-        if (samples) *samples += s1 - s0;
+      const Win &w = wins[kv.second[i]];
+      if (w.s1 <= w.s0) continue;
+      const int64_t n = w.s1 - w.s0;
+      if (b->desc.keep_output) {
+        CK(cudaMemcpyAsync(S.h_wave + hoff, dw + (size_t)i * nout + w.s0, n * 4, cudaMemcpyDeviceToHost, S.cst));
+        b->d2h += n * 4;
       }
-      S.emitted[r->id] = w.e + w.n;
-      if (r->finished && w.e + w.n >= r->step_idx) S.emitted.erase(r->id);
+      S.out.push_back(StreamOut{w.r, (int64_t)hoff, w.dst, n});
+      if (b->desc.keep_output) hoff += n;
     }
-    if (b->desc.keep_output) CK(cudaStreamSynchronize(b->st));
+    coff += (size_t)Bw * nq * Tw;
+    woff += (size_t)Bw * std::max<int64_t>(nout, 1);
   }
+  CK(cudaEventRecord(S.ev_done, S.cst));
+  S.inflight = true;
+  static const bool serial = getenv("Q3T_CODEC_SERIAL") != nullptr;  // no overlap (A/B measurements)
+  bool join = serial;
+  for (Req *r : act) join |= r->finished;  // retired after this call: its last samples must be in place
+  if (join) codec_stream_join(b, samples);
 }
 
 }  // namespace q3t

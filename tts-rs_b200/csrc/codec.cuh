@@ -15,6 +15,8 @@ void codec_decode_host_codes(q3t_model *m, const int64_t *codes, int B, int T, f
 // chunked streaming decode inside a batch (codec_mode 2)
 void codec_stream_init(q3t_model *m, q3t_batch *b);
 void codec_stream_step(q3t_model *m, q3t_batch *b, const std::vector<Req *> &act, int64_t *samples);
+// completes the streaming codec work still in flight; samples (nullable) counts what it emitted
+void codec_stream_join(q3t_batch *b, int64_t *samples);
 void codec_stream_free(q3t_batch *b);
 
 }  // namespace q3t

@@ -334,7 +334,11 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
   b->I2 = 2 * std::max(tc.talker.intermediate_size, tc.predictor.intermediate_size);
   const char *g = getenv("Q3T_GRAPHS");
   b->use_graphs = !(g && g[0] == '0');
-  CK(cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking));
+  {  // highest priority: the streaming codec's windows fill in behind the frame kernels
+    int least = 0, greatest = 0;
+    CK(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+    CK(cudaStreamCreateWithPriority(&b->st, cudaStreamNonBlocking, greatest));
+  }
   CK(cudaEventCreate(&b->ev0));
   CK(cudaEventCreate(&b->ev1));
   for (auto &e : b->evf) CK(cudaEventCreate(&e));
@@ -1244,6 +1248,7 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
     if (stats) *stats = S;
   };
   if (B == 0) {
+    if (b->desc.codec_mode == 2 && b->m->has_codec) codec_stream_join(b, &S.samples);
     report();
     return;
   }
