@@ -49,12 +49,29 @@ Q3T_DEV void mma_f16(float *c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// sin^2(y) in f32 without a libm call.  sin^2 has period pi, so y is reduced
+// to r = y - k pi, k = rint(y / pi), with pi split into three floats
+// (Cody-Waite reduction: k * 3.140625 and k * PI_B are exact for |k| < 4096),
+// and sin r on [-pi/2, pi/2] is its Taylor series to r^11 (truncation below
+// 6e-8).  Max abs error of the square below 4e-7 for |y| <= 3000, far under
+// the fp16 step of the activations it produces.
+Q3T_DEV float sin_sq(float y) {
+  const float k = rintf(y * 0.318309886183790672f);
+  float r = fmaf(-k, 3.140625f, y);
+  r = fmaf(-k, 9.675025939941406e-4f, r);
+  r = fmaf(-k, 1.5099580252808664e-7f, r);
+  const float r2 = r * r;
+  float p = fmaf(r2, -2.505210838544172e-8f, 2.755731922398589e-6f);  // -1/11!, 1/9!
+  p = fmaf(r2, p, -1.984126984126984e-4f);                             // -1/7!
+  p = fmaf(r2, p, 8.333333333333333e-3f);                              // 1/5!
+  p = fmaf(r2, p, -1.666666666666667e-1f);                             // -1/3!
+  const float sn = fmaf(r * r2, p, r);
+  return sn * sn;
+}
+
 // SnakeBeta x + sin^2(e^alpha x) / (e^beta + 1e-9) (activation.rs:16-37) with
 // ea = e^alpha and ib = 1 / (e^beta + 1e-9) precomputed per channel.
-Q3T_DEV float snake(float x, float ea, float ib) {
-  const float s = sinf(x * ea);
-  return x + s * s * ib;
-}
+Q3T_DEV float snake(float x, float ea, float ib) { return fmaf(sin_sq(x * ea), ib, x); }
 Q3T_DEV float gelu_erf(float x) { return 0.5f * x * (1.f + erff(x * 0.70710678118654752f)); }
 
 enum { ACT_NONE = 0, ACT_SNAKE = 1, ACT_GELU = 2 };
@@ -250,6 +267,75 @@ Q3T_DEV uint32_t swz_off(int r, int j) {
   return ACH == 64 ? (uint32_t)(r * 128 + ((j ^ (r & 7)) << 4)) : (uint32_t)(r * 64 + ((j ^ ((r >> 1) & 3)) << 4));
 }
 
+// Epilogue of one output tile: the f32 accumulator tile [128 steps][N + 4]
+// in shared memory is swept row-major (NTH threads, consecutive threads on
+// consecutive 4-channel groups of a row, so global accesses coalesce) through
+// bias, scale, residual, the f32 store and act() -> fp16.
+template <int N, int NTH>
+Q3T_DEV void conv_sweep(const ConvArgs &a, const float *tile, int b, int tq0, int n0, int phase, int tid) {
+  constexpr int TP = N + 4, G4 = N / 4, UN = 4;
+  const int rows = min(128, a.Lq - tq0);
+  const int total = rows * G4;
+  const size_t base0 = (size_t)b * a.Lout + phase;
+  for (int f0 = tid; f0 < total; f0 += NTH * UN) {
+    float4 v[UN], r[UN];
+    size_t e[UN];
+    int nn[UN];
+#pragma unroll
+    for (int u = 0; u < UN; u++) {
+      const int f = f0 + NTH * u;
+      const int ff = f < total ? f : 0, row = ff / G4, c4 = ff - row * G4;
+      nn[u] = f < total ? n0 + 4 * c4 : -1;
+      v[u] = *reinterpret_cast<const float4 *>(tile + row * TP + 4 * c4);
+      e[u] = (base0 + (size_t)(tq0 + row) * a.ostride) * a.Cout + n0 + 4 * c4;
+      if (nn[u] >= 0 && a.R) r[u] = *reinterpret_cast<const float4 *>(a.R + e[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < UN; u++) {
+      const int n = nn[u];
+      if (n < 0) continue;
+      float y[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      if (a.bias) {
+        const float4 bb = *reinterpret_cast<const float4 *>(a.bias + n);
+        y[0] += bb.x;
+        y[1] += bb.y;
+        y[2] += bb.z;
+        y[3] += bb.w;
+      }
+      if (a.scale) {
+        const float4 sc = *reinterpret_cast<const float4 *>(a.scale + n);
+        y[0] *= sc.x;
+        y[1] *= sc.y;
+        y[2] *= sc.z;
+        y[3] *= sc.w;
+      }
+      if (a.R) {
+        y[0] += r[u].x;
+        y[1] += r[u].y;
+        y[2] += r[u].z;
+        y[3] += r[u].w;
+      }
+      if (a.Yf) *reinterpret_cast<float4 *>(a.Yf + e[u]) = make_float4(y[0], y[1], y[2], y[3]);
+      if (a.Yh) {
+        float h[4] = {y[0], y[1], y[2], y[3]};
+        if (a.act == ACT_SNAKE) {
+          const float4 ea = *reinterpret_cast<const float4 *>(a.act_a + n);
+          const float4 ib = *reinterpret_cast<const float4 *>(a.act_b + n);
+          h[0] = snake(y[0], ea.x, ib.x);
+          h[1] = snake(y[1], ea.y, ib.y);
+          h[2] = snake(y[2], ea.z, ib.z);
+          h[3] = snake(y[3], ea.w, ib.w);
+        } else if (a.act == ACT_GELU) {
+#pragma unroll
+          for (int j = 0; j < 4; j++) h[j] = gelu_erf(y[j]);
+        }
+        __half2 p[2] = {__floats2half2_rn(h[0], h[1]), __floats2half2_rn(h[2], h[3])};
+        *reinterpret_cast<uint2 *>(a.Yh + e[u]) = *reinterpret_cast<const uint2 *>(p);
+      }
+    }
+  }
+}
+
 template <int N, int ACH, int S>
 struct ConvTcSmem {
   static constexpr int kA = 128 * ACH * 2, kB = N * ACH * 2, kStage = kA + kB;
@@ -399,76 +485,26 @@ __global__ void __launch_bounds__(256) k_conv_tc(const __grid_constant__ ConvTc 
     }
   }
   __syncthreads();
-  // row-major sweep by all 8 warps: consecutive threads take consecutive
-  // 4-channel groups of a row, UN groups in flight per thread
-  constexpr int G4 = N / 4, UN = 4, NTH = 256;
-  const int rows = min(128, a.Lq - tq0);
-  const int total = rows * G4;
-  const size_t base0 = (size_t)b * a.Lout + phase;
-  for (int f0 = threadIdx.x; f0 < total; f0 += NTH * UN) {
-    float4 v[UN], r[UN];
-    size_t e[UN];
-    int nn[UN];
-#pragma unroll
-    for (int u = 0; u < UN; u++) {
-      const int f = f0 + NTH * u;
-      const int ff = f < total ? f : 0, row = ff / G4, c4 = ff - row * G4;
-      nn[u] = f < total ? n0 + 4 * c4 : -1;
-      v[u] = *reinterpret_cast<const float4 *>(tile + row * TP + 4 * c4);
-      e[u] = (base0 + (size_t)(tq0 + row) * a.ostride) * a.Cout + n0 + 4 * c4;
-      if (nn[u] >= 0 && a.R) r[u] = *reinterpret_cast<const float4 *>(a.R + e[u]);
-    }
-#pragma unroll
-    for (int u = 0; u < UN; u++) {
-      const int n = nn[u];
-      if (n < 0) continue;
-      float y[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-      if (a.bias) {
-        const float4 bb = *reinterpret_cast<const float4 *>(a.bias + n);
-        y[0] += bb.x;
-        y[1] += bb.y;
-        y[2] += bb.z;
-        y[3] += bb.w;
-      }
-      if (a.scale) {
-        const float4 sc = *reinterpret_cast<const float4 *>(a.scale + n);
-        y[0] *= sc.x;
-        y[1] *= sc.y;
-        y[2] *= sc.z;
-        y[3] *= sc.w;
-      }
-      if (a.R) {
-        y[0] += r[u].x;
-        y[1] += r[u].y;
-        y[2] += r[u].z;
-        y[3] += r[u].w;
-      }
-      if (a.Yf) *reinterpret_cast<float4 *>(a.Yf + e[u]) = make_float4(y[0], y[1], y[2], y[3]);
-      if (a.Yh) {
-        float h[4] = {y[0], y[1], y[2], y[3]};
-        if (a.act == ACT_SNAKE) {
-          const float4 ea = *reinterpret_cast<const float4 *>(a.act_a + n);
-          const float4 ib = *reinterpret_cast<const float4 *>(a.act_b + n);
-          h[0] = snake(y[0], ea.x, ib.x);
-          h[1] = snake(y[1], ea.y, ib.y);
-          h[2] = snake(y[2], ea.z, ib.z);
-          h[3] = snake(y[3], ea.w, ib.w);
-        } else if (a.act == ACT_GELU) {
-#pragma unroll
-          for (int j = 0; j < 4; j++) h[j] = gelu_erf(y[j]);
-        }
-        __half2 p[2] = {__floats2half2_rn(h[0], h[1]), __floats2half2_rn(h[2], h[3])};
-        *reinterpret_cast<uint2 *>(a.Yh + e[u]) = *reinterpret_cast<const uint2 *>(p);
-      }
-    }
-  }
+  conv_sweep<N, 256>(a, tile, b, tq0, n0, phase, threadIdx.x);
   if (err && c.err) atomicOr(c.err, (int)err);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, kCols);
 }
 
-static int *g_conv_err = nullptr;  // device word for bounded-wait timeouts of k_conv_tc
+static int *g_conv_err = nullptr;  // device word for bounded-wait timeouts of k_conv_tc / k_conv_pt
+
+// Raises Q3T_DEVICE_TIMEOUT if a convolution's bounded wait gave up since the
+// last check; the caller's stream is idle.
+static void conv_check_err() {
+  if (!g_conv_err) return;
+  int e = 0;
+  CK(cudaMemcpy(&e, g_conv_err, sizeof e, cudaMemcpyDeviceToHost));
+  if (e) {
+    CK(cudaMemset(g_conv_err, 0, sizeof e));
+    FAIL(Q3T_DEVICE_TIMEOUT, "codec convolution: a bounded device wait gave up (code %#x)", e);
+  }
+}
 
 // The fused residual unit's extra operands (FUSE = 1).
 struct ConvFuse {
@@ -522,12 +558,356 @@ static void conv_tc_launch(const ConvArgs &a, int phases, cudaStream_t st, const
   k_conv_tc<N, ACH, S, FUSE><<<grid, 256, L::kBytes, st>>>(c);
 }
 
+// ---------------------------------------------------------------------------
+// Persistent, warp-specialised form of k_conv_tc (and of its fused residual
+// unit).  One CTA per SM walks the output tiles t = blockIdx.x + i * gridDim.x
+// (128 steps x N channels of one sequence and phase; channel blocks vary
+// fastest, then phases, so neighbouring tiles share their input rows in L2):
+//   warp 0 lane 0   TMA producer: im2col input and weight tiles into a ring
+//                   of S stages, running ahead across tile boundaries;
+//   warp 1 lane 0   MMA issuer: tile i into TMEM accumulator i & 1 (columns
+//                   128 (i & 1) ..), released by the epilogue, so tile i + 1's
+//                   MMAs run while tile i's epilogue drains;
+//   warps 2..17     epilogue: warp w reads TMEM lanes 32 (w & 3) .. + 31 (its
+//                   row quadrant) and column quarter (w - 2) >> 2 into an f32
+//                   staging tile, then all sixteen sweep it row-major through
+//                   conv_sweep.
+// FUSE = 1 (residual unit, N = C): the k7 accumulator i is turned into the k1
+// GEMM's A operand (act2(acc + b7), fp16, swizzled as TMA would store it) in
+// its own tile; the k1 weights stay resident; the MMA warp issues tile i's k1
+// GEMM into a third accumulator (columns 256 ..) after tile i + 1's k7 MMAs,
+// and the epilogue drains it (b1, residual, next SnakeBeta) before it builds
+// tile i + 1's A operand.  Every mbarrier wait is bounded; after a timeout a
+// thread skips its remaining waits (the loops keep their trip counts, so
+// every named barrier is still reached) and the kernel reports *err.
+// ---------------------------------------------------------------------------
+constexpr int kPtEpiWarps = 16, kPtThreads = (2 + kPtEpiWarps) * 32;
+
+struct ConvPt {
+  CUtensorMap tx, tw, tw1;  // as ConvTc
+  ConvArgs a;
+  const float *mid_bias, *mid_a, *mid_b;
+  int tiles;                // 128-step tiles per sequence
+  int nb, phases, total;    // channel blocks, phases, tiles of the launch
+  int *err;
+};
+
+template <int N, int ACH, int S, int FUSE>
+struct ConvPtSmem {
+  static constexpr int kA = 128 * ACH * 2, kB = N * ACH * 2, kStage = kA + kB;
+  static constexpr int kStg = 128 * (N + 4) * 4;
+  static constexpr int kA2 = FUSE ? 128 * N * 2 : 0;
+  static constexpr int kW1 = FUSE ? N * N * 2 : 0;
+  static constexpr int kPar = FUSE ? 3 * N * 4 : 0;
+  static constexpr int oStg = S * kStage, oA2 = oStg + kStg, oW1 = oA2 + kA2, oPar = oW1 + kW1, oBar = oPar + kPar;
+  static constexpr int kBars = 2 * S + 8;
+  static constexpr size_t kBytes = (size_t)oBar + kBars * 8 + 16 + 1024;
+  static_assert(kStage % 1024 == 0 && kStg % 1024 == 0 && kA2 % 1024 == 0 && kW1 % 1024 == 0, "1024-byte operands");
+  static_assert(kBytes <= 232448, "shared memory per CTA");
+};
+
+Q3T_DEV void bar_epi() { asm volatile("bar.sync 1, %0;" ::"n"(kPtEpiWarps * 32) : "memory"); }
+Q3T_DEV void mbar_arrive1(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+struct PtTile {
+  int b, tq0, n0, phase;
+};
+Q3T_DEV PtTile pt_tile(const ConvPt &c, int t, int N) {
+  PtTile p;
+  const int nbk = t % c.nb, u = t / c.nb;
+  p.phase = u % c.phases;
+  const int mt = u / c.phases;
+  p.b = mt / c.tiles;
+  p.tq0 = (mt - p.b * c.tiles) * 128;
+  p.n0 = nbk * N;
+  return p;
+}
+
+template <int N, int ACH, int S, int FUSE>
+__global__ void __launch_bounds__(kPtThreads, 1) k_conv_pt(const __grid_constant__ ConvPt c) {
+  using L = ConvPtSmem<N, ACH, S, FUSE>;
+  static_assert(N <= 128 && N % 32 == 0, "two accumulators of <= 128 columns, 8-column groups per quarter");
+  constexpr uint32_t kCols = FUSE ? 512 : 256, kAcc2 = 256;
+  extern __shared__ unsigned char csm_raw[];
+  unsigned char *sm = csm_raw + ((1024 - (smem_addr(csm_raw) & 1023)) & 1023);
+  uint64_t *full = reinterpret_cast<uint64_t *>(sm + L::oBar), *empty = full + S;
+  uint64_t *accf = empty + S, *acce = accf + 2, *a2f = acce + 2, *acc2f = a2f + 1, *w1f = acc2f + 1, *fin = w1f + 1;
+  uint32_t *tslot = reinterpret_cast<uint32_t *>(fin + 1);
+  float *stg = reinterpret_cast<float *>(sm + L::oStg);
+  unsigned char *a2 = sm + L::oA2, *w1 = sm + L::oW1;
+  float *par = reinterpret_cast<float *>(sm + L::oPar);
+  const ConvArgs &a = c.a;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kc = a.Cin / ACH, KS = a.taps * kc;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&accf[i], 1);
+      mbar_init(&acce[i], kPtEpiWarps);
+    }
+    mbar_init(a2f, kPtEpiWarps);
+    mbar_init(acc2f, 1);
+    mbar_init(w1f, 1);
+    mbar_init(fin, 1);
+    fence_mbar_init();
+  }
+  if (FUSE)
+    for (int i = threadIdx.x; i < N; i += blockDim.x) {
+      par[i] = c.mid_bias[i];
+      par[N + i] = c.mid_a[i];
+      par[2 * N + i] = c.mid_b[i];
+    }
+  if (warp == 0) tmem_alloc(tslot, kCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  uint32_t err = 0;
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      if (FUSE) {
+        mbar_expect_tx(w1f, L::kW1);
+        for (int q = 0; q < N / ACH; q++) tma_load_2d(w1 + q * L::kB, &c.tw1, q * ACH, 0, w1f);
+      }
+      int ks = 0;
+      for (int t = blockIdx.x; t < c.total && !err; t += gridDim.x) {
+        const PtTile p = pt_tile(c, t, N);
+        for (int k = 0; k < KS; k++, ks++) {
+          const int s = ks % S, i = ks / S;
+          if (i > 0 && !mbar_wait(&empty[s], (i - 1) & 1)) {
+            err |= 1u;
+            break;
+          }
+          const int tap = k / kc, c0 = (k - tap * kc) * ACH;
+          unsigned char *st = sm + s * L::kStage;
+          mbar_expect_tx(&full[s], L::kStage);
+          tma_load_3d(st, &c.tx, c0, p.tq0 + a.in_off + tap * a.dil, p.b, &full[s]);
+          tma_load_2d(st + L::kA, &c.tw, c0, (p.phase * a.taps + tap) * a.Cout + p.n0, &full[s]);
+        }
+      }
+      // the copies still in flight (none unless a wait above gave up) land before the CTA ends
+      for (int j = ks - 1; j >= 0 && j >= ks - S; j--)
+        if (!mbar_wait(&full[j % S], (j / S) & 1)) err |= 1u;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      constexpr uint32_t idesc = umma_idesc_f16(128, N);
+      if (FUSE && !mbar_wait(w1f, 0)) err |= 8u;
+      auto mma2 = [&](int j) {  // k1 GEMM of tile j: A2 x W1 -> accumulator 2
+        if (!err && !mbar_wait(a2f, j & 1)) err |= 16u;
+        tc_fence_after();
+        if (!err)
+          for (int q = 0; q < N / ACH; q++)
+#pragma unroll
+            for (int kk = 0; kk < ACH / 16; kk++) {
+              const unsigned char *pa = a2 + q * L::kA + kk * 32, *pb = w1 + q * L::kB + kk * 32;
+              const uint64_t ad = ACH == 64 ? sw128_desc(pa) : sw64_desc(pa);
+              const uint64_t bd = ACH == 64 ? sw128_desc(pb) : sw64_desc(pb);
+              umma_kf16(tmem + kAcc2, ad, bd, idesc, (q | kk) != 0 ? 1u : 0u);
+            }
+        umma_commit(acc2f);
+      };
+      int ks = 0, it = 0;
+      for (int t = blockIdx.x; t < c.total; t += gridDim.x, it++) {
+        const int buf = it & 1;
+        if (!err && it >= 2 && !mbar_wait(&acce[buf], ((it >> 1) - 1) & 1)) err |= 4u;
+        tc_fence_after();
+        const uint32_t d = tmem + 128u * buf;
+        for (int k = 0; k < KS && !err; k++, ks++) {
+          const int s = ks % S;
+          if (!mbar_wait(&full[s], (ks / S) & 1)) {
+            err |= 2u;
+            break;
+          }
+          tc_fence_after();
+          const unsigned char *st = sm + s * L::kStage;
+#pragma unroll
+          for (int kk = 0; kk < ACH / 16; kk++) {
+            const uint64_t ad = ACH == 64 ? sw128_desc(st + kk * 32) : sw64_desc(st + kk * 32);
+            const uint64_t bd = ACH == 64 ? sw128_desc(st + L::kA + kk * 32) : sw64_desc(st + L::kA + kk * 32);
+            umma_kf16(d, ad, bd, idesc, (k | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&accf[buf]);
+        if (FUSE && it >= 1) mma2(it - 1);
+      }
+      if (FUSE && it >= 1) mma2(it - 1);
+      umma_commit(fin);  // every MMA issued has completed before TMEM is freed
+      if (!mbar_wait(fin, 0)) err |= 4u;
+    }
+  } else {  // epilogue warps
+    const int ew = warp - 2, quad = warp & 3, part = ew >> 2, r = 32 * quad + lane, etid = threadIdx.x - 64;
+    const uint32_t tl = (uint32_t)(32 * quad) << 16;
+    constexpr int G8 = N / 32;  // 8-column groups per quarter
+    const int col0 = part * G8 * 8;
+    auto drain = [&](uint32_t taddr, uint64_t *release) {  // accumulator rows -> staging tile
+      uint32_t v[G8][8];
+#pragma unroll
+      for (int g = 0; g < G8; g++) tmem_ld8_async(taddr + col0 + 8 * g, v[g]);
+      tmem_wait_ld();
+      float4 *dst = reinterpret_cast<float4 *>(stg + r * (N + 4) + col0);
+#pragma unroll
+      for (int g = 0; g < G8; g++) {
+        dst[2 * g] = make_float4(__uint_as_float(v[g][0]), __uint_as_float(v[g][1]), __uint_as_float(v[g][2]),
+                                 __uint_as_float(v[g][3]));
+        dst[2 * g + 1] = make_float4(__uint_as_float(v[g][4]), __uint_as_float(v[g][5]), __uint_as_float(v[g][6]),
+                                     __uint_as_float(v[g][7]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (release && lane == 0) mbar_arrive1(release);
+    };
+    int it = 0;
+    PtTile prev{0, 0, 0, 0};
+    for (int t = blockIdx.x; t < c.total; t += gridDim.x, it++) {
+      const PtTile p = pt_tile(c, t, N);
+      const int buf = it & 1;
+      if (!err && !mbar_wait(&accf[buf], (it >> 1) & 1)) err |= 32u;
+      tc_fence_after();
+      __syncwarp();
+      const uint32_t acc = tmem + tl + 128u * buf;
+      if (FUSE) {
+        if (it >= 1) {  // tile it - 1's k1 result; also frees A2
+          if (!err && !mbar_wait(acc2f, (it - 1) & 1)) err |= 64u;
+          tc_fence_after();
+          __syncwarp();
+          drain(tmem + tl + kAcc2, nullptr);
+          bar_epi();
+          conv_sweep<N, kPtEpiWarps * 32>(a, stg, prev.b, prev.tq0, prev.n0, prev.phase, etid);
+          bar_epi();
+        }
+        // act2(acc + b7) -> fp16 A operand of the k1 GEMM
+        {
+          uint32_t v[G8][8];
+#pragma unroll
+          for (int g = 0; g < G8; g++) tmem_ld8_async(acc + col0 + 8 * g, v[g]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int g = 0; g < G8; g++) {
+            const int col = col0 + 8 * g, q = col / ACH, j = (col - q * ACH) / 8;
+            uint32_t h[4];
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+              const int n = col + e;
+              const float y0 = snake(__uint_as_float(v[g][e]) + par[n], par[N + n], par[2 * N + n]);
+              const float y1 = snake(__uint_as_float(v[g][e + 1]) + par[n + 1], par[N + n + 1], par[2 * N + n + 1]);
+              const __half2 hp = __floats2half2_rn(y0, y1);
+              h[e / 2] = *reinterpret_cast<const uint32_t *>(&hp);
+            }
+            *reinterpret_cast<uint4 *>(a2 + q * L::kA + swz_off<ACH>(r, j)) = make_uint4(h[0], h[1], h[2], h[3]);
+          }
+        }
+        fence_proxy_async();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive1(&acce[buf]);
+          mbar_arrive1(a2f);
+        }
+        prev = p;
+      } else {
+        drain(acc, &acce[buf]);
+        bar_epi();
+        conv_sweep<N, kPtEpiWarps * 32>(a, stg, p.b, p.tq0, p.n0, p.phase, etid);
+        bar_epi();
+      }
+    }
+    if (FUSE && it >= 1) {
+      if (!err && !mbar_wait(acc2f, (it - 1) & 1)) err |= 64u;
+      tc_fence_after();
+      __syncwarp();
+      drain(tmem + tl + kAcc2, nullptr);
+      bar_epi();
+      conv_sweep<N, kPtEpiWarps * 32>(a, stg, prev.b, prev.tq0, prev.n0, prev.phase, etid);
+    }
+  }
+  if (err && c.err) atomicOr(c.err, (int)(err << 8));
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kCols);
+}
+
+static int g_sm_count = 0;
+
+template <int N, int ACH, int S, int FUSE>
+static void conv_pt_launch(const ConvArgs &a, int phases, cudaStream_t st, const ConvFuse *fu = nullptr) {
+  using L = ConvPtSmem<N, ACH, S, FUSE>;
+  static bool attr = false;
+  if (!attr) {
+    CK(cudaFuncSetAttribute(k_conv_pt<N, ACH, S, FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            (int)L::kBytes));
+    attr = true;
+  }
+  if (!g_sm_count) {
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    CK(cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev));
+  }
+  ConvPt c;
+  memset(&c, 0, sizeof c);
+  const CUtensorMapSwizzle sw = ACH == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  if (FUSE) {
+    if (!fu || a.Cout != N || a.Cin != N || phases != 1)
+      FAIL(Q3T_INVALID_INPUT, "codec fused residual unit: %d -> %d channels, %d phases (%d -> %d, 1 expected)",
+           a.Cin, a.Cout, phases, N, N);
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)N};
+    const uint64_t strides[1] = {(uint64_t)N * 2};
+    const uint32_t box[2] = {(uint32_t)ACH, (uint32_t)N};
+    if (!make_tmap(&c.tw1, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, fu->W1, dims, strides, box, sw))
+      FAIL(Q3T_CUDA_ERROR, "codec conv: TMA descriptor of the k1 weights failed");
+    c.mid_bias = fu->mid_bias;
+    c.mid_a = fu->mid_a;
+    c.mid_b = fu->mid_b;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)a.Cin, (uint64_t)a.Lin, (uint64_t)a.B};
+    const uint64_t strides[2] = {(uint64_t)a.Cin * 2, (uint64_t)a.Lin * a.Cin * 2};
+    const uint32_t box[3] = {(uint32_t)ACH, 128, 1};
+    if (!make_tmap(&c.tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, a.X, dims, strides, box, sw))
+      FAIL(Q3T_CUDA_ERROR, "codec conv: TMA descriptor of the input failed");
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)a.Cin, (uint64_t)phases * a.taps * a.Cout};
+    const uint64_t strides[1] = {(uint64_t)a.Cin * 2};
+    const uint32_t box[2] = {(uint32_t)ACH, (uint32_t)N};
+    if (!make_tmap(&c.tw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.W, dims, strides, box, sw))
+      FAIL(Q3T_CUDA_ERROR, "codec conv: TMA descriptor of the weights failed");
+  }
+  c.a = a;
+  c.tiles = (a.Lq + 127) / 128;
+  c.nb = a.Cout / N;
+  c.phases = phases;
+  const int64_t total = (int64_t)a.B * c.tiles * c.nb * phases;
+  if (total > INT32_MAX) FAIL(Q3T_INVALID_INPUT, "codec conv: %lld output tiles", (long long)total);
+  c.total = (int)total;
+  c.err = g_conv_err;
+  const int grid = (int)std::min<int64_t>(total, g_sm_count);
+  k_conv_pt<N, ACH, S, FUSE><<<grid, kPtThreads, L::kBytes, st>>>(c);
+}
+
 static void launch_conv(const ConvArgs &a, int phases, cudaStream_t st) {
   const int M = a.B * a.Lq;
   if (M <= 0) return;
   if (!g_conv_err) CK(cudaMalloc(&g_conv_err, sizeof(int)));
   const bool tc = a.Cin % 32 == 0 && (a.Cout % 128 == 0 || a.Cout % 96 == 0) && !getenv("Q3T_CONV_MMA_SYNC");
-  if (tc) {
+  static const bool per_tile = getenv("Q3T_CONV_PER_TILE") != nullptr;  // one CTA per tile (k_conv_tc)
+  if (tc && !per_tile) {
+    const bool wide = a.Cin % 64 == 0, n128 = a.Cout % 128 == 0;
+    if (wide && n128)
+      conv_pt_launch<128, 64, 4, 0>(a, phases, st);
+    else if (wide)
+      conv_pt_launch<96, 64, 4, 0>(a, phases, st);
+    else if (n128)
+      conv_pt_launch<128, 32, 6, 0>(a, phases, st);
+    else
+      conv_pt_launch<96, 32, 6, 0>(a, phases, st);
+  } else if (tc) {
     const bool wide = a.Cin % 64 == 0, n128 = a.Cout % 128 == 0;
     if (wide && n128)
       conv_tc_launch<128, 64, 3, 0>(a, phases, st);
@@ -558,7 +938,10 @@ static bool fused_unit_ok(int C) { return C == 96 && !getenv("Q3T_CONV_MMA_SYNC"
 static void launch_unit(const ConvArgs &a, const ConvFuse &fu, cudaStream_t st) {
   if (a.B * a.Lq <= 0) return;
   if (!g_conv_err) CK(cudaMalloc(&g_conv_err, sizeof(int)));
-  conv_tc_launch<96, 32, 6, 1>(a, 1, st, &fu);
+  if (getenv("Q3T_CONV_PER_TILE"))
+    conv_tc_launch<96, 32, 6, 1>(a, 1, st, &fu);
+  else
+    conv_pt_launch<96, 32, 6, 1>(a, 1, st, &fu);
   CK(cudaGetLastError());
   g_launches++;
 }
@@ -1478,6 +1861,7 @@ void codec_decode_host_codes(q3t_model *m, const int64_t *codes, int B, int T, f
   if (dw) CK(cudaFreeAsync(dw, st));
   if (dp) CK(cudaFreeAsync(dp, st));
   CK(cudaStreamSynchronize(st));
+  conv_check_err();
   CK(cudaEventElapsedTime(&g_codec_ms, e0, e1));
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
@@ -1548,6 +1932,7 @@ static void codec_decode_static(q3t_model *m, const int64_t *codes, int B, int T
   if (wave) CK(cudaMemcpyAsync(wave, dw, (size_t)B * n * 4, cudaMemcpyDeviceToHost, st));
   if (pcm) CK(cudaMemcpyAsync(pcm, dp, (size_t)B * n * 2, cudaMemcpyDeviceToHost, st));
   CK(cudaStreamSynchronize(st));
+  conv_check_err();
 }
 
 // ---------------------------------------------------------------------------
@@ -1581,6 +1966,7 @@ struct StreamState {
   cudaEvent_t ev_codes = nullptr, ev_done = nullptr;
   std::vector<StreamOut> out;      // emitted by the work in flight
   bool inflight = false;
+  int *h_err = nullptr;            // pinned copy of the convolutions' timeout word, taken with the work
 };
 static std::map<q3t_batch *, StreamState> g_streams;
 
@@ -1624,7 +2010,10 @@ void codec_stream_init(q3t_model *m, q3t_batch *b) {
     CK(cudaMemsetAsync(S.d_codes, 0, (size_t)Bw * nq * Tw * 8, S.cst));
     decode_device(c, S.d_codes, Bw, Tw, S.d_wave, nullptr, S.cst);
   }
+  CK(cudaHostAlloc(&S.h_err, sizeof(int), cudaHostAllocDefault));
+  *S.h_err = 0;
   CK(cudaStreamSynchronize(S.cst));
+  conv_check_err();
   g_streams[b] = S;
 }
 
@@ -1636,6 +2025,14 @@ void codec_stream_join(q3t_batch *b, int64_t *samples) {
   StreamState &S = it->second;
   CK(cudaEventSynchronize(S.ev_done));
   CK(cudaStreamWaitEvent(b->st, S.ev_done, 0));
+  if (*S.h_err) {
+    const int e = *S.h_err;
+    *S.h_err = 0;
+    S.out.clear();
+    S.inflight = false;
+    CK(cudaMemsetAsync(g_conv_err, 0, sizeof(int), S.cst));
+    FAIL(Q3T_DEVICE_TIMEOUT, "streaming codec: a bounded device wait gave up (code %#x)", e);
+  }
   for (const StreamOut &o : S.out) {
     if (b->desc.keep_output) memcpy(o.r->wave.data() + o.dst, S.h_wave + o.src, (size_t)o.n * 4);
     o.r->samples += o.n;
@@ -1654,6 +2051,7 @@ void codec_stream_free(q3t_batch *b) {
   if (S.d_codes) cudaFree(S.d_codes);
   if (S.d_wave) cudaFree(S.d_wave);
   if (S.h_wave) cudaFreeHost(S.h_wave);
+  if (S.h_err) cudaFreeHost(S.h_err);
   if (S.ev_codes) cudaEventDestroy(S.ev_codes);
   if (S.ev_done) cudaEventDestroy(S.ev_done);
   if (S.cst) cudaStreamDestroy(S.cst);
@@ -1757,6 +2155,7 @@ void codec_stream_step(q3t_model *m, q3t_batch *b, const std::vector<Req *> &act
     coff += (size_t)Bw * nq * Tw;
     woff += (size_t)Bw * std::max<int64_t>(nout, 1);
   }
+  if (g_conv_err) CK(cudaMemcpyAsync(S.h_err, g_conv_err, sizeof(int), cudaMemcpyDeviceToHost, S.cst));
   CK(cudaEventRecord(S.ev_done, S.cst));
   S.inflight = true;
   static const bool serial = getenv("Q3T_CODEC_SERIAL") != nullptr;  // no overlap (A/B measurements)

@@ -105,6 +105,15 @@ Q3T_DEV void tmem_ld16(uint32_t taddr, float *v) {
   for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// tcgen05.ld of 32 lanes x 8 columns without the wait; call tmem_wait_ld()
+// before reading r
+Q3T_DEV void tmem_ld8_async(uint32_t taddr, uint32_t *r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+Q3T_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 // 32 TMEM lanes (one per thread of the warp) x 8 consecutive f32 columns
 Q3T_DEV void tmem_ld8(uint32_t taddr, float *v) {
   uint32_t r[8];
