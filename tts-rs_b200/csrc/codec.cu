@@ -336,6 +336,68 @@ Q3T_DEV void conv_sweep(const ConvArgs &a, const float *tile, int b, int tq0, in
   }
 }
 
+// conv_sweep for the persistent kernel: thread tid owns the 4-channel column
+// group tid % (N / 4) of rows tid / (N / 4) + k * RP (RP = NTH / (N / 4) rows
+// per pass, consecutive threads still cover a row contiguously), so its
+// per-channel parameters load once per tile and UN rows' residual loads are
+// in flight together.
+template <int N, int NTH>
+Q3T_DEV void conv_sweep_cols(const ConvArgs &a, const float *tile, int b, int tq0, int n0, int phase, int tid) {
+  constexpr int TP = N + 4, G4 = N / 4, RP = NTH / G4, UN = 4;
+  const int c4 = tid % G4, r0 = tid / G4;
+  if (r0 >= RP) return;
+  const int n = n0 + 4 * c4;
+  const float4 bb = a.bias ? *reinterpret_cast<const float4 *>(a.bias + n) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 sc = a.scale ? *reinterpret_cast<const float4 *>(a.scale + n) : make_float4(1.f, 1.f, 1.f, 1.f);
+  float4 ea = make_float4(0.f, 0.f, 0.f, 0.f), ib = ea;
+  if (a.act == ACT_SNAKE) {
+    ea = *reinterpret_cast<const float4 *>(a.act_a + n);
+    ib = *reinterpret_cast<const float4 *>(a.act_b + n);
+  }
+  const int rows = min(128, a.Lq - tq0);
+  const size_t rstride = (size_t)a.ostride * a.Cout;
+  const size_t e0 = (((size_t)b * a.Lout + phase) + (size_t)tq0 * a.ostride) * a.Cout + n;
+  for (int row0 = r0; row0 < rows; row0 += RP * UN) {
+    float4 v[UN], r[UN];
+#pragma unroll
+    for (int u = 0; u < UN; u++) {
+      const int row = row0 + RP * u;
+      if (row < rows) {
+        v[u] = *reinterpret_cast<const float4 *>(tile + row * TP + 4 * c4);
+        if (a.R) r[u] = *reinterpret_cast<const float4 *>(a.R + e0 + row * rstride);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < UN; u++) {
+      const int row = row0 + RP * u;
+      if (row >= rows) break;
+      const size_t e = e0 + row * rstride;
+      float y[4] = {(v[u].x + bb.x) * sc.x, (v[u].y + bb.y) * sc.y, (v[u].z + bb.z) * sc.z, (v[u].w + bb.w) * sc.w};
+      if (a.R) {
+        y[0] += r[u].x;
+        y[1] += r[u].y;
+        y[2] += r[u].z;
+        y[3] += r[u].w;
+      }
+      if (a.Yf) *reinterpret_cast<float4 *>(a.Yf + e) = make_float4(y[0], y[1], y[2], y[3]);
+      if (a.Yh) {
+        float h[4] = {y[0], y[1], y[2], y[3]};
+        if (a.act == ACT_SNAKE) {
+          h[0] = snake(y[0], ea.x, ib.x);
+          h[1] = snake(y[1], ea.y, ib.y);
+          h[2] = snake(y[2], ea.z, ib.z);
+          h[3] = snake(y[3], ea.w, ib.w);
+        } else if (a.act == ACT_GELU) {
+#pragma unroll
+          for (int j = 0; j < 4; j++) h[j] = gelu_erf(y[j]);
+        }
+        __half2 hp[2] = {__floats2half2_rn(h[0], h[1]), __floats2half2_rn(h[2], h[3])};
+        *reinterpret_cast<uint2 *>(a.Yh + e) = *reinterpret_cast<const uint2 *>(hp);
+      }
+    }
+  }
+}
+
 template <int N, int ACH, int S>
 struct ConvTcSmem {
   static constexpr int kA = 128 * ACH * 2, kB = N * ACH * 2, kStage = kA + kB;
@@ -779,7 +841,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_conv_pt(const __grid_constant
           __syncwarp();
           drain(tmem + tl + kAcc2, nullptr);
           bar_epi();
-          conv_sweep<N, kPtEpiWarps * 32>(a, stg, prev.b, prev.tq0, prev.n0, prev.phase, etid);
+          conv_sweep_cols<N, kPtEpiWarps * 32>(a, stg, prev.b, prev.tq0, prev.n0, prev.phase, etid);
           bar_epi();
         }
         // act2(acc + b7) -> fp16 A operand of the k1 GEMM
@@ -792,11 +854,17 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_conv_pt(const __grid_constant
           for (int g = 0; g < G8; g++) {
             const int col = col0 + 8 * g, q = col / ACH, j = (col - q * ACH) / 8;
             uint32_t h[4];
+            float pb[8], pa[8], pi[8];
+#pragma unroll
+            for (int e = 0; e < 8; e += 4) {
+              *reinterpret_cast<float4 *>(pb + e) = *reinterpret_cast<const float4 *>(par + col + e);
+              *reinterpret_cast<float4 *>(pa + e) = *reinterpret_cast<const float4 *>(par + N + col + e);
+              *reinterpret_cast<float4 *>(pi + e) = *reinterpret_cast<const float4 *>(par + 2 * N + col + e);
+            }
 #pragma unroll
             for (int e = 0; e < 8; e += 2) {
-              const int n = col + e;
-              const float y0 = snake(__uint_as_float(v[g][e]) + par[n], par[N + n], par[2 * N + n]);
-              const float y1 = snake(__uint_as_float(v[g][e + 1]) + par[n + 1], par[N + n + 1], par[2 * N + n + 1]);
+              const float y0 = snake(__uint_as_float(v[g][e]) + pb[e], pa[e], pi[e]);
+              const float y1 = snake(__uint_as_float(v[g][e + 1]) + pb[e + 1], pa[e + 1], pi[e + 1]);
               const __half2 hp = __floats2half2_rn(y0, y1);
               h[e / 2] = *reinterpret_cast<const uint32_t *>(&hp);
             }
@@ -814,7 +882,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_conv_pt(const __grid_constant
       } else {
         drain(acc, &acce[buf]);
         bar_epi();
-        conv_sweep<N, kPtEpiWarps * 32>(a, stg, p.b, p.tq0, p.n0, p.phase, etid);
+        conv_sweep_cols<N, kPtEpiWarps * 32>(a, stg, p.b, p.tq0, p.n0, p.phase, etid);
         bar_epi();
       }
     }
@@ -824,7 +892,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_conv_pt(const __grid_constant
       __syncwarp();
       drain(tmem + tl + kAcc2, nullptr);
       bar_epi();
-      conv_sweep<N, kPtEpiWarps * 32>(a, stg, prev.b, prev.tq0, prev.n0, prev.phase, etid);
+      conv_sweep_cols<N, kPtEpiWarps * 32>(a, stg, prev.b, prev.tq0, prev.n0, prev.phase, etid);
     }
   }
   if (err && c.err) atomicOr(c.err, (int)(err << 8));
