@@ -739,17 +739,19 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_conv_pt(const __grid_constant
       int ks = 0;
       for (int t = blockIdx.x; t < c.total && !err; t += gridDim.x) {
         const PtTile p = pt_tile(c, t, N);
-        for (int k = 0; k < KS; k++, ks++) {
-          const int s = ks % S, i = ks / S;
-          if (i > 0 && !mbar_wait(&empty[s], (i - 1) & 1)) {
-            err |= 1u;
-            break;
+        for (int tap = 0; tap < a.taps && !err; tap++) {
+          const int row = p.tq0 + a.in_off + tap * a.dil, wrow = (p.phase * a.taps + tap) * a.Cout + p.n0;
+          for (int c0 = 0; c0 < kc * ACH; c0 += ACH, ks++) {
+            const int s = ks % S, i = ks / S;
+            if (i > 0 && !mbar_wait(&empty[s], (i - 1) & 1)) {
+              err |= 1u;
+              break;
+            }
+            unsigned char *st = sm + s * L::kStage;
+            mbar_expect_tx(&full[s], L::kStage);
+            tma_load_3d(st, &c.tx, c0, row, p.b, &full[s]);
+            tma_load_2d(st + L::kA, &c.tw, c0, wrow, &full[s]);
           }
-          const int tap = k / kc, c0 = (k - tap * kc) * ACH;
-          unsigned char *st = sm + s * L::kStage;
-          mbar_expect_tx(&full[s], L::kStage);
-          tma_load_3d(st, &c.tx, c0, p.tq0 + a.in_off + tap * a.dil, p.b, &full[s]);
-          tma_load_2d(st + L::kA, &c.tw, c0, (p.phase * a.taps + tap) * a.Cout + p.n0, &full[s]);
         }
       }
       // the copies still in flight (none unless a wait above gave up) land before the CTA ends
@@ -760,18 +762,24 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_conv_pt(const __grid_constant
     if (lane == 0) {  // MMA issuer
       constexpr uint32_t idesc = umma_idesc_f16(128, N);
       if (FUSE && !mbar_wait(w1f, 0)) err |= 8u;
+      // operand descriptors: the start-address field is (address >> 4) in
+      // bits 0..13, so stepping 32 bytes along K adds 2 and a stage adds
+      // kStage >> 4 (shared addresses stay below 256 KB: no carry)
+      const uint64_t da0 = ACH == 64 ? sw128_desc(sm) : sw64_desc(sm);
+      const uint64_t db0 = ACH == 64 ? sw128_desc(sm + L::kA) : sw64_desc(sm + L::kA);
       auto mma2 = [&](int j) {  // k1 GEMM of tile j: A2 x W1 -> accumulator 2
         if (!err && !mbar_wait(a2f, j & 1)) err |= 16u;
         tc_fence_after();
-        if (!err)
+        if (!err) {
+          const uint64_t a2d = ACH == 64 ? sw128_desc(a2) : sw64_desc(a2);
+          const uint64_t w1d = ACH == 64 ? sw128_desc(w1) : sw64_desc(w1);
+#pragma unroll
           for (int q = 0; q < N / ACH; q++)
 #pragma unroll
-            for (int kk = 0; kk < ACH / 16; kk++) {
-              const unsigned char *pa = a2 + q * L::kA + kk * 32, *pb = w1 + q * L::kB + kk * 32;
-              const uint64_t ad = ACH == 64 ? sw128_desc(pa) : sw64_desc(pa);
-              const uint64_t bd = ACH == 64 ? sw128_desc(pb) : sw64_desc(pb);
-              umma_kf16(tmem + kAcc2, ad, bd, idesc, (q | kk) != 0 ? 1u : 0u);
-            }
+            for (int kk = 0; kk < ACH / 16; kk++)
+              umma_kf16(tmem + kAcc2, a2d + (uint64_t)((q * L::kA) >> 4) + 2 * kk,
+                        w1d + (uint64_t)((q * L::kB) >> 4) + 2 * kk, idesc, (q | kk) != 0 ? 1u : 0u);
+        }
         umma_commit(acc2f);
       };
       int ks = 0, it = 0;
@@ -787,13 +795,10 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_conv_pt(const __grid_constant
             break;
           }
           tc_fence_after();
-          const unsigned char *st = sm + s * L::kStage;
+          const uint64_t so = (uint64_t)((s * L::kStage) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < ACH / 16; kk++) {
-            const uint64_t ad = ACH == 64 ? sw128_desc(st + kk * 32) : sw64_desc(st + kk * 32);
-            const uint64_t bd = ACH == 64 ? sw128_desc(st + L::kA + kk * 32) : sw64_desc(st + L::kA + kk * 32);
-            umma_kf16(d, ad, bd, idesc, (k | kk) != 0 ? 1u : 0u);
-          }
+          for (int kk = 0; kk < ACH / 16; kk++)
+            umma_kf16(d, da0 + so + 2 * kk, db0 + so + 2 * kk, idesc, (k | kk) != 0 ? 1u : 0u);
           umma_commit(&empty[s]);
         }
         umma_commit(&accf[buf]);
@@ -970,11 +975,11 @@ static void launch_conv(const ConvArgs &a, int phases, cudaStream_t st) {
     if (wide && n128)
       conv_pt_launch<128, 64, 4, 0>(a, phases, st);
     else if (wide)
-      conv_pt_launch<96, 64, 4, 0>(a, phases, st);
+      conv_pt_launch<96, 64, 6, 0>(a, phases, st);
     else if (n128)
-      conv_pt_launch<128, 32, 6, 0>(a, phases, st);
+      conv_pt_launch<128, 32, 8, 0>(a, phases, st);
     else
-      conv_pt_launch<96, 32, 6, 0>(a, phases, st);
+      conv_pt_launch<96, 32, 8, 0>(a, phases, st);
   } else if (tc) {
     const bool wide = a.Cin % 64 == 0, n128 = a.Cout % 128 == 0;
     if (wide && n128)
@@ -1009,7 +1014,7 @@ static void launch_unit(const ConvArgs &a, const ConvFuse &fu, cudaStream_t st) 
   if (getenv("Q3T_CONV_PER_TILE"))
     conv_tc_launch<96, 32, 6, 1>(a, 1, st, &fu);
   else
-    conv_pt_launch<96, 32, 6, 1>(a, 1, st, &fu);
+    conv_pt_launch<96, 32, 8, 1>(a, 1, st, &fu);
   CK(cudaGetLastError());
   g_launches++;
 }
