@@ -656,8 +656,9 @@ struct ConvPt {
 
 template <int N, int ACH, int S, int FUSE>
 struct ConvPtSmem {
+  static constexpr int NS = N > 128 ? N / 2 : N;  // columns drained per staging pass
   static constexpr int kA = 128 * ACH * 2, kB = N * ACH * 2, kStage = kA + kB;
-  static constexpr int kStg = 128 * (N + 4) * 4;
+  static constexpr int kStg = 128 * (NS + 4) * 4;
   static constexpr int kA2 = FUSE ? 128 * N * 2 : 0;
   static constexpr int kW1 = FUSE ? N * N * 2 : 0;
   static constexpr int kPar = FUSE ? 3 * N * 4 : 0;
@@ -690,8 +691,11 @@ Q3T_DEV PtTile pt_tile(const ConvPt &c, int t, int N) {
 template <int N, int ACH, int S, int FUSE>
 __global__ void __launch_bounds__(kPtThreads, 1) k_conv_pt(const __grid_constant__ ConvPt c) {
   using L = ConvPtSmem<N, ACH, S, FUSE>;
-  static_assert(N <= 128 && N % 32 == 0, "two accumulators of <= 128 columns, 8-column groups per quarter");
-  constexpr uint32_t kCols = FUSE ? 512 : 256, kAcc2 = 256;
+  constexpr int NS = L::NS;
+  static_assert(N <= 256 && NS % 32 == 0 && (!FUSE || N <= 128), "accumulator / staging shapes");
+  // accumulators: tile i in columns kAccStride * (i & 1) .., the fused k1 GEMM in 256 ..
+  constexpr uint32_t kAccStride = N > 128 ? 256 : 128;
+  constexpr uint32_t kCols = (FUSE || N > 128) ? 512 : 256, kAcc2 = 256;
   extern __shared__ unsigned char csm_raw[];
   unsigned char *sm = csm_raw + ((1024 - (smem_addr(csm_raw) & 1023)) & 1023);
   uint64_t *full = reinterpret_cast<uint64_t *>(sm + L::oBar), *empty = full + S;
@@ -787,7 +791,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_conv_pt(const __grid_constant
         const int buf = it & 1;
         if (!err && it >= 2 && !mbar_wait(&acce[buf], ((it >> 1) - 1) & 1)) err |= 4u;
         tc_fence_after();
-        const uint32_t d = tmem + 128u * buf;
+        const uint32_t d = tmem + kAccStride * buf;
         for (int k = 0; k < KS && !err; k++, ks++) {
           const int s = ks % S;
           if (!mbar_wait(&full[s], (ks / S) & 1)) {
@@ -811,14 +815,14 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_conv_pt(const __grid_constant
   } else {  // epilogue warps
     const int ew = warp - 2, quad = warp & 3, part = ew >> 2, r = 32 * quad + lane, etid = threadIdx.x - 64;
     const uint32_t tl = (uint32_t)(32 * quad) << 16;
-    constexpr int G8 = N / 32;  // 8-column groups per quarter
+    constexpr int G8 = NS / 32;  // 8-column groups per quarter of a staging pass
     const int col0 = part * G8 * 8;
-    auto drain = [&](uint32_t taddr, uint64_t *release) {  // accumulator rows -> staging tile
+    auto drain = [&](uint32_t taddr, uint64_t *release) {  // NS accumulator columns -> staging tile
       uint32_t v[G8][8];
 #pragma unroll
       for (int g = 0; g < G8; g++) tmem_ld8_async(taddr + col0 + 8 * g, v[g]);
       tmem_wait_ld();
-      float4 *dst = reinterpret_cast<float4 *>(stg + r * (N + 4) + col0);
+      float4 *dst = reinterpret_cast<float4 *>(stg + r * (NS + 4) + col0);
 #pragma unroll
       for (int g = 0; g < G8; g++) {
         dst[2 * g] = make_float4(__uint_as_float(v[g][0]), __uint_as_float(v[g][1]), __uint_as_float(v[g][2]),
@@ -838,7 +842,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_conv_pt(const __grid_constant
       if (!err && !mbar_wait(&accf[buf], (it >> 1) & 1)) err |= 32u;
       tc_fence_after();
       __syncwarp();
-      const uint32_t acc = tmem + tl + 128u * buf;
+      const uint32_t acc = tmem + tl + kAccStride * buf;
       if (FUSE) {
         if (it >= 1) {  // tile it - 1's k1 result; also frees A2
           if (!err && !mbar_wait(acc2f, (it - 1) & 1)) err |= 64u;
@@ -846,7 +850,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_conv_pt(const __grid_constant
           __syncwarp();
           drain(tmem + tl + kAcc2, nullptr);
           bar_epi();
-          conv_sweep_cols<N, kPtEpiWarps * 32>(a, stg, prev.b, prev.tq0, prev.n0, prev.phase, etid);
+          conv_sweep_cols<NS, kPtEpiWarps * 32>(a, stg, prev.b, prev.tq0, prev.n0, prev.phase, etid);
           bar_epi();
         }
         // act2(acc + b7) -> fp16 A operand of the k1 GEMM
@@ -885,10 +889,13 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_conv_pt(const __grid_constant
         }
         prev = p;
       } else {
-        drain(acc, &acce[buf]);
-        bar_epi();
-        conv_sweep_cols<N, kPtEpiWarps * 32>(a, stg, p.b, p.tq0, p.n0, p.phase, etid);
-        bar_epi();
+#pragma unroll 1
+        for (int cb = 0; cb < N / NS; cb++) {
+          drain(acc + cb * NS, cb == N / NS - 1 ? &acce[buf] : nullptr);
+          bar_epi();
+          conv_sweep_cols<NS, kPtEpiWarps * 32>(a, stg, p.b, p.tq0, p.n0 + cb * NS, p.phase, etid);
+          bar_epi();
+        }
       }
     }
     if (FUSE && it >= 1) {
@@ -897,7 +904,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_conv_pt(const __grid_constant
       __syncwarp();
       drain(tmem + tl + kAcc2, nullptr);
       bar_epi();
-      conv_sweep_cols<N, kPtEpiWarps * 32>(a, stg, prev.b, prev.tq0, prev.n0, prev.phase, etid);
+      conv_sweep_cols<NS, kPtEpiWarps * 32>(a, stg, prev.b, prev.tq0, prev.n0, prev.phase, etid);
     }
   }
   if (err && c.err) atomicOr(c.err, (int)(err << 8));
@@ -972,7 +979,11 @@ static void launch_conv(const ConvArgs &a, int phases, cudaStream_t st) {
   static const bool per_tile = getenv("Q3T_CONV_PER_TILE") != nullptr;  // one CTA per tile (k_conv_tc)
   if (tc && !per_tile) {
     const bool wide = a.Cin % 64 == 0, n128 = a.Cout % 128 == 0;
-    if (wide && n128)
+    if (wide && a.Cout % 256 == 0)
+      conv_pt_launch<256, 64, 3, 0>(a, phases, st);
+    else if (wide && a.Cout % 192 == 0)
+      conv_pt_launch<192, 64, 4, 0>(a, phases, st);
+    else if (wide && n128)
       conv_pt_launch<128, 64, 4, 0>(a, phases, st);
     else if (wide)
       conv_pt_launch<96, 64, 6, 0>(a, phases, st);
