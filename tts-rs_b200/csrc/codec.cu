@@ -1321,39 +1321,52 @@ __global__ void __launch_bounds__(256) k_dwconv_ln(const float *y, int L, int C,
 }
 
 // output conv C -> 1, k7, causal, + clamp (decoder.rs:273-276) and PCM
-// (codec/infer/mod.rs:80-90); rows [t0 - 6, t0 + kOutTile) staged in shared
-// memory with a row pitch of C + 2 halves (an odd number of 4-byte words, so
-// the 32 threads of a warp, one row each, read 32 different banks).
+// (codec/infer/mod.rs:80-90).  y[t] = bias + sum_j p_j[t - 6 + j] with
+// p_j[u] = a[u] . w[j]: each thread reads one input row of the tile's rows
+// [t0 - 6, t0 + kOutTile) once, 8 channels at a time, and forms its 7 tap
+// products against weights broadcast from shared memory (4 FMAs per shared
+// load); the partial sums meet in shared memory.
 constexpr int kOutTile = 128;
 __global__ void __launch_bounds__(kOutTile) k_out_conv(const __half *a, int L, int C, const float *w, float bias,
                                                        float *wave, int16_t *pcm) {
-  extern __shared__ __half tile[];
-  __shared__ float ws[7 * 192];
-  const int b = blockIdx.y, t0 = blockIdx.x * kOutTile, cp = C + 2;
+  __shared__ __align__(16) float ws[7 * 192];
+  __shared__ float ps[7][kOutTile + 6];
+  const int b = blockIdx.y, t0 = blockIdx.x * kOutTile;
   for (int e = threadIdx.x; e < 7 * C; e += blockDim.x) ws[e] = w[e];
-  const int rows = kOutTile + 6, c8n = C / 8;
-  for (int e = threadIdx.x; e < rows * c8n; e += blockDim.x) {
-    const int r = e / c8n, c8 = e - r * c8n;
-    const int tt = t0 - 6 + r;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (tt >= 0 && tt < L) v = *reinterpret_cast<const uint4 *>(a + ((size_t)b * L + tt) * C + 8 * c8);
-    uint32_t *d = reinterpret_cast<uint32_t *>(tile + (size_t)r * cp + 8 * c8);
-    d[0] = v.x;
-    d[1] = v.y;
-    d[2] = v.z;
-    d[3] = v.w;
+  __syncthreads();
+  for (int r = threadIdx.x; r < kOutTile + 6; r += blockDim.x) {
+    const int u = t0 - 6 + r;
+    float p[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (u >= 0 && u < L) {
+      const uint4 *row = reinterpret_cast<const uint4 *>(a + ((size_t)b * L + u) * C);
+      for (int c8 = 0; c8 < C / 8; c8++) {
+        const uint4 v = row[c8];
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v);
+        float x[8];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float2 f = __half22float2(h[i]);
+          x[2 * i] = f.x;
+          x[2 * i + 1] = f.y;
+        }
+#pragma unroll
+        for (int j = 0; j < 7; j++) {
+          const float4 w0 = *reinterpret_cast<const float4 *>(ws + j * C + 8 * c8);
+          const float4 w1 = *reinterpret_cast<const float4 *>(ws + j * C + 8 * c8 + 4);
+          p[j] += x[0] * w0.x + x[1] * w0.y + x[2] * w0.z + x[3] * w0.w + x[4] * w1.x + x[5] * w1.y + x[6] * w1.z +
+                  x[7] * w1.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 7; j++) ps[j][r] = p[j];
   }
   __syncthreads();
   const int t = t0 + threadIdx.x;
   if (t >= L) return;
   float acc = bias;
-  for (int j = 0; j < 7; j++) {
-    const __half *row = tile + (size_t)(threadIdx.x + j) * cp;
-    for (int c = 0; c < C; c += 2) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(row + c));
-      acc += f.x * ws[j * C + c] + f.y * ws[j * C + c + 1];
-    }
-  }
+#pragma unroll
+  for (int j = 0; j < 7; j++) acc += ps[j][threadIdx.x + j];
   const float y = fminf(fmaxf(acc, -1.f), 1.f);
   if (wave) wave[(size_t)b * L + t] = y;
   if (pcm) {
@@ -1898,8 +1911,7 @@ static void decode_with(CodecModel *c, const CodecScratch &ws, const int64_t *d_
   if (C % 8 || C > 192) FAIL(Q3T_INVALID_INPUT, "codec output conv: %d channels (multiple of 8, <= 192 supported)", C);
   {
     dim3 grid((Lc + kOutTile - 1) / kOutTile, B);
-    const size_t sm = (size_t)(kOutTile + 6) * (C + 2) * sizeof(__half);
-    k_out_conv<<<grid, kOutTile, sm, st>>>(act, Lc, C, c->out_w, c->out_b, d_wave, d_pcm);
+    k_out_conv<<<grid, kOutTile, 0, st>>>(act, Lc, C, c->out_w, c->out_b, d_wave, d_pcm);
     CK(cudaGetLastError());
     g_launches++;
   }
