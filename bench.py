@@ -58,6 +58,8 @@ def parse():
     p.add_argument("--only-codec", action="store_true",
                    help="run only the T=750 codec decode measurement (prints its JSON object; for profiling)")
     p.add_argument("--codec-batches", default="1,8")
+    p.add_argument("--codec-frames", type=int, default=750,
+                   help="--only-codec: frames per sequence (750 = 60 s; smaller cases for ncu captures)")
     p.add_argument("--no-components", action="store_true",
                    help="skip the predictor-loop (B=1/16/64) and codec (T=750, B=1/8) measurements")
     p.add_argument("--c3-frames", type=int, default=512)
@@ -291,7 +293,7 @@ def main():
         pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))).get("bf16_tflops", 1590.0) \
             if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
         bs = tuple(int(x) for x in args.codec_batches.split(","))
-        print(json.dumps(codec_decode_t750(model, cc, batches=bs, peak_tflops=pk)), flush=True)
+        print(json.dumps(codec_decode_t750(model, cc, batches=bs, T=args.codec_frames, peak_tflops=pk)), flush=True)
         model.close()
         return
     if args.only_b1:
