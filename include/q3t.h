@@ -225,14 +225,42 @@ q3t_status q3t_codec_decode_static(q3t_model *model, const int64_t *codes, int B
  * Qwen3TtsTalkerResizeMlp (talker/network/mlp.rs:36-40, config.rs:200-209)
  * over the text embedding: out[i] = linear_fc2(silu(linear_fc1(
  * text_embedding[ids[i]]))) with biases, [n][hidden] f32 rows holding bf16
- * values (the model dtype).  The session seed is assembled from these rows by
- * the caller (session_seed.rs:151-215).  Needs the optional tensors
+ * values (the model dtype).  q3t_session_seed assembles a whole prompt seed
+ * from these rows on the device.  Needs the optional tensors
  * talker.model.text_embedding.weight [text_vocab][text_hidden] and
  * talker.text_projection.linear_fc{1,2}.{weight,bias} in q3t_model_load;
  * INVALID_INPUT without them or for ids outside [0, text_vocab). */
 q3t_status q3t_text_project(q3t_model *model, const int64_t *ids, int n, float *out);
 /* text_vocab / text_hidden of the loaded text projection (0 if absent). */
 q3t_status q3t_text_dims(const q3t_model *model, int *text_vocab, int *text_hidden);
+
+/* Control token ids of a profile (the reference's ProfileControlIds). */
+typedef struct {
+  int64_t tts_bos_token_id, tts_eos_token_id, tts_pad_token_id; /* text vocabulary */
+  const int64_t *codec_prefix_ids;                               /* talker codec vocabulary */
+  int n_codec_prefix;                                            /* >= 2 */
+  int64_t codec_pad_id, codec_bos_id;                            /* talker codec vocabulary */
+} q3t_seed_controls;
+
+/* The prompt seed of the non-voice-clone recipes, build_non_streaming_seed
+ * (session_seed.rs:151-215), computed on the device: with P(ids) the text
+ * projection above and E(id) the talker codec embedding,
+ *   inputs_embeds = [ P(leading_ids)                      (instruct, nullable)
+ *                     P(text_ids[0..3])                   (role)
+ *                     P(pad) x (n_codec_prefix - 2), P(bos)  + E(codec_prefix_ids[0..n-1])
+ *                     P(text_ids[3..n_text-5])             + E(codec_pad_id)
+ *                     P(eos)                               + E(codec_pad_id)
+ *                     P(pad)                               + E(codec_bos_id) ]
+ * as [rows][hidden] f32 rows holding bf16 values (sums rounded as the
+ * reference's bf16 adds), rows = n_leading + 3 + (n_codec_prefix - 1) +
+ * (n_text - 8) + 2; pad_embed [hidden] = P(tts_pad), which is also the
+ * trailing text hidden of these recipes.  inputs_embeds == NULL only reports
+ * *rows; max_rows < rows or n_text < 8, n_codec_prefix < 2 or an id outside
+ * its vocabulary is INVALID_INPUT.  The voice-clone seeds need the codec and
+ * speaker encoders, which this library does not have. */
+q3t_status q3t_session_seed(q3t_model *model, const int64_t *text_ids, int n_text, const int64_t *leading_ids,
+                            int n_leading, const q3t_seed_controls *controls, float *inputs_embeds, int max_rows,
+                            int *rows, float *pad_embed);
 
 /* ------------------------------- file IO --------------------------------- */
 /* A memory-mapped .safetensors checkpoint whose float tensors (F32 and BF16

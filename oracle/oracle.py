@@ -142,6 +142,13 @@ def ip(a):
     return None if a is None else a.ctypes.data_as(I64)
 
 
+def bf16_round(a):
+    """Round f32 values to the nearest bf16 (ties to even), kept as f32."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    u = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    return u.view(np.float32)
+
+
 def f32(a):
     return np.ascontiguousarray(a, dtype=np.float32)
 
@@ -226,6 +233,28 @@ class OracleTalker:
         lib().orc_text_project(fp(emb), fp(keep[0]), fp(keep[1]), fp(keep[2]), fp(keep[3]), Ht, H,
                                ids.ctypes.data_as(I64), len(ids), fp(out))
         return out
+
+    def session_seed(self, text_ids, controls, leading_ids=None):
+        """build_non_streaming_seed (session_seed.rs:151-215): (inputs_embeds
+        [rows][hidden], tts_pad embedding).  Text rows are project_text_ids
+        (:668-679), codec rows the talker codec_embedding (:681-688); every
+        sum is rounded to bf16, the talker dtype (the reference adds bf16
+        tensors)."""
+        text_ids = np.asarray(text_ids, np.int64)
+        cp = np.asarray(controls["codec_prefix_ids"], np.int64)
+        if len(text_ids) < 8 or len(cp) < 2:
+            raise ValueError("need >= 8 text ids and >= 2 codec prefix ids")
+        E = f32(self.w["talker.model.codec_embedding.weight"])
+        bos, eos, pad = self.text_project([controls["tts_bos_token_id"], controls["tts_eos_token_id"],
+                                           controls["tts_pad_token_id"]])
+        role = self.text_project(text_ids[:3])
+        body = self.text_project(text_ids[3:len(text_ids) - 5])
+        n = len(cp)
+        prefix = np.concatenate([np.repeat(pad[None], max(n - 2, 0), 0), bos[None]]) + E[cp[:n - 1]]
+        segs = [] if leading_ids is None else [self.text_project(np.asarray(leading_ids, np.int64))]
+        segs += [role, prefix, body + E[controls["codec_pad_id"]], (eos + E[controls["codec_pad_id"]])[None],
+                 (pad + E[controls["codec_bos_id"]])[None]]
+        return bf16_round(np.concatenate(segs)), pad
 
     def codec_head(self, hidden):
         h = f32(hidden).reshape(-1, self.cfg.talker.hidden)

@@ -87,3 +87,40 @@ def test_session_from_text_ids(text_model):
         _close(tl, otl, f"talker logits frame {f}")
         _close(pl, opl, f"predictor logits frame {f}")
     sess.close()
+
+
+# Control ids of the reference's compiler fixture for an explicit language
+# (execution/compiler/tests.rs:108-124): [think, think_bos, language,
+# think_eos, pad, bos]; text control ids inside the synthetic text vocabulary.
+SEED_CONTROLS = {"tts_bos_token_id": TEXT_VOCAB - 3, "tts_eos_token_id": TEXT_VOCAB - 2,
+                 "tts_pad_token_id": TEXT_VOCAB - 1,
+                 "codec_prefix_ids": [2050, 2052, 3001, 2053, 2049, 2048], "codec_pad_id": 2049, "codec_bos_id": 2048}
+
+
+@pytest.mark.parametrize("n_text,n_lead", [(8, 0), (40, 0), (90, 12)])
+def test_session_seed_matches_oracle(text_model, n_text, n_lead):
+    """q3t_session_seed (build_non_streaming_seed, session_seed.rs:151-215) on
+    the device vs the oracle's assembly: same rows (text projection tolerance
+    above), same row count, the pad embedding = P(tts_pad)."""
+    cfg, w, model, ot = text_model
+    g = np.random.default_rng([n_text, n_lead])
+    text = g.integers(0, TEXT_VOCAB - 3, n_text)
+    lead = g.integers(0, TEXT_VOCAB - 3, n_lead) if n_lead else None
+    got, pad = model.session_seed(text, SEED_CONTROLS, leading_ids=lead)
+    ref, ref_pad = ot.session_seed(text, SEED_CONTROLS, leading_ids=lead)
+    assert got.shape == ref.shape == (n_lead + 3 + 5 + (n_text - 8) + 2, cfg.talker.hidden)
+    assert np.array_equal(got, S.bf16_round(got)), "rows hold bf16 values"
+    _close(got, ref, f"seed rows n_text={n_text}")
+    _close(pad, ref_pad, "pad embedding")
+
+
+def test_session_seed_rejects_bad_input(text_model):
+    cfg, w, model, ot = text_model
+    text = np.arange(20, dtype=np.int64)
+    for bad_text, ctl in ((text[:7], SEED_CONTROLS),
+                          (text, dict(SEED_CONTROLS, codec_prefix_ids=[2048])),
+                          (text, dict(SEED_CONTROLS, codec_pad_id=cfg.talker.vocab)),
+                          (text, dict(SEED_CONTROLS, tts_pad_token_id=TEXT_VOCAB))):
+        with pytest.raises(q3t.Q3TError) as e:
+            model.session_seed(bad_text, ctl)
+        assert e.value.status == 1  # INVALID_INPUT

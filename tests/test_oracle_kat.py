@@ -172,3 +172,41 @@ def test_text_projection_oracle_matches_numpy():
     assert (diff <= np.abs(ref) * 2.0 ** -7 + 1e-3 * np.abs(ref).max()).all()
     assert (diff == 0).mean() > 0.97
     assert np.array_equal(got[2], got[3]), "equal ids give equal rows"
+
+
+# Control ids of the reference's base-profile compiler fixture with automatic
+# language (execution/compiler/tests.rs:87-106): codec prefix
+# [nothink, think_bos, think_eos, pad, bos]; pad 2049 and bos 2048 are its
+# last two entries (compiler/mod.rs:326).
+SEED_CONTROLS = {"tts_bos_token_id": 501, "tts_eos_token_id": 502, "tts_pad_token_id": 503,
+                 "codec_prefix_ids": [2051, 2052, 2053, 2049, 2048], "codec_pad_id": 2049, "codec_bos_id": 2048}
+
+
+def test_session_seed_oracle_layout():
+    """build_non_streaming_seed (session_seed.rs:151-215) in the oracle: rows
+    = leading + 3 role + (prefix - 1) + body + 2, each row the bf16 sum of the
+    projected text row and the codec embedding row the reference pairs it
+    with; the pad embedding is P(tts_pad)."""
+    cfg = S.TalkerConfig().small(talker_layers=1, predictor_layers=1)
+    w = S.make_talker_weights(cfg, seed=0)
+    w.update(S.make_text_weights(cfg, seed=0, text_vocab=512, text_hidden=256))
+    ot = O.OracleTalker(cfg, w)
+    text = np.arange(10, 22, dtype=np.int64)  # role 10..12, body 13..16, 5 trailing ids
+    lead = np.array([40, 41], np.int64)
+    rows, pad = ot.session_seed(text, SEED_CONTROLS, leading_ids=lead)
+    c = SEED_CONTROLS
+    assert rows.shape == (2 + 3 + 4 + 4 + 2, cfg.talker.hidden)
+    P = lambda ids: ot.text_project(np.asarray(ids, np.int64))
+    E = w["talker.model.codec_embedding.weight"].astype(np.float32)
+    bos, eos, tpad = P([c["tts_bos_token_id"], c["tts_eos_token_id"], c["tts_pad_token_id"]])
+    np.testing.assert_array_equal(pad, tpad)
+    np.testing.assert_array_equal(rows[0:2], P(lead))
+    np.testing.assert_array_equal(rows[2:5], P(text[:3]))
+    for i, cid in enumerate(c["codec_prefix_ids"][:4]):
+        t = bos if i == 3 else tpad
+        np.testing.assert_array_equal(rows[5 + i], S.bf16_round(t + E[cid]))
+    np.testing.assert_array_equal(rows[9:13], S.bf16_round(P(text[3:7]) + E[2049]))
+    np.testing.assert_array_equal(rows[13], S.bf16_round(eos + E[2049]))
+    np.testing.assert_array_equal(rows[14], S.bf16_round(tpad + E[2048]))
+    short, _ = ot.session_seed(text[:8], SEED_CONTROLS)  # empty body, no leading ids
+    assert short.shape[0] == 3 + 4 + 0 + 2

@@ -1782,6 +1782,66 @@ extern "C" void q3t_session_free(q3t_session *s) {
 // (rounded to bf16), linear_fc2 + bias (rounded to bf16), 64 ids per pass on
 // the tensor-core GEMM.
 // ----------------------------------------------------------------------------
+// project_text_ids (session_seed.rs:668-679) of n validated ids in chunks of
+// 64 through the text-projection workspace (tp_mu held); rows go to `out`
+// with copy kind `kind` (device -> host or device -> device) on m->tp_st.
+static void text_project_rows(q3t_model *m, const int64_t *ids, int n, float *out, cudaMemcpyKind kind) {
+  const int Ht = m->text_hidden, H = m->tc.talker.hidden_size, TB = 64;
+  if (!m->tp_st) {
+    CK(cudaStreamCreateWithFlags(&m->tp_st, cudaStreamNonBlocking));
+    m->tp_x = m->arena.alloc<uint16_t>((size_t)TB * Ht);
+    m->tp_h = m->arena.alloc<uint16_t>((size_t)TB * Ht);
+    m->tp_out = m->arena.alloc<float>((size_t)TB * H);
+    m->tp_ids = m->arena.alloc<int>(TB);
+    m->tp_ntok = m->arena.alloc<int>(1);
+    m->tp_err = m->arena.zalloc<int>(1);
+    CK(cudaDeviceSynchronize());
+    if (!make_tmap_bf16(&m->tp_xmap, m->tp_x, Ht, TB, (uint64_t)Ht * 2, 64, TB) ||
+        !make_tmap_bf16(&m->tp_hmap, m->tp_h, Ht, TB, (uint64_t)Ht * 2, 64, TB))
+      FAIL(Q3T_CUDA_ERROR, "TMA descriptor encoding failed for the text projection workspace");
+  }
+  cudaStream_t st = m->tp_st;
+  std::vector<int> hid(TB);
+  for (int c0 = 0; c0 < n; c0 += TB) {
+    const int cnt = std::min(TB, n - c0);
+    for (int i = 0; i < cnt; i++) hid[i] = (int)ids[c0 + i];
+    CK(cudaMemcpyAsync(m->tp_ids, hid.data(), cnt * sizeof(int), cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(m->tp_ntok, &cnt, sizeof(int), cudaMemcpyHostToDevice, st));
+    gather_rows_bf16(m->text_emb, m->tp_ids, cnt, Ht, m->tp_x, st);
+    GemmArgs g1 = gemm_args(m->tp_fc1, m->tp_ntok, TB);
+    g1.xmode = GX_BF16;
+    g1.tx = m->tp_xmap;
+    g1.xb = m->tp_x;
+    g1.ldx = Ht;
+    g1.epi = GE_BIAS_SILU;
+    g1.h = m->tp_h;
+    g1.ldh = Ht;
+    g1.bias = m->tp_b1;
+    g1.err = m->tp_err;
+    gemm(g1, TB, st);
+    GemmArgs g2 = gemm_args(m->tp_fc2, m->tp_ntok, TB);
+    g2.xmode = GX_BF16;
+    g2.tx = m->tp_hmap;
+    g2.xb = m->tp_h;
+    g2.ldx = Ht;
+    g2.epi = GE_BIAS_BF16;
+    g2.y = m->tp_out;
+    g2.ldy = H;
+    g2.bias = m->tp_b2;
+    g2.err = m->tp_err;
+    gemm(g2, TB, st);
+    check_launches();
+    CK(cudaMemcpyAsync(out + (size_t)c0 * H, m->tp_out, (size_t)cnt * H * sizeof(float), kind, st));
+    CK(cudaStreamSynchronize(st));  // hid and the workspace are reused by the next pass
+  }
+  int e = 0;
+  CK(cudaMemcpy(&e, m->tp_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (e) {
+    CK(cudaMemset(m->tp_err, 0, sizeof(int)));
+    FAIL(Q3T_DEVICE_TIMEOUT, "text projection: a bounded device wait gave up (code %d)", e);
+  }
+}
+
 extern "C" q3t_status q3t_text_project(q3t_model *m, const int64_t *ids, int n, float *out) {
   if (!m || n < 0 || (n > 0 && (!ids || !out))) {
     set_error("q3t_text_project: bad argument");
@@ -1799,61 +1859,88 @@ extern "C" q3t_status q3t_text_project(q3t_model *m, const int64_t *ids, int n, 
   std::lock_guard<std::mutex> lock(m->tp_mu);
   return guard([&] {
     CK(cudaSetDevice(m->device));
-    const int Ht = m->text_hidden, H = m->tc.talker.hidden_size, TB = 64;
-    if (!m->tp_st) {
-      CK(cudaStreamCreateWithFlags(&m->tp_st, cudaStreamNonBlocking));
-      m->tp_x = m->arena.alloc<uint16_t>((size_t)TB * Ht);
-      m->tp_h = m->arena.alloc<uint16_t>((size_t)TB * Ht);
-      m->tp_out = m->arena.alloc<float>((size_t)TB * H);
-      m->tp_ids = m->arena.alloc<int>(TB);
-      m->tp_ntok = m->arena.alloc<int>(1);
-      m->tp_err = m->arena.zalloc<int>(1);
-      CK(cudaDeviceSynchronize());
-      if (!make_tmap_bf16(&m->tp_xmap, m->tp_x, Ht, TB, (uint64_t)Ht * 2, 64, TB) ||
-          !make_tmap_bf16(&m->tp_hmap, m->tp_h, Ht, TB, (uint64_t)Ht * 2, 64, TB))
-        FAIL(Q3T_CUDA_ERROR, "TMA descriptor encoding failed for the text projection workspace");
+    text_project_rows(m, ids, n, out, cudaMemcpyDeviceToHost);
+  });
+}
+
+extern "C" q3t_status q3t_session_seed(q3t_model *m, const int64_t *text_ids, int n_text, const int64_t *leading_ids,
+                                       int n_leading, const q3t_seed_controls *c, float *inputs_embeds, int max_rows,
+                                       int *rows, float *pad_embed) {
+  if (!m || !text_ids || !c || !rows || n_leading < 0 || (n_leading > 0 && !leading_ids) ||
+      (c->n_codec_prefix > 0 && !c->codec_prefix_ids)) {
+    set_error("q3t_session_seed: bad argument");
+    return Q3T_INVALID_INPUT;
+  }
+  if (!m->text_emb) {
+    set_error("q3t_session_seed: the model has no text_embedding / text_projection tensors");
+    return Q3T_INVALID_INPUT;
+  }
+  // text_ids = 3 role ids, the body, 5 trailing ids (session_seed.rs:159-160)
+  if (n_text < 8 || c->n_codec_prefix < 2) {
+    set_error("q3t_session_seed: %d text ids (>= 8: role 3 + body + 5) and %d codec prefix ids (>= 2)", n_text,
+              c->n_codec_prefix);
+    return Q3T_INVALID_INPUT;
+  }
+  const int H = m->tc.talker.hidden_size, V = m->tc.talker.vocab_size, ncp = c->n_codec_prefix;
+  const int body = n_text - 8, S = n_leading + 3 + (ncp - 1) + body + 2;
+  *rows = S;
+  if (!inputs_embeds) return Q3T_OK;
+  if (max_rows < S) {
+    set_error("q3t_session_seed: the seed has %d rows, the output holds %d", S, max_rows);
+    return Q3T_INVALID_INPUT;
+  }
+  // projected ids: [bos, eos, pad] + role (3) + body + leading
+  std::vector<int64_t> pid = {c->tts_bos_token_id, c->tts_eos_token_id, c->tts_pad_token_id};
+  for (int i = 0; i < 3 + body; i++) pid.push_back(text_ids[i]);
+  for (int i = 0; i < n_leading; i++) pid.push_back(leading_ids[i]);
+  for (int64_t id : pid)
+    if (id < 0 || id >= m->text_vocab) {
+      set_error("q3t_session_seed: text token id %lld outside [0, %d)", (long long)id, m->text_vocab);
+      return Q3T_INVALID_INPUT;
     }
+  std::vector<int64_t> cid(c->codec_prefix_ids, c->codec_prefix_ids + ncp - 1);
+  cid.push_back(c->codec_pad_id);
+  cid.push_back(c->codec_bos_id);
+  for (int64_t id : cid)
+    if (id < 0 || id >= V) {
+      set_error("q3t_session_seed: codec token id %lld outside [0, %d)", (long long)id, V);
+      return Q3T_INVALID_INPUT;
+    }
+  enum { BOS = 0, EOS = 1, PAD = 2, ROLE = 3, BODY = 6 };
+  const int LEAD = BODY + body;
+  std::vector<int> tr, ci;  // per output row: projected row, codec id (-1: none)
+  for (int i = 0; i < n_leading; i++) tr.push_back(LEAD + i), ci.push_back(-1);
+  for (int i = 0; i < 3; i++) tr.push_back(ROLE + i), ci.push_back(-1);
+  for (int i = 0; i < ncp - 1; i++) tr.push_back(i < ncp - 2 ? PAD : BOS), ci.push_back((int)c->codec_prefix_ids[i]);
+  for (int i = 0; i < body; i++) tr.push_back(BODY + i), ci.push_back((int)c->codec_pad_id);
+  tr.push_back(EOS), ci.push_back((int)c->codec_pad_id);
+  tr.push_back(PAD), ci.push_back((int)c->codec_bos_id);
+  std::lock_guard<std::mutex> lock(m->tp_mu);
+  return guard([&] {
+    CK(cudaSetDevice(m->device));
+    const int np = (int)pid.size();
+    float *P = nullptr, *out = nullptr;
+    int *d_tr = nullptr, *d_ci = nullptr;
+    CK(cudaMalloc(&P, (size_t)np * H * sizeof(float)));
+    CK(cudaMalloc(&out, (size_t)S * H * sizeof(float)));
+    CK(cudaMalloc(&d_tr, (size_t)S * 2 * sizeof(int)));
+    d_ci = d_tr + S;
+    struct Free {
+      void *p[3];
+      ~Free() {
+        for (void *q : p) cudaFree(q);
+      }
+    } fr{{P, out, d_tr}};
+    text_project_rows(m, pid.data(), np, P, cudaMemcpyDeviceToDevice);
     cudaStream_t st = m->tp_st;
-    std::vector<int> hid(TB);
-    for (int c0 = 0; c0 < n; c0 += TB) {
-      const int cnt = std::min(TB, n - c0);
-      for (int i = 0; i < cnt; i++) hid[i] = (int)ids[c0 + i];
-      CK(cudaMemcpyAsync(m->tp_ids, hid.data(), cnt * sizeof(int), cudaMemcpyHostToDevice, st));
-      CK(cudaMemcpyAsync(m->tp_ntok, &cnt, sizeof(int), cudaMemcpyHostToDevice, st));
-      gather_rows_bf16(m->text_emb, m->tp_ids, cnt, Ht, m->tp_x, st);
-      GemmArgs g1 = gemm_args(m->tp_fc1, m->tp_ntok, TB);
-      g1.xmode = GX_BF16;
-      g1.tx = m->tp_xmap;
-      g1.xb = m->tp_x;
-      g1.ldx = Ht;
-      g1.epi = GE_BIAS_SILU;
-      g1.h = m->tp_h;
-      g1.ldh = Ht;
-      g1.bias = m->tp_b1;
-      g1.err = m->tp_err;
-      gemm(g1, TB, st);
-      GemmArgs g2 = gemm_args(m->tp_fc2, m->tp_ntok, TB);
-      g2.xmode = GX_BF16;
-      g2.tx = m->tp_hmap;
-      g2.xb = m->tp_h;
-      g2.ldx = Ht;
-      g2.epi = GE_BIAS_BF16;
-      g2.y = m->tp_out;
-      g2.ldy = H;
-      g2.bias = m->tp_b2;
-      g2.err = m->tp_err;
-      gemm(g2, TB, st);
-      check_launches();
-      CK(cudaMemcpyAsync(out + (size_t)c0 * H, m->tp_out, (size_t)cnt * H * sizeof(float), cudaMemcpyDeviceToHost,
-                         st));
-      CK(cudaStreamSynchronize(st));  // hid and the workspace are reused by the next pass
-    }
-    int e = 0;
-    CK(cudaMemcpy(&e, m->tp_err, sizeof(int), cudaMemcpyDeviceToHost));
-    if (e) {
-      CK(cudaMemset(m->tp_err, 0, sizeof(int)));
-      FAIL(Q3T_DEVICE_TIMEOUT, "text projection: a bounded device wait gave up (code %d)", e);
-    }
+    CK(cudaMemcpyAsync(d_tr, tr.data(), S * sizeof(int), cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(d_ci, ci.data(), S * sizeof(int), cudaMemcpyHostToDevice, st));
+    seed_rows(P, m->talker_emb, d_tr, d_ci, S, H, out, st);
+    check_launches();
+    CK(cudaMemcpyAsync(inputs_embeds, out, (size_t)S * H * sizeof(float), cudaMemcpyDeviceToHost, st));
+    if (pad_embed)
+      CK(cudaMemcpyAsync(pad_embed, P + (size_t)PAD * H, H * sizeof(float), cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
   });
 }
 

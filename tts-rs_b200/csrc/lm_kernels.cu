@@ -635,6 +635,26 @@ void gather_rows_bf16(const uint16_t *table, const int *ids, int n, int width, u
   g_launches++;
 }
 
+// Prompt seed rows (session_seed.rs:151-215): out[s] = bf16(P[text_row[s]] +
+// codec_emb[codec_id[s]]), either term absent when its index is negative.
+__global__ void k_seed_rows(const float *P, const uint16_t *codec_emb, const int *text_row, const int *codec_id,
+                            int H, float *out) {
+  const int s = blockIdx.x, tr = text_row[s], ci = codec_id[s];
+  for (int h = threadIdx.x; h < H; h += blockDim.x) {
+    float v = tr >= 0 ? P[(size_t)tr * H + h] : 0.f;
+    if (ci >= 0) v += __uint_as_float((uint32_t)codec_emb[(size_t)ci * H + h] << 16);
+    out[(size_t)s * H + h] = __bfloat162float(__float2bfloat16_rn(v));
+  }
+}
+
+void seed_rows(const float *P, const uint16_t *codec_emb, const int *text_row, const int *codec_id, int S, int H,
+               float *out, cudaStream_t st) {
+  if (S <= 0) return;
+  k_seed_rows<<<S, 256, 0, st>>>(P, codec_emb, text_row, codec_id, H, out);
+  note(cudaGetLastError(), "k_seed_rows");
+  g_launches++;
+}
+
 __global__ void k_kv_import(const uint16_t *k, const uint16_t *v, int len, KVView kv, int seq) {
   const int l = blockIdx.z, h = blockIdx.y, j = blockIdx.x;
   const size_t src = (((size_t)l * kv.n_kv + h) * len + j) * 128;

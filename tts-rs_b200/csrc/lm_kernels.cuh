@@ -261,6 +261,9 @@ void run_phases(const Phase *phases, int n_phases, cudaStream_t st);
 
 // out[i] = table[ids[i]] (device ids, i < n): rows of `width` bf16.
 void gather_rows_bf16(const uint16_t *table, const int *ids, int n, int width, uint16_t *out, cudaStream_t st);
+// out[s] = bf16-rounded P[text_row[s]] + codec_emb[codec_id[s]] (negative index: term absent), S rows of H
+void seed_rows(const float *P, const uint16_t *codec_emb, const int *text_row, const int *codec_id, int S, int H,
+               float *out, cudaStream_t st);
 
 // Scatter dense bf16 K/V [layers][n_kv][len][hd] into the pages of `seq`.
 void kv_import(const uint16_t *k, const uint16_t *v, int layers, int len, KVView kv, int seq,

@@ -105,8 +105,15 @@ EXPORTS = [
     "q3t_batch_pending", "q3t_batch_stream", "q3t_batch_free", "q3t_last_error", "q3t_version",
     "q3t_kernel_launches", "q3t_text_project", "q3t_text_dims",
     "q3t_safetensors_open", "q3t_tensor_set_list", "q3t_tensor_set_free", "q3t_wav_write",
-    "q3t_codec_last_ms",
+    "q3t_codec_last_ms", "q3t_session_seed",
 ]
+
+
+class SeedControls(C.Structure):
+    """q3t_seed_controls: a profile's control ids (ProfileControlIds)."""
+    _fields_ = [("tts_bos_token_id", C.c_int64), ("tts_eos_token_id", C.c_int64),
+                ("tts_pad_token_id", C.c_int64), ("codec_prefix_ids", C.POINTER(C.c_int64)),
+                ("n_codec_prefix", C.c_int), ("codec_pad_id", C.c_int64), ("codec_bos_id", C.c_int64)]
 
 _F = C.POINTER(C.c_float)
 _I64 = C.POINTER(C.c_int64)
@@ -154,6 +161,8 @@ def lib():
         L.q3t_batch_free.restype = None
         L.q3t_text_project.argtypes = [C.c_void_p, _I64, C.c_int, _F]
         L.q3t_text_dims.argtypes = [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        L.q3t_session_seed.argtypes = [C.c_void_p, _I64, C.c_int, _I64, C.c_int, C.POINTER(SeedControls), _F,
+                                       C.c_int, C.POINTER(C.c_int), _F]
         L.q3t_safetensors_open.argtypes = [C.c_char_p, C.POINTER(C.c_void_p)]
         L.q3t_tensor_set_list.argtypes = [C.c_void_p, C.POINTER(C.POINTER(Tensor)), C.POINTER(C.c_int)]
         L.q3t_tensor_set_free.argtypes = [C.c_void_p]
@@ -317,6 +326,26 @@ class Model:
         out = np.zeros((len(ids), self.talker_cfg.talker.hidden), np.float32)
         check(lib().q3t_text_project(self.h, ids.ctypes.data_as(_I64) if len(ids) else None, len(ids), _fp(out)))
         return out
+
+    def session_seed(self, text_ids, controls, leading_ids=None):
+        """build_non_streaming_seed on the device: (inputs_embeds [rows][hidden],
+        tts_pad embedding [hidden]); controls: dict of q3t_seed_controls fields
+        with codec_prefix_ids as a sequence."""
+        text_ids = np.ascontiguousarray(text_ids, np.int64)
+        lead = None if leading_ids is None else np.ascontiguousarray(leading_ids, np.int64)
+        cp = np.ascontiguousarray(controls["codec_prefix_ids"], np.int64)
+        ctl = SeedControls(controls["tts_bos_token_id"], controls["tts_eos_token_id"], controls["tts_pad_token_id"],
+                           cp.ctypes.data_as(_I64), len(cp), controls["codec_pad_id"], controls["codec_bos_id"])
+        args = (self.h, text_ids.ctypes.data_as(_I64), len(text_ids),
+                None if lead is None else lead.ctypes.data_as(_I64), 0 if lead is None else len(lead),
+                C.byref(ctl))
+        rows = C.c_int()
+        check(lib().q3t_session_seed(*args, None, 0, C.byref(rows), None))
+        H = self.talker_cfg.talker.hidden
+        out = np.zeros((rows.value, H), np.float32)
+        pad = np.zeros(H, np.float32)
+        check(lib().q3t_session_seed(*args, _fp(out), rows.value, C.byref(rows), _fp(pad)))
+        return out, pad
 
     @staticmethod
     def codec_last_ms():
