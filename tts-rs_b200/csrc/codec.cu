@@ -49,23 +49,18 @@ Q3T_DEV void mma_f16(float *c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// sin^2(y) in f32 without a libm call.  sin^2 has period pi, so y is reduced
-// to r = y - k pi, k = rint(y / pi), with pi split into three floats
-// (Cody-Waite reduction: k * 3.140625 and k * PI_B are exact for |k| < 4096),
-// and sin r on [-pi/2, pi/2] is its Taylor series to r^11 (truncation below
-// 6e-8).  Max abs error of the square below 4e-7 for |y| <= 3000, far under
-// the fp16 step of the activations it produces.
+// sin^2(y) in f32.  sin^2 has period pi, so y is reduced to r = y - k pi,
+// k = rint(y / pi), with pi split into three floats (Cody-Waite reduction:
+// k * 3.140625 and k * PI_B are exact for |k| < 4096), and sin r on
+// [-pi/2, pi/2] is the __sinf intrinsic, whose documented absolute error on
+// [-pi, pi] is 2^-21.41.  Max abs error of the square below 1e-6 for
+// |y| <= 3000, far under the fp16 step of the activations it produces.
 Q3T_DEV float sin_sq(float y) {
   const float k = rintf(y * 0.318309886183790672f);
   float r = fmaf(-k, 3.140625f, y);
   r = fmaf(-k, 9.675025939941406e-4f, r);
   r = fmaf(-k, 1.5099580252808664e-7f, r);
-  const float r2 = r * r;
-  float p = fmaf(r2, -2.505210838544172e-8f, 2.755731922398589e-6f);  // -1/11!, 1/9!
-  p = fmaf(r2, p, -1.984126984126984e-4f);                             // -1/7!
-  p = fmaf(r2, p, 8.333333333333333e-3f);                              // 1/5!
-  p = fmaf(r2, p, -1.666666666666667e-1f);                             // -1/3!
-  const float sn = fmaf(r * r2, p, r);
+  const float sn = __sinf(r);
   return sn * sn;
 }
 
