@@ -549,16 +549,51 @@ __global__ void __launch_bounds__(256) k_conv_tc(const __grid_constant__ ConvTc 
   if (warp == 0) tmem_dealloc(tmem, kCols);
 }
 
-static int *g_conv_err = nullptr;  // device word for bounded-wait timeouts of k_conv_tc / k_conv_pt
+// Device words for bounded-wait timeouts of k_conv_tc / k_conv_pt, one per
+// device, created by codec_load (model load may allocate; the decode paths,
+// the static one included, only look the word up).
+constexpr int kConvErrDevices = 64;
+static int *g_conv_err_dev[kConvErrDevices] = {};
+static std::mutex g_conv_err_mu;
+
+static void conv_err_init() {
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kConvErrDevices) FAIL(Q3T_INVALID_INPUT, "device %d beyond %d", dev, kConvErrDevices);
+  std::lock_guard<std::mutex> lk(g_conv_err_mu);
+  if (!g_conv_err_dev[dev]) {
+    CK(cudaMalloc(&g_conv_err_dev[dev], sizeof(int)));
+    CK(cudaMemset(g_conv_err_dev[dev], 0, sizeof(int)));
+  }
+}
+
+// The current device's timeout word (null before a codec was loaded there).
+static int *conv_err_word() {
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  return dev >= 0 && dev < kConvErrDevices ? g_conv_err_dev[dev] : nullptr;
+}
+
+// True the first time it is called for the current device with this mask
+// (kernel attributes are per device).
+static bool first_on_device(uint64_t &mask) {
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if (mask & bit) return false;
+  mask |= bit;
+  return true;
+}
 
 // Raises Q3T_DEVICE_TIMEOUT if a convolution's bounded wait gave up since the
 // last check; the caller's stream is idle.
 static void conv_check_err() {
-  if (!g_conv_err) return;
+  int *w = conv_err_word();
+  if (!w) return;
   int e = 0;
-  CK(cudaMemcpy(&e, g_conv_err, sizeof e, cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(&e, w, sizeof e, cudaMemcpyDeviceToHost));
   if (e) {
-    CK(cudaMemset(g_conv_err, 0, sizeof e));
+    CK(cudaMemset(w, 0, sizeof e));
     FAIL(Q3T_DEVICE_TIMEOUT, "codec convolution: a bounded device wait gave up (code %#x)", e);
   }
 }
@@ -572,12 +607,10 @@ struct ConvFuse {
 template <int N, int ACH, int S, int FUSE>
 static void conv_tc_launch(const ConvArgs &a, int phases, cudaStream_t st, const ConvFuse *fu = nullptr) {
   using L = ConvTcSmem<N, ACH, S>;
-  static bool attr = false;
-  if (!attr) {
+  static uint64_t attr = 0;
+  if (first_on_device(attr))
     CK(cudaFuncSetAttribute(k_conv_tc<N, ACH, S, FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             (int)L::kBytes));
-    attr = true;
-  }
   ConvTc c;
   memset(&c, 0, sizeof c);
   const CUtensorMapSwizzle sw = ACH == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
@@ -610,7 +643,7 @@ static void conv_tc_launch(const ConvArgs &a, int phases, cudaStream_t st, const
   }
   c.a = a;
   c.tiles = (a.Lq + 127) / 128;
-  c.err = g_conv_err;
+  c.err = conv_err_word();
   const dim3 grid((unsigned)(a.B * c.tiles), a.Cout / N, phases);
   k_conv_tc<N, ACH, S, FUSE><<<grid, 256, L::kBytes, st>>>(c);
 }
@@ -913,12 +946,10 @@ static int g_sm_count = 0;
 template <int N, int ACH, int S, int FUSE>
 static void conv_pt_launch(const ConvArgs &a, int phases, cudaStream_t st, const ConvFuse *fu = nullptr) {
   using L = ConvPtSmem<N, ACH, S, FUSE>;
-  static bool attr = false;
-  if (!attr) {
+  static uint64_t attr = 0;
+  if (first_on_device(attr))
     CK(cudaFuncSetAttribute(k_conv_pt<N, ACH, S, FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             (int)L::kBytes));
-    attr = true;
-  }
   if (!g_sm_count) {
     int dev = 0;
     CK(cudaGetDevice(&dev));
@@ -961,7 +992,7 @@ static void conv_pt_launch(const ConvArgs &a, int phases, cudaStream_t st, const
   const int64_t total = (int64_t)a.B * c.tiles * c.nb * phases;
   if (total > INT32_MAX) FAIL(Q3T_INVALID_INPUT, "codec conv: %lld output tiles", (long long)total);
   c.total = (int)total;
-  c.err = g_conv_err;
+  c.err = conv_err_word();
   const int grid = (int)std::min<int64_t>(total, g_sm_count);
   k_conv_pt<N, ACH, S, FUSE><<<grid, kPtThreads, L::kBytes, st>>>(c);
 }
@@ -969,7 +1000,6 @@ static void conv_pt_launch(const ConvArgs &a, int phases, cudaStream_t st, const
 static void launch_conv(const ConvArgs &a, int phases, cudaStream_t st) {
   const int M = a.B * a.Lq;
   if (M <= 0) return;
-  if (!g_conv_err) CK(cudaMalloc(&g_conv_err, sizeof(int)));
   const bool tc = a.Cin % 32 == 0 && (a.Cout % 128 == 0 || a.Cout % 96 == 0) && !getenv("Q3T_CONV_MMA_SYNC");
   static const bool per_tile = getenv("Q3T_CONV_PER_TILE") != nullptr;  // one CTA per tile (k_conv_tc)
   if (tc && !per_tile) {
@@ -1016,7 +1046,6 @@ static bool fused_unit_ok(int C) { return C == 96 && !getenv("Q3T_CONV_MMA_SYNC"
 
 static void launch_unit(const ConvArgs &a, const ConvFuse &fu, cudaStream_t st) {
   if (a.B * a.Lq <= 0) return;
-  if (!g_conv_err) CK(cudaMalloc(&g_conv_err, sizeof(int)));
   if (getenv("Q3T_CONV_PER_TILE"))
     conv_tc_launch<96, 32, 6, 1>(a, 1, st, &fu);
   else
@@ -1656,12 +1685,12 @@ CodecModel *codec_load(q3t_model *m, const q3t_model_desc *d, cudaStream_t st) {
       c->out_w = to_dev(c->ar, wt, st);
       c->out_b = host(find(d, "decoder.decoder." + std::to_string(n + 2) + ".conv.bias", {1}))[0];
     }
-    static bool attrs = false;
-    if (!attrs) {
+    static uint64_t attrs = 0;
+    if (first_on_device(attrs)) {
       CK(cudaFuncSetAttribute(k_conv<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)conv_smem(128)));
       CK(cudaFuncSetAttribute(k_conv<96>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)conv_smem(96)));
-      attrs = true;
     }
+    conv_err_init();
   } catch (...) {
     delete c;
     throw;
@@ -2121,7 +2150,7 @@ void codec_stream_join(q3t_batch *b, int64_t *samples) {
     *S.h_err = 0;
     S.out.clear();
     S.inflight = false;
-    CK(cudaMemsetAsync(g_conv_err, 0, sizeof(int), S.cst));
+    if (int *w = conv_err_word()) CK(cudaMemsetAsync(w, 0, sizeof(int), S.cst));
     FAIL(Q3T_DEVICE_TIMEOUT, "streaming codec: a bounded device wait gave up (code %#x)", e);
   }
   for (const StreamOut &o : S.out) {
@@ -2246,7 +2275,7 @@ void codec_stream_step(q3t_model *m, q3t_batch *b, const std::vector<Req *> &act
     coff += (size_t)Bw * nq * Tw;
     woff += (size_t)Bw * std::max<int64_t>(nout, 1);
   }
-  if (g_conv_err) CK(cudaMemcpyAsync(S.h_err, g_conv_err, sizeof(int), cudaMemcpyDeviceToHost, S.cst));
+  if (int *w = conv_err_word()) CK(cudaMemcpyAsync(S.h_err, w, sizeof(int), cudaMemcpyDeviceToHost, S.cst));
   CK(cudaEventRecord(S.ev_done, S.cst));
   S.inflight = true;
   static const bool serial = getenv("Q3T_CODEC_SERIAL") != nullptr;  // no overlap (A/B measurements)
