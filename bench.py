@@ -21,6 +21,7 @@ import json
 import os
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -327,8 +328,8 @@ def main():
         b.step()
     stream = torch.cuda.ExternalStream(b.stream(), device=local)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = Clocks(local, os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out"))
-                                        else "/tmp", f"clocks_r{rank}.csv"))
+    # raw nvidia-smi samples of the timed region (the JSON line carries their summary)
+    clocks = Clocks(local, os.path.join(os.environ.get("Q3T_BENCH_OUT", tempfile.gettempdir()), f"clocks_r{rank}.csv"))
     launches0 = q3t.kernel_launches()
     barrier()
     if args.profile:
