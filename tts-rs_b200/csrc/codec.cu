@@ -2065,12 +2065,14 @@ static void codec_decode_static(q3t_model *m, const int64_t *codes, int B, int T
 // The windows of step n decode on a second, lowest-priority stream while the
 // (highest-priority) batch stream runs step n + 1's talker / predictor
 // kernels, which are latency bound and leave most of the GPU idle.  The
-// window codes are gathered on the batch stream (so a slot that a later step
-// reuses cannot change them), samples go to a pinned staging buffer, and the
-// next codec call joins the work: host wait, a device-side wait of the batch
-// stream, copies into the requests' sample vectors and the sample counts.
-// A step in which a request finishes joins at once, so a retired request's
-// output is complete.
+// window codes are gathered on the batch stream at the end of step n (so a
+// slot that a later step reuses cannot change them); the decode is launched
+// right after step n + 1's frame is enqueued, so the host issues those
+// launches while the frame runs; samples go to a pinned staging buffer, and
+// the codec call at the end of step n + 1 joins the work: host wait, a
+// device-side wait of the batch stream, copies into the requests' sample
+// vectors and the sample counts.  A step in which a request finishes
+// launches and joins at once, so a retired request's output is complete.
 // ---------------------------------------------------------------------------
 struct StreamOut {
   Req *r;
@@ -2086,6 +2088,18 @@ struct StreamState {
   cudaEvent_t ev_codes = nullptr, ev_done = nullptr;
   std::vector<StreamOut> out;      // emitted by the work in flight
   bool inflight = false;
+  struct PendWin {
+    Req *r;
+    int64_t s0, n, dst;             // samples [s0, s0 + n) of the window's decode, offset in r->wave
+  };
+  struct PendGroup {
+    int Tw, Bw;
+    int64_t nout;
+    int64_t *dc;
+    float *dw;
+    std::vector<PendWin> w;
+  };
+  std::vector<PendGroup> pend;     // gathered windows whose decode is not launched yet
   int *h_err = nullptr;            // pinned copy of the convolutions' timeout word, taken with the work
 };
 static std::map<q3t_batch *, StreamState> g_streams;
@@ -2139,7 +2153,37 @@ void codec_stream_init(q3t_model *m, q3t_batch *b) {
 
 // Completes the codec work in flight (see above); samples (nullable) counts
 // the samples it emitted.
+// Launches the decode of the windows gathered by the last codec_stream_step
+// on the codec stream (after their gather on the batch stream).
+void codec_stream_launch(q3t_batch *b) {
+  auto it = g_streams.find(b);
+  if (it == g_streams.end() || it->second.pend.empty()) return;
+  StreamState &S = it->second;
+  CodecModel *c = b->m->codec;
+  CK(cudaStreamWaitEvent(S.cst, S.ev_codes, 0));
+  size_t hoff = 0;
+  for (const auto &g : S.pend) {
+    if (g.nout > 0) decode_device(c, g.dc, g.Bw, g.Tw, g.dw, nullptr, S.cst);
+    for (int i = 0; i < (int)g.w.size(); i++) {
+      const auto &w = g.w[i];
+      if (w.n <= 0) continue;
+      if (b->desc.keep_output) {
+        CK(cudaMemcpyAsync(S.h_wave + hoff, g.dw + (size_t)i * g.nout + w.s0, w.n * 4, cudaMemcpyDeviceToHost,
+                           S.cst));
+        b->d2h += w.n * 4;
+      }
+      S.out.push_back(StreamOut{w.r, (int64_t)hoff, w.dst, w.n});
+      if (b->desc.keep_output) hoff += w.n;
+    }
+  }
+  S.pend.clear();
+  if (int *w = conv_err_word()) CK(cudaMemcpyAsync(S.h_err, w, sizeof(int), cudaMemcpyDeviceToHost, S.cst));
+  CK(cudaEventRecord(S.ev_done, S.cst));
+  S.inflight = true;
+}
+
 void codec_stream_join(q3t_batch *b, int64_t *samples) {
+  codec_stream_launch(b);
   auto it = g_streams.find(b);
   if (it == g_streams.end() || !it->second.inflight) return;
   StreamState &S = it->second;
@@ -2166,6 +2210,7 @@ void codec_stream_free(q3t_batch *b) {
   auto it = g_streams.find(b);
   if (it == g_streams.end()) return;
   StreamState &S = it->second;
+  S.pend.clear();  // gathered but never decoded: the batch is going away
   if (S.inflight) cudaEventSynchronize(S.ev_done);
   if (S.cst) cudaStreamSynchronize(S.cst);
   if (S.d_codes) cudaFree(S.d_codes);
@@ -2244,44 +2289,33 @@ void codec_stream_step(q3t_model *m, q3t_batch *b, const std::vector<Req *> &act
     need_wave += kv.second.size() * (size_t)std::max<int64_t>(nout, 1);
   }
   stream_capacity(S, need_codes, need_wave);  // nothing is in flight here
-  size_t coff = 0, woff = 0, hoff = 0;
+  size_t coff = 0, woff = 0;
   for (auto &kv : groups) {
     const int Tw = kv.first, Bw = (int)kv.second.size();
     int64_t nout = 0;
     codec_out_len(c, Tw, &nout);
-    int64_t *dc = S.d_codes + coff;
-    float *dw = S.d_wave + woff;
+    StreamState::PendGroup g{Tw, Bw, nout, S.d_codes + coff, S.d_wave + woff, {}};
     for (int i = 0; i < Bw; i++) {
       const Win &w = wins[kv.second[i]];
       k_window_codes<<<8, 256, 0, b->st>>>(b->d_hist_codes, b->maxF, b->G, nq, w.r->slot, w.f0, Tw,
-                                           dc + (size_t)i * nq * Tw);
+                                           g.dc + (size_t)i * nq * Tw);
       CK(cudaGetLastError());
       g_launches++;
+      g.w.push_back(StreamState::PendWin{w.r, w.s0, std::max<int64_t>(0, w.s1 - w.s0), w.dst});
     }
-    CK(cudaEventRecord(S.ev_codes, b->st));
-    CK(cudaStreamWaitEvent(S.cst, S.ev_codes, 0));
-    if (nout > 0) decode_device(c, dc, Bw, Tw, dw, nullptr, S.cst);
-    for (int i = 0; i < Bw; i++) {
-      const Win &w = wins[kv.second[i]];
-      if (w.s1 <= w.s0) continue;
-      const int64_t n = w.s1 - w.s0;
-      if (b->desc.keep_output) {
-        CK(cudaMemcpyAsync(S.h_wave + hoff, dw + (size_t)i * nout + w.s0, n * 4, cudaMemcpyDeviceToHost, S.cst));
-        b->d2h += n * 4;
-      }
-      S.out.push_back(StreamOut{w.r, (int64_t)hoff, w.dst, n});
-      if (b->desc.keep_output) hoff += n;
-    }
+    S.pend.push_back(std::move(g));
     coff += (size_t)Bw * nq * Tw;
     woff += (size_t)Bw * std::max<int64_t>(nout, 1);
   }
-  if (int *w = conv_err_word()) CK(cudaMemcpyAsync(S.h_err, w, sizeof(int), cudaMemcpyDeviceToHost, S.cst));
-  CK(cudaEventRecord(S.ev_done, S.cst));
-  S.inflight = true;
+  CK(cudaEventRecord(S.ev_codes, b->st));
+  // The decode is launched by the next step right after its frame is
+  // enqueued (codec_stream_launch), so these launches overlap that frame on
+  // the device instead of delaying it; a step in which a request finishes
+  // decodes and joins now.
   static const bool serial = getenv("Q3T_CODEC_SERIAL") != nullptr;  // no overlap (A/B measurements)
   bool join = serial;
   for (Req *r : act) join |= r->finished;  // retired after this call: its last samples must be in place
-  if (join) codec_stream_join(b, samples);
+  if (join) codec_stream_join(b, samples);  // launches, then waits
 }
 
 }  // namespace q3t

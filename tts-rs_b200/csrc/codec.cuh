@@ -17,6 +17,8 @@ void codec_stream_init(q3t_model *m, q3t_batch *b);
 void codec_stream_step(q3t_model *m, q3t_batch *b, const std::vector<Req *> &act, int64_t *samples);
 // completes the streaming codec work still in flight; samples (nullable) counts what it emitted
 void codec_stream_join(q3t_batch *b, int64_t *samples);
+// launches the decode of the windows the last codec_stream_step gathered (no-op if none)
+void codec_stream_launch(q3t_batch *b);
 void codec_stream_free(q3t_batch *b);
 
 }  // namespace q3t

@@ -1281,6 +1281,8 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
   const int mt = bucket_tok(B), ms = kAttnMaxUnits;
   b->h2d += b->meta_n * sizeof(int) + B * sizeof(float *);
   enqueue_frame(b, mt, ms);
+  // the previous step's codec windows decode on their own stream under this frame
+  if (b->desc.codec_mode == 2 && b->m->has_codec) codec_stream_launch(b);
   CK(cudaMemcpyAsync(b->h_eosflag, b->d_eosflag, B * sizeof(int), cudaMemcpyDeviceToHost, b->st));
   CK(cudaMemcpyAsync(b->h_err, b->d_err, sizeof(int), cudaMemcpyDeviceToHost, b->st));
   CK(cudaStreamSynchronize(b->st));
