@@ -946,3 +946,210 @@ void orc_to_pcm(const float *x, int64_t n, int16_t *out) {
     out[i] = (int16_t)v;
   }
 }
+
+/* ------------------------------------------------------------------------ */
+/* Codec encoder: codec/network/encoder.rs, init in codec/config.rs:136-346  */
+/* ------------------------------------------------------------------------ */
+/* Conv1d behind conv1d_padding + pad_1d (encoder.rs:155-161, conv.rs:33-83):
+ * left pad = effective kernel - stride, right pad = the extra that completes
+ * the last stride window; mode 0 = constant 0, 1 = edge.  x [ci][L] ->
+ * y [co][Lo]; returns Lo. */
+static int enc_conv(const orc_conv *c, const float *x, int L, int mode, float *y) {
+  int pt, ex;
+  orc_conv1d_padding(L, c->k, 1, c->stride, &pt, &ex);
+  const int Lp = L + pt + ex;
+  float *xp = (float *)malloc((size_t)c->ci * Lp * sizeof(float));
+  orc_pad_1d(x, c->ci, L, pt, ex, mode, xp);
+  const int Lo = (Lp - c->k) / c->stride + 1;
+#pragma omp parallel for schedule(static)
+  for (int o = 0; o < c->co; o++) {
+    float *yo = y + (size_t)o * Lo;
+    for (int t = 0; t < Lo; t++) yo[t] = c->b ? c->b[o] : 0.f;
+    for (int i = 0; i < c->ci; i++) {
+      const float *xi = xp + (size_t)i * Lp;
+      for (int j = 0; j < c->k; j++) {
+        const float wv = c->w[((size_t)o * c->ci + i) * c->k + j];
+        for (int t = 0; t < Lo; t++) yo[t] += wv * xi[t * c->stride + j];
+      }
+    }
+  }
+  free(xp);
+  return Lo;
+}
+
+/* output length of enc_conv for input length L */
+static int enc_conv_len(const orc_conv *c, int L) {
+  int pt, ex;
+  orc_conv1d_padding(L, c->k, 1, c->stride, &pt, &ex);
+  return (L + pt + ex - c->k) / c->stride + 1;
+}
+
+static void elu_inplace(float *x, int64_t n) { /* burn elu, alpha 1 (encoder.rs:163-167) */
+  for (int64_t i = 0; i < n; i++) x[i] = x[i] > 0.f ? x[i] : expf(x[i]) - 1.f;
+}
+
+/* burn LayerNorm with bias, biased variance */
+static void layer_norm(const float *x, const float *w, const float *b, int n, float eps, float *y) {
+  float mean = 0.f, var = 0.f;
+  for (int i = 0; i < n; i++) mean += x[i];
+  mean /= (float)n;
+  for (int i = 0; i < n; i++) var += (x[i] - mean) * (x[i] - mean);
+  var /= (float)n;
+  const float inv = 1.f / sqrtf(var + eps);
+  for (int i = 0; i < n; i++) y[i] = (x[i] - mean) * inv * w[i] + b[i];
+}
+
+/* one encoder transformer layer on h [T][H] (encoder.rs:202-288): causal
+ * (autoregressive mask) GQA attention with burn RotaryEncoding at offset 0,
+ * GELU MLP, LayerScale on both branches */
+static void enc_layer(const orc_codec_encoder *e, const orc_enc_layer *L, float *h, int T) {
+  const int H = e->hidden, nh = e->n_heads, nkv = e->n_kv, hd = e->head_dim;
+  const int qd = nh * hd, kd = nkv * hd, I = e->inter;
+  float *n = (float *)malloc((size_t)T * H * sizeof(float));
+  float *q = (float *)malloc((size_t)T * qd * sizeof(float));
+  float *k = (float *)malloc((size_t)T * kd * sizeof(float));
+  float *v = (float *)malloc((size_t)T * kd * sizeof(float));
+  for (int t = 0; t < T; t++) layer_norm(h + (size_t)t * H, L->ln1_w, L->ln1_b, H, e->norm_eps, n + (size_t)t * H);
+  linear_rows(L->wq, L->bq, n, T, H, qd, q, 0);
+  linear_rows(L->wk, L->bk, n, T, H, kd, k, 0);
+  linear_rows(L->wv, L->bv, n, T, H, kd, v, 0);
+  rope_pairs(q, T, nh, hd, e->theta);
+  rope_pairs(k, T, nkv, hd, e->theta);
+  const int rep = nh / nkv;
+  float *qh = (float *)malloc((size_t)nh * T * hd * sizeof(float));
+  float *ke = (float *)malloc((size_t)nh * T * hd * sizeof(float));
+  float *ve = (float *)malloc((size_t)nh * T * hd * sizeof(float));
+  for (int hh = 0; hh < nh; hh++)
+    for (int t = 0; t < T; t++) {
+      memcpy(qh + ((size_t)hh * T + t) * hd, q + (size_t)t * qd + hh * hd, hd * sizeof(float));
+      memcpy(ke + ((size_t)hh * T + t) * hd, k + (size_t)t * kd + (hh / rep) * hd, hd * sizeof(float));
+      memcpy(ve + ((size_t)hh * T + t) * hd, v + (size_t)t * kd + (hh / rep) * hd, hd * sizeof(float));
+    }
+  uint8_t *mask = (uint8_t *)malloc((size_t)T * T);
+  for (int s = 0; s < T; s++)
+    for (int j = 0; j < T; j++) mask[(size_t)s * T + j] = j > s; /* generate_autoregressive_mask */
+  float *ao = (float *)malloc((size_t)nh * T * hd * sizeof(float));
+  orc_sdpa(qh, ke, ve, mask, nh, T, T, hd, 1.0f / sqrtf((float)hd), ao);
+  float *ar = (float *)malloc((size_t)T * qd * sizeof(float));
+  for (int hh = 0; hh < nh; hh++)
+    for (int t = 0; t < T; t++)
+      memcpy(ar + (size_t)t * qd + hh * hd, ao + ((size_t)hh * T + t) * hd, hd * sizeof(float));
+  float *o = (float *)malloc((size_t)T * H * sizeof(float));
+  linear_rows(L->wo, L->bo, ar, T, qd, H, o, 0);
+  for (int64_t i = 0; i < (int64_t)T * H; i++) h[i] += o[i] * L->attn_scale[i % H];
+  for (int t = 0; t < T; t++) layer_norm(h + (size_t)t * H, L->ln2_w, L->ln2_b, H, e->norm_eps, n + (size_t)t * H);
+  float *f = (float *)malloc((size_t)T * I * sizeof(float));
+  linear_rows(L->fc1, NULL, n, T, H, I, f, 0);
+  for (int64_t i = 0; i < (int64_t)T * I; i++) f[i] = gelu_erf(f[i]);
+  linear_rows(L->fc2, NULL, f, T, I, H, o, 0);
+  for (int64_t i = 0; i < (int64_t)T * H; i++) h[i] += o[i] * L->mlp_scale[i % H];
+  free(n); free(q); free(k); free(v); free(qh); free(ke); free(ve); free(mask); free(ao); free(ar); free(o); free(f);
+}
+
+void orc_rvq_encode(const float *const *embed_sum, const float *const *usage, int n_layers, int codebook_size,
+                    int vq, float *x, int T, int64_t *codes) {
+  /* encoder.rs:319-368, codebook.rs:4-41: centroids = embed_sum /
+   * clamp_min(usage, 1e-6); id = argmin_j sum_d (x_d - c_jd)^2 (first index
+   * on ties); the residual loses the chosen centroid */
+  float *cent = (float *)malloc((size_t)codebook_size * vq * sizeof(float));
+  for (int l = 0; l < n_layers; l++) {
+    for (int j = 0; j < codebook_size; j++) {
+      const float u = usage[l][j] < 1e-6f ? 1e-6f : usage[l][j];
+      for (int d = 0; d < vq; d++) cent[(size_t)j * vq + d] = embed_sum[l][(size_t)j * vq + d] / u;
+    }
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < T; t++) {
+      int best = 0;
+      float bd = INFINITY;
+      for (int j = 0; j < codebook_size; j++) {
+        float s = 0.f;
+        for (int d = 0; d < vq; d++) {
+          const float df = x[(size_t)d * T + t] - cent[(size_t)j * vq + d];
+          s += df * df;
+        }
+        if (s < bd) {
+          bd = s;
+          best = j;
+        }
+      }
+      codes[(size_t)l * T + t] = best;
+      for (int d = 0; d < vq; d++) x[(size_t)d * T + t] -= cent[(size_t)best * vq + d];
+    }
+  }
+  free(cent);
+}
+
+int orc_codec_encode(const orc_codec_encoder *e, const float *wave, int n, int n_valid, int64_t *codes,
+                     int max_frames) {
+  if (!e || !wave || n <= 0 || e->semantic.n_layers <= 0 || n_valid < e->semantic.n_layers) return -1;
+  /* backbone (encoder.rs:138-175; layers as config.rs:174-236 builds them) */
+  int L = n, C = 1;
+  float *x = (float *)malloc((size_t)n * sizeof(float));
+  memcpy(x, wave, (size_t)n * sizeof(float));
+  {
+    const int Lo = enc_conv_len(&e->in_conv, L);
+    float *y = (float *)malloc((size_t)e->in_conv.co * Lo * sizeof(float));
+    enc_conv(&e->in_conv, x, L, 0, y);
+    free(x); x = y; L = Lo; C = e->in_conv.co;
+  }
+  for (int s = 0; s < e->n_stages; s++) {
+    /* resnet: x + conv_out(elu(conv_in(elu(x)))) */
+    float *h = (float *)malloc((size_t)C * L * sizeof(float));
+    memcpy(h, x, (size_t)C * L * sizeof(float));
+    elu_inplace(h, (int64_t)C * L);
+    float *m = (float *)malloc((size_t)e->res_in[s].co * L * sizeof(float));
+    enc_conv(&e->res_in[s], h, L, 0, m);
+    elu_inplace(m, (int64_t)e->res_in[s].co * L);
+    enc_conv(&e->res_out[s], m, L, 0, h);
+    for (int64_t i = 0; i < (int64_t)C * L; i++) x[i] += h[i];
+    free(m); free(h);
+    elu_inplace(x, (int64_t)C * L);
+    const int Lo = enc_conv_len(&e->down[s], L);
+    float *y = (float *)malloc((size_t)e->down[s].co * Lo * sizeof(float));
+    enc_conv(&e->down[s], x, L, 0, y);
+    free(x); x = y; L = Lo; C = e->down[s].co;
+  }
+  elu_inplace(x, (int64_t)C * L);
+  {
+    const int Lo = enc_conv_len(&e->out_conv, L);
+    float *y = (float *)malloc((size_t)e->out_conv.co * Lo * sizeof(float));
+    enc_conv(&e->out_conv, x, L, 0, y);
+    free(x); x = y; L = Lo; C = e->out_conv.co;
+  }
+  /* transformer on [T][H] (encoder.rs:179-200) */
+  const int H = e->hidden;
+  if (C != H) { free(x); return -1; }
+  float *h = (float *)malloc((size_t)L * H * sizeof(float));
+  transpose(x, H, L, h);
+  for (int l = 0; l < e->n_layers; l++) enc_layer(e, &e->layers[l], h, L);
+  transpose(h, L, H, x);
+  free(h);
+  /* downsample: stride 2, edge padding (config.rs:155-166) */
+  const int T = enc_conv_len(&e->downsample, L);
+  float *z = (float *)malloc((size_t)H * T * sizeof(float));
+  enc_conv(&e->downsample, x, L, 1, z);
+  free(x);
+  if (T > max_frames || T <= 0) { free(z); return -1; }
+  /* quantizers on the same hidden (encoder.rs:290-317) */
+  const int vq = e->vq_dim;
+  const orc_enc_rvq *q[2] = {&e->semantic, &e->acoustic};
+  int want[2] = {e->semantic.n_layers, n_valid - e->semantic.n_layers};
+  if (want[1] > e->acoustic.n_layers) want[1] = e->acoustic.n_layers;
+  int row = 0;
+  for (int g = 0; g < 2; g++) {
+    if (want[g] <= 0) continue;
+    float *r = (float *)malloc((size_t)vq * T * sizeof(float)); /* input_proj, Conv1d k1 without bias */
+#pragma omp parallel for schedule(static)
+    for (int d = 0; d < vq; d++)
+      for (int t = 0; t < T; t++) {
+        float s = 0.f;
+        for (int c = 0; c < H; c++) s += q[g]->in_proj[(size_t)d * H + c] * z[(size_t)c * T + t];
+        r[(size_t)d * T + t] = s;
+      }
+    orc_rvq_encode(q[g]->embed_sum, q[g]->usage, want[g], e->codebook_size, vq, r, T, codes + (size_t)row * T);
+    row += want[g];
+    free(r);
+  }
+  free(z);
+  return T;
+}

@@ -226,6 +226,54 @@ void orc_sdpa(const float *q, const float *k, const float *v,
               const uint8_t *mask, int H, int S, int L, int D, float scale,
               float *out);
 
+/* ------------------------------------------------------------------------ */
+/* Codec encoder (voice-clone reference audio): codec/network/encoder.rs,    */
+/* codec/config.rs:136-346                                                   */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+  const float *w, *b; /* Conv1d weight [co][ci][k], bias [co] (nullable) */
+  int ci, co, k, stride;
+} orc_conv;
+
+typedef struct {
+  const float *ln1_w, *ln1_b, *ln2_w, *ln2_b;               /* [H] */
+  const float *wq, *bq, *wk, *bk, *wv, *bv, *wo, *bo;       /* [out][in], biases nullable */
+  const float *attn_scale, *mlp_scale;                      /* LayerScale [H] */
+  const float *fc1, *fc2;                                   /* [inter][H], [H][inter] */
+} orc_enc_layer;
+
+typedef struct {
+  const float *in_proj;             /* Conv1d k1 [vq][H][1], no bias */
+  const float *const *embed_sum;    /* n_layers x [codebook_size][vq] */
+  const float *const *usage;        /* n_layers x [codebook_size] */
+  int n_layers;
+} orc_enc_rvq;
+
+typedef struct {
+  int hidden, n_layers, n_heads, n_kv, head_dim, inter, codebook_size, vq_dim;
+  float norm_eps, theta;
+  int n_stages;
+  orc_conv in_conv;                 /* audio -> num_filters, constant pad */
+  orc_conv res_in[8], res_out[8];   /* per stage: resnet k_res (C -> C/compress) and k1 back */
+  orc_conv down[8];                 /* per stage: C -> 2C, kernel 2r, stride r */
+  orc_conv out_conv;                /* -> hidden, last_kernel_size */
+  const orc_enc_layer *layers;
+  orc_conv downsample;              /* hidden -> hidden, stride 2, edge pad, no bias */
+  orc_enc_rvq semantic, acoustic;
+} orc_codec_encoder;
+
+/* Qwen3TtsAudioCodecEncoder::encode_reference_prefix (encoder.rs:121-136):
+ * wave [n] (one channel) -> codes [n_valid][T] (semantic layers first, then
+ * n_valid - n_semantic acoustic ones).  Returns T, or < 0 on bad input or
+ * when the codes would not fit max_frames. */
+int orc_codec_encode(const orc_codec_encoder *e, const float *wave, int n, int n_valid, int64_t *codes,
+                     int max_frames);
+/* one residual vector quantizer's encode (encoder.rs:319-368) on x [vq][T]
+ * (already through input_proj): codes [n_layers][T]; x is left holding the
+ * final residual */
+void orc_rvq_encode(const float *const *embed_sum, const float *const *usage, int n_layers, int codebook_size,
+                    int vq, float *x, int T, int64_t *codes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -85,6 +85,28 @@ class Codec(C.Structure):
                 ("out_conv_w", F), ("out_conv_b", F)]
 
 
+class Conv(C.Structure):
+    _fields_ = [("w", F), ("b", F), ("ci", C.c_int), ("co", C.c_int), ("k", C.c_int), ("stride", C.c_int)]
+
+
+class EncLayer(C.Structure):
+    _fields_ = [(n, F) for n in ("ln1_w", "ln1_b", "ln2_w", "ln2_b", "wq", "bq", "wk", "bk", "wv", "bv",
+                                 "wo", "bo", "attn_scale", "mlp_scale", "fc1", "fc2")]
+
+
+class EncRvq(C.Structure):
+    _fields_ = [("in_proj", F), ("embed_sum", C.POINTER(F)), ("usage", C.POINTER(F)), ("n_layers", C.c_int)]
+
+
+class CodecEncoder(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("hidden", "n_layers", "n_heads", "n_kv", "head_dim", "inter",
+                                       "codebook_size", "vq_dim")] + \
+               [("norm_eps", C.c_float), ("theta", C.c_float), ("n_stages", C.c_int), ("in_conv", Conv),
+                ("res_in", Conv * 8), ("res_out", Conv * 8), ("down", Conv * 8), ("out_conv", Conv),
+                ("layers", C.POINTER(EncLayer)), ("downsample", Conv), ("semantic", EncRvq),
+                ("acoustic", EncRvq)]
+
+
 def lib():
     """Load liboracle.so, building it with make if it is missing."""
     global _LIB
@@ -126,6 +148,8 @@ def lib():
         L.orc_conv1d_padding.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int,
                                          C.POINTER(C.c_int), C.POINTER(C.c_int)]
         L.orc_to_pcm.argtypes = [F, C.c_int64, C.POINTER(C.c_int16)]
+        L.orc_codec_encode.argtypes = [C.POINTER(CodecEncoder), F, C.c_int, C.c_int, I64, C.c_int]
+        L.orc_rvq_encode.argtypes = [C.POINTER(F), C.POINTER(F), C.c_int, C.c_int, C.c_int, F, C.c_int, I64]
         L.orc_sdpa.argtypes = [F, F, F, C.POINTER(C.c_uint8), C.c_int, C.c_int, C.c_int,
                                C.c_int, C.c_float, F]
         L.orc_set_threads.argtypes = [C.c_int]
@@ -415,3 +439,92 @@ class OracleCodec:
         out = np.zeros(n, np.float32)
         lib().orc_codec_decode_tap(C.byref(self.s), ip(codes), T, tap, fp(out))
         return out
+
+
+class OracleCodecEncoder:
+    """Speech-tokenizer encoder of the voice-clone path
+    (Qwen3TtsAudioCodecEncoder::encode_reference_prefix, codec/network/
+    encoder.rs:121-136): 24 kHz samples -> codes [n_valid][frames].  Weights
+    are named by the reference's module paths (synthetic.codec_encoder_tensor_specs)."""
+
+    def __init__(self, cfg, weights: dict):
+        self.cfg = cfg
+        w = {k: f32(v) for k, v in weights.items()}
+        self.w = w
+        self._keep = []
+        e = CodecEncoder()
+        for n in ("hidden", "n_layers", "n_heads", "n_kv", "head_dim", "inter", "codebook_size", "vq_dim"):
+            setattr(e, n, getattr(cfg, n))
+        e.norm_eps, e.theta = cfg.norm_eps, cfg.theta
+        e.n_stages = len(cfg.upsampling_ratios)
+        if e.n_stages > 8:
+            raise ValueError("at most 8 encoder stages")
+        p = "encoder.encoder.layers"
+
+        def conv(name, ci, co, k, stride, bias=True):
+            wt = w[f"{name}.weight"]
+            assert wt.shape == (co, ci, k), (name, wt.shape)
+            return Conv(fp(wt), fp(w[f"{name}.bias"]) if bias else None, ci, co, k, stride)
+
+        e.in_conv = conv(f"{p}.0.conv", cfg.audio_channels, cfg.num_filters, cfg.kernel_size, 1)
+        li, scale = 1, 1
+        for s_, r in enumerate(reversed(cfg.upsampling_ratios)):
+            Cc = scale * cfg.num_filters
+            e.res_in[s_] = conv(f"{p}.{li}.conv_in.conv", Cc, Cc // cfg.compress, cfg.residual_kernel_size, 1)
+            e.res_out[s_] = conv(f"{p}.{li}.conv_out.conv", Cc // cfg.compress, Cc, 1, 1)
+            e.down[s_] = conv(f"{p}.{li + 2}.conv", Cc, 2 * Cc, 2 * r, r)
+            li += 3
+            scale *= 2
+        e.out_conv = conv(f"{p}.{li + 1}.conv", scale * cfg.num_filters, cfg.hidden, cfg.last_kernel_size, 1)
+        layers = (EncLayer * cfg.n_layers)()
+        for l in range(cfg.n_layers):
+            q = f"encoder.encoder_transformer.layers.{l}"
+            g = lambda n: fp(w[f"{q}.{n}"]) if f"{q}.{n}" in w else None
+            layers[l] = EncLayer(g("input_layernorm.weight"), g("input_layernorm.bias"),
+                                 g("post_attention_layernorm.weight"), g("post_attention_layernorm.bias"),
+                                 g("self_attn.q_proj.weight"), g("self_attn.q_proj.bias"),
+                                 g("self_attn.k_proj.weight"), g("self_attn.k_proj.bias"),
+                                 g("self_attn.v_proj.weight"), g("self_attn.v_proj.bias"),
+                                 g("self_attn.o_proj.weight"), g("self_attn.o_proj.bias"),
+                                 g("self_attn_layer_scale.scale"), g("mlp_layer_scale.scale"),
+                                 g("mlp.fc1.weight"), g("mlp.fc2.weight"))
+        self._keep.append(layers)
+        e.layers = C.cast(layers, C.POINTER(EncLayer))
+        e.downsample = conv("encoder.downsample.conv", cfg.hidden, cfg.hidden, 2 * cfg.downsample_factor, 2,
+                            bias=False)
+        for grp, n in (("semantic", cfg.n_semantic), ("acoustic", cfg.n_q - cfg.n_semantic)):
+            q = f"encoder.quantizer.{grp}_residual_vector_quantizer"
+            es = (F * max(n, 1))(*[fp(w[f"{q}.layers.{j}.codebook.embed_sum"]) for j in range(n)])
+            us = (F * max(n, 1))(*[fp(w[f"{q}.layers.{j}.codebook.cluster_usage"]) for j in range(n)])
+            self._keep += [es, us]
+            setattr(e, grp, EncRvq(fp(w[f"{q}.input_proj.weight"]), C.cast(es, C.POINTER(F)),
+                                   C.cast(us, C.POINTER(F)), n))
+        self.e = e
+
+    def encode(self, wave, n_valid=None):
+        """wave [n] f32 -> codes [n_valid][frames] (n_valid defaults to all codebooks)."""
+        wave = np.ascontiguousarray(wave, np.float32)
+        n_valid = self.cfg.n_q if n_valid is None else n_valid
+        T = self.cfg.frames(len(wave))
+        codes = np.zeros((n_valid, T), np.int64)
+        got = lib().orc_codec_encode(C.byref(self.e), fp(wave), len(wave), n_valid,
+                                     codes.ctypes.data_as(I64), T)
+        if got < 0:
+            raise ValueError("bad encoder input")
+        assert got == T, (got, T)
+        return codes
+
+
+def rvq_encode(embed_sum, usage, x):
+    """One residual vector quantizer's encode (encoder.rs:319-368) of x
+    [vq][T]: (codes [n_layers][T], final residual [vq][T])."""
+    x = np.array(x, np.float32, order="C", copy=True)
+    es = [f32(a) for a in embed_sum]
+    us = [f32(a) for a in usage]
+    n, (cb, vq), T = len(es), es[0].shape, x.shape[1]
+    pe = (F * n)(*[fp(a) for a in es])
+    pu = (F * n)(*[fp(a) for a in us])
+    codes = np.zeros((n, T), np.int64)
+    lib().orc_rvq_encode(C.cast(pe, C.POINTER(F)), C.cast(pu, C.POINTER(F)), n, cb, vq, fp(x), T,
+                         codes.ctypes.data_as(I64))
+    return codes, x

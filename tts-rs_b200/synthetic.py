@@ -17,7 +17,7 @@ from __future__ import annotations
 
 import os
 import zlib
-from dataclasses import dataclass, field, asdict
+from dataclasses import dataclass, field, asdict, replace
 
 import numpy as np
 
@@ -288,6 +288,134 @@ def make_codec_weights(cfg: CodecConfig, seed: int = 0) -> dict:
             raise ValueError(kind)
         return name, np.ascontiguousarray(a, dtype=np.float32)
     return _parallel(one, codec_tensor_specs(cfg))
+
+
+@dataclass
+class CodecEncoderConfig:
+    """Speech-tokenizer encoder of the voice-clone path
+    (codec/config.rs:79-121, built by config.rs:136-346).  The tokenizer's
+    config.json is not available, so these dims are the Mimi-style shape the
+    12 Hz tokenizer is published with: 64 filters, ratios [8, 6, 5, 4]
+    (960 samples per 25 Hz step, then a stride-2 downsample to 12.5 Hz),
+    hidden 512, 8 transformer layers of 8 x 64 heads, MLP 2048, 32 codebooks
+    (1 semantic) of 2048 x 256."""
+    audio_channels: int = 1
+    num_filters: int = 64
+    kernel_size: int = 7
+    residual_kernel_size: int = 3
+    last_kernel_size: int = 3
+    compress: int = 2
+    upsampling_ratios: tuple = (8, 6, 5, 4)
+    hidden: int = 512
+    n_layers: int = 8
+    n_heads: int = 8
+    n_kv: int = 8
+    head_dim: int = 64
+    inter: int = 2048
+    norm_eps: float = 1e-5
+    theta: float = 1e4
+    layer_scale: float = 0.01
+    attention_bias: bool = False
+    codebook_size: int = 2048
+    vq_dim: int = 256
+    n_q: int = 32
+    n_semantic: int = 1
+    downsample_factor: int = 2  # round(sampling_rate * encode_downsample_rate / (prod(ratios) * input_rate))
+
+    def small(self, **kw):
+        """A reduced encoder for fast CPU tests (same structure)."""
+        d = dict(num_filters=16, upsampling_ratios=(4, 3), hidden=64, n_layers=2, n_heads=4, n_kv=2,
+                 head_dim=16, inter=128, codebook_size=64, vq_dim=32, n_q=4, n_semantic=1)
+        d.update(kw)
+        return replace(self, **d)
+
+    def frames(self, n: int) -> int:
+        """Codec frames the encoder emits for n samples (conv.rs:44-64 lengths)."""
+        def conv_len(L, k, stride):
+            pt = max(k - stride, 0)
+            padded = L + pt
+            missing = max(k - padded, 0)
+            extra = missing if missing > 0 else (stride - (padded - k) % stride) % stride
+            return (padded + extra - k) // stride + 1
+        L = conv_len(n, self.kernel_size, 1)
+        for r in reversed(self.upsampling_ratios):
+            L = conv_len(L, 2 * r, r)
+        L = conv_len(L, self.last_kernel_size, 1)
+        return conv_len(L, 2 * self.downsample_factor, 2)
+
+
+def codec_encoder_tensor_specs(c: CodecEncoderConfig):
+    """(name, shape, init) of the encoder tensors, named by the reference's
+    module paths (encoder.rs:20-110)."""
+    s = []
+    p = "encoder.encoder.layers"
+    s.append((f"{p}.0.conv.weight", (c.num_filters, c.audio_channels, c.kernel_size),
+              ("fan", c.audio_channels * c.kernel_size, 1.0)))
+    s.append((f"{p}.0.conv.bias", (c.num_filters,), ("normal", 0.02)))
+    li, scale = 1, 1
+    for r in reversed(c.upsampling_ratios):
+        C = scale * c.num_filters
+        hid = C // c.compress
+        s += [(f"{p}.{li}.conv_in.conv.weight", (hid, C, c.residual_kernel_size),
+               ("fan", C * c.residual_kernel_size, 1.0)),
+              (f"{p}.{li}.conv_in.conv.bias", (hid,), ("normal", 0.02)),
+              (f"{p}.{li}.conv_out.conv.weight", (C, hid, 1), ("fan", hid, 0.5)),
+              (f"{p}.{li}.conv_out.conv.bias", (C,), ("normal", 0.02))]
+        s += [(f"{p}.{li + 2}.conv.weight", (2 * C, C, 2 * r), ("fan", C * 2 * r, 1.0)),
+              (f"{p}.{li + 2}.conv.bias", (2 * C,), ("normal", 0.02))]
+        li += 3  # resnet, activation, downsample conv
+        scale *= 2
+    li += 1  # final activation
+    s += [(f"{p}.{li}.conv.weight", (c.hidden, scale * c.num_filters, c.last_kernel_size),
+           ("fan", scale * c.num_filters * c.last_kernel_size, 1.0)),
+          (f"{p}.{li}.conv.bias", (c.hidden,), ("normal", 0.02))]
+    H, qd, kd = c.hidden, c.n_heads * c.head_dim, c.n_kv * c.head_dim
+    for l in range(c.n_layers):
+        q = f"encoder.encoder_transformer.layers.{l}"
+        s += [(f"{q}.input_layernorm.weight", (H,), ("gamma",)), (f"{q}.input_layernorm.bias", (H,), ("normal", 0.02)),
+              (f"{q}.post_attention_layernorm.weight", (H,), ("gamma",)),
+              (f"{q}.post_attention_layernorm.bias", (H,), ("normal", 0.02)),
+              (f"{q}.self_attn.q_proj.weight", (qd, H), ("fan", H, 1.0)),
+              (f"{q}.self_attn.k_proj.weight", (kd, H), ("fan", H, 1.0)),
+              (f"{q}.self_attn.v_proj.weight", (kd, H), ("fan", H, 1.0)),
+              (f"{q}.self_attn.o_proj.weight", (H, qd), ("fan", qd, 1.0)),
+              (f"{q}.self_attn_layer_scale.scale", (H,), ("normal", 0.02, c.layer_scale * 10)),
+              (f"{q}.mlp_layer_scale.scale", (H,), ("normal", 0.02, c.layer_scale * 10)),
+              (f"{q}.mlp.fc1.weight", (c.inter, H), ("fan", H, 1.0)),
+              (f"{q}.mlp.fc2.weight", (H, c.inter), ("fan", c.inter, 1.0))]
+        if c.attention_bias:
+            s += [(f"{q}.self_attn.{n}_proj.bias", (qd if n == "q" else (H if n == "o" else kd),), ("normal", 0.02))
+                  for n in ("q", "k", "v", "o")]
+    s.append(("encoder.downsample.conv.weight", (H, H, 2 * c.downsample_factor),
+              ("fan", H * 2 * c.downsample_factor, 1.0)))
+    for grp, n in (("semantic", c.n_semantic), ("acoustic", c.n_q - c.n_semantic)):
+        q = f"encoder.quantizer.{grp}_residual_vector_quantizer"
+        s.append((f"{q}.input_proj.weight", (c.vq_dim, H, 1), ("fan", H, 1.0)))
+        for j in range(n):
+            s += [(f"{q}.layers.{j}.codebook.embed_sum", (c.codebook_size, c.vq_dim), ("normal", 1.0)),
+                  (f"{q}.layers.{j}.codebook.cluster_usage", (c.codebook_size,), ("usage",))]
+    return s
+
+
+def make_codec_encoder_weights(cfg: CodecEncoderConfig, seed: int = 0) -> dict:
+    """Seeded encoder weights (f32), initialised like make_codec_weights
+    (convs / linears ~N(0, gain^2 / fan_in), LayerNorm gains ~N(1, 0.1),
+    codebooks ~N(0, 1) with usage in [0.5, 2))."""
+    def one(spec):
+        name, shape, init = spec
+        kind = init[0]
+        if kind == "normal":
+            a = _normal(seed, name, shape, init[1], init[2] if len(init) > 2 else 0.0)
+        elif kind == "fan":
+            a = _normal(seed, name, shape, init[2] / np.sqrt(init[1]))
+        elif kind == "gamma":
+            a = _normal(seed, name, shape, 0.1, 1.0)
+        elif kind == "usage":
+            a = _rng(seed, name).uniform(0.5, 2.0, shape).astype(np.float32)
+        else:
+            raise ValueError(kind)
+        return name, np.ascontiguousarray(a, dtype=np.float32)
+    return _parallel(one, codec_encoder_tensor_specs(cfg))
 
 
 def synthetic_talker_inputs(cfg: TalkerConfig, S: int, seed: int = 0):
