@@ -1153,3 +1153,255 @@ int orc_codec_encode(const orc_codec_encoder *e, const float *wave, int n, int n
   free(z);
   return T;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Speaker encoder: model/speaker/infer/feature.rs, model/speaker/network    */
+/* ------------------------------------------------------------------------ */
+/* in-place iterative radix-2 DFT (the transform rustfft computes; forward,
+ * unnormalised), n a power of two */
+static void fft_pow2(double *re, double *im, int n) {
+  for (int i = 1, j = 0; i < n; i++) {
+    int bit = n >> 1;
+    for (; j & bit; bit >>= 1) j ^= bit;
+    j ^= bit;
+    if (i < j) {
+      double t = re[i]; re[i] = re[j]; re[j] = t;
+      t = im[i]; im[i] = im[j]; im[j] = t;
+    }
+  }
+  for (int len = 2; len <= n; len <<= 1) {
+    const double ang = -2.0 * M_PI / len;
+    for (int i = 0; i < n; i += len)
+      for (int k = 0; k < len / 2; k++) {
+        const double wr = cos(ang * k), wi = sin(ang * k);
+        const double ur = re[i + k], ui = im[i + k];
+        const double vr = re[i + k + len / 2] * wr - im[i + k + len / 2] * wi;
+        const double vi = re[i + k + len / 2] * wi + im[i + k + len / 2] * wr;
+        re[i + k] = ur + vr; im[i + k] = ui + vi;
+        re[i + k + len / 2] = ur - vr; im[i + k + len / 2] = ui - vi;
+      }
+  }
+}
+
+static float hz_to_mel(float hz) { return 2595.0f * log10f(1.0f + hz / 700.0f); }
+static float mel_to_hz(float m) { return 700.0f * (powf(10.0f, m / 2595.0f) - 1.0f); }
+
+int orc_speaker_mel(const float *x, int n, int sr, int n_mels, float *out, int max_frames) {
+  /* feature.rs:32-150 (n_fft 1024, hop 256, win 1024, fmin 0, fmax sr / 2) */
+  const int n_fft = 1024, hop = 256, pad = (n_fft - hop) / 2, nf = n_fft / 2 + 1;
+  if (!x || n < n_fft - 2 * pad || n_mels <= 0) return -1;
+  const int plen = n + 2 * pad, frames = (plen - n_fft) / hop + 1;
+  if (frames > max_frames) return -1;
+  float *p = (float *)malloc((size_t)plen * sizeof(float));
+  for (int i = 0; i < pad; i++) { /* left: samples[pad], ..., samples[1] (feature.rs:100-102) */
+    int idx = pad - i;
+    p[i] = x[idx < n - 1 ? idx : n - 1];
+  }
+  memcpy(p + pad, x, (size_t)n * sizeof(float));
+  for (int i = 0; i < pad; i++) { /* right: samples[n - 2 - i], saturating (feature.rs:104-109) */
+    int idx = n - 2 - i;
+    if (idx < 0) idx = 0;
+    if (idx > n - 1) idx = n - 1;
+    p[pad + n + i] = x[idx];
+  }
+  float win[1024];
+  for (int i = 0; i < n_fft; i++) { /* periodic Hann (feature.rs:135-142), f32 */
+    const float ph = 2.0f * (float)M_PI * (float)i / (float)n_fft;
+    win[i] = 0.5f - 0.5f * cosf(ph);
+  }
+  /* mel filterbank (feature.rs:156-194), f32 */
+  float *fb = (float *)calloc((size_t)n_mels * nf, sizeof(float));
+  float *hz = (float *)malloc((size_t)(n_mels + 2) * sizeof(float));
+  const float mn = hz_to_mel(0.0f), mx = hz_to_mel((float)sr / 2.0f);
+  for (int i = 0; i <= n_mels + 1; i++) hz[i] = mel_to_hz(mn + (mx - mn) * (float)i / (float)(n_mels + 1));
+  for (int m = 0; m < n_mels; m++) {
+    const float l = hz[m], c = hz[m + 1], r = hz[m + 2];
+    for (int f = 0; f < nf; f++) {
+      const float fq = (float)f * (float)sr / (float)n_fft;
+      float v = 0.f;
+      if (fq >= l && fq <= c && c > l) v = (fq - l) / (c - l);
+      else if (fq > c && fq <= r && r > c) v = (r - fq) / (r - c);
+      fb[(size_t)m * nf + f] = v;
+    }
+    const float bw = hz[m + 2] - hz[m];
+    if (bw > 0.f)
+      for (int f = 0; f < nf; f++) fb[(size_t)m * nf + f] *= 2.0f / bw;
+  }
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < frames; t++) {
+    double re[1024], im[1024];
+    float mag[513];
+    for (int i = 0; i < n_fft; i++) {
+      re[i] = (double)(p[t * hop + i] * win[i]);
+      im[i] = 0.0;
+    }
+    fft_pow2(re, im, n_fft);
+    for (int f = 0; f < nf; f++) {
+      const float a = (float)re[f], b = (float)im[f];
+      mag[f] = sqrtf(a * a + b * b + 1e-9f);
+    }
+    for (int m = 0; m < n_mels; m++) {
+      float sum = 0.f;
+      for (int f = 0; f < nf; f++) sum += fb[(size_t)m * nf + f] * mag[f];
+      out[(size_t)m * frames + t] = logf(sum > 1e-5f ? sum : 1e-5f);
+    }
+  }
+  free(p); free(fb); free(hz);
+  return frames;
+}
+
+/* TimeDelayNetBlock (tdnn.rs:16-82): reflect pad (total / 2 left, the rest
+ * right), dilated valid conv with bias, ReLU; x [ci][T] -> y [co][T] */
+static int tdnn_forward(const orc_tdnn *b, const float *x, int T, float *y) {
+  const int total = b->dil * (b->k - 1), pl = total / 2, pr = total - pl;
+  if ((pl > 0 && T < pl + 1) || (pr > 0 && T < pr + 1)) return -1; /* the reference's slices need these */
+  const int Tp = T + total;
+  float *xp = (float *)malloc((size_t)b->ci * Tp * sizeof(float));
+  for (int c = 0; c < b->ci; c++) {
+    const float *xi = x + (size_t)c * T;
+    float *o = xp + (size_t)c * Tp;
+    for (int i = 0; i < pl; i++) o[i] = xi[pl - i];           /* x[pl], ..., x[1] */
+    memcpy(o + pl, xi, (size_t)T * sizeof(float));
+    for (int i = 0; i < pr; i++) o[pl + T + i] = xi[T - 2 - i]; /* x[T-2], ..., x[T-1-pr] */
+  }
+#pragma omp parallel for schedule(static)
+  for (int o = 0; o < b->co; o++) {
+    float *yo = y + (size_t)o * T;
+    for (int t = 0; t < T; t++) yo[t] = b->b[o];
+    for (int i = 0; i < b->ci; i++) {
+      const float *xi = xp + (size_t)i * Tp;
+      for (int j = 0; j < b->k; j++) {
+        const float wv = b->w[((size_t)o * b->ci + i) * b->k + j];
+        for (int t = 0; t < T; t++) yo[t] += wv * xi[t + j * b->dil];
+      }
+    }
+    for (int t = 0; t < T; t++) yo[t] = yo[t] > 0.f ? yo[t] : 0.f;
+  }
+  free(xp);
+  return 0;
+}
+
+/* SqueezeExcitationRes2NetBlock (res2net.rs:96-119) on x [C][T] in place */
+static int se_block_forward(const orc_se_block *b, float *x, int C, int T) {
+  float *h = (float *)malloc((size_t)C * T * sizeof(float));
+  float *g = (float *)malloc((size_t)C * T * sizeof(float));
+  int rc = tdnn_forward(&b->tdnn1, x, T, h);
+  /* Res2Net (res2net.rs:37-58): out = [c0, y1, ..., y_{s-1}], y1 = B1(c1),
+   * y_i = B_i(c_i + y_{i-1}) */
+  const int cs = C / b->scale;
+  memcpy(g, h, (size_t)cs * T * sizeof(float));
+  float *in = (float *)malloc((size_t)cs * T * sizeof(float));
+  for (int i = 1; i < b->scale && rc == 0; i++) {
+    const float *ci = h + (size_t)i * cs * T;
+    for (int64_t e = 0; e < (int64_t)cs * T; e++) in[e] = ci[e] + (i > 1 ? g[(size_t)(i - 1) * cs * T + e] : 0.f);
+    rc = tdnn_forward(&b->res[i - 1], in, T, g + (size_t)i * cs * T);
+  }
+  free(in);
+  if (rc == 0) rc = tdnn_forward(&b->tdnn2, g, T, h);
+  if (rc == 0) { /* squeeze-excitation (res2net.rs:62-90) */
+    float *m = (float *)malloc((size_t)C * sizeof(float));
+    float *z = (float *)malloc((size_t)b->se_ch * sizeof(float));
+    for (int c = 0; c < C; c++) {
+      float s = 0.f;
+      for (int t = 0; t < T; t++) s += h[(size_t)c * T + t];
+      m[c] = s / (float)T;
+    }
+    for (int j = 0; j < b->se_ch; j++) {
+      float s = b->se_b1[j];
+      for (int c = 0; c < C; c++) s += b->se_w1[(size_t)j * C + c] * m[c];
+      z[j] = s > 0.f ? s : 0.f;
+    }
+    for (int c = 0; c < C; c++) {
+      float s = b->se_b2[c];
+      for (int j = 0; j < b->se_ch; j++) s += b->se_w2[(size_t)c * b->se_ch + j] * z[j];
+      const float sc = 1.f / (1.f + expf(-s));
+      for (int t = 0; t < T; t++) x[(size_t)c * T + t] += h[(size_t)c * T + t] * sc;
+    }
+    free(m); free(z);
+  }
+  free(h); free(g);
+  return rc;
+}
+
+int orc_speaker_forward(const orc_speaker *s, const float *mel, int T, float *emb) {
+  if (!s || !mel || T <= 0) return -1;
+  const int C = s->channels[1], C4 = s->channels[4];
+  float *x = (float *)malloc((size_t)C * T * sizeof(float));
+  float *cat = (float *)malloc((size_t)3 * C * T * sizeof(float));
+  int rc = tdnn_forward(&s->block0, mel, T, x);
+  for (int i = 0; i < 3 && rc == 0; i++) { /* network/mod.rs:75-92 */
+    rc = se_block_forward(&s->se[i], x, C, T);
+    memcpy(cat + (size_t)i * C * T, x, (size_t)C * T * sizeof(float));
+  }
+  float *h = (float *)malloc((size_t)C4 * T * sizeof(float));
+  if (rc == 0) rc = tdnn_forward(&s->mfa, cat, T, h);
+  if (rc == 0) { /* AttentiveStatisticsPooling (pooling.rs:25-72) */
+    float *ain = (float *)malloc((size_t)3 * C4 * T * sizeof(float));
+    float *mean = (float *)malloc((size_t)C4 * sizeof(float)), *sd = (float *)malloc((size_t)C4 * sizeof(float));
+    for (int c = 0; c < C4; c++) {
+      float s1 = 0.f, s2 = 0.f;
+      for (int t = 0; t < T; t++) {
+        const float v = h[(size_t)c * T + t];
+        s1 += v;
+        s2 += v * v;
+      }
+      const float mu = s1 / (float)T, var = s2 / (float)T - mu * mu;
+      mean[c] = mu;
+      sd[c] = sqrtf((var > 0.f ? var : 0.f) + 1e-5f);
+      for (int t = 0; t < T; t++) {
+        ain[(size_t)c * T + t] = h[(size_t)c * T + t];
+        ain[(size_t)(C4 + c) * T + t] = mu;
+        ain[(size_t)(2 * C4 + c) * T + t] = sd[c];
+      }
+    }
+    const int A = s->asp_tdnn.co;
+    float *a = (float *)malloc((size_t)A * T * sizeof(float));
+    rc = tdnn_forward(&s->asp_tdnn, ain, T, a);
+    for (int64_t e = 0; e < (int64_t)A * T; e++) a[e] = tanhf(a[e]);
+    float *pooled = (float *)malloc((size_t)2 * C4 * sizeof(float));
+#pragma omp parallel for schedule(static)
+    for (int c = 0; c < C4; c++) {
+      float *sc = (float *)malloc((size_t)T * sizeof(float));
+      float mx = -INFINITY;
+      for (int t = 0; t < T; t++) {
+        float v = s->asp_b[c];
+        for (int j = 0; j < A; j++) v += s->asp_w[(size_t)c * A + j] * a[(size_t)j * T + t];
+        sc[t] = v;
+        mx = v > mx ? v : mx;
+      }
+      float z = 0.f;
+      for (int t = 0; t < T; t++) {
+        sc[t] = expf(sc[t] - mx);
+        z += sc[t];
+      }
+      float wm = 0.f, w2 = 0.f;
+      for (int t = 0; t < T; t++) {
+        const float p = sc[t] / z, v = h[(size_t)c * T + t];
+        wm += v * p;
+        w2 += v * v * p;
+      }
+      const float wv = w2 - wm * wm;
+      pooled[c] = wm;
+      pooled[C4 + c] = sqrtf((wv > 0.f ? wv : 0.f) + 1e-5f);
+      free(sc);
+    }
+    for (int o = 0; o < s->enc_dim; o++) { /* fc: Conv1d k1 (network/mod.rs:59-61) */
+      float v = s->fc_b[o];
+      for (int c = 0; c < 2 * C4; c++) v += s->fc_w[(size_t)o * 2 * C4 + c] * pooled[c];
+      emb[o] = v;
+    }
+    free(ain); free(mean); free(sd); free(a); free(pooled);
+  }
+  free(x); free(cat); free(h);
+  return rc;
+}
+
+int orc_speaker_embed(const orc_speaker *s, const float *samples, int n, float *emb) {
+  if (!s || !samples || n < 256) return -1;
+  const int frames = (n + 768 - 1024) / 256 + 1;
+  float *mel = (float *)malloc((size_t)s->mel_dim * frames * sizeof(float));
+  int T = orc_speaker_mel(samples, n, s->sample_rate, s->mel_dim, mel, frames);
+  int rc = T < 0 ? -1 : orc_speaker_forward(s, mel, T, emb);
+  free(mel);
+  return rc;
+}

@@ -274,6 +274,46 @@ int orc_codec_encode(const orc_codec_encoder *e, const float *wave, int n, int n
 void orc_rvq_encode(const float *const *embed_sum, const float *const *usage, int n_layers, int codebook_size,
                     int vq, float *x, int T, int64_t *codes);
 
+/* ------------------------------------------------------------------------ */
+/* Speaker encoder (voice-clone x-vector): model/speaker/{infer,network}     */
+/* ------------------------------------------------------------------------ */
+/* speaker/infer/feature.rs: log-mel features of n samples (n >= 256):
+ * reflect-padded STFT (n_fft 1024, hop 256, periodic Hann window; the DFT
+ * rustfft 6.4.1 computes), magnitudes, mel filters with area normalisation,
+ * ln(max(., 1e-5)) -> out [n_mels][frames].  Returns frames, < 0 on bad input
+ * or when they would not fit max_frames. */
+int orc_speaker_mel(const float *samples, int n, int sample_rate, int n_mels, float *out, int max_frames);
+
+typedef struct {
+  const float *w, *b; /* Conv1d [co][ci][k], bias [co] */
+  int ci, co, k, dil;
+} orc_tdnn;           /* reflect pad, conv, ReLU (speaker/network/tdnn.rs) */
+
+typedef struct {
+  orc_tdnn tdnn1, tdnn2;     /* k1 */
+  orc_tdnn res[15];          /* scale - 1 Res2Net branches */
+  int scale;
+  const float *se_w1, *se_b1, *se_w2, *se_b2; /* [se][C][1], [se], [C][se][1], [C] */
+  int se_ch;
+} orc_se_block;
+
+typedef struct {
+  int mel_dim, enc_dim, sample_rate;
+  int channels[5];
+  orc_tdnn block0;
+  orc_se_block se[3];
+  orc_tdnn mfa;
+  orc_tdnn asp_tdnn;               /* 3C -> attention channels, k1 */
+  const float *asp_w, *asp_b;      /* [C][att][1], [C] */
+  const float *fc_w, *fc_b;        /* [enc_dim][2C][1], [enc_dim] */
+} orc_speaker;
+
+/* SpeakerEncoderNetwork::forward (network/mod.rs:71-99) on mel [mel_dim][T]
+ * -> emb [enc_dim]; < 0 on bad input */
+int orc_speaker_forward(const orc_speaker *s, const float *mel, int T, float *emb);
+/* encode_embedding (infer/mod.rs:11-20): samples -> emb [enc_dim] */
+int orc_speaker_embed(const orc_speaker *s, const float *samples, int n, float *emb);
+
 #ifdef __cplusplus
 }
 #endif

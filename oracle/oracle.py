@@ -107,6 +107,21 @@ class CodecEncoder(C.Structure):
                 ("acoustic", EncRvq)]
 
 
+class Tdnn(C.Structure):
+    _fields_ = [("w", F), ("b", F), ("ci", C.c_int), ("co", C.c_int), ("k", C.c_int), ("dil", C.c_int)]
+
+
+class SeBlock(C.Structure):
+    _fields_ = [("tdnn1", Tdnn), ("tdnn2", Tdnn), ("res", Tdnn * 15), ("scale", C.c_int),
+                ("se_w1", F), ("se_b1", F), ("se_w2", F), ("se_b2", F), ("se_ch", C.c_int)]
+
+
+class Speaker(C.Structure):
+    _fields_ = [("mel_dim", C.c_int), ("enc_dim", C.c_int), ("sample_rate", C.c_int), ("channels", C.c_int * 5),
+                ("block0", Tdnn), ("se", SeBlock * 3), ("mfa", Tdnn), ("asp_tdnn", Tdnn),
+                ("asp_w", F), ("asp_b", F), ("fc_w", F), ("fc_b", F)]
+
+
 def lib():
     """Load liboracle.so, building it with make if it is missing."""
     global _LIB
@@ -148,6 +163,9 @@ def lib():
         L.orc_conv1d_padding.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int,
                                          C.POINTER(C.c_int), C.POINTER(C.c_int)]
         L.orc_to_pcm.argtypes = [F, C.c_int64, C.POINTER(C.c_int16)]
+        L.orc_speaker_mel.argtypes = [F, C.c_int, C.c_int, C.c_int, F, C.c_int]
+        L.orc_speaker_forward.argtypes = [C.POINTER(Speaker), F, C.c_int, F]
+        L.orc_speaker_embed.argtypes = [C.POINTER(Speaker), F, C.c_int, F]
         L.orc_codec_encode.argtypes = [C.POINTER(CodecEncoder), F, C.c_int, C.c_int, I64, C.c_int]
         L.orc_rvq_encode.argtypes = [C.POINTER(F), C.POINTER(F), C.c_int, C.c_int, C.c_int, F, C.c_int, I64]
         L.orc_sdpa.argtypes = [F, F, F, C.POINTER(C.c_uint8), C.c_int, C.c_int, C.c_int,
@@ -528,3 +546,69 @@ def rvq_encode(embed_sum, usage, x):
     lib().orc_rvq_encode(C.cast(pe, C.POINTER(F)), C.cast(pu, C.POINTER(F)), n, cb, vq, fp(x), T,
                          codes.ctypes.data_as(I64))
     return codes, x
+
+
+def speaker_mel(samples, n_mels=128, sample_rate=24000):
+    """Log-mel features of the speaker encoder (speaker/infer/feature.rs):
+    [n_mels][frames]."""
+    x = np.ascontiguousarray(samples, np.float32)
+    frames = (len(x) + 768 - 1024) // 256 + 1
+    out = np.zeros((n_mels, max(frames, 1)), np.float32)
+    got = lib().orc_speaker_mel(fp(x), len(x), sample_rate, n_mels, fp(out), max(frames, 0))
+    if got < 0:
+        raise ValueError("speaker mel needs at least 256 samples")
+    return out[:, :got]
+
+
+class OracleSpeaker:
+    """ECAPA-TDNN speaker encoder of the voice-clone path
+    (LoadedQwen3TtsSpeakerEncoder::encode_embedding, speaker/infer/mod.rs:11-20;
+    network in speaker/network/*.rs)."""
+
+    def __init__(self, cfg, weights: dict):
+        self.cfg = cfg
+        w = {k: f32(v) for k, v in weights.items()}
+        self.w = w
+        p = "speaker_encoder"
+        sp = Speaker()
+        sp.mel_dim, sp.enc_dim, sp.sample_rate = cfg.mel_dim, cfg.enc_dim, cfg.sample_rate
+        for i, c in enumerate(cfg.enc_channels):
+            sp.channels[i] = c
+        if cfg.enc_res2net_scale > 16:
+            raise ValueError("Res2Net scale above 16")
+
+        def tdnn(name, k=1, dil=1):
+            wt = w[f"{name}.weight"]
+            return Tdnn(fp(wt), fp(w[f"{name}.bias"]), wt.shape[1], wt.shape[0], k, dil)
+
+        ks, dl = cfg.enc_kernel_sizes, cfg.enc_dilations
+        sp.block0 = tdnn(f"{p}.blocks.0.conv", ks[0], dl[0])
+        for i in range(1, 4):
+            b = f"{p}.blocks.{i}"
+            se = SeBlock()
+            se.tdnn1, se.tdnn2 = tdnn(f"{b}.tdnn1.conv"), tdnn(f"{b}.tdnn2.conv")
+            for j in range(cfg.enc_res2net_scale - 1):
+                se.res[j] = tdnn(f"{b}.res2net_block.blocks.{j}.conv", ks[i], dl[i])
+            se.scale, se.se_ch = cfg.enc_res2net_scale, cfg.enc_se_channels
+            se.se_w1, se.se_b1 = fp(w[f"{b}.se_block.conv1.weight"]), fp(w[f"{b}.se_block.conv1.bias"])
+            se.se_w2, se.se_b2 = fp(w[f"{b}.se_block.conv2.weight"]), fp(w[f"{b}.se_block.conv2.bias"])
+            sp.se[i - 1] = se
+        sp.mfa = tdnn(f"{p}.mfa.conv", ks[4], dl[4])
+        sp.asp_tdnn = tdnn(f"{p}.asp.tdnn.conv")
+        sp.asp_w, sp.asp_b = fp(w[f"{p}.asp.conv.weight"]), fp(w[f"{p}.asp.conv.bias"])
+        sp.fc_w, sp.fc_b = fp(w[f"{p}.fc.weight"]), fp(w[f"{p}.fc.bias"])
+        self.s = sp
+
+    def forward(self, mel):
+        mel = np.ascontiguousarray(mel, np.float32)
+        emb = np.zeros(self.cfg.enc_dim, np.float32)
+        if lib().orc_speaker_forward(C.byref(self.s), fp(mel), mel.shape[1], fp(emb)) < 0:
+            raise ValueError("speaker encoder: too few frames for the reflect padding")
+        return emb
+
+    def embed(self, samples):
+        x = np.ascontiguousarray(samples, np.float32)
+        emb = np.zeros(self.cfg.enc_dim, np.float32)
+        if lib().orc_speaker_embed(C.byref(self.s), fp(x), len(x), fp(emb)) < 0:
+            raise ValueError("speaker encoder: bad input")
+        return emb

@@ -418,6 +418,71 @@ def make_codec_encoder_weights(cfg: CodecEncoderConfig, seed: int = 0) -> dict:
     return _parallel(one, codec_encoder_tensor_specs(cfg))
 
 
+@dataclass
+class SpeakerEncoderConfig:
+    """ECAPA-TDNN speaker encoder of the voice-clone path: the reference's own
+    defaults (model/speaker/config.rs:18-32)."""
+    mel_dim: int = 128
+    enc_dim: int = 1024
+    enc_channels: tuple = (512, 512, 512, 512, 1536)
+    enc_kernel_sizes: tuple = (5, 3, 3, 3, 1)
+    enc_dilations: tuple = (1, 2, 3, 4, 1)
+    enc_attention_channels: int = 128
+    enc_res2net_scale: int = 8
+    enc_se_channels: int = 128
+    sample_rate: int = 24000
+
+    def small(self, **kw):
+        """A reduced encoder for fast CPU tests (same structure)."""
+        d = dict(mel_dim=32, enc_dim=48, enc_channels=(32, 32, 32, 32, 96), enc_attention_channels=16,
+                 enc_res2net_scale=4, enc_se_channels=8)
+        d.update(kw)
+        return replace(self, **d)
+
+    def frames(self, n: int) -> int:
+        """Mel frames for n samples (feature.rs:92-115: pad 384 each side, hop 256)."""
+        return (n + 768 - 1024) // 256 + 1
+
+
+def speaker_tensor_specs(c: SpeakerEncoderConfig):
+    """(name, shape, init) of the speaker encoder tensors: 'speaker_encoder.'
+    + the reference's module paths (speaker/weights.rs:73, network/*.rs)."""
+    p = "speaker_encoder"
+    s = []
+
+    def conv(name, co, ci, k):
+        s.extend([(f"{name}.weight", (co, ci, k), ("fan", ci * k, 1.0)), (f"{name}.bias", (co,), ("normal", 0.02))])
+
+    ch, ks, dil = c.enc_channels, c.enc_kernel_sizes, c.enc_dilations
+    conv(f"{p}.blocks.0.conv", ch[0], c.mel_dim, ks[0])
+    for i in range(1, 4):
+        b = f"{p}.blocks.{i}"
+        C, cs = ch[i], ch[i] // c.enc_res2net_scale
+        conv(f"{b}.tdnn1.conv", C, C, 1)
+        for j in range(c.enc_res2net_scale - 1):
+            conv(f"{b}.res2net_block.blocks.{j}.conv", cs, cs, ks[i])
+        conv(f"{b}.tdnn2.conv", C, C, 1)
+        conv(f"{b}.se_block.conv1", c.enc_se_channels, C, 1)
+        conv(f"{b}.se_block.conv2", C, c.enc_se_channels, 1)
+    conv(f"{p}.mfa.conv", ch[4], sum(ch[1:4]), ks[4])
+    conv(f"{p}.asp.tdnn.conv", c.enc_attention_channels, 3 * ch[4], 1)
+    conv(f"{p}.asp.conv", ch[4], c.enc_attention_channels, 1)
+    conv(f"{p}.fc", c.enc_dim, 2 * ch[4], 1)
+    return s
+
+
+def make_speaker_weights(cfg: SpeakerEncoderConfig, seed: int = 0) -> dict:
+    """Seeded speaker encoder weights (f32), convs ~N(0, 1/fan_in)."""
+    def one(spec):
+        name, shape, init = spec
+        if init[0] == "normal":
+            a = _normal(seed, name, shape, init[1])
+        else:
+            a = _normal(seed, name, shape, init[2] / np.sqrt(init[1]))
+        return name, np.ascontiguousarray(a, dtype=np.float32)
+    return _parallel(one, speaker_tensor_specs(cfg))
+
+
 def synthetic_talker_inputs(cfg: TalkerConfig, S: int, seed: int = 0):
     """Prompt embeddings [S, H], trailing text [1, H] and pad embed [H]:
     stand-ins for the host-side session seed (compiler/session_seed.rs)."""
