@@ -1079,9 +1079,9 @@ void orc_rvq_encode(const float *const *embed_sum, const float *const *usage, in
   free(cent);
 }
 
-int orc_codec_encode(const orc_codec_encoder *e, const float *wave, int n, int n_valid, int64_t *codes,
-                     int max_frames) {
-  if (!e || !wave || n <= 0 || e->semantic.n_layers <= 0 || n_valid < e->semantic.n_layers) return -1;
+/* encoder.rs:128-130: backbone, transformer and downsample; returns the
+ * hidden [H][T] (malloc'd, caller frees) and T, or NULL */
+static float *encoder_hidden(const orc_codec_encoder *e, const float *wave, int n, int *T_out) {
   /* backbone (encoder.rs:138-175; layers as config.rs:174-236 builds them) */
   int L = n, C = 1;
   float *x = (float *)malloc((size_t)n * sizeof(float));
@@ -1118,7 +1118,7 @@ int orc_codec_encode(const orc_codec_encoder *e, const float *wave, int n, int n
   }
   /* transformer on [T][H] (encoder.rs:179-200) */
   const int H = e->hidden;
-  if (C != H) { free(x); return -1; }
+  if (C != H) { free(x); return NULL; }
   float *h = (float *)malloc((size_t)L * H * sizeof(float));
   transpose(x, H, L, h);
   for (int l = 0; l < e->n_layers; l++) enc_layer(e, &e->layers[l], h, L);
@@ -1129,6 +1129,28 @@ int orc_codec_encode(const orc_codec_encoder *e, const float *wave, int n, int n
   float *z = (float *)malloc((size_t)H * T * sizeof(float));
   enc_conv(&e->downsample, x, L, 1, z);
   free(x);
+  *T_out = T;
+  return z;
+}
+
+int orc_codec_encoder_hidden(const orc_codec_encoder *e, const float *wave, int n, float *out, int max_frames) {
+  if (!e || !wave || n <= 0) return -1;
+  int T = 0;
+  float *z = encoder_hidden(e, wave, n, &T);
+  if (!z) return -1;
+  if (T > max_frames) { free(z); return -1; }
+  memcpy(out, z, (size_t)e->hidden * T * sizeof(float));
+  free(z);
+  return T;
+}
+
+int orc_codec_encode(const orc_codec_encoder *e, const float *wave, int n, int n_valid, int64_t *codes,
+                     int max_frames) {
+  if (!e || !wave || n <= 0 || e->semantic.n_layers <= 0 || n_valid < e->semantic.n_layers) return -1;
+  int T = 0;
+  float *z = encoder_hidden(e, wave, n, &T);
+  if (!z) return -1;
+  const int H = e->hidden;
   if (T > max_frames || T <= 0) { free(z); return -1; }
   /* quantizers on the same hidden (encoder.rs:290-317) */
   const int vq = e->vq_dim;

@@ -268,6 +268,9 @@ typedef struct {
  * when the codes would not fit max_frames. */
 int orc_codec_encode(const orc_codec_encoder *e, const float *wave, int n, int n_valid, int64_t *codes,
                      int max_frames);
+/* the hidden [hidden][T] the quantizers read (after the stride-2
+ * downsample); returns T or < 0 */
+int orc_codec_encoder_hidden(const orc_codec_encoder *e, const float *wave, int n, float *out, int max_frames);
 /* one residual vector quantizer's encode (encoder.rs:319-368) on x [vq][T]
  * (already through input_proj): codes [n_layers][T]; x is left holding the
  * final residual */

@@ -166,6 +166,7 @@ def lib():
         L.orc_speaker_mel.argtypes = [F, C.c_int, C.c_int, C.c_int, F, C.c_int]
         L.orc_speaker_forward.argtypes = [C.POINTER(Speaker), F, C.c_int, F]
         L.orc_speaker_embed.argtypes = [C.POINTER(Speaker), F, C.c_int, F]
+        L.orc_codec_encoder_hidden.argtypes = [C.POINTER(CodecEncoder), F, C.c_int, F, C.c_int]
         L.orc_codec_encode.argtypes = [C.POINTER(CodecEncoder), F, C.c_int, C.c_int, I64, C.c_int]
         L.orc_rvq_encode.argtypes = [C.POINTER(F), C.POINTER(F), C.c_int, C.c_int, C.c_int, F, C.c_int, I64]
         L.orc_sdpa.argtypes = [F, F, F, C.POINTER(C.c_uint8), C.c_int, C.c_int, C.c_int,
@@ -531,6 +532,19 @@ class OracleCodecEncoder:
             raise ValueError("bad encoder input")
         assert got == T, (got, T)
         return codes
+
+
+def _encoder_hidden(self, wave):
+    """The hidden [hidden][frames] the quantizers read (after the downsample)."""
+    wave = np.ascontiguousarray(wave, np.float32)
+    T = self.cfg.frames(len(wave))
+    out = np.zeros((self.cfg.hidden, T), np.float32)
+    if lib().orc_codec_encoder_hidden(C.byref(self.e), fp(wave), len(wave), fp(out), T) != T:
+        raise ValueError("bad encoder input")
+    return out
+
+
+OracleCodecEncoder.hidden = _encoder_hidden
 
 
 def rvq_encode(embed_sum, usage, x):

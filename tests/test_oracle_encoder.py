@@ -14,7 +14,9 @@ reference's structure fixes exactly:
   last frame, whose stride windows the prefix cuts (bit-exact, same order of
   operations);
 * semantic codes come first, and asking for fewer codebooks returns a prefix
-  of the rows.
+  of the rows;
+* the hidden state the quantizers read matches an independent float64 numpy
+  restatement of the backbone, transformer and downsample (1e-5 relative).
 """
 import numpy as np
 import pytest
@@ -96,3 +98,87 @@ def test_rvq_encode_kat():
     assert 5 not in codes[0], "a zero-usage row is never chosen"
     np.testing.assert_array_equal(codes[0], [0, 1, 2, 0])
     np.testing.assert_array_equal(codes[1], [3, 4, 4, 1])
+
+
+def _conv_np(x, w, b, stride, edge):
+    """conv1d_padding + pad_1d + Conv1d (conv.rs:44-83) in float64."""
+    L, k = x.shape[1], w.shape[2]
+    pt = max(k - stride, 0)
+    padded = L + pt
+    missing = max(k - padded, 0)
+    extra = missing if missing > 0 else (stride - (padded - k) % stride) % stride
+    xp = np.pad(x, ((0, 0), (pt, extra)), mode="edge" if edge else "constant")
+    Lo = (L + pt + extra - k) // stride + 1
+    win = xp[:, np.arange(Lo)[:, None] * stride + np.arange(k)[None]]  # [ci][Lo][k]
+    y = np.einsum("oik,itk->ot", w, win)
+    return y + (b[:, None] if b is not None else 0.0)
+
+
+def encoder_hidden_numpy(cfg, w):
+    from scipy.special import erf
+    W = lambda n: w[n].astype(np.float64)
+    elu = lambda v: np.where(v > 0, v, np.expm1(v))
+    p = "encoder.encoder.layers"
+
+    def run(wave):
+        x = _conv_np(wave[None].astype(np.float64), W(f"{p}.0.conv.weight"), W(f"{p}.0.conv.bias"), 1, False)
+        li = 1
+        for r in reversed(cfg.upsampling_ratios):
+            h = _conv_np(elu(x), W(f"{p}.{li}.conv_in.conv.weight"), W(f"{p}.{li}.conv_in.conv.bias"), 1, False)
+            x = x + _conv_np(elu(h), W(f"{p}.{li}.conv_out.conv.weight"), W(f"{p}.{li}.conv_out.conv.bias"), 1,
+                             False)
+            x = _conv_np(elu(x), W(f"{p}.{li + 2}.conv.weight"), W(f"{p}.{li + 2}.conv.bias"), r, False)
+            li += 3
+        x = _conv_np(elu(x), W(f"{p}.{li + 1}.conv.weight"), W(f"{p}.{li + 1}.conv.bias"), 1, False)
+        h = x.T  # [T][H]
+        T, hd = h.shape[0], cfg.head_dim
+        inv = cfg.theta ** (-np.arange(0, hd, 2) / hd)
+        ang = np.arange(T)[:, None] * inv[None]
+        cs, sn = np.cos(ang), np.sin(ang)
+
+        def rope(v):  # [T][heads][hd], adjacent pairs
+            a, b = v[..., 0::2], v[..., 1::2]
+            out = np.empty_like(v)
+            out[..., 0::2] = a * cs[:, None] - b * sn[:, None]
+            out[..., 1::2] = b * cs[:, None] + a * sn[:, None]
+            return out
+
+        def ln(v, g, bb):
+            mu = v.mean(-1, keepdims=True)
+            var = ((v - mu) ** 2).mean(-1, keepdims=True)
+            return (v - mu) / np.sqrt(var + cfg.norm_eps) * g + bb
+
+        for l in range(cfg.n_layers):
+            q_ = f"encoder.encoder_transformer.layers.{l}"
+            n = ln(h, W(f"{q_}.input_layernorm.weight"), W(f"{q_}.input_layernorm.bias"))
+            q = rope((n @ W(f"{q_}.self_attn.q_proj.weight").T).reshape(T, cfg.n_heads, hd))
+            k = rope((n @ W(f"{q_}.self_attn.k_proj.weight").T).reshape(T, cfg.n_kv, hd))
+            v = (n @ W(f"{q_}.self_attn.v_proj.weight").T).reshape(T, cfg.n_kv, hd)
+            rep = cfg.n_heads // cfg.n_kv
+            k, v = np.repeat(k, rep, axis=1), np.repeat(v, rep, axis=1)
+            s = np.einsum("thd,shd->hts", q, k) / np.sqrt(hd)
+            s = np.where(np.triu(np.ones((T, T), bool), 1)[None], -np.inf, s)
+            a = np.exp(s - s.max(-1, keepdims=True))
+            a /= a.sum(-1, keepdims=True)
+            o = np.einsum("hts,shd->thd", a, v).reshape(T, -1) @ W(f"{q_}.self_attn.o_proj.weight").T
+            h = h + o * W(f"{q_}.self_attn_layer_scale.scale")
+            n = ln(h, W(f"{q_}.post_attention_layernorm.weight"), W(f"{q_}.post_attention_layernorm.bias"))
+            f = n @ W(f"{q_}.mlp.fc1.weight").T
+            f = 0.5 * f * (1 + erf(f / np.sqrt(2)))
+            h = h + (f @ W(f"{q_}.mlp.fc2.weight").T) * W(f"{q_}.mlp_layer_scale.scale")
+        return _conv_np(h.T, W("encoder.downsample.conv.weight"), None, 2, True)
+
+    return run
+
+
+@pytest.mark.parametrize("n", [500, 2417])
+def test_encoder_hidden_matches_numpy(enc, n):
+    """Backbone, causal transformer and edge-padded downsample against an
+    independent float64 numpy restatement (f32 vs f64 arithmetic only)."""
+    cfg, e = enc
+    w = S.make_codec_encoder_weights(cfg, seed=0)
+    wave = _wave(n, seed=4)
+    got = e.hidden(wave)
+    ref = encoder_hidden_numpy(cfg, w)(wave)
+    assert got.shape == ref.shape == (cfg.hidden, cfg.frames(n))
+    assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max()
