@@ -339,6 +339,16 @@ q3t_status q3t_batch_stream(q3t_batch *b, void **stream);
 void q3t_batch_free(q3t_batch *b);
 
 /* ------------------------------- misc ----------------------------------- */
+/* Struct layout as this library was compiled (no reference counterpart: the
+ * reference is one Rust crate, so its structs need no cross-language check).
+ * A binding that re-declares the structs above (a Rust `#[repr(C)]` -sys
+ * crate, a ctypes mirror) compares its own sizes and offsets with these at
+ * start-up or in its tests.  `name` is the C struct name ("q3t_step_stats");
+ * fields are numbered in declaration order.  INVALID_INPUT for an unknown
+ * struct or an index outside [0, num_fields). */
+q3t_status q3t_abi_struct(const char *name, size_t *size, size_t *align, int *num_fields);
+q3t_status q3t_abi_field(const char *name, int index, const char **field, size_t *offset,
+                         size_t *size);
 const char *q3t_last_error(void);
 const char *q3t_version(void);
 /* Number of kernel launches this thread has issued into the library's

@@ -105,7 +105,7 @@ EXPORTS = [
     "q3t_batch_pending", "q3t_batch_stream", "q3t_batch_free", "q3t_last_error", "q3t_version",
     "q3t_kernel_launches", "q3t_text_project", "q3t_text_dims",
     "q3t_safetensors_open", "q3t_tensor_set_list", "q3t_tensor_set_free", "q3t_wav_write",
-    "q3t_codec_last_ms", "q3t_session_seed",
+    "q3t_codec_last_ms", "q3t_session_seed", "q3t_abi_struct", "q3t_abi_field",
 ]
 
 
@@ -169,8 +169,33 @@ def lib():
         L.q3t_tensor_set_free.restype = None
         L.q3t_wav_write.argtypes = [C.POINTER(C.c_int16), C.c_int64, C.c_int, C.c_int, C.POINTER(C.c_uint8),
                                     C.c_int64, _I64]
+        L.q3t_abi_struct.argtypes = [C.c_char_p, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t),
+                                     C.POINTER(C.c_int)]
+        L.q3t_abi_field.argtypes = [C.c_char_p, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_size_t),
+                                    C.POINTER(C.c_size_t)]
         _LIB = L
     return _LIB
+
+
+def abi_layout(name):
+    """(size, align, [(field, offset, size), ...]) of a public struct as the
+    library was compiled (q3t_abi_struct / q3t_abi_field); no GPU needed."""
+    L = lib()
+    size, align, n = C.c_size_t(), C.c_size_t(), C.c_int()
+    check(L.q3t_abi_struct(name.encode(), C.byref(size), C.byref(align), C.byref(n)))
+    fields = []
+    for i in range(n.value):
+        f, off, fs = C.c_char_p(), C.c_size_t(), C.c_size_t()
+        check(L.q3t_abi_field(name.encode(), i, C.byref(f), C.byref(off), C.byref(fs)))
+        fields.append((f.value.decode(), off.value, fs.value))
+    return size.value, align.value, fields
+
+
+# ctypes mirrors of the public structs, by their C names
+STRUCTS = {"q3t_lm_config": LMConfig, "q3t_talker_config": TalkerConfig, "q3t_codec_config": CodecConfig,
+           "q3t_tensor": Tensor, "q3t_model_desc": ModelDesc, "q3t_sampling": Sampling,
+           "q3t_session_desc": SessionDesc, "q3t_seed_controls": SeedControls, "q3t_batch_desc": BatchDesc,
+           "q3t_step_stats": StepStats}
 
 
 def check(rc):
