@@ -212,11 +212,15 @@ q3t_status q3t_codec_last_ms(float *ms);
  * the samples use one static 48 MiB device array per process: B x T up to
  * about 26 frames (a 24-frame streaming window at B = 1); larger requests are
  * INVALID_INPUT with the needed size in q3t_last_error().  Runs on `stream`
- * (a cudaStream_t; NULL is the default stream) and returns when wave / pcm
- * (host buffers, nullable) hold the result.  The first call on each device
- * looks up the array's address (cudaGetSymbolAddress) with the model's device
- * current; make that first call before any stream capture.  Calls that
- * overlap in time on one device share the array and race: serialise them. */
+ * (a cudaStream_t; NULL is the default stream) and blocks: it synchronises
+ * `stream` and returns only when wave / pcm (host buffers, nullable) hold the
+ * result.  A convolution timeout is read from a word inside the array on
+ * `stream` (other decodes running at the same time neither see nor clear
+ * it).  The first call on each device looks up the array's address
+ * (cudaGetSymbolAddress) with the model's device current; make that first
+ * call before any stream capture.  The calling thread's current device is
+ * the same on return as on entry.  Calls that overlap in time on one device
+ * share the array and race: serialise them. */
 q3t_status q3t_codec_decode_static(q3t_model *model, const int64_t *codes, int B, int T,
                                    float *wave, int16_t *pcm, int64_t *n, void *stream);
 

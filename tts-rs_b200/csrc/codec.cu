@@ -549,29 +549,24 @@ __global__ void __launch_bounds__(256) k_conv_tc(const __grid_constant__ ConvTc 
   if (warp == 0) tmem_dealloc(tmem, kCols);
 }
 
-// Device words for bounded-wait timeouts of k_conv_tc / k_conv_pt, one per
-// device, created by codec_load (model load may allocate; the decode paths,
-// the static one included, only look the word up).
-constexpr int kConvErrDevices = 64;
-static int *g_conv_err_dev[kConvErrDevices] = {};
-static std::mutex g_conv_err_mu;
+// Device word for the bounded-wait timeouts of k_conv_tc / k_conv_pt.  Each
+// decode path owns its own word (the allocating decode one per call, the
+// static decode one inside its static array, a streaming batch one per
+// batch), zeroes it on its stream before its kernels and reads it back on the
+// same stream after them, so decodes that run at the same time on one device
+// never see or clear each other's timeouts.  The word of the decode being
+// enqueued by this thread is set by ConvErrScope.
+static thread_local int *t_conv_err = nullptr;
 
-static void conv_err_init() {
-  int dev = 0;
-  CK(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= kConvErrDevices) FAIL(Q3T_INVALID_INPUT, "device %d beyond %d", dev, kConvErrDevices);
-  std::lock_guard<std::mutex> lk(g_conv_err_mu);
-  if (!g_conv_err_dev[dev]) {
-    CK(cudaMalloc(&g_conv_err_dev[dev], sizeof(int)));
-    CK(cudaMemset(g_conv_err_dev[dev], 0, sizeof(int)));
-  }
-}
+struct ConvErrScope {
+  int *prev;
+  explicit ConvErrScope(int *w) : prev(t_conv_err) { t_conv_err = w; }
+  ~ConvErrScope() { t_conv_err = prev; }
+};
 
-// The current device's timeout word (null before a codec was loaded there).
 static int *conv_err_word() {
-  int dev = 0;
-  CK(cudaGetDevice(&dev));
-  return dev >= 0 && dev < kConvErrDevices ? g_conv_err_dev[dev] : nullptr;
+  if (!t_conv_err) FAIL(Q3T_INVALID_INPUT, "internal: codec convolution enqueued without a timeout word");
+  return t_conv_err;
 }
 
 // True the first time it is called for the current device with this mask
@@ -585,17 +580,10 @@ static bool first_on_device(uint64_t &mask) {
   return true;
 }
 
-// Raises Q3T_DEVICE_TIMEOUT if a convolution's bounded wait gave up since the
-// last check; the caller's stream is idle.
-static void conv_check_err() {
-  int *w = conv_err_word();
-  if (!w) return;
-  int e = 0;
-  CK(cudaMemcpy(&e, w, sizeof e, cudaMemcpyDeviceToHost));
-  if (e) {
-    CK(cudaMemset(w, 0, sizeof e));
-    FAIL(Q3T_DEVICE_TIMEOUT, "codec convolution: a bounded device wait gave up (code %#x)", e);
-  }
+// Raises Q3T_DEVICE_TIMEOUT if the timeout word read back after a decode
+// (host copy, taken on the decode's stream after its kernels) is set.
+static void conv_check_err(int e, const char *what) {
+  if (e) FAIL(Q3T_DEVICE_TIMEOUT, "%s: a bounded device wait of a convolution gave up (code %#x)", what, e);
 }
 
 // The fused residual unit's extra operands (FUSE = 1).
@@ -1690,7 +1678,6 @@ CodecModel *codec_load(q3t_model *m, const q3t_model_desc *d, cudaStream_t st) {
       CK(cudaFuncSetAttribute(k_conv<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)conv_smem(128)));
       CK(cudaFuncSetAttribute(k_conv<96>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)conv_smem(96)));
     }
-    conv_err_init();
   } catch (...) {
     delete c;
     throw;
@@ -1965,7 +1952,10 @@ void codec_decode_host_codes(q3t_model *m, const int64_t *codes, int B, int T, f
   int64_t *dc;
   float *dw = nullptr;
   int16_t *dp = nullptr;
+  int *derr = nullptr, herr = 0;  // this call's convolution timeout word
   CK(cudaMallocAsync((void **)&dc, ncodes * 8, st));
+  CK(cudaMallocAsync((void **)&derr, sizeof(int), st));
+  CK(cudaMemsetAsync(derr, 0, sizeof(int), st));
   CK(cudaMemcpyAsync(dc, codes, ncodes * 8, cudaMemcpyHostToDevice, st));
   if (wave) CK(cudaMallocAsync((void **)&dw, (size_t)B * n * 4, st));
   if (pcm) CK(cudaMallocAsync((void **)&dp, (size_t)B * n * 2, st));
@@ -1973,18 +1963,23 @@ void codec_decode_host_codes(q3t_model *m, const int64_t *codes, int B, int T, f
   CK(cudaEventCreate(&e0));
   CK(cudaEventCreate(&e1));
   CK(cudaEventRecord(e0, st));
-  decode_device(c, dc, B, T, dw, dp, st);
+  {
+    ConvErrScope scope(derr);
+    decode_device(c, dc, B, T, dw, dp, st);
+  }
   CK(cudaEventRecord(e1, st));
   if (wave) CK(cudaMemcpyAsync(wave, dw, (size_t)B * n * 4, cudaMemcpyDeviceToHost, st));
   if (pcm) CK(cudaMemcpyAsync(pcm, dp, (size_t)B * n * 2, cudaMemcpyDeviceToHost, st));
+  CK(cudaMemcpyAsync(&herr, derr, sizeof(int), cudaMemcpyDeviceToHost, st));
   CK(cudaFreeAsync(dc, st));
+  CK(cudaFreeAsync(derr, st));
   if (dw) CK(cudaFreeAsync(dw, st));
   if (dp) CK(cudaFreeAsync(dp, st));
   CK(cudaStreamSynchronize(st));
-  conv_check_err();
   CK(cudaEventElapsedTime(&g_codec_ms, e0, e1));
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
+  conv_check_err(herr, "codec decode");
 }
 
 extern "C" q3t_status q3t_codec_last_ms(float *ms) {
@@ -1994,11 +1989,12 @@ extern "C" q3t_status q3t_codec_last_ms(float *ms) {
 }
 
 // ---------------------------------------------------------------------------
-// decode without allocation: the codes, every intermediate buffer and the
-// output samples are carved out of one file-scope device array.  No part of it
-// needs to start at zero: each kernel writes its output buffer before a later
-// kernel reads it.  Calls that overlap in time on one device (from any thread
-// or stream) share the array and race.
+// decode without allocation: the call's convolution timeout word, the codes,
+// every intermediate buffer and the output samples are carved out of one
+// file-scope device array.  Only the timeout word must start at zero (it is
+// cleared on the caller's stream before the kernels); every other buffer is
+// written by a kernel before a later kernel reads it.  Calls that overlap in
+// time on one device (from any thread or stream) share the array and race.
 // ---------------------------------------------------------------------------
 constexpr int64_t kStaticScratchBytes = 48ll << 20;  // one 24-frame window at B = 1 needs 42.7 MiB
 constexpr int kStaticMaxDevices = 64;
@@ -2027,8 +2023,9 @@ static void codec_decode_static(q3t_model *m, const int64_t *codes, int B, int T
   if (n <= 0) FAIL(Q3T_INVALID_INPUT, "T = %d frames decode to no samples", T);
   CodecScratch ws = codec_scratch(c, B, T);
   auto up = [](int64_t b) { return (b + 255) & ~(int64_t)255; };
-  const int64_t codes_b = up(ncodes * 8), wave_b = wave ? up(B * n * 4) : 0, pcm_b = pcm ? up(B * n * 2) : 0;
-  int64_t need = codes_b + wave_b + pcm_b;
+  const int64_t err_b = 256, codes_b = up(ncodes * 8), wave_b = wave ? up(B * n * 4) : 0,
+                pcm_b = pcm ? up(B * n * 2) : 0;
+  int64_t need = err_b + codes_b + wave_b + pcm_b;
   for (int i = 0; i < CodecScratch::N; i++) need += up(ws.bytes[i]);
   if (need > kStaticScratchBytes)
     FAIL(Q3T_INVALID_INPUT,
@@ -2036,7 +2033,8 @@ static void codec_decode_static(q3t_model *m, const int64_t *codes, int B, int T
          "(about 26 frames in total)",
          B, T, (long long)need, (long long)kStaticScratchBytes);
   unsigned char *base = static_scratch(m->device);
-  int64_t off = 0;
+  int *derr = (int *)base;
+  int64_t off = err_b;
   int64_t *dc = (int64_t *)(base + off);
   off += codes_b;
   float *dw = wave ? (float *)(base + off) : nullptr;
@@ -2047,12 +2045,18 @@ static void codec_decode_static(q3t_model *m, const int64_t *codes, int B, int T
     ws.p[i] = base + off;
     off += up(ws.bytes[i]);
   }
+  int herr = 0;
+  CK(cudaMemsetAsync(derr, 0, sizeof(int), st));
   CK(cudaMemcpyAsync(dc, codes, ncodes * 8, cudaMemcpyHostToDevice, st));
-  decode_with(c, ws, dc, B, T, dw, dp, st);
+  {
+    ConvErrScope scope(derr);
+    decode_with(c, ws, dc, B, T, dw, dp, st);
+  }
   if (wave) CK(cudaMemcpyAsync(wave, dw, (size_t)B * n * 4, cudaMemcpyDeviceToHost, st));
   if (pcm) CK(cudaMemcpyAsync(pcm, dp, (size_t)B * n * 2, cudaMemcpyDeviceToHost, st));
+  CK(cudaMemcpyAsync(&herr, derr, sizeof(int), cudaMemcpyDeviceToHost, st));
   CK(cudaStreamSynchronize(st));
-  conv_check_err();
+  conv_check_err(herr, "static codec decode");
 }
 
 // ---------------------------------------------------------------------------
@@ -2100,7 +2104,8 @@ struct StreamState {
     std::vector<PendWin> w;
   };
   std::vector<PendGroup> pend;     // gathered windows whose decode is not launched yet
-  int *h_err = nullptr;            // pinned copy of the convolutions' timeout word, taken with the work
+  int *d_err = nullptr;            // the batch's convolution timeout word
+  int *h_err = nullptr;            // its pinned copy, taken with the work
 };
 static std::map<q3t_batch *, StreamState> g_streams;
 
@@ -2137,18 +2142,27 @@ void codec_stream_init(q3t_model *m, q3t_batch *b) {
   int64_t nmax = 0;
   codec_out_len(c, chunk + ctx, &nmax);
   stream_capacity(S, (size_t)Bw * nq * (chunk + ctx), (size_t)Bw * std::max<int64_t>(nmax, 1));
-  for (int Tw : {chunk, chunk + ctx}) {
-    int64_t nout = 0;
-    codec_out_len(c, Tw, &nout);
-    if (nout <= 0) continue;
-    CK(cudaMemsetAsync(S.d_codes, 0, (size_t)Bw * nq * Tw * 8, S.cst));
-    decode_device(c, S.d_codes, Bw, Tw, S.d_wave, nullptr, S.cst);
-  }
+  CK(cudaMalloc(&S.d_err, sizeof(int)));
+  CK(cudaMemsetAsync(S.d_err, 0, sizeof(int), S.cst));
   CK(cudaHostAlloc(&S.h_err, sizeof(int), cudaHostAllocDefault));
   *S.h_err = 0;
+  g_streams[b] = S;  // codec_stream_free releases it if the warm-up below fails
+  {
+    ConvErrScope scope(S.d_err);
+    for (int Tw : {chunk, chunk + ctx}) {
+      int64_t nout = 0;
+      codec_out_len(c, Tw, &nout);
+      if (nout <= 0) continue;
+      CK(cudaMemsetAsync(S.d_codes, 0, (size_t)Bw * nq * Tw * 8, S.cst));
+      decode_device(c, S.d_codes, Bw, Tw, S.d_wave, nullptr, S.cst);
+    }
+  }
+  CK(cudaMemcpyAsync(S.h_err, S.d_err, sizeof(int), cudaMemcpyDeviceToHost, S.cst));
   CK(cudaStreamSynchronize(S.cst));
-  conv_check_err();
-  g_streams[b] = S;
+  const int e = *S.h_err;
+  *S.h_err = 0;
+  CK(cudaMemsetAsync(S.d_err, 0, sizeof(int), S.cst));
+  conv_check_err(e, "streaming codec warm-up");
 }
 
 // Completes the codec work in flight (see above); samples (nullable) counts
@@ -2162,6 +2176,7 @@ void codec_stream_launch(q3t_batch *b) {
   CodecModel *c = b->m->codec;
   CK(cudaStreamWaitEvent(S.cst, S.ev_codes, 0));
   size_t hoff = 0;
+  ConvErrScope scope(S.d_err);
   for (const auto &g : S.pend) {
     if (g.nout > 0) decode_device(c, g.dc, g.Bw, g.Tw, g.dw, nullptr, S.cst);
     for (int i = 0; i < (int)g.w.size(); i++) {
@@ -2177,7 +2192,7 @@ void codec_stream_launch(q3t_batch *b) {
     }
   }
   S.pend.clear();
-  if (int *w = conv_err_word()) CK(cudaMemcpyAsync(S.h_err, w, sizeof(int), cudaMemcpyDeviceToHost, S.cst));
+  CK(cudaMemcpyAsync(S.h_err, S.d_err, sizeof(int), cudaMemcpyDeviceToHost, S.cst));
   CK(cudaEventRecord(S.ev_done, S.cst));
   S.inflight = true;
 }
@@ -2194,8 +2209,8 @@ void codec_stream_join(q3t_batch *b, int64_t *samples) {
     *S.h_err = 0;
     S.out.clear();
     S.inflight = false;
-    if (int *w = conv_err_word()) CK(cudaMemsetAsync(w, 0, sizeof(int), S.cst));
-    FAIL(Q3T_DEVICE_TIMEOUT, "streaming codec: a bounded device wait gave up (code %#x)", e);
+    CK(cudaMemsetAsync(S.d_err, 0, sizeof(int), S.cst));
+    conv_check_err(e, "streaming codec");
   }
   for (const StreamOut &o : S.out) {
     if (b->desc.keep_output) memcpy(o.r->wave.data() + o.dst, S.h_wave + o.src, (size_t)o.n * 4);
@@ -2217,6 +2232,7 @@ void codec_stream_free(q3t_batch *b) {
   if (S.d_wave) cudaFree(S.d_wave);
   if (S.h_wave) cudaFreeHost(S.h_wave);
   if (S.h_err) cudaFreeHost(S.h_err);
+  if (S.d_err) cudaFree(S.d_err);
   if (S.ev_codes) cudaEventDestroy(S.ev_codes);
   if (S.ev_done) cudaEventDestroy(S.ev_done);
   if (S.cst) cudaStreamDestroy(S.cst);
@@ -2367,6 +2383,16 @@ extern "C" q3t_status q3t_codec_decode_static(q3t_model *m, const int64_t *codes
     set_error("q3t_codec_decode_static: null argument");
     return Q3T_INVALID_INPUT;
   }
+  // the calling thread's current device is put back on every return
+  struct DeviceRestore {
+    int dev = -1;
+    DeviceRestore() {
+      if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+    }
+    ~DeviceRestore() {
+      if (dev >= 0) cudaSetDevice(dev);
+    }
+  } restore;
   try {
     CK(cudaSetDevice(m->device));
     if (!m->has_codec || !m->codec) FAIL(Q3T_INVALID_INPUT, "model has no codec");

@@ -1404,6 +1404,7 @@ extern "C" q3t_status q3t_batch_create(q3t_model *m, const q3t_batch_desc *d, q3
     if (d->codec_mode == 2) codec_stream_init(m, b);
   });
   if (rc != Q3T_OK) {
+    if (d->codec_mode == 2) codec_stream_free(b);
     batch_destroy(b);
     delete b;
     return rc;
