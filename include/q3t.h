@@ -342,6 +342,17 @@ q3t_status q3t_batch_pending(q3t_batch *b, int *queued, int *active);
 q3t_status q3t_batch_stream(q3t_batch *b, void **stream);
 void q3t_batch_free(q3t_batch *b);
 
+/* Test hook of sample_token (tts_qwen3_tts/src/model/talker/infer/sampling.rs:
+ * 33-90): runs the device sampler of the decode frames on one row of logits
+ * [vocab] (vocab <= 4096) with the suppress list applied, using the given
+ * uniform draw u in [0, 1) for the categorical step instead of the on-device
+ * counter hash, so a test can compare it with a host restatement fed the
+ * same u.  *token receives the pick; kept (nullable) [vocab] receives 1 for
+ * every token that is still a candidate after suppress, top-k and top-p. */
+q3t_status q3t_sample_logits(q3t_model *model, const float *logits, int vocab, const q3t_sampling *sampling,
+                             const int64_t *suppress_ids, int num_suppress, double u, int64_t *token,
+                             uint8_t *kept);
+
 /* ------------------------------- misc ----------------------------------- */
 /* Struct layout as this library was compiled (no reference counterpart: the
  * reference is one Rust crate, so its structs need no cross-language check).

@@ -413,7 +413,12 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
     b->mk_attn = ar.zalloc<uint2>((size_t)kMkMaxTok * 128 *
                                   std::max(tc.talker.num_attention_heads, tc.predictor.num_attention_heads));
     b->mk_part = ar.zalloc<uint2>((size_t)kMkMaxTok * mkv * kAttnMaxUnits * 2 * kMkPartLd);
-    b->mk_ctr = ar.zalloc<unsigned>(2);
+    b->mk_ctr = ar.zalloc<unsigned>(4);
+    // bounded-wait tests: Q3T_WAIT_POLLS sets the poll limit of the tagged
+    // waits, Q3T_TEST_STALL_WAITS=1 makes every CTA wait on a word nothing
+    // sets, so the wait runs out and the call returns Q3T_DEVICE_TIMEOUT
+    if (const char *e = getenv("Q3T_WAIT_POLLS")) b->wait_polls = std::max(0, atoi(e));
+    if (const char *e = getenv("Q3T_TEST_STALL_WAITS")) b->stall_waits = e[0] == '1';
     const unsigned epoch1 = 1u;  // tags of epoch 0 would match the zero-filled buffers
     CK(cudaMemcpy(b->mk_ctr, &epoch1, sizeof epoch1, cudaMemcpyHostToDevice));
   }
@@ -1155,6 +1160,14 @@ static void admit(q3t_batch *b, int *admitted) {
     if (s < 0) break;
     Req *r = b->queue.front();
     const int need = (r->S + kPage - 1) / kPage + 1;
+    if (need > b->n_pages || r->S + 1 > kMaxSeq) {  // can never fit: fail it, keep serving the queue
+      b->queue.pop_front();
+      r->state = 3;
+      r->fail_status = Q3T_OUT_OF_PAGES;
+      r->error = "prompt of " + std::to_string(r->S) + " tokens needs " + std::to_string(need) +
+                 " KV pages; the pool holds " + std::to_string(b->n_pages);
+      continue;
+    }
     if ((int)b->free_pages.size() < need) break;  // wait for pages
     b->queue.pop_front();
     r->slot = s;
@@ -1164,6 +1177,7 @@ static void admit(q3t_batch *b, int *admitted) {
       prefill(b, r);
     } catch (const Status &st) {
       r->state = 3;
+      r->fail_status = st.code;
       r->error = g_err;
       release(b, r);
       continue;
@@ -1230,8 +1244,6 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
     }
     act.push_back(r);
   }
-  const int B = (int)act.size();
-  S.active = B;
   b->frame_timed = false;
   auto report = [&] {
     CK(cudaEventRecord(b->ev1, b->st));
@@ -1247,6 +1259,26 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
     b->h2d = b->d2h = 0;
     if (stats) *stats = S;
   };
+  // KV pages for this frame's token; a request that cannot get one fails
+  // alone (the reference slides its 4096-entry window here, kv.rs:109-132;
+  // this build stops the request with an explicit error) and the others run
+  {
+    size_t k = 0;
+    for (Req *r : act) {
+      if (r->cache_len + 1 > kMaxSeq || r->step_idx >= b->maxF || !ensure_pages(b, r, r->cache_len + 1)) {
+        r->state = 3;
+        r->fail_status = Q3T_OUT_OF_PAGES;
+        r->error = "request " + std::to_string(r->id) + ": KV capacity exhausted at " +
+                   std::to_string(r->cache_len) + " tokens";
+        release(b, r);
+        continue;
+      }
+      act[k++] = r;
+    }
+    act.resize(k);
+  }
+  const int B = (int)act.size();
+  S.active = B;
   if (B == 0) {
     if (b->desc.codec_mode == 2 && b->m->has_codec) codec_stream_join(b, &S.samples);
     report();
@@ -1255,11 +1287,6 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
   int *hm = b->h_meta;
   for (int i = 0; i < B; i++) {
     Req *r = act[i];
-    if (r->cache_len + 1 > kMaxSeq || r->step_idx >= b->maxF || !ensure_pages(b, r, r->cache_len + 1)) {
-      // the reference slides its 4096-entry window here (kv.rs:109-132); this
-      // build stops the request with an explicit error instead
-      FAIL(Q3T_OUT_OF_PAGES, "request %lld: KV capacity exhausted at %d tokens", (long long)r->id, r->cache_len);
-    }
     hm[b->off_slot() + i] = r->slot;
     hm[b->off_tpos() + i] = r->cache_len;
     hm[b->off_frame() + i] = r->step_idx;
@@ -1542,7 +1569,8 @@ extern "C" q3t_status q3t_session_start(q3t_model *m, const q3t_session_desc *d,
     s->r = new_request(b, d, nullptr);
     b->queue.push_back(s->r);
     admit(b, nullptr);
-    if (s->r->state == 3) FAIL(Q3T_INVALID_INPUT, "%s", s->r->error.c_str());
+    if (s->r->state == 3) FAIL(s->r->fail_status, "%s", s->r->error.c_str());
+    if (s->r->state != 1) FAIL(Q3T_OUT_OF_PAGES, "prompt of %d tokens does not fit the KV pool", s->r->S);
   });
   if (rc != Q3T_OK) {
     q3t_batch_free(b);
@@ -1565,7 +1593,7 @@ static q3t_status session_step(q3t_session *s, const int64_t *forced, float *tl,
     CK(cudaSetDevice(b->m->device));
     if (state) *state = 0;
     if (r->state == 2 || r->finished) return;  // Ok(None)
-    if (r->state == 3) FAIL(Q3T_INVALID_INPUT, "%s", r->error.c_str());
+    if (r->state == 3) FAIL(r->fail_status, "%s", r->error.c_str());
     if (r->eos_seen) {
       if (r->step_idx == 0) {
         r->state = 3;
@@ -1590,6 +1618,7 @@ static q3t_status session_step(q3t_session *s, const int64_t *forced, float *tl,
       CK(cudaMemcpyAsync(b->d_thist + (size_t)sl * b->hist_cap + f, &c0, 4, cudaMemcpyHostToDevice, b->st));
     }
     batch_step(b, nullptr);
+    if (r->state == 3) FAIL(r->fail_status, "%s", r->error.c_str());
     if (tl) CK(cudaMemcpyAsync(tl, b->tlog, (size_t)b->V * 4, cudaMemcpyDeviceToHost, b->st));
     if (pl)
       for (int j = 0; j < G - 1; j++)
@@ -1686,7 +1715,7 @@ extern "C" q3t_status q3t_session_decode_embeds(q3t_session *s, const float *emb
       const auto prog = mk_program(b, MKP_TALKER_DECODE);
       MkArgs ma{prog.first, prog.second,
                 TokView{b->d_meta + M_NTOK_B, b->d_meta + b->off_slot(), b->d_meta + b->off_tpos(), 0}, b->mk_ctr,
-                b->d_err, nullptr};
+                b->d_err, nullptr, b->wait_polls, b->stall_waits ? (const int *)(b->mk_ctr + 2) : nullptr};
       const char *tr = getenv("Q3T_MK_TRACE");  // profiling: per-stage device timestamps to this file
       if (tr && tr[0]) {
         const size_t nt = (size_t)b->mk_grid * prog.second * 8;
@@ -1955,6 +1984,85 @@ extern "C" q3t_status q3t_text_dims(const q3t_model *m, int *text_vocab, int *te
 }
 
 // ----------------------------------------------------------------------------
+// The device sampler on one row of logits with a given uniform draw (test
+// hook of sample_token, talker/infer/sampling.rs:33-90): the same k_sample the
+// decode frames run, with the draw and the candidate mask exposed.
+extern "C" q3t_status q3t_sample_logits(q3t_model *m, const float *logits, int vocab, const q3t_sampling *smp,
+                                        const int64_t *suppress, int n_suppress, double u, int64_t *token,
+                                        uint8_t *kept) {
+  if (!m || !logits || !smp || !token || vocab <= 0 || vocab > kSampleMaxV || n_suppress < 0 ||
+      (n_suppress > 0 && !suppress) || !(u >= 0.0 && u < 1.0)) {
+    set_error("q3t_sample_logits: bad argument (vocab 1..%d, u in [0, 1))", kSampleMaxV);
+    return Q3T_INVALID_INPUT;
+  }
+  return guard([&] {
+    CK(cudaSetDevice(m->device));
+    cudaStream_t st;
+    CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    struct Buf {
+      float *lg, *row;
+      int64_t *sup, *codes;
+      SampleParams *params;
+      int *ntok, *zero, *sup_on;
+      double *u;
+      uint8_t *kept;
+    } d{};
+    const size_t nsup = (size_t)std::max(n_suppress, 1);
+    const size_t bytes = (size_t)vocab * 8 + nsup * 8 + 8 + 2 * sizeof(SampleParams) + 16 + 8 + (size_t)vocab + 256;
+    unsigned char *base = nullptr;
+    CK(cudaMallocAsync((void **)&base, bytes, st));
+    unsigned char *p = base;
+    auto take = [&](size_t n) {
+      unsigned char *r = p;
+      p += (n + 15) & ~(size_t)15;
+      return r;
+    };
+    d.lg = (float *)take((size_t)vocab * 4);
+    d.row = (float *)take((size_t)vocab * 4);
+    d.sup = (int64_t *)take(nsup * 8);
+    d.codes = (int64_t *)take(8);
+    d.params = (SampleParams *)take(2 * sizeof(SampleParams));
+    d.ntok = (int *)take(4);
+    d.zero = (int *)take(4);
+    d.sup_on = (int *)take(4);
+    d.u = (double *)take(8);
+    d.kept = (uint8_t *)take((size_t)vocab);
+    SampleParams hp[2] = {to_params(*smp), to_params(*smp)};
+    const int one = 1, zero = 0;
+    CK(cudaMemcpyAsync(d.lg, logits, (size_t)vocab * 4, cudaMemcpyHostToDevice, st));
+    if (n_suppress) CK(cudaMemcpyAsync(d.sup, suppress, (size_t)n_suppress * 8, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(d.params, hp, sizeof hp, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(d.ntok, &one, 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(d.zero, &zero, 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(d.sup_on, &one, 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(d.u, &u, 8, cudaMemcpyHostToDevice, st));
+    SampleArgs a{};
+    a.part = Part{d.lg, 1, 0, vocab};
+    a.logits = d.row;
+    a.ldl = vocab;
+    a.V = vocab;
+    a.ntok = d.ntok;
+    a.slot = d.zero;
+    a.params = d.params;
+    a.suppress = n_suppress ? d.sup : nullptr;
+    a.n_suppress = n_suppress;
+    a.sup_on = d.sup_on;
+    a.codes = d.codes;
+    a.G = 1;
+    a.col = 0;
+    a.frame = d.zero;
+    a.u = d.u;
+    a.kept = d.kept;
+    sample(a, 1, st);
+    check_launches();
+    CK(cudaMemcpyAsync(token, d.codes, 8, cudaMemcpyDeviceToHost, st));
+    if (kept) CK(cudaMemcpyAsync(kept, d.kept, (size_t)vocab, cudaMemcpyDeviceToHost, st));
+    CK(cudaFreeAsync(base, st));
+    CK(cudaStreamSynchronize(st));
+    CK(cudaStreamDestroy(st));
+  });
+}
+
 extern "C" const char *q3t_last_error(void) { return q3t::g_err.c_str(); }
 extern "C" const char *q3t_version(void) { return "q3t-b200 0.1 (sm_100a)"; }
 extern "C" int64_t q3t_kernel_launches(void) { return q3t::g_launches; }

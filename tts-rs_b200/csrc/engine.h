@@ -124,6 +124,7 @@ struct Req {
   int64_t samples = 0;
   int64_t first_token = -1, first_token_raw = -1;
   std::string error;
+  q3t_status fail_status = Q3T_INVALID_INPUT;  // the status of the failure (state 3)
 };
 
 struct GraphEntry {
@@ -230,7 +231,9 @@ struct q3t_batch {
   uint2 *mk_act = nullptr;   // [kMkMaxTok][max intermediate] tagged SwiGLU rows
   uint2 *mk_attn = nullptr;  // [kMkMaxTok][max heads x 128] tagged attention output rows
   uint2 *mk_part = nullptr;  // [kMkMaxTok][max kv heads][kAttnMaxUnits][2][kMkPartLd] tagged attention partials
-  unsigned *mk_ctr = nullptr;  // launch epoch, finished CTAs
+  unsigned *mk_ctr = nullptr;  // launch epoch, finished CTAs, a word nothing sets (the stall test's flag)
+  int wait_polls = 0;          // poll limit of k_mk's tagged-data waits (0: the kernel's default)
+  bool stall_waits = false;    // k_mk first waits on the never-set word (timeout tests)
   std::map<int, std::pair<q3t::MkStage *, int>> mk_progs;
   int step_counter = 0;
   // requests

@@ -505,7 +505,6 @@ Q3T_DEV void d_attn(const AttnArgs &a, int tid, int warp0, int nwarps, AttnSmem 
 // temperature / top-k / top-p / categorical; teacher forcing; history / EOS.
 // Block-wide.  lg/sv/si: shared arrays of kSampleMaxV entries; rv/ri: 32.
 // ---------------------------------------------------------------------------
-constexpr int kSampleMaxV = 4096;
 
 Q3T_DEV uint64_t mix64(uint64_t z) {
   z += 0x9E3779B97F4A7C15ull;
@@ -573,6 +572,9 @@ Q3T_DEV void d_sample(const SampleArgs &a, int t, float *lg, float *sv, int *si,
     __syncthreads();
   }
   int tok = 0;
+  if (a.kept && !P.do_sample) {
+    for (int i = tid; i < V; i += blockDim.x) a.kept[(size_t)t * a.ldl + i] = isfinite(lg[i]) ? 1 : 0;
+  }
   if (!P.do_sample) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
@@ -636,6 +638,9 @@ Q3T_DEV void d_sample(const SampleArgs &a, int t, float *lg, float *sv, int *si,
       }
       __syncthreads();
     }
+    if (a.kept) {
+      for (int i = tid; i < V; i += blockDim.x) a.kept[(size_t)t * a.ldl + i] = isfinite(lg[i]) ? 1 : 0;
+    }
     if (tid == 0) {
       float mx = -INFINITY;
       for (int i = 0; i < V; i++) mx = fmaxf(mx, lg[i]);
@@ -643,7 +648,7 @@ Q3T_DEV void d_sample(const SampleArgs &a, int t, float *lg, float *sv, int *si,
       for (int i = 0; i < V; i++) sum += expf(lg[i] - mx);
       const uint64_t step = (uint64_t)(a.step_seed + (a.seed_p ? *a.seed_p : 0));
       const uint64_t r = mix64(P.seed ^ mix64(step * 131ull + (uint64_t)a.col) ^ ((uint64_t)s << 40));
-      const double u = (double)(r >> 11) * (1.0 / 9007199254740992.0);
+      const double u = a.u ? a.u[t] : (double)(r >> 11) * (1.0 / 9007199254740992.0);
       const double target = u * sum;
       double cum = 0.0;
       tok = V - 1;

@@ -191,6 +191,8 @@ struct AttnArgs {
 void attention(const uint16_t *q, KVView kv, int layer, TokView tv, int max_tok, int nh, int pw,
                int max_units, AttnWork ws, uint16_t *out, cudaStream_t st);
 
+constexpr int kSampleMaxV = 4096;  // widest vocabulary the sampler handles
+
 struct SampleParams {
   int do_sample;
   float temperature;
@@ -235,6 +237,9 @@ struct SampleArgs {
   int step_seed;               // added to *seed_p (device step counter, nullable)
   const int *seed_p;
   int32_t *raw;                // [slot][max_frames][G] sampled tokens before forcing, or null
+  const double *u;             // nullable: [t] categorical draws in [0, 1) instead of the counter hash
+  uint8_t *kept;               // nullable: [t][ldl] 1 where a token stays a candidate after suppress,
+                               // top-k and top-p
 };
 void sample(const SampleArgs &a, int max_tok, cudaStream_t st);
 

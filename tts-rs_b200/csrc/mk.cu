@@ -39,7 +39,8 @@ struct alignas(16) MkMisc {
   float corr[2];
   unsigned epoch;
   int abort;  // set once any wait of this CTA gave up: later waits are skipped so the launch ends quickly
-  int pad[2];
+  int polls;  // poll limit of the tagged-data waits
+  int pad;
   uint64_t full[kMkSlots], empty[kMkSlots];
 };
 
@@ -106,7 +107,7 @@ Q3T_DEV void st_tag(uint2 *p, float v, unsigned tag) {
 // One more poll of a tagged wait?  false once the CTA gave up (or now gives up).
 Q3T_DEV bool poll_again(MkMisc &M, int &k, uint32_t &err) {
   if (*(volatile int *)&M.abort) return false;
-  if (++k >= kMkPolls) {
+  if (++k >= M.polls) {
     err |= 1u << 8;
     *(volatile int *)&M.abort = 1;
     return false;
@@ -221,16 +222,25 @@ Q3T_DEV void attn_unit_of(const MkPlan &P, int u, int &t, int &h, int &j, int &p
 
 // ---- producer: one thread streams every stage's bytes into the ring -------
 
+// Once the CTA has given up (M.abort) the producer issues nothing more: the
+// consumers then skip their waits and may release a slot whose copy has not
+// landed, so a later copy into that slot could overlap it.  The abort check
+// after the slot wait sees every abort made before the consumers released the
+// slot (their arrive is a release, the wait an acquire), so at most one copy
+// per slot is ever in flight and the kernel's final wait on each slot's last
+// chunk covers every copy issued.
 Q3T_DEV void produce(const MkArgs &a, unsigned char *ring, MkMisc &M, int T, uint32_t *last_chunk) {
   const int c = blockIdx.x, G = gridDim.x;
   uint32_t i = 0;
   uint32_t err = 0;
   auto acquire_slot = [&](uint32_t bytes) -> unsigned char * {
     const int s = (int)(i % kMkSlots);
-    if (!*(volatile int *)&M.abort && !mbar_sleep_wait(&M.empty[s], ((i / kMkSlots) & 1u) ^ 1u)) {
+    if (*(volatile int *)&M.abort) return nullptr;
+    if (!mbar_sleep_wait(&M.empty[s], ((i / kMkSlots) & 1u) ^ 1u)) {
       err |= 1u << 9;
       *(volatile int *)&M.abort = 1;
     }
+    if (*(volatile int *)&M.abort) return nullptr;
     mbar_expect_tx(&M.full[s], bytes);
     last_chunk[s] = i;
     i++;
@@ -248,6 +258,7 @@ Q3T_DEV void produce(const MkArgs &a, unsigned char *ring, MkMisc &M, int T, uin
         const int q = gemv_chunk_end(g, p, r1), np = q - p;
         const int s = (int)(i % kMkSlots);
         unsigned char *dst = acquire_slot((uint32_t)(np * rb * (g.pairs ? 2 : 1)));
+        if (!dst) goto done;
         if (p == r0) stamp(a, si, 6);
         if (g.pairs) {
           const size_t rg = (size_t)128 * (p / 64) + (p % 64);
@@ -275,6 +286,7 @@ Q3T_DEV void produce(const MkArgs &a, unsigned char *ring, MkMisc &M, int T, uin
           for (int e = 0; e < kMkChunkPages; e++) pages[e] = e < np ? pt[p + e] : 0;
           const int s = (int)(i % kMkSlots);
           unsigned char *dst = acquire_slot((uint32_t)np * 8192u);
+          if (!dst) goto done;
           if (p == pb && u == c) stamp(a, si, 6);
           for (int e = 0; e < np; e++) {
             const size_t off = ((size_t)pages[e] * at.kv.n_kv + h) * (16 * 128);
@@ -285,6 +297,7 @@ Q3T_DEV void produce(const MkArgs &a, unsigned char *ring, MkMisc &M, int T, uin
       }
     }
   }
+done:
   if (err && a.err) atomicOr(a.err, (int)err);
 }
 
@@ -753,6 +766,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) k_mk(const __grid_constant__ Mk
       last_chunk[s] = 0xffffffffu;
     }
     M.abort = 0;
+    M.polls = a.polls > 0 ? a.polls : kMkPolls;
     M.epoch = a.ctr[0];
     fence_mbar_init();
   }
@@ -764,6 +778,11 @@ __global__ void __launch_bounds__(kMkThreads, 1) k_mk(const __grid_constant__ Mk
     __syncwarp();
   } else {
     uint32_t ci = 0;
+    if (a.stall && threadIdx.x == 0) {  // a plain global-memory wait for a word nothing sets
+      int k = 0;
+      while (*(volatile const int *)a.stall != 1 && poll_again(M, k, err)) {
+      }
+    }
     constexpr int n16 = sizeof(MkStage) / 16;
     static_assert(sizeof(MkStage) % 16 == 0, "MkStage is copied in 16-byte pieces");
     for (int si = 0; si < a.n; si++) {

@@ -111,6 +111,9 @@ struct MkArgs {
   unsigned long long *trace;  // nullable: [grid][n][8] globaltimer ns per CTA and stage: inputs ready,
                               // X staged, first chunk landed, stage done; producer: stage reached,
                               // first chunk issued
+  int polls;               // polls of a tagged-data wait before it gives up (<= 0: the default, ~0.25 s)
+  const int *stall;        // nullable: each CTA first waits for *stall == 1, a word nothing sets, so the
+                           // wait runs out (tests of the timeout path; null in production)
 };
 
 // Dynamic shared memory of k_mk.

@@ -106,6 +106,7 @@ EXPORTS = [
     "q3t_kernel_launches", "q3t_text_project", "q3t_text_dims",
     "q3t_safetensors_open", "q3t_tensor_set_list", "q3t_tensor_set_free", "q3t_wav_write",
     "q3t_codec_last_ms", "q3t_session_seed", "q3t_abi_struct", "q3t_abi_field",
+    "q3t_sample_logits",
 ]
 
 
@@ -169,6 +170,8 @@ def lib():
         L.q3t_tensor_set_free.restype = None
         L.q3t_wav_write.argtypes = [C.POINTER(C.c_int16), C.c_int64, C.c_int, C.c_int, C.POINTER(C.c_uint8),
                                     C.c_int64, _I64]
+        L.q3t_sample_logits.argtypes = [C.c_void_p, _F, C.c_int, C.POINTER(Sampling), _I64, C.c_int, C.c_double,
+                                        _I64, C.POINTER(C.c_uint8)]
         L.q3t_abi_struct.argtypes = [C.c_char_p, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t),
                                      C.POINTER(C.c_int)]
         L.q3t_abi_field.argtypes = [C.c_char_p, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_size_t),
@@ -378,6 +381,18 @@ class Model:
         ms = C.c_float()
         check(lib().q3t_codec_last_ms(C.byref(ms)))
         return ms.value
+
+    def sample_logits(self, logits, sampling, u, suppress=None):
+        """The device sampler on one row with the uniform draw u: (token, kept mask)."""
+        lg = _f32(logits)
+        sup = None if suppress is None else np.ascontiguousarray(suppress, np.int64)
+        tok = C.c_int64()
+        kept = np.zeros(lg.shape[0], np.uint8)
+        check(lib().q3t_sample_logits(self.h, _fp(lg), lg.shape[0], C.byref(sampling),
+                                      None if sup is None else sup.ctypes.data_as(_I64),
+                                      0 if sup is None else sup.shape[0], float(u), C.byref(tok),
+                                      kept.ctypes.data_as(C.POINTER(C.c_uint8))))
+        return tok.value, kept.astype(bool)
 
     def batch(self, max_active=64, codec_mode=0, chunk_frames=16, left_context=8, keep_output=1):
         return Batch(self, max_active, codec_mode, chunk_frames, left_context, keep_output)
