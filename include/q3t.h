@@ -333,6 +333,13 @@ q3t_status q3t_batch_poll(q3t_batch *b, int64_t request_id, int *state, int64_t 
 q3t_status q3t_batch_take(q3t_batch *b, int64_t request_id, int64_t *codes, int32_t *sampled,
                           int max_frames, float *wave, int64_t max_samples);
 q3t_status q3t_batch_pending(q3t_batch *b, int *queued, int *active);
+/* Test hook (the per-frame logits of TalkerGenerator::step, infer/mod.rs:
+ * 249-283, for one request of a batch): copies the logits of request_id's
+ * token in the last decode frame: talker_logits [vocab] (after the repetition
+ * penalty) and predictor_logits [num_code_groups - 1][cp_vocab] (nullable
+ * each).  INVALID_INPUT if the request was not in that frame.  Valid until
+ * the next q3t_batch_step. */
+q3t_status q3t_batch_logits(q3t_batch *b, int64_t request_id, float *talker_logits, float *predictor_logits);
 /* The CUDA stream (cudaStream_t) the batch's device work is ordered on, for
  * callers that time steps with their own CUDA events.  With codec_mode 2 a
  * step's chunk decodes run on a second, lower-priority stream, overlapped

@@ -1307,6 +1307,8 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
   // graph uses the largest and is captured once per token bucket
   const int mt = bucket_tok(B), ms = kAttnMaxUnits;
   b->h2d += b->meta_n * sizeof(int) + B * sizeof(float *);
+  b->last_ids.resize(B);
+  for (int i = 0; i < B; i++) b->last_ids[i] = act[i]->id;
   enqueue_frame(b, mt, ms);
   // the previous step's codec windows decode on their own stream under this frame
   if (b->desc.codec_mode == 2 && b->m->has_codec) codec_stream_launch(b);
@@ -1516,6 +1518,26 @@ extern "C" q3t_status q3t_batch_take(q3t_batch *b, int64_t id, int64_t *codes, i
   }
   b->reqs.erase(it);
   return Q3T_OK;
+}
+
+extern "C" q3t_status q3t_batch_logits(q3t_batch *b, int64_t id, float *talker_logits, float *predictor_logits) {
+  if (!b) return Q3T_INVALID_INPUT;
+  size_t i = 0;
+  while (i < b->last_ids.size() && b->last_ids[i] != id) i++;
+  if (i == b->last_ids.size()) {
+    set_error("request %lld was not in the last decode frame", (long long)id);
+    return Q3T_INVALID_INPUT;
+  }
+  return guard([&] {
+    CK(cudaSetDevice(b->m->device));
+    if (talker_logits)
+      CK(cudaMemcpyAsync(talker_logits, b->tlog + i * b->V, (size_t)b->V * 4, cudaMemcpyDeviceToHost, b->st));
+    if (predictor_logits)
+      for (int j = 0; j < b->G - 1; j++)
+        CK(cudaMemcpyAsync(predictor_logits + (size_t)j * b->PV, b->plog + ((size_t)j * b->A + i) * b->PV,
+                           (size_t)b->PV * 4, cudaMemcpyDeviceToHost, b->st));
+    CK(cudaStreamSynchronize(b->st));
+  });
 }
 
 extern "C" q3t_status q3t_batch_pending(q3t_batch *b, int *queued, int *active) {

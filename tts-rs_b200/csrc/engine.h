@@ -244,6 +244,7 @@ struct q3t_batch {
   float last_ms = 0.f;
   bool session_mode = false;
   int64_t h2d = 0, d2h = 0;  // bytes copied since the last step report
+  std::vector<int64_t> last_ids;  // request ids of the last decode frame, in token order
 
   int off_slot() const { return q3t::M_HDR; }
   int off_tpos() const { return q3t::M_HDR + A; }

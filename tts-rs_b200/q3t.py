@@ -106,7 +106,7 @@ EXPORTS = [
     "q3t_kernel_launches", "q3t_text_project", "q3t_text_dims",
     "q3t_safetensors_open", "q3t_tensor_set_list", "q3t_tensor_set_free", "q3t_wav_write",
     "q3t_codec_last_ms", "q3t_session_seed", "q3t_abi_struct", "q3t_abi_field",
-    "q3t_sample_logits",
+    "q3t_sample_logits", "q3t_batch_logits",
 ]
 
 
@@ -157,6 +157,7 @@ def lib():
         L.q3t_batch_take.argtypes = [C.c_void_p, C.c_int64, _I64, C.POINTER(C.c_int32), C.c_int, _F,
                                      C.c_int64]
         L.q3t_batch_pending.argtypes = [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        L.q3t_batch_logits.argtypes = [C.c_void_p, C.c_int64, _F, _F]
         L.q3t_batch_stream.argtypes = [C.c_void_p, C.POINTER(C.c_void_p)]
         L.q3t_batch_free.argtypes = [C.c_void_p]
         L.q3t_batch_free.restype = None
@@ -507,10 +508,12 @@ class Batch:
         self._keep = {}
 
     def submit(self, prompt, trailing, pad, max_new_tokens, talker_sampling=None,
-               predictor_sampling=None, eos=-1, suppress=None, forced=None):
+               predictor_sampling=None, eos=-1, suppress=None, forced=None, first_logits=None):
+        """first_logits (nullable): a float32 [vocab] array that receives the
+        logits of the first talker token at admission."""
         keep = []
         d = _session_desc(self.model, prompt, trailing, pad, talker_sampling, predictor_sampling,
-                          max_new_tokens, eos, suppress, -1, None, keep)
+                          max_new_tokens, eos, suppress, -1, first_logits, keep)
         fz = None
         if forced is not None:
             fz = np.ascontiguousarray(forced, np.int64)
@@ -549,6 +552,15 @@ class Batch:
         p = C.c_void_p()
         check(lib().q3t_batch_stream(self.h, C.byref(p)))
         return p.value or 0
+
+    def logits(self, rid):
+        """(talker [vocab], predictor [G-1][cp_vocab]) logits of the request's
+        token in the last decode frame."""
+        tc = self.model.talker_cfg
+        tl = np.zeros(tc.talker.vocab, np.float32)
+        pl = np.zeros((tc.n_groups - 1, tc.predictor.vocab), np.float32)
+        check(lib().q3t_batch_logits(self.h, rid, _fp(tl), _fp(pl)))
+        return tl, pl
 
     def pending(self):
         q, a = C.c_int(), C.c_int()
