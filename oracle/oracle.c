@@ -39,7 +39,18 @@ void orc_bf16_round_array(float *x, int64_t n) {
   for (int64_t i = 0; i < n; i++) x[i] = orc_bf16_round(x[i]);
 }
 
-/* 8-lane dot product: keeps the loop vectorisable without -ffast-math */
+/* 8-lane dot product: keeps the loop vectorisable without -ffast-math.
+ * Built with -DORC_WIDE_ACC (liboracle_wide.so) it accumulates in double
+ * instead: the same math in another summation precision, which measures how
+ * far two correct implementations of this path drift apart through bf16
+ * rounding flips alone (the argmax noise floor on random-init weights). */
+#ifdef ORC_WIDE_ACC
+static float dot8(const float *a, const float *b, int n) {
+  double s = 0.0;
+  for (int k = 0; k < n; k++) s += (double)a[k] * (double)b[k];
+  return (float)s;
+}
+#else
 static float dot8(const float *a, const float *b, int n) {
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   int k = 0;
@@ -50,6 +61,7 @@ static float dot8(const float *a, const float *b, int n) {
   for (int j = 0; j < 8; j++) s += acc[j];
   return s;
 }
+#endif
 
 /* burn::nn::Linear on rows (weights in PyTorch [out][in] layout); the
  * reference runs Linear in the runtime dtype, restated as bf16 inputs with

@@ -122,11 +122,26 @@ class Speaker(C.Structure):
                 ("asp_w", F), ("asp_b", F), ("fc_w", F), ("fc_b", F)]
 
 
+_LIBS = {}
+_VARIANT = "liboracle.so"
+
+
+def use_library(name):
+    """Select the oracle build later calls go through: "liboracle.so" (the
+    oracle) or "liboracle_wide.so" (the same restatement with double
+    accumulation in its dot products, for noise-floor measurements).
+    Returns the previous selection."""
+    global _VARIANT, _LIB
+    prev, _VARIANT = _VARIANT, name
+    _LIB = _LIBS.get(name)
+    return prev
+
+
 def lib():
-    """Load liboracle.so, building it with make if it is missing."""
+    """Load the selected oracle build, running make if it is missing."""
     global _LIB
     if _LIB is None:
-        path = os.path.join(_HERE, "liboracle.so")
+        path = os.path.join(_HERE, _VARIANT)
         if not os.path.exists(path):
             subprocess.run(["make", "-C", _HERE], check=True, capture_output=True)
         L = C.CDLL(path)
@@ -174,6 +189,7 @@ def lib():
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_get_threads.restype = C.c_int
         _LIB = L
+        _LIBS[_VARIANT] = L
     return _LIB
 
 

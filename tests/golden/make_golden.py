@@ -2,7 +2,7 @@
 tests/golden/reference_kats.json.
 
 Run in a container where the reference checkout exists:
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path of the tts-rs checkout>
 
 Each KAT is parsed out of the Rust test it comes from (the file:line is
 recorded next to it), so the oracle is pinned to the reference's numbers,
@@ -115,4 +115,6 @@ def main(ref):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <path of the tts-rs checkout>")
+    main(sys.argv[1])

@@ -336,3 +336,48 @@ def test_codec_decoder(T):
     got = twin_codec_decode(c, w, codes)
     assert got.shape == ref.shape == (c.out_len(T),)
     assert rel_err(got, ref) <= REL_CODEC, rel_err(got, ref)
+
+
+@pytest.mark.slow
+def test_argmax_noise_floor():
+    """How well two correct implementations of the full-depth path can agree
+    on the argmax of seed-0 random-init logits: the oracle against itself
+    built with double accumulation (liboracle_wide.so: the same math and bf16
+    rounding points, another summation precision).  Their logits differ by
+    ~4e-3 RMS through cascading bf16 rounding flips, and the random-init
+    logits have many top-2 gaps below that, so raw argmax agreement sits near
+    99 % (99.05 % over 1158 rows measured when this test was written), under
+    the 99.5 % the path's tolerance names.  The GPU parity tests hold the GPU
+    to this floor; here both builds must agree on every row whose top-2
+    margin exceeds 2e-2."""
+    cfg = S.TalkerConfig()
+    w = S.make_talker_weights(cfg, seed=0)
+    ot = O.OracleTalker(cfg, w)
+
+    def run(variant, seed, frames=8):
+        prev = O.use_library(variant)
+        try:
+            prompt, trailing, pad = S.synthetic_talker_inputs(cfg, 64, seed=seed)
+            codes = S.teacher_codes(frames + 1, seed=seed)
+            og = O.OracleGenerator(ot, prompt, trailing, pad, max_new_tokens=frames + 1,
+                                   forced_first=int(codes[0, 0]))
+            rows = [og.first_logits[None]]
+            for f in range(frames):
+                _, tl, pl, _ = og.step(forced=codes[f])
+                rows += [pl, tl[None]]
+            return rows
+        finally:
+            O.use_library(prev)
+
+    agree = total = 0
+    for seed in range(3):
+        a, b = run("liboracle.so", seed), run("liboracle_wide.so", seed)
+        for ra, rb in zip(a, b):
+            same = ra.argmax(-1) == rb.argmax(-1)
+            top2 = np.sort(ra, -1)[:, -2:]
+            assert same[(top2[:, 1] - top2[:, 0]) > 2e-2].all()
+            agree += int(same.sum())
+            total += len(same)
+    floor = agree / total
+    print(f"\noracle vs wide-accumulation oracle: argmax agreement {floor:.4f} over {total} rows")
+    assert floor >= 0.98
