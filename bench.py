@@ -65,6 +65,9 @@ def parse():
                    help="skip the predictor-loop (B=1/16/64) and codec (T=750, B=1/8) measurements")
     p.add_argument("--c3-frames", type=int, default=512)
     p.add_argument("--kv-pages", type=int, default=8192, help="talker KV pool size (16-token pages)")
+    p.add_argument("--no-steady", action="store_true",
+                   help="time right after the warm-up steps instead of after the first retirements")
+    p.add_argument("--no-drain", action="store_true", help="skip the full-workload run to completion")
     p.add_argument("--profile", action="store_true",
                    help="bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     return p.parse_args()
@@ -277,6 +280,7 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return reference_arm(args, rank, world)
+    args.steady_off = args.no_steady
     import torch
     dist = None
     if world > 1:
@@ -326,6 +330,22 @@ def main():
         submit(b, i)
     for _ in range(args.warmup):
         b.step()
+    # steady state: untimed steps until the first requests retire, so the
+    # timed window holds the workload's mix of admissions (prompt prefill),
+    # decode frames and retirements rather than the initial fill (every rank
+    # takes the same number of steps; bounded by the longest target)
+    fill = 0
+    if not args.steady_off:
+        while fill < 2000:
+            fill += 1
+            if b.step()["retired"] > 0:
+                break
+    if dist:
+        t = torch.tensor([fill], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        for _ in range(int(t.item()) - fill):
+            b.step()
+        fill = int(t.item())
     stream = torch.cuda.ExternalStream(b.stream(), device=local)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # raw nvidia-smi samples of the timed region (the JSON line carries their summary)
@@ -353,7 +373,33 @@ def main():
     step_ms = [s["device_ms"] for s in steps]
     decode_ms = [s["device_ms"] for s in steps if s["admitted"] == 0 and s["samples"] == 0 and s["active"] > 0]
     bytes_ = [step_bytes(s, cfg) for s in steps if s["admitted"] == 0 and s["samples"] == 0 and s["active"] > 0]
+    window = {"fill_steps": fill, "admissions": int(sum(s["admitted"] for s in steps)),
+              "retirements": int(sum(s["retired"] for s in steps))}
     b.close()
+
+    # ---------------- drain: the whole workload of this rank to completion ---
+    drain = None
+    if not args.no_drain:
+        bd = model.batch(max_active=args.max_active, codec_mode=2, chunk_frames=args.chunk,
+                         left_context=args.left_context, keep_output=0)
+        for i in mine:
+            submit(bd, i)
+        streamd = torch.cuda.ExternalStream(bd.stream(), device=local)
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        d0.record(streamd)
+        std = []
+        while True:
+            std.append(bd.step())
+            if bd.pending() == (0, 0):
+                break
+        d1.record(streamd)
+        barrier()
+        bd.close()
+        drain = {"_samples": sum(s["samples"] for s in std), "_dev_s": d0.elapsed_time(d1) / 1e3,
+                 "steps": len(std), "admissions": int(sum(s["admitted"] for s in std)),
+                 "p50_step_ms": round(float(np.percentile([s["device_ms"] for s in std], 50)), 4),
+                 "p99_step_ms": round(float(np.percentile([s["device_ms"] for s in std], 99)), 4)}
 
     # ---------------- e2e: host buffers in and out through the C ABI ---------
     e2e = None
@@ -389,8 +435,16 @@ def main():
     # ---------------- reduce over ranks (the one collective) -----------------
     red = dp.reduce_stats({"samples": (samples, "sum"), "frames": (frames, "sum"), "dev_s": (dev_s, "max"),
                            "e2e_samples": (e2e["_samples"] if e2e else 0, "sum"),
-                           "e2e_wall": (e2e["_wall"] if e2e else 0.0, "max")},
+                           "e2e_wall": (e2e["_wall"] if e2e else 0.0, "max"),
+                           "drain_samples": (drain["_samples"] if drain else 0, "sum"),
+                           "drain_dev_s": (drain["_dev_s"] if drain else 0.0, "max")},
                           device="cuda" if dist else "cpu")
+    if drain:
+        drain = {"workload": f"all {len(reqs)} requests run to completion (this line: {world} GPU(s))",
+                 "value": round(red["drain_samples"] / SAMPLE_RATE / red["drain_dev_s"], 3), "unit": "audio-s/s",
+                 "device_s": round(red["drain_dev_s"], 3), "steps_rank0": drain["steps"],
+                 "admissions_rank0": drain["admissions"], "p50_step_ms_rank0": drain["p50_step_ms"],
+                 "p99_step_ms_rank0": drain["p99_step_ms"]}
     tot_samples, tot_frames, max_dev = red["samples"], red["frames"], red["dev_s"]
     e2e_tot, e2e_wall = red["e2e_samples"], red["e2e_wall"]
     value = tot_samples / SAMPLE_RATE / max_dev
@@ -451,7 +505,11 @@ def main():
             "config": {"workload": WORKLOAD, "requests": args.requests, "max_active_per_gpu": args.max_active,
                        "page_tokens": 16, "codec": f"streaming chunks of {args.chunk} frames, "
                        f"{args.left_context} frames left context", "parallelism": f"dp{world} (replicas)",
-                       "l2_policy": "working set > L2 (talker+predictor weights 1.2 GB per step)"},
+                       "l2_policy": "working set > L2 (talker+predictor weights 1.2 GB per step)",
+                       "window": ("timed from steady state: untimed steps after the warm-up until the first "
+                                  "retirements, so admissions (prompt prefill) and retirements fall inside the "
+                                  "window" if not args.steady_off else "timed right after the warm-up steps"),
+                       "window_counts": window},
             "roofline": {"bound": "hbm", "unit": "GB/s",
                          "kernel": "decode frame step (CUDA graph of talker + predictor kernels)",
                          "achieved": round(ach, 1) if ach else None, "peak": hbm_peak,
@@ -464,6 +522,7 @@ def main():
             "codec_t750": c4,
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "drain": drain,
             "gpu_launches": int(launches),
             "clocks": ck,
         }

@@ -142,6 +142,21 @@ def test_batch16_full_depth_matches_oracle(full):
     _batch_vs_oracle(cfg, model, ot, lens, frames=4, seed0=100)
 
 
+def test_persistent_frame_kernel_matches_oracle(full, monkeypatch):
+    """The code-predictor loop as one persistent launch (k_frame, switched on
+    with Q3T_FRAME_KERNEL=1 at batch creation): 8 requests, 2 frames, the
+    same parity bars.  The launch counter shows the loop ran as one kernel:
+    8 one-chunk prefills (~144 launches each) and 3 frames come to ~1600
+    launches with it and ~2800 with the per-phase kernels (~550 per frame)."""
+    cfg, w, model, ot = full
+    monkeypatch.setenv("Q3T_FRAME_KERNEL", "1")
+    n0 = q3t.kernel_launches()
+    lens = np.random.default_rng([8, 1]).integers(16, 65, size=8)
+    _batch_vs_oracle(cfg, model, ot, lens, frames=2, seed0=500)
+    launches = q3t.kernel_launches() - n0
+    assert launches < 2200, launches
+
+
 def test_batch64_ragged_full_depth_matches_oracle(full):
     """64 active requests with the bench's prompt lengths U[16, 256]: the
     batch-64 frame graph of the bench, 3 teacher-forced frames each."""

@@ -10,6 +10,7 @@
 // max_new_tokens -> talker decode -> codec_head -> repetition penalty ->
 // sample -> EOS check; finalize = codes [G][T].
 #include <cmath>
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -351,8 +352,22 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
   b->tk = ar.alloc<uint16_t>((size_t)b->t_layer_stride * L);
   b->tv = ar.alloc<uint16_t>((size_t)b->t_layer_stride * L);
   for (int p = b->n_pages - 1; p >= 0; p--) b->free_pages.push_back(p);
-  b->h_pt.assign((size_t)A * kPtStride, 0);
+  CK(cudaMallocHost(&b->h_pt, (size_t)A * kPtStride * sizeof(int)));
+  memset(b->h_pt, 0, (size_t)A * kPtStride * sizeof(int));
   b->d_pt = ar.zalloc<int>((size_t)A * kPtStride);
+  {  // request inputs come from a stream-ordered pool that keeps its memory
+    cudaMemPoolProps pp{};
+    pp.allocType = cudaMemAllocationTypePinned;
+    pp.location.type = cudaMemLocationTypeDevice;
+    pp.location.id = m->device;
+    CK(cudaMemPoolCreate(&b->pool, &pp));
+    uint64_t keep = UINT64_MAX;
+    CK(cudaMemPoolSetAttribute(b->pool, cudaMemPoolAttrReleaseThreshold, &keep));
+  }
+  CK(cudaMallocHost(&b->h_init, (size_t)A * sizeof(SlotInit)));
+  b->d_first_eos = ar.zalloc<int>(A);
+  CK(cudaMallocHost(&b->h_first_eos, (size_t)A * sizeof(int)));
+  b->d_zero = ar.zalloc<int>(1);
   // predictor pool: slot s owns pages 2s, 2s+1 (capacity 32 >= num_code_groups + 1)
   const int pnkv = tc.predictor.num_key_value_heads, PL = tc.predictor.num_hidden_layers;
   b->p_layer_stride = (int64_t)2 * A * pnkv * kPage * 128;
@@ -422,6 +437,16 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
     const unsigned epoch1 = 1u;  // tags of epoch 0 would match the zero-filled buffers
     CK(cudaMemcpy(b->mk_ctr, &epoch1, sizeof epoch1, cudaMemcpyHostToDevice));
   }
+  // persistent frame kernel for the predictor loop: off unless
+  // Q3T_FRAME_KERNEL=1 (correct, but measured slower than the per-phase
+  // kernels under programmatic dependent launch; see frame.cu)
+  {
+    const char *e = getenv("Q3T_FRAME_KERNEL");
+    if (e && e[0] == '1' && frame_init(m->device, &b->frame_grid, &b->frame_hc)) {
+      b->use_frame = true;
+      b->frame_bar = ar.zalloc<unsigned>(1);
+    }
+  }
   // metadata
   b->meta_n = M_HDR + 8 * A;
   b->d_meta = ar.zalloc<int>(b->meta_n);
@@ -448,8 +473,13 @@ static void batch_destroy(q3t_batch *b) {
   if (b->h_err) cudaFreeHost(b->h_err);
   for (auto &r : b->reqs)
     for (void *p : {(void *)r.second->d_trailing, (void *)r.second->d_pad, (void *)r.second->d_prompt,
-                    (void *)r.second->d_forced})
-      if (p) cudaFree(p);
+                    (void *)r.second->d_forced, (void *)r.second->d_suppress})
+      if (p) cudaFreeAsync(p, b->st);
+  if (b->st) cudaStreamSynchronize(b->st);
+  if (b->pool) cudaMemPoolDestroy(b->pool);
+  if (b->h_pt) cudaFreeHost(b->h_pt);
+  if (b->h_init) cudaFreeHost(b->h_init);
+  if (b->h_first_eos) cudaFreeHost(b->h_first_eos);
   if (b->h_meta) cudaFreeHost(b->h_meta);
   if (b->h_extra) cudaFreeHost(b->h_extra);
   if (b->h_pmeta) cudaFreeHost(b->h_pmeta);
@@ -998,10 +1028,60 @@ static void enqueue_frame(q3t_batch *b, int mt, int max_units) {
               kv.second.second / kv.second.first, kv.second.second);
   } else {
     // two graphs, the code-predictor loop and the talker step, with an event
-    // between them so a step reports both device times
+    // between them so a step reports both device times; the predictor loop
+    // runs as one persistent k_frame launch where the device can host it
     const int talker_from = (int)pr.size() - m_talker_phases(b);
+    Phase *fp = nullptr;
+    if (b->use_frame) {
+      auto fit = b->frame_progs.find(key);
+      if (fit == b->frame_progs.end()) {
+        bool ok = true;
+        for (int i = 0; i < talker_from && ok; i++) ok = frame_phase_ok(pr[i], b->frame_hc);
+        Phase *d = nullptr;
+        if (ok) {
+          std::vector<Phase> cp(pr.begin(), pr.begin() + talker_from);
+          int next = -1;  // Phase::pad = the next GEMM phase, which the kernel's weight prefetch follows
+          for (int i = talker_from - 1; i >= 0; i--) {
+            cp[i].pad = next;
+            if (cp[i].type == PH_GEMM) next = i;
+          }
+          d = b->ar.alloc<Phase>(talker_from);
+          CK(cudaMemcpyAsync(d, cp.data(), (size_t)talker_from * sizeof(Phase), cudaMemcpyHostToDevice, b->st));
+          CK(cudaStreamSynchronize(b->st));
+        }
+        fit = b->frame_progs.emplace(key, d).first;
+      }
+      fp = fit->second;
+    }
     CK(cudaEventRecord(b->evf[0], b->st));
-    run_graph(b, std::make_tuple(4, mt, max_units), [&] { run_phases(pr.data(), talker_from, b->st); });
+    const char *tr = fp ? getenv("Q3T_FRAME_TRACE") : nullptr;  // profiling: per-phase device timestamps
+    if (tr && tr[0]) {
+      const size_t nt = (size_t)b->frame_grid * talker_from * 8;
+      unsigned long long *d_tr = nullptr;
+      CK(cudaMallocAsync((void **)&d_tr, nt * 8, b->st));
+      CK(cudaMemsetAsync(d_tr, 0, nt * 8, b->st));
+      frame_launch(FrameArgs{fp, talker_from, b->frame_bar, b->d_err, b->frame_hc, d_tr}, b->frame_grid, b->st);
+      check_launches();
+      std::vector<unsigned long long> h(nt);
+      CK(cudaMemcpyAsync(h.data(), d_tr, nt * 8, cudaMemcpyDeviceToHost, b->st));
+      CK(cudaStreamSynchronize(b->st));
+      CK(cudaFreeAsync(d_tr, b->st));
+      if (FILE *f = fopen(tr, "wb")) {
+        const int hdr[2] = {b->frame_grid, talker_from};
+        fwrite(hdr, sizeof hdr, 1, f);
+        std::vector<int> types(talker_from);
+        for (int i = 0; i < talker_from; i++) types[i] = pr[i].type;
+        fwrite(types.data(), sizeof(int), talker_from, f);
+        fwrite(h.data(), 8, nt, f);
+        fclose(f);
+      }
+    } else if (fp)
+      run_graph(b, std::make_tuple(6, mt, max_units), [&] {
+        frame_launch(FrameArgs{fp, talker_from, b->frame_bar, b->d_err, b->frame_hc, nullptr}, b->frame_grid,
+                     b->st);
+      });
+    else
+      run_graph(b, std::make_tuple(4, mt, max_units), [&] { run_phases(pr.data(), talker_from, b->st); });
     CK(cudaEventRecord(b->evf[1], b->st));
     run_graph(b, std::make_tuple(5, mt, max_units),
               [&] { run_phases(pr.data() + talker_from, (int)pr.size() - talker_from, b->st); });
@@ -1018,11 +1098,24 @@ static int alloc_page(q3t_batch *b, Req *r) {
   const int idx = (int)r->pages.size();
   r->pages.push_back(p);
   b->h_pt[(size_t)r->slot * kPtStride + idx] = p;
-  CK(cudaMemcpyAsync(b->d_pt + (size_t)r->slot * kPtStride + idx, &b->h_pt[(size_t)r->slot * kPtStride + idx],
-                     sizeof(int), cudaMemcpyHostToDevice, b->st));
+  b->pt_lo = std::min(b->pt_lo, r->slot);
+  b->pt_hi = std::max(b->pt_hi, r->slot);
   return p;
 }
 
+// Uploads the page-table rows changed since the last upload (one copy from
+// pinned memory, ordered before the kernels that read them).
+static void flush_pages(q3t_batch *b) {
+  if (b->pt_hi < b->pt_lo) return;
+  const size_t off = (size_t)b->pt_lo * kPtStride, n = (size_t)(b->pt_hi - b->pt_lo + 1) * kPtStride;
+  CK(cudaMemcpyAsync(b->d_pt + off, b->h_pt + off, n * sizeof(int), cudaMemcpyHostToDevice, b->st));
+  b->h2d += (int64_t)n * sizeof(int);
+  b->pt_lo = 1 << 30;
+  b->pt_hi = -1;
+}
+
+// Pages for `len` tokens of r; the page-table rows go to the device with the
+// next flush_pages(), which every path calls before its kernels run.
 static bool ensure_pages(q3t_batch *b, Req *r, int len) {
   const int need = (len + kPage - 1) / kPage;
   if (need > kPtStride) return false;
@@ -1036,10 +1129,11 @@ static void release(q3t_batch *b, Req *r) {
   r->pages.clear();
   if (r->slot >= 0) b->slots[r->slot] = nullptr;
   r->slot = -1;
-  for (void *p : {(void *)r->d_trailing, (void *)r->d_pad, (void *)r->d_prompt, (void *)r->d_forced})
-    if (p) cudaFree(p);
+  for (void *p : {(void *)r->d_trailing, (void *)r->d_pad, (void *)r->d_prompt, (void *)r->d_forced,
+                  (void *)r->d_suppress})
+    if (p) CK(cudaFreeAsync(p, b->st));  // stream-ordered: no device-wide synchronisation
   r->d_trailing = r->d_pad = r->d_prompt = nullptr;
-  r->d_forced = nullptr;
+  r->d_forced = r->d_suppress = nullptr;
 }
 
 static SampleParams to_params(const q3t_sampling &s) {
@@ -1056,25 +1150,42 @@ static SampleParams to_params(const q3t_sampling &s) {
 
 // TalkerGenerator::start: prefill the prompt into the request's pages, then
 // codec_head + first sample with the suppress list (infer/mod.rs:135-157).
+// Everything is enqueued on the batch stream without a host round trip: the
+// slot state goes up from pinned staging, teacher forcing of the first token
+// happens in the sampler (forced[slot][0][0]), the sampled token before
+// forcing lands in raw[slot][0][0], and the first token's EOS flag in
+// first_eos[slot], which the step reads back with the frame's own flags.
 static void prefill(q3t_batch *b, Req *r) {
   q3t_model *m = b->m;
   const auto &tc = m->tc;
   const int H = b->H, V = b->V, s = r->slot;
   if (!ensure_pages(b, r, r->S)) FAIL(Q3T_OUT_OF_PAGES, "KV page pool exhausted (prompt of %d tokens)", r->S);
-  // per-slot state
-  SampleParams pp[2] = {to_params(r->ts), to_params(r->cs)};
-  CK(cudaMemcpyAsync(b->d_params + 2 * s, pp, sizeof pp, cudaMemcpyHostToDevice, b->st));
-  CK(cudaMemcpyAsync(b->d_eos + s, &r->eos, sizeof(int64_t), cudaMemcpyHostToDevice, b->st));
-  const int zero = 0, one = 1;
-  CK(cudaMemcpyAsync(b->d_thist_len + s, &zero, sizeof(int), cudaMemcpyHostToDevice, b->st));
+  flush_pages(b);
+  // per-slot state (the staging entry of slot s is reused only after the step that admitted it synchronised)
+  SlotInit &in = b->h_init[s];
+  in.params[0] = to_params(r->ts);
+  in.params[1] = to_params(r->cs);
+  in.eos = r->eos;
+  int64_t ff = r->forced_first;
+  if (ff < 0 && !r->forced.empty()) ff = r->forced[0];
+  in.forced_first = ff;
+  in.forced_first32 = (int32_t)ff;
+  in.zero = 0;
   const int nsup = std::min<int>((int)r->suppress.size(), b->n_suppress_cap);
-  if (nsup) CK(cudaMemcpyAsync(b->d_suppress, r->suppress.data(), nsup * 8, cudaMemcpyHostToDevice, b->st));
-  CK(cudaMemcpyAsync(b->d_sup_on + s, nsup ? &one : &zero, sizeof(int), cudaMemcpyHostToDevice, b->st));
-  const int fc = r->forced.empty() ? 0 : r->max_new;
-  CK(cudaMemcpyAsync(b->d_forced_count + s, &fc, sizeof(int), cudaMemcpyHostToDevice, b->st));
-  if (fc)
+  in.sup_on = nsup ? 1 : 0;
+  in.forced_count = r->forced.empty() ? (ff >= 0 ? 1 : 0) : r->max_new;
+  CK(cudaMemcpyAsync(b->d_params + 2 * s, in.params, sizeof in.params, cudaMemcpyHostToDevice, b->st));
+  CK(cudaMemcpyAsync(b->d_eos + s, &in.eos, sizeof(int64_t), cudaMemcpyHostToDevice, b->st));
+  CK(cudaMemcpyAsync(b->d_thist_len + s, &in.zero, sizeof(int), cudaMemcpyHostToDevice, b->st));
+  if (nsup) CK(cudaMemcpyAsync(b->d_suppress, r->d_suppress, nsup * 8, cudaMemcpyDeviceToDevice, b->st));
+  CK(cudaMemcpyAsync(b->d_sup_on + s, &in.sup_on, sizeof(int), cudaMemcpyHostToDevice, b->st));
+  CK(cudaMemcpyAsync(b->d_forced_count + s, &in.forced_count, sizeof(int), cudaMemcpyHostToDevice, b->st));
+  if (!r->forced.empty())
     CK(cudaMemcpyAsync(b->d_forced + (size_t)s * b->maxF * b->G, r->d_forced, r->forced.size() * 8,
                        cudaMemcpyDeviceToDevice, b->st));
+  else if (ff >= 0)
+    CK(cudaMemcpyAsync(b->d_forced + (size_t)s * b->maxF * b->G, &in.forced_first, 8, cudaMemcpyHostToDevice, b->st));
+  b->h2d += sizeof(SlotInit);
   const float *d_prompt = r->d_prompt;
   // chunks of kPrefillTok tokens; each token attends to [0, pos] (causal by position)
   const int nch = (r->S + kPrefillTok - 1) / kPrefillTok;
@@ -1120,33 +1231,17 @@ static void prefill(q3t_batch *b, Req *r) {
   a.n_suppress = nsup;
   a.sup_on = b->d_sup_on;
   a.col = 0;
-  a.forced = nullptr;
+  a.frame = b->d_zero;  // the first token is frame 0, group 0 of the forced / raw records
+  a.fadd = 0;
   a.hist_mode = 1;
-  a.eos_flag = b->d_eosflag;
-  a.frame = dm + 2;
-  a.raw = nullptr;
+  a.eos_flag = b->d_first_eos + s;
   sample(a, 1, b->st);
+  check_launches();
   if (r->first_logits)  // the reduced logits (the sampler writes them before suppression)
     CK(cudaMemcpyAsync(r->first_logits, b->tlog, (size_t)V * 4, cudaMemcpyDeviceToHost, b->st));
-  // teacher forcing of the first token replaces it where it was sampled
-  check_launches();
-  CK(cudaMemcpyAsync(b->h_codes, b->d_codes + (size_t)s * b->G, 8, cudaMemcpyDeviceToHost, b->st));
-  CK(cudaStreamSynchronize(b->st));
-  const int64_t raw_first = b->h_codes[0];
-  int64_t ff = r->forced_first;
-  if (ff < 0 && !r->forced.empty()) ff = r->forced[0];
-  if (ff >= 0) {
-    const int32_t f32v = (int32_t)ff;
-    CK(cudaMemcpyAsync(b->d_codes + (size_t)s * b->G, &ff, 8, cudaMemcpyHostToDevice, b->st));
-    CK(cudaMemcpyAsync(b->d_thist + (size_t)s * b->hist_cap, &f32v, 4, cudaMemcpyHostToDevice, b->st));
-  }
-  CK(cudaMemcpyAsync(b->h_codes, b->d_codes + (size_t)s * b->G, 8, cudaMemcpyDeviceToHost, b->st));
-  CK(cudaStreamSynchronize(b->st));
-  r->first_token = b->h_codes[0];
-  r->first_token_raw = raw_first;
-  r->eos_seen = r->eos >= 0 && r->first_token == r->eos;
   r->cache_len = r->S;
   r->step_idx = 0;
+  r->admitted_now = true;
 }
 
 static void admit(q3t_batch *b, int *admitted) {
@@ -1205,7 +1300,6 @@ static void retire(q3t_batch *b, Req *r, int64_t *samples) {
       r->codes[(size_t)q * T + t] = tg[(size_t)t * G + q];
       r->sampled[(size_t)q * T + t] = rg[(size_t)t * G + q];
     }
-  r->sampled[0] = (int32_t)r->first_token_raw;
   if (b->desc.codec_mode == 1 && b->m->has_codec && T > 0) {
     int64_t n = 0;
     codec_out_len(b->m->codec, T, &n);
@@ -1297,6 +1391,7 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
     b->h_extra[i] = r->step_idx < r->trailing_len ? r->d_trailing + (size_t)r->step_idx * b->H : r->d_pad;
     S.kv_tokens += r->cache_len + 1;
   }
+  flush_pages(b);
   hm[M_NTOK_B] = B;
   hm[M_NTOK_2B] = 2 * B;
   hm[M_ONE] = 1;
@@ -1314,6 +1409,12 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
   if (b->desc.codec_mode == 2 && b->m->has_codec) codec_stream_launch(b);
   CK(cudaMemcpyAsync(b->h_eosflag, b->d_eosflag, B * sizeof(int), cudaMemcpyDeviceToHost, b->st));
   CK(cudaMemcpyAsync(b->h_err, b->d_err, sizeof(int), cudaMemcpyDeviceToHost, b->st));
+  bool any_new = false;
+  for (Req *r : act) any_new |= r->admitted_now;
+  if (any_new) {
+    CK(cudaMemcpyAsync(b->h_first_eos, b->d_first_eos, b->A * sizeof(int), cudaMemcpyDeviceToHost, b->st));
+    b->d2h += b->A * sizeof(int);
+  }
   CK(cudaStreamSynchronize(b->st));
   b->d2h += B * sizeof(int) + sizeof(int);
   if (*b->h_err) {
@@ -1324,6 +1425,17 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
   }
   for (int i = 0; i < B; i++) {
     Req *r = act[i];
+    if (r->admitted_now) {  // its first token came out of this step's admission
+      r->admitted_now = false;
+      if (r->eos >= 0 && b->h_first_eos[r->slot]) {  // infer/mod.rs:197-202; this frame's output is dropped
+        r->eos_seen = true;
+        r->state = 3;
+        r->error = "talker emitted EOS before any audio codec token";
+        release(b, r);
+        act[i] = nullptr;
+        continue;
+      }
+    }
     r->step_idx++;
     S.frames++;
     if (r->step_idx >= r->max_new) {
@@ -1336,6 +1448,7 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
       }
     }
   }
+  act.erase(std::remove(act.begin(), act.end(), nullptr), act.end());
   if (b->desc.codec_mode == 2 && b->m->has_codec) codec_stream_step(b->m, b, act, &S.samples);
   for (Req *r : act)
     if (r->finished) {
@@ -1383,20 +1496,22 @@ static Req *new_request(q3t_batch *b, const q3t_session_desc *d, const int64_t *
   if (r->forced_first >= tc.talker.vocab_size) FAIL(Q3T_INVALID_INPUT, "forced first token out of range");
   for (auto id : r->suppress)
     if (id < 0) FAIL(Q3T_INVALID_INPUT, "negative suppress id");
-  // inputs go to device memory at submit time, so admission finds them resident
-  CK(cudaMalloc(&r->d_prompt, r->prompt.size() * 4));
-  CK(cudaMalloc(&r->d_trailing, r->trailing.size() * 4));
-  CK(cudaMalloc(&r->d_pad, r->pad.size() * 4));
-  CK(cudaMemcpyAsync(r->d_prompt, r->prompt.data(), r->prompt.size() * 4, cudaMemcpyHostToDevice, b->st));
-  CK(cudaMemcpyAsync(r->d_trailing, r->trailing.data(), r->trailing.size() * 4, cudaMemcpyHostToDevice, b->st));
-  CK(cudaMemcpyAsync(r->d_pad, r->pad.data(), r->pad.size() * 4, cudaMemcpyHostToDevice, b->st));
-  b->h2d += (r->prompt.size() + r->trailing.size() + r->pad.size()) * 4;
-  if (!r->forced.empty()) {
-    CK(cudaMalloc(&r->d_forced, r->forced.size() * 8));
-    CK(cudaMemcpyAsync(r->d_forced, r->forced.data(), r->forced.size() * 8, cudaMemcpyHostToDevice, b->st));
-    b->h2d += r->forced.size() * 8;
-  }
-  CK(cudaStreamSynchronize(b->st));
+  // inputs go to device memory at submit time, so admission finds them
+  // resident; the stream-ordered pool keeps its memory, so neither this
+  // allocation nor the free at retirement synchronises the device, and a
+  // copy from pageable memory returns once the data is staged
+  auto up = [&](void **d, const void *h, size_t bytes) {
+    CK(cudaMallocFromPoolAsync(d, bytes ? bytes : 8, b->pool, b->st));
+    if (bytes) CK(cudaMemcpyAsync(*d, h, bytes, cudaMemcpyHostToDevice, b->st));
+    b->h2d += (int64_t)bytes;
+  };
+  up((void **)&r->d_prompt, r->prompt.data(), r->prompt.size() * 4);
+  up((void **)&r->d_trailing, r->trailing.data(), r->trailing.size() * 4);
+  up((void **)&r->d_pad, r->pad.data(), r->pad.size() * 4);
+  if (!r->forced.empty()) up((void **)&r->d_forced, r->forced.data(), r->forced.size() * 8);
+  if (!r->suppress.empty())
+    up((void **)&r->d_suppress, r->suppress.data(),
+       std::min<size_t>(r->suppress.size(), (size_t)b->n_suppress_cap) * 8);
   std::vector<float>().swap(r->prompt);  // the device copy is the one that is used
   Req *raw = r.get();
   b->reqs[raw->id] = std::move(r);
@@ -1593,6 +1708,11 @@ extern "C" q3t_status q3t_session_start(q3t_model *m, const q3t_session_desc *d,
     admit(b, nullptr);
     if (s->r->state == 3) FAIL(s->r->fail_status, "%s", s->r->error.c_str());
     if (s->r->state != 1) FAIL(Q3T_OUT_OF_PAGES, "prompt of %d tokens does not fit the KV pool", s->r->S);
+    // TalkerGenerator::start returns with the first token known: read its EOS flag now
+    CK(cudaMemcpyAsync(b->h_first_eos, b->d_first_eos, b->A * sizeof(int), cudaMemcpyDeviceToHost, b->st));
+    CK(cudaStreamSynchronize(b->st));
+    s->r->admitted_now = false;
+    s->r->eos_seen = s->r->eos >= 0 && b->h_first_eos[s->r->slot];
   });
   if (rc != Q3T_OK) {
     q3t_batch_free(b);
@@ -1723,6 +1843,7 @@ extern "C" q3t_status q3t_session_decode_embeds(q3t_session *s, const float *emb
     if (r->slot < 0) FAIL(Q3T_INVALID_INPUT, "session is finished");
     if (r->cache_len + 1 > kMaxSeq || !ensure_pages(b, r, r->cache_len + 1))
       FAIL(Q3T_OUT_OF_PAGES, "KV capacity exhausted at %d tokens", r->cache_len);
+    flush_pages(b);
     int *hm = b->h_meta;
     hm[b->off_slot()] = r->slot;
     hm[b->off_tpos()] = r->cache_len;
@@ -1796,6 +1917,7 @@ extern "C" q3t_status q3t_session_load_kv(q3t_session *s, const uint16_t *k, con
     CK(cudaSetDevice(m->device));
     if (r->slot < 0) FAIL(Q3T_INVALID_INPUT, "session is finished");
     if (len + 1 > kMaxSeq || !ensure_pages(b, r, len + 1)) FAIL(Q3T_OUT_OF_PAGES, "KV capacity exhausted");
+    flush_pages(b);
     const auto &c = m->tc.talker;
     const size_t n = (size_t)c.num_hidden_layers * c.num_key_value_heads * len * 128;
     if (len > 0) {

@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "../../include/q3t.h"
+#include "frame.cuh"
 #include "lm_kernels.cuh"
 #include "mk.cuh"
 
@@ -117,14 +118,21 @@ struct Req {
   int cache_len = 0;
   std::vector<int> pages;
   float *d_trailing = nullptr, *d_pad = nullptr, *d_prompt = nullptr;
-  int64_t *d_forced = nullptr;
+  int64_t *d_forced = nullptr, *d_suppress = nullptr;
+  bool admitted_now = false;  // prefilled in the current step (its first-token EOS flag is read after the frame)
   std::vector<int64_t> codes;  // [G][T] once retired
   std::vector<int32_t> sampled;  // [G][T] sampled tokens before teacher forcing
   std::vector<float> wave;
   int64_t samples = 0;
-  int64_t first_token = -1, first_token_raw = -1;
   std::string error;
   q3t_status fail_status = Q3T_INVALID_INPUT;  // the status of the failure (state 3)
+};
+
+// Slot state a prefill uploads, staged in pinned memory (one per slot).
+struct SlotInit {
+  SampleParams params[2];
+  int64_t eos, forced_first;
+  int32_t forced_first32, zero, sup_on, forced_count;
 };
 
 struct GraphEntry {
@@ -187,7 +195,8 @@ struct q3t_batch {
   int n_pages = 0;
   std::vector<int> free_pages;
   int *d_pt = nullptr;
-  std::vector<int> h_pt;
+  int *h_pt = nullptr;                   // pinned host copy of the page table [A][kPtStride]
+  int pt_lo = 1 << 30, pt_hi = -1;       // slot rows changed since the last upload
   // predictor pool (2 pages per slot)
   uint16_t *pk = nullptr, *pv = nullptr;
   int64_t p_layer_stride = 0;
@@ -217,6 +226,13 @@ struct q3t_batch {
   int *d_pmeta = nullptr, *h_pmeta = nullptr;  // prefill metadata, one block per chunk
   int *d_eosflag = nullptr, *h_eosflag = nullptr;
   int64_t *h_codes = nullptr;
+  // admission without host round trips: per-slot pinned staging of the slot
+  // state a prefill uploads, and the first token's EOS flag per slot (read
+  // back with the step's other flags)
+  q3t::SlotInit *h_init = nullptr;
+  int *d_first_eos = nullptr, *h_first_eos = nullptr;
+  int *d_zero = nullptr;                 // one device int that stays 0 (frame index of a first token)
+  cudaMemPool_t pool = nullptr;          // stream-ordered pool for request inputs (no device-wide syncs)
   // graphs
   bool use_graphs = true;
   std::map<std::tuple<int, int, int>, q3t::GraphEntry> graphs;
@@ -235,6 +251,11 @@ struct q3t_batch {
   int wait_polls = 0;          // poll limit of k_mk's tagged-data waits (0: the kernel's default)
   bool stall_waits = false;    // k_mk first waits on the never-set word (timeout tests)
   std::map<int, std::pair<q3t::MkStage *, int>> mk_progs;
+  // persistent frame kernel (frame.cu) for the code-predictor loop
+  bool use_frame = false;
+  int frame_grid = 0, frame_hc = 0;
+  unsigned *frame_bar = nullptr;
+  std::map<std::pair<int, int>, q3t::Phase *> frame_progs;  // device copies of the predictor phases
   int step_counter = 0;
   // requests
   std::vector<q3t::Req *> slots;
