@@ -455,8 +455,11 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
   b->d_extra = ar.zalloc<const float *>(A);
   CK(cudaMallocHost(&b->h_extra, A * sizeof(float *)));
   const int nchunks = kMaxSeq / kPrefillTok;
-  b->d_pmeta = ar.zalloc<int>((size_t)nchunks * b->pmeta_stride());
-  CK(cudaMallocHost(&b->h_pmeta, (size_t)nchunks * b->pmeta_stride() * sizeof(int)));
+  // one block per prefill chunk of every admission of a step (admissions do
+  // not synchronise, so a block is rewritten only after the step's sync)
+  b->pmeta_blocks = nchunks * A;
+  b->d_pmeta = ar.zalloc<int>((size_t)b->pmeta_blocks * b->pmeta_stride());
+  CK(cudaMallocHost(&b->h_pmeta, (size_t)b->pmeta_blocks * b->pmeta_stride() * sizeof(int)));
   b->d_eosflag = ar.zalloc<int>(T);
   CK(cudaMallocHost(&b->h_eosflag, T * sizeof(int)));
   CK(cudaMallocHost(&b->h_codes, (size_t)A * G * sizeof(int64_t)));
@@ -1190,10 +1193,16 @@ static void prefill(q3t_batch *b, Req *r) {
   // chunks of kPrefillTok tokens; each token attends to [0, pos] (causal by position)
   const int nch = (r->S + kPrefillTok - 1) / kPrefillTok;
   const int ps = b->pmeta_stride();
+  if (b->pmeta_used + nch > b->pmeta_blocks) {  // every block is in flight: wait for their copies
+    CK(cudaStreamSynchronize(b->st));
+    b->pmeta_used = 0;
+  }
+  const int blk0 = b->pmeta_used;
+  b->pmeta_used += nch;
   int last_n = 0;
   for (int c = 0; c < nch; c++) {
     const int c0 = c * kPrefillTok, n = std::min(kPrefillTok, r->S - c0);
-    int *hm = b->h_pmeta + (size_t)c * ps;
+    int *hm = b->h_pmeta + (size_t)(blk0 + c) * ps;
     hm[0] = n;
     hm[1] = 1;
     hm[2] = s;
@@ -1201,14 +1210,14 @@ static void prefill(q3t_batch *b, Req *r) {
       hm[8 + i] = s;
       hm[8 + kPrefillTok + i] = c0 + i;
     }
-    int *dm = b->d_pmeta + (size_t)c * ps;
+    int *dm = b->d_pmeta + (size_t)(blk0 + c) * ps;
     CK(cudaMemcpyAsync(dm, hm, ps * sizeof(int), cudaMemcpyHostToDevice, b->st));
     CK(cudaMemcpyAsync(b->x, d_prompt + (size_t)c0 * H, (size_t)n * H * 4, cudaMemcpyDeviceToDevice, b->st));
     TokView tv{dm, dm + 8, dm + 8 + kPrefillTok, 0};
     run_stack(b, m->talker, talker_kv(b), tv, n, bucket_units(c0 + n, attn_pw(n)));
     last_n = n;
   }
-  int *dm = b->d_pmeta + (size_t)(nch - 1) * ps;
+  int *dm = b->d_pmeta + (size_t)(blk0 + nch - 1) * ps;
   // final norm of the last prompt token -> hidden[slot] and codec_head input
   rmsnorm(b->x, H, 1, last_n - 1, Part{nullptr, 0, 0, 0}, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps,
           dm + 1, 1, b->d_hidden, dm + 2, b->st);
@@ -1317,6 +1326,7 @@ static void retire(q3t_batch *b, Req *r, int64_t *samples) {
 
 static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
   q3t_step_stats S{};
+  b->pmeta_used = 0;  // the previous step (or call) synchronised the stream
   CK(cudaEventRecord(b->ev0, b->st));
   admit(b, &S.admitted);
   std::vector<Req *> act;

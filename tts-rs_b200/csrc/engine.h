@@ -223,7 +223,8 @@ struct q3t_batch {
   int meta_n = 0;
   int *d_meta = nullptr, *h_meta = nullptr;
   const float **d_extra = nullptr, **h_extra = nullptr;
-  int *d_pmeta = nullptr, *h_pmeta = nullptr;  // prefill metadata, one block per chunk
+  int *d_pmeta = nullptr, *h_pmeta = nullptr;  // prefill metadata blocks (pinned staging + device)
+  int pmeta_blocks = 0, pmeta_used = 0;        // capacity; blocks handed out since the stream last synchronised
   int *d_eosflag = nullptr, *h_eosflag = nullptr;
   int64_t *h_codes = nullptr;
   // admission without host round trips: per-slot pinned staging of the slot
