@@ -298,8 +298,9 @@ typedef struct {
 } q3t_batch_desc;
 
 typedef struct {
-  int active;                /* requests in the decode step */
-  int admitted;              /* requests prefilled this step */
+  int active;                /* requests in the decode frame (first token known) */
+  int admitted;              /* requests admitted into a slot this step (their prompts run in
+                                chunks inside this and the following talker passes) */
   int retired;               /* requests finished this step */
   int64_t frames;            /* frames generated this step */
   int64_t samples;           /* PCM samples emitted this step */
@@ -308,7 +309,10 @@ typedef struct {
   int64_t h2d_bytes;         /* host -> device bytes copied during this step */
   int64_t d2h_bytes;         /* device -> host bytes copied during this step */
   float predictor_ms;        /* device time of the frame's code-predictor loop (15 codebooks) */
-  float talker_ms;           /* device time of the frame's talker decode, codec_head and sampling */
+  float talker_ms;           /* device time of the frame's talker pass (decode tokens and
+                                prompt-chunk tokens), codec_head and sampling */
+  int prefill_tokens;        /* prompt tokens that ran in this step's talker pass */
+  int first_tokens;          /* prompts completed this step (their first token sampled) */
 } q3t_step_stats;
 
 typedef struct q3t_batch q3t_batch;
@@ -320,9 +324,12 @@ q3t_status q3t_batch_create(q3t_model *model, const q3t_batch_desc *desc, q3t_ba
  * max_new_tokens). */
 q3t_status q3t_batch_submit(q3t_batch *b, const q3t_session_desc *req,
                             const int64_t *forced_codes, int64_t *request_id);
-/* One scheduler iteration: admit + prefill queued requests into free slots,
- * one decode frame for every active request, retire finished ones (codec
- * decode per codec_mode). */
+/* One scheduler iteration: admit queued requests into free slots, one decode
+ * frame for every request whose first token is known, with prompt tokens of
+ * admitted requests packed into the same talker pass (up to 128 tokens in
+ * all; a prompt's first token is sampled in the step its last chunk runs,
+ * and it decodes from the next step on), retire finished ones (codec decode
+ * per codec_mode). */
 q3t_status q3t_batch_step(q3t_batch *b, q3t_step_stats *stats);
 /* state: 0 queued, 1 active, 2 finished, 3 failed */
 q3t_status q3t_batch_poll(q3t_batch *b, int64_t request_id, int *state, int64_t *frames,

@@ -101,16 +101,32 @@ def _batch_vs_oracle(cfg, model, ot, prompt_lens, frames, seed0):
         fl = np.zeros(V, np.float32)
         rid = b.submit(prompt, trailing, pad, frames + 1, forced=codes, first_logits=fl)
         reqs.append(dict(rid=rid, inputs=(prompt, trailing, pad), codes=codes, first=fl, tl=[], pl=[]))
-    for f in range(frames):
+    # prompts run in chunks inside the talker passes (up to 128 tokens a
+    # step, in admission order); a request decodes from the step after its
+    # last chunk, so frame f of each request is its (f + 1)-th decode frame
+    admitted = prompt_tok = firsts = 0
+    total_prompt = int(sum(prompt_lens))
+    for _ in range(total_prompt // 64 + 4 * frames + 8):
         st = b.step()
-        assert st["active"] == len(reqs), st
-        if f == 0:
-            assert st["admitted"] == len(reqs)
+        admitted += st["admitted"]
+        prompt_tok += st["prefill_tokens"]
+        firsts += st["first_tokens"]
+        assert st["active"] + st["prefill_tokens"] <= 128, st
         for r in reqs:
-            tl, pl = b.logits(r["rid"])
+            if len(r["tl"]) == frames:
+                continue
+            try:
+                tl, pl = b.logits(r["rid"])
+            except q3t.Q3TError:  # not in this frame: its prompt is still running
+                assert not r["tl"], "a decoding request left the frame"
+                continue
             r["tl"].append(tl)
             r["pl"].append(pl)
-    for _ in range(4):  # the limit frame, then retirement
+        if all(len(r["tl"]) == frames for r in reqs):
+            break
+    assert admitted == len(reqs) and firsts == len(reqs) and prompt_tok == total_prompt
+    assert all(len(r["tl"]) == frames for r in reqs)
+    for _ in range(8):  # the limit frames, then retirement
         b.step()
         if b.pending() == (0, 0):
             break

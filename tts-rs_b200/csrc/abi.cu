@@ -84,7 +84,8 @@ const FieldRow k_step_stats[] = {
     Q3T_F(q3t_step_stats, active),    Q3T_F(q3t_step_stats, admitted),     Q3T_F(q3t_step_stats, retired),
     Q3T_F(q3t_step_stats, frames),    Q3T_F(q3t_step_stats, samples),      Q3T_F(q3t_step_stats, device_ms),
     Q3T_F(q3t_step_stats, kv_tokens), Q3T_F(q3t_step_stats, h2d_bytes),    Q3T_F(q3t_step_stats, d2h_bytes),
-    Q3T_F(q3t_step_stats, predictor_ms), Q3T_F(q3t_step_stats, talker_ms),
+    Q3T_F(q3t_step_stats, predictor_ms), Q3T_F(q3t_step_stats, talker_ms), Q3T_F(q3t_step_stats, prefill_tokens),
+    Q3T_F(q3t_step_stats, first_tokens),
 };
 #undef Q3T_F
 

@@ -321,6 +321,13 @@ namespace q3t {
 
 namespace q3t {
 
+static int bucket_tok(int B) {
+  if (B <= 1) return 1;
+  int n = 8;
+  while (n < B) n <<= 1;
+  return n;
+}
+
 static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
   b->m = m;
   b->desc = d;
@@ -389,14 +396,18 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
   b->d_forced_count = ar.zalloc<int>(A);
   b->d_raw = ar.zalloc<int32_t>((size_t)A * b->maxF * G);
   b->d_eos = ar.zalloc<int64_t>(A);
-  b->d_suppress = ar.zalloc<int64_t>(b->n_suppress_cap);
+  b->d_suppress = ar.zalloc<int64_t>((size_t)A * b->n_suppress_cap);
+  b->d_nsup = ar.zalloc<int>(A);
   b->d_hidden = ar.zalloc<float>((size_t)A * H);
   b->d_thist = ar.zalloc<int32_t>((size_t)A * b->hist_cap);
   b->d_thist_len = ar.zalloc<int>(A);
   b->d_sup_on = ar.zalloc<int>(A);
   b->d_params = ar.zalloc<SampleParams>((size_t)A * 2);
-  // activations: up to 2A tokens (predictor prefill) or one prefill chunk
-  b->Tmax = std::max(2 * A, kPrefillTok);
+  // activation rows: the predictor's pass 0 (two rows per decode token) or a
+  // talker pass (decode tokens + prompt-chunk tokens), each rounded up to the
+  // token bucket the frame graphs run at, so every GEMM token tile of a
+  // bucket lies inside the buffers
+  b->Tmax = std::max(2 * bucket_tok(A), kTalkerTok);
   const int T = b->Tmax;
   b->x = ar.zalloc<float>((size_t)T * H);
   b->xn = ar.zalloc<uint16_t>((size_t)T * H);
@@ -448,7 +459,7 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
     }
   }
   // metadata
-  b->meta_n = M_HDR + 8 * A;
+  b->meta_n = M_HDR + 8 * A + 5 * b->TT();
   b->d_meta = ar.zalloc<int>(b->meta_n);
   CK(cudaMallocHost(&b->h_meta, b->meta_n * sizeof(int)));
   memset(b->h_meta, 0, b->meta_n * sizeof(int));
@@ -540,12 +551,6 @@ static void run_graph(q3t_batch *b, std::tuple<int, int, int> key, F &&body) {
   g_launches += it->second.nodes;
 }
 
-static int bucket_tok(int B) {
-  if (B <= 1) return 1;
-  int n = 8;
-  while (n < B) n <<= 1;
-  return n;
-}
 // minimum pages per attention work unit: larger with more tokens in the
 // batch, so that the units stay a few waves deep at every batch size
 static int attn_pw(int max_tok) { return max_tok >= 32 ? 8 : max_tok >= 8 ? 2 : 1; }
@@ -868,10 +873,11 @@ static SampleArgs base_sample(q3t_batch *b) {
   return a;
 }
 
-static void build_frame(q3t_batch *b, int mt, int max_units, std::vector<Phase> &out) {
+// The code-predictor loop of a decode frame over the frame's decode tokens.
+static void build_pred(q3t_batch *b, int mt, std::vector<Phase> &out) {
   q3t_model *m = b->m;
   const auto &tc = m->tc;
-  const int G = b->G, H = b->H, PV = b->PV, V = b->V;
+  const int G = b->G, H = b->H, PV = b->PV;
   int *meta = b->d_meta;
   const int *ntokB = meta + M_NTOK_B, *ntok2B = meta + M_NTOK_2B;
   const int *slot = meta + b->off_slot(), *frame = meta + b->off_frame();
@@ -945,13 +951,36 @@ static void build_frame(q3t_batch *b, int mt, int max_units, std::vector<Phase> 
     }
     P.sample(a, mt, &t);
   }
-  // ---- talker decode (model.rs:94-113) + codec_head + sample ----
-  TokView tvt{ntokB, slot, meta + b->off_tpos(), 0};
+  out.swap(P.ph);
+}
+
+// The talker pass of a decode frame (model.rs:94-113) over the decode tokens
+// followed by this step's prompt-chunk tokens (chunked prefill, infer/mod.rs:
+// 135-147: causal by position, K/V appended to the request's pages), then
+// the final norm, codec_head and sampler over the head tokens: the decode
+// tokens and the last prompt token of every prompt completed in this step
+// (TalkerGenerator::start's first sample with the suppress list,
+// :148-157).  with_prefill: the prompt rows were copied into x after the
+// code-predictor loop, so every talker row is normalised first.
+static void build_talker(q3t_batch *b, int mt, int max_units, bool with_prefill, std::vector<Phase> &out) {
+  q3t_model *m = b->m;
+  const auto &tc = m->tc;
+  const int H = b->H, V = b->V;
+  int *meta = b->d_meta;
+  const int *ntokT = meta + M_NTOK_T, *ntokH = meta + M_NTOK_H;
+  const int *hslot = meta + b->off_hslot();
+  ProgBuilder P{b, false, {}};
+  if (with_prefill)
+    P.norm(rms_args(b->x, H, 1, 0, Part{}, m->talker.in_norm[0], b->xn, H, H, tc.talker.rms_norm_eps, ntokT, nullptr,
+                    nullptr),
+           mt);
+  TokView tvt{ntokT, meta + b->off_tseq(), meta + b->off_ttpos(), 0};
   P.stack(m->talker, talker_kv(b), tvt, mt, max_units, attn_pw(mt));
-  P.norm(rms_args(b->x, H, 1, 0, Part{}, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps, ntokB,
-                  b->d_hidden, slot),
-         mt);
-  GemmArgs hg = P.bf16_x(gemm_args(m->codec_head, ntokB, mt), b->xn, H);
+  RmsArgs fn = rms_args(b->x, H, 1, 0, Part{}, m->talker.final_norm, b->xn, H, H, tc.talker.rms_norm_eps, ntokH,
+                        b->d_hidden, hslot);
+  fn.row_idx = meta + b->off_hrow();
+  P.norm(fn, mt);
+  GemmArgs hg = P.bf16_x(gemm_args(m->codec_head, ntokH, mt), b->xn, H);
   hg.epi = GE_F32;
   hg.y = b->hlog;
   hg.ldy = V;
@@ -961,11 +990,15 @@ static void build_frame(q3t_batch *b, int mt, int max_units, std::vector<Phase> 
   a.logits = b->tlog;
   a.ldl = V;
   a.V = V;
-  a.ntok = ntokB;
-  a.slot = slot;
+  a.ntok = ntokH;
+  a.slot = hslot;
   a.use_pred_params = 0;
+  a.suppress = b->d_suppress;  // applied where sup_on[slot] (a first token of a prompt with a suppress list)
+  a.suppress_ld = b->n_suppress_cap;
+  a.n_sup = b->d_nsup;
+  a.sup_on = b->d_sup_on;
   a.col = 0;
-  a.frame = frame;
+  a.frame = meta + b->off_hframe();  // decode token: its frame; first token: -1 (record index 0)
   a.fadd = 1;
   a.hist_mode = 1;
   a.eos_flag = b->d_eosflag;
@@ -975,122 +1008,148 @@ static void build_frame(q3t_batch *b, int mt, int max_units, std::vector<Phase> 
   out.swap(P.ph);
 }
 
-// phases the talker part of the frame program takes (it is the tail)
-static int m_talker_phases(q3t_batch *b) { return 5 * b->m->tc.talker.num_hidden_layers + 3; }
+// Prompt rows of a chunk: x rows [row0, row0 + rows) <- src (device rows of H floats).
+struct PromptCopy {
+  const float *src;
+  int rows, row0;
+};
 
-// Runs the decode frame: one kernel per phase, captured into a CUDA graph
-// per (mt, max_units) on first use.  Q3T_FRAME_PROFILE=1 instead launches the
-// phases eagerly with an event after each and prints per-phase device times.
-static void enqueue_frame(q3t_batch *b, int mt, int max_units) {
-  auto key = std::make_pair(mt, max_units);
-  auto it = b->programs.find(key);
-  if (it == b->programs.end()) {
-    std::vector<Phase> ph;
-    build_frame(b, mt, max_units, ph);
-    it = b->programs.emplace(key, std::move(ph)).first;
+// Eager launch of a phase list with an event after each phase; adds the
+// per-shape device times to `by_shape` (Q3T_FRAME_PROFILE).
+static void profile_phases(q3t_batch *b, const std::vector<Phase> &pr, const char *part,
+                           std::map<std::string, std::pair<int, double>> &by_shape, double &total) {
+  const size_t n = pr.size();
+  std::vector<cudaEvent_t> ev(n + 1);
+  for (auto &e : ev) CK(cudaEventCreate(&e));
+  CK(cudaEventRecord(ev[0], b->st));
+  for (size_t i = 0; i < n; i++) {
+    run_phases(&pr[i], 1, b->st);
+    CK(cudaEventRecord(ev[i + 1], b->st));
   }
-  const std::vector<Phase> &pr = it->second;
+  CK(cudaStreamSynchronize(b->st));
+  for (size_t i = 0; i < n; i++) {
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+    const Phase &p = pr[i];
+    char key[96];
+    if (p.type == PH_GEMM)
+      snprintf(key, sizeof key, "%s gemm N%d K%d cs%d epi%d", part, p.gemm.N, p.gemm.K, p.gemm.cs, p.gemm.epi);
+    else
+      snprintf(key, sizeof key, "%s type%d", part, p.type);
+    by_shape[key].first++;
+    by_shape[key].second += ms * 1e3;
+    total += ms * 1e3;
+  }
+  for (auto &e : ev) cudaEventDestroy(e);
+}
+
+// Runs a decode frame: the code-predictor loop over the B decode tokens
+// (bucket mt; skipped when B == 0), the prompt-row copies of this step's
+// chunks, then the talker pass over the talker tokens (bucket mtT).  Each
+// part is one CUDA graph per bucket, captured on first use; the predictor
+// loop runs as one persistent k_frame launch where that is switched on.
+// Q3T_FRAME_PROFILE=1 instead launches the phases eagerly with an event
+// after each and prints per-phase device times.
+static void enqueue_frame(q3t_batch *b, int B, int mt, int mtT, int max_units, bool with_prefill,
+                          const std::vector<PromptCopy> &copies) {
+  const auto pkey = std::make_pair(mt, -1);
+  const auto tkey = std::make_pair(mtT, 2 * max_units + (with_prefill ? 1 : 0));
+  const std::vector<Phase> *pp = nullptr;
+  if (B > 0) {
+    auto it = b->programs.find(pkey);
+    if (it == b->programs.end()) {
+      std::vector<Phase> ph;
+      build_pred(b, mt, ph);
+      it = b->programs.emplace(pkey, std::move(ph)).first;
+    }
+    pp = &it->second;
+  }
+  auto tt = b->programs.find(tkey);
+  if (tt == b->programs.end()) {
+    std::vector<Phase> ph;
+    build_talker(b, mtT, max_units, with_prefill, ph);
+    tt = b->programs.emplace(tkey, std::move(ph)).first;
+  }
+  const std::vector<Phase> &tp = tt->second;
+  auto do_copies = [&] {
+    for (const PromptCopy &c : copies)
+      CK(cudaMemcpyAsync(b->x + (size_t)c.row0 * b->H, c.src, (size_t)c.rows * b->H * 4, cudaMemcpyDeviceToDevice,
+                         b->st));
+  };
   if (getenv("Q3T_FRAME_PROFILE")) {
-    const size_t n = pr.size();
-    std::vector<cudaEvent_t> ev(n + 1);
-    for (auto &e : ev) CK(cudaEventCreate(&e));
-    CK(cudaEventRecord(ev[0], b->st));
-    for (size_t i = 0; i < n; i++) {
-      run_phases(&pr[i], 1, b->st);
-      CK(cudaEventRecord(ev[i + 1], b->st));
-    }
-    CK(cudaStreamSynchronize(b->st));
-    double by_type[8] = {0}, pred = 0, talk = 0;
-    int cnt[8] = {0};
-    const size_t talker_from = n - (size_t)m_talker_phases(b);
     std::map<std::string, std::pair<int, double>> by_shape;
-    for (size_t i = 0; i < n; i++) {
-      float ms = 0.f;
-      CK(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
-      const Phase &p = pr[i];
-      by_type[p.type] += ms * 1e3;
-      cnt[p.type]++;
-      (i < talker_from ? pred : talk) += ms * 1e3;
-      char key[96];
-      if (p.type == PH_GEMM)
-        snprintf(key, sizeof key, "%s gemm N%d K%d cs%d epi%d", i < talker_from ? "pred" : "talk", p.gemm.N,
-                 p.gemm.K, p.gemm.cs, p.gemm.epi);
-      else
-        snprintf(key, sizeof key, "%s type%d", i < talker_from ? "pred" : "talk", p.type);
-      by_shape[key].first++;
-      by_shape[key].second += ms * 1e3;
-    }
-    for (auto &e : ev) cudaEventDestroy(e);
-    fprintf(stderr, "phase profile (eager) mt=%d mu=%d phases=%zu: pred %.1f us talker %.1f us |", mt, max_units, n,
-            pred, talk);
-    const char *nm[8] = {"", "norm", "gemm", "attn", "sample", "", "", ""};
-    for (int k = 1; k < 5; k++) fprintf(stderr, " %s %d %.1f us", nm[k], cnt[k], by_type[k]);
-    fprintf(stderr, "\n");
+    double pred = 0, talk = 0;
+    if (pp) profile_phases(b, *pp, "pred", by_shape, pred);
+    do_copies();
+    profile_phases(b, tp, "talk", by_shape, talk);
+    fprintf(stderr, "phase profile (eager) B=%d mt=%d mtT=%d prefill=%d: pred %.1f us talker %.1f us\n", B, mt, mtT,
+            (int)with_prefill, pred, talk);
     for (auto &kv : by_shape)
       fprintf(stderr, "   %-36s %4d x %8.2f us = %9.1f us\n", kv.first.c_str(), kv.second.first,
               kv.second.second / kv.second.first, kv.second.second);
-  } else {
-    // two graphs, the code-predictor loop and the talker step, with an event
-    // between them so a step reports both device times; the predictor loop
-    // runs as one persistent k_frame launch where the device can host it
-    const int talker_from = (int)pr.size() - m_talker_phases(b);
+    check_launches();
+    return;
+  }
+  CK(cudaEventRecord(b->evf[0], b->st));
+  if (pp) {
+    const std::vector<Phase> &pr = *pp;
+    const int n = (int)pr.size();
     Phase *fp = nullptr;
     if (b->use_frame) {
-      auto fit = b->frame_progs.find(key);
+      auto fit = b->frame_progs.find(pkey);
       if (fit == b->frame_progs.end()) {
         bool ok = true;
-        for (int i = 0; i < talker_from && ok; i++) ok = frame_phase_ok(pr[i], b->frame_hc);
+        for (int i = 0; i < n && ok; i++) ok = frame_phase_ok(pr[i], b->frame_hc);
         Phase *d = nullptr;
         if (ok) {
-          std::vector<Phase> cp(pr.begin(), pr.begin() + talker_from);
+          std::vector<Phase> cp(pr);
           int next = -1;  // Phase::pad = the next GEMM phase, which the kernel's weight prefetch follows
-          for (int i = talker_from - 1; i >= 0; i--) {
+          for (int i = n - 1; i >= 0; i--) {
             cp[i].pad = next;
             if (cp[i].type == PH_GEMM) next = i;
           }
-          d = b->ar.alloc<Phase>(talker_from);
-          CK(cudaMemcpyAsync(d, cp.data(), (size_t)talker_from * sizeof(Phase), cudaMemcpyHostToDevice, b->st));
+          d = b->ar.alloc<Phase>(n);
+          CK(cudaMemcpyAsync(d, cp.data(), (size_t)n * sizeof(Phase), cudaMemcpyHostToDevice, b->st));
           CK(cudaStreamSynchronize(b->st));
         }
-        fit = b->frame_progs.emplace(key, d).first;
+        fit = b->frame_progs.emplace(pkey, d).first;
       }
       fp = fit->second;
     }
-    CK(cudaEventRecord(b->evf[0], b->st));
     const char *tr = fp ? getenv("Q3T_FRAME_TRACE") : nullptr;  // profiling: per-phase device timestamps
     if (tr && tr[0]) {
-      const size_t nt = (size_t)b->frame_grid * talker_from * 8;
+      const size_t nt = (size_t)b->frame_grid * n * 8;
       unsigned long long *d_tr = nullptr;
       CK(cudaMallocAsync((void **)&d_tr, nt * 8, b->st));
       CK(cudaMemsetAsync(d_tr, 0, nt * 8, b->st));
-      frame_launch(FrameArgs{fp, talker_from, b->frame_bar, b->d_err, b->frame_hc, d_tr}, b->frame_grid, b->st);
+      frame_launch(FrameArgs{fp, n, b->frame_bar, b->d_err, b->frame_hc, d_tr}, b->frame_grid, b->st);
       check_launches();
       std::vector<unsigned long long> h(nt);
       CK(cudaMemcpyAsync(h.data(), d_tr, nt * 8, cudaMemcpyDeviceToHost, b->st));
       CK(cudaStreamSynchronize(b->st));
       CK(cudaFreeAsync(d_tr, b->st));
       if (FILE *f = fopen(tr, "wb")) {
-        const int hdr[2] = {b->frame_grid, talker_from};
+        const int hdr[2] = {b->frame_grid, n};
         fwrite(hdr, sizeof hdr, 1, f);
-        std::vector<int> types(talker_from);
-        for (int i = 0; i < talker_from; i++) types[i] = pr[i].type;
-        fwrite(types.data(), sizeof(int), talker_from, f);
+        std::vector<int> types(n);
+        for (int i = 0; i < n; i++) types[i] = pr[i].type;
+        fwrite(types.data(), sizeof(int), n, f);
         fwrite(h.data(), 8, nt, f);
         fclose(f);
       }
-    } else if (fp)
-      run_graph(b, std::make_tuple(6, mt, max_units), [&] {
-        frame_launch(FrameArgs{fp, talker_from, b->frame_bar, b->d_err, b->frame_hc, nullptr}, b->frame_grid,
-                     b->st);
+    } else if (fp) {
+      run_graph(b, std::make_tuple(6, mt, 0), [&] {
+        frame_launch(FrameArgs{fp, n, b->frame_bar, b->d_err, b->frame_hc, nullptr}, b->frame_grid, b->st);
       });
-    else
-      run_graph(b, std::make_tuple(4, mt, max_units), [&] { run_phases(pr.data(), talker_from, b->st); });
-    CK(cudaEventRecord(b->evf[1], b->st));
-    run_graph(b, std::make_tuple(5, mt, max_units),
-              [&] { run_phases(pr.data() + talker_from, (int)pr.size() - talker_from, b->st); });
-    CK(cudaEventRecord(b->evf[2], b->st));
-    b->frame_timed = true;
+    } else {
+      run_graph(b, std::make_tuple(4, mt, 0), [&] { run_phases(pr.data(), n, b->st); });
+    }
   }
+  CK(cudaEventRecord(b->evf[1], b->st));
+  do_copies();
+  run_graph(b, std::make_tuple(5, mtT, tkey.second), [&] { run_phases(tp.data(), (int)tp.size(), b->st); });
+  CK(cudaEventRecord(b->evf[2], b->st));
+  b->frame_timed = true;
   check_launches();
 }
 
@@ -1151,21 +1210,13 @@ static SampleParams to_params(const q3t_sampling &s) {
   return p;
 }
 
-// TalkerGenerator::start: prefill the prompt into the request's pages, then
-// codec_head + first sample with the suppress list (infer/mod.rs:135-157).
-// Everything is enqueued on the batch stream without a host round trip: the
-// slot state goes up from pinned staging, teacher forcing of the first token
-// happens in the sampler (forced[slot][0][0]), the sampled token before
-// forcing lands in raw[slot][0][0], and the first token's EOS flag in
-// first_eos[slot], which the step reads back with the frame's own flags.
-static void prefill(q3t_batch *b, Req *r) {
-  q3t_model *m = b->m;
-  const auto &tc = m->tc;
-  const int H = b->H, V = b->V, s = r->slot;
-  if (!ensure_pages(b, r, r->S)) FAIL(Q3T_OUT_OF_PAGES, "KV page pool exhausted (prompt of %d tokens)", r->S);
-  flush_pages(b);
-  // per-slot state (the staging entry of slot s is reused only after the step that admitted it synchronised)
-  SlotInit &in = b->h_init[s];
+// The per-slot state a request's sampling and teacher forcing read (from
+// pinned staging, no host round trip): sampling parameters, EOS id, talker
+// history length, suppress list (first token only), teacher-forced codes
+// (forced[slot][0][0] is the first token).
+static void upload_slot_state(q3t_batch *b, Req *r) {
+  const int s = r->slot;
+  SlotInit &in = b->h_init[s];  // reused only after the step that admitted it synchronised
   in.params[0] = to_params(r->ts);
   in.params[1] = to_params(r->cs);
   in.eos = r->eos;
@@ -1176,11 +1227,15 @@ static void prefill(q3t_batch *b, Req *r) {
   in.zero = 0;
   const int nsup = std::min<int>((int)r->suppress.size(), b->n_suppress_cap);
   in.sup_on = nsup ? 1 : 0;
+  in.nsup = nsup;
   in.forced_count = r->forced.empty() ? (ff >= 0 ? 1 : 0) : r->max_new;
   CK(cudaMemcpyAsync(b->d_params + 2 * s, in.params, sizeof in.params, cudaMemcpyHostToDevice, b->st));
   CK(cudaMemcpyAsync(b->d_eos + s, &in.eos, sizeof(int64_t), cudaMemcpyHostToDevice, b->st));
   CK(cudaMemcpyAsync(b->d_thist_len + s, &in.zero, sizeof(int), cudaMemcpyHostToDevice, b->st));
-  if (nsup) CK(cudaMemcpyAsync(b->d_suppress, r->d_suppress, nsup * 8, cudaMemcpyDeviceToDevice, b->st));
+  if (nsup)
+    CK(cudaMemcpyAsync(b->d_suppress + (size_t)s * b->n_suppress_cap, r->d_suppress, nsup * 8,
+                       cudaMemcpyDeviceToDevice, b->st));
+  CK(cudaMemcpyAsync(b->d_nsup + s, &in.nsup, sizeof(int), cudaMemcpyHostToDevice, b->st));
   CK(cudaMemcpyAsync(b->d_sup_on + s, &in.sup_on, sizeof(int), cudaMemcpyHostToDevice, b->st));
   CK(cudaMemcpyAsync(b->d_forced_count + s, &in.forced_count, sizeof(int), cudaMemcpyHostToDevice, b->st));
   if (!r->forced.empty())
@@ -1189,6 +1244,20 @@ static void prefill(q3t_batch *b, Req *r) {
   else if (ff >= 0)
     CK(cudaMemcpyAsync(b->d_forced + (size_t)s * b->maxF * b->G, &in.forced_first, 8, cudaMemcpyHostToDevice, b->st));
   b->h2d += sizeof(SlotInit);
+}
+
+// TalkerGenerator::start for a session (infer/mod.rs:135-157): the whole
+// prompt through the talker in 64-token chunks, then codec_head + first
+// sample with the suppress list, all enqueued without a host round trip (the
+// first token's EOS flag lands in first_eos[slot]).  Batched requests
+// instead run their prompt chunks inside the decode frames (batch_step).
+static void prefill(q3t_batch *b, Req *r) {
+  q3t_model *m = b->m;
+  const auto &tc = m->tc;
+  const int H = b->H, V = b->V, s = r->slot;
+  if (!ensure_pages(b, r, r->S)) FAIL(Q3T_OUT_OF_PAGES, "KV page pool exhausted (prompt of %d tokens)", r->S);
+  flush_pages(b);
+  upload_slot_state(b, r);
   const float *d_prompt = r->d_prompt;
   // chunks of kPrefillTok tokens; each token attends to [0, pos] (causal by position)
   const int nch = (r->S + kPrefillTok - 1) / kPrefillTok;
@@ -1237,7 +1306,8 @@ static void prefill(q3t_batch *b, Req *r) {
   a.slot = dm + 2;
   a.use_pred_params = 0;
   a.suppress = b->d_suppress;
-  a.n_suppress = nsup;
+  a.suppress_ld = b->n_suppress_cap;
+  a.n_sup = b->d_nsup;
   a.sup_on = b->d_sup_on;
   a.col = 0;
   a.frame = b->d_zero;  // the first token is frame 0, group 0 of the forced / raw records
@@ -1249,8 +1319,10 @@ static void prefill(q3t_batch *b, Req *r) {
   if (r->first_logits)  // the reduced logits (the sampler writes them before suppression)
     CK(cudaMemcpyAsync(r->first_logits, b->tlog, (size_t)V * 4, cudaMemcpyDeviceToHost, b->st));
   r->cache_len = r->S;
+  r->prefill_pos = r->S;
   r->step_idx = 0;
   r->admitted_now = true;
+  r->decoding = true;
 }
 
 static void admit(q3t_batch *b, int *admitted) {
@@ -1277,8 +1349,18 @@ static void admit(q3t_batch *b, int *admitted) {
     r->slot = s;
     b->slots[s] = r;
     r->state = 1;
+    r->admit_order = b->admit_counter++;
     try {
-      prefill(b, r);
+      if (b->session_mode) {
+        prefill(b, r);
+      } else {  // the prompt runs in chunks inside the next decode frames; its pages are taken now
+        if (!ensure_pages(b, r, r->S)) FAIL(Q3T_OUT_OF_PAGES, "KV page pool exhausted (prompt of %d tokens)", r->S);
+        upload_slot_state(b, r);
+        r->prefill_pos = 0;
+        r->cache_len = 0;
+        r->step_idx = 0;
+        r->decoding = false;
+      }
     } catch (const Status &st) {
       r->state = 3;
       r->fail_status = st.code;
@@ -1324,16 +1406,27 @@ static void retire(q3t_batch *b, Req *r, int64_t *samples) {
   release(b, r);
 }
 
+// One scheduler step.  Decode requests (first token known) get one frame:
+// the code-predictor loop, then the talker pass, which also carries prompt
+// tokens of admitted requests up to kTalkerTok tokens in all (chunked
+// prefill, served in admission order); a prompt that completes in this step
+// has its last token normed, headed and sampled with the decode tokens, and
+// decodes from the next step on.  One synchronisation per step (the flags
+// read back).
 static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
   q3t_step_stats S{};
   b->pmeta_used = 0;  // the previous step (or call) synchronised the stream
   CK(cudaEventRecord(b->ev0, b->st));
   admit(b, &S.admitted);
-  std::vector<Req *> act;
+  std::vector<Req *> act, pre;
   for (int i = 0; i < b->A; i++) {
     Req *r = b->slots[i];
     if (!r) continue;
     if (r->finished) continue;
+    if (!r->decoding) {
+      pre.push_back(r);
+      continue;
+    }
     if (r->eos_seen) {  // infer/mod.rs:197-204
       if (r->step_idx == 0) {
         r->state = 3;
@@ -1363,6 +1456,12 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
     b->h2d = b->d2h = 0;
     if (stats) *stats = S;
   };
+  auto fail_pages = [&](Req *r, int len) {
+    r->state = 3;
+    r->fail_status = Q3T_OUT_OF_PAGES;
+    r->error = "request " + std::to_string(r->id) + ": KV capacity exhausted at " + std::to_string(len) + " tokens";
+    release(b, r);
+  };
   // KV pages for this frame's token; a request that cannot get one fails
   // alone (the reference slides its 4096-entry window here, kv.rs:109-132;
   // this build stops the request with an explicit error) and the others run
@@ -1370,20 +1469,40 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
     size_t k = 0;
     for (Req *r : act) {
       if (r->cache_len + 1 > kMaxSeq || r->step_idx >= b->maxF || !ensure_pages(b, r, r->cache_len + 1)) {
-        r->state = 3;
-        r->fail_status = Q3T_OUT_OF_PAGES;
-        r->error = "request " + std::to_string(r->id) + ": KV capacity exhausted at " +
-                   std::to_string(r->cache_len) + " tokens";
-        release(b, r);
+        fail_pages(r, r->cache_len);
         continue;
       }
       act[k++] = r;
     }
     act.resize(k);
   }
+  // this step's prompt chunks, in admission order, filling the talker pass up to kTalkerTok tokens
+  struct Chunk {
+    Req *r;
+    int pos0, n;
+  };
+  std::vector<Chunk> chunks;
+  std::sort(pre.begin(), pre.end(), [](const Req *x, const Req *y) { return x->admit_order < y->admit_order; });
+  {
+    int budget = kTalkerTok - (int)act.size();
+    for (Req *r : pre) {
+      if (budget == 0) break;
+      const int n = std::min(budget, r->S - r->prefill_pos);
+      if (n <= 0) continue;
+      if (!ensure_pages(b, r, r->prefill_pos + n)) {
+        fail_pages(r, r->prefill_pos);
+        continue;
+      }
+      chunks.push_back({r, r->prefill_pos, n});
+      budget -= n;
+    }
+  }
   const int B = (int)act.size();
+  int P = 0;
+  for (const Chunk &c : chunks) P += c.n;
   S.active = B;
-  if (B == 0) {
+  S.prefill_tokens = P;
+  if (B == 0 && P == 0) {
     if (b->desc.codec_mode == 2 && b->m->has_codec) codec_stream_join(b, &S.samples);
     report();
     return;
@@ -1399,53 +1518,91 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
     hm[b->off_p0pos() + 2 * i] = 0;
     hm[b->off_p0pos() + 2 * i + 1] = 1;
     b->h_extra[i] = r->step_idx < r->trailing_len ? r->d_trailing + (size_t)r->step_idx * b->H : r->d_pad;
+    hm[b->off_tseq() + i] = r->slot;
+    hm[b->off_ttpos() + i] = r->cache_len;
+    hm[b->off_hrow() + i] = i;
+    hm[b->off_hslot() + i] = r->slot;
+    hm[b->off_hframe() + i] = r->step_idx;
     S.kv_tokens += r->cache_len + 1;
   }
+  // prompt-chunk tokens follow the decode tokens in the talker pass; a chunk
+  // that completes its prompt adds its last token to the head
+  std::vector<PromptCopy> copies;
+  std::vector<Req *> firsts;
+  int t = B, h = B;
+  for (const Chunk &c : chunks) {
+    for (int j = 0; j < c.n; j++) {
+      hm[b->off_tseq() + t + j] = c.r->slot;
+      hm[b->off_ttpos() + t + j] = c.pos0 + j;
+      S.kv_tokens += c.pos0 + j + 1;
+    }
+    copies.push_back({c.r->d_prompt + (size_t)c.pos0 * b->H, c.n, t});
+    if (c.pos0 + c.n == c.r->S) {
+      hm[b->off_hrow() + h] = t + c.n - 1;
+      hm[b->off_hslot() + h] = c.r->slot;
+      hm[b->off_hframe() + h] = -1;  // the first token: record index 0 of the forced / raw codes
+      firsts.push_back(c.r);
+      h++;
+    }
+    t += c.n;
+  }
+  const int F = (int)firsts.size();
   flush_pages(b);
   hm[M_NTOK_B] = B;
   hm[M_NTOK_2B] = 2 * B;
   hm[M_ONE] = 1;
   hm[M_SEED] = b->step_counter++;
+  hm[M_NTOK_T] = B + P;
+  hm[M_NTOK_H] = B + F;
   CK(cudaMemcpyAsync(b->d_meta, hm, b->meta_n * sizeof(int), cudaMemcpyHostToDevice, b->st));
-  CK(cudaMemcpyAsync(b->d_extra, b->h_extra, B * sizeof(float *), cudaMemcpyHostToDevice, b->st));
+  if (B) CK(cudaMemcpyAsync(b->d_extra, b->h_extra, B * sizeof(float *), cudaMemcpyHostToDevice, b->st));
   // the attention's unit bound only sizes its (persistent) grid, so the frame
-  // graph uses the largest and is captured once per token bucket
-  const int mt = bucket_tok(B), ms = kAttnMaxUnits;
+  // graphs use the largest and are captured once per token bucket
+  const int mt = bucket_tok(B), mtT = bucket_tok(B + P), ms = kAttnMaxUnits;
   b->h2d += b->meta_n * sizeof(int) + B * sizeof(float *);
   b->last_ids.resize(B);
   for (int i = 0; i < B; i++) b->last_ids[i] = act[i]->id;
-  enqueue_frame(b, mt, ms);
+  enqueue_frame(b, B, mt, mtT, ms, P > 0, copies);
   // the previous step's codec windows decode on their own stream under this frame
   if (b->desc.codec_mode == 2 && b->m->has_codec) codec_stream_launch(b);
-  CK(cudaMemcpyAsync(b->h_eosflag, b->d_eosflag, B * sizeof(int), cudaMemcpyDeviceToHost, b->st));
+  CK(cudaMemcpyAsync(b->h_eosflag, b->d_eosflag, (B + F) * sizeof(int), cudaMemcpyDeviceToHost, b->st));
   CK(cudaMemcpyAsync(b->h_err, b->d_err, sizeof(int), cudaMemcpyDeviceToHost, b->st));
-  bool any_new = false;
-  for (Req *r : act) any_new |= r->admitted_now;
-  if (any_new) {
-    CK(cudaMemcpyAsync(b->h_first_eos, b->d_first_eos, b->A * sizeof(int), cudaMemcpyDeviceToHost, b->st));
-    b->d2h += b->A * sizeof(int);
-  }
   CK(cudaStreamSynchronize(b->st));
-  b->d2h += B * sizeof(int) + sizeof(int);
+  b->d2h += (B + F) * sizeof(int) + sizeof(int);
   if (*b->h_err) {
     const int e = *b->h_err;
     *b->h_err = 0;
     CK(cudaMemsetAsync(b->d_err, 0, sizeof(int), b->st));
     FAIL(Q3T_DEVICE_TIMEOUT, "decode frame: a bounded device wait gave up (code %d)", e);
   }
+  for (const Chunk &c : chunks) {
+    c.r->prefill_pos += c.n;
+    c.r->cache_len = c.r->prefill_pos;
+  }
+  S.first_tokens = F;
+  bool copied = false;
+  for (int f = 0; f < F; f++)  // the reduced logits (the sampler writes them before suppression)
+    if (firsts[f]->first_logits) {
+      CK(cudaMemcpyAsync(firsts[f]->first_logits, b->tlog + (size_t)(B + f) * b->V, (size_t)b->V * 4,
+                         cudaMemcpyDeviceToHost, b->st));
+      copied = true;
+    }
+  if (copied) CK(cudaStreamSynchronize(b->st));
+  for (int f = 0; f < F; f++) {  // TalkerGenerator::start done: the first token is known
+    Req *r = firsts[f];
+    if (r->eos >= 0 && b->h_eosflag[B + f]) {  // infer/mod.rs:197-202: EOS before any audio codec token
+      r->eos_seen = true;
+      r->state = 3;
+      r->error = "talker emitted EOS before any audio codec token";
+      release(b, r);
+      continue;
+    }
+    r->decoding = true;
+    r->cache_len = r->S;
+    r->step_idx = 0;
+  }
   for (int i = 0; i < B; i++) {
     Req *r = act[i];
-    if (r->admitted_now) {  // its first token came out of this step's admission
-      r->admitted_now = false;
-      if (r->eos >= 0 && b->h_first_eos[r->slot]) {  // infer/mod.rs:197-202; this frame's output is dropped
-        r->eos_seen = true;
-        r->state = 3;
-        r->error = "talker emitted EOS before any audio codec token";
-        release(b, r);
-        act[i] = nullptr;
-        continue;
-      }
-    }
     r->step_idx++;
     S.frames++;
     if (r->step_idx >= r->max_new) {
@@ -1458,7 +1615,6 @@ static void batch_step(q3t_batch *b, q3t_step_stats *stats) {
       }
     }
   }
-  act.erase(std::remove(act.begin(), act.end(), nullptr), act.end());
   if (b->desc.codec_mode == 2 && b->m->has_codec) codec_stream_step(b->m, b, act, &S.samples);
   for (Req *r : act)
     if (r->finished) {

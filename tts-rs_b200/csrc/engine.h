@@ -98,7 +98,8 @@ constexpr int kPage = 16;
 constexpr int kMaxSeq = 4096;                 // the reference's talker cache capacity
 constexpr int kPtStride = kMaxSeq / kPage;    // pages per sequence
 constexpr int kPredPages = 2;                 // predictor KV pages per slot (num_code_groups + 1 <= 32 keys)
-constexpr int kPrefillTok = 64;
+constexpr int kPrefillTok = 64;               // prompt tokens per chunk of a session's prefill
+constexpr int kTalkerTok = 128;               // tokens of a batched talker pass: decode tokens + prompt-chunk tokens
 
 struct Req {
   int64_t id = 0;
@@ -120,6 +121,9 @@ struct Req {
   float *d_trailing = nullptr, *d_pad = nullptr, *d_prompt = nullptr;
   int64_t *d_forced = nullptr, *d_suppress = nullptr;
   bool admitted_now = false;  // prefilled in the current step (its first-token EOS flag is read after the frame)
+  bool decoding = false;      // first token known: the request takes part in decode frames
+  int prefill_pos = 0;        // prompt tokens already run through the talker (chunked prefill inside frames)
+  int64_t admit_order = 0;    // admission sequence number (prompt chunks are served in this order)
   std::vector<int64_t> codes;  // [G][T] once retired
   std::vector<int32_t> sampled;  // [G][T] sampled tokens before teacher forcing
   std::vector<float> wave;
@@ -132,7 +136,7 @@ struct Req {
 struct SlotInit {
   SampleParams params[2];
   int64_t eos, forced_first;
-  int32_t forced_first32, zero, sup_on, forced_count;
+  int32_t forced_first32, zero, sup_on, forced_count, nsup, pad;
 };
 
 struct GraphEntry {
@@ -141,11 +145,13 @@ struct GraphEntry {
 };
 
 enum MetaOff {
-  M_NTOK_B = 0,
+  M_NTOK_B = 0,   // decode tokens of the frame (the code-predictor loop's batch)
   M_NTOK_2B = 1,
   M_ONE = 2,
   M_NPRE = 3,
   M_SEED = 4,
+  M_NTOK_T = 5,   // tokens of the talker pass: decode tokens, then prompt-chunk tokens
+  M_NTOK_H = 6,   // tokens sampled by the talker head: decode tokens, then completed prompts' last tokens
   M_HDR = 8,
 };
 
@@ -204,7 +210,8 @@ struct q3t_batch {
   // slot state
   int maxF = 0;
   int64_t *d_codes = nullptr, *d_hist_codes = nullptr, *d_forced = nullptr, *d_eos = nullptr;
-  int64_t *d_suppress = nullptr;
+  int64_t *d_suppress = nullptr;   // [slot][n_suppress_cap] suppress list of each slot's request
+  int *d_nsup = nullptr;           // [slot] its length
   int32_t *d_raw = nullptr;
   int n_suppress_cap = 4096;
   float *d_hidden = nullptr;
@@ -274,6 +281,14 @@ struct q3t_batch {
   int off_zero() const { return q3t::M_HDR + 3 * A; }
   int off_p0seq() const { return q3t::M_HDR + 4 * A; }
   int off_p0pos() const { return q3t::M_HDR + 6 * A; }
+  // talker pass and talker head token lists (decode tokens first), TT entries each
+  int TT() const { return q3t::kTalkerTok; }
+  int off_tseq() const { return q3t::M_HDR + 8 * A; }
+  int off_ttpos() const { return off_tseq() + TT(); }
+  int off_hslot() const { return off_tseq() + 2 * TT(); }
+  int off_hframe() const { return off_tseq() + 3 * TT(); }
+  int off_hrow() const { return off_tseq() + 4 * TT(); }
+  int64_t admit_counter = 0;
   int pmeta_stride() const { return 8 + 2 * q3t::kPrefillTok + 8; }
 };
 

@@ -79,7 +79,7 @@ Q3T_DEV void norm_rope_lane(float4 v, const float *__restrict__ gm, float eps, i
 // ---------------------------------------------------------------------------
 Q3T_DEV void d_rmsnorm(const RmsArgs &a, int t, float *red) {
   if (t >= *a.ntok) return;
-  const int r = t * a.row_mul + a.row_add;
+  const int r = a.row_idx ? a.row_idx[t] : t * a.row_mul + a.row_add;
   float *xr = a.x + (size_t)r * a.ldx;
   const int H = a.H;
   const EmbedArgs &e = a.emb;
@@ -565,8 +565,10 @@ Q3T_DEV void d_sample(const SampleArgs &a, int t, float *lg, float *sv, int *si,
     __syncthreads();
   }
   if (a.suppress && a.sup_on && a.sup_on[s]) {
-    for (int i = tid; i < a.n_suppress; i += blockDim.x) {
-      const int64_t id = a.suppress[i];
+    const int64_t *sl = a.suppress + (size_t)s * a.suppress_ld;
+    const int ns = a.n_sup ? a.n_sup[s] : a.n_suppress;
+    for (int i = tid; i < ns; i += blockDim.x) {
+      const int64_t id = sl[i];
       if (id >= 0 && id < V) lg[id] = -INFINITY;
     }
     __syncthreads();

@@ -85,6 +85,7 @@ struct EmbedArgs {
 struct RmsArgs {
   float *x;
   int ldx, row_mul, row_add;
+  const int *row_idx;  // nullable: row t is x[row_idx[t]] instead of t * row_mul + row_add
   Part add;
   const float *gamma;
   uint16_t *out;
@@ -217,8 +218,10 @@ struct SampleArgs {
   const int *slot;
   const SampleParams *params;  // [slot]
   int use_pred_params;         // 0: params[slot*2], 1: params[slot*2+1]
-  const int64_t *suppress;     // [n_suppress] (applied where sup_on[slot] != 0)
-  int n_suppress;
+  const int64_t *suppress;     // slot s's list at suppress + s * suppress_ld (applied where sup_on[slot] != 0)
+  int n_suppress;              // its length, or n_sup[s] when n_sup is set
+  int suppress_ld;
+  const int *n_sup;            // [slot] or null
   int *sup_on;                 // [slot], cleared after use
   int64_t *codes;              // [slot][G]
   int G;

@@ -92,7 +92,8 @@ class StepStats(C.Structure):
     _fields_ = [("active", C.c_int), ("admitted", C.c_int), ("retired", C.c_int),
                 ("frames", C.c_int64), ("samples", C.c_int64), ("device_ms", C.c_float),
                 ("kv_tokens", C.c_int64), ("h2d_bytes", C.c_int64), ("d2h_bytes", C.c_int64),
-                ("predictor_ms", C.c_float), ("talker_ms", C.c_float)]
+                ("predictor_ms", C.c_float), ("talker_ms", C.c_float),
+                ("prefill_tokens", C.c_int), ("first_tokens", C.c_int)]
 
 
 EXPORTS = [
@@ -529,7 +530,8 @@ class Batch:
         return {"active": s.active, "admitted": s.admitted, "retired": s.retired,
                 "frames": s.frames, "samples": s.samples, "device_ms": s.device_ms,
                 "kv_tokens": s.kv_tokens, "h2d_bytes": s.h2d_bytes, "d2h_bytes": s.d2h_bytes,
-                "predictor_ms": s.predictor_ms, "talker_ms": s.talker_ms}
+                "predictor_ms": s.predictor_ms, "talker_ms": s.talker_ms,
+                "prefill_tokens": s.prefill_tokens, "first_tokens": s.first_tokens}
 
     def poll(self, rid):
         st, fr, sm = C.c_int(), C.c_int64(), C.c_int64()
