@@ -21,7 +21,8 @@ Q3T_DEV uint32_t pack_bf16x2(float lo, float hi) {
 Q3T_DEV float bf16_round(float f) { return bf2f(f2bf(f)); }
 
 // Programmatic dependent launch: everything before pdl_wait() may only read
-// data no earlier kernel writes (weights); pdl_wait() returns once the
+// data no earlier kernel writes (weights, and the metadata and page tables
+// that host copies put in place before the launch); pdl_wait() returns once the
 // preceding grid has completed and its memory is visible.  Both are no-ops
 // when the kernel was launched without the PDL attribute.
 Q3T_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

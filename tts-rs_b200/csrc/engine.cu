@@ -1090,6 +1090,10 @@ static void enqueue_frame(q3t_batch *b, int B, int mt, int mtT, int max_units, b
     check_launches();
     return;
   }
+  // profiling: Q3T_KERNEL_TRACE=<file> records every kernel of this frame
+  // (grid id, per-CTA device timestamps) and writes the records to the file
+  const char *ktr = getenv("Q3T_KERNEL_TRACE");
+  const bool ktrace = ktr && ktr[0] && trace_start((size_t)1 << 18, b->st);
   CK(cudaEventRecord(b->evf[0], b->st));
   if (pp) {
     const std::vector<Phase> &pr = *pp;
@@ -1151,6 +1155,17 @@ static void enqueue_frame(q3t_batch *b, int B, int mt, int mtT, int max_units, b
   CK(cudaEventRecord(b->evf[2], b->st));
   b->frame_timed = true;
   check_launches();
+  if (ktrace) {
+    std::vector<TraceRec> rec;
+    trace_stop(rec, b->st);
+    if (FILE *f = fopen(ktr, "wb")) {
+      const int n = (int)rec.size(), sz = (int)sizeof(TraceRec);
+      fwrite(&n, 4, 1, f);
+      fwrite(&sz, 4, 1, f);
+      fwrite(rec.data(), sizeof(TraceRec), rec.size(), f);
+      fclose(f);
+    }
+  }
 }
 
 static int alloc_page(q3t_batch *b, Req *r) {

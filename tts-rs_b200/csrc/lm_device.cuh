@@ -456,9 +456,10 @@ Q3T_DEV void attn_unit(const AttnArgs &a, int t, int r, float (*ps)[16], float (
 }
 
 // A group of kAttnWarps warps (tid 0..127, `sync` its barrier): numbers the
-// units of the launch, then its warps take units warp0 + w, + nwarps, ...
+// units of the launch (host-written metadata only, so this part may run
+// before the dependency wait) ...
 template <class Sync>
-Q3T_DEV void d_attn(const AttnArgs &a, int tid, int warp0, int nwarps, AttnSmem &S, uint16_t *ring, Sync sync) {
+Q3T_DEV void d_attn_number(const AttnArgs &a, int tid, AttnSmem &S, Sync sync) {
   const int w = tid >> 5, lane = tid & 31;
   int ntok = *a.tv.ntok;
   ntok = ntok < kAttnMaxTok ? ntok : kAttnMaxTok;
@@ -483,6 +484,14 @@ Q3T_DEV void d_attn(const AttnArgs &a, int tid, int warp0, int nwarps, AttnSmem 
     if (lane == 0) S.pre[0] = 0;
   }
   sync();
+}
+
+// ... then its warps take units warp0 + w, + nwarps, ...
+template <class Sync>
+Q3T_DEV void d_attn_run(const AttnArgs &a, int tid, int warp0, int nwarps, AttnSmem &S, uint16_t *ring, Sync sync) {
+  const int w = tid >> 5, lane = tid & 31;
+  int ntok = *a.tv.ntok;
+  ntok = ntok < kAttnMaxTok ? ntok : kAttnMaxTok;
   const int total = S.pre[ntok];
   for (int u = warp0 + w; u < total; u += nwarps) {
     int lo = 0, hi = ntok;  // largest t with pre[t] <= u
@@ -496,6 +505,12 @@ Q3T_DEV void d_attn(const AttnArgs &a, int tid, int warp0, int nwarps, AttnSmem 
     attn_unit(a, lo, u - S.pre[lo], S.ps[w], S.ob[w], ring + (size_t)w * kAttnStages * 2 * kPageElems, lane);
   }
   sync();  // S is reused by the caller's next item
+}
+
+template <class Sync>
+Q3T_DEV void d_attn(const AttnArgs &a, int tid, int warp0, int nwarps, AttnSmem &S, uint16_t *ring, Sync sync) {
+  d_attn_number(a, tid, S, sync);
+  d_attn_run(a, tid, warp0, nwarps, S, ring, sync);
 }
 
 // ---------------------------------------------------------------------------

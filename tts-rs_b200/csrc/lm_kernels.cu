@@ -43,6 +43,63 @@ static void note(cudaError_t e, const char *what) {
 
 void note_launch(cudaError_t e, const char *what) { note(e, what); }
 
+// ---------------------------------------------------------------------------
+// Launch trace (see lm_kernels.cuh)
+// ---------------------------------------------------------------------------
+__device__ TraceRec *g_trace = nullptr;
+__device__ unsigned g_trace_n = 0;
+__device__ unsigned g_trace_cap = 0;
+static TraceRec *h_trace_buf = nullptr;
+
+Q3T_DEV unsigned long long gclock() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// thread 0 of a CTA: append the record (no-op when tracing is off)
+Q3T_DEV void trace_put(TraceRec *buf, int kind, const unsigned long long *t, int n, int k) {
+  if (!buf) return;
+  const unsigned i = atomicAdd(&g_trace_n, 1u);
+  if (i >= g_trace_cap) return;
+  TraceRec r;
+  asm volatile("mov.u64 %0, %%gridid;" : "=l"(r.grid));
+#pragma unroll
+  for (int j = 0; j < 7; j++) r.t[j] = t[j];
+  r.kind = kind;
+  r.cta = (int)(blockIdx.x + blockIdx.y * gridDim.x);
+  r.n = n;
+  r.k = k;
+  buf[i] = r;
+}
+
+bool trace_start(size_t cap, cudaStream_t st) {
+  if (h_trace_buf) return false;
+  if (cudaMalloc(&h_trace_buf, cap * sizeof(TraceRec)) != cudaSuccess) {
+    h_trace_buf = nullptr;
+    return false;
+  }
+  const unsigned zero = 0, c = (unsigned)cap;
+  cudaMemcpyToSymbolAsync(g_trace_n, &zero, 4, 0, cudaMemcpyHostToDevice, st);
+  cudaMemcpyToSymbolAsync(g_trace_cap, &c, 4, 0, cudaMemcpyHostToDevice, st);
+  cudaMemcpyToSymbolAsync(g_trace, &h_trace_buf, sizeof(void *), 0, cudaMemcpyHostToDevice, st);
+  return cudaStreamSynchronize(st) == cudaSuccess;
+}
+
+void trace_stop(std::vector<TraceRec> &out, cudaStream_t st) {
+  if (!h_trace_buf) return;
+  TraceRec *none = nullptr;
+  unsigned n = 0, cap = 0;
+  cudaMemcpyToSymbolAsync(g_trace, &none, sizeof(void *), 0, cudaMemcpyHostToDevice, st);
+  cudaMemcpyFromSymbolAsync(&n, g_trace_n, 4, 0, cudaMemcpyDeviceToHost, st);
+  cudaMemcpyFromSymbolAsync(&cap, g_trace_cap, 4, 0, cudaMemcpyDeviceToHost, st);
+  cudaStreamSynchronize(st);
+  out.resize(n < cap ? n : cap);
+  cudaMemcpy(out.data(), h_trace_buf, out.size() * sizeof(TraceRec), cudaMemcpyDeviceToHost);
+  cudaFree(h_trace_buf);
+  h_trace_buf = nullptr;
+}
+
 template <typename... KArgs, typename... Args>
 static void launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args &&...args) {
   cudaLaunchConfig_t cfg = {};
@@ -111,9 +168,17 @@ void f32_to_bf16(const float *src, uint16_t *dst, int64_t n, cudaStream_t st) {
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_rmsnorm(RmsArgs a) {
   __shared__ float red[33];
+  TraceRec *trb = threadIdx.x == 0 ? g_trace : nullptr;
+  unsigned long long tst[7] = {0, 0, 0, 0, 0, 0, 0};
+  if (trb) tst[0] = gclock();
   pdl_wait();
   pdl_launch();
+  if (trb) tst[1] = gclock();
   d_rmsnorm(a, blockIdx.x, red);
+  if (trb) {
+    tst[6] = gclock();
+    trace_put(trb, 1, tst, 0, 0);
+  }
 }
 
 RmsArgs rms_args(float *x, int ldx, int row_mul, int row_add, Part add, const float *gamma, uint16_t *out, int ldo,
@@ -264,6 +329,9 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  TraceRec *trb = threadIdx.x == 0 ? g_trace : nullptr;
+  unsigned long long tst[7] = {0, 0, 0, 0, 0, 0, 0};
+  if (trb) tst[0] = gclock();
   if (threadIdx.x == 0) {  // weights: independent of earlier kernels
     mbar_expect_tx(&bars[0], L::kW);
 #pragma unroll
@@ -288,12 +356,25 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
       g1 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8 * 8 + 4);
     }
   }
+  // The token count, and for GE_QKV the position and page of this CTA's
+  // epilogue tokens, come from host-written metadata and page tables, so
+  // they load before the dependency wait.
+  const int ts = (N + cs - 1) / cs, t_lo = ks * ts;
+  int ntok = *a.ntok - tok0;
+  ntok = ntok < 0 ? 0 : (ntok > N ? N : ntok);
+  const int t_hi = min(t_lo + ts, ntok);
+  if (a.epi == GE_QKV && (int)threadIdx.x < t_hi - t_lo) {
+    const int t = tok0 + t_lo + threadIdx.x;
+    const int pos = a.tv.pos[t] + a.tv.pos_add;
+    meta[2 * threadIdx.x] = pos;
+    meta[2 * threadIdx.x + 1] = a.kv.page_table[(size_t)a.tv.seq[t] * a.kv.pt_stride + (pos >> 4)];
+  }
   pdl_wait();
   pdl_launch();
+  if (trb) tst[1] = gclock();
   // Loads that do not wait for the token count: rows tok0 .. tok0 + N - 1 of
   // every activation buffer exist (buffers hold >= tok0 + N rows); rows at or
   // beyond the count are read but never used.
-  const int ts = (N + cs - 1) / cs, t_lo = ks * ts;
   // GE_RESID: the residual rows of this warp's first two epilogue tokens
   // (final once the previous kernel completed)
   float4 xres[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
@@ -326,16 +407,6 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
         for (int i = 0; i < kMaxNss; i++) ssp[i] = i < a.nss ? sp[(size_t)i * a.ss_ld] : 0.f;
       }
     }
-  }
-  int ntok = *a.ntok - tok0;
-  ntok = ntok < 0 ? 0 : (ntok > N ? N : ntok);
-  const int t_hi = min(t_lo + ts, ntok);
-  if (a.epi == GE_QKV && (int)threadIdx.x < t_hi - t_lo) {
-    // position and page of this CTA's epilogue tokens (loads overlap the GEMM)
-    const int t = tok0 + t_lo + threadIdx.x;
-    const int pos = a.tv.pos[t] + a.tv.pos_add;
-    meta[2 * threadIdx.x] = pos;
-    meta[2 * threadIdx.x + 1] = a.kv.page_table[(size_t)a.tv.seq[t] * a.kv.pt_stride + (pos >> 4)];
   }
   if (a.xmode == GX_BF16) {
     if (threadIdx.x == 0) {
@@ -372,6 +443,7 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
     fence_proxy_async();
   }
   __syncthreads();
+  if (trb) tst[2] = gclock();
   uint32_t err = 0;
   if (threadIdx.x == 0) {
     if (!mbar_wait(&bars[0], 0)) err |= 1u;
@@ -386,6 +458,7 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
     }
     umma_commit(&bars[2]);
     if (!mbar_wait(&bars[2], 0)) err |= 4u;  // the other threads block in the barrier below, not polling
+    if (trb) tst[3] = gclock();
   }
   tc_fence_before();
   __syncthreads();
@@ -407,6 +480,7 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
     cluster_sync();
   else
     __syncthreads();
+  if (trb) tst[4] = gclock();
   for (int tt = t_lo + warp; tt < t_hi; tt += 8) {
     const float *src = tile + tt * kTileLd + 4 * lane;
     float4 v;
@@ -430,9 +504,14 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
     const int i = (tt - t_lo - warp) >> 3;
     gemm_epilogue(a, tok0 + tt, rg, lane, v, meta + 2 * (tt - t_lo), i == 0 ? xres[0] : xres[1], i < 2, gqk, fr);
   }
+  if (trb) tst[5] = gclock();
   if (cs > 1) cluster_sync();  // no CTA leaves while another still reads its tile
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, kCols);
+  if (trb) {
+    tst[6] = gclock();
+    trace_put(trb, 2, tst, a.N, a.K);
+  }
 }
 
 GemmArgs gemm_args(const Linear &W, const int *ntok, int max_tok) {
@@ -554,9 +633,18 @@ struct BlockSync {
 __global__ void __launch_bounds__(128, 3) k_attn(AttnArgs a) {
   __shared__ AttnSmem S;
   extern __shared__ __align__(16) uint16_t attn_ring[];
+  TraceRec *trb = threadIdx.x == 0 ? g_trace : nullptr;
+  unsigned long long tst[7] = {0, 0, 0, 0, 0, 0, 0};
+  if (trb) tst[0] = gclock();
+  d_attn_number(a, threadIdx.x, S, BlockSync{});  // host-written metadata only
   pdl_wait();
   pdl_launch();
-  d_attn(a, threadIdx.x, blockIdx.x * kAttnWarps, gridDim.x * kAttnWarps, S, attn_ring, BlockSync{});
+  if (trb) tst[1] = gclock();
+  d_attn_run(a, threadIdx.x, blockIdx.x * kAttnWarps, gridDim.x * kAttnWarps, S, attn_ring, BlockSync{});
+  if (trb) {
+    tst[6] = gclock();
+    trace_put(trb, 3, tst, 0, 0);
+  }
 }
 
 static int g_attn_grid = 0;
@@ -607,9 +695,17 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a) {
   extern __shared__ __align__(16) float smem_f[];
   __shared__ float rv[32];
   __shared__ int ri[32];
+  TraceRec *trb = threadIdx.x == 0 ? g_trace : nullptr;
+  unsigned long long tst[7] = {0, 0, 0, 0, 0, 0, 0};
+  if (trb) tst[0] = gclock();
   pdl_wait();
   pdl_launch();
+  if (trb) tst[1] = gclock();
   d_sample(a, blockIdx.x, smem_f, smem_f + kSampleMaxV, reinterpret_cast<int *>(smem_f + 2 * kSampleMaxV), rv, ri);
+  if (trb) {
+    tst[6] = gclock();
+    trace_put(trb, 4, tst, 0, 0);
+  }
 }
 
 void sample(const SampleArgs &a, int max_tok, cudaStream_t st) {

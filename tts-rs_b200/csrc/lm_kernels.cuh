@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <vector>
+
 namespace q3t {
 
 // Paged KV cache of one decoder stack.  Layout per layer l:
@@ -48,6 +50,23 @@ struct Part {
 };
 
 extern bool g_use_pdl;
+
+// Launch trace (profiling): while enabled, thread 0 of every CTA of k_gemm,
+// k_attn, k_sample and k_rmsnorm appends one record with the launch's grid
+// id and device timestamps (%globaltimer, ns): entry, after the dependency
+// wait, after X staging, after the MMAs, after the split-K reduction
+// barrier, after the epilogue, exit (stamps a kernel does not have are 0).
+struct TraceRec {
+  unsigned long long grid;
+  unsigned long long t[7];
+  int kind;  // 1 rmsnorm, 2 gemm, 3 attention, 4 sampler
+  int cta;
+  int n, k;  // k_gemm: N, K
+};
+// Starts recording into a device buffer of `cap` records (false if it
+// cannot be allocated); trace_stop copies the records out and stops.
+bool trace_start(size_t cap, cudaStream_t st);
+void trace_stop(std::vector<TraceRec> &out, cudaStream_t st);
 // one-time kernel attribute setup (dynamic shared memory limits)
 void init_kernel_attributes();
 extern int64_t g_launches;
