@@ -691,10 +691,14 @@ void attention(const uint16_t *q, KVView kv, int layer, TokView tv, int max_tok,
 constexpr int kSampleThreads = 512;
 constexpr size_t kSampleSmem = (size_t)kSampleMaxV * 12;
 
-__global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a) {
+// One token per CTA: the sampler, then (has_tail) the next input row of the
+// same token built from the code just sampled and normalised, so the two
+// steps of a code-predictor position share one launch.
+__global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a, RmsArgs tail, int has_tail) {
   extern __shared__ __align__(16) float smem_f[];
   __shared__ float rv[32];
   __shared__ int ri[32];
+  __shared__ float red[33];
   TraceRec *trb = threadIdx.x == 0 ? g_trace : nullptr;
   unsigned long long tst[7] = {0, 0, 0, 0, 0, 0, 0};
   if (trb) tst[0] = gclock();
@@ -702,14 +706,17 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a) {
   pdl_launch();
   if (trb) tst[1] = gclock();
   d_sample(a, blockIdx.x, smem_f, smem_f + kSampleMaxV, reinterpret_cast<int *>(smem_f + 2 * kSampleMaxV), rv, ri);
+  if (has_tail) d_rmsnorm(tail, blockIdx.x, red);  // d_sample ended with a block barrier: its codes are visible
   if (trb) {
     tst[6] = gclock();
     trace_put(trb, 4, tst, 0, 0);
   }
 }
 
-void sample(const SampleArgs &a, int max_tok, cudaStream_t st) {
-  launch(k_sample, dim3(max_tok), dim3(kSampleThreads), kSampleSmem, st, a);
+void sample(const SampleArgs &a, int max_tok, cudaStream_t st, const RmsArgs *tail) {
+  RmsArgs t{};
+  if (tail) t = *tail;
+  launch(k_sample, dim3(max_tok), dim3(kSampleThreads), kSampleSmem, st, a, t, tail ? 1 : 0);
 }
 
 // out[i] = table[ids[i]] for i < n, rows of `width` bf16 (width % 8 == 0).
@@ -775,10 +782,7 @@ void run_phases(const Phase *ph, int n, cudaStream_t st) {
       case PH_NORM: rmsnorm(p.norm, p.max_tok, st); break;
       case PH_GEMM: gemm(p.gemm, p.max_tok, st); break;
       case PH_ATTN: attention_launch(p.attn, p.max_tok, st); break;
-      case PH_SAMPLE:
-        sample(p.smp, p.max_tok, st);
-        if (p.has_tail) rmsnorm(p.tail, p.max_tok, st);
-        break;
+      case PH_SAMPLE: sample(p.smp, p.max_tok, st, p.has_tail ? &p.tail : nullptr); break;
       default: note(cudaErrorInvalidValue, "run_phases: unknown phase"); break;
     }
   }

@@ -263,7 +263,9 @@ struct SampleArgs {
   uint8_t *kept;               // nullable: [t][ldl] 1 where a token stays a candidate after suppress,
                                // top-k and top-p
 };
-void sample(const SampleArgs &a, int max_tok, cudaStream_t st);
+// tail (nullable): the next input row of each token (RmsArgs over the same
+// tokens), built and normalised by the sampler's CTA right after its sample
+void sample(const SampleArgs &a, int max_tok, cudaStream_t st, const RmsArgs *tail = nullptr);
 
 // ---------------------------------------------------------------------------
 // A decode frame as a list of phases, each one kernel launch (captured once
