@@ -193,6 +193,61 @@ q3t_status q3t_session_load_kv(q3t_session *s, const uint16_t *k, const uint16_t
 q3t_status q3t_session_last_ms(q3t_session *s, float *ms);
 void q3t_session_free(q3t_session *s);
 
+/* Speech-tokenizer encoder of the voice-clone path (codec/config.rs:79-121,
+ * built as config.rs:136-346 builds it).  ratios are the tokenizer's
+ * upsampling_ratios; the encoder downsamples by them in reverse order. */
+typedef struct {
+  int audio_channels;            /* 1 */
+  int num_filters;               /* 64 */
+  int kernel_size;               /* 7 */
+  int residual_kernel_size;      /* 3 */
+  int last_kernel_size;          /* 3 */
+  int compress;                  /* 2 */
+  int num_ratios;
+  int ratios[8];                 /* [8, 6, 5, 4] */
+  int hidden_size;               /* 512 */
+  int num_hidden_layers;         /* 8 */
+  int num_attention_heads;       /* 8 */
+  int num_key_value_heads;       /* 8 */
+  int head_dim;                  /* 64 */
+  int intermediate_size;         /* 2048 */
+  float norm_eps;                /* 1e-5 */
+  float rope_theta;              /* 1e4 */
+  int codebook_size;             /* 2048 */
+  int codebook_dim;              /* 256 (the quantizers' vector width) */
+  int num_quantizers;            /* 32 */
+  int num_semantic_quantizers;   /* 1 */
+  int downsample_factor;         /* 2 */
+} q3t_codec_encoder_config;
+
+typedef struct {
+  int device;                    /* CUDA device ordinal */
+  q3t_codec_encoder_config config;
+  const q3t_tensor *tensors;     /* "encoder.encoder.layers.*", "encoder.encoder_transformer.*",
+                                    "encoder.downsample.conv.weight", "encoder.quantizer.*" */
+  int num_tensors;
+} q3t_codec_encoder_desc;
+
+typedef struct q3t_codec_encoder q3t_codec_encoder;
+
+/* Replaces the Burn load of Qwen3TtsAudioCodecEncoder (codec/weights.rs,
+ * codec/config.rs:136-346): weights to device memory as f32, the codebook
+ * centroids embed_sum / clamp_min(cluster_usage, 1e-6) computed once. */
+q3t_status q3t_codec_encoder_load(const q3t_codec_encoder_desc *desc, q3t_codec_encoder **out);
+void q3t_codec_encoder_free(q3t_codec_encoder *enc);
+/* Frames the encoder emits for num_samples samples (conv.rs:44-64 lengths). */
+q3t_status q3t_codec_encoder_frames(const q3t_codec_encoder *enc, int64_t num_samples, int *frames);
+/* Qwen3TtsAudioCodecEncoder::encode_reference_prefix (codec/network/
+ * encoder.rs:121-136): wave [num_samples] 24 kHz mono f32 -> codes
+ * [n_valid][frames] (semantic codebooks first, then acoustic), n_valid in
+ * num_semantic_quantizers..num_quantizers; INVALID_INPUT when the frames
+ * exceed max_frames. */
+q3t_status q3t_codec_encode(q3t_codec_encoder *enc, const float *wave, int64_t num_samples, int n_valid,
+                            int64_t *codes, int max_frames, int *frames);
+/* Test hook: the hidden the quantizers read, [hidden_size][frames]. */
+q3t_status q3t_codec_encoder_hidden(q3t_codec_encoder *enc, const float *wave, int64_t num_samples,
+                                    float *hidden, int max_frames, int *frames);
+
 /* Codec decode (decode_waveform, codec/infer/mod.rs:94-111): codes
  * [B][num_quantizers][T] -> wave [B][n] f32 clamped to [-1, 1] and/or pcm
  * [B][n] i16 (to_pcm, :80-90).  *n = samples per item = (((4T-1)*8-1)*5-1)...

@@ -87,6 +87,23 @@ const FieldRow k_step_stats[] = {
     Q3T_F(q3t_step_stats, predictor_ms), Q3T_F(q3t_step_stats, talker_ms), Q3T_F(q3t_step_stats, prefill_tokens),
     Q3T_F(q3t_step_stats, first_tokens),
 };
+const FieldRow k_enc_config[] = {
+    Q3T_F(q3t_codec_encoder_config, audio_channels),      Q3T_F(q3t_codec_encoder_config, num_filters),
+    Q3T_F(q3t_codec_encoder_config, kernel_size),         Q3T_F(q3t_codec_encoder_config, residual_kernel_size),
+    Q3T_F(q3t_codec_encoder_config, last_kernel_size),    Q3T_F(q3t_codec_encoder_config, compress),
+    Q3T_F(q3t_codec_encoder_config, num_ratios),          Q3T_F(q3t_codec_encoder_config, ratios),
+    Q3T_F(q3t_codec_encoder_config, hidden_size),         Q3T_F(q3t_codec_encoder_config, num_hidden_layers),
+    Q3T_F(q3t_codec_encoder_config, num_attention_heads), Q3T_F(q3t_codec_encoder_config, num_key_value_heads),
+    Q3T_F(q3t_codec_encoder_config, head_dim),            Q3T_F(q3t_codec_encoder_config, intermediate_size),
+    Q3T_F(q3t_codec_encoder_config, norm_eps),            Q3T_F(q3t_codec_encoder_config, rope_theta),
+    Q3T_F(q3t_codec_encoder_config, codebook_size),       Q3T_F(q3t_codec_encoder_config, codebook_dim),
+    Q3T_F(q3t_codec_encoder_config, num_quantizers),      Q3T_F(q3t_codec_encoder_config, num_semantic_quantizers),
+    Q3T_F(q3t_codec_encoder_config, downsample_factor),
+};
+const FieldRow k_enc_desc[] = {
+    Q3T_F(q3t_codec_encoder_desc, device),  Q3T_F(q3t_codec_encoder_desc, config),
+    Q3T_F(q3t_codec_encoder_desc, tensors), Q3T_F(q3t_codec_encoder_desc, num_tensors),
+};
 #undef Q3T_F
 
 #define Q3T_S(S, table) {#S, sizeof(S), alignof(S), table, (int)(sizeof(table) / sizeof(table[0]))}
@@ -101,6 +118,8 @@ const StructRow k_structs[] = {
     Q3T_S(q3t_seed_controls, k_seed_controls),
     Q3T_S(q3t_batch_desc, k_batch_desc),
     Q3T_S(q3t_step_stats, k_step_stats),
+    Q3T_S(q3t_codec_encoder_config, k_enc_config),
+    Q3T_S(q3t_codec_encoder_desc, k_enc_desc),
 };
 #undef Q3T_S
 

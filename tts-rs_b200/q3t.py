@@ -96,6 +96,20 @@ class StepStats(C.Structure):
                 ("prefill_tokens", C.c_int), ("first_tokens", C.c_int)]
 
 
+class CodecEncoderConfig(C.Structure):
+    _fields_ = [(n, C.c_int) for n in (
+        "audio_channels", "num_filters", "kernel_size", "residual_kernel_size", "last_kernel_size",
+        "compress", "num_ratios")] + [("ratios", C.c_int * 8)] + [(n, C.c_int) for n in (
+        "hidden_size", "num_hidden_layers", "num_attention_heads", "num_key_value_heads", "head_dim",
+        "intermediate_size")] + [("norm_eps", C.c_float), ("rope_theta", C.c_float)] + [(n, C.c_int) for n in (
+        "codebook_size", "codebook_dim", "num_quantizers", "num_semantic_quantizers", "downsample_factor")]
+
+
+class CodecEncoderDesc(C.Structure):
+    _fields_ = [("device", C.c_int), ("config", CodecEncoderConfig), ("tensors", C.POINTER(Tensor)),
+                ("num_tensors", C.c_int)]
+
+
 EXPORTS = [
     "q3t_model_load", "q3t_model_free", "q3t_session_start", "q3t_session_step",
     "q3t_session_step_forced", "q3t_session_codes", "q3t_session_finish",
@@ -107,7 +121,8 @@ EXPORTS = [
     "q3t_kernel_launches", "q3t_text_project", "q3t_text_dims",
     "q3t_safetensors_open", "q3t_tensor_set_list", "q3t_tensor_set_free", "q3t_wav_write",
     "q3t_codec_last_ms", "q3t_session_seed", "q3t_abi_struct", "q3t_abi_field",
-    "q3t_sample_logits", "q3t_batch_logits",
+    "q3t_sample_logits", "q3t_batch_logits", "q3t_codec_encoder_load", "q3t_codec_encoder_free",
+    "q3t_codec_encoder_frames", "q3t_codec_encode", "q3t_codec_encoder_hidden",
 ]
 
 
@@ -174,6 +189,12 @@ def lib():
                                     C.c_int64, _I64]
         L.q3t_sample_logits.argtypes = [C.c_void_p, _F, C.c_int, C.POINTER(Sampling), _I64, C.c_int, C.c_double,
                                         _I64, C.POINTER(C.c_uint8)]
+        L.q3t_codec_encoder_load.argtypes = [C.POINTER(CodecEncoderDesc), C.POINTER(C.c_void_p)]
+        L.q3t_codec_encoder_free.argtypes = [C.c_void_p]
+        L.q3t_codec_encoder_free.restype = None
+        L.q3t_codec_encoder_frames.argtypes = [C.c_void_p, C.c_int64, C.POINTER(C.c_int)]
+        L.q3t_codec_encode.argtypes = [C.c_void_p, _F, C.c_int64, C.c_int, _I64, C.c_int, C.POINTER(C.c_int)]
+        L.q3t_codec_encoder_hidden.argtypes = [C.c_void_p, _F, C.c_int64, _F, C.c_int, C.POINTER(C.c_int)]
         L.q3t_abi_struct.argtypes = [C.c_char_p, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t),
                                      C.POINTER(C.c_int)]
         L.q3t_abi_field.argtypes = [C.c_char_p, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_size_t),
@@ -200,7 +221,8 @@ def abi_layout(name):
 STRUCTS = {"q3t_lm_config": LMConfig, "q3t_talker_config": TalkerConfig, "q3t_codec_config": CodecConfig,
            "q3t_tensor": Tensor, "q3t_model_desc": ModelDesc, "q3t_sampling": Sampling,
            "q3t_session_desc": SessionDesc, "q3t_seed_controls": SeedControls, "q3t_batch_desc": BatchDesc,
-           "q3t_step_stats": StepStats}
+           "q3t_step_stats": StepStats, "q3t_codec_encoder_config": CodecEncoderConfig,
+           "q3t_codec_encoder_desc": CodecEncoderDesc}
 
 
 def check(rc):
@@ -238,6 +260,79 @@ def codec_config(c) -> CodecConfig:
         cc.upsample_rates[i] = r
     cc.output_sample_rate = c.sample_rate
     return cc
+
+
+def codec_encoder_config(c) -> CodecEncoderConfig:
+    """q3t_codec_encoder_config from a synthetic.CodecEncoderConfig."""
+    e = CodecEncoderConfig()
+    e.audio_channels, e.num_filters, e.kernel_size = c.audio_channels, c.num_filters, c.kernel_size
+    e.residual_kernel_size, e.last_kernel_size, e.compress = c.residual_kernel_size, c.last_kernel_size, c.compress
+    e.num_ratios = len(c.upsampling_ratios)
+    for i, r in enumerate(c.upsampling_ratios):
+        e.ratios[i] = r
+    e.hidden_size, e.num_hidden_layers, e.num_attention_heads = c.hidden, c.n_layers, c.n_heads
+    e.num_key_value_heads, e.head_dim, e.intermediate_size = c.n_kv, c.head_dim, c.inter
+    e.norm_eps, e.rope_theta = c.norm_eps, c.theta
+    e.codebook_size, e.codebook_dim, e.num_quantizers = c.codebook_size, c.vq_dim, c.n_q
+    e.num_semantic_quantizers, e.downsample_factor = c.n_semantic, c.downsample_factor
+    return e
+
+
+class CodecEncoder:
+    """Speech-tokenizer encoder of the voice-clone path on the device
+    (q3t_codec_encoder_*; Qwen3TtsAudioCodecEncoder::encode_reference_prefix,
+    codec/network/encoder.rs:121-136).  Weights map checkpoint names to float
+    arrays (synthetic.codec_encoder_tensor_specs names)."""
+
+    def __init__(self, cfg, weights, device=0):
+        L = lib()
+        keep, tens = [], []
+        for name, arr in weights.items():
+            a = _f32(arr)
+            nb = name.encode()
+            keep += [a, nb]
+            tens.append(Tensor(nb, 0, a.ndim, (C.c_int64 * 4)(*(list(a.shape) + [0] * (4 - a.ndim))),
+                               a.ctypes.data))
+        arr = (Tensor * max(1, len(tens)))(*tens)
+        d = CodecEncoderDesc(device, codec_encoder_config(cfg), arr, len(tens))
+        h = C.c_void_p()
+        check(L.q3t_codec_encoder_load(C.byref(d), C.byref(h)))
+        self.h, self.cfg = h, cfg
+
+    def frames(self, n):
+        f = C.c_int()
+        check(lib().q3t_codec_encoder_frames(self.h, int(n), C.byref(f)))
+        return f.value
+
+    def encode(self, wave, n_valid=None):
+        """wave [n] f32 -> codes [n_valid][frames] (n_valid defaults to all codebooks)."""
+        wave = _f32(wave)
+        n_valid = self.cfg.n_q if n_valid is None else n_valid
+        T = self.frames(len(wave))
+        codes = np.zeros((n_valid, T), np.int64)
+        got = C.c_int()
+        check(lib().q3t_codec_encode(self.h, _fp(wave), len(wave), n_valid, codes.ctypes.data_as(_I64), T,
+                                     C.byref(got)))
+        assert got.value == T
+        return codes
+
+    def hidden(self, wave):
+        """The hidden [hidden][frames] the quantizers read."""
+        wave = _f32(wave)
+        T = self.frames(len(wave))
+        out = np.zeros((self.cfg.hidden, T), np.float32)
+        got = C.c_int()
+        check(lib().q3t_codec_encoder_hidden(self.h, _fp(wave), len(wave), _fp(out), T, C.byref(got)))
+        assert got.value == T
+        return out
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().q3t_codec_encoder_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
 
 
 class TensorSet:
