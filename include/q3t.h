@@ -248,6 +248,47 @@ q3t_status q3t_codec_encode(q3t_codec_encoder *enc, const float *wave, int64_t n
 q3t_status q3t_codec_encoder_hidden(q3t_codec_encoder *enc, const float *wave, int64_t num_samples,
                                     float *hidden, int max_frames, int *frames);
 
+/* ECAPA-TDNN speaker encoder of the voice-clone path (speaker/config.rs:
+ * 18-32).  channels[1..3] are the three SE-Res2Net blocks' width (equal,
+ * divisible by res2net_scale, <= 4096) and channels[0] must match it. */
+typedef struct {
+  int mel_dim;                   /* 128 */
+  int enc_dim;                   /* 1024 (the x-vector width) */
+  int channels[5];               /* [512, 512, 512, 512, 1536] */
+  int kernel_sizes[5];           /* [5, 3, 3, 3, 1] */
+  int dilations[5];              /* [1, 2, 3, 4, 1] */
+  int attention_channels;        /* 128 */
+  int res2net_scale;             /* 8 */
+  int se_channels;               /* 128 */
+  int sample_rate;               /* 24000 */
+} q3t_speaker_encoder_config;
+
+typedef struct {
+  int device;                    /* CUDA device ordinal */
+  q3t_speaker_encoder_config config;
+  const q3t_tensor *tensors;     /* "speaker_encoder.*" (speaker/weights.rs:73) */
+  int num_tensors;
+} q3t_speaker_encoder_desc;
+
+typedef struct q3t_speaker_encoder q3t_speaker_encoder;
+
+/* Replaces the Burn load of the speaker encoder (speaker/weights.rs): conv
+ * weights to device memory as f32, the Hann window and mel filterbank built
+ * once. */
+q3t_status q3t_speaker_encoder_load(const q3t_speaker_encoder_desc *desc, q3t_speaker_encoder **out);
+void q3t_speaker_encoder_free(q3t_speaker_encoder *enc);
+/* LoadedQwen3TtsSpeakerEncoder::encode_embedding (speaker/infer/mod.rs:
+ * 11-20): samples [num_samples] at sample_rate (>= 256 of them) -> the
+ * x-vector embedding [enc_dim] f32.  Clips too short for the TDNN blocks'
+ * reflect padding are INVALID_INPUT, as the reference's slices reject them. */
+q3t_status q3t_speaker_embed(q3t_speaker_encoder *enc, const float *samples, int64_t num_samples,
+                             float *embedding);
+/* Test hook: the log-mel features [mel_dim][frames] (feature.rs:32-150),
+ * frames = (num_samples + 768 - 1024) / 256 + 1; INVALID_INPUT when they
+ * exceed max_frames. */
+q3t_status q3t_speaker_mel(q3t_speaker_encoder *enc, const float *samples, int64_t num_samples, float *mel,
+                           int max_frames, int *frames);
+
 /* Codec decode (decode_waveform, codec/infer/mod.rs:94-111): codes
  * [B][num_quantizers][T] -> wave [B][n] f32 clamped to [-1, 1] and/or pcm
  * [B][n] i16 (to_pcm, :80-90).  *n = samples per item = (((4T-1)*8-1)*5-1)...
@@ -315,8 +356,9 @@ typedef struct {
  * (n_text - 8) + 2; pad_embed [hidden] = P(tts_pad), which is also the
  * trailing text hidden of these recipes.  inputs_embeds == NULL only reports
  * *rows; max_rows < rows or n_text < 8, n_codec_prefix < 2 or an id outside
- * its vocabulary is INVALID_INPUT.  The voice-clone seeds need the codec and
- * speaker encoders, which this library does not have. */
+ * its vocabulary is INVALID_INPUT.  The voice-clone recipes' seeds also hold
+ * the reference clip's codes (q3t_codec_encode) and x-vector
+ * (q3t_speaker_embed); this entry point does not build them. */
 q3t_status q3t_session_seed(q3t_model *model, const int64_t *text_ids, int n_text, const int64_t *leading_ids,
                             int n_leading, const q3t_seed_controls *controls, float *inputs_embeds, int max_rows,
                             int *rows, float *pad_embed);

@@ -104,6 +104,17 @@ const FieldRow k_enc_desc[] = {
     Q3T_F(q3t_codec_encoder_desc, device),  Q3T_F(q3t_codec_encoder_desc, config),
     Q3T_F(q3t_codec_encoder_desc, tensors), Q3T_F(q3t_codec_encoder_desc, num_tensors),
 };
+const FieldRow k_spk_config[] = {
+    Q3T_F(q3t_speaker_encoder_config, mel_dim),       Q3T_F(q3t_speaker_encoder_config, enc_dim),
+    Q3T_F(q3t_speaker_encoder_config, channels),      Q3T_F(q3t_speaker_encoder_config, kernel_sizes),
+    Q3T_F(q3t_speaker_encoder_config, dilations),     Q3T_F(q3t_speaker_encoder_config, attention_channels),
+    Q3T_F(q3t_speaker_encoder_config, res2net_scale), Q3T_F(q3t_speaker_encoder_config, se_channels),
+    Q3T_F(q3t_speaker_encoder_config, sample_rate),
+};
+const FieldRow k_spk_desc[] = {
+    Q3T_F(q3t_speaker_encoder_desc, device),  Q3T_F(q3t_speaker_encoder_desc, config),
+    Q3T_F(q3t_speaker_encoder_desc, tensors), Q3T_F(q3t_speaker_encoder_desc, num_tensors),
+};
 #undef Q3T_F
 
 #define Q3T_S(S, table) {#S, sizeof(S), alignof(S), table, (int)(sizeof(table) / sizeof(table[0]))}
@@ -120,6 +131,8 @@ const StructRow k_structs[] = {
     Q3T_S(q3t_step_stats, k_step_stats),
     Q3T_S(q3t_codec_encoder_config, k_enc_config),
     Q3T_S(q3t_codec_encoder_desc, k_enc_desc),
+    Q3T_S(q3t_speaker_encoder_config, k_spk_config),
+    Q3T_S(q3t_speaker_encoder_desc, k_spk_desc),
 };
 #undef Q3T_S
 

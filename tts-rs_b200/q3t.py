@@ -110,6 +110,17 @@ class CodecEncoderDesc(C.Structure):
                 ("num_tensors", C.c_int)]
 
 
+class SpeakerEncoderConfig(C.Structure):
+    _fields_ = [("mel_dim", C.c_int), ("enc_dim", C.c_int), ("channels", C.c_int * 5),
+                ("kernel_sizes", C.c_int * 5), ("dilations", C.c_int * 5)] + [(n, C.c_int) for n in (
+        "attention_channels", "res2net_scale", "se_channels", "sample_rate")]
+
+
+class SpeakerEncoderDesc(C.Structure):
+    _fields_ = [("device", C.c_int), ("config", SpeakerEncoderConfig), ("tensors", C.POINTER(Tensor)),
+                ("num_tensors", C.c_int)]
+
+
 EXPORTS = [
     "q3t_model_load", "q3t_model_free", "q3t_session_start", "q3t_session_step",
     "q3t_session_step_forced", "q3t_session_codes", "q3t_session_finish",
@@ -123,6 +134,7 @@ EXPORTS = [
     "q3t_codec_last_ms", "q3t_session_seed", "q3t_abi_struct", "q3t_abi_field",
     "q3t_sample_logits", "q3t_batch_logits", "q3t_codec_encoder_load", "q3t_codec_encoder_free",
     "q3t_codec_encoder_frames", "q3t_codec_encode", "q3t_codec_encoder_hidden",
+    "q3t_speaker_encoder_load", "q3t_speaker_encoder_free", "q3t_speaker_embed", "q3t_speaker_mel",
 ]
 
 
@@ -195,6 +207,11 @@ def lib():
         L.q3t_codec_encoder_frames.argtypes = [C.c_void_p, C.c_int64, C.POINTER(C.c_int)]
         L.q3t_codec_encode.argtypes = [C.c_void_p, _F, C.c_int64, C.c_int, _I64, C.c_int, C.POINTER(C.c_int)]
         L.q3t_codec_encoder_hidden.argtypes = [C.c_void_p, _F, C.c_int64, _F, C.c_int, C.POINTER(C.c_int)]
+        L.q3t_speaker_encoder_load.argtypes = [C.POINTER(SpeakerEncoderDesc), C.POINTER(C.c_void_p)]
+        L.q3t_speaker_encoder_free.argtypes = [C.c_void_p]
+        L.q3t_speaker_encoder_free.restype = None
+        L.q3t_speaker_embed.argtypes = [C.c_void_p, _F, C.c_int64, _F]
+        L.q3t_speaker_mel.argtypes = [C.c_void_p, _F, C.c_int64, _F, C.c_int, C.POINTER(C.c_int)]
         L.q3t_abi_struct.argtypes = [C.c_char_p, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t),
                                      C.POINTER(C.c_int)]
         L.q3t_abi_field.argtypes = [C.c_char_p, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_size_t),
@@ -222,7 +239,8 @@ STRUCTS = {"q3t_lm_config": LMConfig, "q3t_talker_config": TalkerConfig, "q3t_co
            "q3t_tensor": Tensor, "q3t_model_desc": ModelDesc, "q3t_sampling": Sampling,
            "q3t_session_desc": SessionDesc, "q3t_seed_controls": SeedControls, "q3t_batch_desc": BatchDesc,
            "q3t_step_stats": StepStats, "q3t_codec_encoder_config": CodecEncoderConfig,
-           "q3t_codec_encoder_desc": CodecEncoderDesc}
+           "q3t_codec_encoder_desc": CodecEncoderDesc, "q3t_speaker_encoder_config": SpeakerEncoderConfig,
+           "q3t_speaker_encoder_desc": SpeakerEncoderDesc}
 
 
 def check(rc):
@@ -329,6 +347,64 @@ class CodecEncoder:
     def close(self):
         if getattr(self, "h", None):
             lib().q3t_codec_encoder_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
+def speaker_encoder_config(c) -> SpeakerEncoderConfig:
+    """q3t_speaker_encoder_config from a synthetic.SpeakerEncoderConfig."""
+    e = SpeakerEncoderConfig()
+    e.mel_dim, e.enc_dim = c.mel_dim, c.enc_dim
+    for i in range(5):
+        e.channels[i], e.kernel_sizes[i], e.dilations[i] = c.enc_channels[i], c.enc_kernel_sizes[i], c.enc_dilations[i]
+    e.attention_channels, e.res2net_scale = c.enc_attention_channels, c.enc_res2net_scale
+    e.se_channels, e.sample_rate = c.enc_se_channels, c.sample_rate
+    return e
+
+
+class SpeakerEncoder:
+    """ECAPA-TDNN speaker encoder of the voice-clone path on the device
+    (q3t_speaker_*; LoadedQwen3TtsSpeakerEncoder::encode_embedding,
+    speaker/infer/mod.rs:11-20).  Weights map checkpoint names to float
+    arrays (synthetic.speaker_tensor_specs names)."""
+
+    def __init__(self, cfg, weights, device=0):
+        L = lib()
+        keep, tens = [], []
+        for name, arr in weights.items():
+            a = _f32(arr)
+            nb = name.encode()
+            keep += [a, nb]
+            tens.append(Tensor(nb, 0, a.ndim, (C.c_int64 * 4)(*(list(a.shape) + [0] * (4 - a.ndim))),
+                               a.ctypes.data))
+        arr = (Tensor * max(1, len(tens)))(*tens)
+        d = SpeakerEncoderDesc(device, speaker_encoder_config(cfg), arr, len(tens))
+        h = C.c_void_p()
+        check(L.q3t_speaker_encoder_load(C.byref(d), C.byref(h)))
+        self.h, self.cfg = h, cfg
+
+    def embed(self, samples):
+        """samples [n] f32 at the config's sample rate -> x-vector [enc_dim]."""
+        x = _f32(samples)
+        out = np.zeros(self.cfg.enc_dim, np.float32)
+        check(lib().q3t_speaker_embed(self.h, _fp(x), len(x), _fp(out)))
+        return out
+
+    def mel(self, samples):
+        """The log-mel features [mel_dim][frames] the network reads."""
+        x = _f32(samples)
+        T = max(self.cfg.frames(len(x)), 1)
+        out = np.zeros((self.cfg.mel_dim, T), np.float32)
+        got = C.c_int()
+        check(lib().q3t_speaker_mel(self.h, _fp(x), len(x), _fp(out), T, C.byref(got)))
+        assert got.value == T
+        return out
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().q3t_speaker_encoder_free(self.h)
             self.h = None
 
     def __del__(self):
