@@ -411,6 +411,7 @@ static void batch_init(q3t_batch *b, q3t_model *m, const q3t_batch_desc &d) {
   const int T = b->Tmax;
   b->x = ar.zalloc<float>((size_t)T * H);
   b->xn = ar.zalloc<uint16_t>((size_t)T * H);
+  b->xg = ar.zalloc<uint16_t>((size_t)T * H);
   b->ss = ar.zalloc<float>((size_t)(std::max(tc.talker.hidden_size, tc.predictor.hidden_size) / 128) * T);
   b->hlog = ar.zalloc<float>((size_t)T * std::max(b->V, b->PV));
   b->q = ar.zalloc<uint16_t>((size_t)T * 128 * std::max(tc.talker.num_attention_heads, tc.predictor.num_attention_heads));
@@ -573,9 +574,11 @@ static KVView pred_kv(q3t_batch *b) {
 
 
 // ---------------------------------------------------------------------------
-// X = bf16 rows [Tmax][ldx] of a batch buffer, loaded by TMA (descriptor per
-// buffer and token-tile height, made on first use); GEMM timeouts go to d_err.
-static GemmArgs gemm_bf16_x(q3t_batch *b, GemmArgs g, const uint16_t *x, int ldx) {
+// X = bf16 rows of a batch buffer, row t at x + t * ldx, `width` columns
+// (default ldx) and `rows` rows (default Tmax), loaded by TMA (descriptor per
+// buffer, row pitch and token-tile height, made on first use); GEMM timeouts
+// go to d_err.
+static GemmArgs gemm_bf16_x(q3t_batch *b, GemmArgs g, const uint16_t *x, int ldx, int width = 0, int rows = 0) {
   g.xmode = GX_BF16;
   g.xb = x;
   g.ldx = ldx;
@@ -584,7 +587,8 @@ static GemmArgs gemm_bf16_x(q3t_batch *b, GemmArgs g, const uint16_t *x, int ldx
   auto it = b->xmaps.find(key);
   if (it == b->xmaps.end()) {
     CUtensorMap m;
-    if (!make_tmap_bf16(&m, x, (uint64_t)ldx, (uint64_t)b->Tmax, (uint64_t)ldx * 2, 64, (uint32_t)(8 * g.nt)))
+    if (!make_tmap_bf16(&m, x, (uint64_t)(width ? width : ldx), (uint64_t)(rows ? rows : b->Tmax), (uint64_t)ldx * 2,
+                        64, (uint32_t)(8 * g.nt)))
       FAIL(Q3T_CUDA_ERROR, "TMA descriptor encoding failed for an activation buffer");
     it = b->xmaps.emplace(key, m).first;
   }
@@ -653,25 +657,52 @@ struct ProgBuilder {
     g.err = b->d_err;
     return g;
   }
-  GemmArgs resid(GemmArgs g) const {
+  // X = RMSNorm(x rows t * row_mul + row_add) as GX_SCALED: the bf16 rows of
+  // x * gamma the residual epilogue that wrote x left in xg, and the scale
+  // from its sum-of-squares partials.  The persistent frame kernel takes
+  // GX_NORM instead.
+  GemmArgs scaled_x(GemmArgs g, const float *gamma, float eps, int row_mul = 1, int row_add = 0) const {
+    if (b->use_frame) return norm_x(g, gamma, eps, row_mul, row_add);
+    const int H = g.K;
+    g = row_mul == 1 ? gemm_bf16_x(b, g, b->xg, H)
+                     : gemm_bf16_x(b, g, b->xg + (size_t)row_add * H, row_mul * H, H,
+                                   (b->Tmax - 1 - row_add) / row_mul + 1);
+    g.xmode = GX_SCALED;
+    g.xrow_mul = row_mul;
+    g.xrow_add = row_add;
+    g.ss = b->ss;
+    g.nss = g.K / 128;
+    g.ss_ld = b->Tmax;
+    g.eps = eps;
+    return g;
+  }
+  // residual epilogue; next_gamma (nullable): the gamma of the RMSNorm that
+  // reads the new rows through scaled_x
+  GemmArgs resid(GemmArgs g, const float *next_gamma) const {
     g.epi = GE_RESID;
     g.y = b->x;
     g.ldy = g.N;
     g.ss_out = b->ss;
     g.ss_ld = b->Tmax;
+    if (!b->use_frame && next_gamma) {
+      g.xg_out = b->xg;
+      g.xg_gamma = next_gamma;
+    }
     return g;
   }
   // One decoder stack (layer.rs:23-44) over the tokens of tv; the caller has
   // built the input rows x and their normalised bf16 copy xn.  Afterwards x
-  // holds the output residual rows and ss their sum-of-squares partials.
-  void stack(const LMStack &S, KVView kv, TokView tv, int max_tok, int max_units, int pw) {
+  // holds the output residual rows and ss their sum-of-squares partials,
+  // and with out_gamma xg holds bf16(x * out_gamma) for a scaled_x reader.
+  void stack(const LMStack &S, KVView kv, TokView tv, int max_tok, int max_units, int pw,
+             const float *out_gamma = nullptr) {
     const auto &c = S.cfg;
     const int H = c.hidden_size, I = c.intermediate_size, nh = c.num_attention_heads, nkv = c.num_key_value_heads;
     const int QD = nh * 128;
     const float eps = c.rms_norm_eps;
     for (int l = 0; l < c.num_hidden_layers; l++) {
       GemmArgs q = gemm_args(S.qkv[l], tv.ntok, max_tok);
-      q = l == 0 ? bf16_x(q, b->xn, H) : norm_x(q, S.in_norm[l], eps);
+      q = l == 0 ? bf16_x(q, b->xn, H) : scaled_x(q, S.in_norm[l], eps);
       q.epi = GE_QKV;
       q.q_norm = S.q_norm[l];
       q.k_norm = S.k_norm[l];
@@ -696,13 +727,15 @@ struct ProgBuilder {
       aa.ws = b->ws;
       aa.out = b->attn;
       push(at);
-      gemm(resid(bf16_x(gemm_args(S.o[l], tv.ntok, max_tok), b->attn, QD)), max_tok);
-      GemmArgs gu = norm_x(gemm_args(S.gu[l], tv.ntok, max_tok), S.post_norm[l], eps);
+      gemm(resid(bf16_x(gemm_args(S.o[l], tv.ntok, max_tok), b->attn, QD), S.post_norm[l]), max_tok);
+      GemmArgs gu = scaled_x(gemm_args(S.gu[l], tv.ntok, max_tok), S.post_norm[l], eps);
       gu.epi = GE_SILU;
       gu.h = b->act;
       gu.ldh = I;
       gemm(gu, max_tok);
-      gemm(resid(bf16_x(gemm_args(S.down[l], tv.ntok, max_tok), b->act, I)), max_tok);
+      gemm(resid(bf16_x(gemm_args(S.down[l], tv.ntok, max_tok), b->act, I),
+                 l + 1 < c.num_hidden_layers ? S.in_norm[l + 1] : out_gamma),
+           max_tok);
     }
   }
 };
@@ -899,14 +932,14 @@ static void build_pred(q3t_batch *b, int mt, std::vector<Phase> &out) {
   for (int j = 0; j < G - 1; j++) {
     if (j == 0) {
       TokView tv0{ntok2B, meta + b->off_p0seq(), meta + b->off_p0pos(), 0};
-      P.stack(m->pred, pred_kv(b), tv0, 2 * mt, 1, kPredPages);
+      P.stack(m->pred, pred_kv(b), tv0, 2 * mt, 1, kPredPages, m->pred.final_norm);
     } else {
       TokView tvj{ntokB, slot, meta + b->off_zero(), j + 1};
-      P.stack(m->pred, pred_kv(b), tvj, mt, 1, kPredPages);
+      P.stack(m->pred, pred_kv(b), tvj, mt, 1, kPredPages, m->pred.final_norm);
     }
     // lm_head j on the final-normed last position of each token's pass
-    GemmArgs hg = P.norm_x(gemm_args(m->lm_heads[j], ntokB, mt), m->pred.final_norm, pc.rms_norm_eps,
-                           j == 0 ? 2 : 1, j == 0 ? 1 : 0);
+    GemmArgs hg = P.scaled_x(gemm_args(m->lm_heads[j], ntokB, mt), m->pred.final_norm, pc.rms_norm_eps,
+                             j == 0 ? 2 : 1, j == 0 ? 1 : 0);
     hg.epi = GE_F32;
     hg.y = b->hlog;
     hg.ldy = PV;

@@ -225,6 +225,7 @@ struct q3t_batch {
   float *ss = nullptr;    // [hidden / 128][Tmax] sum-of-squares partials of the residual rows
   float *hlog = nullptr;  // [Tmax][max(V, PV)] head GEMM output
   uint16_t *xn = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
+  uint16_t *xg = nullptr;  // [Tmax][hidden] bf16(x * gamma of the next RMSNorm), written with x
   q3t::AttnWork ws{};
   // metadata
   int meta_n = 0;

@@ -267,6 +267,8 @@ Q3T_DEV void gemm_epilogue(const GemmArgs &a, int t, int rg, int lane, float4 v,
     x.z += v.z;
     x.w += v.w;
     *xp = x;
+    if (a.xg_out)  // gqk holds this lane's xg_gamma
+      store_bf16x4(a.xg_out + (size_t)t * a.ldy + n, x.x * gqk.x, x.y * gqk.y, x.z * gqk.z, x.w * gqk.w);
     const float ss = warp_sum(x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w);
     if (lane == 0) a.ss_out[(size_t)rg * a.ss_ld + t] = ss;
   } else if (a.epi == GE_BIAS_SILU || a.epi == GE_BIAS_BF16) {
@@ -350,6 +352,7 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
     gqk = *reinterpret_cast<const float4 *>((rg < a.nh ? a.q_norm : a.k_norm) + lane * 4);
     fr = *reinterpret_cast<const float4 *>(a.inv_freq + ((lane * 4) & 63));
   }
+  if (a.epi == GE_RESID && a.xg_out) gqk = *reinterpret_cast<const float4 *>(a.xg_gamma + rg * 128 + lane * 4);
   if constexpr (KA <= 4) {
     if (a.xmode == GX_NORM && r0 < rstep) {
       g0 = *reinterpret_cast<const float4 *>(a.gamma + k0 + c8 * 8);
@@ -408,11 +411,24 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
       }
     }
   }
-  if (a.xmode == GX_BF16) {
+  if (a.xmode != GX_NORM) {
     if (threadIdx.x == 0) {
       mbar_expect_tx(&bars[1], L::kX);
 #pragma unroll
       for (int i = 0; i < KA; i++) tma_load_2d(xsm + i * L::kXAtom, &a.tx, k0 + 64 * i, tok0, &bars[1]);
+    }
+    // GX_SCALED: 1 / rms of this CTA's epilogue tokens (partials summed in
+    // index order, as GX_NORM does), for the epilogue; the barriers before
+    // the MMA order these stores before their reads
+    if (a.xmode == GX_SCALED && (int)threadIdx.x < t_hi - t_lo) {
+      const float *sp = a.ss + (size_t)(tok0 + t_lo + threadIdx.x) * a.xrow_mul + a.xrow_add;
+      float p[kMaxNss];
+#pragma unroll
+      for (int i = 0; i < kMaxNss; i++) p[i] = i < a.nss ? sp[(size_t)i * a.ss_ld] : 0.f;
+      float sum = p[0];
+#pragma unroll
+      for (int i = 1; i < kMaxNss; i++) sum += p[i];
+      rms[threadIdx.x] = 1.f / sqrtf(sum / (float)a.K + a.eps);
     }
   } else if constexpr (KA <= 4) {
     // the scale of each row, then x * (1 / rms) * gamma -> bf16 at chunk
@@ -447,7 +463,7 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
   uint32_t err = 0;
   if (threadIdx.x == 0) {
     if (!mbar_wait(&bars[0], 0)) err |= 1u;
-    if (a.xmode == GX_BF16 && !mbar_wait(&bars[1], 0)) err |= 2u;
+    if (a.xmode != GX_NORM && !mbar_wait(&bars[1], 0)) err |= 2u;
     tc_fence_after();
     constexpr uint32_t idesc = umma_idesc_bf16(128, N);
 #pragma unroll
@@ -500,6 +516,13 @@ __global__ void __launch_bounds__(256, KA > 4 ? 1 : 2) k_gemm(const __grid_const
           v.z += p[c].z;
           v.w += p[c].w;
         }
+    }
+    if (a.xmode == GX_SCALED) {
+      const float d = rms[tt - t_lo];
+      v.x *= d;
+      v.y *= d;
+      v.z *= d;
+      v.w *= d;
     }
     const int i = (tt - t_lo - warp) >> 3;
     gemm_epilogue(a, tok0 + tt, rg, lane, v, meta + 2 * (tt - t_lo), i == 0 ? xres[0] : xres[1], i < 2, gqk, fr);
@@ -572,7 +595,8 @@ void gemm(const GemmArgs &a, int max_tok, cudaStream_t st) {
       ((a.epi == GE_BIAS_SILU || a.epi == GE_BIAS_BF16) && a.bias == nullptr) ||
       (a.epi == GE_BIAS_SILU && a.h == nullptr) || (a.epi == GE_BIAS_BF16 && a.y == nullptr) ||
       a.nss > kMaxNss || (a.epi == GE_RESID && (a.ss_out == nullptr || a.y == nullptr)) ||
-      (a.xmode == GX_NORM && atoms / a.cs > 4)) {
+      (a.xmode == GX_NORM && atoms / a.cs > 4) || (a.xmode == GX_SCALED && a.ss == nullptr) ||
+      (a.epi == GE_RESID && a.xg_out && a.xg_gamma == nullptr)) {
     note(cudaErrorInvalidValue, "k_gemm (shape / arguments)");
     return;
   }

@@ -128,14 +128,18 @@ void rmsnorm(float *x, int ldx, int row_mul, int row_add, Part add, const float 
 // thread-block clusters: the cs CTAs of a cluster share one 128-row output
 // block and split K; their f32 tiles are summed through distributed shared
 // memory in cluster-rank order (deterministic), and the epilogue runs on the
-// reduced rows.  X is bf16 rows, or f32 residual rows normalised on the fly
-// (RMSNorm from sum-of-squares partials).
+// reduced rows.  X is bf16 rows; f32 residual rows normalised on the fly
+// (RMSNorm from sum-of-squares partials); or bf16 rows of x * gamma written
+// by the residual epilogue that produced x, loaded like plain bf16 rows, with
+// the RMSNorm scale 1 / rms(x) of every token applied to the reduced
+// accumulator (W (x * gamma) / rms(x) = W RMSNorm(x)).
 // ---------------------------------------------------------------------------
-enum GemmX { GX_BF16 = 0, GX_NORM = 1 };
+enum GemmX { GX_BF16 = 0, GX_NORM = 1, GX_SCALED = 2 };
 enum GemmEpi {
   GE_F32 = 0,    // y[t][n] = acc
   GE_QKV = 1,    // q/k RMSNorm + RoPE; q -> bf16 q[t], k / v appended to the paged cache
-  GE_RESID = 2,  // y[t][n] += acc (residual stream), ss_out[n / 128][t] = sum of squares of the new rows
+  GE_RESID = 2,  // y[t][n] += acc (residual stream), ss_out[n / 128][t] = sum of squares of the new rows;
+                 // with xg_out also xg_out[t][n] = bf16(y[t][n] * xg_gamma[n]) (the next GX_SCALED input)
   GE_SILU = 3,   // row block r = [gate 64r..64r+63 | up 64r..64r+63]: h[t][64r + i] = bf16(silu(g) * u)
   GE_BIAS_SILU = 4,  // h[t][n] = bf16(silu(acc + bias[n]))
   GE_BIAS_BF16 = 5,  // y[t][n] = bf16-rounded (acc + bias[n]), stored as f32
@@ -158,7 +162,7 @@ bool make_tmap(CUtensorMap *m, CUtensorMapDataType type, int rank, const void *b
 
 struct GemmArgs {
   CUtensorMap tw;      // weights W [N][K] (Linear::tm)
-  CUtensorMap tx;      // GX_BF16: X rows [rows][K], box 64 x 8*nt
+  CUtensorMap tx;      // GX_BF16 / GX_SCALED: X rows [rows][K], box 64 x 8*nt
   int N, K;
   int cs;              // cluster size = K splits (1, 2, 4 or 8)
   int nt;              // 8-token MMA tiles per CTA (1, 2, 4 or 8)
@@ -167,7 +171,8 @@ struct GemmArgs {
   const uint16_t *xb;  // GX_BF16: X[t][ldx]
   const float *x;      // GX_NORM: row t is x[t * xrow_mul + xrow_add][0..K)
   int ldx, xrow_mul, xrow_add;
-  const float *ss;     // GX_NORM: sum of squares of row r = sum_i ss[i * ss_ld + r], i < nss
+  const float *ss;     // GX_NORM / GX_SCALED: sum of squares of row r = sum_i ss[i * ss_ld + r], i < nss
+                       // (GX_SCALED: row r = t * xrow_mul + xrow_add of token t)
   int nss, ss_ld;
   const float *gamma;  // GX_NORM: RMSNorm weight [K]
   float eps;
@@ -175,6 +180,8 @@ struct GemmArgs {
   float *y;            // GE_F32 output / GE_RESID residual, [t][ldy]
   int ldy;
   float *ss_out;       // GE_RESID: [N / 128][ss_ld]
+  uint16_t *xg_out;    // GE_RESID, nullable: bf16 rows [t][ldy] of the new residual times xg_gamma
+  const float *xg_gamma;
   uint16_t *h;         // GE_SILU / GE_BIAS_SILU: [t][ldh]
   int ldh;
   const float *bias;   // GE_BIAS_SILU / GE_BIAS_BF16: [N]
