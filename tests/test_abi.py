@@ -139,3 +139,26 @@ def test_layout_check_catches_a_missing_field():
     cache = {}
     rust_layout("q3t_step_stats", structs, cache)
     assert cache["q3t_step_stats"][2] != q3t.abi_layout("q3t_step_stats")[2]
+
+
+def test_encoder_loads_reject_bad_input_without_a_gpu():
+    """The voice-clone encoders validate their config and arguments on the
+    host before any CUDA call, so these fail the same way with no GPU."""
+    import numpy as np
+    import synthetic as S
+    with pytest.raises(q3t.Q3TError) as e:  # 32 channels do not split into 5 Res2Net groups
+        q3t.SpeakerEncoder(S.SpeakerEncoderConfig().small(enc_res2net_scale=5), {})
+    assert e.value.status == q3t.INVALID_INPUT
+    with pytest.raises(q3t.Q3TError) as e:  # an SE bottleneck wider than the gate kernel holds
+        q3t.SpeakerEncoder(S.SpeakerEncoderConfig().small(enc_se_channels=2048), {})
+    assert e.value.status == q3t.INVALID_INPUT
+    with pytest.raises(q3t.Q3TError) as e:  # query heads not a multiple of the kv heads
+        q3t.CodecEncoder(S.CodecEncoderConfig().small(n_heads=3, n_kv=2), {})
+    assert e.value.status == q3t.INVALID_INPUT
+    L = q3t.lib()
+    x = np.zeros(4096, np.float32)
+    out = np.zeros(4096, np.float32)
+    fp = lambda a: a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    assert L.q3t_speaker_embed(None, fp(x), len(x), fp(out)) == q3t.INVALID_INPUT
+    assert L.q3t_speaker_mel(None, fp(x), len(x), fp(out), 16, None) == q3t.INVALID_INPUT
+    assert L.q3t_codec_encode(None, fp(x), len(x), 1, None, 16, None) == q3t.INVALID_INPUT
