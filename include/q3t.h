@@ -356,12 +356,41 @@ typedef struct {
  * (n_text - 8) + 2; pad_embed [hidden] = P(tts_pad), which is also the
  * trailing text hidden of these recipes.  inputs_embeds == NULL only reports
  * *rows; max_rows < rows or n_text < 8, n_codec_prefix < 2 or an id outside
- * its vocabulary is INVALID_INPUT.  The voice-clone recipes' seeds also hold
- * the reference clip's codes (q3t_codec_encode) and x-vector
- * (q3t_speaker_embed); this entry point does not build them. */
+ * its vocabulary is INVALID_INPUT.  The voice-clone recipes' seeds are
+ * q3t_session_seed_voice_clone. */
 q3t_status q3t_session_seed(q3t_model *model, const int64_t *text_ids, int n_text, const int64_t *leading_ids,
                             int n_leading, const q3t_seed_controls *controls, float *inputs_embeds, int max_rows,
                             int *rows, float *pad_embed);
+
+/* The prompt seed of the voice-clone recipes, build_voice_clone_seed
+ * (session_seed.rs:248-322), on the device, from the x-vector of
+ * q3t_speaker_embed (speaker [hidden], cast to bf16) and, for the in-context
+ * recipe, the reference clip's codes of q3t_codec_encode (ref_codes
+ * [num_code_groups][ref_frames], group 0 in the talker codec vocabulary,
+ * the others in the predictor's) with its text ids (3 role ids, body, 2
+ * trailing ids).  With P and E as in q3t_session_seed and n =
+ * n_codec_prefix:
+ *   inputs_embeds = [ P(text_ids[0..3])
+ *                     P(pad) + E(codec_prefix_ids[i]), i < n - 2
+ *                     P(pad) + speaker,  P(bos) + E(codec_pad_id)
+ *                     then, ref_text_ids == NULL (x-vector recipe):
+ *                       P(body[0]) + E(codec_bos_id)           (if any body)
+ *                     else (build_voice_clone_icl_seed, :324-396), with
+ *                     text = P(ref body + body + eos), codec = [E(codec_bos_id),
+ *                     frame t: sum over groups g of Emb_g(ref_codes[g][t])]:
+ *                       text[i] (P(pad) past its end) + codec[i], i < 1 + ref_frames ]
+ * trailing_text = P(body[1..]), P(eos) (x-vector), or the text rows past
+ * the codec rows, or P(pad) when there are none (in-context); every sum is
+ * rounded to bf16 as the reference's bf16 adds, the frame sums group by
+ * group.  inputs_embeds == NULL only reports *rows and *trailing_rows;
+ * outputs too small, ids outside their vocabularies, n_text < 8,
+ * n_ref_text < 5, n_codec_prefix < 2 or an in-context call without codes
+ * are INVALID_INPUT. */
+q3t_status q3t_session_seed_voice_clone(q3t_model *model, const int64_t *text_ids, int n_text, const float *speaker,
+                                        const int64_t *ref_text_ids, int n_ref_text, const int64_t *ref_codes,
+                                        int ref_frames, const q3t_seed_controls *controls, float *inputs_embeds,
+                                        int max_rows, int *rows, float *trailing_text, int max_trailing,
+                                        int *trailing_rows, float *pad_embed);
 
 /* ------------------------------- file IO --------------------------------- */
 /* A memory-mapped .safetensors checkpoint whose float tensors (F32 and BF16

@@ -315,6 +315,68 @@ class OracleTalker:
                  (pad + E[controls["codec_bos_id"]])[None]]
         return bf16_round(np.concatenate(segs)), pad
 
+    def ref_codec_sum(self, ref_codes):
+        """sum_ref_codec_embeddings (session_seed.rs:602-641): codes
+        [groups][T] -> [T][hidden], group 0 through the talker codec
+        embedding, group g >= 1 through the predictor's embedding g - 1
+        (:643-655), added group by group as bf16 tensors."""
+        ref_codes = np.asarray(ref_codes, np.int64)
+        G = self.cfg.n_groups
+        if ref_codes.ndim != 2 or ref_codes.shape[0] != G or ref_codes.shape[1] == 0:
+            raise ValueError(f"reference codes must be [{G}, T > 0]")
+        s = f32(self.w["talker.model.codec_embedding.weight"])[ref_codes[0]]
+        for g in range(1, G):
+            s = bf16_round(s + f32(self.w[f"talker.code_predictor.model.codec_embedding.{g - 1}.weight"])[ref_codes[g]])
+        return s
+
+    def session_seed_voice_clone(self, text_ids, controls, speaker, ref_text_ids=None, ref_codes=None):
+        """build_voice_clone_seed (session_seed.rs:248-322): (inputs_embeds,
+        trailing_text_hidden, tts_pad embedding).  The codec prefix is
+        voice_clone_codec_prefix (:538-584): [pad + E(tag) per tag id, pad +
+        speaker x-vector (cast to bf16), bos + E(codec_pad)].  Without
+        reference text (x-vector only) the seed ends with P(body[0]) +
+        E(codec_bos) (:474-493) and the trailing text is P(body[1..]) then
+        P(eos) (:495-512); with it, build_voice_clone_icl_seed (:324-396):
+        P(reference body + target body + eos) aligned with [E(codec_bos),
+        summed reference frames], the longer side's excess becoming the
+        trailing text (or pad rows filling the text side, trailing P(pad))."""
+        text_ids = np.asarray(text_ids, np.int64)
+        cp = np.asarray(controls["codec_prefix_ids"], np.int64)
+        H = self.cfg.talker.hidden
+        spk = bf16_round(np.asarray(speaker, np.float32).reshape(-1))
+        if len(text_ids) < 8 or len(cp) < 2 or spk.shape != (H,):
+            raise ValueError("need >= 8 text ids, >= 2 codec prefix ids and a [hidden] speaker embedding")
+        E = f32(self.w["talker.model.codec_embedding.weight"])
+        bos, eos, pad = self.text_project([controls["tts_bos_token_id"], controls["tts_eos_token_id"],
+                                           controls["tts_pad_token_id"]])
+        role = self.text_project(text_ids[:3])
+        n = len(cp)
+        codec_prefix = np.concatenate([E[cp[:n - 2]], spk[None], E[controls["codec_pad_id"]][None]])
+        prefix_text = np.concatenate([np.repeat(pad[None], n - 1, 0), bos[None]])
+        prefix = bf16_round(prefix_text + codec_prefix)
+        body_ids = text_ids[3:len(text_ids) - 5]
+        if ref_text_ids is None:
+            segs = [role, prefix]
+            if len(body_ids):
+                segs.append(bf16_round(self.text_project(body_ids[:1]) + E[controls["codec_bos_id"]]))
+            rest = body_ids[1:]
+            trailing = eos[None] if len(rest) == 0 else np.concatenate([self.text_project(rest), eos[None]])
+            return np.concatenate(segs), trailing, pad
+        ref_text_ids = np.asarray(ref_text_ids, np.int64)
+        if len(ref_text_ids) < 5 or ref_codes is None:
+            raise ValueError("the in-context recipe needs >= 5 reference text ids and reference codes")
+        all_ids = np.concatenate([ref_text_ids[3:len(ref_text_ids) - 2], body_ids,
+                                  [controls["tts_eos_token_id"]]]).astype(np.int64)
+        text = self.text_project(all_ids)
+        codec = np.concatenate([E[controls["codec_bos_id"]][None], self.ref_codec_sum(ref_codes)])
+        tl, cl = len(text), len(codec)
+        if tl > cl:
+            icl, trailing = bf16_round(text[:cl] + codec), text[cl:]
+        else:
+            icl = bf16_round(np.concatenate([text, np.repeat(pad[None], cl - tl, 0)]) + codec)
+            trailing = pad[None]
+        return np.concatenate([role, prefix, icl]), trailing, pad
+
     def codec_head(self, hidden):
         h = f32(hidden).reshape(-1, self.cfg.talker.hidden)
         out = np.zeros((h.shape[0], self.cfg.talker.vocab), np.float32)

@@ -124,3 +124,61 @@ def test_session_seed_rejects_bad_input(text_model):
         with pytest.raises(q3t.Q3TError) as e:
             model.session_seed(bad_text, ctl)
         assert e.value.status == 1  # INVALID_INPUT
+
+
+@pytest.mark.parametrize("recipe,ref_frames", [("xvector", 0), ("icl", 3), ("icl", 40)])
+def test_voice_clone_seed_matches_oracle(text_model, recipe, ref_frames):
+    """q3t_session_seed_voice_clone (build_voice_clone_seed,
+    session_seed.rs:248-322) on the device vs the oracle's assembly, for the
+    x-vector recipe and the in-context recipe with fewer reference frames
+    than text rows (the excess text trails) and more (pad rows fill the text
+    side): same row counts, bf16 rows within the text projection tolerance,
+    the rows that hold no projected text (x-vector sum, reference frame
+    sums) bit-identical where the oracle's text term is identical too."""
+    cfg, w, model, ot = text_model
+    g = np.random.default_rng([7, ref_frames])
+    H, G = cfg.talker.hidden, cfg.n_groups
+    text = g.integers(0, TEXT_VOCAB - 3, 20)
+    spk = g.standard_normal(H).astype(np.float32)
+    kw = {}
+    if recipe == "icl":
+        kw = dict(ref_text_ids=g.integers(0, TEXT_VOCAB - 3, 16),
+                  ref_codes=np.concatenate([g.integers(0, cfg.talker.vocab, (1, ref_frames)),
+                                            g.integers(0, cfg.predictor.vocab, (G - 1, ref_frames))]))
+    got, trail, pad = model.session_seed_voice_clone(text, SEED_CONTROLS, spk, **kw)
+    ref, ref_trail, ref_pad = ot.session_seed_voice_clone(text, SEED_CONTROLS, spk, **kw)
+    assert got.shape == ref.shape and trail.shape == ref_trail.shape
+    n = len(SEED_CONTROLS["codec_prefix_ids"])
+    if recipe == "xvector":
+        assert got.shape[0] == 3 + n + 1 and trail.shape[0] == 12 - 1 + 1
+    else:
+        assert got.shape[0] == 3 + n + 1 + ref_frames
+        text_len = (16 - 5) + 12 + 1
+        assert trail.shape[0] == (text_len - 1 - ref_frames if text_len > 1 + ref_frames else 1)
+    for a in (got, trail, pad):
+        assert np.array_equal(a, S.bf16_round(a)), "rows hold bf16 values"
+    _close(got, ref, f"voice-clone seed rows ({recipe}, {ref_frames} frames)")
+    _close(trail, ref_trail, "trailing text")
+    _close(pad, ref_pad, "pad embedding")
+    if recipe == "icl" and ref_frames > 1 + 24 - 1:  # pad rows past the text: P(pad) + frame sum
+        pad_rows = slice(3 + n + 24, 3 + n + 1 + ref_frames)
+        exact = np.array_equal(pad, ref_pad)
+        assert not exact or np.array_equal(got[pad_rows], ref[pad_rows])
+
+
+def test_voice_clone_seed_rejects_bad_input(text_model):
+    cfg, w, model, ot = text_model
+    text = np.arange(20, dtype=np.int64)
+    spk = np.zeros(cfg.talker.hidden, np.float32)
+    G = cfg.n_groups
+    codes = np.zeros((G, 4), np.int64)
+    bad_codes = codes.copy()
+    bad_codes[3, 1] = cfg.predictor.vocab  # a predictor-group code outside its vocabulary
+    for args, kw in (((text[:7], SEED_CONTROLS, spk), {}),
+                     ((text, dict(SEED_CONTROLS, codec_prefix_ids=[2048]), spk), {}),
+                     ((text, SEED_CONTROLS, spk), dict(ref_text_ids=text[:4], ref_codes=codes)),
+                     ((text, SEED_CONTROLS, spk), dict(ref_text_ids=text, ref_codes=bad_codes)),
+                     ((text, SEED_CONTROLS, spk), dict(ref_text_ids=text))):
+        with pytest.raises(q3t.Q3TError) as e:
+            model.session_seed_voice_clone(*args, **kw)
+        assert e.value.status == 1  # INVALID_INPUT

@@ -210,3 +210,78 @@ def test_session_seed_oracle_layout():
     np.testing.assert_array_equal(rows[14], S.bf16_round(tpad + E[2048]))
     short, _ = ot.session_seed(text[:8], SEED_CONTROLS)  # empty body, no leading ids
     assert short.shape[0] == 3 + 4 + 0 + 2
+
+
+def _clone_fixture():
+    cfg = S.TalkerConfig().small(talker_layers=1, predictor_layers=1)
+    w = S.make_talker_weights(cfg, seed=0)
+    w.update(S.make_text_weights(cfg, seed=0, text_vocab=512, text_hidden=256))
+    return cfg, w, O.OracleTalker(cfg, w)
+
+
+def test_voice_clone_seed_oracle_layout():
+    """build_voice_clone_seed without reference text (the x-vector recipe,
+    session_seed.rs:248-322) in the oracle: 3 role rows, the codec prefix of
+    voice_clone_codec_prefix (:538-584: pad + E(tag) for all prefix ids but
+    the last two, pad + bf16(x-vector), bos + E(codec_pad)), then P(body[0])
+    + E(codec_bos); trailing text P(body[1..]) then P(eos)."""
+    cfg, w, ot = _clone_fixture()
+    c = SEED_CONTROLS
+    H = cfg.talker.hidden
+    text = np.arange(10, 22, dtype=np.int64)  # role 10..12, body 13..16, 5 trailing ids
+    spk = np.random.default_rng(4).standard_normal(H).astype(np.float32)
+    rows, trailing, pad = ot.session_seed_voice_clone(text, c, spk)
+    P = lambda ids: ot.text_project(np.asarray(ids, np.int64))
+    E = w["talker.model.codec_embedding.weight"].astype(np.float32)
+    bos, eos, tpad = P([c["tts_bos_token_id"], c["tts_eos_token_id"], c["tts_pad_token_id"]])
+    n = len(c["codec_prefix_ids"])
+    assert rows.shape == (3 + n + 1, H)
+    np.testing.assert_array_equal(pad, tpad)
+    np.testing.assert_array_equal(rows[:3], P(text[:3]))
+    for i, cid in enumerate(c["codec_prefix_ids"][:n - 2]):
+        np.testing.assert_array_equal(rows[3 + i], S.bf16_round(tpad + E[cid]))
+    np.testing.assert_array_equal(rows[3 + n - 2], S.bf16_round(tpad + S.bf16_round(spk)))
+    np.testing.assert_array_equal(rows[3 + n - 1], S.bf16_round(bos + E[c["codec_pad_id"]]))
+    np.testing.assert_array_equal(rows[3 + n], S.bf16_round(P(text[3:4])[0] + E[c["codec_bos_id"]]))
+    np.testing.assert_array_equal(trailing, np.concatenate([P(text[4:7]), eos[None]]))
+    short, tr, _ = ot.session_seed_voice_clone(text[:8], c, spk)  # empty body: no bos row, trailing = eos
+    assert short.shape[0] == 3 + n and tr.shape[0] == 1
+    np.testing.assert_array_equal(tr[0], eos)
+
+
+@pytest.mark.parametrize("ref_frames", [2, 9])
+def test_voice_clone_icl_seed_oracle_layout(ref_frames):
+    """build_voice_clone_icl_seed (session_seed.rs:324-396): text = P(ref
+    body + target body + eos) against codec = [E(codec_bos), the summed
+    reference frames]; with more text than codec rows the excess text is the
+    trailing text, otherwise pad rows fill the text side and the trailing
+    text is P(pad).  The frame sum (:602-655) adds the 16 group embeddings
+    as bf16 tensors in group order."""
+    cfg, w, ot = _clone_fixture()
+    c = SEED_CONTROLS
+    H, G = cfg.talker.hidden, cfg.n_groups
+    text = np.arange(30, 42, dtype=np.int64)              # target body 33..36
+    ref_text = np.arange(60, 68, dtype=np.int64)          # ref body 63..65 (3 ids, 2 trailing)
+    g = np.random.default_rng(ref_frames)
+    codes = g.integers(0, 2048, (G, ref_frames))
+    spk = g.standard_normal(H).astype(np.float32)
+    rows, trailing, pad = ot.session_seed_voice_clone(text, c, spk, ref_text_ids=ref_text, ref_codes=codes)
+    n = len(c["codec_prefix_ids"])
+    P = lambda ids: ot.text_project(np.asarray(ids, np.int64))
+    E = w["talker.model.codec_embedding.weight"].astype(np.float32)
+    s = E[codes[0]]
+    for j in range(1, G):
+        s = S.bf16_round(s + w[f"talker.code_predictor.model.codec_embedding.{j - 1}.weight"][codes[j]])
+    codec = np.concatenate([E[c["codec_bos_id"]][None], s])
+    all_text = P(np.concatenate([ref_text[3:6], text[3:7], [c["tts_eos_token_id"]]]))  # 8 rows
+    assert rows.shape == (3 + n + 1 + ref_frames, H)
+    icl = rows[3 + n:]
+    if len(all_text) > len(codec):  # 8 text rows against 3 codec rows
+        np.testing.assert_array_equal(icl, S.bf16_round(all_text[:len(codec)] + codec))
+        np.testing.assert_array_equal(trailing, all_text[len(codec):])
+    else:  # 8 text rows + 2 pad rows against 10 codec rows
+        filled = np.concatenate([all_text, np.repeat(pad[None], len(codec) - len(all_text), 0)])
+        np.testing.assert_array_equal(icl, S.bf16_round(filled + codec))
+        np.testing.assert_array_equal(trailing, pad[None])
+    with pytest.raises(ValueError):
+        ot.session_seed_voice_clone(text, c, spk, ref_text_ids=ref_text)  # no reference codes

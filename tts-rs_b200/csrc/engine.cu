@@ -2334,6 +2334,144 @@ extern "C" q3t_status q3t_session_seed(q3t_model *m, const int64_t *text_ids, in
   });
 }
 
+extern "C" q3t_status q3t_session_seed_voice_clone(q3t_model *m, const int64_t *text_ids, int n_text,
+                                                   const float *speaker, const int64_t *ref_text_ids, int n_ref_text,
+                                                   const int64_t *ref_codes, int ref_frames,
+                                                   const q3t_seed_controls *c, float *inputs_embeds, int max_rows,
+                                                   int *rows, float *trailing, int max_trailing, int *trailing_rows,
+                                                   float *pad_embed) {
+  const bool icl = ref_text_ids != nullptr;
+  if (!m || !text_ids || !speaker || !c || !rows || !trailing_rows ||
+      (c->n_codec_prefix > 0 && !c->codec_prefix_ids) || (icl && (!ref_codes || ref_frames < 1))) {
+    set_error("q3t_session_seed_voice_clone: bad argument");
+    return Q3T_INVALID_INPUT;
+  }
+  if (!m->text_emb || !m->has_talker) {
+    set_error("q3t_session_seed_voice_clone: the model has no talker / text_embedding / text_projection tensors");
+    return Q3T_INVALID_INPUT;
+  }
+  // text_ids = 3 role ids, the body, 5 trailing ids; reference text = 3 role
+  // ids, its body, 2 trailing ids (session_seed.rs:337-338)
+  if (n_text < 8 || c->n_codec_prefix < 2 || (icl && n_ref_text < 5)) {
+    set_error("q3t_session_seed_voice_clone: %d text ids (>= 8), %d reference text ids (>= 5) and %d codec prefix "
+              "ids (>= 2)",
+              n_text, n_ref_text, c->n_codec_prefix);
+    return Q3T_INVALID_INPUT;
+  }
+  const int H = m->tc.talker.hidden_size, V = m->tc.talker.vocab_size, PV = m->tc.predictor.vocab_size;
+  const int G = m->tc.num_code_groups, ncp = c->n_codec_prefix, body = n_text - 8;
+  const int T = icl ? ref_frames : 0;
+  // projected rows: [bos, eos, pad], role (3), then the body (x-vector
+  // recipe) or reference body + target body + eos (in-context recipe)
+  enum { BOS = 0, EOS = 1, PAD = 2, ROLE = 3, TXT = 6 };
+  std::vector<int64_t> pid = {c->tts_bos_token_id, c->tts_eos_token_id, c->tts_pad_token_id};
+  for (int i = 0; i < 3; i++) pid.push_back(text_ids[i]);
+  if (icl)
+    for (int i = 3; i < n_ref_text - 2; i++) pid.push_back(ref_text_ids[i]);
+  for (int i = 3; i < n_text - 5; i++) pid.push_back(text_ids[i]);
+  if (icl) pid.push_back(c->tts_eos_token_id);
+  const int text_len = (int)pid.size() - TXT;
+  for (int64_t id : pid)
+    if (id < 0 || id >= m->text_vocab) {
+      set_error("q3t_session_seed_voice_clone: text token id %lld outside [0, %d)", (long long)id, m->text_vocab);
+      return Q3T_INVALID_INPUT;
+    }
+  std::vector<int64_t> cid(c->codec_prefix_ids, c->codec_prefix_ids + ncp - 2);
+  cid.push_back(c->codec_pad_id);
+  cid.push_back(c->codec_bos_id);
+  for (int64_t id : cid)
+    if (id < 0 || id >= V) {
+      set_error("q3t_session_seed_voice_clone: codec token id %lld outside [0, %d)", (long long)id, V);
+      return Q3T_INVALID_INPUT;
+    }
+  for (int g = 0; g < (icl ? G : 0); g++)
+    for (int t = 0; t < T; t++) {
+      const int64_t id = ref_codes[(size_t)g * T + t];
+      if (id < 0 || id >= (g == 0 ? V : PV)) {
+        set_error("q3t_session_seed_voice_clone: reference code %lld of group %d outside [0, %d)", (long long)id, g,
+                  g == 0 ? V : PV);
+        return Q3T_INVALID_INPUT;
+      }
+    }
+  // per output row: projected row, codec id, X row (-1: none); X row 0 is
+  // the x-vector, X row 1 + t reference frame t
+  std::vector<int> tr, ci, xr;
+  auto row = [&](int t, int c_id, int x) {
+    tr.push_back(t);
+    ci.push_back(c_id);
+    xr.push_back(x);
+  };
+  for (int i = 0; i < 3; i++) row(ROLE + i, -1, -1);
+  // voice_clone_codec_prefix (session_seed.rs:538-584)
+  for (int i = 0; i < ncp - 2; i++) row(PAD, (int)c->codec_prefix_ids[i], -1);
+  row(PAD, -1, 0);
+  row(BOS, (int)c->codec_pad_id, -1);
+  std::vector<int> trail;  // trailing text hidden: projected rows
+  if (!icl) {  // x-vector recipe (:299-318)
+    if (body > 0) row(TXT, (int)c->codec_bos_id, -1);
+    for (int i = 1; i < body; i++) trail.push_back(TXT + i);
+    trail.push_back(EOS);
+  } else {  // build_voice_clone_icl_seed (:324-396)
+    const int codec_len = 1 + T;
+    for (int i = 0; i < codec_len; i++) row(i < text_len ? TXT + i : PAD, i == 0 ? (int)c->codec_bos_id : -1, i);
+    if (text_len > codec_len)
+      for (int i = codec_len; i < text_len; i++) trail.push_back(TXT + i);
+    else
+      trail.push_back(PAD);
+  }
+  const int S = (int)tr.size(), NT = (int)trail.size();
+  *rows = S;
+  *trailing_rows = NT;
+  if (!inputs_embeds) return Q3T_OK;
+  if (max_rows < S || max_trailing < NT || !trailing) {
+    set_error("q3t_session_seed_voice_clone: the seed has %d rows and %d trailing rows, the outputs hold %d and %d",
+              S, NT, max_rows, max_trailing);
+    return Q3T_INVALID_INPUT;
+  }
+  for (int t : trail) row(t, -1, -1);  // trailing rows: the projected rows as they are
+  std::lock_guard<std::mutex> lock(m->tp_mu);
+  return guard([&] {
+    CK(cudaSetDevice(m->device));
+    const int np = (int)pid.size(), R = S + NT;
+    float *P = nullptr, *out = nullptr, *X = nullptr;
+    int *d_idx = nullptr;
+    int64_t *d_codes = nullptr;
+    CK(cudaMalloc(&P, (size_t)np * H * sizeof(float)));
+    struct Free {
+      std::vector<void *> p;
+      ~Free() {
+        for (void *q : p) cudaFree(q);
+      }
+    } fr;
+    fr.p.push_back(P);
+    CK(cudaMalloc(&out, (size_t)R * H * sizeof(float)));
+    fr.p.push_back(out);
+    CK(cudaMalloc(&X, (size_t)(1 + T) * H * sizeof(float)));
+    fr.p.push_back(X);
+    CK(cudaMalloc(&d_idx, (size_t)R * 3 * sizeof(int)));
+    fr.p.push_back(d_idx);
+    CK(cudaMalloc(&d_codes, (size_t)std::max(1, G * T) * sizeof(int64_t)));
+    fr.p.push_back(d_codes);
+    float *d_spk = X;  // the x-vector in row 0 of X, rounded there in place
+    text_project_rows(m, pid.data(), np, P, cudaMemcpyDeviceToDevice);
+    cudaStream_t st = m->tp_st;
+    CK(cudaMemcpyAsync(d_spk, speaker, (size_t)H * sizeof(float), cudaMemcpyHostToDevice, st));
+    if (T > 0)
+      CK(cudaMemcpyAsync(d_codes, ref_codes, (size_t)G * T * sizeof(int64_t), cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(d_idx, tr.data(), R * sizeof(int), cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(d_idx + R, ci.data(), R * sizeof(int), cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(d_idx + 2 * R, xr.data(), R * sizeof(int), cudaMemcpyHostToDevice, st));
+    clone_rows(d_spk, d_codes, G, T, m->talker_emb, m->cp_emb_dev, H, X, st);
+    seed_rows(P, m->talker_emb, d_idx, d_idx + R, R, H, out, st, X, d_idx + 2 * R);
+    check_launches();
+    CK(cudaMemcpyAsync(inputs_embeds, out, (size_t)S * H * sizeof(float), cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(trailing, out + (size_t)S * H, (size_t)NT * H * sizeof(float), cudaMemcpyDeviceToHost, st));
+    if (pad_embed)
+      CK(cudaMemcpyAsync(pad_embed, P + (size_t)PAD * H, H * sizeof(float), cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+  });
+}
+
 extern "C" q3t_status q3t_text_dims(const q3t_model *m, int *text_vocab, int *text_hidden) {
   if (!m) return Q3T_INVALID_INPUT;
   if (text_vocab) *text_vocab = m->text_vocab;

@@ -765,20 +765,51 @@ void gather_rows_bf16(const uint16_t *table, const int *ids, int n, int width, u
 // Prompt seed rows (session_seed.rs:151-215): out[s] = bf16(P[text_row[s]] +
 // codec_emb[codec_id[s]]), either term absent when its index is negative.
 __global__ void k_seed_rows(const float *P, const uint16_t *codec_emb, const int *text_row, const int *codec_id,
-                            int H, float *out) {
-  const int s = blockIdx.x, tr = text_row[s], ci = codec_id[s];
+                            const float *X, const int *x_row, int H, float *out) {
+  const int s = blockIdx.x, tr = text_row[s], ci = codec_id[s], xr = x_row ? x_row[s] : -1;
   for (int h = threadIdx.x; h < H; h += blockDim.x) {
     float v = tr >= 0 ? P[(size_t)tr * H + h] : 0.f;
-    if (ci >= 0) v += __uint_as_float((uint32_t)codec_emb[(size_t)ci * H + h] << 16);
+    if (ci >= 0)
+      v += __uint_as_float((uint32_t)codec_emb[(size_t)ci * H + h] << 16);
+    else if (xr >= 0)
+      v += X[(size_t)xr * H + h];
     out[(size_t)s * H + h] = __bfloat162float(__float2bfloat16_rn(v));
   }
 }
 
 void seed_rows(const float *P, const uint16_t *codec_emb, const int *text_row, const int *codec_id, int S, int H,
-               float *out, cudaStream_t st) {
+               float *out, cudaStream_t st, const float *X, const int *x_row) {
   if (S <= 0) return;
-  k_seed_rows<<<S, 256, 0, st>>>(P, codec_emb, text_row, codec_id, H, out);
+  k_seed_rows<<<S, 256, 0, st>>>(P, codec_emb, text_row, codec_id, X, x_row, H, out);
   note(cudaGetLastError(), "k_seed_rows");
+  g_launches++;
+}
+
+// Row 0: bf16(spk); row 1 + t: frame t of the reference codes [G][T], the
+// talker codec embedding of group 0 plus the predictor embedding g - 1 of
+// every group g >= 1, each partial sum rounded to bf16 in group order.
+__global__ void k_clone_rows(const float *spk, const int64_t *codes, int G, int T, const uint16_t *emb0,
+                             const uint16_t *const *embs, int H, float *X) {
+  const int r = blockIdx.x;
+  for (int h = threadIdx.x; h < H; h += blockDim.x) {
+    float v;
+    if (r == 0) {
+      v = __bfloat162float(__float2bfloat16_rn(spk[h]));
+    } else {
+      const int t = r - 1;
+      v = __uint_as_float((uint32_t)emb0[(size_t)codes[t] * H + h] << 16);
+      for (int g = 1; g < G; g++)
+        v = __bfloat162float(__float2bfloat16_rn(
+            v + __uint_as_float((uint32_t)embs[g - 1][(size_t)codes[(size_t)g * T + t] * H + h] << 16)));
+    }
+    X[(size_t)r * H + h] = v;
+  }
+}
+
+void clone_rows(const float *spk, const int64_t *codes, int G, int T, const uint16_t *emb0,
+                const uint16_t *const *embs, int H, float *X, cudaStream_t st) {
+  k_clone_rows<<<1 + T, 256, 0, st>>>(spk, codes, G, T, emb0, embs, H, X);
+  note(cudaGetLastError(), "k_clone_rows");
   g_launches++;
 }
 

@@ -297,9 +297,15 @@ void run_phases(const Phase *phases, int n_phases, cudaStream_t st);
 
 // out[i] = table[ids[i]] (device ids, i < n): rows of `width` bf16.
 void gather_rows_bf16(const uint16_t *table, const int *ids, int n, int width, uint16_t *out, cudaStream_t st);
-// out[s] = bf16-rounded P[text_row[s]] + codec_emb[codec_id[s]] (negative index: term absent), S rows of H
+// out[s] = bf16-rounded P[text_row[s]] + (codec_emb[codec_id[s]], or when
+// codec_id[s] < 0, X[x_row[s]]) (negative index: term absent), S rows of H
 void seed_rows(const float *P, const uint16_t *codec_emb, const int *text_row, const int *codec_id, int S, int H,
-               float *out, cudaStream_t st);
+               float *out, cudaStream_t st, const float *X = nullptr, const int *x_row = nullptr);
+// X [1 + T][H]: row 0 = bf16(spk), row 1 + t = the bf16 group-order sum of
+// frame t's code embeddings (codes [G][T]: group 0 from emb0, group g from
+// embs[g - 1], device pointer array)
+void clone_rows(const float *spk, const int64_t *codes, int G, int T, const uint16_t *emb0,
+                const uint16_t *const *embs, int H, float *X, cudaStream_t st);
 
 // Scatter dense bf16 K/V [layers][n_kv][len][hd] into the pages of `seq`.
 void kv_import(const uint16_t *k, const uint16_t *v, int layers, int len, KVView kv, int seq,

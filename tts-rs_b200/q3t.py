@@ -135,6 +135,7 @@ EXPORTS = [
     "q3t_sample_logits", "q3t_batch_logits", "q3t_codec_encoder_load", "q3t_codec_encoder_free",
     "q3t_codec_encoder_frames", "q3t_codec_encode", "q3t_codec_encoder_hidden",
     "q3t_speaker_encoder_load", "q3t_speaker_encoder_free", "q3t_speaker_embed", "q3t_speaker_mel",
+    "q3t_session_seed_voice_clone",
 ]
 
 
@@ -191,6 +192,9 @@ def lib():
         L.q3t_batch_free.restype = None
         L.q3t_text_project.argtypes = [C.c_void_p, _I64, C.c_int, _F]
         L.q3t_text_dims.argtypes = [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        L.q3t_session_seed_voice_clone.argtypes = [C.c_void_p, _I64, C.c_int, _F, _I64, C.c_int, _I64, C.c_int,
+                                                   C.POINTER(SeedControls), _F, C.c_int, C.POINTER(C.c_int), _F,
+                                                   C.c_int, C.POINTER(C.c_int), _F]
         L.q3t_session_seed.argtypes = [C.c_void_p, _I64, C.c_int, _I64, C.c_int, C.POINTER(SeedControls), _F,
                                        C.c_int, C.POINTER(C.c_int), _F]
         L.q3t_safetensors_open.argtypes = [C.c_char_p, C.POINTER(C.c_void_p)]
@@ -547,6 +551,31 @@ class Model:
         pad = np.zeros(H, np.float32)
         check(lib().q3t_session_seed(*args, _fp(out), rows.value, C.byref(rows), _fp(pad)))
         return out, pad
+
+    def session_seed_voice_clone(self, text_ids, controls, speaker, ref_text_ids=None, ref_codes=None):
+        """build_voice_clone_seed on the device: (inputs_embeds [rows][hidden],
+        trailing text [rows][hidden], tts_pad embedding [hidden]); speaker =
+        the x-vector [hidden]; ref_text_ids / ref_codes [groups][frames] select
+        the in-context recipe."""
+        text_ids = np.ascontiguousarray(text_ids, np.int64)
+        spk = _f32(np.asarray(speaker).reshape(-1))
+        rt = None if ref_text_ids is None else np.ascontiguousarray(ref_text_ids, np.int64)
+        rc = None if ref_codes is None else np.ascontiguousarray(ref_codes, np.int64)
+        cp = np.ascontiguousarray(controls["codec_prefix_ids"], np.int64)
+        ctl = SeedControls(controls["tts_bos_token_id"], controls["tts_eos_token_id"], controls["tts_pad_token_id"],
+                           cp.ctypes.data_as(_I64), len(cp), controls["codec_pad_id"], controls["codec_bos_id"])
+        head = (self.h, text_ids.ctypes.data_as(_I64), len(text_ids), _fp(spk),
+                None if rt is None else rt.ctypes.data_as(_I64), 0 if rt is None else len(rt),
+                None if rc is None else rc.ctypes.data_as(_I64), 0 if rc is None else rc.shape[-1], C.byref(ctl))
+        rows, trows = C.c_int(), C.c_int()
+        check(lib().q3t_session_seed_voice_clone(*head, None, 0, C.byref(rows), None, 0, C.byref(trows), None))
+        H = self.talker_cfg.talker.hidden
+        out = np.zeros((rows.value, H), np.float32)
+        tr = np.zeros((trows.value, H), np.float32)
+        pad = np.zeros(H, np.float32)
+        check(lib().q3t_session_seed_voice_clone(*head, _fp(out), rows.value, C.byref(rows), _fp(tr), trows.value,
+                                                 C.byref(trows), _fp(pad)))
+        return out, tr, pad
 
     @staticmethod
     def codec_last_ms():
