@@ -413,6 +413,22 @@ void q3t_tensor_set_free(q3t_tensor_set *set);
 q3t_status q3t_wav_write(const int16_t *pcm, int64_t num_samples, int sample_rate, int channels, uint8_t *out,
                          int64_t capacity, int64_t *size);
 
+/* decode_reference_audio (execution/reference_audio.rs:17-50, 76-121): a
+ * RIFF/WAVE image (integer PCM 16 / 24 / 32-bit, or 32-bit float; the
+ * extensible header resolved to its sub-format) -> mono f32 samples, each
+ * frame the mean of its channels (integer samples / 2^(bits-1), clamped to
+ * [-1, 1]); *n_samples = frames, *sample_rate (nullable) the file's rate
+ * (samples = NULL: size query).  Other formats, zero channels, no samples
+ * or no complete frame are INVALID_INPUT.  Host code, no GPU. */
+q3t_status q3t_wav_read(const uint8_t *bytes, int64_t n_bytes, float *samples, int64_t max_samples,
+                        int64_t *n_samples, int *sample_rate);
+/* resample_linear (reference_audio.rs:123-156): linear interpolation from
+ * source_rate to target_rate, (n * target + source / 2) / source output
+ * samples (at least 1); none for n = 0 or a zero rate, a copy for equal
+ * rates or one sample (out = NULL: size query).  Host code, no GPU. */
+q3t_status q3t_resample_linear(const float *in, int64_t n, int source_rate, int target_rate, float *out,
+                               int64_t max_out, int64_t *n_out);
+
 /* ------------------------ ragged continuous batching --------------------- */
 typedef struct {
   int max_active;            /* <= model max_active */

@@ -640,6 +640,84 @@ def rvq_encode(embed_sum, usage, x):
     return codes, x
 
 
+def decode_reference_audio(data):
+    """decode_reference_audio (execution/reference_audio.rs:17-50, 76-121)
+    on a WAV image, restated with hound's reading rules: (mono f32 samples,
+    sample rate).  Integer PCM 16 / 24 / 32-bit is value / 2^(bits-1)
+    clamped to [-1, 1], 32-bit float as stored; each whole frame is the f32
+    sum of its channels (from -0.0, in channel order) over the channel
+    count.  Raises ValueError where the reference returns an error."""
+    import struct
+    b = bytes(data)
+    if len(b) < 12 or b[:4] != b"RIFF" or b[8:12] != b"WAVE":
+        raise ValueError("not a RIFF/WAVE image")
+    off, fmt, payload = 12, None, None
+    while off + 8 <= len(b) and payload is None:
+        cid, n = b[off:off + 4], struct.unpack_from("<I", b, off + 4)[0]
+        if off + 8 + n > len(b):
+            raise ValueError("chunk runs past the image")
+        if cid == b"fmt ":
+            tag, ch, rate, _, align, bits = struct.unpack_from("<HHIIHH", b, off + 8)
+            if tag == 0xFFFE:
+                tag = struct.unpack_from("<H", b, off + 8 + 24)[0]
+            fmt = (tag, ch, rate, align, bits)
+        elif cid == b"data":
+            if fmt is None:
+                raise ValueError("data before fmt")
+            payload = b[off + 8:off + 8 + n]
+        off += 8 + n + (n & 1)
+    if fmt is None or payload is None:
+        raise ValueError("missing chunk")
+    tag, ch, rate, align, bits = fmt
+    if ch == 0:
+        raise ValueError("zero channels")
+    if not ((tag == 3 and bits == 32) or (tag == 1 and bits in (16, 24, 32))):
+        raise ValueError("unsupported wav format")
+    bps = bits // 8
+    if align != ch * bps:
+        raise ValueError("block align")
+    total = len(payload) // bps
+    if total == 0:
+        raise ValueError("contains no audio samples")
+    raw = np.frombuffer(payload[:total * bps], np.uint8).reshape(total, bps)
+    if tag == 3:
+        x = raw.copy().view("<f4").reshape(-1)
+    else:
+        v = np.zeros(total, np.int64)
+        for k in range(bps):
+            v |= raw[:, k].astype(np.int64) << (8 * k)
+        v = np.where(v >= 1 << (bits - 1), v - (1 << bits), v)
+        x = np.clip(v.astype(np.float32) / np.float32(2.0 ** (bits - 1)), np.float32(-1), np.float32(1))
+    frames = total // ch
+    if frames == 0:
+        raise ValueError("contains no complete audio frames")
+    x = x[:frames * ch].reshape(frames, ch).astype(np.float32)
+    acc = np.full(frames, -0.0, np.float32)
+    for c in range(ch):
+        acc = (acc + x[:, c]).astype(np.float32)
+    return (acc / np.float32(ch)).astype(np.float32), rate
+
+
+def resample_linear(samples, source_rate, target_rate):
+    """resample_linear (reference_audio.rs:123-156) in f32: out[i] =
+    s[l] (1 - m) + s[r] m with l = i src / dst, r = min(l + 1, n - 1),
+    m = (i src mod dst) / dst; (n dst + src / 2) / src outputs (at least
+    one), none for an empty input or a zero rate, a copy for equal rates or
+    a single sample."""
+    s = np.ascontiguousarray(samples, np.float32).reshape(-1)
+    n = len(s)
+    if n == 0 or source_rate == 0 or target_rate == 0:
+        return np.zeros(0, np.float32)
+    if source_rate == target_rate or n == 1:
+        return s.copy()
+    m = max((n * target_rate + source_rate // 2) // source_rate, 1)
+    pos = np.arange(m, dtype=np.uint64) * np.uint64(source_rate)
+    left = (pos // np.uint64(target_rate)).astype(np.int64)
+    right = np.minimum(left + 1, n - 1)
+    mix = (pos % np.uint64(target_rate)).astype(np.float32) / np.float32(target_rate)
+    return (s[left] * (np.float32(1) - mix) + s[right] * mix).astype(np.float32)
+
+
 def speaker_mel(samples, n_mels=128, sample_rate=24000):
     """Log-mel features of the speaker encoder (speaker/infer/feature.rs):
     [n_mels][frames]."""

@@ -5,7 +5,11 @@
 //    codec/weights.rs:77-81, driven by loading/runtime.rs:131-156);
 //  - the WAV image of 16-bit PCM (PcmAudio::write_wav,
 //    tts_infer/src/audio.rs:12-49, which writes hound's canonical RIFF
-//    layout for integer 16-bit samples).
+//    layout for integer 16-bit samples);
+//  - the voice-clone reference audio in front of the encoders: a WAV image
+//    decoded to mono f32 (decode_reference_audio,
+//    tts_qwen3_tts/src/execution/reference_audio.rs:17-50, 76-121) and the
+//    linear resampler (resample_linear, :123-156).
 //
 // safetensors layout: u64 little-endian header length N, N bytes of JSON
 // {name: {"dtype", "shape", "data_offsets": [begin, end]}, "__metadata__":
@@ -251,6 +255,54 @@ void put_u16(unsigned char *p, uint16_t v) {
   p[0] = (unsigned char)v;
   p[1] = (unsigned char)(v >> 8);
 }
+uint32_t get_u32(const unsigned char *p) {
+  return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+uint16_t get_u16(const unsigned char *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+// The fields of a WAVE file that the decoder reads (hound's WavSpec plus
+// where the sample bytes are).
+struct WavInfo {
+  int format = 0;  // 1 integer PCM, 3 IEEE float (WAVE_FORMAT_EXTENSIBLE resolved to its sub-format)
+  int channels = 0, bits = 0, block_align = 0;
+  uint32_t rate = 0;
+  const unsigned char *data = nullptr;
+  uint64_t data_len = 0;
+};
+
+// RIFF/WAVE chunk walk: "fmt " (16 bytes, or 40 with the extensible
+// sub-format GUID) and "data"; other chunks are skipped, chunks are padded
+// to even sizes.
+void parse_wav(const unsigned char *b, uint64_t n, WavInfo *w) {
+  if (n < 12 || memcmp(b, "RIFF", 4) || memcmp(b + 8, "WAVE", 4))
+    FAIL(Q3T_INVALID_INPUT, "not a RIFF/WAVE image");
+  bool have_fmt = false, have_data = false;
+  for (uint64_t off = 12; off + 8 <= n && !have_data;) {
+    const unsigned char *c = b + off;
+    const uint64_t len = get_u32(c + 4);
+    if (off + 8 + len > n) FAIL(Q3T_INVALID_INPUT, "wav chunk of %llu bytes runs past the image", (unsigned long long)len);
+    if (!memcmp(c, "fmt ", 4)) {
+      if (len < 16) FAIL(Q3T_INVALID_INPUT, "wav fmt chunk of %llu bytes", (unsigned long long)len);
+      w->format = get_u16(c + 8);
+      w->channels = get_u16(c + 10);
+      w->rate = get_u32(c + 12);
+      w->block_align = get_u16(c + 20);
+      w->bits = get_u16(c + 22);
+      if (w->format == 0xFFFE) {  // WAVE_FORMAT_EXTENSIBLE: the GUID's first two bytes are the format tag
+        if (len < 40) FAIL(Q3T_INVALID_INPUT, "wav extensible fmt chunk of %llu bytes", (unsigned long long)len);
+        w->format = get_u16(c + 8 + 24);
+      }
+      have_fmt = true;
+    } else if (!memcmp(c, "data", 4)) {
+      if (!have_fmt) FAIL(Q3T_INVALID_INPUT, "wav data chunk before its fmt chunk");
+      w->data = c + 8;
+      w->data_len = len;
+      have_data = true;
+    }
+    off += 8 + len + (len & 1);
+  }
+  if (!have_fmt || !have_data) FAIL(Q3T_INVALID_INPUT, "wav image without %s chunk", have_fmt ? "a data" : "a fmt");
+}
 
 }  // namespace
 }  // namespace q3t
@@ -340,5 +392,107 @@ extern "C" q3t_status q3t_wav_write(const int16_t *pcm, int64_t num_samples, int
   memcpy(out + 36, "data", 4);
   put_u32(out + 40, (uint32_t)data);
   for (int64_t i = 0; i < num_samples; i++) put_u16(out + 44 + 2 * i, (uint16_t)pcm[i]);
+  return Q3T_OK;
+}
+
+extern "C" q3t_status q3t_wav_read(const uint8_t *bytes, int64_t n_bytes, float *samples, int64_t max_samples,
+                                   int64_t *n_samples, int *sample_rate) {
+  if (!bytes || n_bytes < 0 || !n_samples) {
+    set_error("q3t_wav_read: bad argument");
+    return Q3T_INVALID_INPUT;
+  }
+  return io_guard([&] {
+    WavInfo w;
+    parse_wav(bytes, (uint64_t)n_bytes, &w);
+    if (w.channels == 0) FAIL(Q3T_INVALID_INPUT, "wav has zero channels");
+    // read_wav_samples (reference_audio.rs:76-96): float 32, integer 16 / 24 / 32
+    const bool flt = w.format == 3 && w.bits == 32;
+    const bool pcm = w.format == 1 && (w.bits == 16 || w.bits == 24 || w.bits == 32);
+    if (!flt && !pcm) FAIL(Q3T_INVALID_INPUT, "unsupported wav format: tag %d / %d-bit", w.format, w.bits);
+    const int bps = w.bits / 8;
+    if (w.block_align != w.channels * bps)
+      FAIL(Q3T_INVALID_INPUT, "wav block align %d is not %d channels x %d bytes", w.block_align, w.channels, bps);
+    const uint64_t total = w.data_len / (uint64_t)bps;  // interleaved samples
+    if (total == 0) FAIL(Q3T_INVALID_INPUT, "wav contains no audio samples");
+    const uint64_t frames = total / (uint64_t)w.channels;  // mixdown_to_mono keeps whole frames (:114-121)
+    if (frames == 0) FAIL(Q3T_INVALID_INPUT, "wav contains no complete audio frames");
+    *n_samples = (int64_t)frames;
+    if (sample_rate) *sample_rate = (int)w.rate;
+    if (!samples) return;  // size query
+    if (max_samples < (int64_t)frames)
+      FAIL(Q3T_INVALID_INPUT, "wav has %llu frames, the output holds %lld", (unsigned long long)frames,
+           (long long)max_samples);
+    // integer samples: (value as f32 / 2^(bits-1)).clamp(-1, 1) (:98-112)
+    const float scale = w.bits == 16 ? 32768.0f : (w.bits == 24 ? 8388608.0f : 2147483648.0f);
+    auto sample = [&](uint64_t i) -> float {
+      const unsigned char *p = w.data + i * (uint64_t)bps;
+      if (flt) {
+        const uint32_t u = get_u32(p);
+        float f;
+        memcpy(&f, &u, 4);
+        return f;
+      }
+      int32_t v;
+      if (bps == 2)
+        v = (int16_t)get_u16(p);
+      else if (bps == 3)
+        v = (int32_t)((uint32_t)p[0] << 8 | (uint32_t)p[1] << 16 | (uint32_t)p[2] << 24) >> 8;
+      else
+        v = (int32_t)get_u32(p);
+      const float x = (float)v / scale;
+      return x < -1.0f ? -1.0f : (x > 1.0f ? 1.0f : x);
+    };
+    const float ch = (float)w.channels;
+    for (uint64_t f = 0; f < frames; f++) {
+      float acc = -0.0f;  // f32 Sum starts from -0.0
+      for (int c = 0; c < w.channels; c++) acc += sample(f * (uint64_t)w.channels + (uint64_t)c);
+      samples[f] = acc / ch;
+    }
+  });
+}
+
+extern "C" q3t_status q3t_resample_linear(const float *in, int64_t n, int source_rate, int target_rate, float *out,
+                                          int64_t max_out, int64_t *n_out) {
+  if ((n > 0 && !in) || n < 0 || source_rate < 0 || target_rate < 0 || !n_out) {
+    set_error("q3t_resample_linear: bad argument");
+    return Q3T_INVALID_INPUT;
+  }
+  // resample_linear (reference_audio.rs:123-156): no output for an empty
+  // input or a zero rate, a copy for equal rates or a single sample
+  const uint64_t src = (uint64_t)source_rate, dst = (uint64_t)target_rate;
+  uint64_t len = 0;
+  if (n > 0 && src > 0 && dst > 0) {
+    if (src == dst || n == 1) {
+      len = (uint64_t)n;
+    } else {
+      const unsigned __int128 num = (unsigned __int128)(uint64_t)n * dst + src / 2;
+      const unsigned __int128 q = num / src;
+      if (q > (unsigned __int128)((uint64_t)1 << 40)) {
+        set_error("q3t_resample_linear: output of %llu+ samples", (unsigned long long)((uint64_t)1 << 40));
+        return Q3T_INVALID_INPUT;
+      }
+      len = q == 0 ? 1 : (uint64_t)q;
+    }
+  }
+  *n_out = (int64_t)len;
+  if (!out || len == 0) return Q3T_OK;  // size query / empty
+  if (max_out < (int64_t)len) {
+    set_error("q3t_resample_linear: %llu output samples, the output holds %lld", (unsigned long long)len,
+              (long long)max_out);
+    return Q3T_INVALID_INPUT;
+  }
+  if (src == dst || n == 1) {
+    memcpy(out, in, (size_t)len * sizeof(float));
+    return Q3T_OK;
+  }
+  const float dst_f = (float)target_rate;
+  const uint64_t last = (uint64_t)n - 1;
+  for (uint64_t i = 0; i < len; i++) {
+    const unsigned __int128 pos = (unsigned __int128)i * src;  // saturating u64 in the reference, never reached
+    const uint64_t left = (uint64_t)(pos / dst), right = left + 1 < last ? left + 1 : last;
+    const float mix = (float)(uint32_t)(pos % dst) / dst_f;
+    const float a = in[left] * (1.0f - mix), b = in[right] * mix;
+    out[i] = a + b;
+  }
   return Q3T_OK;
 }

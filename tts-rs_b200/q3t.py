@@ -135,7 +135,7 @@ EXPORTS = [
     "q3t_sample_logits", "q3t_batch_logits", "q3t_codec_encoder_load", "q3t_codec_encoder_free",
     "q3t_codec_encoder_frames", "q3t_codec_encode", "q3t_codec_encoder_hidden",
     "q3t_speaker_encoder_load", "q3t_speaker_encoder_free", "q3t_speaker_embed", "q3t_speaker_mel",
-    "q3t_session_seed_voice_clone",
+    "q3t_session_seed_voice_clone", "q3t_wav_read", "q3t_resample_linear",
 ]
 
 
@@ -201,6 +201,9 @@ def lib():
         L.q3t_tensor_set_list.argtypes = [C.c_void_p, C.POINTER(C.POINTER(Tensor)), C.POINTER(C.c_int)]
         L.q3t_tensor_set_free.argtypes = [C.c_void_p]
         L.q3t_tensor_set_free.restype = None
+        L.q3t_wav_read.argtypes = [C.POINTER(C.c_uint8), C.c_int64, _F, C.c_int64, C.POINTER(C.c_int64),
+                                   C.POINTER(C.c_int)]
+        L.q3t_resample_linear.argtypes = [_F, C.c_int64, C.c_int, C.c_int, _F, C.c_int64, C.POINTER(C.c_int64)]
         L.q3t_wav_write.argtypes = [C.POINTER(C.c_int16), C.c_int64, C.c_int, C.c_int, C.POINTER(C.c_uint8),
                                     C.c_int64, _I64]
         L.q3t_sample_logits.argtypes = [C.c_void_p, _F, C.c_int, C.POINTER(Sampling), _I64, C.c_int, C.c_double,
@@ -454,6 +457,29 @@ def wav_bytes(pcm, sample_rate=24000, channels=1):
     check(lib().q3t_wav_write(pp, pcm.size, sample_rate, channels, out.ctypes.data_as(C.POINTER(C.c_uint8)),
                               size.value, C.byref(size)))
     return out.tobytes()
+
+
+def wav_read(data):
+    """decode_reference_audio on a WAV image: (mono f32 samples, sample rate)."""
+    buf = np.frombuffer(bytes(data), np.uint8)
+    bp = buf.ctypes.data_as(C.POINTER(C.c_uint8))
+    n, rate = C.c_int64(), C.c_int()
+    check(lib().q3t_wav_read(bp, buf.size, None, 0, C.byref(n), C.byref(rate)))
+    out = np.zeros(n.value, np.float32)
+    check(lib().q3t_wav_read(bp, buf.size, _fp(out), n.value, C.byref(n), C.byref(rate)))
+    return out, rate.value
+
+
+def resample_linear(samples, source_rate, target_rate):
+    """resample_linear: linear interpolation to target_rate (f32)."""
+    x = _f32(np.asarray(samples).reshape(-1))
+    n = C.c_int64()
+    xp = _fp(x) if x.size else None
+    check(lib().q3t_resample_linear(xp, x.size, int(source_rate), int(target_rate), None, 0, C.byref(n)))
+    out = np.zeros(n.value, np.float32)
+    check(lib().q3t_resample_linear(xp, x.size, int(source_rate), int(target_rate),
+                                    _fp(out) if out.size else None, n.value, C.byref(n)))
+    return out
 
 
 class Model:
