@@ -285,3 +285,23 @@ def test_voice_clone_icl_seed_oracle_layout(ref_frames):
         np.testing.assert_array_equal(trailing, pad[None])
     with pytest.raises(ValueError):
         ot.session_seed_voice_clone(text, c, spk, ref_text_ids=ref_text)  # no reference codes
+
+
+def test_voice_clone_icl_seed_equal_lengths():
+    """build_voice_clone_icl_seed with as many text rows as codec rows
+    (session_seed.rs:366-381, the else branch with no pad rows): every text
+    row pairs with a codec row and the trailing text is P(pad)."""
+    cfg, w, ot = _clone_fixture()
+    c = SEED_CONTROLS
+    text = np.arange(30, 40, dtype=np.int64)      # target body 33..34 (2 ids)
+    ref_text = np.arange(60, 66, dtype=np.int64)  # ref body 63 (1 id)
+    codes = np.random.default_rng(5).integers(0, 2048, (cfg.n_groups, 3))  # 1 + 3 codec rows, 1 + 2 + 1 text rows
+    rows, trailing, pad = ot.session_seed_voice_clone(text, c, np.zeros(cfg.talker.hidden, np.float32),
+                                                      ref_text_ids=ref_text, ref_codes=codes)
+    n = len(c["codec_prefix_ids"])
+    assert rows.shape[0] == 3 + n + 4
+    np.testing.assert_array_equal(trailing, pad[None])
+    all_text = ot.text_project(np.array([63, 33, 34, c["tts_eos_token_id"]], np.int64))
+    E = w["talker.model.codec_embedding.weight"].astype(np.float32)
+    np.testing.assert_array_equal(rows[3 + n], S.bf16_round(all_text[0] + E[c["codec_bos_id"]]))
+    np.testing.assert_array_equal(rows[3 + n + 1:], S.bf16_round(all_text[1:] + ot.ref_codec_sum(codes)))
