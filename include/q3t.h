@@ -421,12 +421,12 @@ q3t_status q3t_wav_write(const int16_t *pcm, int64_t num_samples, int sample_rat
  * (samples = NULL: size query).  Other formats, zero channels, no samples
  * or no complete frame are INVALID_INPUT.  Host code, no GPU. */
 q3t_status q3t_wav_read(const uint8_t *bytes, int64_t n_bytes, float *samples, int64_t max_samples,
-                        int64_t *n_samples, int *sample_rate);
+                        int64_t *n_samples, uint32_t *sample_rate);
 /* resample_linear (reference_audio.rs:123-156): linear interpolation from
  * source_rate to target_rate, (n * target + source / 2) / source output
  * samples (at least 1); none for n = 0 or a zero rate, a copy for equal
  * rates or one sample (out = NULL: size query).  Host code, no GPU. */
-q3t_status q3t_resample_linear(const float *in, int64_t n, int source_rate, int target_rate, float *out,
+q3t_status q3t_resample_linear(const float *in, int64_t n, uint32_t source_rate, uint32_t target_rate, float *out,
                                int64_t max_out, int64_t *n_out);
 
 /* ------------------------ ragged continuous batching --------------------- */

@@ -138,7 +138,48 @@ def test_resample_matches_oracle(src, dst, n):
     np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
 
 
-def test_resample_rejects_negative_rates():
-    with pytest.raises(q3t.Q3TError) as e:
-        q3t.resample_linear([0.0, 1.0], -1, 24000)
-    assert e.value.status == q3t.INVALID_INPUT
+def test_wav_write_then_read_round_trip():
+    """q3t_wav_write's image (PcmAudio::write_wav) read back by q3t_wav_read:
+    mono samples / 32768, and stereo frames as the mean of their channels."""
+    pcm = np.random.default_rng(9).integers(-32768, 32768, 600).astype(np.int16)
+    x, rate = q3t.wav_read(q3t.wav_bytes(pcm, 24000, 1))
+    assert rate == 24000
+    np.testing.assert_array_equal(x, pcm.astype(np.float32) / np.float32(32768))
+    y, _ = q3t.wav_read(q3t.wav_bytes(pcm, 48000, 2))
+    lr = pcm.reshape(-1, 2).astype(np.float32) / np.float32(32768)
+    np.testing.assert_array_equal(y, ((np.float32(-0.0) + lr[:, 0]) + lr[:, 1]) / np.float32(2))
+
+
+def test_wav_read_differential_on_corrupted_images():
+    """Byte flips and truncations of valid images: the library either
+    rejects the image (INVALID_INPUT) or decodes exactly what the oracle
+    decodes, and rejects exactly what the oracle rejects; it never reads
+    outside the image (the parser bounds every chunk by the image size)."""
+    g = np.random.default_rng(11)
+    bases = [_wav(_int_bytes(g.integers(-2 ** 15, 2 ** 15, 64), 16), 2, 24000, 16, extra_chunk=True),
+             _wav(_int_bytes(g.integers(-2 ** 23, 2 ** 23, 48), 24), 3, 16000, 24, extensible=True),
+             _wav((g.standard_normal(40) * 0.5).astype("<f4").tobytes(), 1, 44100, 32, tag=3)]
+    agree = 0
+    for trial in range(600):
+        img = bytearray(bases[trial % 3])
+        if trial % 4 == 3:
+            img = img[:g.integers(0, len(img))]
+        else:
+            for _ in range(g.integers(1, 4)):
+                img[g.integers(0, len(img))] = g.integers(0, 256)
+        img = bytes(img)
+        try:
+            ref = O.decode_reference_audio(img)
+        except ValueError:
+            ref = None
+        try:
+            got = q3t.wav_read(img)
+        except q3t.Q3TError as e:
+            assert e.status == q3t.INVALID_INPUT
+            got = None
+        assert (got is None) == (ref is None), trial
+        if got is not None:
+            assert got[1] == ref[1]
+            np.testing.assert_array_equal(got[0].view(np.uint32), ref[0].view(np.uint32))
+            agree += 1
+    assert agree > 100

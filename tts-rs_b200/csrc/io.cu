@@ -396,7 +396,7 @@ extern "C" q3t_status q3t_wav_write(const int16_t *pcm, int64_t num_samples, int
 }
 
 extern "C" q3t_status q3t_wav_read(const uint8_t *bytes, int64_t n_bytes, float *samples, int64_t max_samples,
-                                   int64_t *n_samples, int *sample_rate) {
+                                   int64_t *n_samples, uint32_t *sample_rate) {
   if (!bytes || n_bytes < 0 || !n_samples) {
     set_error("q3t_wav_read: bad argument");
     return Q3T_INVALID_INPUT;
@@ -417,7 +417,7 @@ extern "C" q3t_status q3t_wav_read(const uint8_t *bytes, int64_t n_bytes, float 
     const uint64_t frames = total / (uint64_t)w.channels;  // mixdown_to_mono keeps whole frames (:114-121)
     if (frames == 0) FAIL(Q3T_INVALID_INPUT, "wav contains no complete audio frames");
     *n_samples = (int64_t)frames;
-    if (sample_rate) *sample_rate = (int)w.rate;
+    if (sample_rate) *sample_rate = w.rate;
     if (!samples) return;  // size query
     if (max_samples < (int64_t)frames)
       FAIL(Q3T_INVALID_INPUT, "wav has %llu frames, the output holds %lld", (unsigned long long)frames,
@@ -451,9 +451,9 @@ extern "C" q3t_status q3t_wav_read(const uint8_t *bytes, int64_t n_bytes, float 
   });
 }
 
-extern "C" q3t_status q3t_resample_linear(const float *in, int64_t n, int source_rate, int target_rate, float *out,
-                                          int64_t max_out, int64_t *n_out) {
-  if ((n > 0 && !in) || n < 0 || source_rate < 0 || target_rate < 0 || !n_out) {
+extern "C" q3t_status q3t_resample_linear(const float *in, int64_t n, uint32_t source_rate, uint32_t target_rate,
+                                          float *out, int64_t max_out, int64_t *n_out) {
+  if ((n > 0 && !in) || n < 0 || !n_out) {
     set_error("q3t_resample_linear: bad argument");
     return Q3T_INVALID_INPUT;
   }

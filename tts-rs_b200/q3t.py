@@ -202,8 +202,9 @@ def lib():
         L.q3t_tensor_set_free.argtypes = [C.c_void_p]
         L.q3t_tensor_set_free.restype = None
         L.q3t_wav_read.argtypes = [C.POINTER(C.c_uint8), C.c_int64, _F, C.c_int64, C.POINTER(C.c_int64),
-                                   C.POINTER(C.c_int)]
-        L.q3t_resample_linear.argtypes = [_F, C.c_int64, C.c_int, C.c_int, _F, C.c_int64, C.POINTER(C.c_int64)]
+                                   C.POINTER(C.c_uint32)]
+        L.q3t_resample_linear.argtypes = [_F, C.c_int64, C.c_uint32, C.c_uint32, _F, C.c_int64,
+                                          C.POINTER(C.c_int64)]
         L.q3t_wav_write.argtypes = [C.POINTER(C.c_int16), C.c_int64, C.c_int, C.c_int, C.POINTER(C.c_uint8),
                                     C.c_int64, _I64]
         L.q3t_sample_logits.argtypes = [C.c_void_p, _F, C.c_int, C.POINTER(Sampling), _I64, C.c_int, C.c_double,
@@ -463,7 +464,7 @@ def wav_read(data):
     """decode_reference_audio on a WAV image: (mono f32 samples, sample rate)."""
     buf = np.frombuffer(bytes(data), np.uint8)
     bp = buf.ctypes.data_as(C.POINTER(C.c_uint8))
-    n, rate = C.c_int64(), C.c_int()
+    n, rate = C.c_int64(), C.c_uint32()
     check(lib().q3t_wav_read(bp, buf.size, None, 0, C.byref(n), C.byref(rate)))
     out = np.zeros(n.value, np.float32)
     check(lib().q3t_wav_read(bp, buf.size, _fp(out), n.value, C.byref(n), C.byref(rate)))
