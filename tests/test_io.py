@@ -87,3 +87,39 @@ def test_wav_matches_python_wave(channels, n):
 def test_wav_rejects_partial_frames():
     with pytest.raises(q3t.Q3TError):
         q3t.wav_bytes(np.zeros(3, np.int16), 24000, 2)
+
+
+def test_safetensors_corrupted_headers_fail_cleanly(tmp_path):
+    """Byte flips in the JSON header and truncations of a valid checkpoint:
+    the reader either lists tensors whose bytes lie inside the file (each
+    read back here) or fails with RUNTIME_LOAD; it never reads past the
+    header (numbers are parsed from bounded copies) or past the file."""
+    g = np.random.default_rng(2)
+    good = tmp_path / "good.safetensors"
+    write_safetensors(good, {"a.weight": (g.standard_normal((3, 5)).astype(np.float32), "F32"),
+                             "b.weight": (S.bf16_round(g.standard_normal((4, 2)).astype(np.float32)), "BF16"),
+                             "c.weight": (g.standard_normal(7).astype(np.float16), "F16"),
+                             "ids": (np.arange(3), "I64")})
+    blob = good.read_bytes()
+    hlen = struct.unpack("<Q", blob[:8])[0]
+    ok = 0
+    for trial in range(300):
+        img = bytearray(blob)
+        if trial % 5 == 4:
+            img = img[:g.integers(0, len(img))]
+        else:
+            for _ in range(g.integers(1, 4)):
+                img[8 + g.integers(0, hlen)] = g.choice(list(b'0123456789-,:[]{}" e'))
+        p = tmp_path / f"c{trial}.safetensors"
+        p.write_bytes(bytes(img))
+        try:
+            ts = q3t.TensorSet(p)
+        except q3t.Q3TError as e:
+            assert e.status == 2  # RUNTIME_LOAD
+            continue
+        for t in ts.raw():
+            v = _values(t)
+            assert v.size == int(np.prod(t.shape[:t.ndim])) if t.ndim else 1
+        ts.close()
+        ok += 1
+    assert ok > 0

@@ -20,6 +20,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <cerrno>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -86,12 +87,20 @@ struct Json {
     p++;
     return s;
   }
-  long long integer() {
+  long long integer() {  // parsed from a bounded copy: the header is not NUL-terminated
     ws();
+    char buf[24];
+    size_t k = 0;
+    while (p + k < end && k < sizeof buf - 1 && (p[k] == '-' || (p[k] >= '0' && p[k] <= '9'))) {
+      buf[k] = p[k];
+      k++;
+    }
+    buf[k] = 0;
     char *e = nullptr;
-    const long long v = strtoll(p, &e, 10);
-    if (e == p) bad("number expected");
-    p = e;
+    errno = 0;
+    const long long v = strtoll(buf, &e, 10);
+    if (e == buf || errno == ERANGE || (size_t)(e - buf) != k) bad("number expected");
+    p += k;
     return v;
   }
   void skip() {  // any value
@@ -208,6 +217,8 @@ void parse(q3t_tensor_set *s, const unsigned char *base, size_t len) {
     long long numel = 1;
     for (long long d : en.shape) {
       if (d < 0) FAIL(Q3T_RUNTIME_LOAD, "safetensors: tensor %s has a negative dimension", en.name.c_str());
+      if (d > 0 && numel > (1LL << 40) / d)
+        FAIL(Q3T_RUNTIME_LOAD, "safetensors: tensor %s has more than 2^40 elements", en.name.c_str());
       numel *= d;
     }
     if (en.b < 0 || en.e < en.b || (size_t)en.e > data_len || en.e - en.b != numel * esz)
