@@ -176,7 +176,10 @@ q3t_status q3t_session_step_forced(q3t_session *s, const int64_t *codes,
 q3t_status q3t_session_codes(q3t_session *s, int64_t *out, int *num_frames);
 /* SessionImpl::finish (execution/loaded_model.rs:112-152) without the
  * voice-clone prefix: codec-decodes the generated codes; wave (nullable)
- * receives f32 samples, pcm (nullable) the i16 PCM of Waveform::to_pcm. */
+ * receives f32 samples, pcm (nullable) the i16 PCM of Waveform::to_pcm.  An
+ * in-context voice-clone session instead decodes [clip codes, generated
+ * codes] with q3t_codec_decode and drops the first clip_frames * n /
+ * (clip_frames + T) samples, as :115-135 do. */
 q3t_status q3t_session_finish(q3t_session *s, float *wave, int16_t *pcm,
                               int64_t capacity, int64_t *num_samples);
 /* Isolated talker decode step (decode_step + codec_head, infer/mod.rs:
