@@ -108,6 +108,37 @@ def main(ref):
                          "mask": [int(mk.group(i)) for i in range(1, 5)], "shape": [1, 2, 2, 2],
                          "source": f"tts_qwen3_tts/src/model/nn/attention.rs:{_line_of(src, 'fn attention_restores_requested_dtype')}"}
 
+    # execution/reference_audio.rs: the voice-clone clip reader's tests
+    path = os.path.join(ref, "tts_qwen3_tts", "src", "execution", "reference_audio.rs")
+    src = open(path).read()
+    at = lambda name: f"tts_qwen3_tts/src/execution/reference_audio.rs:{_line_of(src, 'fn ' + name)}"
+    m = re.search(r"fn linear_resample_changes_length_for_new_sample_rate\(\).*?vec!\[([^\]]*)\];\s*"
+                  r"let resampled = resample_linear\(&source, (\d+), (\d+)\);\s*"
+                  r"assert_eq!\(resampled.len\(\), (\d+)\);", src, re.S)
+    out["resample_length"] = {"input": _floats(m.group(1)), "source_rate": int(m.group(2)),
+                              "target_rate": int(m.group(3)), "expected_len": int(m.group(4)),
+                              "source": at("linear_resample_changes_length_for_new_sample_rate")}
+    m = re.search(r"fn linear_resample_returns_empty_for_invalid_rates\(\) \{(.*?)\n    \}", src, re.S)
+    out["resample_invalid_rates"] = {
+        "cases": [{"input": _floats(a), "source_rate": int(b.replace("_", "")), "target_rate": int(c.replace("_", ""))}
+                  for a, b, c in re.findall(r"resample_linear\(&\[([^\]]*)\], ([\d_]+), ([\d_]+)\)", m.group(1))],
+        "source": at("linear_resample_returns_empty_for_invalid_rates")}
+    m = re.search(r"fn decoded_reference_audio_can_prepare_multiple_sample_rates\(\).*?write_wav_i16\(\s*&path,\s*"
+                  r"([\d_]+),\s*(\d+),\s*&\[([^\]]*)\],\s*\);.*?prepare_reference_audio\(&decoded, ([\d_]+)\).*?"
+                  r"prepare_reference_audio\(&decoded, ([\d_]+)\).*?native.samples.len\(\), (\d+)\);.*?"
+                  r"resampled.samples.len\(\), (\d+)\);", src, re.S)
+    out["wav_stereo_prepare"] = {"rate": int(m.group(1).replace("_", "")), "channels": int(m.group(2)),
+                                 "pcm": [int(x.replace("_", "")) for x in re.findall(r"-?[\d_]+", m.group(3))],
+                                 "native_rate": int(m.group(4).replace("_", "")),
+                                 "target_rate": int(m.group(5).replace("_", "")),
+                                 "native_len": int(m.group(6)), "resampled_len": int(m.group(7)),
+                                 "source": at("decoded_reference_audio_can_prepare_multiple_sample_rates")}
+    m = re.search(r"fn decoded_reference_audio_mixdowns_stereo_and_resamples\(\).*?"
+                  r"sample.abs\(\) < ([\d.]+)\)", src, re.S)
+    out["wav_stereo_prepare"]["max_abs"] = float(m.group(1))
+    m = re.search(r"fn decode_reference_audio_rejects_empty_payload\(\).*?contains\(\"([^\"]*)\"\)", src, re.S)
+    out["wav_empty_payload"] = {"message": m.group(1), "source": at("decode_reference_audio_rejects_empty_payload")}
+
     dst = os.path.join(os.path.dirname(os.path.abspath(__file__)), "reference_kats.json")
     with open(dst, "w") as f:
         json.dump(out, f, indent=1)

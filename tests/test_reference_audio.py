@@ -3,9 +3,10 @@ ABI (no GPU): q3t_wav_read (decode_reference_audio,
 execution/reference_audio.rs:17-50, 76-121) and q3t_resample_linear
 (resample_linear, :123-156).
 
-* the reference's own tests (reference_audio.rs:159-219): resampled
-  lengths, empty output for a zero rate, a 48 kHz stereo file mixed down
-  and resampled to 24 kHz, the empty-payload error;
+* the reference's own tests (reference_audio.rs:159-219, their literals
+  extracted into tests/golden/reference_kats.json): resampled lengths,
+  empty output for a zero rate, a 48 kHz stereo file mixed down and
+  resampled to 24 kHz, the empty-payload error;
 * bit-exact against the oracle's restatement for every format the
   reference reads (integer 16 / 24 / 32-bit, 32-bit float, the extensible
   header, extra chunks with odd-size padding) and 1-3 channels, and for
@@ -13,6 +14,8 @@ execution/reference_audio.rs:17-50, 76-121) and q3t_resample_linear
 * 16-bit PCM images written by Python's wave module.
 """
 import io
+import json
+import os
 import struct
 import wave
 
@@ -43,31 +46,41 @@ def _int_bytes(v, bits):
     return np.stack([(v >> (8 * k)) & 0xFF for k in range(bits // 8)], 1).astype(np.uint8).tobytes()
 
 
-# ---- the reference's tests ----
+# ---- the reference's tests (literals extracted by tests/golden/make_golden.py) ----
 
-def test_resample_changes_length_for_new_sample_rate():
-    out = q3t.resample_linear([0.0, 0.5, -0.5, 1.0], 4, 8)
-    assert len(out) == 8 and (out > 0).any()
-
-
-def test_resample_returns_empty_for_invalid_rates():
-    assert len(q3t.resample_linear([0.0, 1.0], 0, 24000)) == 0
-    assert len(q3t.resample_linear([0.0, 1.0], 24000, 0)) == 0
+@pytest.fixture(scope="module")
+def kats():
+    with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "reference_kats.json")) as f:
+        return json.load(f)
 
 
-def test_stereo_mixdown_and_resample():
-    pcm = np.array([500, -500, 1000, -1000, 1500, -1500, 2000, -2000], np.int16)
-    x, rate = q3t.wav_read(_wav(pcm.tobytes(), 2, 48000, 16))
-    assert rate == 48000 and len(x) == 4  # the native-rate preparation
-    y = q3t.resample_linear(x, rate, 24000)
-    assert len(y) == 2 and (np.abs(y) < 0.01).all()
+def test_resample_changes_length_for_new_sample_rate(kats):
+    k = kats["resample_length"]
+    for fn in (q3t.resample_linear, O.resample_linear):
+        out = fn(k["input"], k["source_rate"], k["target_rate"])
+        assert len(out) == k["expected_len"] and (out > 0).any()
 
 
-def test_empty_payload_is_rejected():
+def test_resample_returns_empty_for_invalid_rates(kats):
+    for c in kats["resample_invalid_rates"]["cases"]:
+        for fn in (q3t.resample_linear, O.resample_linear):
+            assert len(fn(c["input"], c["source_rate"], c["target_rate"])) == 0
+
+
+def test_stereo_mixdown_and_resample(kats):
+    k = kats["wav_stereo_prepare"]
+    img = _wav(np.array(k["pcm"], np.int16).tobytes(), k["channels"], k["rate"], 16)
+    x, rate = q3t.wav_read(img)
+    assert rate == k["native_rate"] and len(x) == k["native_len"]
+    y = q3t.resample_linear(x, rate, k["target_rate"])
+    assert len(y) == k["resampled_len"] and (np.abs(y) < k["max_abs"]).all()
+
+
+def test_empty_payload_is_rejected(kats):
     with pytest.raises(q3t.Q3TError) as e:
         q3t.wav_read(_wav(b"", 1, 24000, 16))
     assert e.value.status == q3t.INVALID_INPUT
-    assert "contains no audio samples" in str(e.value)
+    assert kats["wav_empty_payload"]["message"] in str(e.value)
 
 
 # ---- against the oracle ----
