@@ -196,3 +196,18 @@ def test_wav_read_differential_on_corrupted_images():
             np.testing.assert_array_equal(got[0].view(np.uint32), ref[0].view(np.uint32))
             agree += 1
     assert agree > 100
+
+
+def test_resample_random_rates_match_oracle():
+    """Random rate pairs (1 Hz .. 384 kHz, including ones whose products
+    pass 2^32) and lengths: same length and bits as the oracle."""
+    g = np.random.default_rng(21)
+    for trial in range(300):
+        src, dst = (int(v) for v in g.integers(1, 384001, 2))
+        if trial % 10 == 0:
+            src, dst = 4_000_000_000 - trial, 3_999_999_999  # u32 rates near the top of the range
+        n = int(g.integers(1, 400))
+        x = (g.standard_normal(n) * 0.5).astype(np.float32)
+        got, ref = q3t.resample_linear(x, src, dst), O.resample_linear(x, src, dst)
+        assert got.shape == ref.shape, (src, dst, n)
+        np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
